@@ -1,0 +1,326 @@
+"""Benchmark of the B200 decode hot path (one JSON line on rank 0).
+
+Workload (N=1, default): isolated absorbed-MLA decode attention at DeepSeek-V3
+shape - B=64 sequences, 128 heads, kv_lora_rank 512, rope 64, per-sequence
+context uniform in [1024, 8192] (seed 1), paged latent cache with 64-token
+pages and a random block-table permutation, bf16.  A step is one
+dsb_mla_decode call over the whole batch (64 query tokens).  Under torchrun
+each rank decodes its own batch (attention is data-parallel over the batch,
+no collective): weak scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s (box) at 1/2/4/8 B200; MLA/MoE HBM GB/s as % of peak"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                for i, n in enumerate(names):
+                    if r[5 + i].strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU baselines
+
+
+def _cpu_port_worker(args):
+    """Time the oracle port of the reference's attention loop on sequences."""
+    import numpy as np
+
+    import oracle as O
+
+    q_lat, q_rope, cache, bt, lens, scale = args
+    t0 = time.perf_counter()
+    O.mla_decode_paged(q_lat, q_rope, cache, bt, lens, scale)
+    return time.perf_counter() - t0, int(np.asarray(lens).size)
+
+
+def _cpu_sample(case, n_seq):
+    """A bounded sample: the n_seq sequences nearest the mean length, with their
+    pages gathered into a compact host cache."""
+    import numpy as np
+
+    from deepseek_cpp_infer_b200.workloads import to_u16
+
+    mean = case.seq_lens.mean()
+    idx = list(np.argsort(np.abs(case.seq_lens - mean))[:n_seq])
+    q_lat = to_u16(case.q_lat)[idx]
+    q_rope = to_u16(case.q_rope)[idx]
+    pages = [case.block_table_host[b, : (case.seq_lens[b] + 63) // 64] for b in idx]
+    allp = np.concatenate(pages)
+    cache = to_u16(case.cache[torch_index(allp)])
+    bt = np.zeros((len(idx), max(len(p) for p in pages)), np.int32)
+    k = 0
+    for i, p in enumerate(pages):
+        bt[i, : len(p)] = np.arange(k, k + len(p))
+        k += len(p)
+    lens = case.seq_lens[idx]
+    return q_lat, q_rope, cache, bt, lens, float(lens.mean() / mean)
+
+
+def torch_index(a):
+    import torch
+
+    return torch.from_numpy(a.astype("int64")).to("cuda")
+
+
+def cpu_baseline_port(case, budget_s=15.0):
+    """1-thread oracle port on sequences near the mean length; tokens/s scaled
+    to the workload's mean context."""
+    q_lat, q_rope, cache, bt, lens, len_ratio = _cpu_sample(case, 2)
+    dt, n = _cpu_port_worker((q_lat[:1], q_rope[:1], cache, bt[:1], lens[:1], case.scale))
+    n_seq = 1
+    if dt < budget_s / 2:
+        dt2, _ = _cpu_port_worker((q_lat[1:], q_rope[1:], cache, bt[1:], lens[1:], case.scale))
+        dt += dt2
+        n_seq = 2
+    tok_s = n_seq / dt * len_ratio
+    return {"value": tok_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n_seq} sequence(s) nearest the mean context ({', '.join(str(int(x)) for x in lens[:n_seq])} "
+                      f"tokens) through orc_mla_decode_paged (the reference's attention loop, mla.cpp:86-116), "
+                      f"scaled to the mean context"}
+
+
+# ------------------------------------------------------------------ arms
+
+
+def run_reference(args):
+    """The reference's CPU attention loop (oracle port) on the host cores."""
+    import multiprocessing as mp
+
+    import torch
+
+    from deepseek_cpp_infer_b200.workloads import mla_case
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    case = mla_case(seed=1, device="cuda" if torch.cuda.is_available() else "cpu")
+    q_lat, q_rope, cache, bt, lens, len_ratio = _cpu_sample(case, cores)
+    jobs = [(q_lat[i:i + 1], q_rope[i:i + 1], cache, bt[i:i + 1], lens[i:i + 1], case.scale) for i in range(len(lens))]
+    ctxm = mp.get_context("spawn")
+    with ctxm.Pool(cores) as pool:
+        for _ in range(args.warmup):
+            pool.map(_cpu_port_worker, jobs[:1])
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            pool.map(_cpu_port_worker, jobs)
+        dt = time.perf_counter() - t0
+    tok_s = len(jobs) * args.steps / dt * len_ratio
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "isolated MLA decode, DeepSeek-V3 shape (B=64, H=128, R=512, P=64, ctx U[1024,8192], "
+                               "page 64, seed 1)", "sample": f"{len(jobs)} sequences per step"},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{len(jobs)} sequences nearest the mean context per step, one per process "
+                                   f"(spawn pool of {cores}), orc_mla_decode_paged"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import deepseek_cpp_infer_b200 as dsb
+    from deepseek_cpp_infer_b200.workloads import mla_case
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ctx = dsb.Context(local)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    case = mla_case(seed=1 + 1000 * rank, device=f"cuda:{local}")
+    out = torch.empty(case.B, case.H, case.R, dtype=torch.bfloat16, device=f"cuda:{local}")
+
+    def step():
+        ctx.mla_decode(case.q_lat, case.q_rope, case.cache, case.block_table, case.seq_lens, case.scale, out)
+
+    # ---------------- device-resident timing
+    for _ in range(max(3, args.warmup)):
+        step()
+    ctx.sync()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ctx.reset_stats()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    ctx.sync()
+    clocks = sampler.stop()
+    launches = ctx.stats()["kernel_launches"]
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---------------- end to end: pinned host q in, latent out back, per step
+    q_lat_h = case.q_lat.cpu().pin_memory()
+    q_rope_h = case.q_rope.cpu().pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_lat_d = torch.empty_like(case.q_lat)
+    q_rope_d = torch.empty_like(case.q_rope)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            q_lat_d.copy_(q_lat_h, non_blocking=True)
+            q_rope_d.copy_(q_rope_h, non_blocking=True)
+        ctx.mla_decode(q_lat_d, q_rope_d, case.cache, case.block_table, case.seq_lens, case.scale, out)
+        with torch.cuda.stream(stream):
+            out_h.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    ctx.sync()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    ctx.sync()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms_e2e], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t.item())
+    h2d = case.q_lat.numel() * 2 + case.q_rope.numel() * 2 + case.B * 4
+    d2h = out.numel() * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_port(case)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = case.algorithmic_bytes / (ms_max * 1e-3) / 1e9
+        tok_s = world * case.B / (ms_max * 1e-3)
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q and cache, seed 1 + 1000*rank)",
+            "config": {
+                "workload": "isolated MLA decode attention, DeepSeek-V3 shape: B=64 per GPU, H=128, kv_lora_rank 512, "
+                            "rope 64, scale 1/sqrt(192), ctx U[1024,8192] (seed 1), 64-token pages, random block table",
+                "kv_bytes_per_step": case.kv_bytes, "l2": "inputs larger than L2 (KV cache %.0f MB > 126 MB)"
+                % (case.kv_bytes / 1e6), "parallelism": f"dp{world} (attention data-parallel over the batch)",
+            },
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "note": "algorithmic bytes (KV rows + q + latent out) per dsb_mla_decode call / call time"},
+            "e2e": {"value": world * case.B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches, "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

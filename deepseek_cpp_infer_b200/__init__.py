@@ -1,0 +1,156 @@
+"""Python view of libdsb.so, the B200 decode hot path of deepseek_cpp_infer.
+
+The product is the C ABI declared in include/dsb/dsb.h; this module only binds
+it with ctypes so that tests and bench.py can drive it with device buffers
+(torch tensors are used for allocation; only raw pointers cross the ABI).
+There is no CPU fallback: if libdsb.so is missing, importing the bindings
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdsb.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "dsb", "dsb.h")
+
+DSB_OK = 0
+DSB_EINVAL = 1
+DSB_ECUDA = 2
+DSB_ENOMEM = 3
+DSB_ETIMEOUT = 4
+DSB_EUNSUPPORTED = 5
+
+_c_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+class DsbError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"dsb error {code}: {msg}")
+        self.code = code
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [
+        ("kernel_launches", ctypes.c_uint64),
+        ("mla_calls", ctypes.c_uint64),
+        ("mla_work_items", ctypes.c_uint64),
+        ("mla_partials", ctypes.c_uint64),
+        ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+# (name, restype, argtypes) for every function of include/dsb/dsb.h
+_PROTOS = [
+    ("dsb_version", ctypes.c_int, []),
+    ("dsb_ctx_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_ctx_destroy", ctypes.c_int, [ctypes.c_void_p]),
+    ("dsb_ctx_set_stream", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ("dsb_ctx_stream", ctypes.c_void_p, [ctypes.c_void_p]),
+    ("dsb_last_error", ctypes.c_char_p, [ctypes.c_void_p]),
+    ("dsb_sync", ctypes.c_int, [ctypes.c_void_p]),
+    ("dsb_get_stats", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(Stats)]),
+    ("dsb_reset_stats", ctypes.c_int, [ctypes.c_void_p]),
+    (
+        "dsb_mla_decode",
+        ctypes.c_int,
+        [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_int, _c_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_float, ctypes.c_void_p,
+        ],
+    ),
+]
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libdsb.so (built in-tree by `make -C deepseek_cpp_infer_b200`)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {_HERE}` (no CPU fallback exists)")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, res, args in _PROTOS:
+            fn = getattr(l, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = l
+    return _lib
+
+
+def header_functions() -> list[str]:
+    """Names of the functions declared in include/dsb/dsb.h."""
+    with open(HEADER_PATH) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dsb_\w+)\s*\(", text)))
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+class Context:
+    """One dsb_ctx: a device, a stream, a workspace and counters."""
+
+    def __init__(self, device: int = 0):
+        self._l = lib()
+        h = ctypes.c_void_p()
+        rc = self._l.dsb_ctx_create(device, ctypes.byref(h))
+        if rc != DSB_OK:
+            raise DsbError(rc, f"dsb_ctx_create({device}) failed")
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            self._l.dsb_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int):
+        if rc != DSB_OK:
+            raise DsbError(rc, self._l.dsb_last_error(self.h).decode())
+
+    def set_stream(self, stream_handle: int | None):
+        self._check(self._l.dsb_ctx_set_stream(self.h, stream_handle or None))
+
+    @property
+    def stream(self) -> int:
+        return self._l.dsb_ctx_stream(self.h) or 0
+
+    def sync(self):
+        self._check(self._l.dsb_sync(self.h))
+
+    def stats(self) -> dict:
+        s = Stats()
+        self._check(self._l.dsb_get_stats(self.h, ctypes.byref(s)))
+        return {k: getattr(s, k) for k, _ in Stats._fields_}
+
+    def reset_stats(self):
+        self._check(self._l.dsb_reset_stats(self.h))
+
+    def mla_decode(self, q_lat, q_rope, kv_cache, block_table, seq_lens, softmax_scale, out, block_size=64):
+        """Absorbed MLA decode (dsb_mla_decode).  q_lat [B,H,R], q_rope [B,H,P],
+        kv_cache [n_blocks, 64, R+P] bf16 on the device; block_table int32
+        device [B, max_blocks]; seq_lens a host sequence of ints; out [B,H,R] bf16."""
+        B, H, R = q_lat.shape
+        P = q_rope.shape[2]
+        n_blocks = kv_cache.shape[0]
+        lens = (ctypes.c_int32 * B)(*[int(x) for x in seq_lens])
+        self._check(
+            self._l.dsb_mla_decode(
+                self.h, _ptr(q_lat), _ptr(q_rope), _ptr(kv_cache), n_blocks, block_size, _ptr(block_table),
+                block_table.shape[1], lens, B, H, R, P, float(softmax_scale), _ptr(out),
+            )
+        )

@@ -1,0 +1,604 @@
+// Absorbed MLA decode attention over a paged latent cache, sm_100a.
+//
+// Math (one query token per sequence, per head h):
+//   s_t = ([q_lat_h | q_rope_h] . [c_t | kr_t]) * scale,  p = softmax(s),
+//   out_h = sum_t p_t c_t
+// which is the reference's per-head attention (src/models/deepseek/mla.cpp:86-116)
+// with W_UK folded into the query and W_UV applied after the sum.
+//
+// Work decomposition.  A work item is a run of whole 64-token pages of one
+// sequence.  Each item is processed by a cluster of NCTA CTAs; CTA r owns the
+// latent columns [r*VD, (r+1)*VD) (VD = R / NCTA) and rope columns
+// [R + r*PD, R + (r+1)*PD) (PD = P / NCTA) of every cache row, so every cache
+// byte is read from HBM once.  Per 64-token page:
+//   TMA warp   : loads the CTA's column slice of the page (SW128 / SW64 tiles)
+//   MMA warp   : S = Q_r K_r^T (tcgen05, A = Q from TMEM, B = page from smem)
+//                then O_r += P V_r (A = P from TMEM, B = the same page, MN-major)
+//   4 softmax warps (thread i <-> head i <-> TMEM lane i):
+//                read S_r, exchange it with the peer CTA through distributed
+//                shared memory, S = S_0 + S_1 (bitwise equal in both CTAs),
+//                online softmax in the exp2 domain with a lazy running max,
+//                write P (bf16) to TMEM.
+// TMEM (512 columns): O [VD] | S [64] | P [32] | Q [(VD+PD)/2].
+// Items that cover a whole sequence write bf16 output; split sequences write
+// fp32 partials (O, running max, sum) merged by mla_combine_kernel.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <queue>
+#include <vector>
+
+#include "dsb_internal.h"
+#include "dsb_ptx.cuh"
+
+namespace dsb {
+namespace {
+
+constexpr int kTok = 64;            // tokens per tile == page size
+constexpr int kMaxItemPages = 256;  // pages per work item (16384 tokens)
+constexpr int kHeadsPad = 128;      // MMA M (heads padded to 128)
+constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
+
+struct MlaItem {
+  int32_t b;        // sequence
+  int32_t page0;    // first page index within the sequence
+  int32_t npages;   // pages in this item
+  int32_t tok_end;  // absolute end token (exclusive) of this item
+  int32_t partial;  // -1: whole sequence, write out; else partial slot
+};
+
+struct MlaCombine {
+  int32_t b;
+  int32_t first;  // first partial slot
+  int32_t n;      // number of partial slots
+};
+
+template <int R, int P, int NCTA>
+struct MlaShape {
+  static constexpr int VD = R / NCTA;             // latent columns per CTA
+  static constexpr int PD = P / NCTA;             // rope columns per CTA
+  static constexpr int QD = VD + PD;              // QK contraction per CTA
+  static constexpr int NCH = VD / 64;             // SW128 chunks per page slice
+  static constexpr int CH_BYTES = kTok * 128;     // 64 rows x 128 B
+  static constexpr int ROPE_BYTES = kTok * PD * 2;
+  static constexpr int STAGE_BYTES = NCH * CH_BYTES + ROPE_BYTES;
+  static constexpr int NSTAGE = (NCTA == 2) ? 5 : 8;
+  static constexpr int XCH_BYTES = (NCTA == 2) ? kHeadsPad * kTok * 4 : 0;
+  // TMEM column map
+  static constexpr uint32_t T_O = 0;
+  static constexpr uint32_t T_S = VD;
+  static constexpr uint32_t T_P = VD + 64;
+  static constexpr uint32_t T_Q = VD + 96;
+  static constexpr uint32_t T_COLS = 512;
+  static_assert(T_Q + QD / 2 <= T_COLS, "TMEM overflow");
+  static_assert(PD == 32, "rope slice must be 32 columns (SW64 tile)");
+  static_assert(VD % 64 == 0, "latent slice must be whole 64-column chunks");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
+  // shared memory map (offsets from a 1024-aligned base)
+  static constexpr int OFF_STAGE = 0;
+  static constexpr int OFF_XCH = NSTAGE * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_XCH + XCH_BYTES;
+  static constexpr int NBAR = 2 * NSTAGE + 9;
+  static constexpr int OFF_PAGES = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_MISC = OFF_PAGES + kMaxItemPages * 4;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+template <int R, int P, int NCTA>
+__global__ void __launch_bounds__(192, 1)
+    mla_decode_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
+                      const __nv_bfloat16* __restrict__ q_lat, const __nv_bfloat16* __restrict__ q_rope,
+                      const int32_t* __restrict__ block_table, int max_blocks, const MlaItem* __restrict__ items,
+                      int H, float scale_log2, __nv_bfloat16* __restrict__ out, float* __restrict__ ws_o,
+                      float2* __restrict__ ws_ml, int* __restrict__ status) {
+  using S = MlaShape<R, P, NCTA>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* full = bars;                  // [NSTAGE] page slice landed
+  uint64_t* empty = bars + S::NSTAGE;     // [NSTAGE] page slice consumed by PV
+  uint64_t* s_full = bars + 2 * S::NSTAGE + 0;
+  uint64_t* s_free = bars + 2 * S::NSTAGE + 1;
+  uint64_t* p_full = bars + 2 * S::NSTAGE + 2;
+  uint64_t* pv_done = bars + 2 * S::NSTAGE + 3;
+  uint64_t* q_ready = bars + 2 * S::NSTAGE + 4;
+  uint64_t* xch_full = bars + 2 * S::NSTAGE + 5;   // peer's partial S landed in my XCH
+  uint64_t* peer_free = bars + 2 * S::NSTAGE + 6;  // peer finished reading its XCH
+  uint64_t* drain = bars + 2 * S::NSTAGE + 7;
+  int32_t* pages = reinterpret_cast<int32_t*>(smem + S::OFF_PAGES);
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
+  // never raised: drain waits keep their time limit but ignore the abort flag
+  volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
+  float* xch = reinterpret_cast<float*>(smem + S::OFF_XCH);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = (NCTA == 2) ? cluster_ctarank() : 0u;
+  const MlaItem item = items[blockIdx.x / NCTA];
+  const int n_tiles = item.npages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(q_ready, 128);
+    mbar_init(xch_full, 128);
+    mbar_init(peer_free, 128);
+    mbar_init(drain, 1);
+    *abort = 0;
+    *no_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_base_smem, S::T_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 4) {
+    for (int i = lane; i < n_tiles; i += 32)
+      pages[i] = block_table[(int64_t)item.b * max_blocks + item.page0 + i];
+    if (lane == 0) {
+      tma_prefetch_desc(&map_v);
+      tma_prefetch_desc(&map_r);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (NCTA == 2) cluster_sync();  // peer barriers initialised before any remote arrive
+  const uint32_t tmem = *tmem_base_smem;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % S::NSTAGE;
+        if (j >= S::NSTAGE && !mbar_wait(&empty[s], ((j / S::NSTAGE) - 1) & 1, abort)) {
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+        uint8_t* st = smem + S::OFF_STAGE + s * S::STAGE_BYTES;
+        const int y = pages[j] * kTok;
+#pragma unroll
+        for (int c = 0; c < S::NCH; ++c)
+          tma_load_2d(st + c * S::CH_BYTES, &map_v, &full[s], (int)(rank * S::VD + 64 * c), y, policy);
+        tma_load_2d(st + S::NCH * S::CH_BYTES, &map_r, &full[s], (int)(R + rank * S::PD), y, policy);
+        ++issued;
+      }
+      if (*abort) {
+        // drain loads still in flight before shared memory is released
+        const int first = issued > S::NSTAGE ? issued - S::NSTAGE : 0;
+        for (int j = first; j < issued; ++j) mbar_wait(&full[j % S::NSTAGE], (j / S::NSTAGE) & 1, no_abort);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 64, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, S::VD, 0, 1);
+      const uint32_t tS = tmem + S::T_S, tO = tmem + S::T_O, tP = tmem + S::T_P, tQ = tmem + S::T_Q;
+      bool ok = mbar_wait(q_ready, 0, abort);
+      auto issue_pv = [&](int jj) {
+        const uint32_t base = smem_base + S::OFF_STAGE + (jj % S::NSTAGE) * S::STAGE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < kTok / 16; ++ks) {
+          const uint64_t bdesc = smem_desc(base + ks * 16 * 128, S::CH_BYTES, 1024, kSwizzle128B);
+          mma_bf16_ts(tO, tP + ks * 8, bdesc, IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(&empty[jj % S::NSTAGE]);
+      };
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j % S::NSTAGE;
+        if (!mbar_wait(&full[s], (j / S::NSTAGE) & 1, abort)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t base = smem_base + S::OFF_STAGE + s * S::STAGE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < S::QD / 16; ++ks) {
+          uint64_t bdesc;
+          if (ks < S::VD / 16) {
+            bdesc = smem_desc(base + (ks >> 2) * S::CH_BYTES + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+          } else {
+            const int rk = ks - S::VD / 16;
+            bdesc = smem_desc(base + S::NCH * S::CH_BYTES + rk * 32, 16, 512, kSwizzle64B);
+          }
+          mma_bf16_ts(tS, tQ + ks * 8, bdesc, IDESC_QK, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        if (j > 0) {
+          if (!mbar_wait(p_full, (j - 1) & 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(j - 1);
+        }
+      }
+      if (ok && n_tiles > 0) {
+        if (mbar_wait(p_full, (n_tiles - 1) & 1, abort)) {
+          tc_fence_after();
+          issue_pv(n_tiles - 1);
+        } else {
+          ok = false;
+        }
+      }
+      if (!ok) raise_abort(abort, status, kStatusTimeout);
+      // all issued tensor-core work must finish before TMEM is released
+      tc_commit(drain);
+      mbar_wait(drain, 0, no_abort);
+    }
+  } else {
+    // ------------------------------------------------------- softmax warps 0-3
+    const int t = threadIdx.x;  // head index == TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // Q slice -> TMEM (K order: latent columns of this CTA, then its rope columns)
+    {
+      uint32_t qv[16];
+      const bool live = t < H;
+      const uint32_t* ql = reinterpret_cast<const uint32_t*>(q_lat + ((int64_t)item.b * H + (live ? t : 0)) * R + rank * S::VD);
+      const uint32_t* qr = reinterpret_cast<const uint32_t*>(q_rope + ((int64_t)item.b * H + (live ? t : 0)) * P + rank * S::PD);
+#pragma unroll 1
+      for (int c = 0; c < S::QD / 32; ++c) {  // 16 columns (32 bf16) per chunk
+        const uint32_t* src = (c < S::VD / 32) ? ql + c * 16 : qr + (c - S::VD / 32) * 16;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          uint4 v = live ? *reinterpret_cast<const uint4*>(src + i) : make_uint4(0, 0, 0, 0);
+          qv[i] = v.x; qv[i + 1] = v.y; qv[i + 2] = v.z; qv[i + 3] = v.w;
+        }
+        tmem_st16(tmem + lane_off + S::T_Q + c * 16, qv);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(q_ready);
+    }
+
+    uint32_t peer_xch = 0, peer_xch_full = 0, peer_peer_free = 0;
+    if (NCTA == 2) {
+      const uint32_t peer = rank ^ 1u;
+      peer_xch = mapa_shared(smem_base + S::OFF_XCH + t * 256, peer);
+      peer_xch_full = mapa_shared(smem_u32(xch_full), peer);
+      peer_peer_free = mapa_shared(smem_u32(peer_free), peer);
+    }
+
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    const int tok0 = item.page0 * kTok;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, abort))) { ok = false; break; }
+      tc_fence_after();
+      float s[64];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tmem + lane_off + S::T_S, r0);
+        tmem_ld32(tmem + lane_off + S::T_S + 32, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(r0[i]);
+          s[32 + i] = __uint_as_float(r1[i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+
+      if (NCTA == 2) {
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait<true>(peer_free, (j - 1) & 1, abort))) { ok = false; break; }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int cc = c ^ (t & 15);
+          st_cluster_v4(peer_xch + cc * 16, s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
+        }
+        mbar_arrive_cluster(peer_xch_full);
+        if (!__all_sync(0xffffffffu, mbar_wait<true>(xch_full, j & 1, abort))) { ok = false; break; }
+        const float4* row = reinterpret_cast<const float4*>(xch + t * 64);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float4 v = row[c ^ (t & 15)];
+          s[4 * c] += v.x;
+          s[4 * c + 1] += v.y;
+          s[4 * c + 2] += v.z;
+          s[4 * c + 3] += v.w;
+        }
+        if (j + 1 < n_tiles) mbar_arrive_cluster(peer_peer_free);
+      }
+
+      const int tbase = tok0 + j * kTok;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float v = (tbase + i < item.tok_end) ? s[i] * scale_log2 : -INFINITY;
+        s[i] = v;
+        mt = fmaxf(mt, v);
+      }
+      float factor = 1.0f;
+      bool rescale = false;
+      if (mt > m_run + kLazyRescale) {
+        factor = fast_exp2(m_run - mt);
+        m_run = mt;
+        rescale = (j > 0);
+      }
+      uint32_t pk[32];
+      float psum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t w = pack_bf16x2(fast_exp2(s[2 * i] - m_run), fast_exp2(s[2 * i + 1] - m_run));
+        pk[i] = w;
+        psum += bf16lo_to_f32(w) + bf16hi_to_f32(w);
+      }
+      l_run = l_run * factor + psum;
+      if (j > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort))) { ok = false; break; }
+        tc_fence_after();
+      }
+      // tcgen05.ld/st are warp-collective: rescale the whole warp's rows when any
+      // head of the warp needs it (factor is 1 for the others)
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < S::VD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st32(tmem + lane_off + S::T_O + c * 32, o);
+        }
+      }
+      tmem_st32(tmem + lane_off + S::T_P, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (n_tiles - 1) & 1, abort))) ok = false;
+    const bool live = t < H;
+    if (!ok) {
+      raise_abort(abort, status, kStatusTimeout);
+    } else {
+      tc_fence_after();
+      if (item.partial < 0) {
+        const float inv = 1.0f / l_run;
+        __nv_bfloat16* dst = out + ((int64_t)item.b * H + (live ? t : 0)) * R + rank * S::VD;
+#pragma unroll 1
+        for (int c = 0; c < S::VD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
+          tmem_ld_wait();
+          uint32_t pkd[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pkd[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          }
+        }
+      } else {
+        float* dst = ws_o + ((int64_t)item.partial * kHeadsPad + t) * R + rank * S::VD;
+#pragma unroll 1
+        for (int c = 0; c < S::VD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
+          tmem_ld_wait();
+          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                  __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+          }
+        }
+        if (rank == 0 && live) ws_ml[(int64_t)item.partial * kHeadsPad + t] = make_float2(m_run, l_run);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (NCTA == 2) cluster_sync();  // no CTA leaves while its peer may still address its smem
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::T_COLS);
+  }
+}
+
+// Merge split-KV partials: out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i.
+template <int R>
+__global__ void __launch_bounds__(128) mla_combine_kernel(const MlaCombine* __restrict__ list, int H,
+                                                          const float* __restrict__ ws_o,
+                                                          const float2* __restrict__ ws_ml,
+                                                          __nv_bfloat16* __restrict__ out) {
+  const MlaCombine cmb = list[blockIdx.x];
+  const int h = blockIdx.y;
+  float M = -INFINITY;
+  for (int i = 0; i < cmb.n; ++i) M = fmaxf(M, ws_ml[(int64_t)(cmb.first + i) * kHeadsPad + h].x);
+  float den = 0.0f;
+  constexpr int PER = R / 128;
+  float acc[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) acc[k] = 0.0f;
+  for (int i = 0; i < cmb.n; ++i) {
+    const float2 ml = ws_ml[(int64_t)(cmb.first + i) * kHeadsPad + h];
+    const float w = exp2f(ml.x - M);
+    den += w * ml.y;
+    const float* o = ws_o + ((int64_t)(cmb.first + i) * kHeadsPad + h) * R;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) acc[k] += w * o[threadIdx.x + 128 * k];
+  }
+  const float inv = 1.0f / den;
+  __nv_bfloat16* dst = out + ((int64_t)cmb.b * H + h) * R;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) dst[threadIdx.x + 128 * k] = __float2bfloat16_rn(acc[k] * inv);
+}
+
+// Split each sequence into page runs so that the clusters of one wave finish
+// together: candidate caps are scored by a longest-first list schedule over
+// the available cluster slots (cost = pages + a fixed per-item overhead).
+void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>* items,
+                std::vector<MlaCombine>* combines, int* n_partial) {
+  std::vector<int> pages(B);
+  long total = 0;
+  int maxp = 1;
+  for (int b = 0; b < B; ++b) {
+    pages[b] = (seq_lens[b] + kTok - 1) / kTok;
+    total += pages[b];
+    maxp = std::max(maxp, pages[b]);
+  }
+  const double overhead = 3.0;  // pages-equivalent cost of an item's setup and partial write
+  int best_cap = std::min(maxp, kMaxItemPages);
+  double best_cost = 1e300;
+  for (int cap = 1; cap <= std::min(maxp, kMaxItemPages); cap = cap < 8 ? cap + 1 : cap + cap / 8) {
+    std::vector<double> costs;
+    for (int b = 0; b < B; ++b) {
+      const int n = (pages[b] + cap - 1) / cap;
+      for (int i = 0; i < n; ++i) {
+        const int np = (int)((int64_t)(i + 1) * pages[b] / n - (int64_t)i * pages[b] / n);
+        costs.push_back(np + overhead + (n > 1 ? overhead : 0));
+      }
+    }
+    std::sort(costs.begin(), costs.end(), std::greater<double>());
+    std::priority_queue<double, std::vector<double>, std::greater<double>> q;
+    for (int i = 0; i < slots; ++i) q.push(0.0);
+    double makespan = 0.0;
+    for (double c : costs) {
+      double t0 = q.top();
+      q.pop();
+      q.push(t0 + c);
+      makespan = std::max(makespan, t0 + c);
+    }
+    if (makespan < best_cost - 1e-9) {
+      best_cost = makespan;
+      best_cap = cap;
+    }
+  }
+  (void)total;
+  items->clear();
+  combines->clear();
+  int slot = 0;
+  for (int b = 0; b < B; ++b) {
+    const int n = (pages[b] + best_cap - 1) / best_cap;
+    if (n > 1) combines->push_back(MlaCombine{b, slot, n});
+    for (int i = 0; i < n; ++i) {
+      const int p0 = (int)((int64_t)i * pages[b] / n), p1 = (int)((int64_t)(i + 1) * pages[b] / n);
+      const int end = std::min(seq_lens[b], p1 * kTok);
+      items->push_back(MlaItem{b, p0, p1 - p0, end, n > 1 ? slot++ : -1});
+    }
+  }
+  // longest items first so the block scheduler back-fills with short ones
+  std::stable_sort(items->begin(), items->end(),
+                   [](const MlaItem& a, const MlaItem& b) { return a.npages > b.npages; });
+  *n_partial = slot;
+}
+
+template <int R, int P, int NCTA>
+int launch_mla(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
+               const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B, int H, float scale,
+               void* out) {
+  using S = MlaShape<R, P, NCTA>;
+  std::vector<MlaItem> items;
+  std::vector<MlaCombine> combines;
+  int n_partial = 0;
+  plan_items(seq_lens, B, std::max(1, ctx->sm_count / NCTA), &items, &combines, &n_partial);
+
+  // workspace: items | combines | partial O | partial (m, l)
+  auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t off_items = 0;
+  const size_t off_comb = align(off_items + items.size() * sizeof(MlaItem));
+  const size_t off_o = align(off_comb + std::max<size_t>(1, combines.size()) * sizeof(MlaCombine));
+  const size_t off_ml = align(off_o + (size_t)n_partial * kHeadsPad * R * sizeof(float));
+  const size_t need = align(off_ml + (size_t)n_partial * kHeadsPad * sizeof(float2));
+  int rc = ensure_workspace(ctx, need);
+  if (rc != DSB_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(ws + off_items, items.data(), items.size() * sizeof(MlaItem),
+                                    cudaMemcpyHostToDevice, ctx->stream));
+  if (!combines.empty())
+    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(ws + off_comb, combines.data(), combines.size() * sizeof(MlaCombine),
+                                      cudaMemcpyHostToDevice, ctx->stream));
+
+  CUtensorMap map_v, map_r;
+  const uint64_t rows = (uint64_t)n_blocks * kTok;
+  rc = make_tmap_2d(ctx, &map_v, kv_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R + P, rows, (R + P) * 2, 64, kTok,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != DSB_OK) return rc;
+  rc = make_tmap_2d(ctx, &map_r, kv_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R + P, rows, (R + P) * 2, S::PD, kTok,
+                    CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc != DSB_OK) return rc;
+
+  auto kern = mla_decode_kernel<R, P, NCTA>;
+  DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(items.size() * NCTA));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = NCTA;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  DSB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, map_v, map_r, static_cast<const __nv_bfloat16*>(q_lat),
+                                       static_cast<const __nv_bfloat16*>(q_rope), block_table, max_blocks,
+                                       reinterpret_cast<const MlaItem*>(ws + off_items), H, scale_log2,
+                                       static_cast<__nv_bfloat16*>(out), reinterpret_cast<float*>(ws + off_o),
+                                       reinterpret_cast<float2*>(ws + off_ml), ctx->d_status));
+  ctx->stats.kernel_launches++;
+  if (!combines.empty()) {
+    mla_combine_kernel<R><<<dim3((unsigned)combines.size(), (unsigned)H), 128, 0, ctx->stream>>>(
+        reinterpret_cast<const MlaCombine*>(ws + off_comb), H, reinterpret_cast<const float*>(ws + off_o),
+        reinterpret_cast<const float2*>(ws + off_ml), static_cast<__nv_bfloat16*>(out));
+    DSB_CUDA_TRY(ctx, cudaGetLastError());
+    ctx->stats.kernel_launches++;
+  }
+  ctx->stats.mla_calls++;
+  ctx->stats.mla_work_items += items.size();
+  ctx->stats.mla_partials += (uint64_t)n_partial;
+  return DSB_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
+                              int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                              const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                              void* out_lat) {
+  using namespace dsb;
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (q_lat == nullptr || q_rope == nullptr || kv_cache == nullptr || block_table == nullptr || seq_lens == nullptr ||
+      out_lat == nullptr)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: null pointer argument");
+  if (B <= 0 || H <= 0 || H > kHeadsPad || n_blocks <= 0 || max_blocks <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: bad sizes B=%d H=%d n_blocks=%lld max_blocks=%d", B, H,
+                (long long)n_blocks, max_blocks);
+  if (block_size != kTok) return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: block_size must be 64");
+  for (int b = 0; b < B; ++b) {
+    if (seq_lens[b] < 1 || seq_lens[b] > (int64_t)max_blocks * kTok)
+      return fail(ctx, DSB_EINVAL, "dsb_mla_decode: seq_lens[%d]=%d outside [1, max_blocks*64]", b, seq_lens[b]);
+  }
+  if ((reinterpret_cast<uintptr_t>(q_lat) | reinterpret_cast<uintptr_t>(q_rope) |
+       reinterpret_cast<uintptr_t>(out_lat) | reinterpret_cast<uintptr_t>(kv_cache)) & 15u)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: pointers must be 16-byte aligned");
+  if (R == 512 && P == 64)
+    return launch_mla<512, 64, 2>(ctx, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, seq_lens, B, H,
+                                  softmax_scale, out_lat);
+  if (R == 128 && P == 32)
+    return launch_mla<128, 32, 1>(ctx, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, seq_lens, B, H,
+                                  softmax_scale, out_lat);
+  return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: (R, P) = (%d, %d) not supported", R, P);
+}

@@ -1,0 +1,118 @@
+/*
+ * dsb.h - C ABI of libdsb.so, the B200 (sm_100a) decode hot path of
+ * deepseek_cpp_infer.
+ *
+ * The reference crosses from its C++ model code into the GPU through the free
+ * functions of ds::rt::cuda (include/ds/models/deepseek/cuda_backend.h:49-80)
+ * and the kernel launchers of ds::rt::cuda::kernels
+ * (include/ds/models/deepseek/cuda_kernels.h:10-25).  This header replaces
+ * that boundary with plain C: opaque handles, raw pointers and sizes, no C++
+ * or torch types.  Each entry point names the reference interface it stands
+ * in for.
+ *
+ * Conventions
+ *  - Every function returns DSB_OK (0) or a DSB_E* code; dsb_last_error()
+ *    gives the message.  Nothing throws across the boundary (the reference's
+ *    *_to_slot functions return bool for the same reason,
+ *    cuda_backend.cpp:782-807).
+ *  - Device pointers are raw CUDA device addresses (bf16 = 16-bit bfloat16
+ *    payload).  Work is enqueued asynchronously on the context stream;
+ *    dsb_sync() waits for it and reports kernel-side errors.
+ *  - One context per GPU and per host thread (the reference keeps one global
+ *    context on device 0, cuda_backend.cpp:565-568; here contexts are
+ *    independent objects).
+ *  - There is no CPU fallback: a call that cannot run on the GPU fails.
+ */
+#ifndef DSB_DSB_H_
+#define DSB_DSB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSB_API __attribute__((visibility("default")))
+#else
+#define DSB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSB_OK 0
+#define DSB_EINVAL 1       /* bad argument, shape or size */
+#define DSB_ECUDA 2        /* a CUDA runtime/driver call failed */
+#define DSB_ENOMEM 3       /* device allocation failed */
+#define DSB_ETIMEOUT 4     /* a kernel's bounded wait ran out (device status word) */
+#define DSB_EUNSUPPORTED 5 /* shape not covered by the sm_100a kernels */
+
+typedef struct dsb_ctx dsb_ctx;
+
+/* Per-context counters; replaces the process-global CudaStats
+ * (cuda_backend.h:26-45, cuda_backend.cpp:573) as the "really ran on the GPU"
+ * evidence. */
+typedef struct dsb_stats {
+  uint64_t kernel_launches; /* kernels enqueued by this context */
+  uint64_t mla_calls;
+  uint64_t mla_work_items; /* cluster work items summed over calls */
+  uint64_t mla_partials;   /* work items that wrote a split-KV partial */
+  uint64_t workspace_bytes;
+} dsb_stats;
+
+/* Library version (major*10000 + minor*100 + patch). */
+DSB_API int dsb_version(void);
+
+/* Create / destroy a context bound to CUDA device `device`.
+ * Replaces ensure_initialized / create_executor_state / destroy_executor_state
+ * (cuda_backend.h:49-56). */
+DSB_API int dsb_ctx_create(int device, dsb_ctx** out);
+DSB_API int dsb_ctx_destroy(dsb_ctx* ctx);
+
+/* Use `stream` (a cudaStream_t) for all work of the context; NULL restores
+ * the context's own stream.  The caller keeps ownership of `stream`. */
+DSB_API int dsb_ctx_set_stream(dsb_ctx* ctx, void* stream);
+DSB_API void* dsb_ctx_stream(dsb_ctx* ctx);
+
+/* Message of the last failed call on this context ("" when none). */
+DSB_API const char* dsb_last_error(const dsb_ctx* ctx);
+
+/* Wait for the context stream, then read and clear the device status word:
+ * DSB_ETIMEOUT if a kernel's bounded wait ran out since the last dsb_sync. */
+DSB_API int dsb_sync(dsb_ctx* ctx);
+
+/* Copy the context counters (replaces stats(), cuda_backend.h:52). */
+DSB_API int dsb_get_stats(const dsb_ctx* ctx, dsb_stats* out);
+DSB_API int dsb_reset_stats(dsb_ctx* ctx); /* replaces reset_stats(), cuda_backend.h:51 */
+
+/*
+ * Absorbed-weight MLA decode attention over a paged latent cache: one query
+ * token per sequence, all heads.
+ *
+ * Replaces the per-head attention loop of mla_decode_to_slot
+ * (src/models/deepseek/cuda_backend.cpp:953-991: ds_scores_kernel,
+ * ds_softmax_kernel, ds_weighted_sum_kernel per head) and of mla_decode_step
+ * (src/models/deepseek/mla.cpp:86-116).  With q_lat = W_UK^T q_nope the
+ * reference's scores q.k/sqrt(nope+rope) equal [q_lat | q_rope].[c | kr] *
+ * softmax_scale, and its per-head output equals W_UV * out_lat, so this call
+ * returns the latent output out_lat.
+ *
+ *  q_lat        bf16 [B, H, R]     absorbed nope query
+ *  q_rope       bf16 [B, H, P]     rotated rope query
+ *  kv_cache     bf16 [n_blocks, block_size, R + P]   rows [c | kr]
+ *  block_table  int32 device [B, max_blocks]  page ids of each sequence
+ *  seq_lens     int32 HOST [B]  tokens in the cache per sequence (>= 1);
+ *               used to plan the split-KV work on the host
+ *  out_lat      bf16 [B, H, R]  softmax(q.k * scale) . c
+ * Supported: block_size 64, (R, P) in {(512, 64), (128, 32)}, 1 <= H <= 128.
+ * Rows of a page past a sequence's length must hold finite values (the
+ * paged-cache pool of dsb is zero-filled at creation).
+ */
+DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
+                   int block_size, const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B, int H,
+                   int R, int P, float softmax_scale, void* out_lat);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSB_DSB_H_ */
