@@ -54,6 +54,14 @@ _PROTOS = [
     ("dsb_sync", ctypes.c_int, [ctypes.c_void_p]),
     ("dsb_get_stats", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(Stats)]),
     ("dsb_reset_stats", ctypes.c_int, [ctypes.c_void_p]),
+    ("dsb_mla_plan_create", ctypes.c_int,
+     [ctypes.c_void_p, _c_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_mla_plan_destroy", ctypes.c_int, [ctypes.c_void_p]),
+    ("dsb_mla_plan_info", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
+    ("dsb_mla_decode_planned", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+      ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -140,6 +148,22 @@ class Context:
     def reset_stats(self):
         self._check(self._l.dsb_reset_stats(self.h))
 
+    def mla_plan(self, seq_lens, H, R, P, block_size=64):
+        """dsb_mla_plan_create: a reusable split-KV plan for these lengths."""
+        B = len(seq_lens)
+        lens = (ctypes.c_int32 * B)(*[int(x) for x in seq_lens])
+        h = ctypes.c_void_p()
+        self._check(self._l.dsb_mla_plan_create(self.h, lens, B, H, R, P, block_size, ctypes.byref(h)))
+        return MlaPlan(self, h, [int(x) for x in seq_lens])
+
+    def mla_decode_planned(self, plan, q_lat, q_rope, kv_cache, block_table, softmax_scale, out):
+        self._check(
+            self._l.dsb_mla_decode_planned(
+                self.h, plan.h, _ptr(q_lat), _ptr(q_rope), _ptr(kv_cache), kv_cache.shape[0], _ptr(block_table),
+                block_table.shape[1], float(softmax_scale), _ptr(out),
+            )
+        )
+
     def mla_decode(self, q_lat, q_rope, kv_cache, block_table, seq_lens, softmax_scale, out, block_size=64):
         """Absorbed MLA decode (dsb_mla_decode).  q_lat [B,H,R], q_rope [B,H,P],
         kv_cache [n_blocks, 64, R+P] bf16 on the device; block_table int32
@@ -154,3 +178,28 @@ class Context:
                 block_table.shape[1], lens, B, H, R, P, float(softmax_scale), _ptr(out),
             )
         )
+
+
+class MlaPlan:
+    """A dsb_mla_plan (released with close() or on garbage collection)."""
+
+    def __init__(self, ctx: Context, h, seq_lens):
+        self.ctx = ctx
+        self.h = h
+        self.seq_lens = seq_lens
+
+    def info(self):
+        n_items, n_part = ctypes.c_int(), ctypes.c_int()
+        self.ctx._check(self.ctx._l.dsb_mla_plan_info(self.h, ctypes.byref(n_items), ctypes.byref(n_part)))
+        return {"n_items": n_items.value, "n_partial": n_part.value}
+
+    def close(self):
+        if self.h:
+            self.ctx._l.dsb_mla_plan_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -47,6 +47,25 @@ int ensure_workspace(dsb_ctx* ctx, size_t bytes) {
   return DSB_OK;
 }
 
+int ensure_aux(dsb_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->aux_bytes) return DSB_OK;
+  size_t grow = ctx->aux_bytes ? ctx->aux_bytes : (size_t)64 << 10;
+  while (grow < bytes) grow *= 2;
+  if (ctx->aux != nullptr) {
+    DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    DSB_CUDA_TRY(ctx, cudaFree(ctx->aux));
+    ctx->aux = nullptr;
+    ctx->aux_bytes = 0;
+  }
+  cudaError_t e = cudaMalloc(&ctx->aux, grow);
+  if (e != cudaSuccess) {
+    ctx->aux = nullptr;
+    return fail(ctx, DSB_ENOMEM, "aux cudaMalloc(%zu): %s", grow, cudaGetErrorString(e));
+  }
+  ctx->aux_bytes = grow;
+  return DSB_OK;
+}
+
 namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -136,6 +155,7 @@ int dsb_ctx_destroy(dsb_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;

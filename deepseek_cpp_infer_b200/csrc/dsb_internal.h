@@ -18,6 +18,8 @@ struct dsb_ctx {
   int* d_status = nullptr;  // device status word written by bounded waits
   void* ws = nullptr;       // reusable device workspace
   size_t ws_bytes = 0;
+  void* aux = nullptr;      // reusable device buffer for per-call plans
+  size_t aux_bytes = 0;
   std::string last_error;
   dsb_stats stats{};
 };
@@ -36,6 +38,8 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 
 // Ensure ctx->ws holds at least `bytes`; grows (never shrinks) the buffer.
 int ensure_workspace(dsb_ctx* ctx, size_t bytes);
+// Same for ctx->aux (small per-call metadata such as work lists).
+int ensure_aux(dsb_ctx* ctx, size_t bytes);
 
 // 2D bf16/u8/f32 tiled tensor map over a row-major matrix [rows, cols] with
 // row pitch `pitch_bytes`; box = box_cols x box_rows; swizzle per CU enum.

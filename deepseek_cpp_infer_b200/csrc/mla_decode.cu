@@ -36,6 +36,16 @@
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
 
+// A split-KV work plan for one set of sequence lengths (see plan_items).
+struct dsb_mla_plan {
+  int B = 0, H = 0, R = 0, P = 0;
+  int n_items = 0, n_combines = 0, n_partial = 0;
+  int max_len = 0;
+  void* d_items = nullptr;     // MlaItem[n_items] on the device
+  void* d_combines = nullptr;  // MlaCombine[n_combines] on the device
+  int device = 0;
+};
+
 namespace dsb {
 namespace {
 
@@ -444,28 +454,40 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaCombine* __re
 }
 
 // Split each sequence into page runs so that the clusters of one wave finish
-// together: candidate caps are scored by a longest-first list schedule over
-// the available cluster slots (cost = pages + a fixed per-item overhead).
+// together.  A handful of candidate run lengths (caps) are scored by a
+// longest-first list schedule over the available cluster slots with cost =
+// pages + a fixed per-item overhead (+ the partial write and merge of split
+// sequences); the cheapest cap wins.
 void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>* items,
                 std::vector<MlaCombine>* combines, int* n_partial) {
   std::vector<int> pages(B);
-  long total = 0;
+  int64_t total = 0;
   int maxp = 1;
   for (int b = 0; b < B; ++b) {
     pages[b] = (seq_lens[b] + kTok - 1) / kTok;
     total += pages[b];
     maxp = std::max(maxp, pages[b]);
   }
-  const double overhead = 3.0;  // pages-equivalent cost of an item's setup and partial write
-  int best_cap = std::min(maxp, kMaxItemPages);
+  const double overhead = 2.0;  // pages-equivalent cost of an item's setup
+  const double split_cost = 2.0;  // partial write + merge of a split sequence
+  std::vector<int> caps;
+  caps.push_back(std::min(maxp, kMaxItemPages));
+  for (int k = 1; k <= 8; ++k) {
+    const int64_t c = (total + (int64_t)k * slots - 1) / ((int64_t)k * slots);
+    caps.push_back((int)std::max<int64_t>(2, std::min<int64_t>(c, kMaxItemPages)));
+  }
+  std::sort(caps.begin(), caps.end());
+  caps.erase(std::unique(caps.begin(), caps.end()), caps.end());
+  int best_cap = caps.back();
   double best_cost = 1e300;
-  for (int cap = 1; cap <= std::min(maxp, kMaxItemPages); cap = cap < 8 ? cap + 1 : cap + cap / 8) {
-    std::vector<double> costs;
+  std::vector<double> costs;
+  for (int cap : caps) {
+    costs.clear();
     for (int b = 0; b < B; ++b) {
       const int n = (pages[b] + cap - 1) / cap;
       for (int i = 0; i < n; ++i) {
         const int np = (int)((int64_t)(i + 1) * pages[b] / n - (int64_t)i * pages[b] / n);
-        costs.push_back(np + overhead + (n > 1 ? overhead : 0));
+        costs.push_back(np + overhead + (n > 1 ? split_cost : 0.0));
       }
     }
     std::sort(costs.begin(), costs.end(), std::greater<double>());
@@ -473,7 +495,7 @@ void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>*
     for (int i = 0; i < slots; ++i) q.push(0.0);
     double makespan = 0.0;
     for (double c : costs) {
-      double t0 = q.top();
+      const double t0 = q.top();
       q.pop();
       q.push(t0 + c);
       makespan = std::max(makespan, t0 + c);
@@ -483,7 +505,6 @@ void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>*
       best_cap = cap;
     }
   }
-  (void)total;
   items->clear();
   combines->clear();
   int slot = 0;
@@ -503,30 +524,15 @@ void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>*
 }
 
 template <int R, int P, int NCTA>
-int launch_mla(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
-               const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B, int H, float scale,
-               void* out) {
+int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const void* q_rope, const void* kv_cache,
+               int64_t n_blocks, const int32_t* block_table, int max_blocks, float scale, void* out) {
   using S = MlaShape<R, P, NCTA>;
-  std::vector<MlaItem> items;
-  std::vector<MlaCombine> combines;
-  int n_partial = 0;
-  plan_items(seq_lens, B, std::max(1, ctx->sm_count / NCTA), &items, &combines, &n_partial);
-
-  // workspace: items | combines | partial O | partial (m, l)
   auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
-  const size_t off_items = 0;
-  const size_t off_comb = align(off_items + items.size() * sizeof(MlaItem));
-  const size_t off_o = align(off_comb + std::max<size_t>(1, combines.size()) * sizeof(MlaCombine));
-  const size_t off_ml = align(off_o + (size_t)n_partial * kHeadsPad * R * sizeof(float));
-  const size_t need = align(off_ml + (size_t)n_partial * kHeadsPad * sizeof(float2));
+  const size_t off_ml = align((size_t)plan->n_partial * kHeadsPad * R * sizeof(float));
+  const size_t need = align(off_ml + (size_t)plan->n_partial * kHeadsPad * sizeof(float2));
   int rc = ensure_workspace(ctx, need);
   if (rc != DSB_OK) return rc;
   uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
-  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(ws + off_items, items.data(), items.size() * sizeof(MlaItem),
-                                    cudaMemcpyHostToDevice, ctx->stream));
-  if (!combines.empty())
-    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(ws + off_comb, combines.data(), combines.size() * sizeof(MlaCombine),
-                                      cudaMemcpyHostToDevice, ctx->stream));
 
   CUtensorMap map_v, map_r;
   const uint64_t rows = (uint64_t)n_blocks * kTok;
@@ -538,9 +544,13 @@ int launch_mla(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* 
   if (rc != DSB_OK) return rc;
 
   auto kern = mla_decode_kernel<R, P, NCTA>;
-  DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
+  static bool attr_set = false;  // per template instance
+  if (!attr_set) {
+    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
+    attr_set = true;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(items.size() * NCTA));
+  cfg.gridDim = dim3((unsigned)(plan->n_items * NCTA));
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = S::SMEM_BYTES;
   cfg.stream = ctx->stream;
@@ -554,25 +564,114 @@ int launch_mla(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* 
   const float scale_log2 = scale * 1.4426950408889634f;
   DSB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, map_v, map_r, static_cast<const __nv_bfloat16*>(q_lat),
                                        static_cast<const __nv_bfloat16*>(q_rope), block_table, max_blocks,
-                                       reinterpret_cast<const MlaItem*>(ws + off_items), H, scale_log2,
-                                       static_cast<__nv_bfloat16*>(out), reinterpret_cast<float*>(ws + off_o),
+                                       static_cast<const MlaItem*>(plan->d_items), plan->H, scale_log2,
+                                       static_cast<__nv_bfloat16*>(out), reinterpret_cast<float*>(ws),
                                        reinterpret_cast<float2*>(ws + off_ml), ctx->d_status));
   ctx->stats.kernel_launches++;
-  if (!combines.empty()) {
-    mla_combine_kernel<R><<<dim3((unsigned)combines.size(), (unsigned)H), 128, 0, ctx->stream>>>(
-        reinterpret_cast<const MlaCombine*>(ws + off_comb), H, reinterpret_cast<const float*>(ws + off_o),
+  if (plan->n_combines > 0) {
+    mla_combine_kernel<R><<<dim3((unsigned)plan->n_combines, (unsigned)plan->H), 128, 0, ctx->stream>>>(
+        static_cast<const MlaCombine*>(plan->d_combines), plan->H, reinterpret_cast<const float*>(ws),
         reinterpret_cast<const float2*>(ws + off_ml), static_cast<__nv_bfloat16*>(out));
     DSB_CUDA_TRY(ctx, cudaGetLastError());
     ctx->stats.kernel_launches++;
   }
   ctx->stats.mla_calls++;
-  ctx->stats.mla_work_items += items.size();
-  ctx->stats.mla_partials += (uint64_t)n_partial;
+  ctx->stats.mla_work_items += (uint64_t)plan->n_items;
+  ctx->stats.mla_partials += (uint64_t)plan->n_partial;
   return DSB_OK;
 }
 
 }  // namespace
 }  // namespace dsb
+
+extern "C" int dsb_mla_plan_create(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P,
+                                   int block_size, dsb_mla_plan** out) {
+  using namespace dsb;
+  if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
+  *out = nullptr;
+  if (seq_lens == nullptr || B <= 0 || H <= 0 || H > kHeadsPad)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_plan_create: bad sizes B=%d H=%d", B, H);
+  if (block_size != kTok) return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_plan_create: block_size must be 64");
+  if (!((R == 512 && P == 64) || (R == 128 && P == 32)))
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_plan_create: (R, P) = (%d, %d) not supported", R, P);
+  int max_len = 0;
+  for (int b = 0; b < B; ++b) {
+    if (seq_lens[b] < 1) return fail(ctx, DSB_EINVAL, "dsb_mla_plan_create: seq_lens[%d]=%d < 1", b, seq_lens[b]);
+    max_len = std::max(max_len, seq_lens[b]);
+  }
+  const int nct = (R == 512) ? 2 : 1;
+  std::vector<MlaItem> items;
+  std::vector<MlaCombine> combines;
+  int n_partial = 0;
+  plan_items(seq_lens, B, std::max(1, ctx->sm_count / nct), &items, &combines, &n_partial);
+  auto* plan = new dsb_mla_plan();
+  plan->B = B;
+  plan->H = H;
+  plan->R = R;
+  plan->P = P;
+  plan->n_items = (int)items.size();
+  plan->n_combines = (int)combines.size();
+  plan->n_partial = n_partial;
+  plan->max_len = max_len;
+  plan->device = ctx->device;
+  cudaError_t e = cudaMalloc(&plan->d_items, items.size() * sizeof(MlaItem) + 256 +
+                                                 std::max<size_t>(1, combines.size()) * sizeof(MlaCombine));
+  if (e != cudaSuccess) {
+    delete plan;
+    return fail(ctx, DSB_ENOMEM, "dsb_mla_plan_create: %s", cudaGetErrorString(e));
+  }
+  plan->d_combines = static_cast<uint8_t*>(plan->d_items) + ((items.size() * sizeof(MlaItem) + 255) & ~size_t(255));
+  e = cudaMemcpyAsync(plan->d_items, items.data(), items.size() * sizeof(MlaItem), cudaMemcpyHostToDevice,
+                      ctx->stream);
+  if (e == cudaSuccess && !combines.empty())
+    e = cudaMemcpyAsync(plan->d_combines, combines.data(), combines.size() * sizeof(MlaCombine),
+                        cudaMemcpyHostToDevice, ctx->stream);
+  // pageable-source async copies are staged before they return, so the host
+  // vectors may die here; the stream orders the copies before any kernel
+  if (e != cudaSuccess) {
+    cudaFree(plan->d_items);
+    delete plan;
+    return fail(ctx, DSB_ECUDA, "dsb_mla_plan_create: %s", cudaGetErrorString(e));
+  }
+  *out = plan;
+  return DSB_OK;
+}
+
+extern "C" int dsb_mla_plan_destroy(dsb_mla_plan* plan) {
+  if (plan == nullptr) return DSB_OK;
+  cudaSetDevice(plan->device);
+  cudaFree(plan->d_items);
+  delete plan;
+  return DSB_OK;
+}
+
+extern "C" int dsb_mla_plan_info(const dsb_mla_plan* plan, int* n_items, int* n_partial) {
+  if (plan == nullptr) return DSB_EINVAL;
+  if (n_items) *n_items = plan->n_items;
+  if (n_partial) *n_partial = plan->n_partial;
+  return DSB_OK;
+}
+
+extern "C" int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const void* q_rope,
+                                      const void* kv_cache, int64_t n_blocks, const int32_t* block_table,
+                                      int max_blocks, float softmax_scale, void* out_lat) {
+  using namespace dsb;
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (plan == nullptr || q_lat == nullptr || q_rope == nullptr || kv_cache == nullptr || block_table == nullptr ||
+      out_lat == nullptr)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: null pointer argument");
+  if (n_blocks <= 0 || max_blocks <= 0 || (int64_t)max_blocks * kTok < plan->max_len)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: n_blocks=%lld, max_blocks=%d cannot hold length %d",
+                (long long)n_blocks, max_blocks, plan->max_len);
+  if ((reinterpret_cast<uintptr_t>(q_lat) | reinterpret_cast<uintptr_t>(q_rope) |
+       reinterpret_cast<uintptr_t>(out_lat) | reinterpret_cast<uintptr_t>(kv_cache)) & 15u)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: pointers must be 16-byte aligned");
+  if (plan->R == 512)
+    return launch_mla<512, 64, 2>(ctx, plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks,
+                                  softmax_scale, out_lat);
+  return launch_mla<128, 32, 1>(ctx, plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, softmax_scale,
+                                out_lat);
+}
 
 extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
                               int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
@@ -580,25 +679,42 @@ extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rop
                               void* out_lat) {
   using namespace dsb;
   if (ctx == nullptr) return DSB_EINVAL;
-  if (q_lat == nullptr || q_rope == nullptr || kv_cache == nullptr || block_table == nullptr || seq_lens == nullptr ||
-      out_lat == nullptr)
-    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: null pointer argument");
-  if (B <= 0 || H <= 0 || H > kHeadsPad || n_blocks <= 0 || max_blocks <= 0)
-    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: bad sizes B=%d H=%d n_blocks=%lld max_blocks=%d", B, H,
-                (long long)n_blocks, max_blocks);
+  if (seq_lens == nullptr || B <= 0 || H <= 0 || H > kHeadsPad)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: bad sizes B=%d H=%d", B, H);
   if (block_size != kTok) return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: block_size must be 64");
+  if (!((R == 512 && P == 64) || (R == 128 && P == 32)))
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: (R, P) = (%d, %d) not supported", R, P);
+  int max_len = 0;
   for (int b = 0; b < B; ++b) {
     if (seq_lens[b] < 1 || seq_lens[b] > (int64_t)max_blocks * kTok)
       return fail(ctx, DSB_EINVAL, "dsb_mla_decode: seq_lens[%d]=%d outside [1, max_blocks*64]", b, seq_lens[b]);
+    max_len = std::max(max_len, seq_lens[b]);
   }
-  if ((reinterpret_cast<uintptr_t>(q_lat) | reinterpret_cast<uintptr_t>(q_rope) |
-       reinterpret_cast<uintptr_t>(out_lat) | reinterpret_cast<uintptr_t>(kv_cache)) & 15u)
-    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: pointers must be 16-byte aligned");
-  if (R == 512 && P == 64)
-    return launch_mla<512, 64, 2>(ctx, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, seq_lens, B, H,
-                                  softmax_scale, out_lat);
-  if (R == 128 && P == 32)
-    return launch_mla<128, 32, 1>(ctx, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, seq_lens, B, H,
-                                  softmax_scale, out_lat);
-  return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: (R, P) = (%d, %d) not supported", R, P);
+  // plan into the context's reusable buffer: stream order protects reuse
+  std::vector<MlaItem> items;
+  std::vector<MlaCombine> combines;
+  int n_partial = 0;
+  plan_items(seq_lens, B, std::max(1, ctx->sm_count / (R == 512 ? 2 : 1)), &items, &combines, &n_partial);
+  const size_t off_comb = (items.size() * sizeof(MlaItem) + 255) & ~size_t(255);
+  int rc = ensure_aux(ctx, off_comb + std::max<size_t>(1, combines.size()) * sizeof(MlaCombine));
+  if (rc != DSB_OK) return rc;
+  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->aux, items.data(), items.size() * sizeof(MlaItem), cudaMemcpyHostToDevice,
+                                    ctx->stream));
+  if (!combines.empty())
+    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(static_cast<uint8_t*>(ctx->aux) + off_comb, combines.data(),
+                                      combines.size() * sizeof(MlaCombine), cudaMemcpyHostToDevice, ctx->stream));
+  dsb_mla_plan plan;
+  plan.B = B;
+  plan.H = H;
+  plan.R = R;
+  plan.P = P;
+  plan.n_items = (int)items.size();
+  plan.n_combines = (int)combines.size();
+  plan.n_partial = n_partial;
+  plan.max_len = max_len;
+  plan.d_items = ctx->aux;
+  plan.d_combines = static_cast<uint8_t*>(ctx->aux) + off_comb;
+  plan.device = ctx->device;
+  return dsb_mla_decode_planned(ctx, &plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, softmax_scale,
+                                out_lat);
 }

@@ -96,20 +96,38 @@ DSB_API int dsb_reset_stats(dsb_ctx* ctx); /* replaces reset_stats(), cuda_backe
  * softmax_scale, and its per-head output equals W_UV * out_lat, so this call
  * returns the latent output out_lat.
  *
+ * Work is split into runs of whole 64-token pages ("work items") planned on
+ * the host from the sequence lengths.  A plan depends only on (seq_lens, H,
+ * R, P) and is reused by every layer of a decode step.
+ *
  *  q_lat        bf16 [B, H, R]     absorbed nope query
  *  q_rope       bf16 [B, H, P]     rotated rope query
  *  kv_cache     bf16 [n_blocks, block_size, R + P]   rows [c | kr]
  *  block_table  int32 device [B, max_blocks]  page ids of each sequence
- *  seq_lens     int32 HOST [B]  tokens in the cache per sequence (>= 1);
- *               used to plan the split-KV work on the host
+ *  seq_lens     int32 HOST [B]  tokens in the cache per sequence (>= 1)
  *  out_lat      bf16 [B, H, R]  softmax(q.k * scale) . c
  * Supported: block_size 64, (R, P) in {(512, 64), (128, 32)}, 1 <= H <= 128.
  * Rows of a page past a sequence's length must hold finite values (the
  * paged-cache pool of dsb is zero-filled at creation).
  */
+typedef struct dsb_mla_plan dsb_mla_plan;
+
+DSB_API int dsb_mla_plan_create(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P, int block_size,
+                                dsb_mla_plan** out);
+DSB_API int dsb_mla_plan_destroy(dsb_mla_plan* plan);
+/* Number of work items and of split-KV partials of a plan. */
+DSB_API int dsb_mla_plan_info(const dsb_mla_plan* plan, int* n_items, int* n_partial);
+
+/* Enqueue the decode for a plan (asynchronous on the context stream). */
+DSB_API int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const void* q_rope,
+                                   const void* kv_cache, int64_t n_blocks, const int32_t* block_table, int max_blocks,
+                                   float softmax_scale, void* out_lat);
+
+/* Plan + decode in one call (the plan goes to a context-owned device buffer;
+ * still asynchronous on the context stream). */
 DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
-                   int block_size, const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B, int H,
-                   int R, int P, float softmax_scale, void* out_lat);
+                           int block_size, const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B,
+                           int H, int R, int P, float softmax_scale, void* out_lat);
 
 #ifdef __cplusplus
 }
