@@ -40,6 +40,21 @@ class Stats(ctypes.Structure):
         ("mla_work_items", ctypes.c_uint64),
         ("mla_partials", ctypes.c_uint64),
         ("workspace_bytes", ctypes.c_uint64),
+        ("gemm_calls", ctypes.c_uint64),
+    ]
+
+
+EPI_STORE, EPI_ADD, EPI_SILU_GATE, EPI_ROWSCALE = 0, 1, 2, 3
+
+
+class LinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("w", ctypes.c_void_p), ("ldw", ctypes.c_int64), ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("x_group_col", ctypes.c_int64), ("tok_offsets", ctypes.c_void_p),
+        ("T", ctypes.c_int), ("M", ctypes.c_int), ("K", ctypes.c_int), ("G", ctypes.c_int),
+        ("max_tokens_per_group", ctypes.c_int), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("y_group_col", ctypes.c_int64), ("y_f32", ctypes.c_int), ("epilogue", ctypes.c_int),
+        ("row_scale", ctypes.c_void_p),
     ]
 
 
@@ -62,6 +77,7 @@ _PROTOS = [
     ("dsb_mla_decode_planned", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
       ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p]),
+    ("dsb_linear", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearArgs)]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -163,6 +179,20 @@ class Context:
                 block_table.shape[1], float(softmax_scale), _ptr(out),
             )
         )
+
+    def linear(self, w, x, y, *, M, K, G=1, T=None, ldw=None, ldx=None, x_group_col=0, tok_offsets=None,
+               max_tokens_per_group=0, ldy=None, y_group_col=0, epilogue=EPI_STORE, row_scale=None):
+        """dsb_linear on torch device tensors (w, x bf16; y bf16 or fp32)."""
+        import torch
+
+        T = x.shape[0] if T is None else T
+        a = LinearArgs(
+            w=_ptr(w), ldw=ldw or w.shape[-1], x=_ptr(x), ldx=ldx or x.shape[-1], x_group_col=x_group_col,
+            tok_offsets=_ptr(tok_offsets), T=T, M=M, K=K, G=G, max_tokens_per_group=max_tokens_per_group,
+            y=_ptr(y), ldy=ldy or y.shape[-1], y_group_col=y_group_col, y_f32=int(y.dtype == torch.float32),
+            epilogue=epilogue, row_scale=_ptr(row_scale),
+        )
+        self._check(self._l.dsb_linear(self.h, ctypes.byref(a)))
 
     def mla_decode(self, q_lat, q_rope, kv_cache, block_table, seq_lens, softmax_scale, out, block_size=64):
         """Absorbed MLA decode (dsb_mla_decode).  q_lat [B,H,R], q_rope [B,H,P],

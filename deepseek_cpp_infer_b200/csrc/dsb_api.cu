@@ -66,6 +66,26 @@ int ensure_aux(dsb_ctx* ctx, size_t bytes) {
   return DSB_OK;
 }
 
+int ensure_counters(dsb_ctx* ctx, size_t n) {
+  if (n <= ctx->n_counters) return DSB_OK;
+  size_t grow = ctx->n_counters ? ctx->n_counters : 4096;
+  while (grow < n) grow *= 2;
+  if (ctx->counters != nullptr) {
+    DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    DSB_CUDA_TRY(ctx, cudaFree(ctx->counters));
+    ctx->counters = nullptr;
+    ctx->n_counters = 0;
+  }
+  cudaError_t e = cudaMalloc(&ctx->counters, grow * sizeof(int));
+  if (e != cudaSuccess) {
+    ctx->counters = nullptr;
+    return fail(ctx, DSB_ENOMEM, "counters cudaMalloc: %s", cudaGetErrorString(e));
+  }
+  DSB_CUDA_TRY(ctx, cudaMemsetAsync(ctx->counters, 0, grow * sizeof(int), ctx->stream));
+  ctx->n_counters = grow;
+  return DSB_OK;
+}
+
 namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -156,6 +176,7 @@ int dsb_ctx_destroy(dsb_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->aux) cudaFree(ctx->aux);
+  if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;

@@ -20,6 +20,8 @@ struct dsb_ctx {
   size_t ws_bytes = 0;
   void* aux = nullptr;      // reusable device buffer for per-call plans
   size_t aux_bytes = 0;
+  int* counters = nullptr;  // zeroed tickets for split-K reductions (kernels re-zero them)
+  size_t n_counters = 0;
   std::string last_error;
   dsb_stats stats{};
 };
@@ -40,6 +42,8 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 int ensure_workspace(dsb_ctx* ctx, size_t bytes);
 // Same for ctx->aux (small per-call metadata such as work lists).
 int ensure_aux(dsb_ctx* ctx, size_t bytes);
+// Ensure ctx->counters holds at least n zeroed ints.
+int ensure_counters(dsb_ctx* ctx, size_t n);
 
 // 2D bf16/u8/f32 tiled tensor map over a row-major matrix [rows, cols] with
 // row pitch `pitch_bytes`; box = box_cols x box_rows; swizzle per CU enum.

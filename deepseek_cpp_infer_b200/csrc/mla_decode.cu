@@ -77,8 +77,9 @@ struct MlaShape {
   static constexpr int CH_BYTES = kTok * 128;     // 64 rows x 128 B
   static constexpr int ROPE_BYTES = kTok * PD * 2;
   static constexpr int STAGE_BYTES = NCH * CH_BYTES + ROPE_BYTES;
-  static constexpr int NSTAGE = (NCTA == 2) ? 5 : 8;
-  static constexpr int XCH_BYTES = (NCTA == 2) ? kHeadsPad * kTok * 4 : 0;
+  static constexpr int NSTAGE = (NCTA == 2) ? 4 : 8;
+  static constexpr int XCH_BUF = kHeadsPad * kTok * 2;             // one tile of fp16 partial scores
+  static constexpr int XCH_BYTES = (NCTA == 2) ? 2 * XCH_BUF : 0;  // double-buffered
   // TMEM column map
   static constexpr uint32_t T_O = 0;
   static constexpr uint32_t T_S = VD;
@@ -92,16 +93,21 @@ struct MlaShape {
   // shared memory map (offsets from a 1024-aligned base)
   static constexpr int OFF_STAGE = 0;
   static constexpr int OFF_XCH = NSTAGE * STAGE_BYTES;
-  static constexpr int OFF_BAR = OFF_XCH + XCH_BYTES;
-  static constexpr int NBAR = 2 * NSTAGE + 9;
+  static constexpr int OFF_RED = OFF_XCH + XCH_BYTES;  // [3 slots][2 half][128]: row maxima (2 parities), final sums
+  static constexpr int OFF_BAR = OFF_RED + 3 * 2 * kHeadsPad * 4;
+  static constexpr int NBAR = 2 * NSTAGE + 13;
   static constexpr int OFF_PAGES = OFF_BAR + NBAR * 8;
   static constexpr int OFF_MISC = OFF_PAGES + kMaxItemPages * 4;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
+constexpr int kSoftmaxWarps = 8;    // two warps per TMEM lane quarter (column halves)
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kMlaThreads = kSoftmaxThreads + 64;  // + TMA warp + MMA warp
+
 template <int R, int P, int NCTA>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kMlaThreads, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
                       const __nv_bfloat16* __restrict__ q_lat, const __nv_bfloat16* __restrict__ q_rope,
                       const int32_t* __restrict__ block_table, int max_blocks, const MlaItem* __restrict__ items,
@@ -118,21 +124,24 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* p_full = bars + 2 * S::NSTAGE + 2;
   uint64_t* pv_done = bars + 2 * S::NSTAGE + 3;
   uint64_t* q_ready = bars + 2 * S::NSTAGE + 4;
-  uint64_t* xch_full = bars + 2 * S::NSTAGE + 5;   // peer's partial S landed in my XCH
-  uint64_t* peer_free = bars + 2 * S::NSTAGE + 6;  // peer finished reading its XCH
-  uint64_t* drain = bars + 2 * S::NSTAGE + 7;
+  uint64_t* drain = bars + 2 * S::NSTAGE + 5;
+  uint64_t* xch_full = bars + 2 * S::NSTAGE + 6;   // [2] peer's partial S landed in my XCH buffer
+  uint64_t* peer_free = bars + 2 * S::NSTAGE + 8;  // [2] peer finished reading its XCH buffer
+  uint64_t* red_bar = bars + 2 * S::NSTAGE + 10;   // [2] both column halves posted their row maxima
+  uint64_t* fin_bar = bars + 2 * S::NSTAGE + 12;   // both halves posted their softmax sums
   int32_t* pages = reinterpret_cast<int32_t*>(smem + S::OFF_PAGES);
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
   // never raised: drain waits keep their time limit but ignore the abort flag
   volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
-  float* xch = reinterpret_cast<float*>(smem + S::OFF_XCH);
+  float* red = reinterpret_cast<float*>(smem + S::OFF_RED);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
   const uint32_t rank = (NCTA == 2) ? cluster_ctarank() : 0u;
   const MlaItem item = items[blockIdx.x / NCTA];
   const int n_tiles = item.npages;
+  constexpr uint32_t kTmaWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::NSTAGE; ++s) {
@@ -140,13 +149,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
+    mbar_init(s_free, kSoftmaxThreads);
+    mbar_init(p_full, kSoftmaxThreads);
     mbar_init(pv_done, 1);
-    mbar_init(q_ready, 128);
-    mbar_init(xch_full, 128);
-    mbar_init(peer_free, 128);
+    mbar_init(q_ready, kSoftmaxThreads);
     mbar_init(drain, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&xch_full[b], 1);            // the local expect_tx arrival + 32 KB of st.async bytes
+      mbar_init(&peer_free[b], kSoftmaxWarps);  // one remote arrival per peer softmax warp
+      mbar_init(&red_bar[b], kSoftmaxThreads);
+    }
+    mbar_init(fin_bar, kSoftmaxThreads);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -155,7 +168,7 @@ __global__ void __launch_bounds__(192, 1)
     tmem_alloc(tmem_base_smem, S::T_COLS);
     tmem_relinquish();
   }
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     for (int i = lane; i < n_tiles; i += 32)
       pages[i] = block_table[(int64_t)item.b * max_blocks + item.page0 + i];
     if (lane == 0) {
@@ -166,11 +179,11 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (NCTA == 2) cluster_sync();  // peer barriers initialised before any remote arrive
+  if (NCTA == 2) cluster_sync();  // peer barriers initialised before any remote access
   const uint32_t tmem = *tmem_base_smem;
   const uint32_t smem_base = smem_u32(smem);
 
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int j = first; j < issued; ++j) mbar_wait(&full[j % S::NSTAGE], (j / S::NSTAGE) & 1, no_abort);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 64, 0, 0);
@@ -251,17 +264,21 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain, 0, no_abort);
     }
   } else {
-    // ------------------------------------------------------- softmax warps 0-3
-    const int t = threadIdx.x;  // head index == TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ---------------------------------------------------- softmax warps 0-7
+    // Warp w reads TMEM lane quarter q = w % 4 (rows = heads 32q..32q+31) and
+    // owns score columns [32h, 32h + 32) of each tile, h = w / 4.
+    const uint32_t q = warp & 3, hf = warp >> 2;
+    const int t = (int)(q * 32 + lane);  // head index == TMEM lane
+    const uint32_t lane_off = (q * 32) << 16;
+    const bool live = t < H;
     // Q slice -> TMEM (K order: latent columns of this CTA, then its rope columns)
     {
       uint32_t qv[16];
-      const bool live = t < H;
       const uint32_t* ql = reinterpret_cast<const uint32_t*>(q_lat + ((int64_t)item.b * H + (live ? t : 0)) * R + rank * S::VD);
       const uint32_t* qr = reinterpret_cast<const uint32_t*>(q_rope + ((int64_t)item.b * H + (live ? t : 0)) * P + rank * S::PD);
+      constexpr int NQC = S::QD / 32;  // 16-column chunks
 #pragma unroll 1
-      for (int c = 0; c < S::QD / 32; ++c) {  // 16 columns (32 bf16) per chunk
+      for (int c = (int)hf; c < NQC; c += 2) {
         const uint32_t* src = (c < S::VD / 32) ? ql + c * 16 : qr + (c - S::VD / 32) * 16;
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
@@ -278,61 +295,91 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t peer_xch = 0, peer_xch_full = 0, peer_peer_free = 0;
     if (NCTA == 2) {
       const uint32_t peer = rank ^ 1u;
-      peer_xch = mapa_shared(smem_base + S::OFF_XCH + t * 256, peer);
+      peer_xch = mapa_shared(smem_base + S::OFF_XCH + t * 128, peer);
       peer_xch_full = mapa_shared(smem_u32(xch_full), peer);
       peer_peer_free = mapa_shared(smem_u32(peer_free), peer);
     }
 
-    float m_run = -INFINITY, l_run = 0.0f;
+    float m_run = -INFINITY, l_half = 0.0f;  // l_half: this thread's 32 columns
     bool ok = true;
     const int tok0 = item.page0 * kTok;
     for (int j = 0; j < n_tiles; ++j) {
+      const int buf = j & 1;
+      if (NCTA == 2 && threadIdx.x == 0) mbar_arrive_expect_tx(&xch_full[buf], S::XCH_BUF);
       if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, abort))) { ok = false; break; }
       tc_fence_after();
-      float s[64];
+      float s[32];
       {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tmem + lane_off + S::T_S, r0);
-        tmem_ld32(tmem + lane_off + S::T_S + 32, r1);
+        uint32_t r0[32];
+        tmem_ld32(tmem + lane_off + S::T_S + hf * 32, r0);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __uint_as_float(r0[i]);
-          s[32 + i] = __uint_as_float(r1[i]);
-        }
+        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(r0[i]);
       }
       tc_fence_before();
       mbar_arrive(s_free);
 
       if (NCTA == 2) {
-        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait<true>(peer_free, (j - 1) & 1, abort))) { ok = false; break; }
+        // Scores are summed over the two CTAs' column slices.  Each partial is
+        // scaled into the log2 domain and rounded to fp16 in both CTAs, so the
+        // pair computes bit-identical sums; my partial goes to the peer with
+        // st.async, completing on the peer's xch_full[buf].
+        uint32_t hv[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int cc = c ^ (t & 15);
-          st_cluster_v4(peer_xch + cc * 16, s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
+        for (int i = 0; i < 16; ++i) {
+          hv[i] = pack_half2(s[2 * i] * scale_log2, s[2 * i + 1] * scale_log2);
+          const float2 f = unpack_half2(hv[i]);
+          s[2 * i] = f.x;
+          s[2 * i + 1] = f.y;
         }
-        mbar_arrive_cluster(peer_xch_full);
-        if (!__all_sync(0xffffffffu, mbar_wait<true>(xch_full, j & 1, abort))) { ok = false; break; }
-        const float4* row = reinterpret_cast<const float4*>(xch + t * 64);
+        if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait<true>(&peer_free[buf], ((j >> 1) - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst = peer_xch + buf * S::XCH_BUF;
+        const uint32_t rbar = peer_xch_full + buf * 8;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float4 v = row[c ^ (t & 15)];
-          s[4 * c] += v.x;
-          s[4 * c + 1] += v.y;
-          s[4 * c + 2] += v.z;
-          s[4 * c + 3] += v.w;
+        for (int c = 0; c < 4; ++c) {
+          const int pc = ((int)hf * 4 + c) ^ (t & 7);  // 16-byte chunk within the 128-byte row
+          st_async_v4_b32(dst + pc * 16, hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3], rbar);
         }
-        if (j + 1 < n_tiles) mbar_arrive_cluster(peer_peer_free);
+        if (!__all_sync(0xffffffffu, mbar_wait<true>(&xch_full[buf], (j >> 1) & 1, abort))) { ok = false; break; }
+        const uint4* row = reinterpret_cast<const uint4*>(smem + S::OFF_XCH + buf * S::XCH_BUF + t * 128);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = row[((int)hf * 4 + c) ^ (t & 7)];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_half2(w[k]);
+            s[8 * c + 2 * k] += f.x;
+            s[8 * c + 2 * k + 1] += f.y;
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && j + 2 < n_tiles) mbar_arrive_cluster_relaxed(peer_peer_free + buf * 8);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] *= scale_log2;
       }
 
-      const int tbase = tok0 + j * kTok;
-      float mt = -INFINITY;
+      // mask tokens past the item, row max (tree)
+      const int tbase = tok0 + j * kTok + (int)hf * 32;
+      float mx[16];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float v = (tbase + i < item.tok_end) ? s[i] * scale_log2 : -INFINITY;
-        s[i] = v;
-        mt = fmaxf(mt, v);
-      }
+      for (int i = 0; i < 32; ++i) s[i] = (tbase + i < item.tok_end) ? s[i] : -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+      float* red_j = red + (j & 1) * 2 * kHeadsPad;
+      red_j[hf * kHeadsPad + t] = mx[0];
+      mbar_arrive(&red_bar[j & 1]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[j & 1], (j >> 1) & 1, abort))) { ok = false; break; }
+      const float mt = fmaxf(mx[0], red_j[(hf ^ 1) * kHeadsPad + t]);
+      // lazy rescale: keep the running max until a tile exceeds it by 2^8
       float factor = 1.0f;
       bool rescale = false;
       if (mt > m_run + kLazyRescale) {
@@ -340,24 +387,28 @@ __global__ void __launch_bounds__(192, 1)
         m_run = mt;
         rescale = (j > 0);
       }
-      uint32_t pk[32];
-      float psum = 0.0f;
+      uint32_t pk[16];
+      float ps[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const uint32_t w = pack_bf16x2(fast_exp2(s[2 * i] - m_run), fast_exp2(s[2 * i + 1] - m_run));
         pk[i] = w;
-        psum += bf16lo_to_f32(w) + bf16hi_to_f32(w);
+        ps[i] = bf16lo_to_f32(w) + bf16hi_to_f32(w);
       }
-      l_run = l_run * factor + psum;
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) ps[i] += ps[i + w];
+      l_half = l_half * factor + ps[0];
       if (j > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort))) { ok = false; break; }
         tc_fence_after();
       }
-      // tcgen05.ld/st are warp-collective: rescale the whole warp's rows when any
-      // head of the warp needs it (factor is 1 for the others)
+      // tcgen05.ld/st are warp-collective: rescale the warp's rows (its half of
+      // the O columns) when any head of the warp needs it (factor 1 otherwise)
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < S::VD / 32; ++c) {
+        for (int c = (int)hf * (S::VD / 64); c < ((int)hf + 1) * (S::VD / 64); ++c) {
           uint32_t o[32];
           tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
           tmem_ld_wait();
@@ -366,22 +417,32 @@ __global__ void __launch_bounds__(192, 1)
           tmem_st32(tmem + lane_off + S::T_O + c * 32, o);
         }
       }
-      tmem_st32(tmem + lane_off + S::T_P, pk);
+      tmem_st16(tmem + lane_off + S::T_P + hf * 16, pk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
     }
     if (ok && n_tiles > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (n_tiles - 1) & 1, abort))) ok = false;
-    const bool live = t < H;
     if (!ok) {
       raise_abort(abort, status, kStatusTimeout);
     } else {
+      // combine the two column halves of the softmax denominator
+      float* red_l = red + 2 * 2 * kHeadsPad;  // slot 2
+      red_l[hf * kHeadsPad + t] = l_half;
+      mbar_arrive(fin_bar);
+      ok = __all_sync(0xffffffffu, mbar_wait(fin_bar, 0, abort));
+    }
+    if (!ok) {
+      raise_abort(abort, status, kStatusTimeout);
+    } else {
+      const float l_run = l_half + red[2 * 2 * kHeadsPad + (hf ^ 1) * kHeadsPad + t];
       tc_fence_after();
+      const int c0 = (int)hf * (S::VD / 64), c1 = c0 + S::VD / 64;  // this warp's 32-column O chunks
       if (item.partial < 0) {
         const float inv = 1.0f / l_run;
         __nv_bfloat16* dst = out + ((int64_t)item.b * H + (live ? t : 0)) * R + rank * S::VD;
 #pragma unroll 1
-        for (int c = 0; c < S::VD / 32; ++c) {
+        for (int c = c0; c < c1; ++c) {
           uint32_t o[32];
           tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
           tmem_ld_wait();
@@ -398,7 +459,7 @@ __global__ void __launch_bounds__(192, 1)
       } else {
         float* dst = ws_o + ((int64_t)item.partial * kHeadsPad + t) * R + rank * S::VD;
 #pragma unroll 1
-        for (int c = 0; c < S::VD / 32; ++c) {
+        for (int c = c0; c < c1; ++c) {
           uint32_t o[32];
           tmem_ld32(tmem + lane_off + S::T_O + c * 32, o);
           tmem_ld_wait();
@@ -410,7 +471,7 @@ __global__ void __launch_bounds__(192, 1)
                                   __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
           }
         }
-        if (rank == 0 && live) ws_ml[(int64_t)item.partial * kHeadsPad + t] = make_float2(m_run, l_run);
+        if (rank == 0 && hf == 0 && live) ws_ml[(int64_t)item.partial * kHeadsPad + t] = make_float2(m_run, l_run);
       }
     }
   }
@@ -551,7 +612,7 @@ int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const 
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(plan->n_items * NCTA));
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kMlaThreads);
   cfg.dynamicSmemBytes = S::SMEM_BYTES;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];

@@ -57,6 +57,7 @@ typedef struct dsb_stats {
   uint64_t mla_work_items; /* cluster work items summed over calls */
   uint64_t mla_partials;   /* work items that wrote a split-KV partial */
   uint64_t workspace_bytes;
+  uint64_t gemm_calls;     /* dsb_linear launches */
 } dsb_stats;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -128,6 +129,59 @@ DSB_API int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, const
 DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
                            int block_size, const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B,
                            int H, int R, int P, float softmax_scale, void* out_lat);
+
+/*
+ * Grouped bf16 linear layer (tcgen05, fp32 accumulation):
+ *   for each group g and token row t of the group,
+ *   acc[t, n] = sum_k x[t, g*x_group_col + k] * w[g*M + n, k],  n < M
+ * then an epilogue writes column g*y_group_col + n of row t of y.
+ *
+ * Replaces the reference's GEMV path - cublasSgemv / cublasGemmEx in
+ * gemv_row_major_mixed (src/models/deepseek/cuda_backend.cpp:459-498) behind
+ * linear_to_slot (cuda_backend.cpp:782-807) and ds::rt::linear
+ * (src/models/deepseek/ops.cpp:49-86) - and the per-expert GEMV chains of
+ * dense_mlp_to_slot / moe_to_slot (cuda_backend.cpp:820-883).
+ *
+ * Groups cover: one plain linear (G = 1); per-head absorbed projections
+ * (G = heads, same tokens, x_group_col / y_group_col select the head's
+ * slice); routed experts (G = experts, tok_offsets gives each expert's rows of
+ * a permuted activation matrix).
+ *
+ * Epilogues:
+ *  DSB_EPI_STORE      y = acc (bf16 or fp32 per y_f32)
+ *  DSB_EPI_ADD        y += acc (fp32 y; residual add, replaces ds_add_inplace_kernel)
+ *  DSB_EPI_SILU_GATE  w holds gate and up rows interleaved per 128-row tile
+ *                     (rows [128i, 128i+64) gate rows [64i, 64i+64), the next 64
+ *                     the matching up rows); y[t, 64i + j] = silu(gate) * up
+ *                     (dense_mlp_step's silu(gate)*up, ops.cpp:103-105)
+ *  DSB_EPI_ROWSCALE   y = acc * row_scale[t] (routed weight of a permuted row)
+ * Requirements: K, ldw, ldx, x_group_col multiples of 64/8/8/8; 16-byte
+ * aligned w and x.  max_tokens_per_group bounds the rows of any group (T when
+ * tok_offsets is NULL); it sets the MMA N tile (16..256).
+ */
+#define DSB_EPI_STORE 0
+#define DSB_EPI_ADD 1
+#define DSB_EPI_SILU_GATE 2
+#define DSB_EPI_ROWSCALE 3
+
+typedef struct dsb_linear_args {
+  const void* w;              /* bf16 [G * M, ldw] */
+  int64_t ldw;                /* row pitch of w (elements) */
+  const void* x;              /* bf16 [T, ldx] */
+  int64_t ldx;                /* row pitch of x (elements) */
+  int64_t x_group_col;        /* group g reads x columns [g*x_group_col, +K) */
+  const int32_t* tok_offsets; /* device int32 [G + 1] row ranges, or NULL: every group uses rows [0, T) */
+  int T, M, K, G;
+  int max_tokens_per_group;   /* host bound on rows per group (<= 0: T) */
+  void* y;                    /* output (bf16 or fp32 per y_f32) */
+  int64_t ldy;                /* row pitch of y (elements) */
+  int64_t y_group_col;        /* group g writes y columns [g*y_group_col, ...) */
+  int y_f32;                  /* 1: y is fp32, 0: bf16 */
+  int epilogue;               /* DSB_EPI_* */
+  const float* row_scale;     /* DSB_EPI_ROWSCALE: fp32 [T] */
+} dsb_linear_args;
+
+DSB_API int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* args);
 
 #ifdef __cplusplus
 }
