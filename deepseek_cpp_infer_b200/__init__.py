@@ -25,6 +25,8 @@ DSB_ETIMEOUT = 4
 DSB_EUNSUPPORTED = 5
 
 _c_i32p = ctypes.POINTER(ctypes.c_int32)
+_vp, _i64, _ci, _cf = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
 
 
 class DsbError(RuntimeError):
@@ -78,6 +80,16 @@ _PROTOS = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
       ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p]),
     ("dsb_linear", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearArgs)]),
+    ("dsb_rmsnorm", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _cf, _vp, _i64, _vp, _i64]),
+    ("dsb_kv_norm_rope_append", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _cf, _vp, _vp]),
+    ("dsb_router_logits", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _vp]),
+    ("dsb_moe_route", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _vp, _vp]),
+    ("dsb_moe_permute", ctypes.c_int, [_vp, _vp, _ci, _ci, _ci, _vp, _vp, _vp, _vp]),
+    ("dsb_gather_rows", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _ci, _vp]),
+    ("dsb_moe_combine", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _vp, _vp]),
+    ("dsb_argmax", ctypes.c_int, [_vp, _vp, _i64, _ci, _ci, _vp]),
+    ("dsb_embed", ctypes.c_int, [_vp, _vp, _ci, _vp, _ci, _ci, _vp]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -193,6 +205,52 @@ class Context:
             epilogue=epilogue, row_scale=_ptr(row_scale),
         )
         self._check(self._l.dsb_linear(self.h, ctypes.byref(a)))
+
+    # ---- row and routing ops (device tensors; shapes from the tensors)
+    def rmsnorm(self, x, w, eps, y_bf16=None, y_f32=None):
+        rows, n = x.shape
+        self._check(self._l.dsb_rmsnorm(self.h, _ptr(x), x.stride(0), _ptr(w), rows, n, float(eps), _ptr(y_bf16),
+                                        y_bf16.stride(0) if y_bf16 is not None else 0, _ptr(y_f32),
+                                        y_f32.stride(0) if y_f32 is not None else 0))
+
+    def kv_norm_rope_append(self, kv_a, w_norm, q, positions, block_table, H, nope, R, P, eps, theta, cache, q_rope):
+        B = kv_a.shape[0]
+        self._check(self._l.dsb_kv_norm_rope_append(
+            self.h, _ptr(kv_a), _ptr(w_norm), _ptr(q), _ptr(positions), _ptr(block_table), block_table.shape[1], B,
+            H, nope, R, P, float(eps), float(theta), _ptr(cache), _ptr(q_rope)))
+
+    def router_logits(self, x, w_gate, logits):
+        T, D = x.shape
+        self._check(self._l.dsb_router_logits(self.h, _ptr(x), _ptr(w_gate), T, D, w_gate.shape[0], _ptr(logits)))
+
+    def moe_route(self, logits, ids, weights, k, scoring=SCORE_SOFTMAX, bias=None, n_group=1, topk_group=1,
+                  norm_topk=0, routed_scale=1.0):
+        T, E = logits.shape
+        self._check(self._l.dsb_moe_route(self.h, _ptr(logits), _ptr(bias), T, E, k, scoring, n_group, topk_group,
+                                          int(norm_topk), float(routed_scale), _ptr(ids), _ptr(weights)))
+
+    def moe_permute(self, ids, E, counts, offsets, dest, src_pair):
+        T, k = ids.shape
+        self._check(self._l.dsb_moe_permute(self.h, _ptr(ids), T, k, E, _ptr(counts), _ptr(offsets), _ptr(dest),
+                                            _ptr(src_pair)))
+
+    def gather_rows(self, x, src_pair, k, out):
+        n, D = out.shape
+        self._check(self._l.dsb_gather_rows(self.h, _ptr(x), x.stride(0), _ptr(src_pair), n, k, D, _ptr(out)))
+
+    def moe_combine(self, y, dest, k, h, shared=None):
+        T, D = h.shape
+        self._check(self._l.dsb_moe_combine(self.h, _ptr(y), _ptr(dest), T, k, D, _ptr(shared), _ptr(h)))
+
+    def argmax(self, logits, out):
+        B, V = logits.shape
+        self._check(self._l.dsb_argmax(self.h, _ptr(logits), logits.stride(0), B, V, _ptr(out)))
+
+    def embed(self, table, tokens, h):
+        import torch
+
+        self._check(self._l.dsb_embed(self.h, _ptr(table), int(table.dtype == torch.bfloat16), _ptr(tokens),
+                                      tokens.shape[0], table.shape[1], _ptr(h)))
 
     def mla_decode(self, q_lat, q_rope, kv_cache, block_table, seq_lens, softmax_scale, out, block_size=64):
         """Absorbed MLA decode (dsb_mla_decode).  q_lat [B,H,R], q_rope [B,H,P],

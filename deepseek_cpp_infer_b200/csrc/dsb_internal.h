@@ -51,4 +51,22 @@ int make_tmap_2d(dsb_ctx* ctx, CUtensorMap* map, const void* base, CUtensorMapDa
                  uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swizzle);
 
+// Launchers shared by the C ABI entry points and the decode step (ops.cu).
+int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
+                 void* y_bf16, int64_t ldyb, float* y_f32, int64_t ldyf);
+int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q, const int32_t* pos,
+                        const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
+                        float theta, void* cache, void* q_rope);
+int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits);
+int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights);
+int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
+                int32_t* src_pair);
+int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
+                void* out);
+int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
+                float* h);
+int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
+int embed(dsb_ctx* ctx, const void* table, int bf16, const int32_t* tokens, int B, int D, float* h);
+
 }  // namespace dsb

@@ -1,0 +1,549 @@
+// Memory-bound and routing kernels of the decode step, sm_100a.
+//
+// Each kernel replaces a reference CPU function or SIMT kernel and keeps its
+// arithmetic order where that decides the result: products are rounded in the
+// reference's order with __fmul_rn/__fadd_rn (no FMA contraction), softmax /
+// RMSNorm use IEEE division and square root, ties go to the lowest index.
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "dsb_internal.h"
+#include "dsb_ptx.cuh"
+
+namespace dsb {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum of one float per thread (blockDim.x multiple of 32, <= 1024).
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = 0.0f;
+  for (int i = 0; i < nw; ++i) r += red[i];
+  return r;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+
+// y = x * (1 / sqrt(mean(x^2) + eps)) * w per row (src/ops/core/ops.cpp:17-23,
+// ds_rmsnorm_kernel elementwise_kernels.cu:13-28), written as bf16 and/or fp32.
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int n,
+                                    float eps, __nv_bfloat16* __restrict__ yb, int64_t ldyb, float* __restrict__ yf,
+                                    int64_t ldyf) {
+  __shared__ float red[32];
+  const float* xr = x + blockIdx.x * ldx;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+  const float mean2 = __fdiv_rn(block_sum(ss, red), (float)n);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+    if (yb) yb[blockIdx.x * ldyb + i] = __float2bfloat16_rn(v);
+    if (yf) yf[blockIdx.x * ldyf + i] = v;
+  }
+}
+
+// -------------------------------------------------- norm + RoPE + cache append
+
+// Interleaved-pair rotation of (x0, x1) at pair index k of a dim-wide rope
+// vector (src/ops/core/rope.cpp:8-23: inv_freq = theta^(-2k/dim)).
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, int k, int dim, int pos, float theta) {
+  const float inv_freq = powf(theta, __fdiv_rn(-(float)(2 * k), (float)dim));
+  const float ang = __fmul_rn((float)pos, inv_freq);
+  const float c = cosf(ang), s = sinf(ang);
+  const float a = x0, b = x1;
+  x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+}
+
+// One block per token b: c = rmsnorm(kv_a[b, :R]) * w and kr = rope(kv_a[b, R:])
+// go to the token's paged-cache row (mla.cpp:74-84); every head's rope query
+// q[b, h, nope:] is rotated into q_rope[b, h] (mla.cpp:97).
+__global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, const float* __restrict__ w_norm,
+                                           const __nv_bfloat16* __restrict__ q, const int32_t* __restrict__ pos,
+                                           const int32_t* __restrict__ block_table, int max_blocks, int H, int nope,
+                                           int R, int P, float eps, float theta, __nv_bfloat16* __restrict__ cache,
+                                           __nv_bfloat16* __restrict__ q_rope) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int p = pos[b];
+  const float* kv = kv_a + (int64_t)b * (R + P);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(kv[i], kv[i]));
+  const float mean2 = __fdiv_rn(block_sum(ss, red), (float)R);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+  const int64_t page = block_table[(int64_t)b * max_blocks + p / 64];
+  __nv_bfloat16* row = cache + (page * 64 + p % 64) * (int64_t)(R + P);
+  for (int i = threadIdx.x; i < R; i += blockDim.x) row[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(kv[i], inv), w_norm[i]));
+  for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
+    float x0 = kv[R + 2 * k], x1 = kv[R + 2 * k + 1];
+    rope_pair(x0, x1, k, P, p, theta);
+    row[R + 2 * k] = __float2bfloat16_rn(x0);
+    row[R + 2 * k + 1] = __float2bfloat16_rn(x1);
+  }
+  const int qh = nope + P;
+  for (int idx = threadIdx.x; idx < H * (P / 2); idx += blockDim.x) {
+    const int h = idx / (P / 2), k = idx % (P / 2);
+    const __nv_bfloat16* src = q + (int64_t)b * H * qh + (int64_t)h * qh + nope + 2 * k;
+    float x0 = __bfloat162float(src[0]), x1 = __bfloat162float(src[1]);
+    rope_pair(x0, x1, k, P, p, theta);
+    __nv_bfloat16* dst = q_rope + ((int64_t)b * H + h) * P + 2 * k;
+    dst[0] = __float2bfloat16_rn(x0);
+    dst[1] = __float2bfloat16_rn(x1);
+  }
+}
+
+// -------------------------------------------------------------------- router
+
+// logits[t, e] = x[t] . W_gate[e] in fp32 (the reference's gate linear,
+// ops.cpp:115-117); one warp per (token, expert).
+__global__ void router_logits_kernel(const float* __restrict__ x, const float* __restrict__ w, int T, int D, int E,
+                                     float* __restrict__ logits) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (gw >= T * E) return;
+  const int t = gw / E, e = gw % E;
+  const float* xr = x + (int64_t)t * D;
+  const float* wr = w + (int64_t)e * D;
+  float acc = 0.0f;
+  for (int i = lane * 4; i < D; i += 128) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + i);
+    const float4 b = *reinterpret_cast<const float4*>(wr + i);
+    acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) logits[(int64_t)t * E + e] = acc;
+}
+
+constexpr int kMaxExpertsPerLane = 8;  // E <= 256
+
+// Warp-wide arg-max over per-lane candidates: the largest value, ties to the
+// lowest index (the strict '>' scan of routing_kernels.cu:21-30).
+__device__ __forceinline__ void warp_argmax(float& v, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+}
+
+// One warp per token.  scoring 0: softmax over the E logits, top-k, optional
+// renormalisation, times routed_scale (ops.cpp:110-131,137).  scoring 1:
+// sigmoid + bias grouped selection (DeepSeek-V3): groups ranked by the sum of
+// their top-2 biased scores, the top topk_group groups kept, top-k experts of
+// the kept groups by biased score, weights = unbiased sigmoid scores of the
+// chosen experts, normalised when norm_topk, times routed_scale.
+__global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
+                             int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
+                             int32_t* __restrict__ ids, float* __restrict__ weights) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* lg = logits + (int64_t)t * E;
+  float sel[kMaxExpertsPerLane], val[kMaxExpertsPerLane];  // selection key, weight source
+#pragma unroll
+  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    const int e = lane + 32 * j;
+    sel[j] = -INFINITY;
+    val[j] = 0.0f;
+    if (e < E) {
+      const float l = lg[e];
+      if (scoring == 0) {
+        sel[j] = l;  // softmax is monotone: rank by logit, weigh by probability
+        val[j] = l;
+      } else {
+        const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l)));
+        sel[j] = __fadd_rn(s, bias[e]);
+        val[j] = s;
+      }
+    }
+  }
+  if (scoring == 0) {
+    // probabilities: p = exp(l - max) / sum (softmax_f32, math.cpp:15-27)
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) mx = fmaxf(mx, sel[j]);
+    mx = warp_max(mx);
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+      const int e = lane + 32 * j;
+      val[j] = e < E ? expf(__fsub_rn(val[j], mx)) : 0.0f;
+      sum = __fadd_rn(sum, val[j]);
+    }
+    sum = warp_sum(sum);
+    const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) val[j] = __fmul_rn(val[j], inv);
+  } else {
+    // group ranking: E/n_group consecutive experts per group
+    const int per = E / n_group;
+    // group score for every group, computed by lane g (n_group <= 32)
+    float gscore = -INFINITY;
+    {
+      // each lane gathers the biased scores of group `lane` from the owners
+      float b1 = -INFINITY, b2 = -INFINITY;
+      for (int i = 0; i < per; ++i) {
+        // expert lane*per + i lives at lane (e % 32), slot (e / 32)
+        float v = -INFINITY;
+        // every lane must take part in each shuffle: loop over the slot index
+#pragma unroll
+        for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+          const int e = lane * per + i;
+          const float cand = __shfl_sync(0xffffffffu, sel[j], e & 31);
+          if ((e >> 5) == j && lane < n_group) v = cand;
+        }
+        if (lane < n_group) {
+          if (v > b1) {
+            b2 = b1;
+            b1 = v;
+          } else if (v > b2) {
+            b2 = v;
+          }
+        }
+      }
+      if (lane < n_group) gscore = per >= 2 ? __fadd_rn(b1, b2) : b1;
+    }
+    // keep the best topk_group groups (ties -> lower group id)
+    unsigned keep = 0;
+    for (int r = 0; r < topk_group; ++r) {
+      float v = (lane < n_group && !((keep >> lane) & 1u)) ? gscore : -INFINITY;
+      int gi = lane < n_group ? lane : 1 << 30;
+      if ((keep >> lane) & 1u) gi = 1 << 30;
+      warp_argmax(v, gi);
+      keep |= 1u << gi;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((keep >> (e / per)) & 1u)) sel[j] = -INFINITY;
+    }
+  }
+  // top-k by selection key, ties to the lower expert id
+  float wsel[8];
+  int isel[8];
+  float wsum = 0.0f;
+  for (int r = 0; r < k; ++r) {
+    float v = -INFINITY;
+    int idx = 1 << 30;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && (sel[j] > v || (sel[j] == v && e < idx))) {
+        v = sel[j];
+        idx = e;
+      }
+    }
+    warp_argmax(v, idx);
+    // owner lane removes the winner and publishes its weight source
+    float wv = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+      if (lane + 32 * j == idx) {
+        wv = val[j];
+        sel[j] = -INFINITY;
+      }
+    wv = __shfl_sync(0xffffffffu, wv, idx & 31);
+    wsel[r] = wv;
+    isel[r] = idx;
+    wsum = __fadd_rn(wsum, wv);
+  }
+  if (lane == 0) {
+    for (int r = 0; r < k; ++r) {
+      float wv = wsel[r];
+      if (norm_topk && wsum > 0.0f) wv = __fdiv_rn(wv, wsum);
+      ids[(int64_t)t * k + r] = isel[r];
+      weights[(int64_t)t * k + r] = __fmul_rn(wv, routed_scale);
+    }
+  }
+}
+
+// Deterministic permutation of the N = T*k (token, slot) pairs by expert: the
+// pair with flat index i goes to dest[i] = offsets[e] + (number of earlier
+// pairs routed to e); src_pair is the inverse.  One warp walks the pairs in
+// order, 32 at a time, ranking equal experts with match.any.
+__global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ counts,
+                               int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
+                               int32_t* __restrict__ src_pair) {
+  extern __shared__ int32_t cnt[];  // [E]
+  const int lane = threadIdx.x;
+  for (int e = lane; e < E; e += 32) cnt[e] = 0;
+  __syncwarp();
+  for (int c = 0; c < N; c += 32) {
+    const int i = c + lane;
+    const int e = i < N ? ids[i] : -1 - lane;  // unique negative keys for idle lanes
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(grp & ((1u << lane) - 1u));
+    const int base = e >= 0 ? cnt[e] : 0;
+    __syncwarp();
+    if (i < N) dest[i] = base + rank;
+    if (e >= 0 && rank == 0) cnt[e] = base + __popc(grp);
+    __syncwarp();
+  }
+  // exclusive prefix sum of the counts
+  int carry = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int v = e < E ? cnt[e] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (e < E) {
+      counts[e] = v;
+      offsets[e] = carry + incl - v;
+    }
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) offsets[E] = carry;
+  __syncwarp();
+  for (int i = lane; i < N; i += 32) {
+    const int d = offsets[ids[i]] + dest[i];
+    dest[i] = d;
+    src_pair[d] = i;
+  }
+}
+
+// out[p] = x[src_pair[p] / k] (bf16 rows, 16-byte vectors).
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src,
+                                   int k, int D, __nv_bfloat16* __restrict__ out) {
+  const int p = blockIdx.x;
+  const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)(src[p] / k) * ldx);
+  uint4* d = reinterpret_cast<uint4*>(out + (int64_t)p * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) d[i] = s[i];
+}
+
+// h[t] += (y[dest[t*k]] + ... + y[dest[t*k+k-1]]) + shared[t]: the order of
+// moe_step's accumulation (ops.cpp:133-145) followed by the residual add
+// (model.cpp:209).
+__global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ dest, int k, int D,
+                                   const float* __restrict__ shared, float* __restrict__ h) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j) acc = __fadd_rn(acc, y[(int64_t)dest[t * k + j] * D + i]);
+    if (shared) acc = __fadd_rn(acc, shared[(int64_t)t * D + i]);
+    h[(int64_t)t * D + i] = __fadd_rn(h[(int64_t)t * D + i], acc);
+  }
+}
+
+// Greedy id per row: first index of the maximum (argmax_f32, math.cpp:29-40).
+__global__ void argmax_rows_kernel(const float* __restrict__ logits, int64_t ld, int V, int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const float* row = logits + blockIdx.x * ld;
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = row[i];
+    if (x > v || (x == v && i < idx)) {  // NaN never wins, like the reference's '>'
+      v = x;
+      idx = i;
+    }
+  }
+  warp_argmax(v, idx);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = v;
+    si[w] = idx;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    v = l < nw ? sv[l] : -INFINITY;
+    idx = l < nw ? si[l] : 0x7fffffff;
+    warp_argmax(v, idx);
+    if (l == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+// h[b] = embedding row of token[b] as fp32 (embedding_lookup_f32,
+// src/hf/weight_ops.cpp:37-65).
+__global__ void embed_kernel(const void* __restrict__ table, int bf16, const int32_t* __restrict__ tokens, int D,
+                             float* __restrict__ h) {
+  const int b = blockIdx.x;
+  const int64_t row = tokens[b];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    h[(int64_t)b * D + i] = bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(table)[row * D + i])
+                                 : static_cast<const float*>(table)[row * D + i];
+  }
+}
+
+int launched(dsb_ctx* ctx) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ctx, DSB_ECUDA, "kernel launch: %s", cudaGetErrorString(e));
+  ctx->stats.kernel_launches++;
+  return DSB_OK;
+}
+
+}  // namespace
+
+int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
+                 void* y_bf16, int64_t ldyb, float* y_f32, int64_t ldyf) {
+  rmsnorm_rows_kernel<<<rows, 256, 0, ctx->stream>>>(x, ldx, w, n, eps, static_cast<__nv_bfloat16*>(y_bf16), ldyb,
+                                                     y_f32, ldyf);
+  return launched(ctx);
+}
+
+int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q, const int32_t* pos,
+                        const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
+                        float theta, void* cache, void* q_rope) {
+  kv_norm_rope_append_kernel<<<B, 128, 0, ctx->stream>>>(kv_a, w_norm, static_cast<const __nv_bfloat16*>(q), pos,
+                                                         block_table, max_blocks, H, nope, R, P, eps, theta,
+                                                         static_cast<__nv_bfloat16*>(cache),
+                                                         static_cast<__nv_bfloat16*>(q_rope));
+  return launched(ctx);
+}
+
+int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits) {
+  const int warps = T * E;
+  router_logits_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(x, w, T, D, E, logits);
+  return launched(ctx);
+}
+
+int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights) {
+  route_kernel<<<(T + 7) / 8, 256, 0, ctx->stream>>>(logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk,
+                                                     routed_scale, ids, weights);
+  return launched(ctx);
+}
+
+int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
+                int32_t* src_pair) {
+  permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair);
+  return launched(ctx);
+}
+
+int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
+                void* out) {
+  gather_rows_kernel<<<n_pairs, 128, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), ldx, src_pair, k, D,
+                                                       static_cast<__nv_bfloat16*>(out));
+  return launched(ctx);
+}
+
+int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
+                float* h) {
+  moe_combine_kernel<<<T, 256, 0, ctx->stream>>>(y, dest, k, D, shared, h);
+  return launched(ctx);
+}
+
+int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out) {
+  argmax_rows_kernel<<<B, 1024, 0, ctx->stream>>>(logits, ld, V, out);
+  return launched(ctx);
+}
+
+int embed(dsb_ctx* ctx, const void* table, int bf16, const int32_t* tokens, int B, int D, float* h) {
+  embed_kernel<<<B, 256, 0, ctx->stream>>>(table, bf16, tokens, D, h);
+  return launched(ctx);
+}
+
+}  // namespace dsb
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" int dsb_rmsnorm(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
+                           void* y_bf16, int64_t ldy_bf16, float* y_f32, int64_t ldy_f32) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (x == nullptr || w == nullptr || rows <= 0 || n <= 0 || (y_bf16 == nullptr && y_f32 == nullptr))
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_rmsnorm: bad arguments");
+  return dsb::rmsnorm_rows(ctx, x, ldx, w, rows, n, eps, y_bf16, ldy_bf16, y_f32, ldy_f32);
+}
+
+extern "C" int dsb_kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q,
+                                       const int32_t* positions, const int32_t* block_table, int max_blocks, int B,
+                                       int H, int nope, int R, int P, float eps, float theta, void* cache,
+                                       void* q_rope) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (kv_a == nullptr || w_norm == nullptr || q == nullptr || positions == nullptr || block_table == nullptr ||
+      cache == nullptr || q_rope == nullptr || B <= 0 || H <= 0 || R <= 0 || P <= 0 || (P % 2) != 0)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_kv_norm_rope_append: bad arguments");
+  return dsb::kv_norm_rope_append(ctx, kv_a, w_norm, q, positions, block_table, max_blocks, B, H, nope, R, P, eps,
+                                  theta, cache, q_rope);
+}
+
+extern "C" int dsb_router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (x == nullptr || w == nullptr || logits == nullptr || T <= 0 || E <= 0 || D <= 0 || (D % 4) != 0)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_router_logits: bad arguments (D must be a multiple of 4)");
+  return dsb::router_logits(ctx, x, w, T, D, E, logits);
+}
+
+extern "C" int dsb_moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring,
+                             int n_group, int topk_group, int norm_topk, float routed_scale, int32_t* ids,
+                             float* weights) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (logits == nullptr || ids == nullptr || weights == nullptr || T <= 0 || E <= 0 || E > 256 || k < 1 || k > 8 ||
+      k > E)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_route: bad arguments (E <= 256, 1 <= k <= 8)");
+  if (scoring == DSB_SCORE_SIGMOID) {
+    if (bias == nullptr || n_group < 1 || n_group > 32 || E % n_group != 0 || topk_group < 1 ||
+        topk_group > n_group || k > topk_group * (E / n_group))
+      return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_route: bad grouped-router arguments");
+  } else if (scoring != DSB_SCORE_SOFTMAX) {
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_route: unknown scoring %d", scoring);
+  }
+  return dsb::moe_route(ctx, logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids,
+                        weights);
+}
+
+extern "C" int dsb_moe_permute(dsb_ctx* ctx, const int32_t* ids, int T, int k, int E, int32_t* counts,
+                               int32_t* offsets, int32_t* dest, int32_t* src_pair) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (ids == nullptr || counts == nullptr || offsets == nullptr || dest == nullptr || src_pair == nullptr || T <= 0 ||
+      k <= 0 || E <= 0 || E > 4096)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_permute: bad arguments");
+  return dsb::moe_permute(ctx, ids, T * k, E, counts, offsets, dest, src_pair);
+}
+
+extern "C" int dsb_gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k,
+                               int D, void* out) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (x == nullptr || src_pair == nullptr || out == nullptr || n_pairs <= 0 || k <= 0 || D <= 0 || (D % 8) ||
+      (ldx % 8))
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_gather_rows: bad arguments (D, ldx multiples of 8)");
+  return dsb::gather_rows(ctx, x, ldx, src_pair, n_pairs, k, D, out);
+}
+
+extern "C" int dsb_moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D,
+                               const float* shared, float* h) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (y == nullptr || dest == nullptr || h == nullptr || T <= 0 || k <= 0 || D <= 0)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_combine: bad arguments");
+  return dsb::moe_combine(ctx, y, dest, T, k, D, shared, h);
+}
+
+extern "C" int dsb_argmax(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (logits == nullptr || out == nullptr || B <= 0 || V <= 0 || ld < V)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_argmax: bad arguments");
+  return dsb::argmax_rows(ctx, logits, ld, B, V, out);
+}
+
+extern "C" int dsb_embed(dsb_ctx* ctx, const void* table, int table_bf16, const int32_t* tokens, int B, int D,
+                         float* h) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (table == nullptr || tokens == nullptr || h == nullptr || B <= 0 || D <= 0)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_embed: bad arguments");
+  return dsb::embed(ctx, table, table_bf16, tokens, B, D, h);
+}

@@ -183,6 +183,73 @@ typedef struct dsb_linear_args {
 
 DSB_API int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* args);
 
+/* ---------------------------------------------------------------- row ops */
+
+/* y = x / sqrt(mean(x^2) + eps) * w per row, written as bf16 (y_bf16) and/or
+ * fp32 (y_f32).  x fp32 [rows, ldx], w fp32 [n].
+ * Replaces rmsnorm_to_slot / ds_rmsnorm_kernel (cuda_backend.cpp:809,
+ * src/ops/cuda/elementwise_kernels.cu:13-28) and rmsnorm_f32
+ * (src/ops/core/ops.cpp:17-23). */
+DSB_API int dsb_rmsnorm(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
+                        void* y_bf16, int64_t ldy_bf16, float* y_f32, int64_t ldy_f32);
+
+/* Fused latent-cache append for B tokens at positions[b] (device int32):
+ *   c = rmsnorm(kv_a[b, :R]) * w_norm, kr = rope(kv_a[b, R:R+P], pos)
+ * written as bf16 into row pos of sequence b in the paged cache
+ * (block_table[b * max_blocks + pos / 64], row pos % 64), and
+ * q_rope[b, h] = rope(q[b, h, nope:nope+P], pos) (bf16) for every head.
+ * kv_a fp32 [B, R+P]; q bf16 [B, H*(nope+P)]; cache bf16 [n_blocks, 64, R+P].
+ * Replaces the kv_a split / rmsnorm / RoPE / per-head cache copies of
+ * mla_decode_to_slot (cuda_backend.cpp:922-982) and mla.cpp:71-102. */
+DSB_API int dsb_kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q,
+                                    const int32_t* positions, const int32_t* block_table, int max_blocks, int B, int H,
+                                    int nope, int R, int P, float eps, float theta, void* cache, void* q_rope);
+
+/* fp32 router logits [T, E] = x [T, D] . W_gate [E, D]^T (ops.cpp:115-117). */
+DSB_API int dsb_router_logits(dsb_ctx* ctx, const float* x, const float* w_gate, int T, int D, int E, float* logits);
+
+#define DSB_SCORE_SOFTMAX 0
+#define DSB_SCORE_SIGMOID 1
+
+/* Expert selection per token from fp32 logits [T, E] (E <= 256, k <= 8):
+ *  DSB_SCORE_SOFTMAX: softmax, top-k, optional renormalisation, times
+ *    routed_scale (moe_step, ops.cpp:110-131,137; ds_select_topk_kernel,
+ *    routing_kernels.cu:8-44).  bias unused.
+ *  DSB_SCORE_SIGMOID: sigmoid + bias[E], n_group groups ranked by their
+ *    top-2 biased scores, topk_group groups kept, top-k by biased score,
+ *    weights = unbiased scores (normalised when norm_topk) times routed_scale.
+ * Ties go to the lower expert id.  ids int32 [T, k], weights fp32 [T, k]. */
+DSB_API int dsb_moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring,
+                          int n_group, int topk_group, int norm_topk, float routed_scale, int32_t* ids,
+                          float* weights);
+
+/* Histogram and permutation of the T*k (token, slot) pairs by expert:
+ * counts [E], offsets [E+1] (exclusive prefix sum), dest [T*k] (position of
+ * pair t*k+j in expert order, stable in pair order), src_pair [T*k] (its
+ * inverse).  Replaces the per-expert host loop of moe_to_slot
+ * (cuda_backend.cpp:854-874) and its top-k download + sync. */
+DSB_API int dsb_moe_permute(dsb_ctx* ctx, const int32_t* ids, int T, int k, int E, int32_t* counts, int32_t* offsets,
+                            int32_t* dest, int32_t* src_pair);
+
+/* out[p] = x[src_pair[p] / k] for bf16 rows of D (D, ldx multiples of 8). */
+DSB_API int dsb_gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k,
+                            int D, void* out);
+
+/* h[t] += (sum_j y[dest[t*k + j]]) + shared[t] (shared may be NULL): the
+ * routed-expert combine of moe_step (ops.cpp:133-145) plus the residual add
+ * (model.cpp:209); replaces ds_scale_add_kernel / ds_add_inplace_kernel. */
+DSB_API int dsb_moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D,
+                            const float* shared, float* h);
+
+/* Greedy ids: first index of the row maximum of logits [B, ld] (argmax_f32,
+ * src/core/math.cpp:29-40; the reference downloads the logits and does this
+ * on the host, cuda_backend.cpp:746-757). */
+DSB_API int dsb_argmax(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
+
+/* h[b] = fp32 embedding row tokens[b] of table [V, D] (bf16 when table_bf16,
+ * else fp32); replaces embedding_to_slot (cuda_backend.cpp:716-732). */
+DSB_API int dsb_embed(dsb_ctx* ctx, const void* table, int table_bf16, const int32_t* tokens, int B, int D, float* h);
+
 #ifdef __cplusplus
 }
 #endif
