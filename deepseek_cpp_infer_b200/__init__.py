@@ -43,6 +43,7 @@ class Stats(ctypes.Structure):
         ("mla_partials", ctypes.c_uint64),
         ("workspace_bytes", ctypes.c_uint64),
         ("gemm_calls", ctypes.c_uint64),
+        ("decode_steps", ctypes.c_uint64),
     ]
 
 
@@ -58,6 +59,23 @@ class LinearArgs(ctypes.Structure):
         ("y_group_col", ctypes.c_int64), ("y_f32", ctypes.c_int), ("epilogue", ctypes.c_int),
         ("row_scale", ctypes.c_void_p),
     ]
+
+
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+
+
+class ModelConfig(ctypes.Structure):
+    """dsb_model_config (the decode-path fields of ds::hf::DeepSeekConfig)."""
+
+    _fields_ = [
+        (n, ctypes.c_int)
+        for n in (
+            "hidden_size", "num_hidden_layers", "num_attention_heads", "vocab_size", "max_position_embeddings",
+            "intermediate_size", "moe_intermediate_size", "n_routed_experts", "n_shared_experts",
+            "num_experts_per_tok", "first_k_dense_replace", "q_lora_rank", "kv_lora_rank", "qk_nope_head_dim",
+            "qk_rope_head_dim", "v_head_dim", "scoring_func", "n_group", "topk_group", "norm_topk_prob",
+        )
+    ] + [("routed_scaling_factor", ctypes.c_float), ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
 
 
 # (name, restype, argtypes) for every function of include/dsb/dsb.h
@@ -85,11 +103,25 @@ _PROTOS = [
      [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _cf, _vp, _vp]),
     ("dsb_router_logits", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _vp]),
     ("dsb_moe_route", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _vp, _vp]),
-    ("dsb_moe_permute", ctypes.c_int, [_vp, _vp, _ci, _ci, _ci, _vp, _vp, _vp, _vp]),
+    ("dsb_moe_permute", ctypes.c_int, [_vp, _vp, _ci, _ci, _ci, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("dsb_gather_rows", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _ci, _vp]),
     ("dsb_moe_combine", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _vp, _vp]),
     ("dsb_argmax", ctypes.c_int, [_vp, _vp, _i64, _ci, _ci, _vp]),
     ("dsb_embed", ctypes.c_int, [_vp, _vp, _ci, _vp, _ci, _ci, _vp]),
+    ("dsb_model_create", ctypes.c_int, [_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_model_destroy", ctypes.c_int, [_vp]),
+    ("dsb_model_set_tensor", ctypes.c_int, [_vp, ctypes.c_char_p, _ci, ctypes.POINTER(ctypes.c_int64), _ci, _vp]),
+    ("dsb_model_init_random", ctypes.c_int, [_vp, ctypes.c_uint64, _cf]),
+    ("dsb_model_finalize", ctypes.c_int, [_vp]),
+    ("dsb_model_weight_bytes", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    ("dsb_kvcache_create", ctypes.c_int, [_vp, _vp, _i64, _ci, _ci, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_kvcache_destroy", ctypes.c_int, [_vp]),
+    ("dsb_kvcache_alloc_seq", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
+    ("dsb_kvcache_free_seq", ctypes.c_int, [_vp, _ci]),
+    ("dsb_kvcache_reset", ctypes.c_int, [_vp]),
+    ("dsb_kvcache_seq_len", ctypes.c_int, [_vp, _ci, ctypes.POINTER(ctypes.c_int)]),
+    ("dsb_kvcache_free_blocks", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int64)]),
+    ("dsb_decode_step", ctypes.c_int, [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, _vp, _c_i32p]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -229,10 +261,10 @@ class Context:
         self._check(self._l.dsb_moe_route(self.h, _ptr(logits), _ptr(bias), T, E, k, scoring, n_group, topk_group,
                                           int(norm_topk), float(routed_scale), _ptr(ids), _ptr(weights)))
 
-    def moe_permute(self, ids, E, counts, offsets, dest, src_pair):
+    def moe_permute(self, ids, E, counts, offsets, dest, src_pair, weights=None, w_perm=None):
         T, k = ids.shape
         self._check(self._l.dsb_moe_permute(self.h, _ptr(ids), T, k, E, _ptr(counts), _ptr(offsets), _ptr(dest),
-                                            _ptr(src_pair)))
+                                            _ptr(src_pair), _ptr(weights), _ptr(w_perm)))
 
     def gather_rows(self, x, src_pair, k, out):
         n, D = out.shape
@@ -291,3 +323,103 @@ class MlaPlan:
             self.close()
         except Exception:
             pass
+
+
+class Model:
+    """A dsb_model: device weights uploaded by checkpoint tensor name."""
+
+    def __init__(self, ctx: Context, cfg: ModelConfig):
+        self.ctx = ctx
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        ctx._check(ctx._l.dsb_model_create(ctx.h, ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+
+    def set_tensor(self, name: str, array):
+        """Upload a host numpy array (float32, or uint16 holding bf16 bits)."""
+        import numpy as np
+
+        a = np.ascontiguousarray(array)
+        dt = DTYPE_BF16 if a.dtype == np.uint16 else DTYPE_F32
+        if dt == DTYPE_F32:
+            a = a.astype(np.float32, copy=False)
+        shape = (ctypes.c_int64 * a.ndim)(*a.shape)
+        self.ctx._check(self.ctx._l.dsb_model_set_tensor(self.h, name.encode(), dt, shape, a.ndim, a.ctypes.data))
+
+    def init_random(self, seed: int, stddev: float = 0.02):
+        self.ctx._check(self.ctx._l.dsb_model_init_random(self.h, seed, stddev))
+
+    def finalize(self):
+        self.ctx._check(self.ctx._l.dsb_model_finalize(self.h))
+
+    def weight_bytes(self) -> int:
+        n = ctypes.c_uint64()
+        self.ctx._check(self.ctx._l.dsb_model_weight_bytes(self.h, ctypes.byref(n)))
+        return n.value
+
+    def close(self):
+        if self.h:
+            self.ctx._l.dsb_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KVCache:
+    """A dsb_kvcache: paged latent cache for every layer of a model."""
+
+    def __init__(self, ctx: Context, model: Model, n_blocks: int, max_seqs: int, max_blocks_per_seq: int):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        ctx._check(ctx._l.dsb_kvcache_create(ctx.h, model.h, n_blocks, max_seqs, max_blocks_per_seq, ctypes.byref(h)))
+        self.h = h
+
+    def alloc_seq(self) -> int:
+        s = ctypes.c_int()
+        self.ctx._check(self.ctx._l.dsb_kvcache_alloc_seq(self.h, ctypes.byref(s)))
+        return s.value
+
+    def free_seq(self, seq: int):
+        self.ctx._check(self.ctx._l.dsb_kvcache_free_seq(self.h, seq))
+
+    def reset(self):
+        self.ctx._check(self.ctx._l.dsb_kvcache_reset(self.h))
+
+    def seq_len(self, seq: int) -> int:
+        n = ctypes.c_int()
+        self.ctx._check(self.ctx._l.dsb_kvcache_seq_len(self.h, seq, ctypes.byref(n)))
+        return n.value
+
+    def free_blocks(self) -> int:
+        n = ctypes.c_int64()
+        self.ctx._check(self.ctx._l.dsb_kvcache_free_blocks(self.h, ctypes.byref(n)))
+        return n.value
+
+    def close(self):
+        if self.h:
+            self.ctx._l.dsb_kvcache_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def decode_step(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_logits=False):
+    """dsb_decode_step: one token per sequence; returns (greedy ids, logits or None)."""
+    import numpy as np
+
+    B = len(seq_ids)
+    sids = (ctypes.c_int32 * B)(*[int(x) for x in seq_ids])
+    toks = (ctypes.c_int32 * B)(*[int(x) for x in tokens])
+    greedy = (ctypes.c_int32 * B)()
+    logits = np.empty((B, model.cfg.vocab_size), np.float32) if want_logits else None
+    ctx._check(ctx._l.dsb_decode_step(ctx.h, model.h, kv.h, sids, toks, B,
+                                      logits.ctypes.data if want_logits else None, greedy))
+    return np.array(greedy[:], np.int32), logits

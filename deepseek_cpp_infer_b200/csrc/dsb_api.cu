@@ -66,6 +66,25 @@ int ensure_aux(dsb_ctx* ctx, size_t bytes) {
   return DSB_OK;
 }
 
+int ensure_step(dsb_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->step_bytes) return DSB_OK;
+  size_t grow = ctx->step_bytes ? ctx->step_bytes : (size_t)1 << 20;
+  while (grow < bytes) grow *= 2;
+  if (ctx->step != nullptr) {
+    DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    DSB_CUDA_TRY(ctx, cudaFree(ctx->step));
+    ctx->step = nullptr;
+    ctx->step_bytes = 0;
+  }
+  cudaError_t e = cudaMalloc(&ctx->step, grow);
+  if (e != cudaSuccess) {
+    ctx->step = nullptr;
+    return fail(ctx, DSB_ENOMEM, "step cudaMalloc(%zu): %s", grow, cudaGetErrorString(e));
+  }
+  ctx->step_bytes = grow;
+  return DSB_OK;
+}
+
 int ensure_counters(dsb_ctx* ctx, size_t n) {
   if (n <= ctx->n_counters) return DSB_OK;
   size_t grow = ctx->n_counters ? ctx->n_counters : 4096;
@@ -177,6 +196,7 @@ int dsb_ctx_destroy(dsb_ctx* ctx) {
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->counters) cudaFree(ctx->counters);
+  if (ctx->step) cudaFree(ctx->step);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;

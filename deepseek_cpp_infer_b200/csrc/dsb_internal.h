@@ -22,8 +22,20 @@ struct dsb_ctx {
   size_t aux_bytes = 0;
   int* counters = nullptr;  // zeroed tickets for split-K reductions (kernels re-zero them)
   size_t n_counters = 0;
+  void* step = nullptr;     // activations of dsb_decode_step
+  size_t step_bytes = 0;
   std::string last_error;
   dsb_stats stats{};
+};
+
+// A split-KV work plan of the MLA decode for one set of sequence lengths.
+struct dsb_mla_plan {
+  int B = 0, H = 0, R = 0, P = 0;
+  int n_items = 0, n_combines = 0, n_partial = 0;
+  int max_len = 0;
+  void* d_items = nullptr;     // work items on the device
+  void* d_combines = nullptr;  // split-sequence merge list on the device
+  int device = 0;
 };
 
 namespace dsb {
@@ -42,6 +54,8 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 int ensure_workspace(dsb_ctx* ctx, size_t bytes);
 // Same for ctx->aux (small per-call metadata such as work lists).
 int ensure_aux(dsb_ctx* ctx, size_t bytes);
+// Same for ctx->step (decode-step activations).
+int ensure_step(dsb_ctx* ctx, size_t bytes);
 // Ensure ctx->counters holds at least n zeroed ints.
 int ensure_counters(dsb_ctx* ctx, size_t n);
 
@@ -61,7 +75,7 @@ int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, in
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
               int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights);
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
-                int32_t* src_pair);
+                int32_t* src_pair, const float* weights, float* w_perm);
 int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
                 void* out);
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,

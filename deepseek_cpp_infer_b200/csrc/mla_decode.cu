@@ -36,16 +36,6 @@
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
 
-// A split-KV work plan for one set of sequence lengths (see plan_items).
-struct dsb_mla_plan {
-  int B = 0, H = 0, R = 0, P = 0;
-  int n_items = 0, n_combines = 0, n_partial = 0;
-  int max_len = 0;
-  void* d_items = nullptr;     // MlaItem[n_items] on the device
-  void* d_combines = nullptr;  // MlaCombine[n_combines] on the device
-  int device = 0;
-};
-
 namespace dsb {
 namespace {
 
@@ -734,24 +724,13 @@ extern "C" int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, co
                                 out_lat);
 }
 
-extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
-                              int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
-                              const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
-                              void* out_lat) {
-  using namespace dsb;
-  if (ctx == nullptr) return DSB_EINVAL;
-  if (seq_lens == nullptr || B <= 0 || H <= 0 || H > kHeadsPad)
-    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: bad sizes B=%d H=%d", B, H);
-  if (block_size != kTok) return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: block_size must be 64");
-  if (!((R == 512 && P == 64) || (R == 128 && P == 32)))
-    return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: (R, P) = (%d, %d) not supported", R, P);
+namespace dsb {
+
+// Plan the split-KV work for these lengths into the context's reusable plan
+// buffer (stream order protects its reuse); `plan` then refers to it.
+int mla_plan_into_aux(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P, dsb_mla_plan* plan) {
   int max_len = 0;
-  for (int b = 0; b < B; ++b) {
-    if (seq_lens[b] < 1 || seq_lens[b] > (int64_t)max_blocks * kTok)
-      return fail(ctx, DSB_EINVAL, "dsb_mla_decode: seq_lens[%d]=%d outside [1, max_blocks*64]", b, seq_lens[b]);
-    max_len = std::max(max_len, seq_lens[b]);
-  }
-  // plan into the context's reusable buffer: stream order protects reuse
+  for (int b = 0; b < B; ++b) max_len = std::max(max_len, seq_lens[b]);
   std::vector<MlaItem> items;
   std::vector<MlaCombine> combines;
   int n_partial = 0;
@@ -764,18 +743,40 @@ extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rop
   if (!combines.empty())
     DSB_CUDA_TRY(ctx, cudaMemcpyAsync(static_cast<uint8_t*>(ctx->aux) + off_comb, combines.data(),
                                       combines.size() * sizeof(MlaCombine), cudaMemcpyHostToDevice, ctx->stream));
+  plan->B = B;
+  plan->H = H;
+  plan->R = R;
+  plan->P = P;
+  plan->n_items = (int)items.size();
+  plan->n_combines = (int)combines.size();
+  plan->n_partial = n_partial;
+  plan->max_len = max_len;
+  plan->d_items = ctx->aux;
+  plan->d_combines = static_cast<uint8_t*>(ctx->aux) + off_comb;
+  plan->device = ctx->device;
+  return DSB_OK;
+}
+
+}  // namespace dsb
+
+extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
+                              int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                              const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                              void* out_lat) {
+  using namespace dsb;
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (seq_lens == nullptr || B <= 0 || H <= 0 || H > kHeadsPad)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: bad sizes B=%d H=%d", B, H);
+  if (block_size != kTok) return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: block_size must be 64");
+  if (!((R == 512 && P == 64) || (R == 128 && P == 32)))
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_mla_decode: (R, P) = (%d, %d) not supported", R, P);
+  for (int b = 0; b < B; ++b) {
+    if (seq_lens[b] < 1 || seq_lens[b] > (int64_t)max_blocks * kTok)
+      return fail(ctx, DSB_EINVAL, "dsb_mla_decode: seq_lens[%d]=%d outside [1, max_blocks*64]", b, seq_lens[b]);
+  }
   dsb_mla_plan plan;
-  plan.B = B;
-  plan.H = H;
-  plan.R = R;
-  plan.P = P;
-  plan.n_items = (int)items.size();
-  plan.n_combines = (int)combines.size();
-  plan.n_partial = n_partial;
-  plan.max_len = max_len;
-  plan.d_items = ctx->aux;
-  plan.d_combines = static_cast<uint8_t*>(ctx->aux) + off_comb;
-  plan.device = ctx->device;
+  int rc = mla_plan_into_aux(ctx, seq_lens, B, H, R, P, &plan);
+  if (rc != DSB_OK) return rc;
   return dsb_mla_decode_planned(ctx, &plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, softmax_scale,
                                 out_lat);
 }

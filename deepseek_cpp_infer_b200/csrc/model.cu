@@ -1,0 +1,814 @@
+// Whole-model batched decode on one GPU: device weights registry, paged latent
+// KV cache manager and the per-token decode step.
+//
+// Replaces the CUDA branch of DeepSeekModel::decode_next
+// (src/models/deepseek/model.cpp:117-184), the slot-addressed executor of
+// src/models/deepseek/cuda_backend.cpp (weight cache :402-457, MLA cache
+// :81-88, per-op *_to_slot functions) and its per-MoE-layer host round trip
+// (:854-860).  One step runs B sequences (one token each) through all layers
+// with every intermediate on the device; the host only plans the split-KV
+// work from the sequence lengths and reads back the greedy ids.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "dsb_internal.h"
+#include "dsb_ptx.cuh"
+
+struct dsb_model {
+  struct Layer {
+    bool moe = false;
+    bool has_moe_tensors = false;
+    float* in_norm = nullptr;
+    float* post_norm = nullptr;
+    __nv_bfloat16* w_q = nullptr;    // [H*(nope+P), D]        (no q-LoRA)
+    __nv_bfloat16* w_qa = nullptr;   // [q_lora, D]            (q-LoRA)
+    float* qa_norm = nullptr;        // [q_lora]
+    __nv_bfloat16* w_qb = nullptr;   // [H*(nope+P), q_lora]
+    __nv_bfloat16* w_kva = nullptr;  // [R+P, D]
+    float* kva_norm = nullptr;       // [R]
+    __nv_bfloat16* w_uk_t = nullptr; // [H*R, nope]   W_UK^T per head (from kv_b_proj)
+    __nv_bfloat16* w_uv = nullptr;   // [H*v, R]      W_UV per head (from kv_b_proj)
+    __nv_bfloat16* w_o = nullptr;    // [D, H*v]
+    __nv_bfloat16* w_gu = nullptr;   // dense gate|up interleaved per 128-row tile [2I, D]
+    __nv_bfloat16* w_down = nullptr; // [D, I]
+    int inter = 0;
+    float* w_router = nullptr;       // [E, D] fp32
+    float* router_bias = nullptr;    // [E]
+    __nv_bfloat16* e_gu = nullptr;   // [E, 2I, D]
+    __nv_bfloat16* e_down = nullptr; // [E, D, I]
+    int e_inter = 0;
+    __nv_bfloat16* s_gu = nullptr;   // shared experts [2Is, D]
+    __nv_bfloat16* s_down = nullptr; // [D, Is]
+    int s_inter = 0;
+    uint8_t seen_gate = 0, seen_up = 0;  // dense/shared gate-up halves uploaded
+  };
+  dsb_ctx* ctx = nullptr;
+  dsb_model_config cfg{};
+  std::vector<Layer> layers;
+  void* embed = nullptr;
+  int embed_bf16 = 1;
+  float* final_norm = nullptr;
+  __nv_bfloat16* lm_head = nullptr;
+  std::vector<void*> allocs;
+  bool finalized = false;
+  uint64_t weight_bytes = 0;
+};
+
+struct dsb_kvcache {
+  dsb_ctx* ctx = nullptr;
+  int n_layers = 0, R = 0, P = 0;
+  int64_t n_blocks = 0;
+  int max_seqs = 0, max_blocks_per_seq = 0;
+  __nv_bfloat16* pool = nullptr;  // [n_layers][n_blocks][64][R+P]
+  std::vector<int32_t> free_pages;
+  std::vector<std::vector<int32_t>> seq_pages;
+  std::vector<int32_t> seq_len;
+  std::vector<uint8_t> seq_live;
+};
+
+namespace dsb {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+float host_to_f32(const void* src, int dtype, int64_t i) {
+  switch (dtype) {
+    case DSB_DTYPE_F32: return static_cast<const float*>(src)[i];
+    case DSB_DTYPE_BF16: {
+      uint32_t u = static_cast<uint32_t>(static_cast<const uint16_t*>(src)[i]) << 16;
+      float f;
+      std::memcpy(&f, &u, 4);
+      return f;
+    }
+    default: {
+      __half h;
+      std::memcpy(&h, static_cast<const uint16_t*>(src) + i, 2);
+      return __half2float(h);
+    }
+  }
+}
+
+uint16_t f32_to_bf16_bits(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+std::vector<uint16_t> to_bf16(const void* src, int dtype, int64_t n) {
+  std::vector<uint16_t> out(static_cast<size_t>(n));
+  if (dtype == DSB_DTYPE_BF16) {
+    std::memcpy(out.data(), src, static_cast<size_t>(n) * 2);
+  } else {
+    for (int64_t i = 0; i < n; ++i) out[i] = f32_to_bf16_bits(host_to_f32(src, dtype, i));
+  }
+  return out;
+}
+
+std::vector<float> to_f32(const void* src, int dtype, int64_t n) {
+  std::vector<float> out(static_cast<size_t>(n));
+  for (int64_t i = 0; i < n; ++i) out[i] = host_to_f32(src, dtype, i);
+  return out;
+}
+
+template <class T>
+int dev_alloc(dsb_model* m, T** p, size_t count) {
+  void* v = nullptr;
+  cudaError_t e = cudaMalloc(&v, count * sizeof(T));
+  if (e != cudaSuccess) return fail(m->ctx, DSB_ENOMEM, "model cudaMalloc(%zu): %s", count * sizeof(T), cudaGetErrorString(e));
+  m->allocs.push_back(v);
+  m->weight_bytes += count * sizeof(T);
+  *p = static_cast<T*>(v);
+  return DSB_OK;
+}
+
+template <class T>
+int upload(dsb_model* m, T** p, const void* host, size_t count) {
+  if (*p == nullptr) {
+    int rc = dev_alloc(m, p, count);
+    if (rc != DSB_OK) return rc;
+  }
+  DSB_CUDA_TRY(m->ctx, cudaMemcpy(*p, host, count * sizeof(T), cudaMemcpyHostToDevice));
+  return DSB_OK;
+}
+
+// Rows [0, I) of a gate (half 0) or up (half 1) projection [I, D] go to the
+// interleaved layout: 128-row tile i holds gate rows [64i, 64i+64) then the
+// matching up rows (the SiLU-gate epilogue of dsb_linear pairs lanes r, r+64).
+int upload_gate_up_half(dsb_model* m, bf16* dst, const std::vector<uint16_t>& src, int I, int D, int half) {
+  if (I % 64 != 0) return fail(m->ctx, DSB_EUNSUPPORTED, "intermediate size %d is not a multiple of 64", I);
+  const size_t row = static_cast<size_t>(D) * 2;
+  DSB_CUDA_TRY(m->ctx, cudaMemcpy2D(reinterpret_cast<uint8_t*>(dst) + half * 64 * row, 128 * row, src.data(), 64 * row,
+                                    64 * row, I / 64, cudaMemcpyHostToDevice));
+  return DSB_OK;
+}
+
+bool parse_layer(const std::string& name, int* layer, std::string* rest) {
+  static const std::string pre = "model.layers.";
+  if (name.compare(0, pre.size(), pre) != 0) return false;
+  size_t i = pre.size(), j = i;
+  while (j < name.size() && name[j] >= '0' && name[j] <= '9') ++j;
+  if (j == i || j >= name.size() || name[j] != '.') return false;
+  *layer = std::stoi(name.substr(i, j - i));
+  *rest = name.substr(j + 1);
+  return true;
+}
+
+bool parse_expert(const std::string& rest, int* e, std::string* proj) {
+  static const std::string pre = "mlp.experts.";
+  if (rest.compare(0, pre.size(), pre) != 0) return false;
+  size_t i = pre.size(), j = i;
+  while (j < rest.size() && rest[j] >= '0' && rest[j] <= '9') ++j;
+  if (j == i || j >= rest.size() || rest[j] != '.') return false;
+  *e = std::stoi(rest.substr(i, j - i));
+  *proj = rest.substr(j + 1);
+  return true;
+}
+
+int64_t numel(const int64_t* shape, int ndim) {
+  int64_t n = 1;
+  for (int i = 0; i < ndim; ++i) n *= shape[i];
+  return n;
+}
+
+// ----------------------------------------------------- synthetic random init
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+  x ^= x >> 30;
+  x *= 0xbf58476d1ce4e5b9ull;
+  x ^= x >> 27;
+  x *= 0x94d049bb133111ebull;
+  x ^= x >> 31;
+  return x;
+}
+
+// N(0, std) bf16 values from a counter-based hash (Box-Muller on two 24-bit
+// uniforms), so a multi-GB random model needs no host traffic.
+__global__ void init_normal_bf16_kernel(bf16* p, int64_t n, uint64_t seed, float stddev) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = mix64(seed * 0x9e3779b97f4a7c15ull + (uint64_t)i);
+    const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = ((float)((h >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+    p[i] = __float2bfloat16_rn(stddev * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+  }
+}
+
+__global__ void init_normal_f32_kernel(float* p, int64_t n, uint64_t seed, float stddev, float mean) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = mix64(seed * 0x9e3779b97f4a7c15ull + (uint64_t)i);
+    const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = ((float)((h >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+    p[i] = mean + stddev * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+  }
+}
+
+int rand_bf16(dsb_model* m, bf16** p, int64_t n, uint64_t seed, float stddev) {
+  int rc = dev_alloc(m, p, (size_t)n);
+  if (rc != DSB_OK) return rc;
+  init_normal_bf16_kernel<<<1184, 256, 0, m->ctx->stream>>>(*p, n, seed, stddev);
+  DSB_CUDA_TRY(m->ctx, cudaGetLastError());
+  return DSB_OK;
+}
+
+int rand_f32(dsb_model* m, float** p, int64_t n, uint64_t seed, float stddev, float mean) {
+  int rc = dev_alloc(m, p, (size_t)n);
+  if (rc != DSB_OK) return rc;
+  init_normal_f32_kernel<<<1184, 256, 0, m->ctx->stream>>>(*p, n, seed, stddev, mean);
+  DSB_CUDA_TRY(m->ctx, cudaGetLastError());
+  return DSB_OK;
+}
+
+// ------------------------------------------------------------- decode step
+
+struct StepBuffers {
+  float *h, *xn32, *kv_a, *qa, *logits_r, *wts, *w_perm, *y_perm, *s_out, *logits;
+  bf16 *xn, *q, *q_rope, *q_lat, *o_lat, *attn, *mid, *x_perm, *mid_perm, *qa_n;
+  int32_t *ids, *counts, *offsets, *dest, *src, *greedy, *tokens, *pos, *bt;
+  void* items;
+  size_t items_off_comb;
+};
+
+int linear(dsb_ctx* ctx, const void* w, int64_t ldw, const void* x, int64_t ldx, int T, int M, int K, void* y,
+           int64_t ldy, int y_f32, int epi, int G = 1, int64_t xgc = 0, int64_t ygc = 0,
+           const int32_t* tok_offsets = nullptr, int max_tok = 0, const float* row_scale = nullptr) {
+  dsb_linear_args a{};
+  a.w = w;
+  a.ldw = ldw;
+  a.x = x;
+  a.ldx = ldx;
+  a.x_group_col = xgc;
+  a.tok_offsets = tok_offsets;
+  a.T = T;
+  a.M = M;
+  a.K = K;
+  a.G = G;
+  a.max_tokens_per_group = max_tok;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_group_col = ygc;
+  a.y_f32 = y_f32;
+  a.epilogue = epi;
+  a.row_scale = row_scale;
+  return dsb_linear(ctx, &a);
+}
+
+}  // namespace
+}  // namespace dsb
+
+using namespace dsb;
+
+// ===================================================================== model
+
+extern "C" int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out) {
+  if (ctx == nullptr || cfg == nullptr || out == nullptr) return DSB_EINVAL;
+  *out = nullptr;
+  const dsb_model_config& c = *cfg;
+  if (c.hidden_size <= 0 || c.num_hidden_layers <= 0 || c.num_attention_heads <= 0 || c.vocab_size <= 0 ||
+      c.kv_lora_rank <= 0 || c.qk_rope_head_dim <= 0 || c.v_head_dim <= 0 || c.qk_nope_head_dim <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_model_create: missing required sizes");
+  if (c.hidden_size % 64 || c.qk_nope_head_dim % 64 || c.kv_lora_rank % 64 || (c.num_attention_heads * c.v_head_dim) % 64)
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_create: hidden, nope, kv_lora_rank and heads*v must be multiples of 64");
+  if (!((c.kv_lora_rank == 512 && c.qk_rope_head_dim == 64) || (c.kv_lora_rank == 128 && c.qk_rope_head_dim == 32)))
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_create: (kv_lora_rank, rope) must be (512, 64) or (128, 32)");
+  if (c.num_attention_heads > 128) return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_create: at most 128 heads");
+  if (c.n_routed_experts > 256 || c.num_experts_per_tok > 8)
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_create: at most 256 experts and top-8");
+  auto* m = new dsb_model();
+  m->ctx = ctx;
+  m->cfg = c;
+  m->layers.resize(c.num_hidden_layers);
+  *out = m;
+  return DSB_OK;
+}
+
+extern "C" int dsb_model_destroy(dsb_model* m) {
+  if (m == nullptr) return DSB_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+  return DSB_OK;
+}
+
+extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, const int64_t* shape, int ndim,
+                                    const void* data) {
+  if (m == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = m->ctx;
+  if (cname == nullptr || shape == nullptr || data == nullptr || ndim < 1 || ndim > 2 ||
+      (dtype != DSB_DTYPE_F32 && dtype != DSB_DTYPE_BF16 && dtype != DSB_DTYPE_F16))
+    return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: bad arguments");
+  if (m->finalized) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: model already finalized");
+  const dsb_model_config& c = m->cfg;
+  const std::string name(cname);
+  const int64_t n = numel(shape, ndim);
+  const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
+  const int nope = c.qk_nope_head_dim, v = c.v_head_dim;
+  auto expect = [&](int64_t r0, int64_t r1) -> bool {
+    return (ndim == 2 && shape[0] == r0 && shape[1] == r1) || (ndim == 1 && r1 == 0 && shape[0] == r0);
+  };
+  auto bad_shape = [&]() { return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s has an unexpected shape", cname); };
+
+  if (name == "model.embed_tokens.weight") {
+    if (!expect(c.vocab_size, D)) return bad_shape();
+    if (dtype == DSB_DTYPE_F32) {
+      m->embed_bf16 = 0;
+      float* p = nullptr;
+      int rc = upload(m, &p, data, (size_t)n);
+      m->embed = p;
+      return rc;
+    }
+    m->embed_bf16 = 1;
+    auto b = to_bf16(data, dtype, n);
+    bf16* p = nullptr;
+    int rc = upload(m, &p, b.data(), (size_t)n);
+    m->embed = p;
+    return rc;
+  }
+  if (name == "model.norm.weight") {
+    if (!expect(D, 0)) return bad_shape();
+    auto f = to_f32(data, dtype, n);
+    return upload(m, &m->final_norm, f.data(), (size_t)n);
+  }
+  if (name == "lm_head.weight") {
+    if (!expect(c.vocab_size, D)) return bad_shape();
+    auto b = to_bf16(data, dtype, n);
+    return upload(m, &m->lm_head, b.data(), (size_t)n);
+  }
+  int li = -1;
+  std::string rest;
+  if (!parse_layer(name, &li, &rest) || li < 0 || li >= c.num_hidden_layers)
+    return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
+  auto& L = m->layers[li];
+  auto norm_f32 = [&](float** dst, int64_t len) -> int {
+    if (!expect(len, 0)) return bad_shape();
+    auto f = to_f32(data, dtype, n);
+    return upload(m, dst, f.data(), (size_t)n);
+  };
+  auto mat_bf16 = [&](bf16** dst, int64_t r0, int64_t r1) -> int {
+    if (!expect(r0, r1)) return bad_shape();
+    auto b = to_bf16(data, dtype, n);
+    return upload(m, dst, b.data(), (size_t)n);
+  };
+  if (rest == "input_layernorm.weight") return norm_f32(&L.in_norm, D);
+  if (rest == "post_attention_layernorm.weight") return norm_f32(&L.post_norm, D);
+  if (rest == "self_attn.q_proj.weight") return mat_bf16(&L.w_q, (int64_t)H * (nope + P), D);
+  if (rest == "self_attn.q_a_proj.weight") return mat_bf16(&L.w_qa, c.q_lora_rank, D);
+  if (rest == "self_attn.q_a_layernorm.weight") return norm_f32(&L.qa_norm, c.q_lora_rank);
+  if (rest == "self_attn.q_b_proj.weight") return mat_bf16(&L.w_qb, (int64_t)H * (nope + P), c.q_lora_rank);
+  if (rest == "self_attn.kv_a_proj_with_mqa.weight") return mat_bf16(&L.w_kva, R + P, D);
+  if (rest == "self_attn.kv_a_layernorm.weight") return norm_f32(&L.kva_norm, R);
+  if (rest == "self_attn.o_proj.weight") return mat_bf16(&L.w_o, D, (int64_t)H * v);
+  if (rest == "self_attn.kv_b_proj.weight") {
+    // kv_b rows per head: [nope rows of W_UK | v rows of W_UV], each [*, R] (mla.cpp:99-102)
+    if (!expect((int64_t)H * (nope + v), R)) return bad_shape();
+    auto b = to_bf16(data, dtype, n);
+    std::vector<uint16_t> uk_t((size_t)H * R * nope), uv((size_t)H * v * R);
+    for (int h = 0; h < H; ++h) {
+      const uint16_t* base = b.data() + (size_t)h * (nope + v) * R;
+      for (int i = 0; i < nope; ++i)
+        for (int r = 0; r < R; ++r) uk_t[((size_t)h * R + r) * nope + i] = base[(size_t)i * R + r];
+      std::memcpy(uv.data() + (size_t)h * v * R, base + (size_t)nope * R, (size_t)v * R * 2);
+    }
+    int rc = upload(m, &L.w_uk_t, uk_t.data(), uk_t.size());
+    if (rc != DSB_OK) return rc;
+    return upload(m, &L.w_uv, uv.data(), uv.size());
+  }
+  if (rest == "mlp.gate.weight") {
+    if (ndim != 2 || shape[0] != c.n_routed_experts || shape[1] != D) return bad_shape();
+    L.has_moe_tensors = true;
+    auto f = to_f32(data, dtype, n);
+    return upload(m, &L.w_router, f.data(), (size_t)n);
+  }
+  if (rest == "mlp.gate.e_score_correction_bias") {
+    if (!expect(c.n_routed_experts, 0)) return bad_shape();
+    auto f = to_f32(data, dtype, n);
+    return upload(m, &L.router_bias, f.data(), (size_t)n);
+  }
+  // dense MLP / shared experts: gate and up go to one interleaved matrix
+  struct Ffn {
+    const char* prefix;
+    bf16** gu;
+    bf16** down;
+    int* inter;
+  } ffns[2] = {{"mlp.", &L.w_gu, &L.w_down, &L.inter}, {"mlp.shared_experts.", &L.s_gu, &L.s_down, &L.s_inter}};
+  for (auto& f : ffns) {
+    const std::string pre(f.prefix);
+    const bool shared = pre != "mlp.";
+    for (int half = 0; half < 2; ++half) {
+      if (rest == pre + (half ? "up_proj.weight" : "gate_proj.weight")) {
+        if (ndim != 2 || shape[1] != D) return bad_shape();
+        const int I = (int)shape[0];
+        if (*f.inter != 0 && *f.inter != I) return bad_shape();
+        *f.inter = I;
+        if (*f.gu == nullptr) {
+          int rc = dev_alloc(m, f.gu, (size_t)2 * I * D);
+          if (rc != DSB_OK) return rc;
+        }
+        auto b = to_bf16(data, dtype, n);
+        if (!shared) (half ? L.seen_up : L.seen_gate) |= 1;
+        else (half ? L.seen_up : L.seen_gate) |= 2;
+        return upload_gate_up_half(m, *f.gu, b, I, D, half);
+      }
+    }
+    if (rest == pre + "down_proj.weight") {
+      if (ndim != 2 || shape[0] != D) return bad_shape();
+      const int I = (int)shape[1];
+      if (*f.inter != 0 && *f.inter != I) return bad_shape();
+      *f.inter = I;
+      auto b = to_bf16(data, dtype, n);
+      return upload(m, f.down, b.data(), (size_t)n);
+    }
+  }
+  int e = -1;
+  std::string proj;
+  if (parse_expert(rest, &e, &proj)) {
+    const int E = c.n_routed_experts;
+    if (e < 0 || e >= E) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: expert index out of range in %s", cname);
+    L.has_moe_tensors = true;
+    const bool is_down = proj == "down_proj.weight";
+    if (!is_down && proj != "gate_proj.weight" && proj != "up_proj.weight")
+      return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
+    if (ndim != 2) return bad_shape();
+    const int I = is_down ? (int)shape[1] : (int)shape[0];
+    if ((is_down ? shape[0] : shape[1]) != D) return bad_shape();
+    if (L.e_inter != 0 && L.e_inter != I) return bad_shape();
+    L.e_inter = I;
+    if (L.e_gu == nullptr) {
+      int rc = dev_alloc(m, &L.e_gu, (size_t)E * 2 * I * D);
+      if (rc == DSB_OK) rc = dev_alloc(m, &L.e_down, (size_t)E * D * I);
+      if (rc != DSB_OK) return rc;
+    }
+    auto b = to_bf16(data, dtype, n);
+    if (is_down) {
+      DSB_CUDA_TRY(ctx, cudaMemcpy(L.e_down + (size_t)e * D * I, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+      return DSB_OK;
+    }
+    return upload_gate_up_half(m, L.e_gu + (size_t)e * 2 * I * D, b, I, D, proj == "up_proj.weight" ? 1 : 0);
+  }
+  return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
+}
+
+extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) {
+  if (m == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = m->ctx;
+  if (m->finalized || !m->allocs.empty()) return fail(ctx, DSB_EINVAL, "dsb_model_init_random: model not empty");
+  const dsb_model_config& c = m->cfg;
+  const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
+  const int nope = c.qk_nope_head_dim, v = c.v_head_dim, E = c.n_routed_experts;
+  uint64_t s = seed * 1000003ull;
+  int rc = DSB_OK;
+  auto nb = [&](bf16** p, int64_t n) { if (rc == DSB_OK) rc = rand_bf16(m, p, n, ++s, stddev); };
+  auto ones = [&](float** p, int64_t n) { if (rc == DSB_OK) rc = rand_f32(m, p, n, ++s, 0.0f, 1.0f); };
+  m->embed_bf16 = 1;
+  bf16* emb = nullptr;
+  nb(&emb, (int64_t)c.vocab_size * D);
+  m->embed = emb;
+  ones(&m->final_norm, D);
+  nb(&m->lm_head, (int64_t)c.vocab_size * D);
+  for (int li = 0; li < c.num_hidden_layers && rc == DSB_OK; ++li) {
+    auto& L = m->layers[li];
+    ones(&L.in_norm, D);
+    ones(&L.post_norm, D);
+    if (c.q_lora_rank > 0) {
+      nb(&L.w_qa, (int64_t)c.q_lora_rank * D);
+      ones(&L.qa_norm, c.q_lora_rank);
+      nb(&L.w_qb, (int64_t)H * (nope + P) * c.q_lora_rank);
+    } else {
+      nb(&L.w_q, (int64_t)H * (nope + P) * D);
+    }
+    nb(&L.w_kva, (int64_t)(R + P) * D);
+    ones(&L.kva_norm, R);
+    nb(&L.w_uk_t, (int64_t)H * R * nope);
+    nb(&L.w_uv, (int64_t)H * v * R);
+    nb(&L.w_o, (int64_t)D * H * v);
+    const bool moe = E > 0 && li >= c.first_k_dense_replace;
+    if (!moe) {
+      L.inter = c.intermediate_size;
+      nb(&L.w_gu, (int64_t)2 * L.inter * D);
+      nb(&L.w_down, (int64_t)D * L.inter);
+    } else {
+      L.has_moe_tensors = true;
+      if (rc == DSB_OK) rc = rand_f32(m, &L.w_router, (int64_t)E * D, ++s, stddev, 0.0f);
+      if (c.scoring_func == DSB_SCORE_SIGMOID && rc == DSB_OK) rc = rand_f32(m, &L.router_bias, E, ++s, 0.01f, 0.0f);
+      L.e_inter = c.moe_intermediate_size;
+      nb(&L.e_gu, (int64_t)E * 2 * L.e_inter * D);
+      nb(&L.e_down, (int64_t)E * D * L.e_inter);
+      if (c.n_shared_experts > 0) {
+        L.s_inter = c.n_shared_experts * c.moe_intermediate_size;
+        nb(&L.s_gu, (int64_t)2 * L.s_inter * D);
+        nb(&L.s_down, (int64_t)D * L.s_inter);
+      }
+    }
+  }
+  if (rc != DSB_OK) return rc;
+  DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  return dsb_model_finalize(m);
+}
+
+extern "C" int dsb_model_finalize(dsb_model* m) {
+  if (m == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = m->ctx;
+  const dsb_model_config& c = m->cfg;
+  if (m->embed == nullptr || m->final_norm == nullptr || m->lm_head == nullptr)
+    return fail(ctx, DSB_EINVAL, "dsb_model_finalize: embed_tokens, norm or lm_head missing");
+  for (int li = 0; li < c.num_hidden_layers; ++li) {
+    auto& L = m->layers[li];
+    // dense vs MoE by the presence of routed experts (weights.cpp:89-96)
+    L.moe = L.has_moe_tensors;
+    const bool q_ok = L.w_q != nullptr || (L.w_qa != nullptr && L.qa_norm != nullptr && L.w_qb != nullptr);
+    if (!L.in_norm || !L.post_norm || !q_ok || !L.w_kva || !L.kva_norm || !L.w_uk_t || !L.w_o)
+      return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d attention weights incomplete", li);
+    if (L.moe) {
+      if (!L.w_router || !L.e_gu || !L.e_down || c.n_routed_experts <= 0 || c.num_experts_per_tok <= 0)
+        return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d MoE weights incomplete", li);
+      if (c.scoring_func == DSB_SCORE_SIGMOID && !L.router_bias)
+        return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d needs e_score_correction_bias", li);
+      if (L.s_gu != nullptr && L.s_down == nullptr)
+        return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d shared experts incomplete", li);
+    } else if (!L.w_gu || !L.w_down) {
+      return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d dense MLP incomplete", li);
+    }
+  }
+  m->finalized = true;
+  return DSB_OK;
+}
+
+extern "C" int dsb_model_weight_bytes(const dsb_model* m, uint64_t* bytes) {
+  if (m == nullptr || bytes == nullptr) return DSB_EINVAL;
+  *bytes = m->weight_bytes;
+  return DSB_OK;
+}
+
+// ================================================================= KV cache
+
+extern "C" int dsb_kvcache_create(dsb_ctx* ctx, const dsb_model* m, int64_t n_blocks, int max_seqs,
+                                  int max_blocks_per_seq, dsb_kvcache** out) {
+  if (ctx == nullptr || m == nullptr || out == nullptr) return DSB_EINVAL;
+  *out = nullptr;
+  if (n_blocks <= 0 || n_blocks > INT32_MAX || max_seqs <= 0 || max_blocks_per_seq <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_kvcache_create: bad sizes");
+  auto* kv = new dsb_kvcache();
+  kv->ctx = ctx;
+  kv->n_layers = m->cfg.num_hidden_layers;
+  kv->R = m->cfg.kv_lora_rank;
+  kv->P = m->cfg.qk_rope_head_dim;
+  kv->n_blocks = n_blocks;
+  kv->max_seqs = max_seqs;
+  kv->max_blocks_per_seq = max_blocks_per_seq;
+  const size_t bytes = (size_t)kv->n_layers * n_blocks * 64 * (kv->R + kv->P) * 2;
+  cudaError_t e = cudaMalloc(&kv->pool, bytes);
+  if (e != cudaSuccess) {
+    delete kv;
+    return fail(ctx, DSB_ENOMEM, "dsb_kvcache_create: %zu bytes: %s", bytes, cudaGetErrorString(e));
+  }
+  // zero-filled, so rows past a sequence's length are finite (MLACache::init zero-fills too, mla.cpp:21-22)
+  e = cudaMemsetAsync(kv->pool, 0, bytes, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    cudaFree(kv->pool);
+    delete kv;
+    return fail(ctx, DSB_ECUDA, "dsb_kvcache_create: %s", cudaGetErrorString(e));
+  }
+  kv->free_pages.reserve((size_t)n_blocks);
+  for (int64_t p = n_blocks - 1; p >= 0; --p) kv->free_pages.push_back((int32_t)p);
+  kv->seq_pages.resize(max_seqs);
+  kv->seq_len.assign(max_seqs, 0);
+  kv->seq_live.assign(max_seqs, 0);
+  *out = kv;
+  return DSB_OK;
+}
+
+extern "C" int dsb_kvcache_destroy(dsb_kvcache* kv) {
+  if (kv == nullptr) return DSB_OK;
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  cudaFree(kv->pool);
+  delete kv;
+  return DSB_OK;
+}
+
+extern "C" int dsb_kvcache_alloc_seq(dsb_kvcache* kv, int* seq_id) {
+  if (kv == nullptr || seq_id == nullptr) return DSB_EINVAL;
+  for (int s = 0; s < kv->max_seqs; ++s) {
+    if (!kv->seq_live[s]) {
+      kv->seq_live[s] = 1;
+      kv->seq_len[s] = 0;
+      kv->seq_pages[s].clear();
+      *seq_id = s;
+      return DSB_OK;
+    }
+  }
+  return fail(kv->ctx, DSB_ENOMEM, "dsb_kvcache_alloc_seq: all %d sequence slots in use", kv->max_seqs);
+}
+
+extern "C" int dsb_kvcache_free_seq(dsb_kvcache* kv, int seq_id) {
+  if (kv == nullptr) return DSB_EINVAL;
+  if (seq_id < 0 || seq_id >= kv->max_seqs || !kv->seq_live[seq_id])
+    return fail(kv->ctx, DSB_EINVAL, "dsb_kvcache_free_seq: %d is not a live sequence", seq_id);
+  for (int32_t p : kv->seq_pages[seq_id]) kv->free_pages.push_back(p);
+  kv->seq_pages[seq_id].clear();
+  kv->seq_len[seq_id] = 0;
+  kv->seq_live[seq_id] = 0;
+  return DSB_OK;
+}
+
+extern "C" int dsb_kvcache_reset(dsb_kvcache* kv) {
+  if (kv == nullptr) return DSB_EINVAL;
+  for (int s = 0; s < kv->max_seqs; ++s)
+    if (kv->seq_live[s]) dsb_kvcache_free_seq(kv, s);
+  return DSB_OK;
+}
+
+extern "C" int dsb_kvcache_seq_len(const dsb_kvcache* kv, int seq_id, int* len) {
+  if (kv == nullptr || len == nullptr || seq_id < 0 || seq_id >= kv->max_seqs || !kv->seq_live[seq_id])
+    return DSB_EINVAL;
+  *len = kv->seq_len[seq_id];
+  return DSB_OK;
+}
+
+extern "C" int dsb_kvcache_free_blocks(const dsb_kvcache* kv, int64_t* n) {
+  if (kv == nullptr || n == nullptr) return DSB_EINVAL;
+  *n = (int64_t)kv->free_pages.size();
+  return DSB_OK;
+}
+
+// =============================================================== decode step
+
+namespace dsb {
+// defined in mla_decode.cu
+int mla_plan_into_aux(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P, dsb_mla_plan* plan);
+}  // namespace dsb
+
+extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
+                               const int32_t* tokens, int B, float* logits_host, int32_t* greedy_host) {
+  if (ctx == nullptr || m == nullptr || kv == nullptr) return DSB_EINVAL;
+  if (!m->finalized) return fail(ctx, DSB_EINVAL, "dsb_decode_step: model not finalized");
+  if (seq_ids == nullptr || tokens == nullptr || greedy_host == nullptr || B <= 0 || B > kv->max_seqs)
+    return fail(ctx, DSB_EINVAL, "dsb_decode_step: bad arguments");
+  const dsb_model_config& c = m->cfg;
+  const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
+  const int nope = c.qk_nope_head_dim, v = c.v_head_dim, V = c.vocab_size, E = c.n_routed_experts;
+  const int k = c.num_experts_per_tok, QH = H * (nope + P), MB = kv->max_blocks_per_seq;
+
+  // ---- host: validate, append one position per sequence, build the step tables
+  for (int b = 0; b < B; ++b) {
+    const int s = seq_ids[b];
+    if (s < 0 || s >= kv->max_seqs || !kv->seq_live[s])
+      return fail(ctx, DSB_EINVAL, "dsb_decode_step: seq_ids[%d]=%d is not a live sequence", b, s);
+    if (tokens[b] < 0 || tokens[b] >= V)
+      return fail(ctx, DSB_EINVAL, "dsb_decode_step: token %d out of range", tokens[b]);
+    for (int b2 = 0; b2 < b; ++b2)
+      if (seq_ids[b2] == s) return fail(ctx, DSB_EINVAL, "dsb_decode_step: sequence %d appears twice", s);
+    if (kv->seq_len[s] >= MB * 64)
+      return fail(ctx, DSB_EINVAL, "dsb_decode_step: sequence %d is full (%d tokens)", s, kv->seq_len[s]);
+  }
+  int need_pages = 0;
+  for (int b = 0; b < B; ++b) need_pages += (kv->seq_len[seq_ids[b]] % 64 == 0) ? 1 : 0;
+  if ((size_t)need_pages > kv->free_pages.size())
+    return fail(ctx, DSB_ENOMEM, "dsb_decode_step: out of cache pages");
+  std::vector<int32_t> host_i((size_t)B * (2 + MB), 0);  // tokens | positions | block table
+  std::vector<int32_t> lens(B);
+  for (int b = 0; b < B; ++b) {
+    const int s = seq_ids[b];
+    const int pos = kv->seq_len[s];
+    if (pos % 64 == 0) {
+      kv->seq_pages[s].push_back(kv->free_pages.back());
+      kv->free_pages.pop_back();
+    }
+    kv->seq_len[s] = pos + 1;
+    lens[b] = pos + 1;
+    host_i[b] = tokens[b];
+    host_i[B + b] = pos;
+    const auto& pg = kv->seq_pages[s];
+    std::memcpy(host_i.data() + 2 * B + (size_t)b * MB, pg.data(), pg.size() * 4);
+  }
+
+  // ---- device buffers for this batch size (in the context workspace after the plan)
+  int max_I = 0, max_eI = 0, max_sI = 0;
+  bool any_moe = false, any_qlora = false;
+  for (auto& L : m->layers) {
+    max_I = std::max(max_I, L.inter);
+    max_eI = std::max(max_eI, L.e_inter);
+    max_sI = std::max(max_sI, L.s_inter);
+    any_moe |= L.moe;
+    any_qlora |= L.w_qa != nullptr;
+  }
+  const int BK = any_moe ? B * k : 1;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_h = take((size_t)B * D * 4), o_xn32 = take((size_t)B * D * 4), o_kva = take((size_t)B * (R + P) * 4);
+  const size_t o_qa = take(any_qlora ? (size_t)B * c.q_lora_rank * 4 : 4);
+  const size_t o_qan = take(any_qlora ? (size_t)B * c.q_lora_rank * 2 : 4);
+  const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)B * k * 4 + 4);
+  const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)BK * D * 4), o_sout = take((size_t)B * D * 4);
+  const size_t o_logits = take((size_t)B * V * 4), o_xn = take((size_t)B * D * 2), o_q = take((size_t)B * QH * 2);
+  const size_t o_qrope = take((size_t)B * H * P * 2), o_qlat = take((size_t)B * H * R * 2);
+  const size_t o_olat = take((size_t)B * H * R * 2), o_attn = take((size_t)B * H * v * 2);
+  const size_t o_mid = take((size_t)B * std::max({max_I, max_sI, 64}) * 2);
+  const size_t o_xperm = take((size_t)BK * D * 2), o_midp = take((size_t)BK * std::max(max_eI, 64) * 2);
+  const size_t o_ids = take((size_t)B * k * 4 + 4), o_cnt = take((size_t)(E + 1) * 4), o_off = take((size_t)(E + 2) * 4);
+  const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)B * 4);
+  const size_t o_tab = take(host_i.size() * 4);
+  // the step buffers live in their own context-owned region (ctx->step); the
+  // workspace ctx->ws stays free for split-K / split-KV partials
+  int rc = ensure_step(ctx, off);
+  if (rc != DSB_OK) return rc;
+  uint8_t* base = static_cast<uint8_t*>(ctx->step);
+  auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
+  auto Bf = [&](size_t o) { return reinterpret_cast<bf16*>(base + o); };
+  auto I32 = [&](size_t o) { return reinterpret_cast<int32_t*>(base + o); };
+  float *h = F(o_h), *xn32 = F(o_xn32), *kva = F(o_kva), *qa = F(o_qa), *lr = F(o_lr), *wts = F(o_wts);
+  float *wperm = F(o_wperm), *yperm = F(o_yperm), *sout = F(o_sout), *logits = F(o_logits);
+  bf16 *xn = Bf(o_xn), *q = Bf(o_q), *qrope = Bf(o_qrope), *qlat = Bf(o_qlat), *olat = Bf(o_olat), *attn = Bf(o_attn);
+  bf16 *mid = Bf(o_mid), *xperm = Bf(o_xperm), *midp = Bf(o_midp), *qan = Bf(o_qan);
+  int32_t *ids = I32(o_ids), *cnt = I32(o_cnt), *offs = I32(o_off), *dest = I32(o_dest), *src = I32(o_src);
+  int32_t *greedy = I32(o_greedy), *tab = I32(o_tab);
+  const int32_t *d_tok = tab, *d_pos = tab + B, *d_bt = tab + 2 * B;
+  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(tab, host_i.data(), host_i.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+
+  dsb_mla_plan plan;
+  rc = mla_plan_into_aux(ctx, lens.data(), B, H, R, P, &plan);
+  if (rc != DSB_OK) return rc;
+
+  const float scale = 1.0f / std::sqrt((float)(nope + P));  // mla.cpp:88
+  const int64_t layer_stride = kv->n_blocks * 64 * (int64_t)(R + P);
+#define DSB_STEP(call)          \
+  do {                          \
+    int rc_ = (call);           \
+    if (rc_ != DSB_OK) return rc_; \
+  } while (0)
+
+  DSB_STEP(embed(ctx, m->embed, m->embed_bf16, d_tok, B, D, h));
+  for (int li = 0; li < c.num_hidden_layers; ++li) {
+    const auto& L = m->layers[li];
+    bf16* cache = kv->pool + (int64_t)li * layer_stride;
+    // attention block (model.cpp:126-138)
+    DSB_STEP(rmsnorm_rows(ctx, h, D, L.in_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+    if (L.w_qa != nullptr) {
+      DSB_STEP(linear(ctx, L.w_qa, D, xn, D, B, c.q_lora_rank, D, qa, c.q_lora_rank, 1, DSB_EPI_STORE));
+      DSB_STEP(rmsnorm_rows(ctx, qa, c.q_lora_rank, L.qa_norm, B, c.q_lora_rank, c.rms_norm_eps, qan, c.q_lora_rank,
+                            nullptr, 0));
+      DSB_STEP(linear(ctx, L.w_qb, c.q_lora_rank, qan, c.q_lora_rank, B, QH, c.q_lora_rank, q, QH, 0, DSB_EPI_STORE));
+    } else {
+      DSB_STEP(linear(ctx, L.w_q, D, xn, D, B, QH, D, q, QH, 0, DSB_EPI_STORE));
+    }
+    DSB_STEP(linear(ctx, L.w_kva, D, xn, D, B, R + P, D, kva, R + P, 1, DSB_EPI_STORE));
+    DSB_STEP(kv_norm_rope_append(ctx, kva, L.kva_norm, q, d_pos, d_bt, MB, B, H, nope, R, P, c.rms_norm_eps,
+                                 c.rope_theta, cache, qrope));
+    // q_lat[:, h] = W_UK[h]^T q_nope[:, h]
+    DSB_STEP(linear(ctx, L.w_uk_t, nope, q, QH, B, R, nope, qlat, (int64_t)H * R, 0, DSB_EPI_STORE, H, nope + P, R));
+    DSB_STEP(dsb_mla_decode_planned(ctx, &plan, qlat, qrope, cache, kv->n_blocks, d_bt, MB, scale, olat));
+    // attn[:, h] = W_UV[h] o_lat[:, h], then h += o_proj(attn)
+    DSB_STEP(linear(ctx, L.w_uv, R, olat, (int64_t)H * R, B, v, R, attn, (int64_t)H * v, 0, DSB_EPI_STORE, H, R, v));
+    DSB_STEP(linear(ctx, L.w_o, (int64_t)H * v, attn, (int64_t)H * v, B, D, H * v, h, D, 1, DSB_EPI_ADD));
+    // feed-forward block (model.cpp:140-157)
+    if (!L.moe) {
+      DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+      DSB_STEP(linear(ctx, L.w_gu, D, xn, D, B, 2 * L.inter, D, mid, L.inter, 0, DSB_EPI_SILU_GATE));
+      DSB_STEP(linear(ctx, L.w_down, L.inter, mid, L.inter, B, D, L.inter, h, D, 1, DSB_EPI_ADD));
+    } else {
+      DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
+      DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
+      DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group, c.norm_topk_prob,
+                         c.routed_scaling_factor, ids, wts));
+      DSB_STEP(moe_permute(ctx, ids, B * k, E, cnt, offs, dest, src, wts, wperm));
+      DSB_STEP(gather_rows(ctx, xn, D, src, B * k, k, D, xperm));
+      const int eI = L.e_inter;
+      // every expert writes the same columns of its own (permuted) token rows
+      DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * k, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, E, 0, 0, offs, B));
+      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * k, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, E, 0, 0, offs, B,
+                      wperm));
+      const float* shared = nullptr;
+      if (L.s_gu != nullptr) {
+        DSB_STEP(linear(ctx, L.s_gu, D, xn, D, B, 2 * L.s_inter, D, mid, L.s_inter, 0, DSB_EPI_SILU_GATE));
+        DSB_STEP(linear(ctx, L.s_down, L.s_inter, mid, L.s_inter, B, D, L.s_inter, sout, D, 1, DSB_EPI_STORE));
+        shared = sout;
+      }
+      DSB_STEP(moe_combine(ctx, yperm, dest, B, k, D, shared, h));
+    }
+  }
+  // final norm, lm_head, greedy (model.cpp:160-179)
+  DSB_STEP(rmsnorm_rows(ctx, h, D, m->final_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+  DSB_STEP(linear(ctx, m->lm_head, D, xn, D, B, V, D, logits, V, 1, DSB_EPI_STORE));
+  DSB_STEP(argmax_rows(ctx, logits, V, B, V, greedy));
+#undef DSB_STEP
+  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(greedy_host, greedy, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (logits_host != nullptr)
+    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(logits_host, logits, (size_t)B * V * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  ctx->stats.decode_steps++;
+  return dsb_sync(ctx);
+}

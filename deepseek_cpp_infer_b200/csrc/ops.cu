@@ -283,7 +283,8 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
 // order, 32 at a time, ranking equal experts with match.any.
 __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ counts,
                                int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
-                               int32_t* __restrict__ src_pair) {
+                               int32_t* __restrict__ src_pair, const float* __restrict__ weights,
+                               float* __restrict__ w_perm) {
   extern __shared__ int32_t cnt[];  // [E]
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cnt[e] = 0;
@@ -322,6 +323,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
     const int d = offsets[ids[i]] + dest[i];
     dest[i] = d;
     src_pair[d] = i;
+    if (w_perm != nullptr) w_perm[d] = weights[i];
   }
 }
 
@@ -430,8 +432,9 @@ int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E
 }
 
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
-                int32_t* src_pair) {
-  permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair);
+                int32_t* src_pair, const float* weights, float* w_perm) {
+  permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair, weights,
+                                                               w_perm);
   return launched(ctx);
 }
 
@@ -508,12 +511,15 @@ extern "C" int dsb_moe_route(dsb_ctx* ctx, const float* logits, const float* bia
 }
 
 extern "C" int dsb_moe_permute(dsb_ctx* ctx, const int32_t* ids, int T, int k, int E, int32_t* counts,
-                               int32_t* offsets, int32_t* dest, int32_t* src_pair) {
+                               int32_t* offsets, int32_t* dest, int32_t* src_pair, const float* weights,
+                               float* w_perm) {
   if (ctx == nullptr) return DSB_EINVAL;
   if (ids == nullptr || counts == nullptr || offsets == nullptr || dest == nullptr || src_pair == nullptr || T <= 0 ||
       k <= 0 || E <= 0 || E > 4096)
     return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_permute: bad arguments");
-  return dsb::moe_permute(ctx, ids, T * k, E, counts, offsets, dest, src_pair);
+  if ((weights == nullptr) != (w_perm == nullptr))
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_permute: weights and w_perm go together");
+  return dsb::moe_permute(ctx, ids, T * k, E, counts, offsets, dest, src_pair, weights, w_perm);
 }
 
 extern "C" int dsb_gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k,

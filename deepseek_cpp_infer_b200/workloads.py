@@ -78,3 +78,76 @@ def to_u16(t) -> np.ndarray:
     import torch
 
     return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+# ------------------------------------------------------------------ models
+
+TINY = dict(
+    hidden_size=512, num_hidden_layers=4, num_attention_heads=8, vocab_size=4096, max_position_embeddings=256,
+    intermediate_size=1024, moe_intermediate_size=256, n_routed_experts=16, n_shared_experts=2,
+    num_experts_per_tok=4, first_k_dense_replace=1, q_lora_rank=0, kv_lora_rank=128, qk_nope_head_dim=64,
+    qk_rope_head_dim=32, v_head_dim=64, scoring_func=0, n_group=1, topk_group=1, norm_topk_prob=0,
+    routed_scaling_factor=1.0, rms_norm_eps=1e-6, rope_theta=10000.0,
+)
+
+V2_LITE = dict(
+    hidden_size=2048, num_hidden_layers=27, num_attention_heads=16, vocab_size=102400, max_position_embeddings=4096,
+    intermediate_size=10944, moe_intermediate_size=1408, n_routed_experts=64, n_shared_experts=2,
+    num_experts_per_tok=6, first_k_dense_replace=1, q_lora_rank=0, kv_lora_rank=512, qk_nope_head_dim=128,
+    qk_rope_head_dim=64, v_head_dim=128, scoring_func=0, n_group=1, topk_group=1, norm_topk_prob=0,
+    routed_scaling_factor=1.0, rms_norm_eps=1e-6, rope_theta=10000.0,
+)
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest bf16 value (ties to even), kept as float32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def model_tensors(cfg: dict, seed: int = 0, std: float = 0.02) -> dict:
+    """HF-named weights of a random-init DeepSeek-V2-style model: N(0, std)
+    matrices from numpy default_rng(seed), rounded to bf16 values, RMSNorm
+    weights 1.  Layers < first_k_dense_replace are dense, the rest MoE."""
+    rng = np.random.default_rng(seed)
+    D, H, R = cfg["hidden_size"], cfg["num_attention_heads"], cfg["kv_lora_rank"]
+    nope, P, v = cfg["qk_nope_head_dim"], cfg["qk_rope_head_dim"], cfg["v_head_dim"]
+    E, I, Is = cfg["n_routed_experts"], cfg["moe_intermediate_size"], cfg["n_shared_experts"] * cfg["moe_intermediate_size"]
+
+    def mat(*shape):
+        return bf16_round(rng.standard_normal(shape, dtype=np.float32) * std)
+
+    t = {"model.embed_tokens.weight": mat(cfg["vocab_size"], D)}
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        t[p + "input_layernorm.weight"] = np.ones(D, np.float32)
+        t[p + "post_attention_layernorm.weight"] = np.ones(D, np.float32)
+        t[p + "self_attn.q_proj.weight"] = mat(H * (nope + P), D)
+        t[p + "self_attn.kv_a_proj_with_mqa.weight"] = mat(R + P, D)
+        t[p + "self_attn.kv_a_layernorm.weight"] = np.ones(R, np.float32)
+        t[p + "self_attn.kv_b_proj.weight"] = mat(H * (nope + v), R)
+        t[p + "self_attn.o_proj.weight"] = mat(D, H * v)
+        if i < cfg["first_k_dense_replace"]:
+            Id = cfg["intermediate_size"]
+            t[p + "mlp.gate_proj.weight"] = mat(Id, D)
+            t[p + "mlp.up_proj.weight"] = mat(Id, D)
+            t[p + "mlp.down_proj.weight"] = mat(D, Id)
+        else:
+            t[p + "mlp.gate.weight"] = mat(E, D)
+            for e in range(E):
+                q = p + f"mlp.experts.{e}."
+                t[q + "gate_proj.weight"] = mat(I, D)
+                t[q + "up_proj.weight"] = mat(I, D)
+                t[q + "down_proj.weight"] = mat(D, I)
+            t[p + "mlp.shared_experts.gate_proj.weight"] = mat(Is, D)
+            t[p + "mlp.shared_experts.up_proj.weight"] = mat(Is, D)
+            t[p + "mlp.shared_experts.down_proj.weight"] = mat(D, Is)
+    t["model.norm.weight"] = np.ones(D, np.float32)
+    t["lm_head.weight"] = mat(cfg["vocab_size"], D)
+    return t
+
+
+def tiny_prompt(seed: int = 0, n: int = 32, vocab: int = 4096) -> np.ndarray:
+    """32 uniform token ids for the tiny-model generate workload."""
+    return np.random.default_rng(seed + 7).integers(0, vocab, n).astype(np.int32)

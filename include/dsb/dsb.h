@@ -58,6 +58,7 @@ typedef struct dsb_stats {
   uint64_t mla_partials;   /* work items that wrote a split-KV partial */
   uint64_t workspace_bytes;
   uint64_t gemm_calls;     /* dsb_linear launches */
+  uint64_t decode_steps;   /* dsb_decode_step calls */
 } dsb_stats;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -226,10 +227,11 @@ DSB_API int dsb_moe_route(dsb_ctx* ctx, const float* logits, const float* bias, 
 /* Histogram and permutation of the T*k (token, slot) pairs by expert:
  * counts [E], offsets [E+1] (exclusive prefix sum), dest [T*k] (position of
  * pair t*k+j in expert order, stable in pair order), src_pair [T*k] (its
- * inverse).  Replaces the per-expert host loop of moe_to_slot
- * (cuda_backend.cpp:854-874) and its top-k download + sync. */
+ * inverse); when weights [T*k] is given, w_perm[dest[i]] = weights[i].
+ * Replaces the per-expert host loop of moe_to_slot (cuda_backend.cpp:854-874)
+ * and its top-k download + sync. */
 DSB_API int dsb_moe_permute(dsb_ctx* ctx, const int32_t* ids, int T, int k, int E, int32_t* counts, int32_t* offsets,
-                            int32_t* dest, int32_t* src_pair);
+                            int32_t* dest, int32_t* src_pair, const float* weights, float* w_perm);
 
 /* out[p] = x[src_pair[p] / k] for bf16 rows of D (D, ldx multiples of 8). */
 DSB_API int dsb_gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k,
@@ -249,6 +251,76 @@ DSB_API int dsb_argmax(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int
 /* h[b] = fp32 embedding row tokens[b] of table [V, D] (bf16 when table_bf16,
  * else fp32); replaces embedding_to_slot (cuda_backend.cpp:716-732). */
 DSB_API int dsb_embed(dsb_ctx* ctx, const void* table, int table_bf16, const int32_t* tokens, int B, int D, float* h);
+
+/* ------------------------------------------------------ whole-model decode */
+
+#define DSB_DTYPE_F32 0
+#define DSB_DTYPE_BF16 1
+#define DSB_DTYPE_F16 2
+
+/* The model hyper-parameters the decode path reads: the fields of
+ * ds::hf::DeepSeekConfig (include/ds/models/deepseek/config.h:10-39) plus the
+ * DeepSeek-V3 router fields that config parser lacks (n_group, topk_group,
+ * scoring_func as DSB_SCORE_*). */
+typedef struct dsb_model_config {
+  int hidden_size, num_hidden_layers, num_attention_heads, vocab_size, max_position_embeddings;
+  int intermediate_size;     /* dense FFN */
+  int moe_intermediate_size; /* per routed expert */
+  int n_routed_experts, n_shared_experts, num_experts_per_tok, first_k_dense_replace;
+  int q_lora_rank; /* 0: q_proj */
+  int kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, v_head_dim;
+  int scoring_func, n_group, topk_group, norm_topk_prob;
+  float routed_scaling_factor, rms_norm_eps, rope_theta;
+} dsb_model_config;
+
+typedef struct dsb_model dsb_model;
+
+/* Device-resident model.  Replaces DeepSeekWeightRegistry
+ * (src/models/deepseek/weights.cpp:54-113) plus the executor's weight cache
+ * (cuda_backend.cpp:402-457): tensors are uploaded once by checkpoint name and
+ * kept in the layouts the kernels read (bf16 matrices; kv_b_proj split into
+ * per-head W_UK^T and W_UV; gate/up interleaved; norms and router fp32).
+ * A layer is MoE when its routed experts are given (weights.cpp:89-96). */
+DSB_API int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out);
+DSB_API int dsb_model_destroy(dsb_model* model);
+/* Upload one checkpoint tensor from HOST memory, named as in the HF
+ * safetensors ("model.layers.3.self_attn.kv_b_proj.weight", ...); dtype is
+ * DSB_DTYPE_*.  The caller keeps ownership of `data`. */
+DSB_API int dsb_model_set_tensor(dsb_model* model, const char* name, int dtype, const int64_t* shape, int ndim,
+                                 const void* data);
+/* Fill every weight on the device with N(0, stddev) (norms 1), layer kinds
+ * from first_k_dense_replace; for benchmarks of random-init models.
+ * Finalizes the model. */
+DSB_API int dsb_model_init_random(dsb_model* model, uint64_t seed, float stddev);
+/* Check completeness (every layer's attention and FFN weights present). */
+DSB_API int dsb_model_finalize(dsb_model* model);
+DSB_API int dsb_model_weight_bytes(const dsb_model* model, uint64_t* bytes);
+
+typedef struct dsb_kvcache dsb_kvcache;
+
+/* Paged latent KV cache for every layer: n_blocks pages of 64 tokens x
+ * (kv_lora_rank + rope) bf16 per layer, zero-filled, shared by up to
+ * max_seqs sequences of at most max_blocks_per_seq pages.  Replaces MLACache
+ * (src/models/deepseek/mla.cpp:16-39) / CudaMLACache (cuda_backend.cpp:81-88),
+ * which hold full per-head K and V in fp32. */
+DSB_API int dsb_kvcache_create(dsb_ctx* ctx, const dsb_model* model, int64_t n_blocks, int max_seqs,
+                               int max_blocks_per_seq, dsb_kvcache** out);
+DSB_API int dsb_kvcache_destroy(dsb_kvcache* kv);
+DSB_API int dsb_kvcache_alloc_seq(dsb_kvcache* kv, int* seq_id);
+DSB_API int dsb_kvcache_free_seq(dsb_kvcache* kv, int seq_id);
+/* Free every sequence (DeepSeekSession::reset, model.cpp:57-69). */
+DSB_API int dsb_kvcache_reset(dsb_kvcache* kv);
+DSB_API int dsb_kvcache_seq_len(const dsb_kvcache* kv, int seq_id, int* len);
+DSB_API int dsb_kvcache_free_blocks(const dsb_kvcache* kv, int64_t* n);
+
+/* One decode step: token tokens[b] of sequence seq_ids[b] (HOST arrays, B
+ * distinct live sequences) is appended at the sequence's current length and
+ * run through every layer; greedy ids (HOST int32 [B]) and, when logits is
+ * not NULL, the logits (HOST fp32 [B, vocab]) are returned.  Batched
+ * replacement of DeepSeekModel::decode_next (model.cpp:112-221); returns
+ * after the step completed on the device. */
+DSB_API int dsb_decode_step(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
+                            const int32_t* tokens, int B, float* logits, int32_t* greedy);
 
 #ifdef __cplusplus
 }

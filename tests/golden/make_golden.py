@@ -99,6 +99,58 @@ def moe(rng):
                 e_down=e_down, s_gate=s_gate, s_up=s_up, s_down=s_down, x=x, **res)
 
 
+def ref_model(cfg: dict, tensors: dict):
+    """Build the reference DeepSeekModel over in-memory f32 tensors."""
+    c = O.RefConfig(
+        hidden_size=cfg["hidden_size"], intermediate_size=cfg["intermediate_size"],
+        num_hidden_layers=cfg["num_hidden_layers"], num_attention_heads=cfg["num_attention_heads"],
+        vocab_size=cfg["vocab_size"], max_position_embeddings=cfg["max_position_embeddings"],
+        n_experts=cfg["n_routed_experts"], n_shared_experts=cfg["n_shared_experts"],
+        moe_top_k=cfg["num_experts_per_tok"], moe_intermediate_size=cfg["moe_intermediate_size"],
+        q_lora_rank=cfg["q_lora_rank"], kv_lora_rank=cfg["kv_lora_rank"], qk_nope_head_dim=cfg["qk_nope_head_dim"],
+        qk_rope_head_dim=cfg["qk_rope_head_dim"], v_head_dim=cfg["v_head_dim"], norm_topk_prob=cfg["norm_topk_prob"],
+        rms_norm_eps=cfg["rms_norm_eps"], rope_theta=cfg["rope_theta"],
+        routed_scaling_factor=cfg["routed_scaling_factor"])
+    names = list(tensors)
+    arrs = [np.ascontiguousarray(tensors[n], np.float32) for n in names]
+    c_names = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+    ndims = (ctypes.c_int * len(names))(*[a.ndim for a in arrs])
+    shapes = (ctypes.c_int64 * sum(a.ndim for a in arrs))(*[d for a in arrs for d in a.shape])
+    datas = (O.f32p * len(names))(*[O.p(a, O.f32p) for a in arrs])
+    h = O.ref().ref_model_create(ctypes.byref(c), len(names), c_names, ndims, shapes, datas)
+    assert h, "ref_model_create failed"
+    return h, arrs
+
+
+def tiny_model():
+    """cfg1: the reference generates 64 greedy tokens after a 32-token prompt;
+    teacher-forced logits on the same sequence are kept at a few steps."""
+    from deepseek_cpp_infer_b200.workloads import TINY, model_tensors, tiny_prompt
+
+    t = model_tensors(TINY, seed=0)
+    prompt = tiny_prompt(0)
+    h, keep = ref_model(TINY, t)
+    gen = np.zeros(64, np.int32)
+    assert O.ref().ref_model_generate(h, O.p(prompt, O.i32p), len(prompt), 64, O.p(gen, O.i32p)) == 0
+    seq = np.concatenate([prompt, gen])
+    O.ref().ref_model_reset(h)
+    steps = [31, 32, 40, 63, 95]
+    logits = np.zeros((len(steps), TINY["vocab_size"]), np.float32)
+    greedy = np.zeros(len(seq), np.int32)
+    row = np.zeros(TINY["vocab_size"], np.float32)
+    g = ctypes.c_int32()
+    for i, tok in enumerate(seq):
+        assert O.ref().ref_model_step(h, int(tok), O.p(row, O.f32p), ctypes.byref(g)) == 0
+        greedy[i] = g.value
+        if i in steps:
+            logits[steps.index(i)] = row
+    O.ref().ref_model_destroy(h)
+    assert np.array_equal(greedy[31:95], gen)  # teacher forcing reproduces the generation
+    checksum = np.array([float(np.sum([np.float64(a).sum() for a in t.values()]))])
+    return dict(prompt=prompt, generated=gen, greedy=greedy, steps=np.array(steps, np.int32), logits=logits,
+                weight_checksum=checksum)
+
+
 def main():
     O.build(with_ref=True)
     assert O.ref_available(), "reference build missing (oracle/_ref/libds_ref.so)"
@@ -106,6 +158,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "primitives.npz"), **primitives(rng))
     np.savez_compressed(os.path.join(HERE, "mla_layer.npz"), **mla_layer(rng))
     np.savez_compressed(os.path.join(HERE, "moe_softmax.npz"), **moe(rng))
+    np.savez_compressed(os.path.join(HERE, "tiny_model.npz"), **tiny_model())
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -1,0 +1,119 @@
+"""Whole-model decode (dsb_decode_step through the C ABI) against the
+reference's own DeepSeekModel on the tiny DeepSeek-V2-style configuration
+(4 layers, hidden 512, 8 heads, kv_lora_rank 128, 1 dense + 3 MoE layers with
+16 experts top-4 and 2 shared experts, vocab 4096; N(0, 0.02) weights rounded
+to bf16 values, seed 0).
+
+Pinned by tests/golden/tiny_model.npz (generated from oracle/_ref by
+tests/golden/make_golden.py): the reference's 64 greedy tokens after a
+32-token prompt, and its logits at a few teacher-forced steps.
+
+Bars: greedy ids identical for the first 32 generated tokens (the decode
+target) and for all 64 here; logits max-rel <= 2e-2 (max|gpu - ref| /
+max|ref|) at every stored step.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+import deepseek_cpp_infer_b200 as dsb
+from deepseek_cpp_infer_b200.workloads import TINY, model_tensors
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "tiny_model.npz")
+
+
+@pytest.fixture(scope="module")
+def tiny(gpu_ctx):
+    g = np.load(GOLD)
+    t = model_tensors(TINY, seed=0)
+    checksum = float(np.sum([np.float64(a).sum() for a in t.values()]))
+    assert abs(checksum - float(g["weight_checksum"][0])) < 1e-6, "weight generator changed"
+    m = dsb.Model(gpu_ctx, dsb.ModelConfig(**TINY))
+    for name, a in t.items():
+        m.set_tensor(name, a)
+    m.finalize()
+    yield m, g
+    m.close()
+
+
+def run_sequence(ctx, m, kv, tokens, n_new):
+    """Teacher-force `tokens`, then greedy-generate n_new; returns (greedy per step, logits per step)."""
+    s = kv.alloc_seq()
+    greedy, logits = [], []
+    nxt = None
+    for i in range(len(tokens) + n_new - 1):
+        tok = tokens[i] if i < len(tokens) else nxt
+        gid, lg = dsb.decode_step(ctx, m, kv, [s], [tok], want_logits=True)
+        greedy.append(int(gid[0]))
+        logits.append(lg[0])
+        nxt = int(gid[0])
+    kv.free_seq(s)
+    return np.array(greedy, np.int32), np.stack(logits)
+
+
+def test_tiny_model_greedy_matches_reference(gpu_ctx, tiny):
+    m, g = tiny
+    kv = dsb.KVCache(gpu_ctx, m, n_blocks=64, max_seqs=4, max_blocks_per_seq=8)
+    prompt, gen_ref = g["prompt"], g["generated"]
+    greedy, logits = run_sequence(gpu_ctx, m, kv, list(prompt), 64)
+    gen = greedy[len(prompt) - 1:]
+    assert gen[:32].tolist() == gen_ref[:32].tolist(), (gen[:32], gen_ref[:32])
+    assert gen.tolist() == gen_ref.tolist()
+    for i, step in enumerate(g["steps"]):
+        if step >= len(logits):  # the last stored step is past the generated sequence
+            continue
+        ref = g["logits"][i]
+        err = float(np.abs(logits[step] - ref).max() / np.abs(ref).max())
+        assert err <= 2e-2, (int(step), err)
+    kv.close()
+
+
+def test_tiny_model_teacher_forced_logits_and_batch_invariance(gpu_ctx, tiny):
+    """Three sequences decoded together (different prompts, different lengths)
+    give the same greedy ids and logits as each decoded alone."""
+    m, g = tiny
+    kv = dsb.KVCache(gpu_ctx, m, n_blocks=64, max_seqs=4, max_blocks_per_seq=8)
+    rng = np.random.default_rng(5)
+    prompts = [list(g["prompt"]), list(rng.integers(0, 4096, 20)), list(rng.integers(0, 4096, 70))]
+    alone = [run_sequence(gpu_ctx, m, kv, p, 1)[1] for p in prompts]
+    seqs = [kv.alloc_seq() for _ in prompts]
+    steps = max(len(p) for p in prompts)
+    together = [[] for _ in prompts]
+    for i in range(steps):
+        live = [j for j, p in enumerate(prompts) if i < len(p)]
+        gid, lg = dsb.decode_step(gpu_ctx, m, kv, [seqs[j] for j in live], [prompts[j][i] for j in live],
+                                  want_logits=True)
+        for r, j in enumerate(live):
+            together[j].append(lg[r])
+    for j in range(len(prompts)):
+        assert np.array_equal(np.stack(together[j]), alone[j])
+        assert kv.seq_len(seqs[j]) == len(prompts[j])
+    # the reference's teacher-forced logits on the golden sequence
+    ref_seq = np.concatenate([g["prompt"], g["generated"]])
+    _, lg = run_sequence(gpu_ctx, m, kv, list(ref_seq), 1)
+    for i, step in enumerate(g["steps"]):
+        ref = g["logits"][i]
+        err = float(np.abs(lg[step] - ref).max() / np.abs(ref).max())
+        print("teacher-forced logits max-rel at step", int(step), err)
+        assert err <= 2e-2
+    kv.close()
+
+
+def test_kvcache_pages_and_errors(gpu_ctx, tiny):
+    m, _ = tiny
+    kv = dsb.KVCache(gpu_ctx, m, n_blocks=3, max_seqs=2, max_blocks_per_seq=2)
+    assert kv.free_blocks() == 3
+    s = kv.alloc_seq()
+    for i in range(65):  # 65 tokens need 2 pages
+        dsb.decode_step(gpu_ctx, m, kv, [s], [i % 100])
+    assert kv.seq_len(s) == 65 and kv.free_blocks() == 1
+    with pytest.raises(dsb.DsbError):  # a token id outside the vocabulary
+        dsb.decode_step(gpu_ctx, m, kv, [s], [10**6])
+    with pytest.raises(dsb.DsbError):  # a sequence that is not live
+        dsb.decode_step(gpu_ctx, m, kv, [1], [0])
+    kv.free_seq(s)
+    assert kv.free_blocks() == 3
+    kv.close()
