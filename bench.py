@@ -1,14 +1,20 @@
 """Benchmark of the B200 decode hot path (one JSON line on rank 0).
 
-Workload (N=1, default): isolated absorbed-MLA decode attention at DeepSeek-V3
-shape - B=64 sequences, 128 heads, kv_lora_rank 512, rope 64, per-sequence
-context uniform in [1024, 8192] (seed 1), paged latent cache with 64-token
-pages and a random block-table permutation, bf16.  A step is one
-dsb_mla_decode call over the whole batch (64 query tokens).  Under torchrun
-each rank decodes its own batch (attention is data-parallel over the batch,
-no collective): weak scaling.
+Workload "model" (default): DeepSeek-V2-Lite-shaped batched decode - 27
+layers, hidden 2048, 16 heads, kv_lora_rank 512, 1 dense + 26 MoE layers (64
+experts top-6, 2 shared), vocab 102400; random-init N(0, 0.02) bf16 weights
+made on the device (seed 3); B=32 sequences per GPU with 512-token random
+prompts (prefilled token by token, untimed), then timed decode steps.  A step
+is one dsb_decode_step: one new token for each of the 32 sequences through
+every layer, greedy ids back to the host.  Under torchrun every rank runs its
+own replica on its own batch (weak scaling, no collective).
+
+Workload "mla": isolated absorbed-MLA decode attention at DeepSeek-V3 shape -
+B=64, 128 heads, kv_lora_rank 512, rope 64, context U[1024, 8192] (seed 1),
+64-token pages, random block table.  A step is one dsb_mla_decode call.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload model|mla]
 """
 
 from __future__ import annotations
@@ -150,7 +156,7 @@ def cpu_baseline_port(case, budget_s=15.0):
 # ------------------------------------------------------------------ arms
 
 
-def run_reference(args):
+def run_mla_reference(args):
     """The reference's CPU attention loop (oracle port) on the host cores."""
     import multiprocessing as mp
 
@@ -188,7 +194,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
+def run_mla_ours(args):
     import torch
     import torch.distributed as dist
 
@@ -315,19 +321,345 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ============================================================ model workload
+
+
+def model_cfg(args):
+    from deepseek_cpp_infer_b200.workloads import V2_LITE
+
+    cfg = dict(V2_LITE)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    return cfg
+
+
+def step_bytes(cfg, B, ctx_len):
+    """Algorithmic HBM bytes of one decode step: every weight the step must
+    read once (routed experts: the expected number touched by B tokens under
+    uniform routing, E * (1 - (1 - k/E)^B)), plus the KV rows attended."""
+    D, H, R, P = cfg["hidden_size"], cfg["num_attention_heads"], cfg["kv_lora_rank"], cfg["qk_rope_head_dim"]
+    nope, v, L = cfg["qk_nope_head_dim"], cfg["v_head_dim"], cfg["num_hidden_layers"]
+    E, k, I = cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
+    Is, Id, V = cfg["n_shared_experts"] * I, cfg["intermediate_size"], cfg["vocab_size"]
+    attn = (H * (nope + P) * D + (R + P) * D + H * R * nope + H * v * R + D * H * v) * 2
+    dense_layers = min(cfg["first_k_dense_replace"], L)
+    touched = E * (1 - (1 - k / E) ** B)
+    moe = touched * 3 * I * D * 2 + 3 * Is * D * 2 + E * D * 4
+    w = L * attn + dense_layers * 3 * Id * D * 2 + (L - dense_layers) * moe + V * D * 2
+    kv = L * B * ctx_len * (R + P) * 2
+    return int(w + kv), int(w), int(kv), touched
+
+
+def time_expert_gemm(ctx, stream, cfg, B, steps):
+    """The dominant kernel in isolation: the routed-expert gate|up GEMM of one
+    MoE layer (E groups of 2I x D bf16 weights, B*k permuted token rows from a
+    random top-k routing), timed with CUDA events on the context stream."""
+    import numpy as np
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+
+    D, E, k, I = cfg["hidden_size"], cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
+    rng = np.random.default_rng(11)
+    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(B)])
+    counts = np.bincount(ids.ravel(), minlength=E)
+    offs = torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).cuda()
+    w = (torch.randn(E * 2 * I, D, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(B * k, D, device="cuda").to(torch.bfloat16)
+    y = torch.empty(B * k, I, dtype=torch.bfloat16, device="cuda")
+
+    def launch():
+        ctx.linear(w, x, y, M=2 * I, K=D, G=E, tok_offsets=offs, max_tokens_per_group=B, epilogue=dsb.EPI_SILU_GATE)
+
+    for _ in range(5):
+        launch()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(steps, 20)
+    e0.record(stream)
+    for _ in range(n):
+        launch()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    touched = int((counts > 0).sum())
+    nbytes = touched * 2 * I * D * 2 + B * k * D * 2 + B * k * I * 2
+    del w
+    return ms, nbytes, touched
+
+
+def run_model_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import deepseek_cpp_infer_b200 as dsb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = model_cfg(args)
+    B, P = args.batch, args.prompt
+    ctx = dsb.Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    model = dsb.Model(ctx, dsb.ModelConfig(**cfg))
+    model.init_random(seed=3, stddev=0.02)
+    warm = max(3, args.warmup)
+    total = P + warm + args.steps * 2 + 64
+    max_blocks = (total + 63) // 64
+    kv = dsb.KVCache(ctx, model, n_blocks=B * max_blocks, max_seqs=B, max_blocks_per_seq=max_blocks)
+    seqs = [kv.alloc_seq() for _ in range(B)]
+    prompts = np.random.default_rng(3 + 1000 * rank).integers(0, cfg["vocab_size"], (B, P)).astype(np.int32)
+    t0 = time.time()
+    for i in range(P):  # token-serial prefill, as the reference's forward() does
+        greedy, _ = dsb.decode_step(ctx, model, kv, seqs, prompts[:, i])
+    prefill_s = time.time() - t0
+    nxt = greedy
+
+    def step(want_logits=False):
+        nonlocal nxt
+        nxt, lg = dsb.decode_step(ctx, model, kv, seqs, nxt, want_logits=want_logits)
+        return lg
+
+    def timed(n, want_logits=False):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            step(want_logits)
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(warm):
+        step()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.4)  # the sampler's first sample lands inside the timed region
+    ctx.reset_stats()
+    torch.cuda.synchronize()
+    ms = timed(args.steps)
+    clocks = sampler.stop()
+    st = ctx.stats()
+    launches = st["kernel_launches"]
+    ms_max = max_over_ranks(ms)
+    ctx_len = kv.seq_len(seqs[0])
+    # end to end: the reference's ForwardOutput carries the logits, so e2e also
+    # copies every step's [B, vocab] fp32 logits back to the host
+    barrier()
+    ms_e2e = max_over_ranks(timed(args.steps, want_logits=True))
+    # the dominant kernel alone, for the roofline line
+    g_ms, g_bytes, g_touched = time_expert_gemm(ctx, stream, cfg, B, args.steps)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = model_cpu_baseline(cfg, ctx_len, cores=1)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        tot, wbytes, kvbytes, touched = step_bytes(cfg, B, ctx_len)
+        line = {
+            "metric": METRIC, "value": world * B / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init N(0,0.02) bf16 weights (seed 3), uniform random prompt ids",
+            "config": {
+                "workload": f"DeepSeek-V2-Lite-shaped batched greedy decode: {cfg['num_hidden_layers']} layers, hidden "
+                            f"2048, 16 heads, kv_lora_rank 512, 1 dense + {cfg['num_hidden_layers'] - 1} MoE layers "
+                            f"(64 experts top-6 softmax, 2 shared, moe_inter 1408), vocab 102400; B={B} per GPU, "
+                            f"{P}-token prompts, step = one token for every sequence",
+                "global_batch": world * B, "seq_len": ctx_len, "parallelism": f"dp{world} (model replica per GPU)",
+                "step_bytes": tot, "weight_bytes_per_step": wbytes, "kv_bytes_per_step": kvbytes,
+                "experts_touched_per_layer": round(touched, 1), "prefill_s": round(prefill_s, 2),
+                "l2": "every step streams ~30 GB of weights, far above the 126 MB L2",
+                "step_roofline_frac": tot / (ms_max * 1e-3) / 1e9 / peak,
+            },
+            "roofline": {"bound": "hbm", "achieved": g_bytes / (g_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "gemm_bf16_kernel (routed-expert gate|up, SiLU epilogue)",
+                         "note": f"{g_touched} of 64 experts' 2816x2048 bf16 tiles + activations per launch / "
+                                 f"CUDA-event launch time ({g_ms * 1e3:.1f} us)"},
+            "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": B * 4 * (2 + max_blocks),
+                    "d2h_bytes_per_step": B * 4 + B * cfg["vocab_size"] * 4},
+            "gpu_launches": launches, "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _model_layer_times(cfg, ctx_len):
+    """Seconds of the reference's CPU path for one token through one layer of
+    each kind at V2-Lite shape, plus the lm_head: attention (mla_decode_step
+    at position 0 - its projections dominate; the per-head attention loop over
+    ctx_len cached tokens is added from a timed 64-token run), a dense MLP
+    (three ds::rt::linear calls), an MoE block (moe_step with 8 experts - the
+    per-token cost of 6 routed + 2 shared experts does not depend on E), and
+    a 1/10 slice of the lm_head scaled by 10.  Uses oracle/_ref (the
+    reference's own code) when present, else the oracle's restatements."""
+    import ctypes
+
+    import numpy as np
+
+    import oracle as O
+
+    D, H, R, P = cfg["hidden_size"], cfg["num_attention_heads"], cfg["kv_lora_rank"], cfg["qk_rope_head_dim"]
+    nope, v, I, Id, V = cfg["qk_nope_head_dim"], cfg["v_head_dim"], cfg["moe_intermediate_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    Is = cfg["n_shared_experts"] * I
+    use_ref = O.ref_available()
+    f = lambda *shape: np.full(shape, 0.01, np.float32)  # noqa: E731  values do not change the cost
+    c = O.RefConfig(hidden_size=D, num_attention_heads=H, qk_nope_head_dim=nope, qk_rope_head_dim=P, v_head_dim=v,
+                    kv_lora_rank=R, num_hidden_layers=1, vocab_size=V, max_position_embeddings=64, rms_norm_eps=1e-6,
+                    rope_theta=10000.0, routed_scaling_factor=1.0, n_experts=8, moe_top_k=6, moe_intermediate_size=I)
+    wq, wkva, wn, wkvb, wo = f(H * (nope + P), D), f(R + P, D), np.ones(R, np.float32), f(H * (nope + v), R), f(D, H * v)
+    hid = f(64, D)
+    out = np.zeros((64, D), np.float32)
+    args = [O.p(a, O.f32p) for a in (wq, wkva, wn, wkvb, wo, hid)]
+    t = time.perf_counter()
+    if use_ref:
+        O.ref().ref_mla_seq(ctypes.byref(c), *args, 1, O.p(out, O.f32p))
+    else:
+        O.oracle().orc_mla_layer_seq_f32(D, H, nope, P, v, R, 1e-6, 10000.0, *args, 1, O.p(out, O.f32p))
+    t_attn1 = time.perf_counter() - t
+    # attention-loop cost per cached token: positions 0..63 cost 64 projections + sum(pos) token visits
+    t = time.perf_counter()
+    if use_ref:
+        O.ref().ref_mla_seq(ctypes.byref(c), *args, 64, O.p(out, O.f32p))
+    else:
+        O.oracle().orc_mla_layer_seq_f32(D, H, nope, P, v, R, 1e-6, 10000.0, *args, 64, O.p(out, O.f32p))
+    t64 = time.perf_counter() - t
+    per_tok = max(0.0, (t64 - 64 * t_attn1) / (64 * 65 / 2))
+    t_attn = t_attn1 + per_tok * ctx_len
+    # dense MLP: gate, up [Id, D] and down [D, Id]
+    wg, wd = f(Id, D), f(D, Id)
+    x, y, z = f(D), np.zeros(Id, np.float32), np.zeros(D, np.float32)
+    lin = (lambda w, xi, n_in, yo, n_out: O.ref().ref_linear_f32(O.p(w, O.f32p), O.p(xi, O.f32p), n_in, O.p(yo, O.f32p), n_out)) \
+        if use_ref else (lambda w, xi, n_in, yo, n_out: O.oracle().orc_linear_f32(O.p(w, O.f32p), O.p(xi, O.f32p), n_in, O.p(yo, O.f32p), n_out))
+    t = time.perf_counter()
+    lin(wg, x, D, y, Id)
+    lin(wg, x, D, y, Id)
+    lin(wd, y, Id, z, D)
+    t_dense = time.perf_counter() - t
+    del wg, wd
+    # MoE block, 8 experts top-6 plus 2 shared (moe_step)
+    E = 8
+    eg, eu, ed = f(E, I, D), f(E, I, D), f(E, D, I)
+    sg, su, sd, gate = f(Is, D), f(Is, D), f(D, Is), f(E, D)
+    xo = np.zeros(D, np.float32)
+    t = time.perf_counter()
+    if use_ref:
+        O.ref().ref_moe_tokens(ctypes.byref(c), *(O.p(a, O.f32p) for a in (gate, eg, eu, ed, sg, su, sd)), Is,
+                               O.p(x, O.f32p), 1, O.p(xo, O.f32p))
+    else:
+        O.oracle().orc_moe_softmax_f32(*(O.p(a, O.f32p) for a in (gate, eg, eu, ed, sg, su, sd)), Is, D, E, 6, I, 0,
+                                       1.0, O.p(x, O.f32p), O.p(xo, O.f32p))
+    t_moe = time.perf_counter() - t
+    del eg, eu, ed
+    # lm_head: a tenth of the vocabulary, scaled
+    wl = f(V // 10, D)
+    yl = np.zeros(V // 10, np.float32)
+    t = time.perf_counter()
+    lin(wl, x, D, yl, V // 10)
+    t_lm = (time.perf_counter() - t) * 10
+    return t_attn, t_dense, t_moe, t_lm, ("reference" if use_ref else "port")
+
+
+def _model_cpu_token_seconds(cfg, ctx_len):
+    t_attn, t_dense, t_moe, t_lm, kind = _model_layer_times(cfg, ctx_len)
+    L = cfg["num_hidden_layers"]
+    nd = min(cfg["first_k_dense_replace"], L)
+    return L * t_attn + nd * t_dense + (L - nd) * t_moe + t_lm, kind
+
+
+def model_cpu_baseline(cfg, ctx_len, cores=1):
+    sec, kind = _model_cpu_token_seconds(cfg, ctx_len)
+    src = "oracle/_ref (the reference's own CPU code)" if kind == "reference" else "the oracle restatement"
+    return {"value": 1.0 / sec, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"one token through one V2-Lite-shaped layer of each kind (attention at context {ctx_len}, "
+                      f"dense MLP, MoE top-6 + 2 shared) and the lm_head on 1 thread via {src}, extrapolated to "
+                      f"{cfg['num_hidden_layers']} layers; the reference decodes one sequence at a time"}
+
+
+def _model_ref_worker(a):
+    cfg, ctx_len = a
+    return _model_cpu_token_seconds(cfg, ctx_len)
+
+
+def run_model_reference(args):
+    """The reference's own CPU decode path on every host core: each core runs
+    one sequence (the reference is single-sequence, single-threaded); a step
+    is one token per core, timed per layer kind and extrapolated to the whole
+    model (a full V2-Lite CPU step does not fit a few minutes)."""
+    import multiprocessing as mp
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = model_cfg(args)
+    cores = os.cpu_count() or 1
+    ctx_len = args.prompt + args.warmup + args.steps
+    with mp.get_context("spawn").Pool(cores) as pool:
+        res = pool.map(_model_ref_worker, [(cfg, ctx_len)] * cores)
+    per_tok = max(r[0] for r in res)  # the slowest core bounds the aggregate
+    kind = res[0][1]
+    tok_s = cores / per_tok
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_tok * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (constant weights; the CPU cost does not depend on values)",
+        "impl": "reference",
+        "config": {"workload": f"DeepSeek-V2-Lite-shaped greedy decode, {cfg['num_hidden_layers']} layers, one sequence "
+                               f"per core at context {ctx_len}", "cores": cores},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": "per core: one token through one layer of each kind and the lm_head, timed once "
+                                   "and extrapolated to the full model"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="model", choices=["model", "mla"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU (64 = the benchmark configuration)")
+    ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
+    ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
+    ap.add_argument("--layers", type=int, default=0, help="model layers (0 = the configuration's 27)")
     args = ap.parse_args()
-    if args.impl == "reference":
-        run_reference(args)
+    if args.workload == "mla":
+        args.batch = args.batch or 64
+        run_mla_reference(args) if args.impl == "reference" else run_mla_ours(args)
     else:
-        run_ours(args)
+        args.batch = args.batch or 32
+        run_model_reference(args) if args.impl == "reference" else run_model_ours(args)
 
 
 if __name__ == "__main__":
