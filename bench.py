@@ -33,6 +33,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s (box) at 1/2/4/8 B200; MLA/MoE HBM GB/s as % of peak"
 L2_BYTES = 126 * 1024 * 1024
+# dram__bytes_read.sum + dram__bytes_write.sum of one routed-expert gate|up
+# launch (B=32, V2-Lite shape) from an ncu --set full capture of
+# `python bench.py --workload expert-gemm --steps 5` (716.0 MB + 4.0 MB)
+EXPERT_GEMM_NCU_TRAFFIC = 719954176
 
 
 def measured_peaks():
@@ -493,7 +497,8 @@ def run_model_ours(args):
                 "step_roofline_frac": tot / (ms_max * 1e-3) / 1e9 / peak,
             },
             "roofline": {"bound": "hbm", "achieved": g_bytes / (g_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
-                         "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak, "traffic": EXPERT_GEMM_NCU_TRAFFIC,
+                         "peak_kind": peak_kind,
                          "kernel": "gemm_bf16_kernel (routed-expert gate|up, SiLU epilogue)",
                          "note": f"{g_touched} of 64 experts' 2816x2048 bf16 tiles + activations per launch / "
                                  f"CUDA-event launch time ({g_ms * 1e3:.1f} us)"},
@@ -642,19 +647,43 @@ def run_model_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_expert_gemm(args):
+    """The dominant kernel of the model step alone (one MoE layer's routed
+    gate|up GEMM at V2-Lite shape, B tokens top-6 of 64 experts); one JSON line."""
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+
+    torch.cuda.set_device(0)
+    ctx = dsb.Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    cfg = model_cfg(args)
+    ms, nbytes, touched = time_expert_gemm(ctx, stream, cfg, args.batch, args.steps)
+    peak, peak_kind = measured_peaks()
+    print(json.dumps({"workload": "routed-expert gate|up GEMM, V2-Lite shape", "tokens": args.batch,
+                      "experts_touched": touched, "us_per_launch": ms * 1e3, "bytes_per_launch": nbytes,
+                      "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_kind": peak_kind}),
+          flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "mla"])
+    ap.add_argument("--workload", default="model", choices=["model", "mla", "expert-gemm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
     ap.add_argument("--layers", type=int, default=0, help="model layers (0 = the configuration's 27)")
     args = ap.parse_args()
-    if args.workload == "mla":
+    if args.workload == "expert-gemm":
+        args.batch = args.batch or 32
+        run_expert_gemm(args)
+    elif args.workload == "mla":
         args.batch = args.batch or 64
         run_mla_reference(args) if args.impl == "reference" else run_mla_ours(args)
     else:
