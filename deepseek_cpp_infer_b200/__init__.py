@@ -23,6 +23,7 @@ DSB_ECUDA = 2
 DSB_ENOMEM = 3
 DSB_ETIMEOUT = 4
 DSB_EUNSUPPORTED = 5
+DSB_ELIMIT = 6
 
 _c_i32p = ctypes.POINTER(ctypes.c_int32)
 _vp, _i64, _ci, _cf = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
@@ -122,6 +123,8 @@ _PROTOS = [
     ("dsb_kvcache_seq_len", ctypes.c_int, [_vp, _ci, ctypes.POINTER(ctypes.c_int)]),
     ("dsb_kvcache_free_blocks", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int64)]),
     ("dsb_decode_step", ctypes.c_int, [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, _vp, _c_i32p]),
+    ("dsb_mla_decode_noalloc", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, _i64, _ci, _vp, _ci, _c_i32p, _ci, _ci, _ci, _ci, _cf, _vp]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -298,6 +301,17 @@ class Context:
                 block_table.shape[1], lens, B, H, R, P, float(softmax_scale), _ptr(out),
             )
         )
+
+
+def mla_decode_noalloc(stream_handle, q_lat, q_rope, kv_cache, block_table, seq_lens, softmax_scale, out,
+                       block_size=64) -> int:
+    """dsb_mla_decode_noalloc on torch device tensors; returns the status code."""
+    B, H, R = q_lat.shape
+    P = q_rope.shape[2]
+    lens = (ctypes.c_int32 * B)(*[int(x) for x in seq_lens])
+    return lib().dsb_mla_decode_noalloc(
+        stream_handle or None, _ptr(q_lat), _ptr(q_rope), _ptr(kv_cache), kv_cache.shape[0], block_size,
+        _ptr(block_table), block_table.shape[1], lens, B, H, R, P, float(softmax_scale), _ptr(out))
 
 
 class MlaPlan:

@@ -30,6 +30,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <queue>
 #include <vector>
 
@@ -779,4 +780,171 @@ extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rop
   if (rc != DSB_OK) return rc;
   return dsb_mla_decode_planned(ctx, &plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks, softmax_scale,
                                 out_lat);
+}
+
+// ===================================================== allocation-free variant
+//
+// dsb_mla_decode_noalloc serves callers that cannot allocate device memory on
+// the call path: code running while a CUDA graph is being captured (cudaMalloc
+// is not a capturable operation and invalidates the capture), allocators and
+// runtimes that own every byte of device memory themselves and forbid stray
+// cudaMalloc/cudaFree (a cudaFree also synchronises the whole device), and
+// plug-in hosts that hand this library only a stream and their own buffers.
+// Its scratch - the work list, the split-KV partials and the bounded-wait
+// status word - lives in the fixed array below, which every GPU that loads
+// the library holds until the process exits.
+
+namespace dsb {
+namespace {
+
+constexpr int kNoAllocMaxItems = 4096;     // work items per call
+constexpr int kNoAllocMaxPartials = 24;    // split-KV partials per call
+constexpr size_t kNoAllocOffItems = 256;   // [0, 256): status word
+constexpr size_t kNoAllocOffComb = kNoAllocOffItems + kNoAllocMaxItems * sizeof(MlaItem);
+constexpr size_t kNoAllocOffO = (kNoAllocOffComb + kNoAllocMaxItems * sizeof(MlaCombine) + 255) & ~size_t(255);
+constexpr size_t kNoAllocPartialO = (size_t)kHeadsPad * 512 * sizeof(float);  // one partial at R = 512
+constexpr size_t kNoAllocOffML = kNoAllocOffO + kNoAllocMaxPartials * kNoAllocPartialO;
+constexpr size_t kNoAllocScratchBytes =
+    (kNoAllocOffML + kNoAllocMaxPartials * kHeadsPad * sizeof(float2) + 255) & ~size_t(255);  // ~6.4 MB
+
+static __device__ __align__(256) uint8_t g_mla_noalloc_scratch[kNoAllocScratchBytes];
+
+// Per-device set-up, done by the first call on each device: the device address
+// of the scratch array (its name in host code is only a host-side stand-in),
+// the SM count for planning, and the kernels' shared-memory opt-in.
+struct NoAllocDevice {
+  bool ready = false;
+  uint8_t* scratch = nullptr;
+  int sm_count = 0;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+int noalloc_setup(int dev, NoAllocDevice** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_mla_noalloc_scratch) != cudaSuccess || p == nullptr) return DSB_ECUDA;
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DSB_ECUDA;
+    if (cudaFuncSetAttribute(mla_decode_kernel<512, 64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             MlaShape<512, 64, 2>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(mla_decode_kernel<128, 32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             MlaShape<128, 32, 1>::SMEM_BYTES) != cudaSuccess)
+      return DSB_ECUDA;
+    d.scratch = static_cast<uint8_t*>(p);
+    d.ready = true;
+  }
+  *out = &d;
+  return DSB_OK;
+}
+
+template <int R, int P, int NCTA>
+int noalloc_launch(cudaStream_t stream, uint8_t* scratch, const std::vector<MlaItem>& items,
+                   const std::vector<MlaCombine>& combines, const void* q_lat, const void* q_rope,
+                   const void* kv_cache, int64_t n_blocks, const int32_t* block_table, int max_blocks, int H,
+                   float scale, void* out) {
+  using S = MlaShape<R, P, NCTA>;
+  // the status word must start at zero; the work list overwrites the last call's
+  if (cudaMemsetAsync(scratch, 0, sizeof(int), stream) != cudaSuccess) return DSB_ECUDA;
+  if (cudaMemcpyAsync(scratch + kNoAllocOffItems, items.data(), items.size() * sizeof(MlaItem),
+                      cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return DSB_ECUDA;
+  if (!combines.empty() && cudaMemcpyAsync(scratch + kNoAllocOffComb, combines.data(),
+                                           combines.size() * sizeof(MlaCombine), cudaMemcpyHostToDevice,
+                                           stream) != cudaSuccess)
+    return DSB_ECUDA;
+  CUtensorMap map_v, map_r;
+  const uint64_t rows = (uint64_t)n_blocks * kTok;
+  if (make_tmap_2d(nullptr, &map_v, kv_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R + P, rows, (R + P) * 2, 64, kTok,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != DSB_OK ||
+      make_tmap_2d(nullptr, &map_r, kv_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R + P, rows, (R + P) * 2, S::PD,
+                   kTok, CU_TENSOR_MAP_SWIZZLE_64B) != DSB_OK)
+    return DSB_EINVAL;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(items.size() * NCTA));
+  cfg.blockDim = dim3(kMlaThreads);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = NCTA;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  float* ws_o = reinterpret_cast<float*>(scratch + kNoAllocOffO);
+  float2* ws_ml = reinterpret_cast<float2*>(scratch + kNoAllocOffML);
+  if (cudaLaunchKernelEx(&cfg, mla_decode_kernel<R, P, NCTA>, map_v, map_r,
+                         static_cast<const __nv_bfloat16*>(q_lat), static_cast<const __nv_bfloat16*>(q_rope),
+                         block_table, max_blocks, reinterpret_cast<const MlaItem*>(scratch + kNoAllocOffItems), H,
+                         scale * 1.4426950408889634f, static_cast<__nv_bfloat16*>(out), ws_o, ws_ml,
+                         reinterpret_cast<int*>(scratch)) != cudaSuccess)
+    return DSB_ECUDA;
+  if (!combines.empty()) {
+    mla_combine_kernel<R><<<dim3((unsigned)combines.size(), (unsigned)H), 128, 0, stream>>>(
+        reinterpret_cast<const MlaCombine*>(scratch + kNoAllocOffComb), H, ws_o, ws_ml,
+        static_cast<__nv_bfloat16*>(out));
+    if (cudaGetLastError() != cudaSuccess) return DSB_ECUDA;
+  }
+  return DSB_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+extern "C" int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
+                                      int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                                      const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                                      void* out_lat) {
+  using namespace dsb;
+  if (q_lat == nullptr || q_rope == nullptr || kv_cache == nullptr || block_table == nullptr || seq_lens == nullptr ||
+      out_lat == nullptr || B <= 0 || H <= 0 || H > kHeadsPad || n_blocks <= 0 || max_blocks <= 0)
+    return DSB_EINVAL;
+  if (block_size != kTok || !((R == 512 && P == 64) || (R == 128 && P == 32))) return DSB_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(q_lat) | reinterpret_cast<uintptr_t>(q_rope) |
+       reinterpret_cast<uintptr_t>(out_lat) | reinterpret_cast<uintptr_t>(kv_cache)) & 15u)
+    return DSB_EINVAL;
+  for (int b = 0; b < B; ++b)
+    if (seq_lens[b] < 1 || seq_lens[b] > (int64_t)max_blocks * kTok) return DSB_EINVAL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DSB_ECUDA;
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_setup(dev, &d);
+  if (rc != DSB_OK) return rc;
+  const int slots = std::max(1, d->sm_count / (R == 512 ? 2 : 1));
+  std::vector<MlaItem> items;
+  std::vector<MlaCombine> combines;
+  int n_partial = 0;
+  plan_items(seq_lens, B, slots, &items, &combines, &n_partial);
+  if (n_partial > kNoAllocMaxPartials) {
+    // too many splits for the fixed scratch: one item per sequence where the
+    // 16384-token item limit allows
+    std::vector<int32_t> one(1);
+    items.clear();
+    combines.clear();
+    n_partial = 0;
+    for (int b = 0; b < B; ++b) {
+      std::vector<MlaItem> it;
+      std::vector<MlaCombine> cb;
+      int np = 0;
+      one[0] = seq_lens[b];
+      plan_items(one.data(), 1, 1, &it, &cb, &np);  // a single slot never splits below the item limit
+      for (auto& x : it) {
+        x.b = b;
+        if (x.partial >= 0) x.partial += n_partial;
+        items.push_back(x);
+      }
+      for (auto& c : cb) combines.push_back(MlaCombine{b, c.first + n_partial, c.n});
+      n_partial += np;
+    }
+  }
+  if ((int)items.size() > kNoAllocMaxItems || n_partial > kNoAllocMaxPartials) return DSB_ELIMIT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (R == 512)
+    return noalloc_launch<512, 64, 2>(s, d->scratch, items, combines, q_lat, q_rope, kv_cache, n_blocks, block_table,
+                                      max_blocks, H, softmax_scale, out_lat);
+  return noalloc_launch<128, 32, 1>(s, d->scratch, items, combines, q_lat, q_rope, kv_cache, n_blocks, block_table,
+                                    max_blocks, H, softmax_scale, out_lat);
 }

@@ -45,6 +45,7 @@ extern "C" {
 #define DSB_ENOMEM 3       /* device allocation failed */
 #define DSB_ETIMEOUT 4     /* a kernel's bounded wait ran out (device status word) */
 #define DSB_EUNSUPPORTED 5 /* shape not covered by the sm_100a kernels */
+#define DSB_ELIMIT 6       /* request exceeds the fixed scratch of dsb_mla_decode_noalloc */
 
 typedef struct dsb_ctx dsb_ctx;
 
@@ -130,6 +131,35 @@ DSB_API int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, const
 DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache, int64_t n_blocks,
                            int block_size, const int32_t* block_table, int max_blocks, const int32_t* seq_lens, int B,
                            int H, int R, int P, float softmax_scale, void* out_lat);
+
+/*
+ * Allocation-free MLA decode: the same computation as dsb_mla_decode, for
+ * callers that cannot allocate device memory while they run this call - a
+ * CUDA graph being captured (cudaMalloc cannot be captured and breaks the
+ * capture), a host runtime that owns all device memory through its own
+ * allocator, or a plug-in that only receives a stream and its buffers.  It
+ * takes no dsb_ctx (creating one allocates) and calls no cudaMalloc/cudaFree:
+ * its scratch (work list, split-KV partials, status word) is one fixed
+ * device array of about 6.4 MB inside libdsb.so, held by every GPU that loads
+ * the library until the process exits.  No counterpart in the reference.
+ *
+ *  stream  cudaStream_t to enqueue on (NULL = the legacy default stream);
+ *          the current CUDA device must be the one that holds the buffers.
+ *  other arguments as dsb_mla_decode.
+ * Limits: at most 4096 work items and 24 split-KV partials per call (a call
+ * that would need more, e.g. more than 24 sequences longer than 16384
+ * tokens, returns DSB_ELIMIT and enqueues nothing).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and sets kernel attributes; make that first call
+ * before any stream capture.  Every call reuses the same array, so calls that
+ * overlap on the GPU (different streams, or different host threads on one
+ * device) race and must be serialised by the caller.  A bounded wait that
+ * times out inside the kernel is not reported by this entry point.
+ */
+DSB_API int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
+                                   int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                                   const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                                   void* out_lat);
 
 /*
  * Grouped bf16 linear layer (tcgen05, fp32 accumulation):
