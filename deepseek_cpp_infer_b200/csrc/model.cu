@@ -38,7 +38,7 @@ struct dsb_model {
     __nv_bfloat16* w_uk_t = nullptr; // [H*R, nope]   W_UK^T per head (from kv_b_proj)
     __nv_bfloat16* w_uv = nullptr;   // [H*v, R]      W_UV per head (from kv_b_proj)
     __nv_bfloat16* w_o = nullptr;    // [D, H*v]
-    __nv_bfloat16* w_gu = nullptr;   // dense gate|up interleaved per 128-row tile [2I, D]
+    __nv_bfloat16* w_gu = nullptr;   // dense gate|up, rows interleaved (2f gate, 2f+1 up) [2I, D]
     __nv_bfloat16* w_down = nullptr; // [D, I]
     int inter = 0;
     float* w_router = nullptr;       // [E, D] fp32
@@ -142,14 +142,15 @@ int upload(dsb_model* m, T** p, const void* host, size_t count) {
   return DSB_OK;
 }
 
-// Rows [0, I) of a gate (half 0) or up (half 1) projection [I, D] go to the
-// interleaved layout: 128-row tile i holds gate rows [64i, 64i+64) then the
-// matching up rows (the SiLU-gate epilogue of dsb_linear pairs lanes r, r+64).
+// Row f of a gate (half 0) or up (half 1) projection [I, D] goes to row
+// 2f + half of the fused [2I, D] matrix, so an output feature's gate and up
+// rows sit in adjacent TMEM lanes (the SiLU-gate epilogue of dsb_linear pairs
+// lanes 2j and 2j+1 with a warp shuffle).
 int upload_gate_up_half(dsb_model* m, bf16* dst, const std::vector<uint16_t>& src, int I, int D, int half) {
   if (I % 64 != 0) return fail(m->ctx, DSB_EUNSUPPORTED, "intermediate size %d is not a multiple of 64", I);
   const size_t row = static_cast<size_t>(D) * 2;
-  DSB_CUDA_TRY(m->ctx, cudaMemcpy2D(reinterpret_cast<uint8_t*>(dst) + half * 64 * row, 128 * row, src.data(), 64 * row,
-                                    64 * row, I / 64, cudaMemcpyHostToDevice));
+  DSB_CUDA_TRY(m->ctx, cudaMemcpy2D(reinterpret_cast<uint8_t*>(dst) + half * row, 2 * row, src.data(), row, row, I,
+                                    cudaMemcpyHostToDevice));
   return DSB_OK;
 }
 

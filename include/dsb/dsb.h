@@ -181,9 +181,8 @@ DSB_API int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* 
  * Epilogues:
  *  DSB_EPI_STORE      y = acc (bf16 or fp32 per y_f32)
  *  DSB_EPI_ADD        y += acc (fp32 y; residual add, replaces ds_add_inplace_kernel)
- *  DSB_EPI_SILU_GATE  w holds gate and up rows interleaved per 128-row tile
- *                     (rows [128i, 128i+64) gate rows [64i, 64i+64), the next 64
- *                     the matching up rows); y[t, 64i + j] = silu(gate) * up
+ *  DSB_EPI_SILU_GATE  w holds gate and up rows interleaved (row 2f = gate row f,
+ *                     row 2f+1 = up row f); y[t, f] = silu(gate) * up
  *                     (dense_mlp_step's silu(gate)*up, ops.cpp:103-105)
  *  DSB_EPI_ROWSCALE   y = acc * row_scale[t] (routed weight of a permuted row)
  * Requirements: K, ldw, ldx, x_group_col multiples of 64/8/8/8; 16-byte

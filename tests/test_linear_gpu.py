@@ -83,8 +83,8 @@ def test_linear_silu_gate(gpu_ctx, T):
     I, K = 1408, 2048
     wg = rand(I, K, scale=0.02, seed=7)
     wu = rand(I, K, scale=0.02, seed=8)
-    # interleave per 128-row tile: 64 gate rows then the matching 64 up rows
-    w = torch.stack([wg.view(I // 64, 64, K), wu.view(I // 64, 64, K)], 1).reshape(2 * I, K).contiguous()
+    # rows interleaved: row 2f = gate row f, row 2f+1 = up row f
+    w = torch.stack([wg, wu], 1).reshape(2 * I, K).contiguous()
     x = rand(T, K, seed=9)
     y = torch.empty(T, I, dtype=torch.bfloat16, device="cuda")
     gpu_ctx.linear(w, x, y, M=2 * I, K=K, epilogue=dsb.EPI_SILU_GATE)
