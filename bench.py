@@ -355,25 +355,29 @@ def step_bytes(cfg, B, ctx_len):
 
 
 def time_expert_gemm(ctx, stream, cfg, B, steps):
-    """The dominant kernel in isolation: the routed-expert gate|up GEMM of one
-    MoE layer (E groups of 2I x D bf16 weights, B*k permuted token rows from a
-    random top-k routing), timed with CUDA events on the context stream."""
+    """The dominant kernel in isolation: the expert gate|up GEMM of one MoE
+    layer as the decode step runs it -- E routed groups plus n_shared shared
+    groups of 2I x D bf16 weights, B*(k + n_shared) permuted token rows from a
+    random top-k routing (every token also visits each shared group) -- timed
+    with CUDA events on the context stream."""
     import numpy as np
     import torch
 
     import deepseek_cpp_infer_b200 as dsb
 
     D, E, k, I = cfg["hidden_size"], cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
+    ns = cfg.get("n_shared_experts", 0)
+    G, kk = E + ns, k + ns
     rng = np.random.default_rng(11)
-    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(B)])
-    counts = np.bincount(ids.ravel(), minlength=E)
+    ids = np.stack([np.concatenate([rng.choice(E, k, replace=False), E + np.arange(ns)]) for _ in range(B)])
+    counts = np.bincount(ids.ravel(), minlength=G)
     offs = torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).cuda()
-    w = (torch.randn(E * 2 * I, D, device="cuda") * 0.02).to(torch.bfloat16)
-    x = torch.randn(B * k, D, device="cuda").to(torch.bfloat16)
-    y = torch.empty(B * k, I, dtype=torch.bfloat16, device="cuda")
+    w = (torch.randn(G * 2 * I, D, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(B * kk, D, device="cuda").to(torch.bfloat16)
+    y = torch.empty(B * kk, I, dtype=torch.bfloat16, device="cuda")
 
     def launch():
-        ctx.linear(w, x, y, M=2 * I, K=D, G=E, tok_offsets=offs, max_tokens_per_group=B, epilogue=dsb.EPI_SILU_GATE)
+        ctx.linear(w, x, y, M=2 * I, K=D, G=G, tok_offsets=offs, max_tokens_per_group=B, epilogue=dsb.EPI_SILU_GATE)
 
     for _ in range(5):
         launch()
@@ -387,7 +391,7 @@ def time_expert_gemm(ctx, stream, cfg, B, steps):
     e1.synchronize()
     ms = e0.elapsed_time(e1) / n
     touched = int((counts > 0).sum())
-    nbytes = touched * 2 * I * D * 2 + B * k * D * 2 + B * k * I * 2
+    nbytes = touched * 2 * I * D * 2 + B * kk * D * 2 + B * kk * I * 2
     del w
     return ms, nbytes, touched
 
@@ -499,8 +503,9 @@ def run_model_ours(args):
             "roofline": {"bound": "hbm", "achieved": g_bytes / (g_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak, "traffic": EXPERT_GEMM_NCU_TRAFFIC,
                          "peak_kind": peak_kind,
-                         "kernel": "gemm_bf16_kernel (routed-expert gate|up, SiLU epilogue)",
-                         "note": f"{g_touched} of 64 experts' 2816x2048 bf16 tiles + activations per launch / "
+                         "kernel": "gemm_bf16_kernel (expert gate|up: routed + shared groups, SiLU epilogue)",
+                         "note": f"{g_touched} of {cfg['n_routed_experts'] + cfg['n_shared_experts']} expert groups' "
+                                 f"2816x2048 bf16 tiles + activations per launch / "
                                  f"CUDA-event launch time ({g_ms * 1e3:.1f} us)"},
             "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": B * 4 * (2 + max_blocks),
                     "d2h_bytes_per_step": B * 4 + B * cfg["vocab_size"] * 4},
@@ -648,8 +653,9 @@ def run_model_reference(args):
 
 
 def run_expert_gemm(args):
-    """The dominant kernel of the model step alone (one MoE layer's routed
-    gate|up GEMM at V2-Lite shape, B tokens top-6 of 64 experts); one JSON line."""
+    """The dominant kernel of the model step alone (one MoE layer's expert
+    gate|up GEMM at V2-Lite shape, B tokens top-6 of 64 routed experts plus the
+    2 shared groups); one JSON line."""
     import torch
 
     import deepseek_cpp_infer_b200 as dsb
@@ -661,7 +667,7 @@ def run_expert_gemm(args):
     cfg = model_cfg(args)
     ms, nbytes, touched = time_expert_gemm(ctx, stream, cfg, args.batch, args.steps)
     peak, peak_kind = measured_peaks()
-    print(json.dumps({"workload": "routed-expert gate|up GEMM, V2-Lite shape", "tokens": args.batch,
+    print(json.dumps({"workload": "expert gate|up GEMM (routed + shared groups), V2-Lite shape", "tokens": args.batch,
                       "experts_touched": touched, "us_per_launch": ms * 1e3, "bytes_per_launch": nbytes,
                       "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "peak_gbs": peak, "peak_kind": peak_kind}),
           flush=True)

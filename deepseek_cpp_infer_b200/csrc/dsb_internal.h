@@ -72,8 +72,10 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, co
                         const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
                         float theta, void* cache, void* q_rope);
 int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits);
+// n_extra > 0 appends groups E..E+n_extra-1 with weight 1 to every token's
+// picks (the shared experts); ids/weights rows then hold k + n_extra entries.
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
-              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights);
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra);
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
                 int32_t* src_pair, const float* weights, float* w_perm);
 int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,

@@ -295,15 +295,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (*last_flag != 0) {
           __threadfence();
+          const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
+          constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
           for (int c = 0; c < NCH; ++c) {
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-            for (int s2 = 0; s2 < p.splits; ++s2) {
-              const float* pp = p.ws + ((int64_t)tile_id * p.splits + s2) * (int64_t)NT * kTileM;
+            // four splits' loads in flight at a time, summed in split order
+            int s2 = 0;
+            for (; s2 + 4 <= p.splits; s2 += 4) {
+              float w4[4][CW];
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (c * 32 + i < NT) v[i] += __ldcg(pp + (c * 32 + i) * kTileM + r);
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < CW; ++i)
+                  w4[j][i] = __ldcg(pbase + (int64_t)(s2 + j) * NT * kTileM + (c * 32 + i) * kTileM);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < CW; ++i) v[i] += w4[j][i];
+            }
+            for (; s2 < p.splits; ++s2) {
+#pragma unroll
+              for (int i = 0; i < CW; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c * 32 + i) * kTileM);
             }
             apply(c, v);
           }
@@ -400,7 +414,7 @@ extern "C" int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* a) {
     // small decode GEMMs: split K so every SM streams a share of the weights
     const int tiles = m_tiles * a->G;
     const int want = (ctx->sm_count + tiles - 1) / std::max(1, tiles);
-    splits = std::max(1, std::min({want, KB / 2, 16}));
+    splits = std::max(1, std::min({want, KB / 4, 8}));
   }
   int NT = 16;
   while (NT < bound && NT < 256) NT *= 2;

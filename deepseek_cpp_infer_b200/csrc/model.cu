@@ -43,13 +43,15 @@ struct dsb_model {
     int inter = 0;
     float* w_router = nullptr;       // [E, D] fp32
     float* router_bias = nullptr;    // [E]
-    __nv_bfloat16* e_gu = nullptr;   // [E, 2I, D]
-    __nv_bfloat16* e_down = nullptr; // [E, D, I]
+    // routed experts followed by the shared experts cut into expert-sized
+    // groups: a shared MLP with intermediate n*I equals the sum of n MLPs of
+    // intermediate I, so all of them run in one grouped GEMM
+    __nv_bfloat16* e_gu = nullptr;   // [E + n_shared, 2I, D]
+    __nv_bfloat16* e_down = nullptr; // [E + n_shared, D, I]
     int e_inter = 0;
-    __nv_bfloat16* s_gu = nullptr;   // shared experts [2Is, D]
-    __nv_bfloat16* s_down = nullptr; // [D, Is]
-    int s_inter = 0;
-    uint8_t seen_gate = 0, seen_up = 0;  // dense/shared gate-up halves uploaded
+    int n_shared = 0;                // shared groups after the routed experts
+    uint8_t shared_seen = 0;         // bit 0 gate, 1 up, 2 down uploaded
+    uint8_t seen_gate = 0, seen_up = 0;  // dense gate-up halves uploaded
   };
   dsb_ctx* ctx = nullptr;
   dsb_model_config cfg{};
@@ -268,6 +270,25 @@ int linear(dsb_ctx* ctx, const void* w, int64_t ldw, const void* x, int64_t ldx,
 
 using namespace dsb;
 
+namespace {
+
+// Allocate a layer's stacked expert matrices: E routed + n_shared groups of
+// moe_intermediate_size (from the config, so tensors may arrive in any order).
+int ensure_experts(dsb_model* m, dsb_model::Layer& L) {
+  if (L.e_gu != nullptr) return DSB_OK;
+  const dsb_model_config& c = m->cfg;
+  const int I = c.moe_intermediate_size, D = c.hidden_size;
+  if (I <= 0 || I % 64 != 0) return fail(m->ctx, DSB_EUNSUPPORTED, "moe_intermediate_size %d must be a positive multiple of 64", I);
+  L.e_inter = I;
+  L.n_shared = std::max(0, c.n_shared_experts);
+  const int G = c.n_routed_experts + L.n_shared;
+  int rc = dev_alloc(m, &L.e_gu, (size_t)G * 2 * I * D);
+  if (rc == DSB_OK) rc = dev_alloc(m, &L.e_down, (size_t)G * D * I);
+  return rc;
+}
+
+}  // namespace
+
 // ===================================================================== model
 
 extern "C" int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out) {
@@ -395,40 +416,61 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
     auto f = to_f32(data, dtype, n);
     return upload(m, &L.router_bias, f.data(), (size_t)n);
   }
-  // dense MLP / shared experts: gate and up go to one interleaved matrix
-  struct Ffn {
-    const char* prefix;
-    bf16** gu;
-    bf16** down;
-    int* inter;
-  } ffns[2] = {{"mlp.", &L.w_gu, &L.w_down, &L.inter}, {"mlp.shared_experts.", &L.s_gu, &L.s_down, &L.s_inter}};
-  for (auto& f : ffns) {
-    const std::string pre(f.prefix);
-    const bool shared = pre != "mlp.";
-    for (int half = 0; half < 2; ++half) {
-      if (rest == pre + (half ? "up_proj.weight" : "gate_proj.weight")) {
-        if (ndim != 2 || shape[1] != D) return bad_shape();
-        const int I = (int)shape[0];
-        if (*f.inter != 0 && *f.inter != I) return bad_shape();
-        *f.inter = I;
-        if (*f.gu == nullptr) {
-          int rc = dev_alloc(m, f.gu, (size_t)2 * I * D);
+  {
+    // shared experts [n*I, D] / [D, n*I] -> expert groups E .. E+n-1
+    static const std::string sp = "mlp.shared_experts.";
+    if (rest.compare(0, sp.size(), sp) == 0) {
+      const std::string proj = rest.substr(sp.size());
+      const bool is_down = proj == "down_proj.weight";
+      if (!is_down && proj != "gate_proj.weight" && proj != "up_proj.weight")
+        return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
+      if (c.n_routed_experts <= 0 || c.n_shared_experts <= 0)
+        return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s given but the config has no shared experts", cname);
+      int rc = ensure_experts(m, L);
+      if (rc != DSB_OK) return rc;
+      const int I = L.e_inter, ns = L.n_shared, E = c.n_routed_experts;
+      if (ndim != 2 || (is_down ? (shape[0] != D || shape[1] != (int64_t)ns * I) : (shape[0] != (int64_t)ns * I || shape[1] != D)))
+        return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_set_tensor: %s must be n_shared_experts x moe_intermediate_size", cname);
+      L.has_moe_tensors = true;
+      auto b = to_bf16(data, dtype, n);
+      for (int j = 0; j < ns; ++j) {
+        if (is_down) {
+          // columns [jI, (j+1)I) of [D, nI] -> group E+j's [D, I]
+          DSB_CUDA_TRY(ctx, cudaMemcpy2D(L.e_down + (size_t)(E + j) * D * I, (size_t)I * 2, b.data() + (size_t)j * I,
+                                         (size_t)ns * I * 2, (size_t)I * 2, D, cudaMemcpyHostToDevice));
+        } else {
+          std::vector<uint16_t> part(b.begin() + (size_t)j * I * D, b.begin() + (size_t)(j + 1) * I * D);
+          rc = upload_gate_up_half(m, L.e_gu + (size_t)(E + j) * 2 * I * D, part, I, D, proj == "up_proj.weight" ? 1 : 0);
           if (rc != DSB_OK) return rc;
         }
-        auto b = to_bf16(data, dtype, n);
-        if (!shared) (half ? L.seen_up : L.seen_gate) |= 1;
-        else (half ? L.seen_up : L.seen_gate) |= 2;
-        return upload_gate_up_half(m, *f.gu, b, I, D, half);
       }
+      L.shared_seen |= is_down ? 4 : (proj == "up_proj.weight" ? 2 : 1);
+      return DSB_OK;
     }
-    if (rest == pre + "down_proj.weight") {
-      if (ndim != 2 || shape[0] != D) return bad_shape();
-      const int I = (int)shape[1];
-      if (*f.inter != 0 && *f.inter != I) return bad_shape();
-      *f.inter = I;
+  }
+  // dense MLP: gate and up go to one row-interleaved matrix
+  for (int half = 0; half < 2; ++half) {
+    if (rest == (half ? "mlp.up_proj.weight" : "mlp.gate_proj.weight")) {
+      if (ndim != 2 || shape[1] != D) return bad_shape();
+      const int I = (int)shape[0];
+      if (L.inter != 0 && L.inter != I) return bad_shape();
+      L.inter = I;
+      if (L.w_gu == nullptr) {
+        int rc = dev_alloc(m, &L.w_gu, (size_t)2 * I * D);
+        if (rc != DSB_OK) return rc;
+      }
       auto b = to_bf16(data, dtype, n);
-      return upload(m, f.down, b.data(), (size_t)n);
+      (half ? L.seen_up : L.seen_gate) |= 1;
+      return upload_gate_up_half(m, L.w_gu, b, I, D, half);
     }
+  }
+  if (rest == "mlp.down_proj.weight") {
+    if (ndim != 2 || shape[0] != D) return bad_shape();
+    const int I = (int)shape[1];
+    if (L.inter != 0 && L.inter != I) return bad_shape();
+    L.inter = I;
+    auto b = to_bf16(data, dtype, n);
+    return upload(m, &L.w_down, b.data(), (size_t)n);
   }
   int e = -1;
   std::string proj;
@@ -442,13 +484,10 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
     if (ndim != 2) return bad_shape();
     const int I = is_down ? (int)shape[1] : (int)shape[0];
     if ((is_down ? shape[0] : shape[1]) != D) return bad_shape();
-    if (L.e_inter != 0 && L.e_inter != I) return bad_shape();
-    L.e_inter = I;
-    if (L.e_gu == nullptr) {
-      int rc = dev_alloc(m, &L.e_gu, (size_t)E * 2 * I * D);
-      if (rc == DSB_OK) rc = dev_alloc(m, &L.e_down, (size_t)E * D * I);
-      if (rc != DSB_OK) return rc;
-    }
+    if (I != c.moe_intermediate_size)
+      return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s does not match moe_intermediate_size", cname);
+    int rc0 = ensure_experts(m, L);
+    if (rc0 != DSB_OK) return rc0;
     auto b = to_bf16(data, dtype, n);
     if (is_down) {
       DSB_CUDA_TRY(ctx, cudaMemcpy(L.e_down + (size_t)e * D * I, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
@@ -502,13 +541,10 @@ extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) 
       if (rc == DSB_OK) rc = rand_f32(m, &L.w_router, (int64_t)E * D, ++s, stddev, 0.0f);
       if (c.scoring_func == DSB_SCORE_SIGMOID && rc == DSB_OK) rc = rand_f32(m, &L.router_bias, E, ++s, 0.01f, 0.0f);
       L.e_inter = c.moe_intermediate_size;
-      nb(&L.e_gu, (int64_t)E * 2 * L.e_inter * D);
-      nb(&L.e_down, (int64_t)E * D * L.e_inter);
-      if (c.n_shared_experts > 0) {
-        L.s_inter = c.n_shared_experts * c.moe_intermediate_size;
-        nb(&L.s_gu, (int64_t)2 * L.s_inter * D);
-        nb(&L.s_down, (int64_t)D * L.s_inter);
-      }
+      L.n_shared = std::max(0, c.n_shared_experts);
+      L.shared_seen = 7;
+      nb(&L.e_gu, (int64_t)(E + L.n_shared) * 2 * L.e_inter * D);
+      nb(&L.e_down, (int64_t)(E + L.n_shared) * D * L.e_inter);
     }
   }
   if (rc != DSB_OK) return rc;
@@ -534,7 +570,7 @@ extern "C" int dsb_model_finalize(dsb_model* m) {
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d MoE weights incomplete", li);
       if (c.scoring_func == DSB_SCORE_SIGMOID && !L.router_bias)
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d needs e_score_correction_bias", li);
-      if (L.s_gu != nullptr && L.s_down == nullptr)
+      if (L.n_shared > 0 && L.shared_seen != 7)
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d shared experts incomplete", li);
     } else if (!L.w_gu || !L.w_down) {
       return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d dense MLP incomplete", li);
@@ -695,16 +731,16 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   }
 
   // ---- device buffers for this batch size (in the context workspace after the plan)
-  int max_I = 0, max_eI = 0, max_sI = 0;
+  int max_I = 0, max_eI = 0, max_ns = 0;
   bool any_moe = false, any_qlora = false;
   for (auto& L : m->layers) {
     max_I = std::max(max_I, L.inter);
     max_eI = std::max(max_eI, L.e_inter);
-    max_sI = std::max(max_sI, L.s_inter);
+    max_ns = std::max(max_ns, L.n_shared);
     any_moe |= L.moe;
     any_qlora |= L.w_qa != nullptr;
   }
-  const int BK = any_moe ? B * k : 1;
+  const int BK = any_moe ? B * (k + max_ns) : 1;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -714,14 +750,15 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   const size_t o_h = take((size_t)B * D * 4), o_xn32 = take((size_t)B * D * 4), o_kva = take((size_t)B * (R + P) * 4);
   const size_t o_qa = take(any_qlora ? (size_t)B * c.q_lora_rank * 4 : 4);
   const size_t o_qan = take(any_qlora ? (size_t)B * c.q_lora_rank * 2 : 4);
-  const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)B * k * 4 + 4);
-  const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)BK * D * 4), o_sout = take((size_t)B * D * 4);
+  const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)BK * 4 + 4);
+  const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)BK * D * 4);
   const size_t o_logits = take((size_t)B * V * 4), o_xn = take((size_t)B * D * 2), o_q = take((size_t)B * QH * 2);
   const size_t o_qrope = take((size_t)B * H * P * 2), o_qlat = take((size_t)B * H * R * 2);
   const size_t o_olat = take((size_t)B * H * R * 2), o_attn = take((size_t)B * H * v * 2);
-  const size_t o_mid = take((size_t)B * std::max({max_I, max_sI, 64}) * 2);
+  const size_t o_mid = take((size_t)B * std::max(max_I, 64) * 2);
   const size_t o_xperm = take((size_t)BK * D * 2), o_midp = take((size_t)BK * std::max(max_eI, 64) * 2);
-  const size_t o_ids = take((size_t)B * k * 4 + 4), o_cnt = take((size_t)(E + 1) * 4), o_off = take((size_t)(E + 2) * 4);
+  const size_t o_ids = take((size_t)BK * 4 + 4), o_cnt = take((size_t)(E + max_ns + 1) * 4);
+  const size_t o_off = take((size_t)(E + max_ns + 2) * 4);
   const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)B * 4);
   const size_t o_tab = take(host_i.size() * 4);
   // the step buffers live in their own context-owned region (ctx->step); the
@@ -733,7 +770,7 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   auto Bf = [&](size_t o) { return reinterpret_cast<bf16*>(base + o); };
   auto I32 = [&](size_t o) { return reinterpret_cast<int32_t*>(base + o); };
   float *h = F(o_h), *xn32 = F(o_xn32), *kva = F(o_kva), *qa = F(o_qa), *lr = F(o_lr), *wts = F(o_wts);
-  float *wperm = F(o_wperm), *yperm = F(o_yperm), *sout = F(o_sout), *logits = F(o_logits);
+  float *wperm = F(o_wperm), *yperm = F(o_yperm), *logits = F(o_logits);
   bf16 *xn = Bf(o_xn), *q = Bf(o_q), *qrope = Bf(o_qrope), *qlat = Bf(o_qlat), *olat = Bf(o_olat), *attn = Bf(o_attn);
   bf16 *mid = Bf(o_mid), *xperm = Bf(o_xperm), *midp = Bf(o_midp), *qan = Bf(o_qan);
   int32_t *ids = I32(o_ids), *cnt = I32(o_cnt), *offs = I32(o_off), *dest = I32(o_dest), *src = I32(o_src);
@@ -784,22 +821,18 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     } else {
       DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
       DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
+      // each token routes to its top-k experts plus every shared group (weight 1)
+      const int kk = k + L.n_shared, G = E + L.n_shared;
       DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group, c.norm_topk_prob,
-                         c.routed_scaling_factor, ids, wts));
-      DSB_STEP(moe_permute(ctx, ids, B * k, E, cnt, offs, dest, src, wts, wperm));
-      DSB_STEP(gather_rows(ctx, xn, D, src, B * k, k, D, xperm));
+                         c.routed_scaling_factor, ids, wts, L.n_shared));
+      DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
+      DSB_STEP(gather_rows(ctx, xn, D, src, B * kk, kk, D, xperm));
       const int eI = L.e_inter;
       // every expert writes the same columns of its own (permuted) token rows
-      DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * k, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, E, 0, 0, offs, B));
-      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * k, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, E, 0, 0, offs, B,
+      DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * kk, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, G, 0, 0, offs, B));
+      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * kk, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, G, 0, 0, offs, B,
                       wperm));
-      const float* shared = nullptr;
-      if (L.s_gu != nullptr) {
-        DSB_STEP(linear(ctx, L.s_gu, D, xn, D, B, 2 * L.s_inter, D, mid, L.s_inter, 0, DSB_EPI_SILU_GATE));
-        DSB_STEP(linear(ctx, L.s_down, L.s_inter, mid, L.s_inter, B, D, L.s_inter, sout, D, 1, DSB_EPI_STORE));
-        shared = sout;
-      }
-      DSB_STEP(moe_combine(ctx, yperm, dest, B, k, D, shared, h));
+      DSB_STEP(moe_combine(ctx, yperm, dest, B, kk, D, nullptr, h));
     }
   }
   // final norm, lm_head, greedy (model.cpp:160-179)

@@ -155,7 +155,7 @@ __device__ __forceinline__ void warp_argmax(float& v, int& idx) {
 // chosen experts, normalised when norm_topk, times routed_scale.
 __global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                              int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
-                             int32_t* __restrict__ ids, float* __restrict__ weights) {
+                             int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (t >= T) return;
   const float* lg = logits + (int64_t)t * E;
@@ -268,11 +268,16 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
     wsum = __fadd_rn(wsum, wv);
   }
   if (lane == 0) {
+    const int kk = k + n_extra;  // row stride: the k routed picks, then n_extra always-on groups
     for (int r = 0; r < k; ++r) {
       float wv = wsel[r];
       if (norm_topk && wsum > 0.0f) wv = __fdiv_rn(wv, wsum);
-      ids[(int64_t)t * k + r] = isel[r];
-      weights[(int64_t)t * k + r] = __fmul_rn(wv, routed_scale);
+      ids[(int64_t)t * kk + r] = isel[r];
+      weights[(int64_t)t * kk + r] = __fmul_rn(wv, routed_scale);
+    }
+    for (int j = 0; j < n_extra; ++j) {
+      ids[(int64_t)t * kk + k + j] = E + j;
+      weights[(int64_t)t * kk + k + j] = 1.0f;
     }
   }
 }
@@ -425,9 +430,9 @@ int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, in
 }
 
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
-              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights) {
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra) {
   route_kernel<<<(T + 7) / 8, 256, 0, ctx->stream>>>(logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk,
-                                                     routed_scale, ids, weights);
+                                                     routed_scale, ids, weights, n_extra);
   return launched(ctx);
 }
 
@@ -507,7 +512,7 @@ extern "C" int dsb_moe_route(dsb_ctx* ctx, const float* logits, const float* bia
     return dsb::fail(ctx, DSB_EINVAL, "dsb_moe_route: unknown scoring %d", scoring);
   }
   return dsb::moe_route(ctx, logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids,
-                        weights);
+                        weights, 0);
 }
 
 extern "C" int dsb_moe_permute(dsb_ctx* ctx, const int32_t* ids, int T, int k, int E, int32_t* counts,

@@ -78,6 +78,8 @@ def oracle() -> ctypes.CDLL:
         _proto(l, "orc_fp8_linear", None, [u8p, f32p, u8p, f32p, i64, i64, i64, f32p])
         _proto(l, "orc_dense_mlp_f32", None, [f32p, f32p, f32p, f32p, i64, i64, f32p])
         _proto(l, "orc_moe_softmax_f32", ctypes.c_int, [f32p] * 7 + [ctypes.c_int] * 6 + [ctypes.c_float, f32p, f32p])
+        _proto(l, "orc_moe_mix_f32", None,
+               [f32p] * 6 + [ctypes.c_int] * 4 + [i32p, f32p, ctypes.c_float, f32p, f32p])
         _oracle = l
     return _oracle
 

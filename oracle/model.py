@@ -1,0 +1,124 @@
+"""Whole-model teacher-forced forward composed from the oracle's layer
+functions (TEST INFRASTRUCTURE ONLY; see oracle/__init__.py for who may
+import it).
+
+It follows DeepSeekModel::decode_next (src/models/deepseek/model.cpp:117-184)
+position by position: embedding row -> per layer RMSNorm -> MLA
+(orc_mla_layer_seq_f32, the absorbed restatement of mla_decode_step) ->
+residual -> RMSNorm -> dense MLP (dense_mlp_step, ops.cpp:96-108) or
+softmax-greedy MoE (moe_step, ops.cpp:110-146) -> residual; final RMSNorm and
+lm_head.  Every position of a layer is computed before the next layer, which
+is the same arithmetic because position t only attends to positions <= t.
+
+Besides the logits it reports, per position, the router margin of every MoE
+layer: the k-th largest minus the (k+1)-th largest fp32 gate logit.  Where it
+is small, a relative perturbation of the layer input far below bf16
+resolution can swap the last routed expert; `swaps` forces such a swap (the
+(k+1)-th expert takes the k-th slot with its own probability) at chosen
+(layer, position) pairs, giving the output the reference would produce had
+its router broken the near-tie the other way.
+
+Covers the configurations with q_lora_rank 0 and softmax scoring (DeepSeek-V2
+style); dimensions come from the same config dict as workloads.TINY.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import f32p, i32p, oracle, p
+
+
+def _f32(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def _rmsnorm_rows(x, w, eps):
+    out = np.zeros_like(x)
+    for i in range(x.shape[0]):
+        o = np.zeros(x.shape[1], np.float32)
+        oracle().orc_rmsnorm_f32(p(_f32(x[i]), f32p), p(w, f32p), x.shape[1], eps, p(o, f32p))
+        out[i] = o
+    return out
+
+
+def forward(cfg: dict, tensors: dict, seq, swaps=()):
+    """Logits [T, V] for every position of `seq` and router margins
+    {layer: [T] float64}.  `swaps`: iterable of (layer, position)."""
+    if cfg.get("q_lora_rank", 0) or cfg.get("scoring_func", 0) != 0:
+        raise NotImplementedError("oracle.model covers q_lora_rank 0 with softmax scoring")
+    c = cfg
+    W = {n: _f32(a) for n, a in tensors.items()}
+    seq = np.asarray(seq, np.int64)
+    T = len(seq)
+    D, H, R = c["hidden_size"], c["num_attention_heads"], c["kv_lora_rank"]
+    nope, rope, v = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+    E, k, I = c["n_routed_experts"], c["num_experts_per_tok"], c["moe_intermediate_size"]
+    eps = c["rms_norm_eps"]
+    swaps = set(swaps)
+    orc = oracle()
+    h = _f32(W["model.embed_tokens.weight"][seq])
+    margins = {}
+    for li in range(c["num_hidden_layers"]):
+        pre = f"model.layers.{li}."
+        xn = _rmsnorm_rows(h, W[pre + "input_layernorm.weight"], eps)
+        out = np.zeros((T, D), np.float32)
+        rc = orc.orc_mla_layer_seq_f32(
+            D, H, nope, rope, v, R, eps, c["rope_theta"],
+            *(p(W[pre + "self_attn." + n + ".weight"], f32p)
+              for n in ("q_proj", "kv_a_proj_with_mqa", "kv_a_layernorm", "kv_b_proj", "o_proj")),
+            p(xn, f32p), T, p(out, f32p))
+        assert rc == 0
+        h = _f32(h + out)
+        xn = _rmsnorm_rows(h, W[pre + "post_attention_layernorm.weight"], eps)
+        out = np.zeros((T, D), np.float32)
+        if pre + "mlp.gate.weight" not in W:
+            wg, wu, wd = (W[pre + "mlp." + n + "_proj.weight"] for n in ("gate", "up", "down"))
+            for t in range(T):
+                o = np.zeros(D, np.float32)
+                orc.orc_dense_mlp_f32(p(wg, f32p), p(wu, f32p), p(wd, f32p), p(_f32(xn[t]), f32p), D, wg.shape[0],
+                                      p(o, f32p))
+                out[t] = o
+        else:
+            eg, eu, ed = (_f32(np.stack([W[pre + f"mlp.experts.{e}.{n}_proj.weight"] for e in range(E)]))
+                          for n in ("gate", "up", "down"))
+            shared = pre + "mlp.shared_experts.gate_proj.weight" in W
+            sg, su, sd = ((W[pre + f"mlp.shared_experts.{n}_proj.weight"] for n in ("gate", "up", "down"))
+                          if shared else (None, None, None))
+            Is = sg.shape[0] if shared else 0
+            wgate = W[pre + "mlp.gate.weight"]
+            margin = np.zeros(T)
+            for t in range(T):
+                x = _f32(xn[t])
+                logits = np.zeros(E, np.float32)
+                orc.orc_linear_f32(p(wgate, f32p), p(x, f32p), D, p(logits, f32p), E)
+                srt = np.sort(logits.astype(np.float64))[::-1]
+                margin[t] = srt[k - 1] - srt[k] if k < E else np.inf
+                ids = np.zeros(k + 1 if k < E else k, np.int32)
+                w = np.zeros(len(ids), np.float32)
+                # top-(k+1) in the reference's order: the (k+1)-th is the swap candidate
+                assert orc.orc_route_softmax_greedy(p(_f32(logits), f32p), 1, E, len(ids), 0, 1.0, p(ids, i32p),
+                                                    p(w, f32p)) == 0
+                if (li, t) in swaps:
+                    ids[k - 1], w[k - 1] = ids[k], w[k]
+                ids, w = np.ascontiguousarray(ids[:k]), _f32(w[:k])
+                if c["norm_topk_prob"]:
+                    s = np.float32(0)
+                    for j in range(k):
+                        s = np.float32(s + w[j])
+                    if s > 0:
+                        w = _f32(w / s)
+                o = np.zeros(D, np.float32)
+                orc.orc_moe_mix_f32(p(eg, f32p), p(eu, f32p), p(ed, f32p),
+                                    *((p(a, f32p) for a in (sg, su, sd)) if shared else (None, None, None)),
+                                    Is, D, I, k, p(ids, i32p), p(w, f32p), c["routed_scaling_factor"], p(x, f32p),
+                                    p(o, f32p))
+                out[t] = o
+            margins[li] = margin
+        h = _f32(h + out)
+    hn = _rmsnorm_rows(h, W["model.norm.weight"], eps)
+    logits = np.zeros((T, W["lm_head.weight"].shape[0]), np.float32)
+    for t in range(T):
+        orc.orc_linear_f32(p(W["lm_head.weight"], f32p), p(_f32(hn[t]), f32p), D, p(logits[t], f32p),
+                           logits.shape[1])
+    return logits, margins

@@ -362,6 +362,31 @@ ORC_API int orc_route_softmax_greedy(const float* logits, int T, int E, int k, i
 }
 
 /*
+ * The expert half of moe_step (src/models/deepseek/ops.cpp:128-145) for one
+ * token whose experts are already chosen: for each pick i in order
+ * out += (w[i] * routed_scale) * mlp_{ids[i]}(x), then out += shared(x).
+ * Expert weights: gate/up [E, I, D], down [E, D, I]; shared gate/up [Is, D],
+ * down [D, Is] (s_gate NULL = no shared experts).
+ */
+ORC_API void orc_moe_mix_f32(const float* e_gate, const float* e_up, const float* e_down, const float* s_gate,
+                             const float* s_up, const float* s_down, int shared_inter, int D, int I, int k,
+                             const int32_t* ids, const float* w, float routed_scale, const float* x, float* out) {
+  float* tmp = (float*)malloc(sizeof(float) * (size_t)D);
+  for (int j = 0; j < D; ++j) out[j] = 0.0f;
+  for (int i = 0; i < k; ++i) {
+    const int64_t e = ids[i];
+    orc_dense_mlp_f32(e_gate + e * I * D, e_up + e * I * D, e_down + e * D * I, x, D, I, tmp);
+    const float scale = w[i] * routed_scale;
+    for (int j = 0; j < D; ++j) out[j] += scale * tmp[j];
+  }
+  if (s_gate != NULL) {
+    orc_dense_mlp_f32(s_gate, s_up, s_down, x, D, shared_inter, tmp);
+    for (int j = 0; j < D; ++j) out[j] += tmp[j];
+  }
+  free(tmp);
+}
+
+/*
  * One token through a softmax-greedy MoE block, step for step as moe_step
  * (src/models/deepseek/ops.cpp:110-146): gate logits -> route -> for each
  * chosen expert out += (p * routed_scale) * mlp_e(x) in selection order ->
@@ -374,24 +399,12 @@ ORC_API int orc_moe_softmax_f32(const float* w_gate, const float* e_gate, const 
   float* logits = (float*)malloc(sizeof(float) * (size_t)E);
   int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * (size_t)k);
   float* w = (float*)malloc(sizeof(float) * (size_t)k);
-  float* tmp = (float*)malloc(sizeof(float) * (size_t)D);
   orc_linear_f32(w_gate, x, D, logits, E);
   const int rc = orc_route_softmax_greedy(logits, 1, E, k, norm_topk, 1.0f, ids, w);
-  for (int j = 0; j < D; ++j) out[j] = 0.0f;
-  for (int i = 0; i < k; ++i) {
-    const int64_t e = ids[i];
-    orc_dense_mlp_f32(e_gate + e * I * D, e_up + e * I * D, e_down + e * D * I, x, D, I, tmp);
-    const float scale = w[i] * routed_scale;
-    for (int j = 0; j < D; ++j) out[j] += scale * tmp[j];
-  }
-  if (s_gate != NULL) {
-    orc_dense_mlp_f32(s_gate, s_up, s_down, x, D, shared_inter, tmp);
-    for (int j = 0; j < D; ++j) out[j] += tmp[j];
-  }
+  orc_moe_mix_f32(e_gate, e_up, e_down, s_gate, s_up, s_down, shared_inter, D, I, k, ids, w, routed_scale, x, out);
   free(logits);
   free(ids);
   free(w);
-  free(tmp);
   return rc;
 }
 

@@ -11,6 +11,15 @@ tests/golden/make_golden.py): the reference's 64 greedy tokens after a
 Bars: greedy ids identical for the first 32 generated tokens (the decode
 target); logits max-rel <= 2e-2 (max|gpu - ref| / max|ref|) at every stored
 step, teacher-forced on the reference's own sequence.
+
+Router near-ties.  The GPU path feeds bf16 activations to the tensor cores,
+so a layer's input differs from the reference's fp32 one by ~2^-9 relative.
+Where the reference's k-th and (k+1)-th gate logits of some MoE layer are
+closer than NEAR_TIE at a stored position, that perturbation may swap the
+last routed expert, a discrete change that moves the logits by a few 1e-2.
+At such a position the logits must instead be within 2e-2 of the reference
+forward with that swap forced (oracle.model.forward with `swaps`, which is
+pinned to the reference's logits by tests/test_oracle.py).
 """
 
 import os
@@ -23,6 +32,39 @@ from deepseek_cpp_infer_b200.workloads import TINY, model_tensors
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "tiny_model.npz")
+TOL = 2e-2
+NEAR_TIE = 0.02  # gate-logit gap (logit units) below which the last routed expert may swap
+
+
+def max_rel(a, ref):
+    return float(np.abs(a - ref).max() / np.abs(ref).max())
+
+
+@pytest.fixture(scope="module")
+def ref_margins():
+    """Router margins of the reference forward on the golden sequence."""
+    import oracle.model as OM
+
+    g = np.load(GOLD)
+    seq = np.concatenate([g["prompt"], g["generated"]])
+    _, margins = OM.forward(TINY, model_tensors(TINY, seed=0), seq[: int(g["steps"].max()) + 1])
+    return margins
+
+
+def check_logits(step, got, ref, margins, seq):
+    """max-rel <= TOL against the reference, or, at a router near-tie,
+    against the reference with the near-tied expert swapped."""
+    err = max_rel(got, ref)
+    if err <= TOL:
+        return err, None
+    import oracle.model as OM
+
+    tied = [li for li, m in margins.items() if m[step] < NEAR_TIE]
+    assert tied, f"step {step}: logits max-rel {err} with no router near-tie"
+    t = model_tensors(TINY, seed=0)
+    best = min((max_rel(got, OM.forward(TINY, t, seq[: step + 1], swaps=[(li, step)])[0][step]), li) for li in tied)
+    assert best[0] <= TOL, (step, err, best)
+    return best[0], best[1]
 
 
 @pytest.fixture(scope="module")
@@ -54,7 +96,7 @@ def run_sequence(ctx, m, kv, tokens, n_new):
     return np.array(greedy, np.int32), np.stack(logits)
 
 
-def test_tiny_model_greedy_matches_reference(gpu_ctx, tiny):
+def test_tiny_model_greedy_matches_reference(gpu_ctx, tiny, ref_margins):
     m, g = tiny
     kv = dsb.KVCache(gpu_ctx, m, n_blocks=64, max_seqs=4, max_blocks_per_seq=8)
     prompt, gen_ref = g["prompt"], g["generated"]
@@ -65,16 +107,16 @@ def test_tiny_model_greedy_matches_reference(gpu_ctx, tiny):
     # summation order differs from the reference's); report where it happens
     same = int(np.argmin(gen == gen_ref)) if not np.array_equal(gen, gen_ref) else len(gen)
     print(f"greedy ids identical to the reference for the first {same} of {len(gen)} generated tokens")
+    seq = np.concatenate([prompt, gen_ref])
     for i, step in enumerate(g["steps"]):
-        if step >= len(logits):  # the last stored step is past the generated sequence
+        # logits are comparable while the generated prefix equals the reference's
+        if step >= len(logits) or step > len(prompt) - 1 + same:
             continue
-        ref = g["logits"][i]
-        err = float(np.abs(logits[step] - ref).max() / np.abs(ref).max())
-        assert err <= 2e-2, (int(step), err)
+        check_logits(int(step), logits[step], g["logits"][i], ref_margins, seq)
     kv.close()
 
 
-def test_tiny_model_teacher_forced_logits_and_batch_invariance(gpu_ctx, tiny):
+def test_tiny_model_teacher_forced_logits_and_batch_invariance(gpu_ctx, tiny, ref_margins):
     """Three sequences decoded together (different prompts, different lengths)
     give the same greedy ids and logits as each decoded alone."""
     m, g = tiny
@@ -98,10 +140,9 @@ def test_tiny_model_teacher_forced_logits_and_batch_invariance(gpu_ctx, tiny):
     ref_seq = np.concatenate([g["prompt"], g["generated"]])
     _, lg = run_sequence(gpu_ctx, m, kv, list(ref_seq), 1)
     for i, step in enumerate(g["steps"]):
-        ref = g["logits"][i]
-        err = float(np.abs(lg[step] - ref).max() / np.abs(ref).max())
-        print("teacher-forced logits max-rel at step", int(step), err)
-        assert err <= 2e-2
+        err, swapped = check_logits(int(step), lg[step], g["logits"][i], ref_margins, ref_seq)
+        note = "" if swapped is None else f" (against the reference with layer {swapped}'s near-tied expert swapped)"
+        print("teacher-forced logits max-rel at step", int(step), err, note)
     kv.close()
 
 

@@ -276,3 +276,23 @@ def test_fp8_linear_equals_reference_linear_on_dequantised():
     # and the quantised product is close to the unquantised one
     full = x @ w.T
     assert np.abs(y - full).max() / np.abs(full).max() < 0.08
+
+
+# ------------------------------------------------------------ whole model
+
+
+def test_composed_model_oracle_matches_reference_golden():
+    """oracle.model.forward (the layer restatements composed as decode_next)
+    reproduces the reference's own teacher-forced logits on the tiny model
+    up to fp32 re-association, and its greedy ids on the whole sequence."""
+    import oracle.model as OM
+    from deepseek_cpp_infer_b200.workloads import TINY, model_tensors
+
+    g = gold("tiny_model.npz")
+    seq = np.concatenate([g["prompt"], g["generated"]])
+    logits, margins = OM.forward(TINY, model_tensors(TINY, seed=0), seq)
+    for i, step in enumerate(g["steps"]):
+        ref = g["logits"][i]
+        assert np.abs(logits[step] - ref).max() <= 1e-5 * np.abs(ref).max()
+    assert np.array_equal(np.argmax(logits, 1)[: len(g["greedy"])], g["greedy"])
+    assert sorted(margins) == [1, 2, 3] and all(np.all(m >= 0) for m in margins.values())
