@@ -62,6 +62,18 @@ class LinearArgs(ctypes.Structure):
     ]
 
 
+class LinearFp8Args(ctypes.Structure):
+    _fields_ = [
+        ("w", ctypes.c_void_p), ("ldw", ctypes.c_int64), ("w_scale", ctypes.c_void_p), ("scale_rows", ctypes.c_int),
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("x_scale", ctypes.c_void_p), ("ld_xs", ctypes.c_int64),
+        ("x_group_col", ctypes.c_int64), ("tok_offsets", ctypes.c_void_p),
+        ("T", ctypes.c_int), ("M", ctypes.c_int), ("K", ctypes.c_int), ("G", ctypes.c_int),
+        ("max_tokens_per_group", ctypes.c_int), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("y_group_col", ctypes.c_int64), ("y_f32", ctypes.c_int), ("epilogue", ctypes.c_int),
+        ("row_scale", ctypes.c_void_p),
+    ]
+
+
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 
 
@@ -99,6 +111,9 @@ _PROTOS = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
       ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p]),
     ("dsb_linear", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearArgs)]),
+    ("dsb_quant_act_1x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _vp, _ci, _ci, _ci, _vp, _i64, _vp, _i64]),
+    ("dsb_quant_weight_128x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _i64, _vp, _vp]),
+    ("dsb_linear_fp8", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearFp8Args)]),
     ("dsb_rmsnorm", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _cf, _vp, _i64, _vp, _i64]),
     ("dsb_kv_norm_rope_append", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _cf, _vp, _vp]),
@@ -240,6 +255,39 @@ class Context:
             epilogue=epilogue, row_scale=_ptr(row_scale),
         )
         self._check(self._l.dsb_linear(self.h, ctypes.byref(a)))
+
+    def quant_act(self, x, q, scales, src_rows=None, k=1, T=None):
+        """dsb_quant_act_1x128: x bf16/fp32 [.., K] -> q uint8 [T, K], scales fp32 [T, K/128]."""
+        import torch
+
+        T = (src_rows.shape[0] if src_rows is not None else x.shape[0]) if T is None else T
+        dt = DTYPE_BF16 if x.dtype == torch.bfloat16 else DTYPE_F32
+        self._check(self._l.dsb_quant_act_1x128(self.h, _ptr(x), dt, x.stride(0), _ptr(src_rows), k, T, q.shape[1],
+                                                _ptr(q), q.stride(0), _ptr(scales), scales.stride(0)))
+
+    def quant_weight(self, w, q, scales):
+        """dsb_quant_weight_128x128: w bf16/fp32 [M, K] -> q uint8 [M, K], scales [ceil(M/128), ceil(K/128)]."""
+        import torch
+
+        dt = DTYPE_BF16 if w.dtype == torch.bfloat16 else DTYPE_F32
+        self._check(self._l.dsb_quant_weight_128x128(self.h, _ptr(w), dt, w.shape[0], w.shape[1], _ptr(q),
+                                                     _ptr(scales)))
+
+    def linear_fp8(self, w, w_scale, x, x_scale, y, *, M, K, G=1, T=None, scale_rows=1, ldw=None, ldx=None,
+                   x_group_col=0, tok_offsets=None, max_tokens_per_group=0, ldy=None, y_group_col=0,
+                   epilogue=EPI_STORE, row_scale=None):
+        """dsb_linear_fp8 on torch device tensors (w, x uint8 e4m3; scales fp32; y bf16 or fp32)."""
+        import torch
+
+        T = x.shape[0] if T is None else T
+        a = LinearFp8Args(
+            w=_ptr(w), ldw=ldw or w.shape[-1], w_scale=_ptr(w_scale), scale_rows=scale_rows, x=_ptr(x),
+            ldx=ldx or x.shape[-1], x_scale=_ptr(x_scale), ld_xs=x_scale.stride(0), x_group_col=x_group_col,
+            tok_offsets=_ptr(tok_offsets), T=T, M=M, K=K, G=G, max_tokens_per_group=max_tokens_per_group,
+            y=_ptr(y), ldy=ldy or y.shape[-1], y_group_col=y_group_col, y_f32=int(y.dtype == torch.float32),
+            epilogue=epilogue, row_scale=_ptr(row_scale),
+        )
+        self._check(self._l.dsb_linear_fp8(self.h, ctypes.byref(a)))
 
     # ---- row and routing ops (device tensors; shapes from the tensors)
     def rmsnorm(self, x, w, eps, y_bf16=None, y_f32=None):

@@ -72,6 +72,10 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, co
                         const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
                         float theta, void* cache, void* q_rope);
 int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits);
+// e4m3 per-token 1x128 quantisation (quant_fp8.cu); arguments as
+// dsb_quant_act_1x128, unchecked.
+int quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const int32_t* src_rows, int k, int T,
+                    int K, void* q, int64_t ldq, float* scales, int64_t ld_scales);
 // n_extra > 0 appends groups E..E+n_extra-1 with weight 1 to every token's
 // picks (the shared experts); ids/weights rows then hold k + n_extra entries.
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,

@@ -270,6 +270,23 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 
 // Instruction descriptor, kind::f16 with bf16 A/B and f32 D.
 // a_mn / b_mn select MN-major (1) instead of K-major (0) operands.
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f8f6f4 (both operands e4m3
+// here), fp32 accumulation; one instruction covers K = 32 bytes.
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor: A and B e4m3 (format code 0), K-major, D f32.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
   return (1u << 4)                              // D format f32
          | (1u << 7)                            // A format bf16

@@ -1,0 +1,444 @@
+// Grouped FP8 (e4m3) linear layer with DeepSeek-V3 block scaling, on tcgen05:
+//     y[t, g*y_group_col + n] = sum_kb  sw(g, n, kb) * sx[t, kb]
+//                               * sum_{k in block kb} xq[t, g*x_group_col + k] * wq[g*M + n, k]
+// wq e4m3 with one fp32 scale per 128x128 block, xq e4m3 with one fp32 scale
+// per token and 128 columns (dsb_quant_act_1x128).
+//
+// The scales change every 128 columns of K, so the tensor cores cannot carry
+// one accumulator across K: each 128-deep K block is its own 4-instruction
+// kind::f8f6f4 MMA chain into one of two TMEM partial buffers, and the
+// epilogue warps promote it - acc += partial * sw * sx[t] in fp32 registers -
+// while the MMAs of the next block fill the other buffer.
+//
+// Same tiling as the bf16 kernel: weights are the 128-row A operand ("swap
+// AB"), tokens the N side (16..128 columns), one persistent CTA per SM walks
+// the work tiles, the TMA ring streams across tile boundaries, and split-K
+// (dense groups with <= 128 tokens) writes fp32 partials reduced in split
+// order by the last split.  One stage (128 weight rows x 128 bytes) is exactly
+// one scale block and one 128-byte swizzle row.
+//
+// The reference has no FP8 path (its safetensors dtype parser stops at
+// F32/F16/BF16, src/hf/safetensors.cpp:12-20); this replaces the expert and
+// linear GEMVs of moe_to_slot / linear_to_slot (src/models/deepseek/
+// cuda_backend.cpp:782-883) for block-scaled FP8 checkpoints.
+//
+// Roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-5
+// promotion + epilogue (warp w owns TMEM lanes 32*(w%4)..+31).
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "dsb_internal.h"
+#include "dsb_ptx.cuh"
+
+namespace dsb {
+namespace {
+
+constexpr int kBK = 128;      // K bytes (e4m3 elements) per stage = one scale block
+constexpr int kTileM = 128;   // weight rows per tile (MMA M)
+constexpr int kThreads = 192;
+
+struct Fp8Params {
+  int T, M, K, G;
+  int64_t x_group_col;         // elements (= bytes)
+  const int32_t* tok_offsets;  // [G+1] or null
+  const float* w_scale;        // [(G*m_tiles)*scale_rows, K/128]
+  int scale_rows;              // 1, or 2 for row-interleaved gate|up
+  const float* x_scale;        // [T, ld_xs]
+  int64_t ld_xs;
+  void* y;
+  int64_t ldy, y_group_col;
+  int y_f32;
+  int epi;
+  const float* row_scale;
+  int splits;
+  int m_tiles;
+  int n_tiles;        // G * m_tiles * splits
+  float* ws;          // split partials
+  int* counters;      // per-tile tickets (zeroed; reset by the last split)
+};
+
+template <int NT>
+struct Fp8Shape {
+  static constexpr int A_BYTES = kTileM * kBK;  // 16 KB
+  static constexpr int B_BYTES = NT * kBK;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int NS = (196 * 1024) / STAGE;
+  static constexpr int OFF_BAR = NS * STAGE;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
+  static constexpr int SMEM = OFF_MISC + 32 + 1024;
+  static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
+  static constexpr uint32_t TCOLS = 2 * TC;
+  static_assert(STAGE % 1024 == 0, "stage alignment");
+  static_assert(SMEM <= 232448, "shared memory");
+};
+
+// Work units of this CTA: tiles blockIdx.x + i*gridDim.x, and inside each
+// tile its token tiles.  Every role walks the same sequence.
+struct UnitIter {
+  const Fp8Params* p;
+  int NT;
+  int tile = -1, nt = 0, n_tt = 0;
+  int g = 0, mt = 0, split = 0, tok0 = 0, tok1 = 0;
+
+  __device__ bool next() {
+    if (tile >= 0 && ++nt < n_tt) return true;
+    for (tile = (tile < 0 ? (int)blockIdx.x : tile + (int)gridDim.x); tile < p->n_tiles; tile += gridDim.x) {
+      split = tile % p->splits;
+      const int gm = tile / p->splits;
+      mt = gm % p->m_tiles;
+      g = gm / p->m_tiles;
+      if (p->tok_offsets != nullptr) {
+        tok0 = p->tok_offsets[g];
+        tok1 = p->tok_offsets[g + 1];
+      } else {
+        tok0 = 0;
+        tok1 = p->T;
+      }
+      n_tt = (tok1 - tok0 + NT - 1) / NT;
+      nt = 0;
+      if (n_tt > 0) return true;
+    }
+    return false;
+  }
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                    Fp8Params p, int* status) {
+  using S = Fp8Shape<NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* empty = full + S::NS;
+  uint64_t* part_full = empty + S::NS;  // [2] partial buffer written by one K block's MMAs
+  uint64_t* part_empty = part_full + 2; // [2] partial buffer promoted by the epilogue
+  uint64_t* drain = part_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
+  volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 12);
+
+  const int KB = p.K / kBK;
+  const uint32_t warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&part_full[b], 1);
+      mbar_init(&part_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    *no_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, S::TCOLS);
+    tmem_relinquish();
+  }
+  if (warp == 1 && lane == 0) {
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      UnitIter it{&p, NT};
+      int q = 0;
+      bool ok = true;
+      while (ok && it.next()) {
+        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
+          const int s = q % S::NS;
+          if (q >= S::NS && !mbar_wait(&empty[s], ((q / S::NS) - 1) & 1, abort)) {
+            raise_abort(abort, status, kStatusTimeout);
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * S::STAGE;
+          mbar_arrive_expect_tx(&full[s], S::STAGE);
+          tma_load_2d(st, &map_w, &full[s], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
+          tma_load_2d(st + S::A_BYTES, &map_x, &full[s], (int)(it.g * p.x_group_col + kb * kBK), it.tok0 + it.nt * NT);
+        }
+      }
+      if (*abort) {
+        const int first = q > S::NS ? q - S::NS : 0;
+        for (int i = first; i < q; ++i) mbar_wait(&full[i % S::NS], (i / S::NS) & 1, no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_e4m3_f32(kTileM, NT < 16 ? 16 : NT);
+      UnitIter it{&p, NT};
+      int q = 0, pk = 0;
+      bool ok = true;
+      while (ok && it.next()) {
+        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+        for (int kb = kb0; kb < kb1; ++kb, ++q, ++pk) {
+          const int s = q % S::NS, b = pk & 1;
+          if (pk >= 2 && !mbar_wait(&part_empty[b], ((pk >> 1) - 1) & 1, abort)) { ok = false; break; }
+          if (!mbar_wait(&full[s], (q / S::NS) & 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + b * S::TC;
+          const uint32_t a = sbase + s * S::STAGE, bb = a + S::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < kBK / 32; ++ks) {
+            mma_f8_ss(d, smem_desc(a + ks * 32, 16, 1024, kSwizzle128B), smem_desc(bb + ks * 32, 16, 1024, kSwizzle128B),
+                      IDESC, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&part_full[b]);
+        }
+      }
+      if (!ok) raise_abort(abort, status, kStatusTimeout);
+      tc_commit(drain);
+      mbar_wait(drain, 0, no_abort);
+    }
+  } else {
+    // ------------------------------------------------- promotion + epilogue
+    const uint32_t qtr = warp & 3;
+    const int r = (int)(qtr * 32 + lane);  // weight row within the tile
+    const int et = threadIdx.x - 64;       // 0..127
+    const bool silu = p.epi == DSB_EPI_SILU_GATE;
+    constexpr int NCH = NT < 32 ? 1 : NT / 32;
+    constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
+    UnitIter it{&p, NT};
+    int pk = 0;
+    bool ok = true;
+    while (ok && it.next()) {
+      const int tbase = it.tok0 + it.nt * NT;
+      const int tcount = min(NT, it.tok1 - tbase);
+      const int tile_id = it.g * p.m_tiles + it.mt;
+      const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+      const float* wsc = p.w_scale + ((int64_t)tile_id * p.scale_rows + (r % p.scale_rows)) * KB;
+      float acc[NCH][32];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c][i] = 0.0f;
+      for (int kb = kb0; kb < kb1; ++kb, ++pk) {
+        const int b = pk & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk >> 1) & 1, abort))) {
+          raise_abort(abort, status, kStatusTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float swk = __ldg(wsc + kb);
+        const float* sxk = p.x_scale + (int64_t)tbase * p.ld_xs + it.g * (p.x_group_col / kBK) + kb;
+        const uint32_t taddr = tmem + ((qtr * 32) << 16) + b * S::TC;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(taddr + c * 32, raw);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < CW; ++i) {
+            const int t = c * 32 + i;
+            const float sx = t < tcount ? __ldg(sxk + (int64_t)t * p.ld_xs) : 0.0f;
+            acc[c][i] = fmaf(__uint_as_float(raw[i]), swk * sx, acc[c][i]);
+          }
+        }
+        // the partial buffer is free once every chunk has been read
+        tc_fence_before();
+        mbar_arrive(&part_empty[b]);
+      }
+      if (!ok) break;
+
+      auto apply = [&](int c, float (&v)[32]) {
+        if (silu) {
+          // rows 2j / 2j+1 of the tile are gate / up of output feature 64*mt + j
+          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            const int t = c * 32 + i;
+            if ((r & 1) == 0 && t < tcount) {
+              const float gt = v[i];
+              const float hval = gt / (1.0f + __expf(-gt)) * up;
+              const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
+              if (p.y_f32) static_cast<float*>(p.y)[o] = hval;
+              else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(hval);
+            }
+          }
+        } else if (it.mt * kTileM + r < p.M) {
+          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            if (t < tcount) {
+              const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
+              float x = v[i];
+              if (p.epi == DSB_EPI_ROWSCALE) x *= p.row_scale[tbase + t];
+              if (p.epi == DSB_EPI_ADD) {
+                static_cast<float*>(p.y)[o] += x;
+              } else if (p.y_f32) {
+                static_cast<float*>(p.y)[o] = x;
+              } else {
+                static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(x);
+              }
+            }
+          }
+        }
+      };
+
+      if (p.splits == 1) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) apply(c, acc[c]);
+        continue;
+      }
+      // split-K: publish this split's promoted sum; the last split reduces
+      float* part = p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int i = 0; i < CW; ++i) part[(c * 32 + i) * kTileM + r] = acc[c][i];
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) {
+        const int prev = atomicAdd(&p.counters[tile_id], 1);
+        *last_flag = (prev == p.splits - 1) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag != 0) {
+        __threadfence();
+        const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+          for (int s2 = 0; s2 < p.splits; ++s2) {
+#pragma unroll
+            for (int i = 0; i < CW; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c * 32 + i) * kTileM);
+          }
+          apply(c, v);
+        }
+        if (et == 0) p.counters[tile_id] = 0;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TCOLS);
+  }
+}
+
+template <int NT>
+int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_tiles) {
+  using S = Fp8Shape<NT>;
+  CUtensorMap map_w, map_x;
+  const uint64_t w_rows = (uint64_t)a->G * a->M;
+  int rc = make_tmap_2d(ctx, &map_w, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->K, w_rows, a->ldw, kBK, kTileM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != DSB_OK) return rc;
+  rc = make_tmap_2d(ctx, &map_x, a->x, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)a->ldx, (uint64_t)a->T, a->ldx, kBK,
+                    NT, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != DSB_OK) return rc;
+  Fp8Params p;
+  p.T = a->T;
+  p.M = a->M;
+  p.K = a->K;
+  p.G = a->G;
+  p.x_group_col = a->x_group_col;
+  p.tok_offsets = a->tok_offsets;
+  p.w_scale = a->w_scale;
+  p.scale_rows = a->scale_rows;
+  p.x_scale = a->x_scale;
+  p.ld_xs = a->ld_xs;
+  p.y = a->y;
+  p.ldy = a->ldy;
+  p.y_group_col = a->y_group_col;
+  p.y_f32 = a->y_f32;
+  p.epi = a->epilogue;
+  p.row_scale = a->row_scale;
+  p.splits = splits;
+  p.m_tiles = m_tiles;
+  p.n_tiles = a->G * m_tiles * splits;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  if (splits > 1) {
+    const size_t tiles = (size_t)m_tiles * a->G;
+    rc = ensure_workspace(ctx, tiles * splits * NT * kTileM * sizeof(float));
+    if (rc != DSB_OK) return rc;
+    rc = ensure_counters(ctx, tiles);
+    if (rc != DSB_OK) return rc;
+    p.ws = static_cast<float*>(ctx->ws);
+    p.counters = ctx->counters;
+  }
+  auto kern = gemm_fp8_kernel<NT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+    attr_set = true;
+  }
+  const int grid = std::min(p.n_tiles, ctx->sm_count);
+  kern<<<grid, kThreads, S::SMEM, ctx->stream>>>(map_w, map_x, p, ctx->d_status);
+  DSB_CUDA_TRY(ctx, cudaGetLastError());
+  ctx->stats.kernel_launches++;
+  ctx->stats.gemm_calls++;
+  return DSB_OK;
+}
+
+}  // namespace
+}  // namespace dsb
+
+extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
+  using namespace dsb;
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (a == nullptr || a->w == nullptr || a->w_scale == nullptr || a->x == nullptr || a->x_scale == nullptr ||
+      a->y == nullptr)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: null argument");
+  if (a->T <= 0 || a->M <= 0 || a->K <= 0 || a->G <= 0 || a->ldw < a->K || a->ldx <= 0 || a->ld_xs <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: bad sizes T=%d M=%d K=%d G=%d", a->T, a->M, a->K, a->G);
+  if ((a->K % kBK) || (a->ldw % 16) || (a->ldx % 16) || (a->x_group_col % kBK))
+    return fail(ctx, DSB_EINVAL,
+                "dsb_linear_fp8: K and group column offsets must be multiples of 128, row pitches multiples of 16");
+  if (a->scale_rows != 1 && a->scale_rows != 2)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: scale_rows must be 1 or 2");
+  if (a->epilogue < DSB_EPI_STORE || a->epilogue > DSB_EPI_ROWSCALE)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: unknown epilogue %d", a->epilogue);
+  if (a->epilogue == DSB_EPI_SILU_GATE && (a->M % kTileM) != 0)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: SiLU-gate needs M (gate+up rows) to be a multiple of 128");
+  if (a->epilogue == DSB_EPI_ADD && !a->y_f32)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: the residual-add epilogue needs an fp32 output");
+  if (a->epilogue == DSB_EPI_ROWSCALE && a->row_scale == nullptr)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: row-scale epilogue needs row_scale");
+  const int bound = a->max_tokens_per_group > 0 ? a->max_tokens_per_group : a->T;
+  const int m_tiles = (a->M + kTileM - 1) / kTileM;
+  const int KB = a->K / kBK;
+  int splits = 1;
+  if (a->tok_offsets == nullptr && a->T <= 128) {
+    // small decode GEMMs (one token tile, so the split partials are per
+    // weight tile): split K so every SM streams a share of the weights
+    const int tiles = m_tiles * a->G;
+    const int want = std::max(1, ctx->sm_count / std::max(1, tiles));
+    splits = std::max(1, std::min({want, KB / 2, 8}));
+  }
+  int NT = 16;
+  while (NT < bound && NT < 128) NT *= 2;
+  switch (NT) {
+    case 16: return launch_fp8<16>(ctx, a, splits, m_tiles);
+    case 32: return launch_fp8<32>(ctx, a, splits, m_tiles);
+    case 64: return launch_fp8<64>(ctx, a, splits, m_tiles);
+    default: return launch_fp8<128>(ctx, a, splits, m_tiles);
+  }
+}

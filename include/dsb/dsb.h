@@ -213,6 +213,64 @@ typedef struct dsb_linear_args {
 
 DSB_API int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* args);
 
+/* -------------------------------------------------------------- FP8 e4m3
+ *
+ * DeepSeek-V3 block-scaled FP8: weights e4m3 with one fp32 scale per 128x128
+ * block (the checkpoints' weight_scale_inv), activations e4m3 with one fp32
+ * scale per token and 128 columns.  The reference has no FP8 path (its
+ * safetensors dtype parser, src/hf/safetensors.cpp:12-20, knows F32/F16/BF16
+ * only); these replace linear_to_slot / moe_to_slot's GEMVs
+ * (src/models/deepseek/cuda_backend.cpp:782-883) for FP8 checkpoints. */
+
+/* q = e4m3(x / s) with s = amax / 448 over each 128 columns of a row (1 for an
+ * all-zero group), round to nearest even, saturating; s written to
+ * scales[row * ld_scales + col / 128].  x bf16 or fp32 (x_dtype DSB_DTYPE_*)
+ * [.., ldx]; with src_rows (device int32 [T]) row t reads x row
+ * src_rows[t] / k (the permuted-token gather of dsb_gather_rows), else row t.
+ * K a multiple of 128. */
+DSB_API int dsb_quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const int32_t* src_rows,
+                                int k, int T, int K, void* q, int64_t ldq, float* scales, int64_t ld_scales);
+
+/* Weight quantisation for bf16/fp32 checkpoints: w [M, K] -> e4m3 q [M, K]
+ * and scales [ceil(M/128), ceil(K/128)] = amax / 448 of each 128x128 block
+ * (1 for an all-zero block); the same rounding as dsb_quant_act_1x128. */
+DSB_API int dsb_quant_weight_128x128(dsb_ctx* ctx, const void* w, int w_dtype, int64_t M, int64_t K, void* q,
+                                     float* scales);
+
+/* Grouped block-scaled FP8 linear; same grouping, token ranges and epilogues
+ * as dsb_linear:
+ *   acc[t, n] = sum_kb sw(g, n, kb) * x_scale[t, g*x_group_col/128 + kb]
+ *               * sum_{k in kb} x[t, g*x_group_col + k] * w[g*M + n, k]
+ * Weight scales are per 128-row tile of a group: with scale_rows 1,
+ * w_scale[(g*ceil(M/128) + n/128) * K/128 + kb] (the checkpoints' per-matrix
+ * [ceil(M/128), K/128] layout stacked over groups); with scale_rows 2 (a
+ * row-interleaved gate|up matrix for DSB_EPI_SILU_GATE), tile j holds
+ * gate and up rows 64j..64j+63 and w_scale[((g*M/128 + j) * 2 + (n & 1)) * K/128 + kb]
+ * is the gate (n even) or up (n odd) scale of those rows.  K, x_group_col
+ * multiples of 128; ldw, ldx multiples of 16 bytes. */
+typedef struct dsb_linear_fp8_args {
+  const void* w;              /* e4m3 [G * M, ldw] */
+  int64_t ldw;                /* row pitch of w (bytes) */
+  const float* w_scale;       /* fp32, layout above */
+  int scale_rows;             /* 1 or 2 */
+  const void* x;              /* e4m3 [T, ldx] */
+  int64_t ldx;                /* row pitch of x (bytes) */
+  const float* x_scale;       /* fp32 [T, ld_xs] */
+  int64_t ld_xs;              /* row pitch of x_scale (floats) */
+  int64_t x_group_col;        /* group g reads x columns [g*x_group_col, +K) */
+  const int32_t* tok_offsets; /* device int32 [G + 1] row ranges, or NULL */
+  int T, M, K, G;
+  int max_tokens_per_group;   /* host bound on rows per group (<= 0: T) */
+  void* y;                    /* output (bf16 or fp32 per y_f32) */
+  int64_t ldy;
+  int64_t y_group_col;
+  int y_f32;
+  int epilogue;               /* DSB_EPI_* */
+  const float* row_scale;     /* DSB_EPI_ROWSCALE: fp32 [T] */
+} dsb_linear_fp8_args;
+
+DSB_API int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* args);
+
 /* ---------------------------------------------------------------- row ops */
 
 /* y = x / sqrt(mean(x^2) + eps) * w per row, written as bf16 (y_bf16) and/or

@@ -76,6 +76,7 @@ def oracle() -> ctypes.CDLL:
         _proto(l, "orc_f32_to_e4m3", ctypes.c_uint8, [ctypes.c_float])
         _proto(l, "orc_quant_act_1x128", None, [f32p, i64, i64, u8p, f32p])
         _proto(l, "orc_fp8_linear", None, [u8p, f32p, u8p, f32p, i64, i64, i64, f32p])
+        _proto(l, "orc_quant_weight_128x128", None, [f32p, i64, i64, u8p, f32p])
         _proto(l, "orc_dense_mlp_f32", None, [f32p, f32p, f32p, f32p, i64, i64, f32p])
         _proto(l, "orc_moe_softmax_f32", ctypes.c_int, [f32p] * 7 + [ctypes.c_int] * 6 + [ctypes.c_float, f32p, f32p])
         _proto(l, "orc_moe_mix_f32", None,

@@ -551,6 +551,24 @@ ORC_API void orc_quant_act_1x128(const float* x, int64_t T, int64_t K, uint8_t* 
   }
 }
 
+/* Weight quantisation per 128x128 block: scale = amax / 448 over the block
+ * (1 when it is all zero), q = e4m3(w / scale); scales [ceil(M/128), ceil(K/128)]. */
+ORC_API void orc_quant_weight_128x128(const float* w, int64_t M, int64_t K, uint8_t* q, float* scales) {
+  const int64_t GM = (M + 127) / 128, GK = (K + 127) / 128;
+  for (int64_t bm = 0; bm < GM; ++bm) {
+    for (int64_t bk = 0; bk < GK; ++bk) {
+      const int64_t r1 = (bm + 1) * 128 < M ? (bm + 1) * 128 : M, c1 = (bk + 1) * 128 < K ? (bk + 1) * 128 : K;
+      float amax = 0.0f;
+      for (int64_t r = bm * 128; r < r1; ++r)
+        for (int64_t c = bk * 128; c < c1; ++c) amax = fmaxf(amax, fabsf(w[r * K + c]));
+      const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
+      scales[bm * GK + bk] = sc;
+      for (int64_t r = bm * 128; r < r1; ++r)
+        for (int64_t c = bk * 128; c < c1; ++c) q[r * K + c] = orc_f32_to_e4m3(w[r * K + c] / sc);
+    }
+  }
+}
+
 /*
  * y[t, o] = sum_k (e4m3(w[o,k]) * sw[o/128][k/128]) * (e4m3(x[t,k]) * sx[t][k/128]),
  * accumulated in double and rounded to float; equals ds::rt::linear
