@@ -674,13 +674,150 @@ def run_expert_gemm(args):
     ctx.close()
 
 
+def fp8_peak_tflops():
+    """Dense e4m3 GEMM throughput of this GPU (torch._scaled_mm, cuBLASLt,
+    8192^3, 20 launches) as the tensor-roofline denominator for FP8 work."""
+    import torch
+
+    n = 8192
+    a = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device="cuda")
+    for _ in range(3):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    e1.record()
+    e1.synchronize()
+    return 2 * n ** 3 / (e0.elapsed_time(e1) / 20 * 1e-3) / 1e12
+
+
+def moe_fp8_cpu_baseline(cfg, n_tokens=1):
+    """The oracle's FP8 restatement of one token through k + n_shared experts
+    (double accumulation, 1 core), as tokens/s of one MoE layer."""
+    import numpy as np
+
+    import oracle.model as OM
+
+    D, I, k, ns = cfg["hidden_size"], cfg["moe_intermediate_size"], cfg["num_experts_per_tok"], cfg["n_shared_experts"]
+    G = k + ns
+    rng = np.random.default_rng(0)
+    q = lambda *s: rng.integers(0, 0x7E, size=s, dtype=np.uint8)  # noqa: E731
+    sc = lambda *s: np.full(s, 1e-3, np.float32)  # noqa: E731
+    x = rng.standard_normal((n_tokens, D)).astype(np.float32)
+    ids = np.tile(np.arange(G, dtype=np.int32), (n_tokens, 1))
+    w = np.ones((n_tokens, G), np.float32)
+    t0 = time.time()
+    OM.moe_fp8(x, ids, w, q(G, I, D), sc(G, I // 128, D // 128), q(G, I, D), sc(G, I // 128, D // 128),
+               q(G, D, I), sc(G, D // 128, I // 128))
+    dt = time.time() - t0
+    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n_tokens} token(s) through {k} routed + {ns} shared FP8 experts (D={D}, I={I}) in the "
+                      f"oracle's C restatement, double accumulation"}
+
+
+def run_moe_fp8(args):
+    """One DeepSeek-V3 MoE layer in FP8 on one GPU: fp32 router logits,
+    sigmoid + bias grouped top-8, dsb_moe_ffn_fp8 (256 routed + 1 shared
+    expert, D=7168, I=2048, e4m3 weights with 128x128 scales) for T tokens."""
+    import numpy as np
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+    from deepseek_cpp_infer_b200.workloads import V3_MOE, MoeFp8Weights
+
+    cfg = dict(V3_MOE)
+    torch.cuda.set_device(0)
+    ctx = dsb.Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    T, D, I = args.batch, cfg["hidden_size"], cfg["moe_intermediate_size"]
+    E, k, ns = cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["n_shared_experts"]
+    layer = MoeFp8Weights(ctx, E, ns, D, I, seed=2)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    w_gate = torch.randn(E, D, generator=gen, device="cuda") * 0.02
+    bias = torch.randn(E, generator=gen, device="cuda") * 0.01
+    x = torch.randn(T, D, generator=gen, device="cuda").to(torch.bfloat16)
+    x32 = x.float()
+    logits = torch.empty(T, E, device="cuda")
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.empty(T, k, device="cuda")
+    h = torch.zeros(T, D, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        ctx.router_logits(x32, w_gate, logits)
+        ctx.moe_route(logits, ids, wts, k, scoring=dsb.SCORE_SIGMOID, bias=bias, n_group=cfg["n_group"],
+                      topk_group=cfg["topk_group"], norm_topk=cfg["norm_topk_prob"],
+                      routed_scale=cfg["routed_scaling_factor"])
+        ctx.moe_ffn_fp8(layer.gate_up, layer.gate_up_scale, layer.down, layer.down_scale, E=E, n_shared=ns, x=x,
+                        ids=ids, weights=wts, h=h)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        ctx.sync()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ctx.sync()
+    sampler = ClockSampler(0)
+    sampler.start()
+    t_probe = timed(step, 3)
+    timed(step, max(1, int(1000.0 / max(t_probe, 1e-3))))
+    ctx.reset_stats()
+    ms = timed(step, args.steps)
+    clocks = sampler.stop()
+    launches = ctx.stats()["kernel_launches"] // args.steps
+
+    picks = ids.cpu().numpy()
+    touched = len(np.unique(picks)) + ns
+    N = T * (k + ns)
+    wbytes = touched * 3 * I * D + touched * (3 * I * D // (128 * 128)) * 4
+    nbytes = wbytes + T * D * 2 + 2 * T * D * 4 + T * E * 4
+    flops = 2 * N * 3 * I * D + 2 * T * E * D
+    peak, peak_kind = measured_peaks()
+    fp8_peak = fp8_peak_tflops()
+    gbs, tfs = nbytes / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / 1e12
+    bound = "hbm" if gbs / peak >= tfs / fp8_peak else "tensor"
+    cpu = None if args.no_cpu_baseline else moe_fp8_cpu_baseline(cfg)
+    line = {
+        "metric": "DeepSeek-V3 MoE layer (FP8 experts) tokens/s", "value": T / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (bf16 activations)",
+        "data": "synthetic: N(0,0.02) weights quantised to e4m3 with 128x128 scales, N(0,1) bf16 tokens",
+        "config": {"workload": f"one V3 MoE layer: router (fp32 logits, sigmoid + bias, 8 groups / top-4 / top-8, "
+                               f"scale 2.5) + 256 routed and 1 shared FP8 expert, D=7168, I=2048; T={T} tokens",
+                   "tokens": T, "experts_touched": int(touched), "weight_bytes": int(wbytes),
+                   "l2": "every step streams the touched experts' weights (GBs), far above the 126 MB L2"},
+        "roofline": {"bound": bound, "achieved": gbs if bound == "hbm" else tfs,
+                     "peak": peak if bound == "hbm" else fp8_peak, "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                     "frac": gbs / peak if bound == "hbm" else tfs / fp8_peak, "traffic": None,
+                     "peak_kind": peak_kind if bound == "hbm" else "measured on this GPU: torch._scaled_mm e4m3 8192^3",
+                     "hbm_frac": gbs / peak, "tensor_frac": tfs / fp8_peak, "fp8_peak_tflops": fp8_peak,
+                     "note": "whole layer: touched experts' e4m3 weights + scales + x, h, logits per step / step time"},
+        "gpu_launches": launches, "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "mla", "expert-gemm"])
+    ap.add_argument("--workload", default="model", choices=["model", "mla", "expert-gemm", "moe-fp8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
@@ -689,6 +826,9 @@ def main():
     if args.workload == "expert-gemm":
         args.batch = args.batch or 32
         run_expert_gemm(args)
+    elif args.workload == "moe-fp8":
+        args.batch = args.batch or 128
+        run_moe_fp8(args)
     elif args.workload == "mla":
         args.batch = args.batch or 64
         run_mla_reference(args) if args.impl == "reference" else run_mla_ours(args)

@@ -74,7 +74,16 @@ class LinearFp8Args(ctypes.Structure):
     ]
 
 
+class MoeFp8Layer(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", ctypes.c_void_p), ("gate_up_scale", ctypes.c_void_p), ("down", ctypes.c_void_p),
+        ("down_scale", ctypes.c_void_p), ("E", ctypes.c_int), ("n_shared", ctypes.c_int), ("D", ctypes.c_int),
+        ("I", ctypes.c_int),
+    ]
+
+
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream as a stream handle
 
 
 class ModelConfig(ctypes.Structure):
@@ -114,6 +123,8 @@ _PROTOS = [
     ("dsb_quant_act_1x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _vp, _ci, _ci, _ci, _vp, _i64, _vp, _i64]),
     ("dsb_quant_weight_128x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _i64, _vp, _vp]),
     ("dsb_linear_fp8", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearFp8Args)]),
+    ("dsb_moe_ffn_fp8", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(MoeFp8Layer), _vp, _i64, _ci, _ci, _vp, _vp, _vp]),
     ("dsb_rmsnorm", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _cf, _vp, _i64, _vp, _i64]),
     ("dsb_kv_norm_rope_append", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _ci, _ci, _cf, _cf, _vp, _vp]),
@@ -211,6 +222,12 @@ class Context:
     def set_stream(self, stream_handle: int | None):
         self._check(self._l.dsb_ctx_set_stream(self.h, stream_handle or None))
 
+    def use_legacy_stream(self):
+        """Run on CUDA's legacy default stream (torch's default stream), so
+        the context's kernels are ordered after the torch operations that
+        produced their inputs and before those that read their outputs."""
+        self.set_stream(STREAM_LEGACY)
+
     @property
     def stream(self) -> int:
         return self._l.dsb_ctx_stream(self.h) or 0
@@ -288,6 +305,15 @@ class Context:
             epilogue=epilogue, row_scale=_ptr(row_scale),
         )
         self._check(self._l.dsb_linear_fp8(self.h, ctypes.byref(a)))
+
+    def moe_ffn_fp8(self, gate_up, gate_up_scale, down, down_scale, *, E, n_shared, x, ids, weights, h):
+        """dsb_moe_ffn_fp8: h[T, D] += experts(x[T, D] bf16) for picks ids/weights [T, k]."""
+        T, D = x.shape
+        I = down.shape[-1]
+        layer = MoeFp8Layer(gate_up=_ptr(gate_up), gate_up_scale=_ptr(gate_up_scale), down=_ptr(down),
+                            down_scale=_ptr(down_scale), E=E, n_shared=n_shared, D=D, I=I)
+        self._check(self._l.dsb_moe_ffn_fp8(self.h, ctypes.byref(layer), _ptr(x), x.stride(0), T, ids.shape[1],
+                                            _ptr(ids), _ptr(weights), _ptr(h)))
 
     # ---- row and routing ops (device tensors; shapes from the tensors)
     def rmsnorm(self, x, w, eps, y_bf16=None, y_f32=None):

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "dsb_internal.h"
+#include "dsb_ptx.cuh"
 
 namespace dsb {
 
@@ -26,63 +27,40 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...) {
   return code;
 }
 
-int ensure_workspace(dsb_ctx* ctx, size_t bytes) {
-  if (bytes <= ctx->ws_bytes) return DSB_OK;
-  size_t grow = ctx->ws_bytes ? ctx->ws_bytes : (size_t)1 << 20;
+// Grow (never shrink) one of the context's device buffers to `bytes`,
+// doubling from `first`.  The old buffer may still be read by queued kernels,
+// so the stream is drained before it is freed.
+int ensure_buffer(dsb_ctx* ctx, void** buf, size_t* cap, size_t bytes, size_t first, const char* what) {
+  if (bytes <= *cap) return DSB_OK;
+  size_t grow = *cap ? *cap : first;
   while (grow < bytes) grow *= 2;
-  if (ctx->ws != nullptr) {
-    // the previous buffer may still be read by queued kernels
+  if (*buf != nullptr) {
     DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    DSB_CUDA_TRY(ctx, cudaFree(ctx->ws));
-    ctx->ws = nullptr;
-    ctx->ws_bytes = 0;
+    DSB_CUDA_TRY(ctx, cudaFree(*buf));
+    *buf = nullptr;
+    *cap = 0;
   }
-  cudaError_t e = cudaMalloc(&ctx->ws, grow);
+  cudaError_t e = cudaMalloc(buf, grow);
   if (e != cudaSuccess) {
-    ctx->ws = nullptr;
-    return fail(ctx, DSB_ENOMEM, "workspace cudaMalloc(%zu): %s", grow, cudaGetErrorString(e));
+    *buf = nullptr;
+    return fail(ctx, DSB_ENOMEM, "%s cudaMalloc(%zu): %s", what, grow, cudaGetErrorString(e));
   }
-  ctx->ws_bytes = grow;
-  ctx->stats.workspace_bytes = grow;
+  *cap = grow;
   return DSB_OK;
+}
+
+int ensure_workspace(dsb_ctx* ctx, size_t bytes) {
+  const int rc = ensure_buffer(ctx, &ctx->ws, &ctx->ws_bytes, bytes, (size_t)1 << 20, "workspace");
+  ctx->stats.workspace_bytes = ctx->ws_bytes;
+  return rc;
 }
 
 int ensure_aux(dsb_ctx* ctx, size_t bytes) {
-  if (bytes <= ctx->aux_bytes) return DSB_OK;
-  size_t grow = ctx->aux_bytes ? ctx->aux_bytes : (size_t)64 << 10;
-  while (grow < bytes) grow *= 2;
-  if (ctx->aux != nullptr) {
-    DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    DSB_CUDA_TRY(ctx, cudaFree(ctx->aux));
-    ctx->aux = nullptr;
-    ctx->aux_bytes = 0;
-  }
-  cudaError_t e = cudaMalloc(&ctx->aux, grow);
-  if (e != cudaSuccess) {
-    ctx->aux = nullptr;
-    return fail(ctx, DSB_ENOMEM, "aux cudaMalloc(%zu): %s", grow, cudaGetErrorString(e));
-  }
-  ctx->aux_bytes = grow;
-  return DSB_OK;
+  return ensure_buffer(ctx, &ctx->aux, &ctx->aux_bytes, bytes, (size_t)64 << 10, "aux");
 }
 
 int ensure_step(dsb_ctx* ctx, size_t bytes) {
-  if (bytes <= ctx->step_bytes) return DSB_OK;
-  size_t grow = ctx->step_bytes ? ctx->step_bytes : (size_t)1 << 20;
-  while (grow < bytes) grow *= 2;
-  if (ctx->step != nullptr) {
-    DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    DSB_CUDA_TRY(ctx, cudaFree(ctx->step));
-    ctx->step = nullptr;
-    ctx->step_bytes = 0;
-  }
-  cudaError_t e = cudaMalloc(&ctx->step, grow);
-  if (e != cudaSuccess) {
-    ctx->step = nullptr;
-    return fail(ctx, DSB_ENOMEM, "step cudaMalloc(%zu): %s", grow, cudaGetErrorString(e));
-  }
-  ctx->step_bytes = grow;
-  return DSB_OK;
+  return ensure_buffer(ctx, &ctx->step, &ctx->step_bytes, bytes, (size_t)1 << 20, "step");
 }
 
 int ensure_counters(dsb_ctx* ctx, size_t n) {
@@ -197,6 +175,8 @@ int dsb_ctx_destroy(dsb_ctx* ctx) {
   if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->step) cudaFree(ctx->step);
+  if (ctx->perm) cudaFree(ctx->perm);
+  if (ctx->moe) cudaFree(ctx->moe);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -235,6 +215,8 @@ int dsb_sync(dsb_ctx* ctx) {
   DSB_CUDA_TRY(ctx, cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   if (st != 0) {
     DSB_CUDA_TRY(ctx, cudaMemset(ctx->d_status, 0, sizeof(int)));
+    if (st == dsb::kStatusBadInput)
+      return dsb::fail(ctx, DSB_EINVAL, "a kernel dropped an out-of-range index (device status %d)", st);
     return dsb::fail(ctx, DSB_ETIMEOUT, "a kernel's bounded wait ran out (device status %d)", st);
   }
   return DSB_OK;

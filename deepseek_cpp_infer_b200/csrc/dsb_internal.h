@@ -24,6 +24,10 @@ struct dsb_ctx {
   size_t n_counters = 0;
   void* step = nullptr;     // activations of dsb_decode_step
   size_t step_bytes = 0;
+  void* perm = nullptr;     // per-chunk expert histograms of the multi-block permute
+  size_t perm_bytes = 0;
+  void* moe = nullptr;      // activations of dsb_moe_ffn_fp8
+  size_t moe_bytes = 0;
   std::string last_error;
   dsb_stats stats{};
 };
@@ -50,6 +54,8 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
     if (e_ != cudaSuccess) return ::dsb::fail((ctx), DSB_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
+// Grow one of the context's device buffers (*buf, capacity *cap) to `bytes`.
+int ensure_buffer(dsb_ctx* ctx, void** buf, size_t* cap, size_t bytes, size_t first, const char* what);
 // Ensure ctx->ws holds at least `bytes`; grows (never shrinks) the buffer.
 int ensure_workspace(dsb_ctx* ctx, size_t bytes);
 // Same for ctx->aux (small per-call metadata such as work lists).

@@ -22,8 +22,9 @@
 // linear GEMVs of moe_to_slot / linear_to_slot (src/models/deepseek/
 // cuda_backend.cpp:782-883) for block-scaled FP8 checkpoints.
 //
-// Roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-5
-// promotion + epilogue (warp w owns TMEM lanes 32*(w%4)..+31).
+// Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-9
+// promotion + epilogue (warp w owns TMEM lanes 32*(w%4)..+31 and half of the
+// token columns).
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -39,7 +40,7 @@ namespace {
 
 constexpr int kBK = 128;      // K bytes (e4m3 elements) per stage = one scale block
 constexpr int kTileM = 128;   // weight rows per tile (MMA M)
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 
 struct Fp8Params {
   int T, M, K, G;
@@ -69,7 +70,8 @@ struct Fp8Shape {
   static constexpr int NS = (196 * 1024) / STAGE;
   static constexpr int OFF_BAR = NS * STAGE;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
-  static constexpr int SMEM = OFF_MISC + 32 + 1024;
+  static constexpr int OFF_SX = OFF_MISC + 64;  // [8 warps][2 buffers][2 row parities][NT/2] scales
+  static constexpr int SMEM = OFF_SX + 8 * 4 * (NT / 2) * 4 + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
   static constexpr uint32_t TCOLS = 2 * TC;
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
   volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 12);
+  float* sx_smem = reinterpret_cast<float*>(smem + S::OFF_SX);
 
   const int KB = p.K / kBK;
   const uint32_t warp = warp_id(), lane = lane_id();
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&part_full[b], 1);
-      mbar_init(&part_empty[b], 128);
+      mbar_init(&part_empty[b], 256);
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -212,12 +215,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------- promotion + epilogue
+    // 8 warps: warp w reads TMEM lanes 32*(w%4)..+31 (weight rows of the
+    // tile) and token columns [h*HC, (h+1)*HC), h = (w-2)/4.
+    constexpr int HC = NT / 2;             // token columns per thread (8..64)
+    constexpr int LW = HC < 32 ? HC : 32;  // columns per tcgen05.ld
+    constexpr int NL = HC / LW;            // loads per K block
+    constexpr int PER = (HC + 31) / 32;    // token scales loaded per lane
     const uint32_t qtr = warp & 3;
-    const int r = (int)(qtr * 32 + lane);  // weight row within the tile
-    const int et = threadIdx.x - 64;       // 0..127
+    const int c0 = (int)((warp - 2) >> 2) * HC;  // this thread's first token column
+    const int r = (int)(qtr * 32 + lane);        // weight row within the tile (parity = lane parity)
+    const int et = threadIdx.x - 64;             // 0..255
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
-    constexpr int NCH = NT < 32 ? 1 : NT / 32;
-    constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
+    // this warp's scale vectors: [2 buffers][row parity][HC], sw(row) * sx[t] of one K block
+    float* sxw = sx_smem + (warp - 2) * 4 * HC;
     UnitIter it{&p, NT};
     int pk = 0;
     bool ok = true;
@@ -226,49 +236,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tcount = min(NT, it.tok1 - tbase);
       const int tile_id = it.g * p.m_tiles + it.mt;
       const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-      const float* wsc = p.w_scale + ((int64_t)tile_id * p.scale_rows + (r % p.scale_rows)) * KB;
-      float acc[NCH][32];
+      const float* ws_even = p.w_scale + (int64_t)tile_id * p.scale_rows * KB;
+      const float* ws_odd = ws_even + (int64_t)(p.scale_rows - 1) * KB;
+      const float* sxrow = p.x_scale + it.g * (p.x_group_col / kBK);
+      float acc[HC];
 #pragma unroll
-      for (int c = 0; c < NCH; ++c)
+      for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
+      // The scales of the next K block are fetched (one value per lane) while
+      // the current one is promoted, then stored premultiplied by the weight
+      // scale of each row parity, so the promotion is one FMA per element.
+      float nx[PER], nwe = 0.0f, nwo = 0.0f;
+      auto load_sx = [&](int kb) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[c][i] = 0.0f;
+        for (int j = 0; j < PER; ++j) {
+          const int i = (int)lane + 32 * j, t = c0 + i;
+          nx[j] = (i < HC && t < tcount) ? __ldg(sxrow + (int64_t)(tbase + t) * p.ld_xs + kb) : 0.0f;
+        }
+        nwe = __ldg(ws_even + kb);
+        nwo = __ldg(ws_odd + kb);
+      };
+      auto store_sx = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+          const int i = (int)lane + 32 * j;
+          if (i < HC) {
+            sxw[(buf * 2 + 0) * HC + i] = nwe * nx[j];
+            sxw[(buf * 2 + 1) * HC + i] = nwo * nx[j];
+          }
+        }
+      };
+      __syncwarp();
+      load_sx(kb0);
+      store_sx(pk & 1);
+      __syncwarp();
       for (int kb = kb0; kb < kb1; ++kb, ++pk) {
         const int b = pk & 1;
+        if (kb + 1 < kb1) load_sx(kb + 1);
         if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk >> 1) & 1, abort))) {
           raise_abort(abort, status, kStatusTimeout);
           ok = false;
           break;
         }
         tc_fence_after();
-        const float swk = __ldg(wsc + kb);
-        const float* sxk = p.x_scale + (int64_t)tbase * p.ld_xs + it.g * (p.x_group_col / kBK) + kb;
-        const uint32_t taddr = tmem + ((qtr * 32) << 16) + b * S::TC;
+        const uint32_t taddr = tmem + ((qtr * 32) << 16) + b * S::TC + c0;
+        const float4* s4 = reinterpret_cast<const float4*>(sxw + (b * 2 + (int)(lane & 1)) * HC);
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          uint32_t raw[32];
-          tmem_ld32(taddr + c * 32, raw);
+        for (int l = 0; l < NL; ++l) {
+          uint32_t raw[LW];
+          if constexpr (LW == 32) tmem_ld32(taddr + l * LW, raw);
+          else if constexpr (LW == 16) tmem_ld16(taddr + l * LW, raw);
+          else tmem_ld8(taddr + l * LW, raw);
           tmem_ld_wait();
+          if (l == NL - 1) {
+            // the partial buffer is free once it has been read into registers
+            tc_fence_before();
+            mbar_arrive(&part_empty[b]);
+          }
 #pragma unroll
-          for (int i = 0; i < CW; ++i) {
-            const int t = c * 32 + i;
-            const float sx = t < tcount ? __ldg(sxk + (int64_t)t * p.ld_xs) : 0.0f;
-            acc[c][i] = fmaf(__uint_as_float(raw[i]), swk * sx, acc[c][i]);
+          for (int i = 0; i < LW; i += 4) {
+            const int ci = l * LW + i;
+            const float4 sv = s4[ci >> 2];
+            acc[ci] = fmaf(__uint_as_float(raw[i]), sv.x, acc[ci]);
+            acc[ci + 1] = fmaf(__uint_as_float(raw[i + 1]), sv.y, acc[ci + 1]);
+            acc[ci + 2] = fmaf(__uint_as_float(raw[i + 2]), sv.z, acc[ci + 2]);
+            acc[ci + 3] = fmaf(__uint_as_float(raw[i + 3]), sv.w, acc[ci + 3]);
           }
         }
-        // the partial buffer is free once every chunk has been read
-        tc_fence_before();
-        mbar_arrive(&part_empty[b]);
+        if (kb + 1 < kb1) {
+          __syncwarp();  // every lane is done with the buffer written next
+          store_sx(b ^ 1);
+          __syncwarp();
+        }
       }
       if (!ok) break;
 
-      auto apply = [&](int c, float (&v)[32]) {
+      auto apply = [&](float (&v)[HC]) {
         if (silu) {
           // rows 2j / 2j+1 of the tile are gate / up of output feature 64*mt + j
           const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < HC; ++i) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            const int t = c * 32 + i;
+            const int t = c0 + i;
             if ((r & 1) == 0 && t < tcount) {
               const float gt = v[i];
               const float hval = gt / (1.0f + __expf(-gt)) * up;
@@ -280,8 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (it.mt * kTileM + r < p.M) {
           const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = c * 32 + i;
+          for (int i = 0; i < HC; ++i) {
+            const int t = c0 + i;
             if (t < tcount) {
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
               float x = v[i];
@@ -299,37 +348,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
 
       if (p.splits == 1) {
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) apply(c, acc[c]);
+        apply(acc);
         continue;
       }
       // split-K: publish this split's promoted sum; the last split reduces
       float* part = p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM;
 #pragma unroll
-      for (int c = 0; c < NCH; ++c)
-#pragma unroll
-        for (int i = 0; i < CW; ++i) part[(c * 32 + i) * kTileM + r] = acc[c][i];
+      for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
       __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (et == 0) {
         const int prev = atomicAdd(&p.counters[tile_id], 1);
         *last_flag = (prev == p.splits - 1) ? 1 : 0;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (*last_flag != 0) {
         __threadfence();
         const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
+        float v[HC];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          float v[32];
+        for (int i = 0; i < HC; ++i) v[i] = 0.0f;
+        for (int s2 = 0; s2 < p.splits; ++s2) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-          for (int s2 = 0; s2 < p.splits; ++s2) {
-#pragma unroll
-            for (int i = 0; i < CW; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c * 32 + i) * kTileM);
-          }
-          apply(c, v);
+          for (int i = 0; i < HC; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c0 + i) * kTileM);
         }
+        apply(v);
         if (et == 0) p.counters[tile_id] = 0;
       }
     }

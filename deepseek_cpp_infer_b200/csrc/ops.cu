@@ -131,6 +131,50 @@ __global__ void router_logits_kernel(const float* __restrict__ x, const float* _
   if (lane == 0) logits[(int64_t)t * E + e] = acc;
 }
 
+// Large batches: a 32-token x 64-expert tile per CTA with both operands staged
+// through shared memory in 64-wide slices of D; each thread accumulates 2 x 4
+// logits in fp32 (sequential over D within a thread).
+constexpr int kRtT = 32, kRtE = 64, kRtD = 64;
+
+__global__ void __launch_bounds__(256) router_logits_tiled_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ w, int T, int D, int E,
+                                                                   float* __restrict__ logits) {
+  __shared__ float xs[kRtT][kRtD + 1];
+  __shared__ float ws[kRtE][kRtD + 1];
+  const int t0 = blockIdx.y * kRtT, e0 = blockIdx.x * kRtE;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads: experts tx+16j, tokens ty+16i
+  float acc[2][4] = {};
+  for (int d0 = 0; d0 < D; d0 += kRtD) {
+    for (int i = threadIdx.x; i < kRtT * kRtD; i += 256) {
+      const int rr = i / kRtD, cc = i % kRtD;
+      xs[rr][cc] = (t0 + rr < T && d0 + cc < D) ? x[(int64_t)(t0 + rr) * D + d0 + cc] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < kRtE * kRtD; i += 256) {
+      const int rr = i / kRtD, cc = i % kRtD;
+      ws[rr][cc] = (e0 + rr < E && d0 + cc < D) ? w[(int64_t)(e0 + rr) * D + d0 + cc] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < kRtD; ++c) {
+      const float a0 = xs[ty][c], a1 = xs[ty + 16][c];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float bv = ws[tx + 16 * j][c];
+        acc[0][j] = fmaf(a0, bv, acc[0][j]);
+        acc[1][j] = fmaf(a1, bv, acc[1][j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + ty + 16 * i, e = e0 + tx + 16 * j;
+      if (t < T && e < E) logits[(int64_t)t * E + e] = acc[i][j];
+    }
+}
+
 constexpr int kMaxExpertsPerLane = 8;  // E <= 256
 
 // Warp-wide arg-max over per-lane candidates: the largest value, ties to the
@@ -289,14 +333,18 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
 __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ counts,
                                int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
                                int32_t* __restrict__ src_pair, const float* __restrict__ weights,
-                               float* __restrict__ w_perm) {
+                               float* __restrict__ w_perm, int* __restrict__ status) {
   extern __shared__ int32_t cnt[];  // [E]
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cnt[e] = 0;
   __syncwarp();
   for (int c = 0; c < N; c += 32) {
     const int i = c + lane;
-    const int e = i < N ? ids[i] : -1 - lane;  // unique negative keys for idle lanes
+    int e = i < N ? ids[i] : -1 - lane;  // unique negative keys for idle lanes
+    if (i < N && (unsigned)e >= (unsigned)E) {  // out-of-range id: flagged, entry dropped
+      atomicExch(status, kStatusBadInput);
+      e = -1 - lane;
+    }
     const unsigned grp = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(grp & ((1u << lane) - 1u));
     const int base = e >= 0 ? cnt[e] : 0;
@@ -325,6 +373,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
   if (lane == 0) offsets[E] = carry;
   __syncwarp();
   for (int i = lane; i < N; i += 32) {
+    if ((unsigned)ids[i] >= (unsigned)E) continue;
     const int d = offsets[ids[i]] + dest[i];
     dest[i] = d;
     src_pair[d] = i;
@@ -339,6 +388,97 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)(src[p] / k) * ldx);
   uint4* d = reinterpret_cast<uint4*>(out + (int64_t)p * D);
   for (int i = threadIdx.x; i < D / 8; i += blockDim.x) d[i] = s[i];
+}
+
+// Multi-block permute for large T*k, with the same result as permute_kernel:
+// entries of one expert keep their input order.  Entries are cut into chunks
+// of kPermChunk; pass 1 counts each chunk's experts, pass 2 turns the counts
+// into per-chunk start positions (expert offset + entries of that expert in
+// earlier chunks), pass 3 walks each chunk in order with one warp and ranks
+// equal experts with match_any.
+constexpr int kPermChunk = 1024;
+constexpr int kPermSingleWarpMax = 4096;
+
+__global__ void permute_count_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ hist,
+                                     int* __restrict__ status) {
+  extern __shared__ int32_t h[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int base = blockIdx.x * kPermChunk;
+  for (int i = threadIdx.x; i < kPermChunk && base + i < N; i += blockDim.x) {
+    const int e = ids[base + i];
+    if ((unsigned)e < (unsigned)E) atomicAdd(&h[e], 1);
+    else atomicExch(status, kStatusBadInput);  // out-of-range id: flagged, entry dropped
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(int64_t)blockIdx.x * E + e] = h[e];
+}
+
+__global__ void permute_scan_kernel(int32_t* __restrict__ hist, int chunks, int E, int32_t* __restrict__ counts,
+                                    int32_t* __restrict__ offsets) {
+  extern __shared__ int32_t tot[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int v = 0;
+    for (int c = 0; c < chunks; ++c) v += hist[(int64_t)c * E + e];
+    tot[e] = v;
+    counts[e] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // exclusive scan of the totals over experts, 32 at a time
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int v = e < E ? tot[e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (e < E) tot[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) offsets[E] = carry;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = tot[e];
+    offsets[e] = run;
+    for (int c = 0; c < chunks; ++c) {
+      const int v = hist[(int64_t)c * E + e];
+      hist[(int64_t)c * E + e] = run;
+      run += v;
+    }
+  }
+}
+
+__global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, int E, const int32_t* __restrict__ hist,
+                                       int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
+                                       const float* __restrict__ weights, float* __restrict__ w_perm) {
+  extern __shared__ int32_t cur[];
+  const int lane = threadIdx.x;
+  for (int e = lane; e < E; e += 32) cur[e] = hist[(int64_t)blockIdx.x * E + e];
+  __syncwarp();
+  const int base = blockIdx.x * kPermChunk;
+  const int end = min(N, base + kPermChunk);
+  for (int c = base; c < end; c += 32) {
+    const int i = c + lane;
+    int e = i < end ? ids[i] : -1 - lane;
+    if ((unsigned)e >= (unsigned)E) e = -1 - lane;
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(grp & ((1u << lane) - 1u));
+    const int pos = e >= 0 ? cur[e] + rank : 0;
+    __syncwarp();
+    if (e >= 0) {
+      dest[i] = pos;
+      src_pair[pos] = i;
+      if (w_perm != nullptr) w_perm[pos] = weights[i];
+    }
+    if (e >= 0 && rank == 0) cur[e] += __popc(grp);
+    __syncwarp();
+  }
 }
 
 // h[t] += (y[dest[t*k]] + ... + y[dest[t*k+k-1]]) + shared[t]: the order of
@@ -425,6 +565,11 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, co
 
 int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits) {
   const int warps = T * E;
+  if (T > 64) {
+    const dim3 grid((E + kRtE - 1) / kRtE, (T + kRtT - 1) / kRtT);
+    router_logits_tiled_kernel<<<grid, 256, 0, ctx->stream>>>(x, w, T, D, E, logits);
+    return launched(ctx);
+  }
   router_logits_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(x, w, T, D, E, logits);
   return launched(ctx);
 }
@@ -438,8 +583,25 @@ int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E
 
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
                 int32_t* src_pair, const float* weights, float* w_perm) {
-  permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair, weights,
-                                                               w_perm);
+  if (N <= kPermSingleWarpMax) {
+    permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair, weights,
+                                                                 w_perm, ctx->d_status);
+    return launched(ctx);
+  }
+  // large batches: per-chunk histograms, one scan, stable per-chunk scatter
+  const int chunks = (N + kPermChunk - 1) / kPermChunk;
+  int rc = ensure_buffer(ctx, &ctx->perm, &ctx->perm_bytes, (size_t)chunks * E * sizeof(int32_t), 64 << 10,
+                         "permute histogram");
+  if (rc != DSB_OK) return rc;
+  int32_t* hist = static_cast<int32_t*>(ctx->perm);
+  const size_t sh = (size_t)E * sizeof(int32_t);
+  permute_count_kernel<<<chunks, 256, sh, ctx->stream>>>(ids, N, E, hist, ctx->d_status);
+  rc = launched(ctx);
+  if (rc != DSB_OK) return rc;
+  permute_scan_kernel<<<1, 1024, sh, ctx->stream>>>(hist, chunks, E, counts, offsets);
+  rc = launched(ctx);
+  if (rc != DSB_OK) return rc;
+  permute_scatter_kernel<<<chunks, 32, sh, ctx->stream>>>(ids, N, E, hist, dest, src_pair, weights, w_perm);
   return launched(ctx);
 }
 

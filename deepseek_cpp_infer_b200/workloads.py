@@ -151,3 +151,53 @@ def model_tensors(cfg: dict, seed: int = 0, std: float = 0.02) -> dict:
 def tiny_prompt(seed: int = 0, n: int = 32, vocab: int = 4096) -> np.ndarray:
     """32 uniform token ids for the tiny-model generate workload."""
     return np.random.default_rng(seed + 7).integers(0, vocab, n).astype(np.int32)
+
+
+# DeepSeek-V3 MoE layer (one layer of the 671B model): 256 routed experts top-8
+# by sigmoid + bias over 8 groups (top-4 groups), 1 shared expert, FP8 weights.
+V3_MOE = dict(hidden_size=7168, moe_intermediate_size=2048, n_routed_experts=256, n_shared_experts=1,
+              num_experts_per_tok=8, n_group=8, topk_group=4, routed_scaling_factor=2.5, norm_topk_prob=1)
+
+
+class MoeFp8Weights:
+    """Random FP8 expert weights of one MoE layer in dsb_moe_ffn_fp8 layout.
+
+    Each of the G = E + n_shared groups gets gate/up [I, D] and down [D, I]
+    ~ N(0, std) (fp32, seeded torch generator on the device), quantised per
+    128x128 block by dsb_quant_weight_128x128; gate and up rows are then
+    interleaved and their scales arranged per 128-row tile (scale_rows 2).
+    With keep_separate the per-matrix e4m3 codes and scales stay available
+    for the oracle (small configurations only)."""
+
+    def __init__(self, ctx, E, n_shared, D, I, seed=2, std=0.02, keep_separate=False):
+        import torch
+
+        G = E + n_shared
+        self.E, self.n_shared, self.D, self.I = E, n_shared, D, I
+        self.gate_up = torch.empty(G, 2 * I, D, dtype=torch.uint8, device="cuda")
+        self.gate_up_scale = torch.empty(G, 2 * I // 128, 2, D // 128, dtype=torch.float32, device="cuda")
+        self.down = torch.empty(G, D, I, dtype=torch.uint8, device="cuda")
+        self.down_scale = torch.empty(G, D // 128, I // 128, dtype=torch.float32, device="cuda")
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        rows = torch.arange(2 * I // 128, device="cuda") * 64 // 128  # scale row of tile j's gate/up rows
+        sep = [] if keep_separate else None
+        qg = torch.empty(I, D, dtype=torch.uint8, device="cuda")
+        qu = torch.empty_like(qg)
+        sg = torch.empty(I // 128, D // 128, dtype=torch.float32, device="cuda")
+        su = torch.empty_like(sg)
+        for g in range(G):
+            ctx.quant_weight(torch.randn(I, D, generator=gen, device="cuda") * std, qg, sg)
+            ctx.quant_weight(torch.randn(I, D, generator=gen, device="cuda") * std, qu, su)
+            ctx.quant_weight(torch.randn(D, I, generator=gen, device="cuda") * std, self.down[g], self.down_scale[g])
+            self.gate_up[g] = torch.stack([qg, qu], 1).reshape(2 * I, D)
+            self.gate_up_scale[g] = torch.stack([sg[rows], su[rows]], 1)
+            if sep is not None:
+                sep.append((qg.clone(), sg.clone(), qu.clone(), su.clone()))
+        if sep is not None:
+            cat = lambda i: np.ascontiguousarray(torch.stack([s[i] for s in sep]).cpu().numpy())  # noqa: E731
+            self.gate_q, self.gate_s, self.up_q, self.up_s = cat(0), cat(1), cat(2), cat(3)
+            self.down_q = np.ascontiguousarray(self.down.cpu().numpy())
+            self.down_s = np.ascontiguousarray(self.down_scale.cpu().numpy())
+
+    def bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.gate_up, self.gate_up_scale, self.down, self.down_scale))

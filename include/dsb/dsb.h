@@ -271,6 +271,33 @@ typedef struct dsb_linear_fp8_args {
 
 DSB_API int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* args);
 
+/* One MoE layer's experts in block-scaled FP8, for routed picks (ids, weights
+ * from dsb_moe_route, [T, k]) plus n_shared shared experts stacked after the
+ * E routed ones (groups E .. E+n_shared-1, weight 1 for every token):
+ *   h[t] += sum_j weights[t,j] * expert_{ids[t,j]}(x[t]) + sum_s shared_s(x[t])
+ * summed in that order (moe_step, src/models/deepseek/ops.cpp:133-145).
+ * expert(x) = down(silu(gate x) * up x): x is quantised per token and 128
+ * columns, gate|up run as one grouped GEMM with the SiLU epilogue (bf16 out),
+ * that is quantised again and the down GEMM scales each row by its routing
+ * weight.  Weights over G = E + n_shared groups:
+ *   gate_up       e4m3 [G, 2I, D], rows interleaved (2f gate f, 2f+1 up f)
+ *   gate_up_scale fp32 [G, 2I/128, 2, D/128] (dsb_linear_fp8 scale_rows 2)
+ *   down          e4m3 [G, D, I]
+ *   down_scale    fp32 [G, D/128, I/128]
+ * x bf16 [T, D] (row pitch ldx), h fp32 [T, D].  D and I multiples of 128.
+ * Scratch comes from the context.  Replaces moe_to_slot's expert loop
+ * (src/models/deepseek/cuda_backend.cpp:836-883) for FP8 checkpoints. */
+typedef struct dsb_moe_fp8_layer {
+  const void* gate_up;
+  const float* gate_up_scale;
+  const void* down;
+  const float* down_scale;
+  int E, n_shared, D, I;
+} dsb_moe_fp8_layer;
+
+DSB_API int dsb_moe_ffn_fp8(dsb_ctx* ctx, const dsb_moe_fp8_layer* layer, const void* x, int64_t ldx, int T, int k,
+                            const int32_t* ids, const float* weights, float* h);
+
 /* ---------------------------------------------------------------- row ops */
 
 /* y = x / sqrt(mean(x^2) + eps) * w per row, written as bf16 (y_bf16) and/or

@@ -26,7 +26,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import f32p, i32p, oracle, p
+from . import f32p, i32p, oracle, p, u8p, u16p
 
 
 def _f32(a):
@@ -122,3 +122,50 @@ def forward(cfg: dict, tensors: dict, seq, swaps=()):
         orc.orc_linear_f32(p(W["lm_head.weight"], f32p), p(_f32(hn[t]), f32p), D, p(logits[t], f32p),
                            logits.shape[1])
     return logits, margins
+
+
+def _bf16_round(a):
+    """fp32 -> bf16 (round to nearest even) -> fp32."""
+    a = _f32(a)
+    u = np.zeros(a.shape, np.uint16)
+    out = np.zeros(a.shape, np.float32)
+    oracle().orc_f32_to_bf16_n(p(a, f32p), a.size, p(u, u16p))
+    oracle().orc_bf16_to_f32_n(p(u, u16p), a.size, p(out, f32p))
+    return out
+
+
+def moe_fp8(x, ids, weights, gate_q, gate_s, up_q, up_s, down_q, down_s):
+    """moe_step (src/models/deepseek/ops.cpp:133-145) with block-scaled FP8
+    expert linears, per token: x quantised per 128 columns, gate/up through
+    orc_fp8_linear, silu(gate) * up in fp32 rounded to the bf16 activation,
+    that quantised again, the down projection, then out += w * expert(x) over
+    the picks in order.
+
+    x fp32 [T, D]; ids int32 / weights fp32 [T, kk] (shared experts included
+    as picks of weight 1); gate_q/up_q uint8 [G, I, D] with scales
+    [G, I/128, D/128]; down_q uint8 [G, D, I] with [G, D/128, I/128].
+    Returns the fp32 [T, D] expert sum (without the residual)."""
+    orc = oracle()
+    T, D = x.shape
+    I = gate_q.shape[1]
+    out = np.zeros((T, D), np.float32)
+    xq = np.zeros((1, D), np.uint8)
+    xs = np.zeros((1, D // 128), np.float32)
+    mq = np.zeros((1, I), np.uint8)
+    ms = np.zeros((1, I // 128), np.float32)
+    for t in range(T):
+        orc.orc_quant_act_1x128(p(_f32(x[t : t + 1]), f32p), 1, D, p(xq, u8p), p(xs, f32p))
+        acc = np.zeros(D, np.float32)
+        for e, wt in zip(ids[t], weights[t]):
+            g = np.zeros(I, np.float32)
+            u = np.zeros(I, np.float32)
+            orc.orc_fp8_linear(p(gate_q[e], u8p), p(gate_s[e], f32p), p(xq, u8p), p(xs, f32p), 1, I, D, p(g, f32p))
+            orc.orc_fp8_linear(p(up_q[e], u8p), p(up_s[e], f32p), p(xq, u8p), p(xs, f32p), 1, I, D, p(u, f32p))
+            # the activation between the two GEMMs is bf16 (then e4m3 per 1x128)
+            mid = _bf16_round(_f32(g / (np.float32(1) + np.exp(-g)) * u))
+            orc.orc_quant_act_1x128(p(mid.reshape(1, I), f32p), 1, I, p(mq, u8p), p(ms, f32p))
+            y = np.zeros(D, np.float32)
+            orc.orc_fp8_linear(p(down_q[e], u8p), p(down_s[e], f32p), p(mq, u8p), p(ms, f32p), 1, D, I, p(y, f32p))
+            acc = _f32(acc + np.float32(wt) * y)
+        out[t] = acc
+    return out

@@ -35,5 +35,7 @@ def gpu_ctx():
     import deepseek_cpp_infer_b200 as dsb
 
     ctx = dsb.Context(0)
+    # torch makes the inputs on its default stream: run the context there too
+    ctx.use_legacy_stream()
     yield ctx
     ctx.close()

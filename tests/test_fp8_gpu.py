@@ -176,7 +176,7 @@ def test_linear_fp8_grouped_experts_rowscale(gpu_ctx):
 
     lut = e4m3_lut()
     E, M, K = 8, 256, 1024
-    counts = [3, 0, 17, 1, 0, 140, 2, 9]
+    counts = [3, 0, 17, 1, 0, 140, 2, 300]
     offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
     T = int(offs[-1])
     wq, ws = zip(*(quant_w(gpu_ctx, normal(M, K, scale=0.05, seed=20 + e)) for e in range(E)))
@@ -198,7 +198,7 @@ def test_linear_fp8_grouped_experts_rowscale(gpu_ctx):
     assert max_rel(y, ref) <= TOL32
 
 
-@pytest.mark.parametrize("T", [4, 64])
+@pytest.mark.parametrize("T", [4, 64, 200])
 def test_linear_fp8_silu_gate_interleaved(gpu_ctx, T):
     """gate and up quantised as separate checkpoint matrices, rows interleaved
     (2f gate, 2f+1 up) with scale_rows 2."""

@@ -72,11 +72,12 @@ def test_kv_norm_rope_append(gpu_ctx, H, nope, R, P):
     assert np.abs(qr - ref_qr).max() <= 2 ** -7 * np.abs(ref_qr).max()
 
 
-def test_router_logits(gpu_ctx):
+@pytest.mark.parametrize("T,D,E", [(33, 2048, 64), (300, 7168, 256), (65, 512, 16)])
+def test_router_logits(gpu_ctx, T, D, E):
+    """fp32 router logits (warp-per-dot kernel up to 64 tokens, tiled above)."""
     import torch
 
     rng = np.random.default_rng(4)
-    T, D, E = 33, 2048, 64
     x = rng.standard_normal((T, D)).astype(np.float32)
     w = (rng.standard_normal((E, D)) * 0.02).astype(np.float32)
     lg = torch.empty(T, E, device="cuda")

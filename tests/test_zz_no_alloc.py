@@ -32,6 +32,7 @@ def run_both(ctx, case):
     ctx.sync()
     stream = torch.cuda.Stream()
     out = torch.full_like(ref, float("nan"))
+    stream.wait_stream(torch.cuda.current_stream())  # inputs and `out` were written on the default stream
     rc = dsb.mla_decode_noalloc(stream.cuda_stream, case.q_lat, case.q_rope, case.cache, case.block_table,
                                 case.seq_lens, case.scale, out)
     assert rc == dsb.DSB_OK, rc
