@@ -729,6 +729,8 @@ def run_moe_fp8(args):
     from deepseek_cpp_infer_b200.workloads import V3_MOE, MoeFp8Weights
 
     cfg = dict(V3_MOE)
+    if args.experts:
+        cfg["n_routed_experts"] = args.experts
     torch.cuda.set_device(0)
     ctx = dsb.Context(0)
     stream = torch.cuda.Stream()
@@ -822,6 +824,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
     ap.add_argument("--layers", type=int, default=0, help="model layers (0 = the configuration's 27)")
+    ap.add_argument("--experts", type=int, default=0,
+                    help="moe-fp8: routed experts (0 = 256; fewer for small profiling captures)")
     args = ap.parse_args()
     if args.workload == "expert-gemm":
         args.batch = args.batch or 32

@@ -94,15 +94,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 
 // Bounded wait.  Returns false when the wait limit passes or another thread of
 // the CTA has raised *abort; the caller then abandons its loop.
+// The clock is read only every 1024 unsuccessful polls (the first read
+// starts the limit), so short waits cost nothing but the polls themselves.
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  uint64_t t0 = 0;
   for (uint32_t it = 1;; ++it) {
     if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if ((it & 1023u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > kWaitLimitNs) return false;
     }
   }
 }

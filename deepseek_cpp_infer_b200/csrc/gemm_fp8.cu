@@ -22,9 +22,9 @@
 // linear GEMVs of moe_to_slot / linear_to_slot (src/models/deepseek/
 // cuda_backend.cpp:782-883) for block-scaled FP8 checkpoints.
 //
-// Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-9
-// promotion + epilogue (warp w owns TMEM lanes 32*(w%4)..+31 and half of the
-// token columns).
+// Roles (192 threads, 320 from 64 tokens up): warp 0 TMA producer, warp 1 MMA
+// issuer, the other warps promotion + epilogue (warp w owns TMEM lanes
+// 32*(w%4)..+31 and all, or from 64 tokens up half, of the token columns).
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -40,7 +40,6 @@ namespace {
 
 constexpr int kBK = 128;      // K bytes (e4m3 elements) per stage = one scale block
 constexpr int kTileM = 128;   // weight rows per tile (MMA M)
-constexpr int kThreads = 320;
 
 struct Fp8Params {
   int T, M, K, G;
@@ -68,12 +67,16 @@ struct Fp8Shape {
   static constexpr int B_BYTES = NT * kBK;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int NS = (196 * 1024) / STAGE;
+  static constexpr int NBUF = 4;  // TMEM partial buffers: the MMAs run up to 3 K blocks ahead
+  static constexpr int CG = NT < 64 ? 1 : 2;        // token-column groups of the epilogue
+  static constexpr int EPI = 128 * CG;              // epilogue threads: 4 lane quarters x CG
+  static constexpr int THREADS = 64 + EPI;
   static constexpr int OFF_BAR = NS * STAGE;
-  static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
-  static constexpr int OFF_SX = OFF_MISC + 64;  // [8 warps][2 buffers][2 row parities][NT/2] scales
-  static constexpr int SMEM = OFF_SX + 8 * 4 * (NT / 2) * 4 + 1024;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 2) * 8;
+  static constexpr int OFF_SX = OFF_MISC + 64;  // [epilogue warps][2 buffers][2 row parities][NT/CG] scales
+  static constexpr int SMEM = OFF_SX + (EPI / 32) * 4 * (NT / CG) * 4 + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
-  static constexpr uint32_t TCOLS = 2 * TC;
+  static constexpr uint32_t TCOLS = NBUF * TC;       // <= 512
   static_assert(STAGE % 1024 == 0, "stage alignment");
   static_assert(SMEM <= 232448, "shared memory");
 };
@@ -109,7 +112,7 @@ struct UnitIter {
 };
 
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                     Fp8Params p, int* status) {
   using S = Fp8Shape<NT>;
@@ -117,9 +120,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   uint64_t* empty = full + S::NS;
-  uint64_t* part_full = empty + S::NS;  // [2] partial buffer written by one K block's MMAs
-  uint64_t* part_empty = part_full + 2; // [2] partial buffer promoted by the epilogue
-  uint64_t* drain = part_full + 4;
+  uint64_t* part_full = empty + S::NS;        // [NBUF] partial buffer written by one K block's MMAs
+  uint64_t* part_empty = part_full + S::NBUF; // [NBUF] partial buffer promoted by the epilogue
+  uint64_t* drain = part_empty + S::NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
   volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
@@ -134,9 +137,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < S::NBUF; ++b) {
       mbar_init(&part_full[b], 1);
-      mbar_init(&part_empty[b], 256);
+      mbar_init(&part_empty[b], S::EPI);
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -194,8 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && it.next()) {
         const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
         for (int kb = kb0; kb < kb1; ++kb, ++q, ++pk) {
-          const int s = q % S::NS, b = pk & 1;
-          if (pk >= 2 && !mbar_wait(&part_empty[b], ((pk >> 1) - 1) & 1, abort)) { ok = false; break; }
+          const int s = q % S::NS, b = pk % S::NBUF;
+          if (pk >= S::NBUF && !mbar_wait(&part_empty[b], ((pk / S::NBUF) - 1) & 1, abort)) { ok = false; break; }
           if (!mbar_wait(&full[s], (q / S::NS) & 1, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d = tmem + b * S::TC;
@@ -217,14 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------- promotion + epilogue
     // 8 warps: warp w reads TMEM lanes 32*(w%4)..+31 (weight rows of the
     // tile) and token columns [h*HC, (h+1)*HC), h = (w-2)/4.
-    constexpr int HC = NT / 2;             // token columns per thread (8..64)
+    constexpr int HC = NT / S::CG;         // token columns per thread (16, 32 or 64)
     constexpr int LW = HC < 32 ? HC : 32;  // columns per tcgen05.ld
     constexpr int NL = HC / LW;            // loads per K block
     constexpr int PER = (HC + 31) / 32;    // token scales loaded per lane
     const uint32_t qtr = warp & 3;
     const int c0 = (int)((warp - 2) >> 2) * HC;  // this thread's first token column
     const int r = (int)(qtr * 32 + lane);        // weight row within the tile (parity = lane parity)
-    const int et = threadIdx.x - 64;             // 0..255
+    const int et = threadIdx.x - 64;             // 0..EPI-1
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     // this warp's scale vectors: [2 buffers][row parity][HC], sw(row) * sx[t] of one K block
     float* sxw = sx_smem + (warp - 2) * 4 * HC;
@@ -270,16 +273,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_sx(pk & 1);
       __syncwarp();
       for (int kb = kb0; kb < kb1; ++kb, ++pk) {
-        const int b = pk & 1;
+        const int b = pk % S::NBUF, sb = pk & 1;  // TMEM partial buffer, scale buffer
         if (kb + 1 < kb1) load_sx(kb + 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk >> 1) & 1, abort))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk / S::NBUF) & 1, abort))) {
           raise_abort(abort, status, kStatusTimeout);
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t taddr = tmem + ((qtr * 32) << 16) + b * S::TC + c0;
-        const float4* s4 = reinterpret_cast<const float4*>(sxw + (b * 2 + (int)(lane & 1)) * HC);
+        const float4* s4 = reinterpret_cast<const float4*>(sxw + (sb * 2 + (int)(lane & 1)) * HC);
 #pragma unroll
         for (int l = 0; l < NL; ++l) {
           uint32_t raw[LW];
@@ -304,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (kb + 1 < kb1) {
           __syncwarp();  // every lane is done with the buffer written next
-          store_sx(b ^ 1);
+          store_sx(sb ^ 1);
           __syncwarp();
         }
       }
@@ -356,12 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
       __threadfence();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      named_bar_sync(1, S::EPI);
       if (et == 0) {
         const int prev = atomicAdd(&p.counters[tile_id], 1);
         *last_flag = (prev == p.splits - 1) ? 1 : 0;
       }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      named_bar_sync(1, S::EPI);
       if (*last_flag != 0) {
         __threadfence();
         const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
@@ -434,7 +437,7 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_til
     attr_set = true;
   }
   const int grid = std::min(p.n_tiles, ctx->sm_count);
-  kern<<<grid, kThreads, S::SMEM, ctx->stream>>>(map_w, map_x, p, ctx->d_status);
+  kern<<<grid, S::THREADS, S::SMEM, ctx->stream>>>(map_w, map_x, p, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   ctx->stats.gemm_calls++;
