@@ -123,6 +123,16 @@ _PROTOS = [
     ("dsb_quant_act_1x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _vp, _ci, _ci, _ci, _vp, _i64, _vp, _i64]),
     ("dsb_quant_weight_128x128", ctypes.c_int, [_vp, _vp, _ci, _i64, _i64, _vp, _vp]),
     ("dsb_linear_fp8", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(LinearFp8Args)]),
+    ("dsb_ep_create", ctypes.c_int, [_vp, _ci, _ci, _ci, _ci, _ci, _ci, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_ep_window_handle", ctypes.c_int, [_vp, _vp]),
+    ("dsb_ep_connect", ctypes.c_int, [_vp, _vp]),
+    ("dsb_ep_info", ctypes.c_int, [_vp, ctypes.POINTER(_ci), ctypes.POINTER(_ci), ctypes.POINTER(ctypes.c_uint64)]),
+    ("dsb_ep_dispatch", ctypes.c_int,
+     [_vp, _vp, _i64, _ci, _vp, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_ep_combine", ctypes.c_int, [_vp, _vp, _i64, _ci, _vp, _vp, _ci, _vp]),
+    ("dsb_ep_destroy", ctypes.c_int, [_vp]),
+    ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
+    ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
     ("dsb_moe_ffn_fp8", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(MoeFp8Layer), _vp, _i64, _ci, _ci, _vp, _vp, _vp]),
     ("dsb_rmsnorm", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _cf, _vp, _i64, _vp, _i64]),
@@ -434,6 +444,10 @@ class Model:
         shape = (ctypes.c_int64 * a.ndim)(*a.shape)
         self.ctx._check(self.ctx._l.dsb_model_set_tensor(self.h, name.encode(), dt, shape, a.ndim, a.ctypes.data))
 
+    def set_ep(self, ep: "EP"):
+        """Keep only the routed experts of `ep`'s rank; MoE layers exchange through the group."""
+        self.ctx._check(self.ctx._l.dsb_model_set_ep(self.h, ep.h))
+
     def init_random(self, seed: int, stddev: float = 0.02):
         self.ctx._check(self.ctx._l.dsb_model_init_random(self.h, seed, stddev))
 
@@ -455,6 +469,79 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+class EP:
+    """An expert-parallel group member (dsb_ep): rank `rank` of `world`, owning
+    experts [rank*E_local, (rank+1)*E_local).  Connect with every rank's
+    window handle (bytes, rank order) before the first dispatch."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, ctx: Context, rank: int, world: int, n_experts: int, hidden: int, top_k: int,
+                 max_tokens: int):
+        self.ctx, self._l = ctx, ctx._l
+        h = ctypes.c_void_p()
+        ctx._check(self._l.dsb_ep_create(ctx.h, rank, world, n_experts, hidden, top_k, max_tokens, ctypes.byref(h)))
+        self.h = h
+        self.rank, self.world, self.hidden, self.top_k = rank, world, hidden, top_k
+        el, cap, nb = _ci(), _ci(), ctypes.c_uint64()
+        ctx._check(self._l.dsb_ep_info(self.h, ctypes.byref(el), ctypes.byref(cap), ctypes.byref(nb)))
+        self.E_local, self.capacity, self.window_bytes = el.value, cap.value, nb.value
+
+    def window_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        self.ctx._check(self._l.dsb_ep_window_handle(self.h, buf))
+        return buf.raw
+
+    def connect(self, handles):
+        blob = b"".join(handles)
+        assert len(blob) == self.world * self.HANDLE_BYTES
+        self.ctx._check(self._l.dsb_ep_connect(self.h, ctypes.create_string_buffer(blob, len(blob))))
+
+    def dispatch(self, x, ids):
+        """x bf16 [T, hidden], ids int32 [T, top_k] -> (recv_x, recv_offsets) torch views of the group's buffers."""
+        import torch
+
+        rx, ro = ctypes.c_void_p(), ctypes.c_void_p()
+        self.ctx._check(self._l.dsb_ep_dispatch(self.h, _ptr(x), x.stride(0), x.shape[0], _ptr(ids), ctypes.byref(rx),
+                                                ctypes.byref(ro)))
+        recv = _device_view(rx.value, (self.capacity, self.hidden), torch.bfloat16, x.device)
+        offs = _device_view(ro.value, (self.E_local + 1,), torch.int32, x.device)
+        return recv, offs
+
+    def combine(self, y, weights, h, shared=None):
+        n_shared = 0 if shared is None else shared.shape[0]
+        self.ctx._check(self._l.dsb_ep_combine(self.h, _ptr(y), y.stride(0), h.shape[0], _ptr(weights), _ptr(shared),
+                                               n_shared, _ptr(h)))
+
+    def close(self):
+        if self.h:
+            self._l.dsb_ep_destroy(self.h)
+            self.h = None
+
+
+def _device_view(ptr: int, shape, dtype, device):
+    """A torch tensor over device memory owned by libdsb (no copy, no ownership)."""
+    import torch
+
+    class _Holder:
+        pass
+
+    hold = _Holder()
+    n = 1
+    for d in shape:
+        n *= d
+    itemsize = torch.empty((), dtype=dtype).element_size()
+    hold.__cuda_array_interface__ = {
+        "shape": tuple(shape), "typestr": {torch.bfloat16: "<V2", torch.int32: "<i4", torch.float32: "<f4"}[dtype],
+        "data": (ptr, False), "version": 3, "strides": None,
+    }
+    if dtype == torch.bfloat16:
+        hold.__cuda_array_interface__["typestr"] = "<i2"
+        return torch.as_tensor(hold, device=device).view(torch.bfloat16)
+    assert n * itemsize > 0
+    return torch.as_tensor(hold, device=device)
 
 
 class KVCache:

@@ -78,6 +78,10 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, co
                         const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
                         float theta, void* cache, void* q_rope);
 int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits);
+// Sizes of an expert-parallel group (ep.cu); any output may be null.
+int ep_params(const dsb_ep* ep, int* rank, int* world, int* n_experts, int* top_k, int* hidden, int* max_tokens,
+              int* E_local);
+
 // e4m3 per-token 1x128 quantisation (quant_fp8.cu); arguments as
 // dsb_quant_act_1x128, unchecked.
 int quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const int32_t* src_rows, int k, int T,

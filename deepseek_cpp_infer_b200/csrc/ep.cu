@@ -1,0 +1,416 @@
+// Expert parallelism over peer memory: token dispatch to the ranks that own
+// the picked experts, and the return of the expert outputs, as kernels that
+// write straight into the other GPUs' memory over NVLink (CUDA IPC windows),
+// with no collective library on the data path.
+//
+// Expert e lives on rank e / E_local.  Every rank keeps its own tokens (data
+// parallel attention) and exchanges, per MoE layer:
+//   1. counts   each rank sends its [world][E_local] pick counts to every rank
+//   2. rows     each pick's bf16 token row goes to the owner's receive buffer,
+//               grouped by local expert, sources in rank order, picks of one
+//               source in pick order (so an expert sees the same row order as
+//               the single-GPU permutation restricted to it)
+//   3. return   each received row's expert output goes back into the home
+//               rank's inbox slot of that pick; the home rank sums
+//               w[t,j] * out[t,j] in pick order, then its shared experts
+//               (moe_step's order, src/models/deepseek/ops.cpp:133-145).
+// Every step publishes with a flag holding the call's epoch; a receiver waits
+// (bounded) until all sources show the epoch.  The windows are reused across
+// calls, which is safe because each rank's next dispatch needs every peer's
+// return of the previous call.
+//
+// Window layout (identical on every rank):
+//   counts [world src][world dst][E_local] int32
+//   flags  [3 phases][world src] uint32 (counts, rows, return)
+//   meta   [cap] int32  (source rank << 24 | source pick index) per received row
+//   recv   [cap][D] bf16 received rows, cap = world * T_max * k
+//   inbox  [T_max * k][D] fp32 returned outputs of this rank's picks
+// Replaces nothing in the reference (single GPU, B = 1); the exchange model
+// is a host permutation: token -> rank = expert / (E / world).
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "dsb_internal.h"
+#include "dsb_ptx.cuh"
+
+namespace dsb {
+namespace {
+
+constexpr int kMaxWorld = 8;
+
+struct EpPeers {
+  uint8_t* win[kMaxWorld];  // every rank's window, mapped here (win[rank] = own)
+};
+
+struct EpLayout {
+  int world, rank, E_local, D, k, T_max, cap;
+  size_t off_counts, off_flags, off_meta, off_recv, off_inbox, bytes;
+};
+
+EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) {
+  EpLayout L{};
+  L.world = world;
+  L.rank = rank;
+  L.E_local = E_local;
+  L.D = D;
+  L.k = k;
+  L.T_max = T_max;
+  L.cap = world * T_max * k;
+  auto a = [](size_t v) { return (v + 255) & ~size_t(255); };
+  size_t o = 0;
+  L.off_counts = o;
+  o += a((size_t)world * world * E_local * 4);
+  L.off_flags = o;
+  o += a((size_t)3 * world * 4);
+  L.off_meta = o;
+  o += a((size_t)L.cap * 4);
+  L.off_recv = o;
+  o += a((size_t)L.cap * D * 2);
+  L.off_inbox = o;
+  o += a((size_t)T_max * k * D * 4);
+  L.bytes = o;
+  return L;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until flags[s] == epoch for every source s (one thread).
+__device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    bool all = true;
+    for (int s = 0; s < world; ++s) all &= ld_acquire_sys(flags + s) == epoch;
+    if (all) return true;
+    if ((it & 255u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// 1. One warp: stable slot of every pick among this rank's picks of the same
+// expert, this rank's [world][E_local] counts written into every window, and
+// the counts flag raised there.
+__global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, int E, EpLayout L, EpPeers peers,
+                                int32_t* __restrict__ slot, uint32_t epoch, int* status) {
+  __shared__ int32_t cnt[256];
+  const int lane = threadIdx.x;
+  for (int e = lane; e < E; e += 32) cnt[e] = 0;
+  __syncwarp();
+  for (int c = 0; c < n_picks; c += 32) {
+    const int i = c + lane;
+    int e = i < n_picks ? ids[i] : -1 - lane;
+    if (i < n_picks && (unsigned)e >= (unsigned)E) {
+      atomicExch(status, kStatusBadInput);
+      e = -1 - lane;
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int r = __popc(grp & ((1u << lane) - 1u));
+    const int base = e >= 0 ? cnt[e] : 0;
+    __syncwarp();
+    if (i < n_picks) slot[i] = e >= 0 ? base + r : -1;
+    if (e >= 0 && r == 0) cnt[e] = base + __popc(grp);
+    __syncwarp();
+  }
+  // this rank's row of the count matrix, into every window
+  const int row = L.world * L.E_local;
+  for (int p = 0; p < L.world; ++p) {
+    int32_t* dst = reinterpret_cast<int32_t*>(peers.win[p] + L.off_counts) + (size_t)L.rank * row;
+    for (int i = lane; i < row; i += 32) dst[i] = cnt[i];
+  }
+  __threadfence_system();
+  __syncwarp();
+  if (lane < L.world)
+    st_release_sys(reinterpret_cast<uint32_t*>(peers.win[lane] + L.off_flags) + 0 * L.world + L.rank, epoch);
+}
+
+// 2. Rows to their owners.  Every CTA waits for all counts, derives this
+// rank's write offsets in each owner's buffer (and, CTA 0, this rank's own
+// receive offsets for the expert GEMMs); warps copy one pick's row each.  The
+// last CTA to finish raises the rows flag in every window.
+__global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ ids,
+                                   const int32_t* __restrict__ slot, int n_picks, EpLayout L, EpPeers peers,
+                                   int32_t* __restrict__ recv_offsets, int* __restrict__ ticket, uint32_t epoch,
+                                   int* status) {
+  __shared__ int32_t my_off[kMaxWorld * 64];  // [dst][el]: this rank's first row in dst's buffer
+  __shared__ int ok_s;
+  const uint8_t* win = peers.win[L.rank];
+  if (threadIdx.x == 0) {
+    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 0 * L.world, L.world, epoch) ? 1 : 0;
+    if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int32_t* counts = reinterpret_cast<const int32_t*>(win + L.off_counts);  // [src][dst][el]
+  const int W = L.world, EL = L.E_local;
+  for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
+    const int dst = idx / EL, el = idx % EL;
+    int o = 0;
+    for (int e2 = 0; e2 < el; ++e2)
+      for (int s = 0; s < W; ++s) o += __ldcv(counts + ((size_t)s * W + dst) * EL + e2);
+    for (int s = 0; s < L.rank; ++s) o += __ldcv(counts + ((size_t)s * W + dst) * EL + el);
+    my_off[idx] = o;
+  }
+  if (blockIdx.x == 0) {
+    // receive offsets of this rank's experts (all sources), the GEMM's groups
+    for (int el = threadIdx.x; el <= EL; el += blockDim.x) {
+      int o = 0;
+      for (int e2 = 0; e2 < el; ++e2)
+        for (int s = 0; s < W; ++s) o += __ldcv(counts + ((size_t)s * W + L.rank) * EL + e2);
+      recv_offsets[el] = o;
+    }
+  }
+  __syncthreads();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int vec_per_row = L.D / 8;  // 16-byte vectors of bf16
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_picks; i += gridDim.x * warps) {
+    const int e = ids[i], s = slot[i];
+    if (s < 0) continue;
+    const int dst = e / EL, el = e % EL;
+    const int row = my_off[dst * EL + el] + s;
+    uint8_t* pw = peers.win[dst];
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i / L.k) * ldx);
+    uint4* out = reinterpret_cast<uint4*>(pw + L.off_recv + (size_t)row * L.D * 2);
+    for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
+    if (lane == 0) reinterpret_cast<int32_t*>(pw + L.off_meta)[row] = (L.rank << 24) | i;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(ticket, 1);
+    if (prev == (int)gridDim.x - 1) {
+      *ticket = 0;
+      __threadfence_system();
+      for (int p = 0; p < W; ++p)
+        st_release_sys(reinterpret_cast<uint32_t*>(peers.win[p] + L.off_flags) + 1 * W + L.rank, epoch);
+    }
+  }
+}
+
+// 3. Wait until every source has raised `phase` here (one thread): phase 1,
+// its rows have landed; phase 2, its returns have.
+__global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t epoch, int* status) {
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.win[L.rank] + L.off_flags) + phase * L.world;
+  if (!wait_flags(flags, L.world, epoch)) atomicCAS(status, 0, kStatusTimeout);
+}
+
+// 4. Expert outputs (fp32 [cap][D], rows in receive order) back to the home
+// ranks' inboxes; the last CTA raises the return flag in every window.
+__global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const int32_t* __restrict__ recv_offsets,
+                                 EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
+  const int n_recv = recv_offsets[L.E_local];
+  const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int vec_per_row = L.D / 4;  // 16-byte vectors of fp32
+  for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < n_recv; r += gridDim.x * warps) {
+    const int m = __ldcv(meta + r);
+    const int home = m >> 24, pick = m & 0xFFFFFF;
+    const uint4* src = reinterpret_cast<const uint4*>(y + (int64_t)r * ldy);
+    uint4* out = reinterpret_cast<uint4*>(peers.win[home] + L.off_inbox + (size_t)pick * L.D * 4);
+    for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(ticket, 1);
+    if (prev == (int)gridDim.x - 1) {
+      *ticket = 0;
+      __threadfence_system();
+      for (int p = 0; p < L.world; ++p)
+        st_release_sys(reinterpret_cast<uint32_t*>(peers.win[p] + L.off_flags) + 2 * L.world + L.rank, epoch);
+    }
+  }
+}
+
+// 5. h[t] += sum_j w[t,j] * inbox[t*k+j] (pick order) + sum_s shared[s*T + t].
+__global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLayout L, EpPeers peers,
+                                  const float* __restrict__ shared, int n_shared, float* __restrict__ h,
+                                  uint32_t epoch, int* status) {
+  __shared__ int ok_s;
+  const uint8_t* win = peers.win[L.rank];
+  if (threadIdx.x == 0) {
+    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 2 * L.world, L.world, epoch) ? 1 : 0;
+    if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const float* inbox = reinterpret_cast<const float*>(win + L.off_inbox);
+  const int t = blockIdx.x, k = L.k, D = L.D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(__ldcv(inbox + ((size_t)t * k + j) * D + i), weights[(size_t)t * k + j]));
+    for (int s = 0; s < n_shared; ++s) acc = __fadd_rn(acc, shared[((size_t)s * T + t) * D + i]);
+    h[(size_t)t * D + i] = __fadd_rn(h[(size_t)t * D + i], acc);
+  }
+}
+
+}  // namespace
+}  // namespace dsb
+
+struct dsb_ep {
+  dsb_ctx* ctx = nullptr;
+  dsb::EpLayout L{};
+  int E = 0;
+  uint8_t* win = nullptr;
+  dsb::EpPeers peers{};
+  bool connected = false;
+  bool opened[dsb::kMaxWorld] = {};
+  uint32_t epoch = 0;
+  int32_t* d_slot = nullptr;      // [T_max * k]
+  int32_t* d_recv_off = nullptr;  // [E_local + 1]
+  int* d_ticket = nullptr;        // [2]: dispatch, return
+};
+
+using namespace dsb;
+
+int dsb::ep_params(const dsb_ep* ep, int* rank, int* world, int* n_experts, int* top_k, int* hidden, int* max_tokens,
+                   int* E_local) {
+  if (rank) *rank = ep->L.rank;
+  if (world) *world = ep->L.world;
+  if (n_experts) *n_experts = ep->E;
+  if (top_k) *top_k = ep->L.k;
+  if (hidden) *hidden = ep->L.D;
+  if (max_tokens) *max_tokens = ep->L.T_max;
+  if (E_local) *E_local = ep->L.E_local;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, int hidden, int top_k,
+                             int max_tokens, dsb_ep** out) {
+  if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
+  *out = nullptr;
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || n_experts <= 0 || n_experts % world ||
+      n_experts > 256 || n_experts / world > 64 || hidden <= 0 || hidden % 8 || top_k <= 0 || max_tokens <= 0 ||
+      (int64_t)world * max_tokens * top_k >= (1 << 24))
+    return fail(ctx, DSB_EINVAL, "dsb_ep_create: bad sizes (world <= 8, E divisible by world, E/world <= 64)");
+  auto* ep = new dsb_ep();
+  ep->ctx = ctx;
+  ep->E = n_experts;
+  ep->L = make_layout(world, rank, n_experts / world, hidden, top_k, max_tokens);
+  cudaError_t e = cudaMalloc(&ep->win, ep->L.bytes);
+  if (e == cudaSuccess) e = cudaMemset(ep->win, 0, ep->L.bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->d_slot, (size_t)max_tokens * top_k * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->d_recv_off, (size_t)(ep->L.E_local + 1) * 4);
+  // zero ranges until the first dispatch (a timed-out exchange leaves them as they were)
+  if (e == cudaSuccess) e = cudaMemset(ep->d_recv_off, 0, (size_t)(ep->L.E_local + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->d_ticket, 2 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ep->d_ticket, 0, 2 * sizeof(int));
+  if (e != cudaSuccess) {
+    cudaFree(ep->win);
+    cudaFree(ep->d_slot);
+    cudaFree(ep->d_recv_off);
+    cudaFree(ep->d_ticket);
+    delete ep;
+    return fail(ctx, DSB_ENOMEM, "dsb_ep_create: %s", cudaGetErrorString(e));
+  }
+  ep->peers.win[rank] = ep->win;
+  *out = ep;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_window_handle(dsb_ep* ep, void* handle) {
+  if (ep == nullptr || handle == nullptr) return DSB_EINVAL;
+  cudaIpcMemHandle_t h;
+  DSB_CUDA_TRY(ep->ctx, cudaIpcGetMemHandle(&h, ep->win));
+  std::memcpy(handle, &h, sizeof(h));
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_connect(dsb_ep* ep, const void* handles) {
+  if (ep == nullptr || handles == nullptr) return DSB_EINVAL;
+  const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int p = 0; p < ep->L.world; ++p) {
+    if (p == ep->L.rank) continue;
+    void* ptr = nullptr;
+    DSB_CUDA_TRY(ep->ctx, cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess));
+    ep->peers.win[p] = static_cast<uint8_t*>(ptr);
+    ep->opened[p] = true;
+  }
+  ep->connected = true;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_destroy(dsb_ep* ep) {
+  if (ep == nullptr) return DSB_OK;
+  cudaStreamSynchronize(ep->ctx->stream);
+  for (int p = 0; p < ep->L.world; ++p)
+    if (ep->opened[p]) cudaIpcCloseMemHandle(ep->peers.win[p]);
+  cudaFree(ep->win);
+  cudaFree(ep->d_slot);
+  cudaFree(ep->d_recv_off);
+  cudaFree(ep->d_ticket);
+  delete ep;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_info(const dsb_ep* ep, int* E_local, int* recv_capacity, uint64_t* window_bytes) {
+  if (ep == nullptr) return DSB_EINVAL;
+  if (E_local) *E_local = ep->L.E_local;
+  if (recv_capacity) *recv_capacity = ep->L.cap;
+  if (window_bytes) *window_bytes = ep->L.bytes;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
+                               int32_t** recv_offsets) {
+  if (ep == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = ep->ctx;
+  if (!ep->connected && ep->L.world > 1) return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: dsb_ep_connect first");
+  if (x == nullptr || ids == nullptr || T < 0 || T > ep->L.T_max || ldx < ep->L.D || (ldx % 8) ||
+      (reinterpret_cast<uintptr_t>(x) & 15u))
+    return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
+  const uint32_t epoch = ++ep->epoch * 2 - 1;  // odd: dispatch, even: the return of the same call
+  const int n = T * ep->L.k;
+  ep_count_kernel<<<1, 32, 0, ctx->stream>>>(ids, n, ep->E, ep->L, ep->peers, ep->d_slot, epoch, ctx->d_status);
+  DSB_CUDA_TRY(ctx, cudaGetLastError());
+  const int blocks = std::max(1, std::min(ctx->sm_count, (n + 7) / 8));
+  ep_dispatch_kernel<<<blocks, 256, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), ldx, ids, ep->d_slot, n,
+                                                      ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch,
+                                                      ctx->d_status);
+  DSB_CUDA_TRY(ctx, cudaGetLastError());
+  ep_wait_kernel<<<1, 1, 0, ctx->stream>>>(ep->L, ep->peers, 1, epoch, ctx->d_status);
+  DSB_CUDA_TRY(ctx, cudaGetLastError());
+  ctx->stats.kernel_launches += 3;
+  if (recv_x) *recv_x = ep->win + ep->L.off_recv;
+  if (recv_offsets) *recv_offsets = ep->d_recv_off;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,
+                              const float* shared, int n_shared, float* h) {
+  if (ep == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = ep->ctx;
+  if (y == nullptr || weights == nullptr || h == nullptr || T < 0 || T > ep->L.T_max || ldy < ep->L.D ||
+      (ldy % 4) || (reinterpret_cast<uintptr_t>(y) & 15u) || n_shared < 0 || (n_shared > 0 && shared == nullptr))
+    return fail(ctx, DSB_EINVAL, "dsb_ep_combine: bad arguments");
+  if (ep->epoch == 0) return fail(ctx, DSB_EINVAL, "dsb_ep_combine: no dispatch to return");
+  const uint32_t epoch = ep->epoch * 2;
+  ep_return_kernel<<<ctx->sm_count, 256, 0, ctx->stream>>>(y, ldy, ep->d_recv_off, ep->L, ep->peers,
+                                                           ep->d_ticket + 1, epoch);
+  DSB_CUDA_TRY(ctx, cudaGetLastError());
+  if (T > 0) {
+    ep_combine_kernel<<<T, 256, 0, ctx->stream>>>(weights, T, ep->L, ep->peers, shared, n_shared, h, epoch,
+                                                  ctx->d_status);
+    DSB_CUDA_TRY(ctx, cudaGetLastError());
+  } else {
+    // no tokens here, but the next dispatch may only start once every peer has returned
+    ep_wait_kernel<<<1, 1, 0, ctx->stream>>>(ep->L, ep->peers, 2, epoch, ctx->d_status);
+    DSB_CUDA_TRY(ctx, cudaGetLastError());
+  }
+  ctx->stats.kernel_launches += 2;
+  return DSB_OK;
+}

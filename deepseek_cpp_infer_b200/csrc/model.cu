@@ -63,6 +63,9 @@ struct dsb_model {
   std::vector<void*> allocs;
   bool finalized = false;
   uint64_t weight_bytes = 0;
+  // expert parallelism: this rank holds routed experts [e_first, e_first + E_own)
+  dsb_ep* ep = nullptr;
+  int e_first = 0, E_own = 0;
 };
 
 struct dsb_kvcache {
@@ -281,7 +284,7 @@ int ensure_experts(dsb_model* m, dsb_model::Layer& L) {
   if (I <= 0 || I % 64 != 0) return fail(m->ctx, DSB_EUNSUPPORTED, "moe_intermediate_size %d must be a positive multiple of 64", I);
   L.e_inter = I;
   L.n_shared = std::max(0, c.n_shared_experts);
-  const int G = c.n_routed_experts + L.n_shared;
+  const int G = m->E_own + L.n_shared;
   int rc = dev_alloc(m, &L.e_gu, (size_t)G * 2 * I * D);
   if (rc == DSB_OK) rc = dev_alloc(m, &L.e_down, (size_t)G * D * I);
   return rc;
@@ -308,8 +311,25 @@ extern "C" int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_m
   auto* m = new dsb_model();
   m->ctx = ctx;
   m->cfg = c;
+  m->E_own = std::max(0, c.n_routed_experts);
   m->layers.resize(c.num_hidden_layers);
   *out = m;
+  return DSB_OK;
+}
+
+extern "C" int dsb_model_set_ep(dsb_model* m, dsb_ep* ep) {
+  if (m == nullptr || ep == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = m->ctx;
+  if (!m->allocs.empty() || m->finalized)
+    return fail(ctx, DSB_EINVAL, "dsb_model_set_ep: call before any tensor is set");
+  int rank = 0, world = 0, E = 0, k = 0, D = 0, T_max = 0, E_local = 0;
+  ep_params(ep, &rank, &world, &E, &k, &D, &T_max, &E_local);
+  const dsb_model_config& c = m->cfg;
+  if (E != c.n_routed_experts || k != c.num_experts_per_tok || D != c.hidden_size)
+    return fail(ctx, DSB_EINVAL, "dsb_model_set_ep: the group's experts, top-k or hidden size differ from the model's");
+  m->ep = ep;
+  m->e_first = rank * E_local;
+  m->E_own = E_local;
   return DSB_OK;
 }
 
@@ -428,7 +448,7 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
         return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s given but the config has no shared experts", cname);
       int rc = ensure_experts(m, L);
       if (rc != DSB_OK) return rc;
-      const int I = L.e_inter, ns = L.n_shared, E = c.n_routed_experts;
+      const int I = L.e_inter, ns = L.n_shared, E = m->E_own;
       if (ndim != 2 || (is_down ? (shape[0] != D || shape[1] != (int64_t)ns * I) : (shape[0] != (int64_t)ns * I || shape[1] != D)))
         return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_set_tensor: %s must be n_shared_experts x moe_intermediate_size", cname);
       L.has_moe_tensors = true;
@@ -478,6 +498,9 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
     const int E = c.n_routed_experts;
     if (e < 0 || e >= E) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: expert index out of range in %s", cname);
     L.has_moe_tensors = true;
+    // with expert parallelism another rank owns this expert: nothing to keep here
+    if (e < m->e_first || e >= m->e_first + m->E_own) return DSB_OK;
+    e -= m->e_first;
     const bool is_down = proj == "down_proj.weight";
     if (!is_down && proj != "gate_proj.weight" && proj != "up_proj.weight")
       return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
@@ -543,8 +566,8 @@ extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) 
       L.e_inter = c.moe_intermediate_size;
       L.n_shared = std::max(0, c.n_shared_experts);
       L.shared_seen = 7;
-      nb(&L.e_gu, (int64_t)(E + L.n_shared) * 2 * L.e_inter * D);
-      nb(&L.e_down, (int64_t)(E + L.n_shared) * D * L.e_inter);
+      nb(&L.e_gu, (int64_t)(m->E_own + L.n_shared) * 2 * L.e_inter * D);
+      nb(&L.e_down, (int64_t)(m->E_own + L.n_shared) * D * L.e_inter);
     }
   }
   if (rc != DSB_OK) return rc;
@@ -713,7 +736,19 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   for (int b = 0; b < B; ++b) need_pages += (kv->seq_len[seq_ids[b]] % 64 == 0) ? 1 : 0;
   if ((size_t)need_pages > kv->free_pages.size())
     return fail(ctx, DSB_ENOMEM, "dsb_decode_step: out of cache pages");
-  std::vector<int32_t> host_i((size_t)B * (2 + MB), 0);  // tokens | positions | block table
+  int max_ns_host = 0;
+  for (auto& L : m->layers) max_ns_host = std::max(max_ns_host, L.n_shared);
+  const bool ep = m->ep != nullptr;
+  int ep_cap = 0, ep_tmax = 0;
+  if (ep) {
+    int rk, wd, Eg, kg, Dg;
+    ep_params(m->ep, &rk, &wd, &Eg, &kg, &Dg, &ep_tmax, nullptr);
+    ep_cap = wd * ep_tmax * kg;
+    if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "dsb_decode_step: B=%d above the expert group's max_tokens", B);
+  }
+  // tokens | positions | block table | (expert parallel) shared-expert row sources and offsets
+  const size_t n_shared_tab = ep ? (size_t)max_ns_host * B + max_ns_host + 1 : 0;
+  std::vector<int32_t> host_i((size_t)B * (2 + MB) + n_shared_tab, 0);
   std::vector<int32_t> lens(B);
   for (int b = 0; b < B; ++b) {
     const int s = seq_ids[b];
@@ -729,6 +764,12 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     const auto& pg = kv->seq_pages[s];
     std::memcpy(host_i.data() + 2 * B + (size_t)b * MB, pg.data(), pg.size() * 4);
   }
+  if (ep) {
+    int32_t* st = host_i.data() + (size_t)B * (2 + MB);
+    for (int j = 0; j < max_ns_host; ++j)
+      for (int b = 0; b < B; ++b) st[(size_t)j * B + b] = b;  // shared group j reads token b
+    for (int j = 0; j <= max_ns_host; ++j) st[(size_t)max_ns_host * B + j] = j * B;
+  }
 
   // ---- device buffers for this batch size (in the context workspace after the plan)
   int max_I = 0, max_eI = 0, max_ns = 0;
@@ -741,6 +782,7 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     any_qlora |= L.w_qa != nullptr;
   }
   const int BK = any_moe ? B * (k + max_ns) : 1;
+  const int RX = std::max(BK, ep_cap);  // expert rows: permuted picks, or the expert group's receive rows
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -751,12 +793,13 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   const size_t o_qa = take(any_qlora ? (size_t)B * c.q_lora_rank * 4 : 4);
   const size_t o_qan = take(any_qlora ? (size_t)B * c.q_lora_rank * 2 : 4);
   const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)BK * 4 + 4);
-  const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)BK * D * 4);
+  const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)RX * D * 4);
+  const size_t o_ys = take(ep ? (size_t)max_ns * B * D * 4 : 4);
   const size_t o_logits = take((size_t)B * V * 4), o_xn = take((size_t)B * D * 2), o_q = take((size_t)B * QH * 2);
   const size_t o_qrope = take((size_t)B * H * P * 2), o_qlat = take((size_t)B * H * R * 2);
   const size_t o_olat = take((size_t)B * H * R * 2), o_attn = take((size_t)B * H * v * 2);
   const size_t o_mid = take((size_t)B * std::max(max_I, 64) * 2);
-  const size_t o_xperm = take((size_t)BK * D * 2), o_midp = take((size_t)BK * std::max(max_eI, 64) * 2);
+  const size_t o_xperm = take((size_t)BK * D * 2), o_midp = take((size_t)RX * std::max(max_eI, 64) * 2);
   const size_t o_ids = take((size_t)BK * 4 + 4), o_cnt = take((size_t)(E + max_ns + 1) * 4);
   const size_t o_off = take((size_t)(E + max_ns + 2) * 4);
   const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)B * 4);
@@ -770,12 +813,14 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   auto Bf = [&](size_t o) { return reinterpret_cast<bf16*>(base + o); };
   auto I32 = [&](size_t o) { return reinterpret_cast<int32_t*>(base + o); };
   float *h = F(o_h), *xn32 = F(o_xn32), *kva = F(o_kva), *qa = F(o_qa), *lr = F(o_lr), *wts = F(o_wts);
-  float *wperm = F(o_wperm), *yperm = F(o_yperm), *logits = F(o_logits);
+  float *wperm = F(o_wperm), *yperm = F(o_yperm), *logits = F(o_logits), *ys = F(o_ys);
   bf16 *xn = Bf(o_xn), *q = Bf(o_q), *qrope = Bf(o_qrope), *qlat = Bf(o_qlat), *olat = Bf(o_olat), *attn = Bf(o_attn);
   bf16 *mid = Bf(o_mid), *xperm = Bf(o_xperm), *midp = Bf(o_midp), *qan = Bf(o_qan);
   int32_t *ids = I32(o_ids), *cnt = I32(o_cnt), *offs = I32(o_off), *dest = I32(o_dest), *src = I32(o_src);
   int32_t *greedy = I32(o_greedy), *tab = I32(o_tab);
   const int32_t *d_tok = tab, *d_pos = tab + B, *d_bt = tab + 2 * B;
+  const int32_t* d_srows = tab + (size_t)B * (2 + MB);           // shared-expert row sources (expert parallel)
+  const int32_t* d_soff = d_srows + (size_t)max_ns_host * B;     // shared-expert row offsets
   DSB_CUDA_TRY(ctx, cudaMemcpyAsync(tab, host_i.data(), host_i.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
 
   dsb_mla_plan plan;
@@ -818,6 +863,27 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
       DSB_STEP(linear(ctx, L.w_gu, D, xn, D, B, 2 * L.inter, D, mid, L.inter, 0, DSB_EPI_SILU_GATE));
       DSB_STEP(linear(ctx, L.w_down, L.inter, mid, L.inter, B, D, L.inter, h, D, 1, DSB_EPI_ADD));
+    } else if (ep) {
+      // expert parallel: routed picks go to the experts' ranks and come back;
+      // the shared experts run here on this rank's tokens
+      DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
+      DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
+      DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group, c.norm_topk_prob,
+                         c.routed_scaling_factor, ids, wts, 0));
+      void* rx = nullptr;
+      int32_t* roff = nullptr;
+      DSB_STEP(dsb_ep_dispatch(m->ep, xn, D, B, ids, &rx, &roff));
+      const int eI = L.e_inter, EL = m->E_own, ns = L.n_shared;
+      DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
+      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
+      if (ns > 0) {
+        const bf16* s_gu = L.e_gu + (size_t)EL * 2 * eI * D;
+        const bf16* s_down = L.e_down + (size_t)EL * D * eI;
+        DSB_STEP(gather_rows(ctx, xn, D, d_srows, ns * B, 1, D, xperm));
+        DSB_STEP(linear(ctx, s_gu, D, xperm, D, ns * B, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, ns, 0, 0, d_soff, B));
+        DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
+      }
+      DSB_STEP(dsb_ep_combine(m->ep, yperm, D, B, wts, ys, ns, h));
     } else {
       DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
       DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));

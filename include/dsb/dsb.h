@@ -357,6 +357,46 @@ DSB_API int dsb_gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int3
 DSB_API int dsb_moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D,
                             const float* shared, float* h);
 
+/* ------------------------------------------------------ expert parallelism
+ *
+ * world ranks (one process and GPU each, world <= 8) split the E routed
+ * experts: expert e lives on rank e / (E / world).  Every rank keeps its own
+ * tokens and, per MoE layer, sends each pick's token row to the expert's
+ * rank and gets the expert's output back, by kernels that write straight
+ * into the other GPUs' memory (one CUDA IPC window per rank; no collective
+ * library on the data path).  The reference is single-GPU: no counterpart.
+ *
+ * Set-up: dsb_ep_create on every rank, exchange the 64-byte window handles
+ * (dsb_ep_window_handle) by any host channel, then dsb_ep_connect with all
+ * world handles in rank order.  Per layer, every rank (also one with T = 0)
+ * calls dsb_ep_dispatch and then dsb_ep_combine, in the same order; the
+ * kernels wait for the peers with bounded waits (dsb_sync reports a timeout).
+ *
+ * dispatch: x bf16 [T, ldx] and the global expert ids [T, top_k] of this
+ *   rank's tokens.  Returns (device pointers owned by the group, valid until
+ *   the next dispatch) the received rows recv_x bf16 [capacity, hidden],
+ *   grouped by local expert (sources in rank order, then pick order), and
+ *   recv_offsets int32 [E_local + 1], the row range of each local expert:
+ *   the tok_offsets of a grouped dsb_linear over the local experts.
+ * combine: y fp32 [capacity, ldy], the experts' outputs in recv_x row order
+ *   (unweighted); every output goes back to its token's rank, which adds
+ *     h[t] += sum_j weights[t,j] * out[t,j] + sum_s shared[s*T + t]
+ *   in that order (moe_step, src/models/deepseek/ops.cpp:133-145); shared
+ *   fp32 [n_shared, T, hidden] holds this rank's shared-expert outputs. */
+typedef struct dsb_ep dsb_ep;
+#define DSB_EP_HANDLE_BYTES 64
+
+DSB_API int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, int hidden, int top_k, int max_tokens,
+                          dsb_ep** out);
+DSB_API int dsb_ep_window_handle(dsb_ep* ep, void* handle);
+DSB_API int dsb_ep_connect(dsb_ep* ep, const void* handles);
+DSB_API int dsb_ep_info(const dsb_ep* ep, int* E_local, int* recv_capacity, uint64_t* window_bytes);
+DSB_API int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
+                            int32_t** recv_offsets);
+DSB_API int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,
+                           const float* shared, int n_shared, float* h);
+DSB_API int dsb_ep_destroy(dsb_ep* ep);
+
 /* Greedy ids: first index of the row maximum of logits [B, ld] (argmax_f32,
  * src/core/math.cpp:29-40; the reference downloads the logits and does this
  * on the host, cuda_backend.cpp:746-757). */
@@ -408,6 +448,15 @@ DSB_API int dsb_model_set_tensor(dsb_model* model, const char* name, int dtype, 
 DSB_API int dsb_model_init_random(dsb_model* model, uint64_t seed, float stddev);
 /* Check completeness (every layer's attention and FFN weights present). */
 DSB_API int dsb_model_finalize(dsb_model* model);
+
+/* Bind a model to an expert-parallel group before any of its tensors is set:
+ * it then keeps only this rank's routed experts (set_tensor accepts and
+ * skips the others; init_random makes only these) plus the shared experts,
+ * and dsb_decode_step exchanges every MoE layer's picks through the group.
+ * Every rank of the group calls dsb_decode_step in step (B >= 1 each, at most
+ * the group's max_tokens). */
+DSB_API int dsb_model_set_ep(dsb_model* m, dsb_ep* ep);
+
 DSB_API int dsb_model_weight_bytes(const dsb_model* model, uint64_t* bytes);
 
 typedef struct dsb_kvcache dsb_kvcache;
