@@ -44,6 +44,25 @@ struct dsb_mla_plan {
 
 namespace dsb {
 
+// Launch a kernel on `stream` with programmatic stream serialization: it may
+// be scheduled while the previous kernel of the stream drains (the kernel
+// calls pdl_wait() before reading that kernel's results).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Record an error message on the context and return `code`.
 int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 

@@ -106,6 +106,7 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch) {
 // the counts flag raised there.
 __global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, int E, EpLayout L, EpPeers peers,
                                 int32_t* __restrict__ slot, uint32_t epoch, int* status) {
+  pdl_wait();
   __shared__ int32_t cnt[256];
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cnt[e] = 0;
@@ -145,6 +146,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    const int32_t* __restrict__ slot, int n_picks, EpLayout L, EpPeers peers,
                                    int32_t* __restrict__ recv_offsets, int* __restrict__ ticket, uint32_t epoch,
                                    int* status) {
+  pdl_wait();
   __shared__ int32_t my_off[kMaxWorld * 64];  // [dst][el]: this rank's first row in dst's buffer
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
@@ -203,6 +205,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
 // 3. Wait until every source has raised `phase` here (one thread): phase 1,
 // its rows have landed; phase 2, its returns have.
 __global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t epoch, int* status) {
+  pdl_wait();
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.win[L.rank] + L.off_flags) + phase * L.world;
   if (!wait_flags(flags, L.world, epoch)) atomicCAS(status, 0, kStatusTimeout);
 }
@@ -211,6 +214,7 @@ __global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t ep
 // ranks' inboxes; the last CTA raises the return flag in every window.
 __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const int32_t* __restrict__ recv_offsets,
                                  EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
+  pdl_wait();
   const int n_recv = recv_offsets[L.E_local];
   const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -239,6 +243,7 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
 __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLayout L, EpPeers peers,
                                   const float* __restrict__ shared, int n_shared, float* __restrict__ h,
                                   uint32_t epoch, int* status) {
+  pdl_wait();
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {
@@ -375,14 +380,14 @@ extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, co
     return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
   const uint32_t epoch = ++ep->epoch * 2 - 1;  // odd: dispatch, even: the return of the same call
   const int n = T * ep->L.k;
-  ep_count_kernel<<<1, 32, 0, ctx->stream>>>(ids, n, ep->E, ep->L, ep->peers, ep->d_slot, epoch, ctx->d_status);
+  launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, n, ep->E, ep->L, ep->peers, ep->d_slot, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   const int blocks = std::max(1, std::min(ctx->sm_count, (n + 7) / 8));
-  ep_dispatch_kernel<<<blocks, 256, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), ldx, ids, ep->d_slot, n,
+  launch_pdl(ep_dispatch_kernel, blocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, ids, ep->d_slot, n,
                                                       ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch,
                                                       ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
-  ep_wait_kernel<<<1, 1, 0, ctx->stream>>>(ep->L, ep->peers, 1, epoch, ctx->d_status);
+  launch_pdl(ep_wait_kernel, 1, 1, 0, ctx->stream, ep->L, ep->peers, 1, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches += 3;
   if (recv_x) *recv_x = ep->win + ep->L.off_recv;
@@ -399,16 +404,16 @@ extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, co
     return fail(ctx, DSB_EINVAL, "dsb_ep_combine: bad arguments");
   if (ep->epoch == 0) return fail(ctx, DSB_EINVAL, "dsb_ep_combine: no dispatch to return");
   const uint32_t epoch = ep->epoch * 2;
-  ep_return_kernel<<<ctx->sm_count, 256, 0, ctx->stream>>>(y, ldy, ep->d_recv_off, ep->L, ep->peers,
+  launch_pdl(ep_return_kernel, ctx->sm_count, 256, 0, ctx->stream, y, ldy, ep->d_recv_off, ep->L, ep->peers,
                                                            ep->d_ticket + 1, epoch);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   if (T > 0) {
-    ep_combine_kernel<<<T, 256, 0, ctx->stream>>>(weights, T, ep->L, ep->peers, shared, n_shared, h, epoch,
+    launch_pdl(ep_combine_kernel, T, 256, 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, epoch,
                                                   ctx->d_status);
     DSB_CUDA_TRY(ctx, cudaGetLastError());
   } else {
     // no tokens here, but the next dispatch may only start once every peer has returned
-    ep_wait_kernel<<<1, 1, 0, ctx->stream>>>(ep->L, ep->peers, 2, epoch, ctx->d_status);
+    launch_pdl(ep_wait_kernel, 1, 1, 0, ctx->stream, ep->L, ep->peers, 2, epoch, ctx->d_status);
     DSB_CUDA_TRY(ctx, cudaGetLastError());
   }
   ctx->stats.kernel_launches += 2;

@@ -144,6 +144,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous
+  // kernel; its outputs (x, token offsets, y for ADD) are read only from here
+  pdl_wait();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
@@ -379,7 +382,7 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int splits, int m_tiles)
     attr_set = true;
   }
   const int grid = std::min(p.n_tiles, ctx->sm_count);
-  kern<<<grid, kThreads, S::SMEM, ctx->stream>>>(map_w, map_x, p, ctx->d_status);
+  DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, kThreads, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   ctx->stats.gemm_calls++;
@@ -413,7 +416,7 @@ extern "C" int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* a) {
   if (a->tok_offsets == nullptr && a->T <= 256) {
     // small decode GEMMs: split K so every SM streams a share of the weights
     const int tiles = m_tiles * a->G;
-    const int want = (ctx->sm_count + tiles - 1) / std::max(1, tiles);
+    const int want = ctx->sm_count / std::max(1, tiles);  // one wave of work units
     splits = std::max(1, std::min({want, KB / 4, 8}));
   }
   int NT = 16;

@@ -157,6 +157,9 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous
+  // kernel; its outputs (x, token offsets, y for ADD) are read only from here
+  pdl_wait();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
@@ -437,7 +440,7 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_til
     attr_set = true;
   }
   const int grid = std::min(p.n_tiles, ctx->sm_count);
-  kern<<<grid, S::THREADS, S::SMEM, ctx->stream>>>(map_w, map_x, p, ctx->d_status);
+  DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, S::THREADS, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   ctx->stats.gemm_calls++;

@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (NCTA == 2) cluster_sync();  // peer barriers initialised before any remote access
+  pdl_wait();                     // the previous kernel's q / cache writes are visible from here
   const uint32_t tmem = *tmem_base_smem;
   const uint32_t smem_base = smem_u32(smem);
 
@@ -482,6 +483,7 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaCombine* __re
                                                           const float* __restrict__ ws_o,
                                                           const float2* __restrict__ ws_ml,
                                                           __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const MlaCombine cmb = list[blockIdx.x];
   const int h = blockIdx.y;
   float M = -INFINITY;
@@ -606,13 +608,15 @@ int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const 
   cfg.blockDim = dim3(kMlaThreads);
   cfg.dynamicSmemBytes = S::SMEM_BYTES;
   cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = NCTA;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // prologue overlaps the previous kernel
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const float scale_log2 = scale * 1.4426950408889634f;
   DSB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, map_v, map_r, static_cast<const __nv_bfloat16*>(q_lat),
                                        static_cast<const __nv_bfloat16*>(q_rope), block_table, max_blocks,
@@ -621,7 +625,7 @@ int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const 
                                        reinterpret_cast<float2*>(ws + off_ml), ctx->d_status));
   ctx->stats.kernel_launches++;
   if (plan->n_combines > 0) {
-    mla_combine_kernel<R><<<dim3((unsigned)plan->n_combines, (unsigned)plan->H), 128, 0, ctx->stream>>>(
+    launch_pdl(mla_combine_kernel<R>, dim3((unsigned)plan->n_combines, (unsigned)plan->H), 128, 0, ctx->stream, 
         static_cast<const MlaCombine*>(plan->d_combines), plan->H, reinterpret_cast<const float*>(ws),
         reinterpret_cast<const float2*>(ws + off_ml), static_cast<__nv_bfloat16*>(out));
     DSB_CUDA_TRY(ctx, cudaGetLastError());
@@ -883,7 +887,7 @@ int noalloc_launch(cudaStream_t stream, uint8_t* scratch, const std::vector<MlaI
                          reinterpret_cast<int*>(scratch)) != cudaSuccess)
     return DSB_ECUDA;
   if (!combines.empty()) {
-    mla_combine_kernel<R><<<dim3((unsigned)combines.size(), (unsigned)H), 128, 0, stream>>>(
+    launch_pdl(mla_combine_kernel<R>, dim3((unsigned)combines.size(), (unsigned)H), 128, 0, stream, 
         reinterpret_cast<const MlaCombine*>(scratch + kNoAllocOffComb), H, ws_o, ws_ml,
         static_cast<__nv_bfloat16*>(out));
     if (cudaGetLastError() != cudaSuccess) return DSB_ECUDA;

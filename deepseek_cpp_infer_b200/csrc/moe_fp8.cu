@@ -13,6 +13,7 @@
 #include <algorithm>
 
 #include "dsb_internal.h"
+#include "dsb_ptx.cuh"
 
 namespace dsb {
 namespace {
@@ -20,6 +21,7 @@ namespace {
 // ids/weights [T, k] -> [T, k + ns] with groups E .. E+ns-1 at weight 1 appended.
 __global__ void append_shared_kernel(const int32_t* __restrict__ ids, const float* __restrict__ weights, int T, int k,
                                      int E, int ns, int32_t* __restrict__ ids_out, float* __restrict__ w_out) {
+  pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const int kk = k + ns;
@@ -71,7 +73,7 @@ extern "C" int dsb_moe_ffn_fp8(dsb_ctx* ctx, const dsb_moe_fp8_layer* w, const v
   int32_t *ids_x = I32(o_ids), *cnt = I32(o_cnt), *offs = I32(o_off), *dest = I32(o_dest), *src = I32(o_src);
   float *w_x = F32(o_w), *wperm = F32(o_wp), *sx = F32(o_sx), *msx = F32(o_msx), *y = F32(o_y);
 
-  append_shared_kernel<<<(T + 127) / 128, 128, 0, ctx->stream>>>(ids, weights, T, k, E, ns, ids_x, w_x);
+  launch_pdl(append_shared_kernel, (T + 127) / 128, 128, 0, ctx->stream, ids, weights, T, k, E, ns, ids_x, w_x);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   rc = moe_permute(ctx, ids_x, (int)N, G, cnt, offs, dest, src, w_x, wperm);

@@ -47,6 +47,7 @@ __device__ float block_sum(float v, float* red) {
 __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int n,
                                     float eps, __nv_bfloat16* __restrict__ yb, int64_t ldyb, float* __restrict__ yf,
                                     int64_t ldyf) {
+  pdl_wait();
   __shared__ float red[32];
   const float* xr = x + blockIdx.x * ldx;
   float ss = 0.0f;
@@ -81,6 +82,7 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, const
                                            const int32_t* __restrict__ block_table, int max_blocks, int H, int nope,
                                            int R, int P, float eps, float theta, __nv_bfloat16* __restrict__ cache,
                                            __nv_bfloat16* __restrict__ q_rope) {
+  pdl_wait();
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int p = pos[b];
@@ -116,6 +118,7 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, const
 // ops.cpp:115-117); one warp per (token, expert).
 __global__ void router_logits_kernel(const float* __restrict__ x, const float* __restrict__ w, int T, int D, int E,
                                      float* __restrict__ logits) {
+  pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= T * E) return;
   const int t = gw / E, e = gw % E;
@@ -139,6 +142,7 @@ constexpr int kRtT = 32, kRtE = 64, kRtD = 64;
 __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ w, int T, int D, int E,
                                                                    float* __restrict__ logits) {
+  pdl_wait();
   __shared__ float xs[kRtT][kRtD + 1];
   __shared__ float ws[kRtE][kRtD + 1];
   const int t0 = blockIdx.y * kRtT, e0 = blockIdx.x * kRtE;
@@ -200,6 +204,7 @@ __device__ __forceinline__ void warp_argmax(float& v, int& idx) {
 __global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                              int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
                              int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra) {
+  pdl_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (t >= T) return;
   const float* lg = logits + (int64_t)t * E;
@@ -334,6 +339,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
                                int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
                                int32_t* __restrict__ src_pair, const float* __restrict__ weights,
                                float* __restrict__ w_perm, int* __restrict__ status) {
+  pdl_wait();
   extern __shared__ int32_t cnt[];  // [E]
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cnt[e] = 0;
@@ -384,6 +390,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
 // out[p] = x[src_pair[p] / k] (bf16 rows, 16-byte vectors).
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src,
                                    int k, int D, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const int p = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)(src[p] / k) * ldx);
   uint4* d = reinterpret_cast<uint4*>(out + (int64_t)p * D);
@@ -401,6 +408,7 @@ constexpr int kPermSingleWarpMax = 4096;
 
 __global__ void permute_count_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ hist,
                                      int* __restrict__ status) {
+  pdl_wait();
   extern __shared__ int32_t h[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
@@ -416,6 +424,7 @@ __global__ void permute_count_kernel(const int32_t* __restrict__ ids, int N, int
 
 __global__ void permute_scan_kernel(int32_t* __restrict__ hist, int chunks, int E, int32_t* __restrict__ counts,
                                     int32_t* __restrict__ offsets) {
+  pdl_wait();
   extern __shared__ int32_t tot[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int v = 0;
@@ -457,6 +466,7 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ hist, int chunks, int 
 __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, int E, const int32_t* __restrict__ hist,
                                        int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
                                        const float* __restrict__ weights, float* __restrict__ w_perm) {
+  pdl_wait();
   extern __shared__ int32_t cur[];
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cur[e] = hist[(int64_t)blockIdx.x * E + e];
@@ -486,6 +496,7 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, i
 // (model.cpp:209).
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ dest, int k, int D,
                                    const float* __restrict__ shared, float* __restrict__ h) {
+  pdl_wait();
   const int t = blockIdx.x;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     float acc = 0.0f;
@@ -497,6 +508,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
 
 // Greedy id per row: first index of the maximum (argmax_f32, math.cpp:29-40).
 __global__ void argmax_rows_kernel(const float* __restrict__ logits, int64_t ld, int V, int32_t* __restrict__ out) {
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const float* row = logits + blockIdx.x * ld;
@@ -529,6 +541,7 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int64_t ld,
 // src/hf/weight_ops.cpp:37-65).
 __global__ void embed_kernel(const void* __restrict__ table, int bf16, const int32_t* __restrict__ tokens, int D,
                              float* __restrict__ h) {
+  pdl_wait();
   const int b = blockIdx.x;
   const int64_t row = tokens[b];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -548,7 +561,7 @@ int launched(dsb_ctx* ctx) {
 
 int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
                  void* y_bf16, int64_t ldyb, float* y_f32, int64_t ldyf) {
-  rmsnorm_rows_kernel<<<rows, 256, 0, ctx->stream>>>(x, ldx, w, n, eps, static_cast<__nv_bfloat16*>(y_bf16), ldyb,
+  launch_pdl(rmsnorm_rows_kernel, rows, 256, 0, ctx->stream, x, ldx, w, n, eps, static_cast<__nv_bfloat16*>(y_bf16), ldyb,
                                                      y_f32, ldyf);
   return launched(ctx);
 }
@@ -556,7 +569,7 @@ int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int 
 int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q, const int32_t* pos,
                         const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
                         float theta, void* cache, void* q_rope) {
-  kv_norm_rope_append_kernel<<<B, 128, 0, ctx->stream>>>(kv_a, w_norm, static_cast<const __nv_bfloat16*>(q), pos,
+  launch_pdl(kv_norm_rope_append_kernel, B, 128, 0, ctx->stream, kv_a, w_norm, static_cast<const __nv_bfloat16*>(q), pos,
                                                          block_table, max_blocks, H, nope, R, P, eps, theta,
                                                          static_cast<__nv_bfloat16*>(cache),
                                                          static_cast<__nv_bfloat16*>(q_rope));
@@ -567,16 +580,16 @@ int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, in
   const int warps = T * E;
   if (T > 64) {
     const dim3 grid((E + kRtE - 1) / kRtE, (T + kRtT - 1) / kRtT);
-    router_logits_tiled_kernel<<<grid, 256, 0, ctx->stream>>>(x, w, T, D, E, logits);
+    launch_pdl(router_logits_tiled_kernel, grid, 256, 0, ctx->stream, x, w, T, D, E, logits);
     return launched(ctx);
   }
-  router_logits_kernel<<<(warps + 7) / 8, 256, 0, ctx->stream>>>(x, w, T, D, E, logits);
+  launch_pdl(router_logits_kernel, (warps + 7) / 8, 256, 0, ctx->stream, x, w, T, D, E, logits);
   return launched(ctx);
 }
 
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
               int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra) {
-  route_kernel<<<(T + 7) / 8, 256, 0, ctx->stream>>>(logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk,
+  launch_pdl(route_kernel, (T + 7) / 8, 256, 0, ctx->stream, logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk,
                                                      routed_scale, ids, weights, n_extra);
   return launched(ctx);
 }
@@ -584,7 +597,7 @@ int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
                 int32_t* src_pair, const float* weights, float* w_perm) {
   if (N <= kPermSingleWarpMax) {
-    permute_kernel<<<1, 32, E * sizeof(int32_t), ctx->stream>>>(ids, N, E, counts, offsets, dest, src_pair, weights,
+    launch_pdl(permute_kernel, 1, 32, E * sizeof(int32_t), ctx->stream, ids, N, E, counts, offsets, dest, src_pair, weights,
                                                                  w_perm, ctx->d_status);
     return launched(ctx);
   }
@@ -595,36 +608,36 @@ int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts,
   if (rc != DSB_OK) return rc;
   int32_t* hist = static_cast<int32_t*>(ctx->perm);
   const size_t sh = (size_t)E * sizeof(int32_t);
-  permute_count_kernel<<<chunks, 256, sh, ctx->stream>>>(ids, N, E, hist, ctx->d_status);
+  launch_pdl(permute_count_kernel, chunks, 256, sh, ctx->stream, ids, N, E, hist, ctx->d_status);
   rc = launched(ctx);
   if (rc != DSB_OK) return rc;
-  permute_scan_kernel<<<1, 1024, sh, ctx->stream>>>(hist, chunks, E, counts, offsets);
+  launch_pdl(permute_scan_kernel, 1, 1024, sh, ctx->stream, hist, chunks, E, counts, offsets);
   rc = launched(ctx);
   if (rc != DSB_OK) return rc;
-  permute_scatter_kernel<<<chunks, 32, sh, ctx->stream>>>(ids, N, E, hist, dest, src_pair, weights, w_perm);
+  launch_pdl(permute_scatter_kernel, chunks, 32, sh, ctx->stream, ids, N, E, hist, dest, src_pair, weights, w_perm);
   return launched(ctx);
 }
 
 int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
                 void* out) {
-  gather_rows_kernel<<<n_pairs, 128, 0, ctx->stream>>>(static_cast<const __nv_bfloat16*>(x), ldx, src_pair, k, D,
+  launch_pdl(gather_rows_kernel, n_pairs, 128, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, src_pair, k, D,
                                                        static_cast<__nv_bfloat16*>(out));
   return launched(ctx);
 }
 
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
                 float* h) {
-  moe_combine_kernel<<<T, 256, 0, ctx->stream>>>(y, dest, k, D, shared, h);
+  launch_pdl(moe_combine_kernel, T, 256, 0, ctx->stream, y, dest, k, D, shared, h);
   return launched(ctx);
 }
 
 int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out) {
-  argmax_rows_kernel<<<B, 1024, 0, ctx->stream>>>(logits, ld, V, out);
+  launch_pdl(argmax_rows_kernel, B, 1024, 0, ctx->stream, logits, ld, V, out);
   return launched(ctx);
 }
 
 int embed(dsb_ctx* ctx, const void* table, int bf16, const int32_t* tokens, int B, int D, float* h) {
-  embed_kernel<<<B, 256, 0, ctx->stream>>>(table, bf16, tokens, D, h);
+  launch_pdl(embed_kernel, B, 256, 0, ctx->stream, table, bf16, tokens, D, h);
   return launched(ctx);
 }
 

@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "dsb_internal.h"
+#include "dsb_ptx.cuh"
 
 namespace dsb {
 namespace {
@@ -35,6 +36,7 @@ template <bool kBf16>
 __global__ void quant_act_kernel(const void* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src_rows,
                                  int k, int T, int G, uint8_t* __restrict__ q, int64_t ldq,
                                  float* __restrict__ scales, int64_t ld_scales) {
+  pdl_wait();
   const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= (int64_t)T * G) return;
@@ -67,6 +69,7 @@ __global__ void quant_act_kernel(const void* __restrict__ x, int64_t ldx, const 
 template <bool kBf16>
 __global__ void quant_weight_kernel(const void* __restrict__ w, int64_t M, int64_t K, uint8_t* __restrict__ q,
                                     float* __restrict__ scales) {
+  pdl_wait();
   const int64_t r0 = (int64_t)blockIdx.y * 128, c0 = (int64_t)blockIdx.x * 128;
   auto load = [&](int64_t r, int64_t c) -> float {
     if (kBf16) return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[r * K + c]);
@@ -105,10 +108,10 @@ int quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const
   const int64_t warps = (int64_t)T * G;
   const int blocks = (int)((warps + 7) / 8);
   if (x_dtype == DSB_DTYPE_BF16)
-    quant_act_kernel<true><<<blocks, 256, 0, ctx->stream>>>(x, ldx, src_rows, k, T, G, static_cast<uint8_t*>(q), ldq,
+    launch_pdl(quant_act_kernel<true>, blocks, 256, 0, ctx->stream, x, ldx, src_rows, k, T, G, static_cast<uint8_t*>(q), ldq,
                                                             scales, ld_scales);
   else
-    quant_act_kernel<false><<<blocks, 256, 0, ctx->stream>>>(x, ldx, src_rows, k, T, G, static_cast<uint8_t*>(q),
+    launch_pdl(quant_act_kernel<false>, blocks, 256, 0, ctx->stream, x, ldx, src_rows, k, T, G, static_cast<uint8_t*>(q),
                                                              ldq, scales, ld_scales);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
@@ -140,9 +143,9 @@ extern "C" int dsb_quant_weight_128x128(dsb_ctx* ctx, const void* w, int w_dtype
   const dim3 grid((unsigned)((K + 127) / 128), (unsigned)((M + 127) / 128));
   if (grid.y > 65535) return fail(ctx, DSB_EINVAL, "dsb_quant_weight_128x128: too many rows");
   if (w_dtype == DSB_DTYPE_BF16)
-    quant_weight_kernel<true><<<grid, 256, 0, ctx->stream>>>(w, M, K, static_cast<uint8_t*>(q), scales);
+    launch_pdl(quant_weight_kernel<true>, grid, 256, 0, ctx->stream, w, M, K, static_cast<uint8_t*>(q), scales);
   else
-    quant_weight_kernel<false><<<grid, 256, 0, ctx->stream>>>(w, M, K, static_cast<uint8_t*>(q), scales);
+    launch_pdl(quant_weight_kernel<false>, grid, 256, 0, ctx->stream, w, M, K, static_cast<uint8_t*>(q), scales);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   return DSB_OK;
