@@ -93,9 +93,12 @@ int make_tmap_2d(dsb_ctx* ctx, CUtensorMap* map, const void* base, CUtensorMapDa
 // Launchers shared by the C ABI entry points and the decode step (ops.cu).
 int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int rows, int n, float eps,
                  void* y_bf16, int64_t ldyb, float* y_f32, int64_t ldyf);
-int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q, const int32_t* pos,
-                        const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
-                        float theta, void* cache, void* q_rope);
+// kv_a rows of pitch ld_kv; the query either bf16 q [B, H*(nope+P)] or fp32 qf
+// (row pitch ld_qf), whose nope parts are then also written to q_out as bf16.
+int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, int64_t ld_kv, const float* w_norm, const void* q,
+                        const float* qf, int64_t ld_qf, void* q_out, const int32_t* pos, const int32_t* block_table,
+                        int max_blocks, int B, int H, int nope, int R, int P, float eps, float theta, void* cache,
+                        void* q_rope);
 int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits);
 // Sizes of an expert-parallel group (ep.cu); any output may be null.
 int ep_params(const dsb_ep* ep, int* rank, int* world, int* n_experts, int* top_k, int* hidden, int* max_tokens,
@@ -113,8 +116,17 @@ int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts,
                 int32_t* src_pair, const float* weights, float* w_perm);
 int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
                 void* out);
+// h[t] += sum of the row's picks (+ shared); with w_next, also writes the
+// row's next RMSNorm (weights w_next) to xn_next as bf16.
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
-                float* h);
+                float* h, const float* w_next = nullptr, float eps = 0.0f, void* xn_next = nullptr);
+// Post-attention RMSNorm + router logits + routing, one CTA per token.
+int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
+              int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
+              float routed_scale, int n_extra, void* xn, int32_t* ids, float* weights);
+// dsb_ep_combine with the next RMSNorm fused as in moe_combine.
+int ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
+               int n_shared, float* h, const float* w_next, float eps, void* xn_next);
 int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
 int embed(dsb_ctx* ctx, const void* table, int bf16, const int32_t* tokens, int B, int D, float* h);
 

@@ -242,6 +242,7 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
 // 5. h[t] += sum_j w[t,j] * inbox[t*k+j] (pick order) + sum_s shared[s*T + t].
 __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLayout L, EpPeers peers,
                                   const float* __restrict__ shared, int n_shared, float* __restrict__ h,
+                                  const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next,
                                   uint32_t epoch, int* status) {
   pdl_wait();
   __shared__ int ok_s;
@@ -254,12 +255,30 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
   if (!ok_s) return;
   const float* inbox = reinterpret_cast<const float*>(win + L.off_inbox);
   const int t = blockIdx.x, k = L.k, D = L.D;
+  float ss = 0.0f;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     float acc = 0.0f;
     for (int j = 0; j < k; ++j)
       acc = __fadd_rn(acc, __fmul_rn(__ldcv(inbox + ((size_t)t * k + j) * D + i), weights[(size_t)t * k + j]));
     for (int s = 0; s < n_shared; ++s) acc = __fadd_rn(acc, shared[((size_t)s * T + t) * D + i]);
-    h[(size_t)t * D + i] = __fadd_rn(h[(size_t)t * D + i], acc);
+    const float hv = __fadd_rn(h[(size_t)t * D + i], acc);
+    h[(size_t)t * D + i] = hv;
+    ss = __fadd_rn(ss, __fmul_rn(hv, hv));
+  }
+  if (w_next != nullptr) {
+    // the next RMSNorm of this row, the arithmetic of the single-GPU combine
+    __shared__ float red[32];
+    float v = ss;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)D), eps)));
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+      xn_next[(size_t)t * D + i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(h[(size_t)t * D + i], inv), w_next[i]));
   }
 }
 
@@ -397,6 +416,11 @@ extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, co
 
 extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,
                               const float* shared, int n_shared, float* h) {
+  return dsb::ep_combine(ep, y, ldy, T, weights, shared, n_shared, h, nullptr, 0.0f, nullptr);
+}
+
+int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
+                    int n_shared, float* h, const float* w_next, float eps, void* xn_next) {
   if (ep == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = ep->ctx;
   if (y == nullptr || weights == nullptr || h == nullptr || T < 0 || T > ep->L.T_max || ldy < ep->L.D ||
@@ -408,7 +432,8 @@ extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, co
                                                            ep->d_ticket + 1, epoch);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   if (T > 0) {
-    launch_pdl(ep_combine_kernel, T, 256, 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, epoch,
+    launch_pdl(ep_combine_kernel, T, 256, 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, w_next,
+               eps, static_cast<__nv_bfloat16*>(xn_next), epoch,
                                                   ctx->d_status);
     DSB_CUDA_TRY(ctx, cudaGetLastError());
   } else {

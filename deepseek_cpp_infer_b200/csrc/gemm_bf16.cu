@@ -145,7 +145,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous
-  // kernel; its outputs (x, token offsets, y for ADD) are read only from here
+  // kernel; its outputs (x, token offsets, y for ADD) are read only from here.
+  // A dense GEMM's first work units are known without them, so its producer
+  // also starts the weight half of the first ring stages before the wait.
+  int npre = 0;
+  if (warp == 0 && lane == 0 && p.tok_offsets == nullptr) {
+    const uint64_t pol_w = l2_policy_evict_first();
+    UnitIter it{&p, NT};
+    while (npre < S::NS && it.next()) {
+      const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+      for (int kb = kb0; kb < kb1 && npre < S::NS; ++kb, ++npre) {
+        mbar_arrive_expect_tx(&full[npre], S::STAGE);
+        tma_load_2d(smem + npre * S::STAGE, &map_w, &full[npre], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
+      }
+    }
+  }
   pdl_wait();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
@@ -167,11 +181,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + s * S::STAGE;
-          mbar_arrive_expect_tx(&full[s], S::STAGE);
-          tma_load_2d(st, &map_w, &full[s], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
+          if (q >= npre) {  // (stages below npre got their weights before pdl_wait)
+            mbar_arrive_expect_tx(&full[s], S::STAGE);
+            tma_load_2d(st, &map_w, &full[s], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
+          }
           tma_load_2d(st + S::A_BYTES, &map_x, &full[s], (int)(it.g * p.x_group_col + kb * kBK), it.tok0 + it.nt * NT);
         }
       }
+      pdl_launch_dependents();  // every load of this CTA is issued: the next kernel may be scheduled
       if (*abort) {
         const int first = q > S::NS ? q - S::NS : 0;
         for (int i = first; i < q; ++i) mbar_wait(&full[i % S::NS], (i / S::NS) & 1, no_abort);

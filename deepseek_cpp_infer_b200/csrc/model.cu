@@ -34,6 +34,9 @@ struct dsb_model {
     float* qa_norm = nullptr;        // [q_lora]
     __nv_bfloat16* w_qb = nullptr;   // [H*(nope+P), q_lora]
     __nv_bfloat16* w_kva = nullptr;  // [R+P, D]
+    // w_q (or w_qa) and w_kva are row ranges of one buffer [Mq + R + P, D]
+    // (Mq = H*(nope+P), or q_lora_rank), so one GEMM projects both from x
+    __nv_bfloat16* w_qkv = nullptr;
     float* kva_norm = nullptr;       // [R]
     __nv_bfloat16* w_uk_t = nullptr; // [H*R, nope]   W_UK^T per head (from kv_b_proj)
     __nv_bfloat16* w_uv = nullptr;   // [H*v, R]      W_UV per head (from kv_b_proj)
@@ -401,13 +404,33 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
     auto b = to_bf16(data, dtype, n);
     return upload(m, dst, b.data(), (size_t)n);
   };
+  // q (or q_a) and kv_a projections: row ranges of the layer's fused buffer
+  const int64_t Mq = c.q_lora_rank > 0 ? c.q_lora_rank : (int64_t)H * (nope + P);
+  auto qkv_rows = [&](int64_t row0, int64_t rows) -> int {
+    if (!expect(rows, D)) return bad_shape();
+    if (L.w_qkv == nullptr) {
+      int rc = dev_alloc(m, &L.w_qkv, (size_t)(Mq + R + P) * D);
+      if (rc != DSB_OK) return rc;
+    }
+    auto b = to_bf16(data, dtype, n);
+    DSB_CUDA_TRY(ctx, cudaMemcpy(L.w_qkv + row0 * D, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+    if (row0 == 0) (c.q_lora_rank > 0 ? L.w_qa : L.w_q) = L.w_qkv;
+    else L.w_kva = L.w_qkv + Mq * D;
+    return DSB_OK;
+  };
   if (rest == "input_layernorm.weight") return norm_f32(&L.in_norm, D);
   if (rest == "post_attention_layernorm.weight") return norm_f32(&L.post_norm, D);
-  if (rest == "self_attn.q_proj.weight") return mat_bf16(&L.w_q, (int64_t)H * (nope + P), D);
-  if (rest == "self_attn.q_a_proj.weight") return mat_bf16(&L.w_qa, c.q_lora_rank, D);
+  if (rest == "self_attn.q_proj.weight") {
+    if (c.q_lora_rank > 0) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: q_proj given but q_lora_rank > 0");
+    return qkv_rows(0, (int64_t)H * (nope + P));
+  }
+  if (rest == "self_attn.q_a_proj.weight") {
+    if (c.q_lora_rank <= 0) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: q_a_proj given but q_lora_rank = 0");
+    return qkv_rows(0, c.q_lora_rank);
+  }
   if (rest == "self_attn.q_a_layernorm.weight") return norm_f32(&L.qa_norm, c.q_lora_rank);
   if (rest == "self_attn.q_b_proj.weight") return mat_bf16(&L.w_qb, (int64_t)H * (nope + P), c.q_lora_rank);
-  if (rest == "self_attn.kv_a_proj_with_mqa.weight") return mat_bf16(&L.w_kva, R + P, D);
+  if (rest == "self_attn.kv_a_proj_with_mqa.weight") return qkv_rows(Mq, R + P);
   if (rest == "self_attn.kv_a_layernorm.weight") return norm_f32(&L.kva_norm, R);
   if (rest == "self_attn.o_proj.weight") return mat_bf16(&L.w_o, D, (int64_t)H * v);
   if (rest == "self_attn.kv_b_proj.weight") {
@@ -542,14 +565,16 @@ extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) 
     auto& L = m->layers[li];
     ones(&L.in_norm, D);
     ones(&L.post_norm, D);
+    const int64_t Mq = c.q_lora_rank > 0 ? c.q_lora_rank : (int64_t)H * (nope + P);
+    nb(&L.w_qkv, (Mq + R + P) * D);
+    if (rc == DSB_OK) {
+      (c.q_lora_rank > 0 ? L.w_qa : L.w_q) = L.w_qkv;
+      L.w_kva = L.w_qkv + Mq * D;
+    }
     if (c.q_lora_rank > 0) {
-      nb(&L.w_qa, (int64_t)c.q_lora_rank * D);
       ones(&L.qa_norm, c.q_lora_rank);
       nb(&L.w_qb, (int64_t)H * (nope + P) * c.q_lora_rank);
-    } else {
-      nb(&L.w_q, (int64_t)H * (nope + P) * D);
     }
-    nb(&L.w_kva, (int64_t)(R + P) * D);
     ones(&L.kva_norm, R);
     nb(&L.w_uk_t, (int64_t)H * R * nope);
     nb(&L.w_uv, (int64_t)H * v * R);
@@ -789,7 +814,8 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     off += (bytes + 255) & ~size_t(255);
     return o;
   };
-  const size_t o_h = take((size_t)B * D * 4), o_xn32 = take((size_t)B * D * 4), o_kva = take((size_t)B * (R + P) * 4);
+  const int Mq = c.q_lora_rank > 0 ? c.q_lora_rank : QH, LQKV = Mq + R + P;  // fused q|kv_a projection row
+  const size_t o_h = take((size_t)B * D * 4), o_xn32 = take((size_t)B * D * 4), o_kva = take((size_t)B * LQKV * 4);
   const size_t o_qa = take(any_qlora ? (size_t)B * c.q_lora_rank * 4 : 4);
   const size_t o_qan = take(any_qlora ? (size_t)B * c.q_lora_rank * 2 : 4);
   const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)BK * 4 + 4);
@@ -836,22 +862,32 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   } while (0)
 
   DSB_STEP(embed(ctx, m->embed, m->embed_bf16, d_tok, B, D, h));
+  bool xn_ready = false;  // the previous MoE combine already wrote this layer's input norm into xn
   for (int li = 0; li < c.num_hidden_layers; ++li) {
     const auto& L = m->layers[li];
     bf16* cache = kv->pool + (int64_t)li * layer_stride;
+    // the RMSNorm after this layer's MoE block: the next layer's input norm, or the final norm
+    const float* next_norm = li + 1 < c.num_hidden_layers ? m->layers[li + 1].in_norm : m->final_norm;
+    // post-attention norm, router and routing in one kernel (one CTA per token):
+    // it pulls the whole router matrix through one SM per token, slower than the
+    // three spread-out kernels at V2-Lite shape, so it is off
+    const bool fused_front = false;
     // attention block (model.cpp:126-138)
-    DSB_STEP(rmsnorm_rows(ctx, h, D, L.in_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+    if (!xn_ready) DSB_STEP(rmsnorm_rows(ctx, h, D, L.in_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+    xn_ready = false;
+    // one GEMM for [q | kv_a] (or [q_a | kv_a]) from x, fp32 rows of LQKV
+    DSB_STEP(linear(ctx, L.w_qkv, D, xn, D, B, LQKV, D, kva, LQKV, 1, DSB_EPI_STORE));
     if (L.w_qa != nullptr) {
-      DSB_STEP(linear(ctx, L.w_qa, D, xn, D, B, c.q_lora_rank, D, qa, c.q_lora_rank, 1, DSB_EPI_STORE));
-      DSB_STEP(rmsnorm_rows(ctx, qa, c.q_lora_rank, L.qa_norm, B, c.q_lora_rank, c.rms_norm_eps, qan, c.q_lora_rank,
+      DSB_STEP(rmsnorm_rows(ctx, kva, LQKV, L.qa_norm, B, c.q_lora_rank, c.rms_norm_eps, qan, c.q_lora_rank,
                             nullptr, 0));
       DSB_STEP(linear(ctx, L.w_qb, c.q_lora_rank, qan, c.q_lora_rank, B, QH, c.q_lora_rank, q, QH, 0, DSB_EPI_STORE));
+      DSB_STEP(kv_norm_rope_append(ctx, kva + Mq, LQKV, L.kva_norm, q, nullptr, 0, nullptr, d_pos, d_bt, MB, B, H,
+                                   nope, R, P, c.rms_norm_eps, c.rope_theta, cache, qrope));
     } else {
-      DSB_STEP(linear(ctx, L.w_q, D, xn, D, B, QH, D, q, QH, 0, DSB_EPI_STORE));
+      // q comes as fp32 from the fused GEMM; the append also writes it as bf16 for the absorb GEMM
+      DSB_STEP(kv_norm_rope_append(ctx, kva + Mq, LQKV, L.kva_norm, nullptr, kva, LQKV, q, d_pos, d_bt, MB, B, H,
+                                   nope, R, P, c.rms_norm_eps, c.rope_theta, cache, qrope));
     }
-    DSB_STEP(linear(ctx, L.w_kva, D, xn, D, B, R + P, D, kva, R + P, 1, DSB_EPI_STORE));
-    DSB_STEP(kv_norm_rope_append(ctx, kva, L.kva_norm, q, d_pos, d_bt, MB, B, H, nope, R, P, c.rms_norm_eps,
-                                 c.rope_theta, cache, qrope));
     // q_lat[:, h] = W_UK[h]^T q_nope[:, h]
     DSB_STEP(linear(ctx, L.w_uk_t, nope, q, QH, B, R, nope, qlat, (int64_t)H * R, 0, DSB_EPI_STORE, H, nope + P, R));
     DSB_STEP(dsb_mla_decode_planned(ctx, &plan, qlat, qrope, cache, kv->n_blocks, d_bt, MB, scale, olat));
@@ -866,10 +902,15 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     } else if (ep) {
       // expert parallel: routed picks go to the experts' ranks and come back;
       // the shared experts run here on this rank's tokens
-      DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
-      DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
-      DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group, c.norm_topk_prob,
-                         c.routed_scaling_factor, ids, wts, 0));
+      if (fused_front) {
+        DSB_STEP(moe_front(ctx, h, L.post_norm, B, D, c.rms_norm_eps, L.w_router, E, L.router_bias, k, c.scoring_func,
+                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, 0, xn, ids, wts));
+      } else {
+        DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
+        DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
+        DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
+                           c.norm_topk_prob, c.routed_scaling_factor, ids, wts, 0));
+      }
       void* rx = nullptr;
       int32_t* roff = nullptr;
       DSB_STEP(dsb_ep_dispatch(m->ep, xn, D, B, ids, &rx, &roff));
@@ -883,14 +924,21 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
         DSB_STEP(linear(ctx, s_gu, D, xperm, D, ns * B, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, ns, 0, 0, d_soff, B));
         DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
       }
-      DSB_STEP(dsb_ep_combine(m->ep, yperm, D, B, wts, ys, ns, h));
+      DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, ys, ns, h, next_norm, c.rms_norm_eps, xn));
+      xn_ready = true;
     } else {
-      DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
-      DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
       // each token routes to its top-k experts plus every shared group (weight 1)
       const int kk = k + L.n_shared, G = E + L.n_shared;
-      DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group, c.norm_topk_prob,
-                         c.routed_scaling_factor, ids, wts, L.n_shared));
+      if (fused_front) {
+        DSB_STEP(moe_front(ctx, h, L.post_norm, B, D, c.rms_norm_eps, L.w_router, E, L.router_bias, k, c.scoring_func,
+                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, L.n_shared, xn, ids,
+                           wts));
+      } else {
+        DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
+        DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
+        DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
+                           c.norm_topk_prob, c.routed_scaling_factor, ids, wts, L.n_shared));
+      }
       DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
       DSB_STEP(gather_rows(ctx, xn, D, src, B * kk, kk, D, xperm));
       const int eI = L.e_inter;
@@ -898,11 +946,12 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * kk, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, G, 0, 0, offs, B));
       DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * kk, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, G, 0, 0, offs, B,
                       wperm));
-      DSB_STEP(moe_combine(ctx, yperm, dest, B, kk, D, nullptr, h));
+      DSB_STEP(moe_combine(ctx, yperm, dest, B, kk, D, nullptr, h, next_norm, c.rms_norm_eps, xn));
+      xn_ready = true;
     }
   }
   // final norm, lm_head, greedy (model.cpp:160-179)
-  DSB_STEP(rmsnorm_rows(ctx, h, D, m->final_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
+  if (!xn_ready) DSB_STEP(rmsnorm_rows(ctx, h, D, m->final_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
   DSB_STEP(linear(ctx, m->lm_head, D, xn, D, B, V, D, logits, V, 1, DSB_EPI_STORE));
   DSB_STEP(argmax_rows(ctx, logits, V, B, V, greedy));
 #undef DSB_STEP

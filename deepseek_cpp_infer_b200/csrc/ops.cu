@@ -77,16 +77,17 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, int k, int dim, 
 // One block per token b: c = rmsnorm(kv_a[b, :R]) * w and kr = rope(kv_a[b, R:])
 // go to the token's paged-cache row (mla.cpp:74-84); every head's rope query
 // q[b, h, nope:] is rotated into q_rope[b, h] (mla.cpp:97).
-__global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, const float* __restrict__ w_norm,
-                                           const __nv_bfloat16* __restrict__ q, const int32_t* __restrict__ pos,
-                                           const int32_t* __restrict__ block_table, int max_blocks, int H, int nope,
-                                           int R, int P, float eps, float theta, __nv_bfloat16* __restrict__ cache,
-                                           __nv_bfloat16* __restrict__ q_rope) {
+__global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64_t ld_kv, const float* __restrict__ w_norm,
+                                           const __nv_bfloat16* __restrict__ q, const float* __restrict__ qf,
+                                           int64_t ld_qf, __nv_bfloat16* __restrict__ q_out,
+                                           const int32_t* __restrict__ pos, const int32_t* __restrict__ block_table,
+                                           int max_blocks, int H, int nope, int R, int P, float eps, float theta,
+                                           __nv_bfloat16* __restrict__ cache, __nv_bfloat16* __restrict__ q_rope) {
   pdl_wait();
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int p = pos[b];
-  const float* kv = kv_a + (int64_t)b * (R + P);
+  const float* kv = kv_a + (int64_t)b * ld_kv;
   float ss = 0.0f;
   for (int i = threadIdx.x; i < R; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(kv[i], kv[i]));
   const float mean2 = __fdiv_rn(block_sum(ss, red), (float)R);
@@ -101,10 +102,25 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, const
     row[R + 2 * k + 1] = __float2bfloat16_rn(x1);
   }
   const int qh = nope + P;
+  if (qf != nullptr) {
+    // fp32 query: its nope parts go out as the bf16 query of the absorb GEMM
+    for (int idx = threadIdx.x; idx < H * nope; idx += blockDim.x) {
+      const int h = idx / nope, i = idx % nope;
+      q_out[(int64_t)b * H * qh + (int64_t)h * qh + i] = __float2bfloat16_rn(qf[(int64_t)b * ld_qf + h * qh + i]);
+    }
+  }
   for (int idx = threadIdx.x; idx < H * (P / 2); idx += blockDim.x) {
     const int h = idx / (P / 2), k = idx % (P / 2);
-    const __nv_bfloat16* src = q + (int64_t)b * H * qh + (int64_t)h * qh + nope + 2 * k;
-    float x0 = __bfloat162float(src[0]), x1 = __bfloat162float(src[1]);
+    float x0, x1;
+    if (qf != nullptr) {
+      const float* src = qf + (int64_t)b * ld_qf + (int64_t)h * qh + nope + 2 * k;
+      x0 = src[0];
+      x1 = src[1];
+    } else {
+      const __nv_bfloat16* src = q + (int64_t)b * H * qh + (int64_t)h * qh + nope + 2 * k;
+      x0 = __bfloat162float(src[0]);
+      x1 = __bfloat162float(src[1]);
+    }
     rope_pair(x0, x1, k, P, p, theta);
     __nv_bfloat16* dst = q_rope + ((int64_t)b * H + h) * P + 2 * k;
     dst[0] = __float2bfloat16_rn(x0);
@@ -201,13 +217,11 @@ __device__ __forceinline__ void warp_argmax(float& v, int& idx) {
 // their top-2 biased scores, the top topk_group groups kept, top-k experts of
 // the kept groups by biased score, weights = unbiased sigmoid scores of the
 // chosen experts, normalised when norm_topk, times routed_scale.
-__global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
-                             int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
-                             int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra) {
-  pdl_wait();
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const float* lg = logits + (int64_t)t * E;
+// One warp routes one token: lg its E logits (global or shared memory); the
+// k picks and weights, then n_extra always-on groups, go to ids_row / w_row.
+__device__ __forceinline__ void route_token(const float* lg, const float* __restrict__ bias, int E, int k, int scoring,
+                                            int n_group, int topk_group, int norm_topk, float routed_scale,
+                                            int32_t* ids_row, float* w_row, int n_extra, int lane) {
   float sel[kMaxExpertsPerLane], val[kMaxExpertsPerLane];  // selection key, weight source
 #pragma unroll
   for (int j = 0; j < kMaxExpertsPerLane; ++j) {
@@ -317,17 +331,76 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
     wsum = __fadd_rn(wsum, wv);
   }
   if (lane == 0) {
-    const int kk = k + n_extra;  // row stride: the k routed picks, then n_extra always-on groups
+    // the k routed picks, then n_extra always-on groups
     for (int r = 0; r < k; ++r) {
       float wv = wsel[r];
       if (norm_topk && wsum > 0.0f) wv = __fdiv_rn(wv, wsum);
-      ids[(int64_t)t * kk + r] = isel[r];
-      weights[(int64_t)t * kk + r] = __fmul_rn(wv, routed_scale);
+      ids_row[r] = isel[r];
+      w_row[r] = __fmul_rn(wv, routed_scale);
     }
     for (int j = 0; j < n_extra; ++j) {
-      ids[(int64_t)t * kk + k + j] = E + j;
-      weights[(int64_t)t * kk + k + j] = 1.0f;
+      ids_row[k + j] = E + j;
+      w_row[k + j] = 1.0f;
     }
+  }
+}
+
+__global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
+                             int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
+                             int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra) {
+  pdl_wait();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int kk = k + n_extra;
+  route_token(logits + (int64_t)t * E, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale,
+              ids + (int64_t)t * kk, weights + (int64_t)t * kk, n_extra, lane);
+}
+
+// Post-attention RMSNorm, router logits and routing of one token per CTA (256
+// threads): the normalised row goes out as bf16 (the experts' input) and
+// stays in shared memory as fp32 for the E router dot products (one warp per
+// expert, the lane striding of router_logits_kernel), then warp 0 routes.
+// Replaces rmsnorm_rows + router_logits + route for decode batches.
+__global__ void __launch_bounds__(256) moe_front_kernel(const float* __restrict__ h, const float* __restrict__ w_norm,
+                                                        int D, float eps, const float* __restrict__ w_router, int E,
+                                                        const float* __restrict__ bias, int k, int scoring,
+                                                        int n_group, int topk_group, int norm_topk,
+                                                        float routed_scale, int n_extra,
+                                                        __nv_bfloat16* __restrict__ xn, int32_t* __restrict__ ids,
+                                                        float* __restrict__ weights) {
+  pdl_wait();
+  extern __shared__ float xs[];  // [D] normalised row, then [E] logits
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const float* hr = h + (int64_t)t * D;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(hr[i], hr[i]));
+  const float mean2 = __fdiv_rn(block_sum(ss, red), (float)D);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(hr[i], inv), w_norm[i]);
+    xn[(int64_t)t * D + i] = __float2bfloat16_rn(v);
+    xs[i] = v;
+  }
+  __syncthreads();
+  float* lg = xs + D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = warp; e < E; e += blockDim.x >> 5) {
+    const float* wr = w_router + (int64_t)e * D;
+    float acc = 0.0f;
+    for (int i = lane * 4; i < D; i += 128) {
+      const float4 a = *reinterpret_cast<const float4*>(xs + i);
+      const float4 b = *reinterpret_cast<const float4*>(wr + i);
+      acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) lg[e] = acc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int kk = k + n_extra;
+    route_token(lg, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids + (int64_t)t * kk,
+                weights + (int64_t)t * kk, n_extra, lane);
   }
 }
 
@@ -495,14 +568,26 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, i
 // moe_step's accumulation (ops.cpp:133-145) followed by the residual add
 // (model.cpp:209).
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ dest, int k, int D,
-                                   const float* __restrict__ shared, float* __restrict__ h) {
+                                   const float* __restrict__ shared, float* __restrict__ h,
+                                   const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next) {
   pdl_wait();
+  __shared__ float red[32];
   const int t = blockIdx.x;
+  float ss = 0.0f;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     float acc = 0.0f;
     for (int j = 0; j < k; ++j) acc = __fadd_rn(acc, y[(int64_t)dest[t * k + j] * D + i]);
     if (shared) acc = __fadd_rn(acc, shared[(int64_t)t * D + i]);
-    h[(int64_t)t * D + i] = __fadd_rn(h[(int64_t)t * D + i], acc);
+    const float hv = __fadd_rn(h[(int64_t)t * D + i], acc);
+    h[(int64_t)t * D + i] = hv;
+    ss = __fadd_rn(ss, __fmul_rn(hv, hv));
+  }
+  if (w_next != nullptr) {
+    // the next RMSNorm of this row (the same arithmetic as rmsnorm_rows_kernel)
+    const float mean2 = __fdiv_rn(block_sum(ss, red), (float)D);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+      xn_next[(int64_t)t * D + i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(h[(int64_t)t * D + i], inv), w_next[i]));
   }
 }
 
@@ -566,13 +651,14 @@ int rmsnorm_rows(dsb_ctx* ctx, const float* x, int64_t ldx, const float* w, int 
   return launched(ctx);
 }
 
-int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const float* w_norm, const void* q, const int32_t* pos,
-                        const int32_t* block_table, int max_blocks, int B, int H, int nope, int R, int P, float eps,
-                        float theta, void* cache, void* q_rope) {
-  launch_pdl(kv_norm_rope_append_kernel, B, 128, 0, ctx->stream, kv_a, w_norm, static_cast<const __nv_bfloat16*>(q), pos,
-                                                         block_table, max_blocks, H, nope, R, P, eps, theta,
-                                                         static_cast<__nv_bfloat16*>(cache),
-                                                         static_cast<__nv_bfloat16*>(q_rope));
+int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, int64_t ld_kv, const float* w_norm, const void* q,
+                        const float* qf, int64_t ld_qf, void* q_out, const int32_t* pos, const int32_t* block_table,
+                        int max_blocks, int B, int H, int nope, int R, int P, float eps, float theta, void* cache,
+                        void* q_rope) {
+  launch_pdl(kv_norm_rope_append_kernel, B, 128, 0, ctx->stream, kv_a, ld_kv, w_norm,
+             static_cast<const __nv_bfloat16*>(q), qf, ld_qf, static_cast<__nv_bfloat16*>(q_out), pos, block_table,
+             max_blocks, H, nope, R, P, eps, theta, static_cast<__nv_bfloat16*>(cache),
+             static_cast<__nv_bfloat16*>(q_rope));
   return launched(ctx);
 }
 
@@ -584,6 +670,22 @@ int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, in
     return launched(ctx);
   }
   launch_pdl(router_logits_kernel, (warps + 7) / 8, 256, 0, ctx->stream, x, w, T, D, E, logits);
+  return launched(ctx);
+}
+
+int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
+              int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
+              float routed_scale, int n_extra, void* xn, int32_t* ids, float* weights) {
+  const size_t smem = (size_t)(D + E) * sizeof(float);
+  if (smem > 48 * 1024) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(moe_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      attr_set = true;
+    }
+  }
+  launch_pdl(moe_front_kernel, T, 256, smem, ctx->stream, h, w_norm, D, eps, w_router, E, bias, k, scoring, n_group,
+             topk_group, norm_topk, routed_scale, n_extra, static_cast<__nv_bfloat16*>(xn), ids, weights);
   return launched(ctx);
 }
 
@@ -626,8 +728,9 @@ int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pai
 }
 
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
-                float* h) {
-  launch_pdl(moe_combine_kernel, T, 256, 0, ctx->stream, y, dest, k, D, shared, h);
+                float* h, const float* w_next, float eps, void* xn_next) {
+  launch_pdl(moe_combine_kernel, T, 256, 0, ctx->stream, y, dest, k, D, shared, h, w_next, eps,
+             static_cast<__nv_bfloat16*>(xn_next));
   return launched(ctx);
 }
 
@@ -661,8 +764,8 @@ extern "C" int dsb_kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const fl
   if (kv_a == nullptr || w_norm == nullptr || q == nullptr || positions == nullptr || block_table == nullptr ||
       cache == nullptr || q_rope == nullptr || B <= 0 || H <= 0 || R <= 0 || P <= 0 || (P % 2) != 0)
     return dsb::fail(ctx, DSB_EINVAL, "dsb_kv_norm_rope_append: bad arguments");
-  return dsb::kv_norm_rope_append(ctx, kv_a, w_norm, q, positions, block_table, max_blocks, B, H, nope, R, P, eps,
-                                  theta, cache, q_rope);
+  return dsb::kv_norm_rope_append(ctx, kv_a, R + P, w_norm, q, nullptr, 0, nullptr, positions, block_table,
+                                  max_blocks, B, H, nope, R, P, eps, theta, cache, q_rope);
 }
 
 extern "C" int dsb_router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, int E, float* logits) {
