@@ -329,9 +329,9 @@ def run_mla_ours(args):
 
 
 def model_cfg(args):
-    from deepseek_cpp_infer_b200.workloads import V2_LITE
+    from deepseek_cpp_infer_b200.workloads import V2_LITE, V3
 
-    cfg = dict(V2_LITE)
+    cfg = dict(V3 if args.workload == "v3" else V2_LITE)
     if args.layers:
         cfg["num_hidden_layers"] = args.layers
     return cfg
@@ -346,11 +346,14 @@ def step_bytes(cfg, B, ctx_len, world=1):
     nope, v, L = cfg["qk_nope_head_dim"], cfg["v_head_dim"], cfg["num_hidden_layers"]
     E, k, I = cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
     Is, Id, V = cfg["n_shared_experts"] * I, cfg["intermediate_size"], cfg["vocab_size"]
-    attn = (H * (nope + P) * D + (R + P) * D + H * R * nope + H * v * R + D * H * v) * 2
+    ql = cfg.get("q_lora_rank", 0)
+    wb = 1 + 4 / (128 * 128) if cfg.get("weights_fp8") else 2  # bytes per projection / FFN weight (+ FP8 scales)
+    q_proj = (ql * D + H * (nope + P) * ql) if ql else H * (nope + P) * D
+    attn = (q_proj + (R + P) * D + D * H * v) * wb + (H * R * nope + H * v * R) * 2  # absorbed W_UK / W_UV in bf16
     dense_layers = min(cfg["first_k_dense_replace"], L)
     touched = E * (1 - (1 - k / E) ** (world * B)) / world
-    moe = touched * 3 * I * D * 2 + 3 * Is * D * 2 + E * D * 4
-    w = L * attn + dense_layers * 3 * Id * D * 2 + (L - dense_layers) * moe + V * D * 2
+    moe = touched * 3 * I * D * wb + 3 * Is * D * wb + E * D * 4
+    w = L * attn + dense_layers * 3 * Id * D * wb + (L - dense_layers) * moe + V * D * 2
     kv = L * B * ctx_len * (R + P) * 2
     return int(w + kv), int(w), int(kv), touched
 
@@ -394,6 +397,52 @@ def time_expert_gemm(ctx, stream, cfg, B, steps):
     touched = int((counts > 0).sum())
     nbytes = touched * 2 * I * D * 2 + B * kk * D * 2 + B * kk * I * 2
     del w
+    return ms, nbytes, touched
+
+
+def time_expert_gemm_fp8(ctx, stream, cfg, B, world, steps):
+    """V3 shape: this rank's FP8 expert gate|up GEMM of one MoE layer in
+    isolation -- E/world routed groups receiving the world*B tokens' picks of
+    them under uniform routing, plus the shared group with this rank's B
+    tokens -- timed with CUDA events on the context stream."""
+    import numpy as np
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+    from deepseek_cpp_infer_b200.workloads import MoeFp8Weights
+
+    D, E, k, I = cfg["hidden_size"], cfg["n_routed_experts"], cfg["num_experts_per_tok"], cfg["moe_intermediate_size"]
+    ns, EL = cfg["n_shared_experts"], E // world
+    rng = np.random.default_rng(11)
+    picks = np.stack([rng.choice(E, k, replace=False) for _ in range(world * B)]).ravel()
+    counts = np.concatenate([np.bincount(picks, minlength=E)[:EL], [B] * ns])
+    G = EL + ns
+    offs = torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).cuda()
+    T = int(counts.sum())
+    layer = MoeFp8Weights(ctx, EL, ns, D, I, seed=12)
+    xq = torch.randint(0, 0x7E, (T, D), dtype=torch.uint8, device="cuda")
+    sx = torch.full((T, D // 128), 1e-2, device="cuda")
+    y = torch.empty(T, I, dtype=torch.bfloat16, device="cuda")
+
+    def launch():
+        ctx.linear_fp8(layer.gate_up.view(G * 2 * I, D), layer.gate_up_scale.view(-1, D // 128), xq, sx, y,
+                       M=2 * I, K=D, G=G, scale_rows=2, tok_offsets=offs, max_tokens_per_group=B,
+                       epilogue=dsb.EPI_SILU_GATE)
+
+    for _ in range(5):
+        launch()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(steps, 20)
+    e0.record(stream)
+    for _ in range(n):
+        launch()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    touched = int((counts > 0).sum())
+    nbytes = touched * (2 * I * D + (2 * I // 128) * 2 * (D // 128) * 4) + T * D + T * I * 2
+    del layer
     return ms, nbytes, touched
 
 
@@ -448,8 +497,16 @@ def run_model_ours(args):
     seqs = [kv.alloc_seq() for _ in range(B)]
     prompts = np.random.default_rng(3 + 1000 * rank).integers(0, cfg["vocab_size"], (B, P)).astype(np.int32)
     t0 = time.time()
-    for i in range(P):  # token-serial prefill, as the reference's forward() does
-        greedy, _ = dsb.decode_step(ctx, model, kv, seqs, prompts[:, i])
+    v3 = args.workload == "v3"
+    if v3:
+        # a 4096-token context per sequence: synthetic N(0,1) latents in every layer's cache rows
+        # (decode reads the same bytes as after a real prefill), then one token each
+        for j, sq in enumerate(seqs):
+            kv.fill_random(sq, P - 1, seed=4 + 1000 * rank + j)
+        greedy, _ = dsb.decode_step(ctx, model, kv, seqs, prompts[:, -1])
+    else:
+        for i in range(P):  # token-serial prefill, as the reference's forward() does
+            greedy, _ = dsb.decode_step(ctx, model, kv, seqs, prompts[:, i])
     prefill_s = time.time() - t0
     nxt = greedy
 
@@ -486,10 +543,13 @@ def run_model_ours(args):
     barrier()
     ms_e2e = max_over_ranks(timed(args.steps, want_logits=True))
     # the dominant kernel alone, for the roofline line
-    g_ms, g_bytes, g_touched = time_expert_gemm(ctx, stream, cfg, B, args.steps)
+    if v3:
+        g_ms, g_bytes, g_touched = time_expert_gemm_fp8(ctx, stream, cfg, B, world, args.steps)
+    else:
+        g_ms, g_bytes, g_touched = time_expert_gemm(ctx, stream, cfg, B, args.steps)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not v3:
         cpu = model_cpu_baseline(cfg, ctx_len, cores=1)
 
     if rank == 0:
@@ -498,27 +558,35 @@ def run_model_ours(args):
         line = {
             "metric": METRIC, "value": world * B / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": warm, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: random-init N(0,0.02) bf16 weights (seed 3), uniform random prompt ids",
+            "vs_baseline": None, "dtype": "e4m3 weights, bf16 activations" if v3 else "bf16",
+            "data": ("synthetic: random-init N(0,0.02) weights quantised to e4m3 with 128x128 scales (seed 3), "
+                     "N(0,1) latent cache rows for the context" if v3 else
+                     "synthetic: random-init N(0,0.02) bf16 weights (seed 3), uniform random prompt ids"),
             "config": {
-                "workload": f"DeepSeek-V2-Lite-shaped batched greedy decode: {cfg['num_hidden_layers']} layers, hidden "
-                            f"2048, 16 heads, kv_lora_rank 512, 1 dense + {cfg['num_hidden_layers'] - 1} MoE layers "
-                            f"(64 experts top-6 softmax, 2 shared, moe_inter 1408), vocab 102400; B={B} per GPU, "
-                            f"{P}-token prompts, step = one token for every sequence",
+                "workload": (f"DeepSeek-V3-shaped batched greedy decode: {cfg['num_hidden_layers']} layers, hidden 7168, "
+                             f"128 heads, q_lora 1536, kv_lora_rank 512, 3 dense (FFN 18432) + "
+                             f"{cfg['num_hidden_layers'] - 3} MoE layers (256 experts top-8 sigmoid grouped, 1 shared, "
+                             f"moe_inter 2048), FP8 e4m3 block-scaled projections / FFN / experts, vocab 129280; "
+                             f"B={B} per GPU, {P}-token context, step = one token for every sequence" if v3 else
+                             f"DeepSeek-V2-Lite-shaped batched greedy decode: {cfg['num_hidden_layers']} layers, hidden "
+                             f"2048, 16 heads, kv_lora_rank 512, 1 dense + {cfg['num_hidden_layers'] - 1} MoE layers "
+                             f"(64 experts top-6 softmax, 2 shared, moe_inter 1408), vocab 102400; B={B} per GPU, "
+                             f"{P}-token prompts, step = one token for every sequence"),
                 "global_batch": world * B, "seq_len": ctx_len,
                 "parallelism": "single GPU" if world == 1 else
                                f"ep{world} routed experts (peer-memory dispatch/combine) + dp{world} attention",
                 "step_bytes": tot, "weight_bytes_per_step": wbytes, "kv_bytes_per_step": kvbytes,
                 "experts_touched_per_layer": round(touched, 1), "prefill_s": round(prefill_s, 2),
-                "l2": "every step streams ~30 GB of weights, far above the 126 MB L2",
+                "l2": f"every step streams {wbytes / 1e9:.1f} GB of weights per GPU, far above the 126 MB L2",
                 "step_roofline_frac": tot / (ms_max * 1e-3) / 1e9 / peak,
             },
             "roofline": {"bound": "hbm", "achieved": g_bytes / (g_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
-                         "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak, "traffic": EXPERT_GEMM_NCU_TRAFFIC,
+                         "frac": g_bytes / (g_ms * 1e-3) / 1e9 / peak,
+                         "traffic": None if v3 else EXPERT_GEMM_NCU_TRAFFIC,
                          "peak_kind": peak_kind,
-                         "kernel": "gemm_bf16_kernel (expert gate|up: routed + shared groups, SiLU epilogue)",
-                         "note": f"{g_touched} of {cfg['n_routed_experts'] + cfg['n_shared_experts']} expert groups' "
-                                 f"2816x2048 bf16 tiles + activations per launch / "
+                         "kernel": ("gemm_fp8_kernel (this rank's expert gate|up groups, SiLU epilogue)" if v3 else
+                                    "gemm_bf16_kernel (expert gate|up: routed + shared groups, SiLU epilogue)"),
+                         "note": f"{g_touched} expert groups' gate|up weights + activations per launch / "
                                  f"CUDA-event launch time ({g_ms * 1e3:.1f} us)"},
             "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": B * 4 * (2 + max_blocks),
                     "d2h_bytes_per_step": B * 4 + B * cfg["vocab_size"] * 4},
@@ -834,7 +902,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "mla", "expert-gemm", "moe-fp8"])
+    ap.add_argument("--workload", default="model", choices=["model", "v3", "mla", "expert-gemm", "moe-fp8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
@@ -851,6 +919,14 @@ def main():
     elif args.workload == "mla":
         args.batch = args.batch or 64
         run_mla_reference(args) if args.impl == "reference" else run_mla_ours(args)
+    elif args.workload == "v3":
+        args.batch = args.batch or 32
+        args.prompt = 4096 if args.prompt == 512 else args.prompt
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no FP8 dtype (safetensors parser: "
+                              "F32/F16/BF16 only) and no multi-GPU path for the 671B-parameter V3 shape"}))
+        else:
+            run_model_ours(args)
     else:
         args.batch = args.batch or 32
         run_model_reference(args) if args.impl == "reference" else run_model_ours(args)

@@ -82,7 +82,7 @@ class MoeFp8Layer(ctypes.Structure):
     ]
 
 
-DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+DTYPE_F32, DTYPE_BF16, DTYPE_F16, DTYPE_F8E4M3 = 0, 1, 2, 3
 STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream as a stream handle
 
 
@@ -97,7 +97,8 @@ class ModelConfig(ctypes.Structure):
             "num_experts_per_tok", "first_k_dense_replace", "q_lora_rank", "kv_lora_rank", "qk_nope_head_dim",
             "qk_rope_head_dim", "v_head_dim", "scoring_func", "n_group", "topk_group", "norm_topk_prob",
         )
-    ] + [("routed_scaling_factor", ctypes.c_float), ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+    ] + [("routed_scaling_factor", ctypes.c_float), ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+         ("weights_fp8", ctypes.c_int)]
 
 
 # (name, restype, argtypes) for every function of include/dsb/dsb.h
@@ -132,7 +133,11 @@ _PROTOS = [
     ("dsb_ep_combine", ctypes.c_int, [_vp, _vp, _i64, _ci, _vp, _vp, _ci, _vp]),
     ("dsb_ep_destroy", ctypes.c_int, [_vp]),
     ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
+    ("dsb_kvcache_fill_random", ctypes.c_int, [_vp, _ci, _ci, ctypes.c_uint64, ctypes.c_float]),
+    ("dsb_generate", ctypes.c_int, [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, _vp, _vp]),
     ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
+    ("dsb_kvcache_fill_random", ctypes.c_int, [_vp, _ci, _ci, ctypes.c_uint64, ctypes.c_float]),
+    ("dsb_generate", ctypes.c_int, [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, _vp, _vp]),
     ("dsb_moe_ffn_fp8", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(MoeFp8Layer), _vp, _i64, _ci, _ci, _vp, _vp, _vp]),
     ("dsb_rmsnorm", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _cf, _vp, _i64, _vp, _i64]),
@@ -434,11 +439,11 @@ class Model:
         self.h = h
 
     def set_tensor(self, name: str, array):
-        """Upload a host numpy array (float32, or uint16 holding bf16 bits)."""
+        """Upload a host numpy array (float32, uint16 holding bf16 bits, or uint8 holding e4m3 bytes)."""
         import numpy as np
 
         a = np.ascontiguousarray(array)
-        dt = DTYPE_BF16 if a.dtype == np.uint16 else DTYPE_F32
+        dt = DTYPE_BF16 if a.dtype == np.uint16 else DTYPE_F8E4M3 if a.dtype == np.uint8 else DTYPE_F32
         if dt == DTYPE_F32:
             a = a.astype(np.float32, copy=False)
         shape = (ctypes.c_int64 * a.ndim)(*a.shape)
@@ -558,6 +563,10 @@ class KVCache:
         self.ctx._check(self.ctx._l.dsb_kvcache_alloc_seq(self.h, ctypes.byref(s)))
         return s.value
 
+    def fill_random(self, seq: int, n_tokens: int, seed: int = 0, stddev: float = 1.0):
+        """dsb_kvcache_fill_random: n_tokens synthetic cache positions for `seq`."""
+        self.ctx._check(self.ctx._l.dsb_kvcache_fill_random(self.h, seq, n_tokens, seed, float(stddev)))
+
     def free_seq(self, seq: int):
         self.ctx._check(self.ctx._l.dsb_kvcache_free_seq(self.h, seq))
 
@@ -598,3 +607,18 @@ def decode_step(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_l
     ctx._check(ctx._l.dsb_decode_step(ctx.h, model.h, kv.h, sids, toks, B,
                                       logits.ctypes.data if want_logits else None, greedy))
     return np.array(greedy[:], np.int32), logits
+
+
+def generate(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, max_new_tokens: int, eos_id: int = -1):
+    """dsb_generate: greedy continuation of every prompt (lists of ids); returns one id list per sequence."""
+    import numpy as np
+
+    B = len(prompts)
+    toks = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int32) for p in prompts]))
+    offs = np.ascontiguousarray(np.concatenate([[0], np.cumsum([len(p) for p in prompts])]).astype(np.int32))
+    sid = np.ascontiguousarray(np.asarray(seq_ids, np.int32))
+    out = np.zeros((B, max(1, max_new_tokens)), np.int32)
+    cnt = np.zeros(B, np.int32)
+    ctx._check(ctx._l.dsb_generate(ctx.h, model.h, kv.h, sid.ctypes.data, B, toks.ctypes.data, offs.ctypes.data,
+                                   max_new_tokens, eos_id, out.ctypes.data, cnt.ctypes.data))
+    return [out[b, :cnt[b]].tolist() for b in range(B)]

@@ -147,7 +147,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    int32_t* __restrict__ recv_offsets, int* __restrict__ ticket, uint32_t epoch,
                                    int* status) {
   pdl_wait();
-  __shared__ int32_t my_off[kMaxWorld * 64];  // [dst][el]: this rank's first row in dst's buffer
+  __shared__ int32_t my_off[256];  // [dst][el] (world * E_local = E <= 256): this rank's first row in dst's buffer
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {
@@ -318,9 +318,9 @@ extern "C" int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, i
   if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
   *out = nullptr;
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || n_experts <= 0 || n_experts % world ||
-      n_experts > 256 || n_experts / world > 64 || hidden <= 0 || hidden % 8 || top_k <= 0 || max_tokens <= 0 ||
+      n_experts > 256 || hidden <= 0 || hidden % 8 || top_k <= 0 || max_tokens <= 0 ||
       (int64_t)world * max_tokens * top_k >= (1 << 24))
-    return fail(ctx, DSB_EINVAL, "dsb_ep_create: bad sizes (world <= 8, E divisible by world, E/world <= 64)");
+    return fail(ctx, DSB_EINVAL, "dsb_ep_create: bad sizes (world <= 8, E <= 256 and divisible by world)");
   auto* ep = new dsb_ep();
   ep->ctx = ctx;
   ep->E = n_experts;

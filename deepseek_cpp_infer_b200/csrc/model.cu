@@ -55,6 +55,20 @@ struct dsb_model {
     int n_shared = 0;                // shared groups after the routed experts
     uint8_t shared_seen = 0;         // bit 0 gate, 1 up, 2 down uploaded
     uint8_t seen_gate = 0, seen_up = 0;  // dense gate-up halves uploaded
+    // Block-scaled FP8 variants (e4m3 bytes + fp32 scale per 128x128 block, in
+    // the dsb_linear_fp8 layouts); a matrix runs in FP8 when its q8 is set.
+    //   qkv8   [Mq + R + P, D], scales [ceil(rows/128)][D/128] (q|kv_a fused as w_qkv)
+    //   qb8    [H*(nope+P), q_lora];  o8 [D, H*v];  down8 [D, I]
+    //   gu8    [2I, D] rows interleaved, scales [2I/128][2][D/128] (scale_rows 2)
+    //   e_gu8 / e_down8: per group (routed then shared) as gu8 / down8
+    uint8_t *qkv8 = nullptr, *qb8 = nullptr, *o8 = nullptr, *gu8 = nullptr, *down8 = nullptr;
+    uint8_t *e_gu8 = nullptr, *e_down8 = nullptr;
+    float *qkv8_s = nullptr, *qb8_s = nullptr, *o8_s = nullptr, *gu8_s = nullptr, *down8_s = nullptr;
+    float *e_gu8_s = nullptr, *e_down8_s = nullptr;
+    std::vector<float> gu8_s_host, e_gu8_s_host;  // fused gate|up scales, assembled on the host
+    std::vector<uint8_t> kvb8;                    // FP8 kv_b_proj waiting for its scales (or the reverse)
+    std::vector<float> kvb8_s;
+    int64_t fp8_weights = 0, fp8_scales = 0;      // FP8 weight / scale tensors received
   };
   dsb_ctx* ctx = nullptr;
   dsb_model_config cfg{};
@@ -127,6 +141,17 @@ std::vector<float> to_f32(const void* src, int dtype, int64_t n) {
   std::vector<float> out(static_cast<size_t>(n));
   for (int64_t i = 0; i < n; ++i) out[i] = host_to_f32(src, dtype, i);
   return out;
+}
+
+// e4m3 (1 sign, 4 exponent bits with bias 7, 3 mantissa bits, no infinities,
+// S.1111.111 = NaN) to float, by its bit definition.
+float e4m3_to_f32(uint8_t v) {
+  const int e = (v >> 3) & 0xF, mant = v & 7;
+  float mag;
+  if (e == 0xF && mant == 7) return NAN;
+  if (e == 0) mag = std::ldexp((float)mant, -9);
+  else mag = std::ldexp(1.0f + mant / 8.0f, e - 7);
+  return (v & 0x80) ? -mag : mag;
 }
 
 template <class T>
@@ -237,6 +262,38 @@ int rand_f32(dsb_model* m, float** p, int64_t n, uint64_t seed, float stddev, fl
   return DSB_OK;
 }
 
+// Scale rows of one half (0 gate, 1 up) of a row-interleaved gate|up matrix:
+// tile j holds rows 64j..64j+63 of each half, i.e. scale row j/2 of that half.
+__global__ void gate_up_scale_kernel(const float* __restrict__ src, int T2, int KB, int h, float* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T2 * KB) return;
+  const int j = i / KB, kb = i % KB;
+  dst[((size_t)j * 2 + h) * KB + kb] = src[(size_t)(j / 2) * KB + kb];
+}
+
+// FP8 random init: N(0, stddev) bf16 in `tmp`, quantised per 128x128 block
+// into q / sc (the dsb_quant_weight_128x128 rule a checkpoint would carry).
+int rand_fp8(dsb_model* m, uint8_t* q, float* sc, int64_t rows, int64_t cols, uint64_t seed, float stddev, bf16* tmp) {
+  init_normal_bf16_kernel<<<1184, 256, 0, m->ctx->stream>>>(tmp, rows * cols, seed, stddev);
+  DSB_CUDA_TRY(m->ctx, cudaGetLastError());
+  return dsb_quant_weight_128x128(m->ctx, tmp, DSB_DTYPE_BF16, rows, cols, q, sc);
+}
+
+// Gate and up halves quantised separately (as checkpoint matrices), then
+// interleaved by row with their scales arranged for scale_rows 2.
+int rand_fp8_gate_up(dsb_model* m, uint8_t* q, float* sc, int64_t I, int64_t D, uint64_t seed, float stddev, bf16* tmp,
+                     uint8_t* tmp8, float* tmps) {
+  const int KB = (int)((D + 127) / 128), T2 = (int)(2 * I / 128);
+  for (int h = 0; h < 2; ++h) {
+    int rc = rand_fp8(m, tmp8, tmps, I, D, seed * 2 + h, stddev, tmp);
+    if (rc != DSB_OK) return rc;
+    DSB_CUDA_TRY(m->ctx, cudaMemcpy2DAsync(q + h * D, 2 * D, tmp8, D, D, I, cudaMemcpyDeviceToDevice, m->ctx->stream));
+    gate_up_scale_kernel<<<(T2 * KB + 255) / 256, 256, 0, m->ctx->stream>>>(tmps, T2, KB, h, sc);
+    DSB_CUDA_TRY(m->ctx, cudaGetLastError());
+  }
+  return DSB_OK;
+}
+
 // ------------------------------------------------------------- decode step
 
 struct StepBuffers {
@@ -278,6 +335,23 @@ using namespace dsb;
 
 namespace {
 
+// kv_b_proj [H*(nope+v), R] (bf16 bits): rows per head [nope rows of W_UK |
+// v rows of W_UV] (mla.cpp:99-102), kept as per-head W_UK^T [R, nope] and W_UV.
+int upload_kv_b(dsb_model* m, dsb_model::Layer& L, const std::vector<uint16_t>& b) {
+  const dsb_model_config& c = m->cfg;
+  const int H = c.num_attention_heads, R = c.kv_lora_rank, nope = c.qk_nope_head_dim, v = c.v_head_dim;
+  std::vector<uint16_t> uk_t((size_t)H * R * nope), uv((size_t)H * v * R);
+  for (int h = 0; h < H; ++h) {
+    const uint16_t* base = b.data() + (size_t)h * (nope + v) * R;
+    for (int i = 0; i < nope; ++i)
+      for (int r = 0; r < R; ++r) uk_t[((size_t)h * R + r) * nope + i] = base[(size_t)i * R + r];
+    std::memcpy(uv.data() + (size_t)h * v * R, base + (size_t)nope * R, (size_t)v * R * 2);
+  }
+  int rc = upload(m, &L.w_uk_t, uk_t.data(), uk_t.size());
+  if (rc != DSB_OK) return rc;
+  return upload(m, &L.w_uv, uv.data(), uv.size());
+}
+
 // Allocate a layer's stacked expert matrices: E routed + n_shared groups of
 // moe_intermediate_size (from the config, so tensors may arrive in any order).
 int ensure_experts(dsb_model* m, dsb_model::Layer& L) {
@@ -291,6 +365,168 @@ int ensure_experts(dsb_model* m, dsb_model::Layer& L) {
   int rc = dev_alloc(m, &L.e_gu, (size_t)G * 2 * I * D);
   if (rc == DSB_OK) rc = dev_alloc(m, &L.e_down, (size_t)G * D * I);
   return rc;
+}
+
+int cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// Storage of one FP8 matrix (G groups of rows x cols, 128x128 scale blocks;
+// gate_up: rows interleaved from gate / up halves with scale_rows 2).
+int ensure_fp8(dsb_model* m, uint8_t** q, float** sc, int64_t G, int64_t rows, int64_t cols, bool gate_up) {
+  if (*q != nullptr) return DSB_OK;
+  int rc = dev_alloc(m, q, (size_t)(G * rows * cols));
+  const int64_t srows = gate_up ? (rows / 128) * 2 : cdiv(rows, 128);
+  if (rc == DSB_OK) rc = dev_alloc(m, sc, (size_t)(G * srows * cdiv(cols, 128)));
+  return rc;
+}
+
+// One tensor of a block-scaled FP8 checkpoint: an e4m3 weight (dtype
+// DSB_DTYPE_F8E4M3) or its "<weight>_scale_inv" fp32 scales, routed to the
+// layer's FP8 storage.  `base` is the weight's name within the layer.
+int set_fp8(dsb_model* m, dsb_model::Layer& L, const std::string& base, bool is_scale, int dtype,
+            const int64_t* shape, int ndim, const void* data, const char* cname) {
+  dsb_ctx* ctx = m->ctx;
+  const dsb_model_config& c = m->cfg;
+  const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
+  const int nope = c.qk_nope_head_dim, v = c.v_head_dim, QH = H * (nope + P);
+  const int64_t Mq = c.q_lora_rank > 0 ? c.q_lora_rank : QH;
+  if (ndim != 2) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s must be 2-D", cname);
+  if (is_scale && dtype == DSB_DTYPE_F8E4M3)
+    return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s must be a float tensor", cname);
+  const int64_t n = shape[0] * shape[1];
+  std::vector<float> sf;
+  if (is_scale) sf = to_f32(data, dtype, n);
+  const uint8_t* w8 = static_cast<const uint8_t*>(data);
+  auto shape_is = [&](int64_t rows, int64_t cols) {
+    return is_scale ? (shape[0] == cdiv(rows, 128) && shape[1] == cdiv(cols, 128)) : (shape[0] == rows && shape[1] == cols);
+  };
+  auto bad = [&]() { return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s has an unexpected shape", cname); };
+  auto put = [&](void* dst, const void* src, size_t bytes) -> int {
+    DSB_CUDA_TRY(ctx, cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    return DSB_OK;
+  };
+  (is_scale ? L.fp8_scales : L.fp8_weights)++;
+  // plain matrix (group g of G): weight rows, or its [rows/128][cols/128] scales
+  auto plain = [&](uint8_t** q, float** sc, int64_t G, int64_t g, int64_t rows, int64_t cols) -> int {
+    if (!shape_is(rows, cols)) return bad();
+    int rc = ensure_fp8(m, q, sc, G, rows, cols, false);
+    if (rc != DSB_OK) return rc;
+    if (is_scale) return put(*sc + g * n, sf.data(), n * 4);
+    return put(*q + g * rows * cols, w8, (size_t)n);
+  };
+  // half h (0 gate, 1 up) of a row-interleaved gate|up matrix (group g of G, I rows per half)
+  auto gate_up = [&](uint8_t** q, float** sc, std::vector<float>& shadow, int64_t G, int64_t g, int64_t I, int h,
+                     const float* sfp, const uint8_t* wp, int64_t src_row_pitch) -> int {
+    if (I % 128) return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_set_tensor: FP8 intermediate size must be a multiple of 128");
+    int rc = ensure_fp8(m, q, sc, G, 2 * I, D, true);
+    if (rc != DSB_OK) return rc;
+    const int64_t KB = cdiv(D, 128), T2 = 2 * I / 128;
+    if (is_scale) {
+      // tile j holds rows 64j..64j+63 of each half: scale row j/2 of that half
+      if (shadow.empty()) shadow.assign((size_t)(G * T2 * 2 * KB), 0.0f);
+      for (int64_t j = 0; j < T2; ++j)
+        for (int64_t kb = 0; kb < KB; ++kb) shadow[((g * T2 + j) * 2 + h) * KB + kb] = sfp[(j / 2) * KB + kb];
+      return put(*sc + g * T2 * 2 * KB, shadow.data() + g * T2 * 2 * KB, (size_t)(T2 * 2 * KB * 4));
+    }
+    DSB_CUDA_TRY(ctx, cudaMemcpy2D(*q + g * 2 * I * D + h * D, 2 * D, wp, src_row_pitch, D, I, cudaMemcpyHostToDevice));
+    return DSB_OK;
+  };
+  if (base == "self_attn.q_proj.weight" || base == "self_attn.q_a_proj.weight" ||
+      base == "self_attn.kv_a_proj_with_mqa.weight") {
+    const bool kv = base == "self_attn.kv_a_proj_with_mqa.weight";
+    const int64_t row0 = kv ? Mq : 0, rows = kv ? R + P : Mq;
+    if (Mq % 128) return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_set_tensor: FP8 q rows must be a multiple of 128");
+    if (!shape_is(rows, D)) return bad();
+    int rc = ensure_fp8(m, &L.qkv8, &L.qkv8_s, 1, Mq + R + P, D, false);
+    if (rc != DSB_OK) return rc;
+    if (is_scale) return put(L.qkv8_s + (row0 / 128) * cdiv(D, 128), sf.data(), n * 4);
+    return put(L.qkv8 + row0 * D, w8, (size_t)n);
+  }
+  if (base == "self_attn.q_b_proj.weight") return plain(&L.qb8, &L.qb8_s, 1, 0, QH, c.q_lora_rank);
+  if (base == "self_attn.o_proj.weight") return plain(&L.o8, &L.o8_s, 1, 0, D, (int64_t)H * v);
+  if (base == "self_attn.kv_b_proj.weight") {
+    // absorbed attention keeps kv_b in bf16: dequantise once both halves are here
+    const int64_t rows = (int64_t)H * (nope + v);
+    if (!shape_is(rows, R)) return bad();
+    if (is_scale) L.kvb8_s = sf;
+    else L.kvb8.assign(w8, w8 + n);
+    if (L.kvb8.empty() || L.kvb8_s.empty()) return DSB_OK;
+    const int64_t KB = cdiv(R, 128);
+    std::vector<uint16_t> b((size_t)(rows * R));
+    for (int64_t r = 0; r < rows; ++r)
+      for (int64_t col = 0; col < R; ++col)
+        b[r * R + col] = f32_to_bf16_bits(e4m3_to_f32(L.kvb8[r * R + col]) * L.kvb8_s[(r / 128) * KB + col / 128]);
+    L.kvb8.clear();
+    L.kvb8_s.clear();
+    return upload_kv_b(m, L, b);
+  }
+  if (base == "mlp.gate_proj.weight" || base == "mlp.up_proj.weight") {
+    const int64_t I = is_scale ? shape[0] * 128 : shape[0];
+    if (is_scale ? shape[1] != cdiv(D, 128) : shape[1] != D) return bad();
+    if (L.inter != 0 && L.inter != I) return bad();
+    L.inter = (int)I;
+    const int h = base == "mlp.up_proj.weight" ? 1 : 0;
+    (h ? L.seen_up : L.seen_gate) |= 1;
+    return gate_up(&L.gu8, &L.gu8_s, L.gu8_s_host, 1, 0, I, h, sf.data(), w8, D);
+  }
+  if (base == "mlp.down_proj.weight") {
+    const int64_t I = is_scale ? shape[1] * 128 : shape[1];
+    if (L.inter != 0 && L.inter != I) return bad();
+    L.inter = (int)I;
+    return plain(&L.down8, &L.down8_s, 1, 0, D, I);
+  }
+  const int I = c.moe_intermediate_size, E = c.n_routed_experts;
+  const int ns = std::max(0, c.n_shared_experts), G = m->E_own + ns;
+  static const std::string sp = "mlp.shared_experts.";
+  int e = -1;
+  std::string proj;
+  const bool shared = base.compare(0, sp.size(), sp) == 0;
+  if (shared || parse_expert(base, &e, &proj)) {
+    if (shared) proj = base.substr(sp.size());
+    const bool is_down = proj == "down_proj.weight";
+    if (!is_down && proj != "gate_proj.weight" && proj != "up_proj.weight")
+      return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
+    if (I % 128) return fail(ctx, DSB_EUNSUPPORTED, "dsb_model_set_tensor: FP8 moe_intermediate_size must be a multiple of 128");
+    L.has_moe_tensors = true;
+    L.e_inter = I;
+    L.n_shared = ns;
+    if (!shared) {
+      if (e < 0 || e >= E) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: expert index out of range in %s", cname);
+      if (e < m->e_first || e >= m->e_first + m->E_own) {  // another rank's expert
+        (is_scale ? L.fp8_scales : L.fp8_weights)--;
+        return DSB_OK;
+      }
+      e -= m->e_first;
+      if (is_down) return plain(&L.e_down8, &L.e_down8_s, G, e, D, I);
+      return gate_up(&L.e_gu8, &L.e_gu8_s, L.e_gu8_s_host, G, e, I, proj == "up_proj.weight" ? 1 : 0, sf.data(), w8, D);
+    }
+    // shared experts [ns*I, D] / [D, ns*I] -> groups E_own .. E_own+ns-1
+    if (ns <= 0) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s given but the config has no shared experts", cname);
+    const int KBD = cdiv(D, 128), KBI = I / 128;
+    if (is_down ? !shape_is(D, (int64_t)ns * I) : !shape_is((int64_t)ns * I, D)) return bad();
+    L.shared_seen |= is_down ? 4 : (proj == "up_proj.weight" ? 2 : 1);
+    for (int j = 0; j < ns; ++j) {
+      const int g = m->E_own + j;
+      int rc;
+      if (is_down) {
+        rc = ensure_fp8(m, &L.e_down8, &L.e_down8_s, G, D, I, false);
+        if (rc != DSB_OK) return rc;
+        if (is_scale) {
+          DSB_CUDA_TRY(ctx, cudaMemcpy2D(L.e_down8_s + (int64_t)g * KBD * KBI, KBI * 4, sf.data() + (int64_t)j * KBI,
+                                         (size_t)ns * KBI * 4, KBI * 4, KBD, cudaMemcpyHostToDevice));
+        } else {
+          DSB_CUDA_TRY(ctx, cudaMemcpy2D(L.e_down8 + (int64_t)g * D * I, I, w8 + (int64_t)j * I, (size_t)ns * I, I, D,
+                                         cudaMemcpyHostToDevice));
+        }
+      } else {
+        rc = gate_up(&L.e_gu8, &L.e_gu8_s, L.e_gu8_s_host, G, g, I, proj == "up_proj.weight" ? 1 : 0,
+                     is_scale ? sf.data() + (int64_t)j * KBI * KBD : nullptr, is_scale ? nullptr : w8 + (int64_t)j * I * D,
+                     D);
+        if (rc != DSB_OK) return rc;
+      }
+    }
+    return DSB_OK;
+  }
+  return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: %s cannot be FP8", cname);
 }
 
 }  // namespace
@@ -350,7 +586,7 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
   if (m == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = m->ctx;
   if (cname == nullptr || shape == nullptr || data == nullptr || ndim < 1 || ndim > 2 ||
-      (dtype != DSB_DTYPE_F32 && dtype != DSB_DTYPE_BF16 && dtype != DSB_DTYPE_F16))
+      (dtype != DSB_DTYPE_F32 && dtype != DSB_DTYPE_BF16 && dtype != DSB_DTYPE_F16 && dtype != DSB_DTYPE_F8E4M3))
     return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: bad arguments");
   if (m->finalized) return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: model already finalized");
   const dsb_model_config& c = m->cfg;
@@ -394,6 +630,13 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
   if (!parse_layer(name, &li, &rest) || li < 0 || li >= c.num_hidden_layers)
     return fail(ctx, DSB_EINVAL, "dsb_model_set_tensor: unknown tensor %s", cname);
   auto& L = m->layers[li];
+  {
+    static const std::string suffix = "_scale_inv";
+    const bool is_scale = rest.size() > suffix.size() && rest.compare(rest.size() - suffix.size(), suffix.size(), suffix) == 0;
+    if (is_scale || dtype == DSB_DTYPE_F8E4M3)
+      return set_fp8(m, L, is_scale ? rest.substr(0, rest.size() - suffix.size()) : rest, is_scale, dtype, shape, ndim,
+                     data, cname);
+  }
   auto norm_f32 = [&](float** dst, int64_t len) -> int {
     if (!expect(len, 0)) return bad_shape();
     auto f = to_f32(data, dtype, n);
@@ -434,19 +677,8 @@ extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, 
   if (rest == "self_attn.kv_a_layernorm.weight") return norm_f32(&L.kva_norm, R);
   if (rest == "self_attn.o_proj.weight") return mat_bf16(&L.w_o, D, (int64_t)H * v);
   if (rest == "self_attn.kv_b_proj.weight") {
-    // kv_b rows per head: [nope rows of W_UK | v rows of W_UV], each [*, R] (mla.cpp:99-102)
     if (!expect((int64_t)H * (nope + v), R)) return bad_shape();
-    auto b = to_bf16(data, dtype, n);
-    std::vector<uint16_t> uk_t((size_t)H * R * nope), uv((size_t)H * v * R);
-    for (int h = 0; h < H; ++h) {
-      const uint16_t* base = b.data() + (size_t)h * (nope + v) * R;
-      for (int i = 0; i < nope; ++i)
-        for (int r = 0; r < R; ++r) uk_t[((size_t)h * R + r) * nope + i] = base[(size_t)i * R + r];
-      std::memcpy(uv.data() + (size_t)h * v * R, base + (size_t)nope * R, (size_t)v * R * 2);
-    }
-    int rc = upload(m, &L.w_uk_t, uk_t.data(), uk_t.size());
-    if (rc != DSB_OK) return rc;
-    return upload(m, &L.w_uv, uv.data(), uv.size());
+    return upload_kv_b(m, L, to_bf16(data, dtype, n));
   }
   if (rest == "mlp.gate.weight") {
     if (ndim != 2 || shape[0] != c.n_routed_experts || shape[1] != D) return bad_shape();
@@ -561,29 +793,71 @@ extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) 
   m->embed = emb;
   ones(&m->final_norm, D);
   nb(&m->lm_head, (int64_t)c.vocab_size * D);
+  const bool f8 = c.weights_fp8 != 0;
+  // FP8: each matrix is drawn in bf16 into a scratch buffer and quantised from there
+  bf16* tmp = nullptr;
+  uint8_t* tmp8 = nullptr;
+  float* tmps = nullptr;
+  if (f8) {
+    const int64_t Mq0 = c.q_lora_rank > 0 ? c.q_lora_rank : (int64_t)H * (nope + P);
+    const int64_t I0 = std::max<int64_t>(c.intermediate_size, c.moe_intermediate_size);
+    const int64_t mx = std::max({(Mq0 + R + P) * D, (int64_t)H * (nope + P) * std::max(c.q_lora_rank, 1),
+                                 (int64_t)D * H * v, I0 * D});
+    if (cudaMalloc(&tmp, mx * 2) != cudaSuccess || cudaMalloc(&tmp8, I0 * D) != cudaSuccess ||
+        cudaMalloc(&tmps, ((I0 + 127) / 128) * ((D + 127) / 128) * 4) != cudaSuccess) {
+      cudaFree(tmp);
+      cudaFree(tmp8);
+      return fail(ctx, DSB_ENOMEM, "dsb_model_init_random: FP8 scratch");
+    }
+  }
+  auto f8mat = [&](uint8_t** q, float** sc, int64_t G, int64_t rows, int64_t cols) {
+    if (rc != DSB_OK) return;
+    rc = ensure_fp8(m, q, sc, G, rows, cols, false);
+    const int64_t ss = ((rows + 127) / 128) * ((cols + 127) / 128);
+    for (int64_t g = 0; g < G && rc == DSB_OK; ++g)
+      rc = rand_fp8(m, *q + g * rows * cols, *sc + g * ss, rows, cols, ++s, stddev, tmp);
+  };
+  auto f8gu = [&](uint8_t** q, float** sc, int64_t G, int64_t I) {
+    if (rc != DSB_OK) return;
+    rc = ensure_fp8(m, q, sc, G, 2 * I, D, true);
+    const int64_t ss = (2 * I / 128) * 2 * ((D + 127) / 128);
+    for (int64_t g = 0; g < G && rc == DSB_OK; ++g)
+      rc = rand_fp8_gate_up(m, *q + g * 2 * I * D, *sc + g * ss, I, D, ++s, stddev, tmp, tmp8, tmps);
+  };
   for (int li = 0; li < c.num_hidden_layers && rc == DSB_OK; ++li) {
     auto& L = m->layers[li];
     ones(&L.in_norm, D);
     ones(&L.post_norm, D);
     const int64_t Mq = c.q_lora_rank > 0 ? c.q_lora_rank : (int64_t)H * (nope + P);
-    nb(&L.w_qkv, (Mq + R + P) * D);
-    if (rc == DSB_OK) {
-      (c.q_lora_rank > 0 ? L.w_qa : L.w_q) = L.w_qkv;
-      L.w_kva = L.w_qkv + Mq * D;
+    if (f8) {
+      f8mat(&L.qkv8, &L.qkv8_s, 1, Mq + R + P, D);
+    } else {
+      nb(&L.w_qkv, (Mq + R + P) * D);
+      if (rc == DSB_OK) {
+        (c.q_lora_rank > 0 ? L.w_qa : L.w_q) = L.w_qkv;
+        L.w_kva = L.w_qkv + Mq * D;
+      }
     }
     if (c.q_lora_rank > 0) {
       ones(&L.qa_norm, c.q_lora_rank);
-      nb(&L.w_qb, (int64_t)H * (nope + P) * c.q_lora_rank);
+      if (f8) f8mat(&L.qb8, &L.qb8_s, 1, (int64_t)H * (nope + P), c.q_lora_rank);
+      else nb(&L.w_qb, (int64_t)H * (nope + P) * c.q_lora_rank);
     }
     ones(&L.kva_norm, R);
     nb(&L.w_uk_t, (int64_t)H * R * nope);
     nb(&L.w_uv, (int64_t)H * v * R);
-    nb(&L.w_o, (int64_t)D * H * v);
+    if (f8) f8mat(&L.o8, &L.o8_s, 1, D, (int64_t)H * v);
+    else nb(&L.w_o, (int64_t)D * H * v);
     const bool moe = E > 0 && li >= c.first_k_dense_replace;
     if (!moe) {
       L.inter = c.intermediate_size;
-      nb(&L.w_gu, (int64_t)2 * L.inter * D);
-      nb(&L.w_down, (int64_t)D * L.inter);
+      if (f8) {
+        f8gu(&L.gu8, &L.gu8_s, 1, L.inter);
+        f8mat(&L.down8, &L.down8_s, 1, D, L.inter);
+      } else {
+        nb(&L.w_gu, (int64_t)2 * L.inter * D);
+        nb(&L.w_down, (int64_t)D * L.inter);
+      }
     } else {
       L.has_moe_tensors = true;
       if (rc == DSB_OK) rc = rand_f32(m, &L.w_router, (int64_t)E * D, ++s, stddev, 0.0f);
@@ -591,9 +865,20 @@ extern "C" int dsb_model_init_random(dsb_model* m, uint64_t seed, float stddev) 
       L.e_inter = c.moe_intermediate_size;
       L.n_shared = std::max(0, c.n_shared_experts);
       L.shared_seen = 7;
-      nb(&L.e_gu, (int64_t)(m->E_own + L.n_shared) * 2 * L.e_inter * D);
-      nb(&L.e_down, (int64_t)(m->E_own + L.n_shared) * D * L.e_inter);
+      if (f8) {
+        f8gu(&L.e_gu8, &L.e_gu8_s, m->E_own + L.n_shared, L.e_inter);
+        f8mat(&L.e_down8, &L.e_down8_s, m->E_own + L.n_shared, D, L.e_inter);
+      } else {
+        nb(&L.e_gu, (int64_t)(m->E_own + L.n_shared) * 2 * L.e_inter * D);
+        nb(&L.e_down, (int64_t)(m->E_own + L.n_shared) * D * L.e_inter);
+      }
     }
+  }
+  if (f8) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    cudaFree(tmp8);
+    cudaFree(tmps);
   }
   if (rc != DSB_OK) return rc;
   DSB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
@@ -610,17 +895,23 @@ extern "C" int dsb_model_finalize(dsb_model* m) {
     auto& L = m->layers[li];
     // dense vs MoE by the presence of routed experts (weights.cpp:89-96)
     L.moe = L.has_moe_tensors;
-    const bool q_ok = L.w_q != nullptr || (L.w_qa != nullptr && L.qa_norm != nullptr && L.w_qb != nullptr);
-    if (!L.in_norm || !L.post_norm || !q_ok || !L.w_kva || !L.kva_norm || !L.w_uk_t || !L.w_o)
+    const bool qkv = L.w_qkv != nullptr || L.qkv8 != nullptr;
+    const bool q_ok = c.q_lora_rank > 0 ? (L.qa_norm != nullptr && (L.w_qb != nullptr || L.qb8 != nullptr)) : true;
+    if (!L.in_norm || !L.post_norm || !qkv || !q_ok || !L.kva_norm || !L.w_uk_t || !(L.w_o || L.o8))
       return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d attention weights incomplete", li);
+    if (L.fp8_weights != L.fp8_scales || !L.kvb8.empty() || !L.kvb8_s.empty())
+      return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d has FP8 weights without their scales", li);
+    if ((L.w_qkv != nullptr) == (L.qkv8 != nullptr) && L.w_qkv != nullptr)
+      return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d mixes bf16 and FP8 q/kv_a projections", li);
     if (L.moe) {
-      if (!L.w_router || !L.e_gu || !L.e_down || c.n_routed_experts <= 0 || c.num_experts_per_tok <= 0)
+      if (!L.w_router || !(L.e_gu || L.e_gu8) || !(L.e_down || L.e_down8) || c.n_routed_experts <= 0 ||
+          c.num_experts_per_tok <= 0)
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d MoE weights incomplete", li);
       if (c.scoring_func == DSB_SCORE_SIGMOID && !L.router_bias)
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d needs e_score_correction_bias", li);
       if (L.n_shared > 0 && L.shared_seen != 7)
         return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d shared experts incomplete", li);
-    } else if (!L.w_gu || !L.w_down) {
+    } else if (!(L.w_gu || L.gu8) || !(L.w_down || L.down8)) {
       return fail(ctx, DSB_EINVAL, "dsb_model_finalize: layer %d dense MLP incomplete", li);
     }
   }
@@ -727,12 +1018,107 @@ extern "C" int dsb_kvcache_free_blocks(const dsb_kvcache* kv, int64_t* n) {
   return DSB_OK;
 }
 
+namespace dsb {
+namespace {
+
+// Rows [r0, r1) of each listed page, in every layer's pool, get N(0, stddev)
+// bf16 values.  runs: int32 triples (page, r0, r1).
+__global__ void kv_fill_kernel(bf16* __restrict__ pool, int64_t layer_stride, int row_elems,
+                               const int32_t* __restrict__ runs, uint64_t seed, float stddev) {
+  const int layer = blockIdx.y, run = blockIdx.x;
+  const int32_t page = runs[3 * run], r0 = runs[3 * run + 1], r1 = runs[3 * run + 2];
+  bf16* base = pool + (int64_t)layer * layer_stride + (int64_t)page * 64 * row_elems;
+  const int64_t n = (int64_t)(r1 - r0) * row_elems;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t idx = (int64_t)r0 * row_elems + i;
+    const uint64_t hsh = mix64((seed + layer * 0x1000193ull + (uint64_t)page * 0x9e3779b1ull) * 0x9e3779b97f4a7c15ull +
+                               (uint64_t)idx);
+    const float u1 = ((float)(hsh >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = ((float)((hsh >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+    base[idx] = __float2bfloat16_rn(stddev * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+  }
+}
+
+}  // namespace
+}  // namespace dsb
+
+// Append n_tokens synthetic positions to a sequence: pages as decode would
+// take them, every layer's rows filled with N(0, stddev) latents (seeded).
+extern "C" int dsb_kvcache_fill_random(dsb_kvcache* kv, int seq_id, int n_tokens, uint64_t seed, float stddev) {
+  if (kv == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = kv->ctx;
+  if (seq_id < 0 || seq_id >= kv->max_seqs || !kv->seq_live[seq_id] || n_tokens < 0)
+    return fail(ctx, DSB_EINVAL, "dsb_kvcache_fill_random: bad arguments");
+  int pos = kv->seq_len[seq_id];
+  if (pos + n_tokens > kv->max_blocks_per_seq * 64)
+    return fail(ctx, DSB_EINVAL, "dsb_kvcache_fill_random: sequence %d would exceed its page limit", seq_id);
+  std::vector<int32_t> runs;
+  int left = n_tokens;
+  while (left > 0) {
+    if (pos % 64 == 0) {
+      if (kv->free_pages.empty()) return fail(ctx, DSB_ENOMEM, "dsb_kvcache_fill_random: out of cache pages");
+      kv->seq_pages[seq_id].push_back(kv->free_pages.back());
+      kv->free_pages.pop_back();
+    }
+    const int r0 = pos % 64, r1 = std::min(64, r0 + left);
+    runs.insert(runs.end(), {kv->seq_pages[seq_id].back(), r0, r1});
+    left -= r1 - r0;
+    pos += r1 - r0;
+  }
+  kv->seq_len[seq_id] = pos;
+  if (runs.empty()) return DSB_OK;
+  int32_t* d_runs = nullptr;
+  DSB_CUDA_TRY(ctx, cudaMalloc(&d_runs, runs.size() * 4));
+  DSB_CUDA_TRY(ctx, cudaMemcpy(d_runs, runs.data(), runs.size() * 4, cudaMemcpyHostToDevice));
+  const int row_elems = kv->R + kv->P;
+  const dim3 grid((unsigned)(runs.size() / 3), (unsigned)kv->n_layers);
+  kv_fill_kernel<<<grid, 256, 0, ctx->stream>>>(kv->pool, kv->n_blocks * 64 * (int64_t)row_elems, row_elems, d_runs,
+                                                seed * 0x2545f4914f6cdd1dull + (uint64_t)seq_id, stddev);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(d_runs);
+  if (e != cudaSuccess) return fail(ctx, DSB_ECUDA, "dsb_kvcache_fill_random: %s", cudaGetErrorString(e));
+  return DSB_OK;
+}
+
 // =============================================================== decode step
 
 namespace dsb {
 // defined in mla_decode.cu
 int mla_plan_into_aux(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P, dsb_mla_plan* plan);
 }  // namespace dsb
+
+namespace {
+
+// FP8 linear of the decode step: x quantised per token and 128 columns into
+// (xq, sx), then dsb_linear_fp8 (no group column offsets).
+int lin8(dsb_ctx* ctx, const uint8_t* w, const float* ws, int scale_rows, const uint8_t* xq, const float* sx, int K,
+         int T, int M, void* y, int64_t ldy, int y_f32, int epi, int G = 1, const int32_t* offs = nullptr,
+         int max_tok = 0, const float* row_scale = nullptr) {
+  dsb_linear_fp8_args a{};
+  a.w = w;
+  a.ldw = K;
+  a.w_scale = ws;
+  a.scale_rows = scale_rows;
+  a.x = xq;
+  a.ldx = K;
+  a.x_scale = sx;
+  a.ld_xs = K / 128;
+  a.tok_offsets = offs;
+  a.T = T;
+  a.M = M;
+  a.K = K;
+  a.G = G;
+  a.max_tokens_per_group = max_tok;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_f32 = y_f32;
+  a.epilogue = epi;
+  a.row_scale = row_scale;
+  return dsb_linear_fp8(ctx, &a);
+}
+
+}  // namespace
 
 extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
                                const int32_t* tokens, int B, float* logits_host, int32_t* greedy_host) {
@@ -830,6 +1216,13 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   const size_t o_off = take((size_t)(E + max_ns + 2) * 4);
   const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)B * 4);
   const size_t o_tab = take(host_i.size() * 4);
+  // FP8 layers: activations quantised per token and 128 columns
+  bool any_fp8 = false;
+  for (auto& L : m->layers) any_fp8 |= L.qkv8 || L.qb8 || L.o8 || L.gu8 || L.e_gu8;
+  const int64_t q8_rows = any_fp8 ? std::max<int64_t>(RX, B) : 0;
+  const int64_t q8_cols = any_fp8 ? std::max({(int64_t)D, (int64_t)H * v, (int64_t)std::max(c.q_lora_rank, 128),
+                                              (int64_t)max_I, (int64_t)max_eI}) : 0;
+  const size_t o_xq8 = take((size_t)(q8_rows * q8_cols) + 16), o_sx8 = take((size_t)(q8_rows * (q8_cols / 128)) * 4 + 16);
   // the step buffers live in their own context-owned region (ctx->step); the
   // workspace ctx->ws stays free for split-K / split-KV partials
   int rc = ensure_step(ctx, off);
@@ -844,6 +1237,12 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   bf16 *mid = Bf(o_mid), *xperm = Bf(o_xperm), *midp = Bf(o_midp), *qan = Bf(o_qan);
   int32_t *ids = I32(o_ids), *cnt = I32(o_cnt), *offs = I32(o_off), *dest = I32(o_dest), *src = I32(o_src);
   int32_t *greedy = I32(o_greedy), *tab = I32(o_tab);
+  uint8_t* xq8 = base + o_xq8;
+  float* sx8 = F(o_sx8);
+  // quantise `rows` bf16 rows of K (pitch ld; gathered through src / k when src is set) into xq8 / sx8
+  auto q8 = [&](const void* x, int64_t ld, int rows, int K, const int32_t* src = nullptr, int k = 1) {
+    return quant_act_1x128(ctx, x, DSB_DTYPE_BF16, ld, src, k, rows, K, xq8, K, sx8, K / 128);
+  };
   const int32_t *d_tok = tab, *d_pos = tab + B, *d_bt = tab + 2 * B;
   const int32_t* d_srows = tab + (size_t)B * (2 + MB);           // shared-expert row sources (expert parallel)
   const int32_t* d_soff = d_srows + (size_t)max_ns_host * B;     // shared-expert row offsets
@@ -876,11 +1275,22 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     if (!xn_ready) DSB_STEP(rmsnorm_rows(ctx, h, D, L.in_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
     xn_ready = false;
     // one GEMM for [q | kv_a] (or [q_a | kv_a]) from x, fp32 rows of LQKV
-    DSB_STEP(linear(ctx, L.w_qkv, D, xn, D, B, LQKV, D, kva, LQKV, 1, DSB_EPI_STORE));
-    if (L.w_qa != nullptr) {
+    if (L.qkv8 != nullptr) {
+      DSB_STEP(q8(xn, D, B, D));
+      DSB_STEP(lin8(ctx, L.qkv8, L.qkv8_s, 1, xq8, sx8, D, B, LQKV, kva, LQKV, 1, DSB_EPI_STORE));
+    } else {
+      DSB_STEP(linear(ctx, L.w_qkv, D, xn, D, B, LQKV, D, kva, LQKV, 1, DSB_EPI_STORE));
+    }
+    if (c.q_lora_rank > 0) {
       DSB_STEP(rmsnorm_rows(ctx, kva, LQKV, L.qa_norm, B, c.q_lora_rank, c.rms_norm_eps, qan, c.q_lora_rank,
                             nullptr, 0));
-      DSB_STEP(linear(ctx, L.w_qb, c.q_lora_rank, qan, c.q_lora_rank, B, QH, c.q_lora_rank, q, QH, 0, DSB_EPI_STORE));
+      if (L.qb8 != nullptr) {
+        DSB_STEP(q8(qan, c.q_lora_rank, B, c.q_lora_rank));
+        DSB_STEP(lin8(ctx, L.qb8, L.qb8_s, 1, xq8, sx8, c.q_lora_rank, B, QH, q, QH, 0, DSB_EPI_STORE));
+      } else {
+        DSB_STEP(linear(ctx, L.w_qb, c.q_lora_rank, qan, c.q_lora_rank, B, QH, c.q_lora_rank, q, QH, 0,
+                        DSB_EPI_STORE));
+      }
       DSB_STEP(kv_norm_rope_append(ctx, kva + Mq, LQKV, L.kva_norm, q, nullptr, 0, nullptr, d_pos, d_bt, MB, B, H,
                                    nope, R, P, c.rms_norm_eps, c.rope_theta, cache, qrope));
     } else {
@@ -893,12 +1303,24 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     DSB_STEP(dsb_mla_decode_planned(ctx, &plan, qlat, qrope, cache, kv->n_blocks, d_bt, MB, scale, olat));
     // attn[:, h] = W_UV[h] o_lat[:, h], then h += o_proj(attn)
     DSB_STEP(linear(ctx, L.w_uv, R, olat, (int64_t)H * R, B, v, R, attn, (int64_t)H * v, 0, DSB_EPI_STORE, H, R, v));
-    DSB_STEP(linear(ctx, L.w_o, (int64_t)H * v, attn, (int64_t)H * v, B, D, H * v, h, D, 1, DSB_EPI_ADD));
+    if (L.o8 != nullptr) {
+      DSB_STEP(q8(attn, (int64_t)H * v, B, H * v));
+      DSB_STEP(lin8(ctx, L.o8, L.o8_s, 1, xq8, sx8, H * v, B, D, h, D, 1, DSB_EPI_ADD));
+    } else {
+      DSB_STEP(linear(ctx, L.w_o, (int64_t)H * v, attn, (int64_t)H * v, B, D, H * v, h, D, 1, DSB_EPI_ADD));
+    }
     // feed-forward block (model.cpp:140-157)
     if (!L.moe) {
       DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
-      DSB_STEP(linear(ctx, L.w_gu, D, xn, D, B, 2 * L.inter, D, mid, L.inter, 0, DSB_EPI_SILU_GATE));
-      DSB_STEP(linear(ctx, L.w_down, L.inter, mid, L.inter, B, D, L.inter, h, D, 1, DSB_EPI_ADD));
+      if (L.gu8 != nullptr) {
+        DSB_STEP(q8(xn, D, B, D));
+        DSB_STEP(lin8(ctx, L.gu8, L.gu8_s, 2, xq8, sx8, D, B, 2 * L.inter, mid, L.inter, 0, DSB_EPI_SILU_GATE));
+        DSB_STEP(q8(mid, L.inter, B, L.inter));
+        DSB_STEP(lin8(ctx, L.down8, L.down8_s, 1, xq8, sx8, L.inter, B, D, h, D, 1, DSB_EPI_ADD));
+      } else {
+        DSB_STEP(linear(ctx, L.w_gu, D, xn, D, B, 2 * L.inter, D, mid, L.inter, 0, DSB_EPI_SILU_GATE));
+        DSB_STEP(linear(ctx, L.w_down, L.inter, mid, L.inter, B, D, L.inter, h, D, 1, DSB_EPI_ADD));
+      }
     } else if (ep) {
       // expert parallel: routed picks go to the experts' ranks and come back;
       // the shared experts run here on this rank's tokens
@@ -915,14 +1337,32 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       int32_t* roff = nullptr;
       DSB_STEP(dsb_ep_dispatch(m->ep, xn, D, B, ids, &rx, &roff));
       const int eI = L.e_inter, EL = m->E_own, ns = L.n_shared;
-      DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
-      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
-      if (ns > 0) {
-        const bf16* s_gu = L.e_gu + (size_t)EL * 2 * eI * D;
-        const bf16* s_down = L.e_down + (size_t)EL * D * eI;
-        DSB_STEP(gather_rows(ctx, xn, D, d_srows, ns * B, 1, D, xperm));
-        DSB_STEP(linear(ctx, s_gu, D, xperm, D, ns * B, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, ns, 0, 0, d_soff, B));
-        DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
+      if (L.e_gu8 != nullptr) {
+        const int64_t gs = (2 * eI / 128) * 2 * (D / 128), ds = (D / 128) * (eI / 128);  // scales per group
+        DSB_STEP(q8(rx, D, ep_cap, D));
+        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, ep_cap, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL,
+                      roff, B));
+        DSB_STEP(q8(midp, eI, ep_cap, eI));
+        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, ep_cap, D, yperm, D, 1, DSB_EPI_STORE, EL, roff, B));
+        if (ns > 0) {
+          DSB_STEP(q8(xn, D, ns * B, D, d_srows, 1));
+          DSB_STEP(lin8(ctx, L.e_gu8 + (size_t)EL * 2 * eI * D, L.e_gu8_s + EL * gs, 2, xq8, sx8, D, ns * B, 2 * eI,
+                        midp, eI, 0, DSB_EPI_SILU_GATE, ns, d_soff, B));
+          DSB_STEP(q8(midp, eI, ns * B, eI));
+          DSB_STEP(lin8(ctx, L.e_down8 + (size_t)EL * D * eI, L.e_down8_s + EL * ds, 1, xq8, sx8, eI, ns * B, D, ys, D,
+                        1, DSB_EPI_STORE, ns, d_soff, B));
+        }
+      } else {
+        DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
+        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
+        if (ns > 0) {
+          const bf16* s_gu = L.e_gu + (size_t)EL * 2 * eI * D;
+          const bf16* s_down = L.e_down + (size_t)EL * D * eI;
+          DSB_STEP(gather_rows(ctx, xn, D, d_srows, ns * B, 1, D, xperm));
+          DSB_STEP(linear(ctx, s_gu, D, xperm, D, ns * B, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, ns, 0, 0, d_soff,
+                          B));
+          DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
+        }
       }
       DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, ys, ns, h, next_norm, c.rms_norm_eps, xn));
       xn_ready = true;
@@ -940,12 +1380,23 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
                            c.norm_topk_prob, c.routed_scaling_factor, ids, wts, L.n_shared));
       }
       DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
-      DSB_STEP(gather_rows(ctx, xn, D, src, B * kk, kk, D, xperm));
       const int eI = L.e_inter;
-      // every expert writes the same columns of its own (permuted) token rows
-      DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * kk, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, G, 0, 0, offs, B));
-      DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * kk, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, G, 0, 0, offs, B,
-                      wperm));
+      if (L.e_gu8 != nullptr) {
+        // gather + quantise the permuted rows in one pass, then the FP8 expert GEMMs
+        DSB_STEP(q8(xn, D, B * kk, D, src, kk));
+        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, B * kk, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, G, offs,
+                      B));
+        DSB_STEP(q8(midp, eI, B * kk, eI));
+        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, B * kk, D, yperm, D, 1, DSB_EPI_ROWSCALE, G, offs,
+                      B, wperm));
+      } else {
+        DSB_STEP(gather_rows(ctx, xn, D, src, B * kk, kk, D, xperm));
+        // every expert writes the same columns of its own (permuted) token rows
+        DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * kk, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, G, 0, 0, offs,
+                        B));
+        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * kk, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, G, 0, 0, offs, B,
+                        wperm));
+      }
       DSB_STEP(moe_combine(ctx, yperm, dest, B, kk, D, nullptr, h, next_norm, c.rms_norm_eps, xn));
       xn_ready = true;
     }
@@ -960,4 +1411,61 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     DSB_CUDA_TRY(ctx, cudaMemcpyAsync(logits_host, logits, (size_t)B * V * 4, cudaMemcpyDeviceToHost, ctx->stream));
   ctx->stats.decode_steps++;
   return dsb_sync(ctx);
+}
+
+// Batched greedy generation on the host over dsb_decode_step: ds::rt::generate
+// (src/runtime/model.cpp:14-49) for B sequences at once.  Each sequence first
+// consumes its prompt token by token (DeepSeekModel::forward,
+// src/models/deepseek/model.cpp:104-110), then feeds back its greedy id; it
+// stops after max_new_tokens ids or at eos_id (>= 0; the eos id is kept, as
+// the reference does).  Sequences with different prompt lengths are stepped
+// together: each call decodes one token for every sequence still running.
+extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+                            const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
+                            int32_t eos_id, int32_t* out_ids, int32_t* out_counts) {
+  if (ctx == nullptr || m == nullptr || kv == nullptr) return DSB_EINVAL;
+  if (seq_ids == nullptr || prompt_tokens == nullptr || prompt_offsets == nullptr || out_ids == nullptr ||
+      out_counts == nullptr || B <= 0 || max_new_tokens < 0)
+    return fail(ctx, DSB_EINVAL, "dsb_generate: bad arguments");
+  if (m->ep != nullptr)
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_generate: expert-parallel models step every rank together; drive "
+                                       "dsb_decode_step directly");
+  for (int b = 0; b < B; ++b) {
+    out_counts[b] = 0;
+    if (prompt_offsets[b + 1] - prompt_offsets[b] < 1)
+      return fail(ctx, DSB_EINVAL, "dsb_generate: sequence %d has an empty prompt", b);
+  }
+  if (max_new_tokens == 0) return DSB_OK;
+  std::vector<int> fed(B, 0);           // prompt tokens consumed
+  std::vector<int32_t> last(B, 0);      // last generated id
+  std::vector<uint8_t> done(B, 0);
+  std::vector<int32_t> ids, toks, greedy;
+  std::vector<int> rows;
+  for (;;) {
+    ids.clear();
+    toks.clear();
+    rows.clear();
+    for (int b = 0; b < B; ++b) {
+      if (done[b]) continue;
+      const int plen = prompt_offsets[b + 1] - prompt_offsets[b];
+      ids.push_back(seq_ids[b]);
+      toks.push_back(fed[b] < plen ? prompt_tokens[prompt_offsets[b] + fed[b]] : last[b]);
+      rows.push_back(b);
+    }
+    if (rows.empty()) break;
+    greedy.resize(rows.size());
+    const int rc = dsb_decode_step(ctx, m, kv, ids.data(), toks.data(), (int)rows.size(), nullptr, greedy.data());
+    if (rc != DSB_OK) return rc;
+    for (size_t r = 0; r < rows.size(); ++r) {
+      const int b = rows[r];
+      const int plen = prompt_offsets[b + 1] - prompt_offsets[b];
+      if (fed[b] < plen) ++fed[b];
+      if (fed[b] < plen) continue;  // still inside the prompt
+      const int32_t nxt = greedy[r];
+      out_ids[(size_t)b * max_new_tokens + out_counts[b]] = nxt;
+      last[b] = nxt;
+      if (++out_counts[b] >= max_new_tokens || (eos_id >= 0 && nxt == eos_id)) done[b] = 1;
+    }
+  }
+  return DSB_OK;
 }

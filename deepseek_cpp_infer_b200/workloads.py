@@ -99,6 +99,16 @@ V2_LITE = dict(
 )
 
 
+# DeepSeek-V3 (671B) shape: FP8 block-scaled projections, FFN and experts.
+V3 = dict(
+    hidden_size=7168, num_hidden_layers=61, num_attention_heads=128, vocab_size=129280, max_position_embeddings=163840,
+    intermediate_size=18432, moe_intermediate_size=2048, n_routed_experts=256, n_shared_experts=1,
+    num_experts_per_tok=8, first_k_dense_replace=3, q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=128,
+    qk_rope_head_dim=64, v_head_dim=128, scoring_func=1, n_group=8, topk_group=4, norm_topk_prob=1,
+    routed_scaling_factor=2.5, rms_norm_eps=1e-6, rope_theta=10000.0, weights_fp8=1,
+)
+
+
 def bf16_round(a: np.ndarray) -> np.ndarray:
     """Round float32 values to the nearest bf16 value (ties to even), kept as float32."""
     u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)

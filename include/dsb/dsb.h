@@ -410,6 +410,7 @@ DSB_API int dsb_embed(dsb_ctx* ctx, const void* table, int table_bf16, const int
 
 #define DSB_DTYPE_F32 0
 #define DSB_DTYPE_BF16 1
+#define DSB_DTYPE_F8E4M3 3 /* raw e4m3 bytes (model weights with *_scale_inv) */
 #define DSB_DTYPE_F16 2
 
 /* The model hyper-parameters the decode path reads: the fields of
@@ -425,6 +426,9 @@ typedef struct dsb_model_config {
   int kv_lora_rank, qk_nope_head_dim, qk_rope_head_dim, v_head_dim;
   int scoring_func, n_group, topk_group, norm_topk_prob;
   float routed_scaling_factor, rms_norm_eps, rope_theta;
+  /* dsb_model_init_random only: 1 = the projections and FFN / expert weights
+   * in block-scaled FP8 (e4m3 + 128x128 fp32 scales, DeepSeek-V3 style). */
+  int weights_fp8;
 } dsb_model_config;
 
 typedef struct dsb_model dsb_model;
@@ -439,7 +443,12 @@ DSB_API int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_mode
 DSB_API int dsb_model_destroy(dsb_model* model);
 /* Upload one checkpoint tensor from HOST memory, named as in the HF
  * safetensors ("model.layers.3.self_attn.kv_b_proj.weight", ...); dtype is
- * DSB_DTYPE_*.  The caller keeps ownership of `data`. */
+ * DSB_DTYPE_*.  The caller keeps ownership of `data`.
+ * Block-scaled FP8 checkpoints: a projection, FFN or expert weight given as
+ * DSB_DTYPE_F8E4M3 (raw e4m3 bytes) is kept in FP8 and needs its fp32
+ * "<name>_scale_inv" tensor [ceil(rows/128), ceil(cols/128)] (either order);
+ * those layers then run the FP8 GEMM with 1x128-quantised activations.
+ * kv_b_proj is dequantised to bf16 at load (absorbed attention). */
 DSB_API int dsb_model_set_tensor(dsb_model* model, const char* name, int dtype, const int64_t* shape, int ndim,
                                  const void* data);
 /* Fill every weight on the device with N(0, stddev) (norms 1), layer kinds
@@ -475,6 +484,11 @@ DSB_API int dsb_kvcache_free_seq(dsb_kvcache* kv, int seq_id);
 DSB_API int dsb_kvcache_reset(dsb_kvcache* kv);
 DSB_API int dsb_kvcache_seq_len(const dsb_kvcache* kv, int seq_id, int* len);
 DSB_API int dsb_kvcache_free_blocks(const dsb_kvcache* kv, int64_t* n);
+/* Append n_tokens synthetic positions to a live sequence: pages are taken as
+ * decoding would take them and every layer's rows get N(0, stddev) bf16
+ * latents (seeded).  For benchmarks that need a long context without
+ * prefilling it token by token; no counterpart in the reference. */
+DSB_API int dsb_kvcache_fill_random(dsb_kvcache* kv, int seq_id, int n_tokens, uint64_t seed, float stddev);
 
 /* One decode step: token tokens[b] of sequence seq_ids[b] (HOST arrays, B
  * distinct live sequences) is appended at the sequence's current length and
@@ -484,6 +498,19 @@ DSB_API int dsb_kvcache_free_blocks(const dsb_kvcache* kv, int64_t* n);
  * after the step completed on the device. */
 DSB_API int dsb_decode_step(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
                             const int32_t* tokens, int B, float* logits, int32_t* greedy);
+
+/* Batched greedy generation: ds::rt::generate (src/runtime/model.cpp:14-49)
+ * for B sequences of the cache at once, on the host over dsb_decode_step.
+ * Sequence b's prompt is prompt_tokens[prompt_offsets[b] .. prompt_offsets[b+1])
+ * (at least one token), consumed token by token as the reference's forward()
+ * does; then its greedy ids are fed back until max_new_tokens ids or eos_id
+ * (>= 0, kept in the output; < 0 for none).  out_ids [B, max_new_tokens]
+ * (host), out_counts [B] (host) the ids written per sequence.  Sampling
+ * (temperature / top-k / top-p) is not covered: greedy only.  Not for models
+ * bound to an expert-parallel group (their ranks step together). */
+DSB_API int dsb_generate(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+                         const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
+                         int32_t eos_id, int32_t* out_ids, int32_t* out_counts);
 
 #ifdef __cplusplus
 }

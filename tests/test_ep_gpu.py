@@ -1,5 +1,6 @@
 """Expert parallelism on several GPUs (one process per GPU): the tiny
-DeepSeek-V2-style model with its 16 routed experts split over the ranks
+DeepSeek-V2-style model (bf16, and as a block-scaled FP8 checkpoint) with its
+16 routed experts split over the ranks
 (dsb_model_set_ep; picks exchanged through dsb_ep_dispatch / dsb_ep_combine,
 kernels writing into the peers' memory) against the same model unsplit on
 each rank, on the same sequences.
@@ -28,7 +29,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, fp8):
     import torch
     import torch.distributed as dist
 
@@ -45,16 +46,21 @@ def _worker(rank, world, port, out_dir):
     handles = [None] * world
     dist.all_gather_object(handles, ep.window_handle())
     ep.connect(handles)
-    tensors = model_tensors(TINY, seed=0)
-    models = []
-    for use_ep in (True, False):
-        m = dsb.Model(ctx, dsb.ModelConfig(**TINY))
-        if use_ep:
-            m.set_ep(ep)
-        for name, a in tensors.items():
-            m.set_tensor(name, a)
-        m.finalize()
-        models.append(m)
+    if fp8:
+        from fp8_tiny import build
+
+        models = [build(ctx, True, ep), build(ctx, True)]
+    else:
+        tensors = model_tensors(TINY, seed=0)
+        models = []
+        for use_ep in (True, False):
+            m = dsb.Model(ctx, dsb.ModelConfig(**TINY))
+            if use_ep:
+                m.set_ep(ep)
+            for name, a in tensors.items():
+                m.set_tensor(name, a)
+            m.finalize()
+            models.append(m)
     kvs = [dsb.KVCache(ctx, m, n_blocks=16, max_seqs=4, max_blocks_per_seq=2) for m in models]
     B = 1 + rank  # ranks decode different batch sizes
     rng = np.random.default_rng(50 + rank)
@@ -80,14 +86,15 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_ep_model_decode_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("fp8", [False, True], ids=["bf16", "fp8"])
+def test_ep_model_decode_matches_single_gpu(tmp_path, fp8):
     import torch
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("expert parallelism needs at least 2 GPUs")
-    mp.spawn(_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _port(), str(tmp_path), fp8), nprocs=world, join=True)
     worst = [float(open(tmp_path / f"rank{r}").read()) for r in range(world)]
     print("EP vs single-GPU logits max-rel per rank:", worst)
     assert all(w == 0.0 for w in worst), worst
