@@ -334,6 +334,9 @@ def model_cfg(args):
     cfg = dict(V3 if args.workload == "v3" else V2_LITE)
     if args.layers:
         cfg["num_hidden_layers"] = args.layers
+    if args.experts:
+        # fewer routed experts: one GPU doing the per-rank expert work of a larger expert-parallel run
+        cfg["n_routed_experts"] = args.experts
     return cfg
 
 
@@ -908,7 +911,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
     ap.add_argument("--layers", type=int, default=0, help="model layers (0 = the configuration's 27)")
     ap.add_argument("--experts", type=int, default=0,
-                    help="moe-fp8: routed experts (0 = 256; fewer for small profiling captures)")
+                    help="moe-fp8 / v3: routed experts (0 = the configuration's; fewer for small profiling captures "
+                         "or for one GPU standing in for one rank of an expert-parallel run)")
     args = ap.parse_args()
     if args.workload == "expert-gemm":
         args.batch = args.batch or 32

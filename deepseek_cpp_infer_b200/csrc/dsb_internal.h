@@ -44,6 +44,28 @@ struct dsb_mla_plan {
 
 namespace dsb {
 
+// Split-K count for a dense decode GEMM: `tiles` 128-row weight tiles of
+// tile_bytes each, over `sm` SMs.  Each count s (1..8, every split at least
+// min_kb of the KB K blocks) costs the weight bytes plus, for s > 1, its fp32
+// partials (written and read back: tiles * s * 128 * NT * 8 bytes), divided
+// by the share of SM slots its waves of work units fill; the cheapest wins.
+inline int pick_splits(int tiles, int KB, int sm, int min_kb, double tile_bytes, int NT) {
+  int best = 1;
+  double best_cost = 0.0;
+  for (int s = 1; s <= 8; ++s) {
+    if (s > 1 && KB / s < min_kb) break;
+    const int units = tiles * s, waves = (units + sm - 1) / sm;
+    const double fill = (double)units / ((double)waves * sm);
+    const double bytes = tiles * tile_bytes + (s > 1 ? (double)tiles * s * 128.0 * NT * 8.0 : 0.0);
+    const double cost = bytes / fill;
+    if (s == 1 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
 // Launch a kernel on `stream` with programmatic stream serialization: it may
 // be scheduled while the previous kernel of the stream drains (the kernel
 // calls pdl_wait() before reading that kernel's results).

@@ -36,6 +36,7 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "rows.cuh"
 
 namespace dsb {
 namespace {
@@ -255,31 +256,16 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
   if (!ok_s) return;
   const float* inbox = reinterpret_cast<const float*>(win + L.off_inbox);
   const int t = blockIdx.x, k = L.k, D = L.D;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    float acc = 0.0f;
-    for (int j = 0; j < k; ++j)
-      acc = __fadd_rn(acc, __fmul_rn(__ldcv(inbox + ((size_t)t * k + j) * D + i), weights[(size_t)t * k + j]));
-    for (int s = 0; s < n_shared; ++s) acc = __fadd_rn(acc, shared[((size_t)s * T + t) * D + i]);
-    const float hv = __fadd_rn(h[(size_t)t * D + i], acc);
-    h[(size_t)t * D + i] = hv;
-    ss = __fadd_rn(ss, __fmul_rn(hv, hv));
-  }
-  if (w_next != nullptr) {
-    // the next RMSNorm of this row, the arithmetic of the single-GPU combine
-    __shared__ float red[32];
-    float v = ss;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float tot = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)D), eps)));
-    for (int i = threadIdx.x; i < D; i += blockDim.x)
-      xn_next[(size_t)t * D + i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(h[(size_t)t * D + i], inv), w_next[i]));
-  }
+  __shared__ float red[32];
+  // the weighted outputs w * out, the single-GPU combine's pre-weighted rows
+  auto pick = [&](int j, int i4) {
+    const float4 v = __ldcv(reinterpret_cast<const float4*>(inbox + ((size_t)t * k + j) * D) + i4);
+    const float wj = weights[(size_t)t * k + j];
+    return make_float4(__fmul_rn(v.x, wj), __fmul_rn(v.y, wj), __fmul_rn(v.z, wj), __fmul_rn(v.w, wj));
+  };
+  combine_row(pick, k, D, n_shared > 0 ? shared + (size_t)t * D : nullptr, n_shared, (int64_t)T * D, h + (size_t)t * D,
+              w_next, eps,
+              xn_next ? xn_next + (size_t)t * D : nullptr, red);
 }
 
 }  // namespace

@@ -429,15 +429,13 @@ extern "C" int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* a) {
   const int bound = a->max_tokens_per_group > 0 ? a->max_tokens_per_group : a->T;
   const int m_tiles = (a->M + kTileM - 1) / kTileM;
   const int KB = (a->K + kBK - 1) / kBK;
-  int splits = 1;
-  if (a->tok_offsets == nullptr && a->T <= 256) {
-    // small decode GEMMs: split K so every SM streams a share of the weights
-    const int tiles = m_tiles * a->G;
-    const int want = ctx->sm_count / std::max(1, tiles);  // one wave of work units
-    splits = std::max(1, std::min({want, KB / 4, 8}));
-  }
   int NT = 16;
   while (NT < bound && NT < 256) NT *= 2;
+  int splits = 1;
+  if (a->tok_offsets == nullptr && a->T <= 256) {
+    // small decode GEMMs: split K so the SMs share the weight stream
+    splits = pick_splits(m_tiles * a->G, KB, ctx->sm_count, 4, 128.0 * a->K * 2, NT);
+  }
   switch (NT) {
     case 16: return launch_gemm<16>(ctx, a, splits, m_tiles);
     case 32: return launch_gemm<32>(ctx, a, splits, m_tiles);

@@ -491,16 +491,18 @@ extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
   const int bound = a->max_tokens_per_group > 0 ? a->max_tokens_per_group : a->T;
   const int m_tiles = (a->M + kTileM - 1) / kTileM;
   const int KB = a->K / kBK;
+  int NT = 16;
+  while (NT < bound && NT < 128) NT *= 2;
   int splits = 1;
   if (a->tok_offsets == nullptr && a->T <= 128) {
     // small decode GEMMs (one token tile, so the split partials are per
-    // weight tile): split K so every SM streams a share of the weights
+    // weight tile): split K so the SMs share the weight stream, in one wave
+    // of work units (the per-K-block promotion keeps this kernel's per-SM
+    // stream rate below the bf16 kernel's, so extra waves cost more than
+    // the idle SMs of a partial wave)
     const int tiles = m_tiles * a->G;
-    const int want = std::max(1, ctx->sm_count / std::max(1, tiles));
-    splits = std::max(1, std::min({want, KB / 2, 8}));
+    splits = std::max(1, std::min({ctx->sm_count / std::max(1, tiles), KB / 2, 8}));
   }
-  int NT = 16;
-  while (NT < bound && NT < 128) NT *= 2;
   switch (NT) {
     case 16: return launch_fp8<16>(ctx, a, splits, m_tiles);
     case 32: return launch_fp8<32>(ctx, a, splits, m_tiles);

@@ -12,6 +12,7 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "rows.cuh"
 
 namespace dsb {
 namespace {
@@ -51,7 +52,18 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, co
   __shared__ float red[32];
   const float* xr = x + blockIdx.x * ldx;
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+  const bool vec = (n % 4) == 0 && (ldx % 4) == 0;  // 16-byte rows
+  if (vec) {
+    for (int i4 = threadIdx.x; i4 < n / 4; i4 += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(xr)[i4];
+      ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+      ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+      ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+      ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+  }
   const float mean2 = __fdiv_rn(block_sum(ss, red), (float)n);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -63,12 +75,10 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, co
 
 // -------------------------------------------------- norm + RoPE + cache append
 
-// Interleaved-pair rotation of (x0, x1) at pair index k of a dim-wide rope
-// vector (src/ops/core/rope.cpp:8-23: inv_freq = theta^(-2k/dim)).
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, int k, int dim, int pos, float theta) {
-  const float inv_freq = powf(theta, __fdiv_rn(-(float)(2 * k), (float)dim));
-  const float ang = __fmul_rn((float)pos, inv_freq);
-  const float c = cosf(ang), s = sinf(ang);
+// Interleaved-pair rotation of (x0, x1) by the angle whose cosine / sine are
+// c / s (src/ops/core/rope.cpp:8-23; pair k of a dim-wide rope vector turns by
+// pos * theta^(-2k/dim)).
+__device__ __forceinline__ void rotate_pair(float& x0, float& x1, float c, float s) {
   const float a = x0, b = x1;
   x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
   x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
@@ -85,9 +95,17 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
                                            __nv_bfloat16* __restrict__ cache, __nv_bfloat16* __restrict__ q_rope) {
   pdl_wait();
   __shared__ float red[32];
+  __shared__ float cs[2][64];  // cos / sin of each rope pair at this token's position (P <= 128)
   const int b = blockIdx.x;
   const int p = pos[b];
   const float* kv = kv_a + (int64_t)b * ld_kv;
+  for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
+    const float inv_freq = powf(theta, __fdiv_rn(-(float)(2 * k), (float)P));  // rope.cpp:8-23
+    const float ang = __fmul_rn((float)p, inv_freq);
+    cs[0][k] = cosf(ang);
+    cs[1][k] = sinf(ang);
+  }
+  __syncthreads();
   float ss = 0.0f;
   for (int i = threadIdx.x; i < R; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(kv[i], kv[i]));
   const float mean2 = __fdiv_rn(block_sum(ss, red), (float)R);
@@ -97,7 +115,7 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
   for (int i = threadIdx.x; i < R; i += blockDim.x) row[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(kv[i], inv), w_norm[i]));
   for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
     float x0 = kv[R + 2 * k], x1 = kv[R + 2 * k + 1];
-    rope_pair(x0, x1, k, P, p, theta);
+    rotate_pair(x0, x1, cs[0][k], cs[1][k]);
     row[R + 2 * k] = __float2bfloat16_rn(x0);
     row[R + 2 * k + 1] = __float2bfloat16_rn(x1);
   }
@@ -121,7 +139,7 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
       x0 = __bfloat162float(src[0]);
       x1 = __bfloat162float(src[1]);
     }
-    rope_pair(x0, x1, k, P, p, theta);
+    rotate_pair(x0, x1, cs[0][k], cs[1][k]);
     __nv_bfloat16* dst = q_rope + ((int64_t)b * H + h) * P + 2 * k;
     dst[0] = __float2bfloat16_rn(x0);
     dst[1] = __float2bfloat16_rn(x1);
@@ -573,22 +591,10 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
   pdl_wait();
   __shared__ float red[32];
   const int t = blockIdx.x;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    float acc = 0.0f;
-    for (int j = 0; j < k; ++j) acc = __fadd_rn(acc, y[(int64_t)dest[t * k + j] * D + i]);
-    if (shared) acc = __fadd_rn(acc, shared[(int64_t)t * D + i]);
-    const float hv = __fadd_rn(h[(int64_t)t * D + i], acc);
-    h[(int64_t)t * D + i] = hv;
-    ss = __fadd_rn(ss, __fmul_rn(hv, hv));
-  }
-  if (w_next != nullptr) {
-    // the next RMSNorm of this row (the same arithmetic as rmsnorm_rows_kernel)
-    const float mean2 = __fdiv_rn(block_sum(ss, red), (float)D);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
-    for (int i = threadIdx.x; i < D; i += blockDim.x)
-      xn_next[(int64_t)t * D + i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(h[(int64_t)t * D + i], inv), w_next[i]));
-  }
+  const int32_t* dt = dest + (int64_t)t * k;
+  auto pick = [&](int j, int i4) { return reinterpret_cast<const float4*>(y + (int64_t)dt[j] * D)[i4]; };
+  combine_row(pick, k, D, shared ? shared + (int64_t)t * D : nullptr, shared ? 1 : 0, 0, h + (int64_t)t * D, w_next,
+              eps, xn_next ? xn_next + (int64_t)t * D : nullptr, red);
 }
 
 // Greedy id per row: first index of the maximum (argmax_f32, math.cpp:29-40).
@@ -655,7 +661,7 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, int64_t ld_kv, const fl
                         const float* qf, int64_t ld_qf, void* q_out, const int32_t* pos, const int32_t* block_table,
                         int max_blocks, int B, int H, int nope, int R, int P, float eps, float theta, void* cache,
                         void* q_rope) {
-  launch_pdl(kv_norm_rope_append_kernel, B, 128, 0, ctx->stream, kv_a, ld_kv, w_norm,
+  launch_pdl(kv_norm_rope_append_kernel, B, 256, 0, ctx->stream, kv_a, ld_kv, w_norm,
              static_cast<const __nv_bfloat16*>(q), qf, ld_qf, static_cast<__nv_bfloat16*>(q_out), pos, block_table,
              max_blocks, H, nope, R, P, eps, theta, static_cast<__nv_bfloat16*>(cache),
              static_cast<__nv_bfloat16*>(q_rope));
@@ -762,7 +768,7 @@ extern "C" int dsb_kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, const fl
                                        void* q_rope) {
   if (ctx == nullptr) return DSB_EINVAL;
   if (kv_a == nullptr || w_norm == nullptr || q == nullptr || positions == nullptr || block_table == nullptr ||
-      cache == nullptr || q_rope == nullptr || B <= 0 || H <= 0 || R <= 0 || P <= 0 || (P % 2) != 0)
+      cache == nullptr || q_rope == nullptr || B <= 0 || H <= 0 || R <= 0 || P <= 0 || (P % 2) != 0 || P > 128)
     return dsb::fail(ctx, DSB_EINVAL, "dsb_kv_norm_rope_append: bad arguments");
   return dsb::kv_norm_rope_append(ctx, kv_a, R + P, w_norm, q, nullptr, 0, nullptr, positions, block_table,
                                   max_blocks, B, H, nope, R, P, eps, theta, cache, q_rope);
