@@ -22,9 +22,10 @@
 // linear GEMVs of moe_to_slot / linear_to_slot (src/models/deepseek/
 // cuda_backend.cpp:782-883) for block-scaled FP8 checkpoints.
 //
-// Roles (192 threads, 320 from 64 tokens up): warp 0 TMA producer, warp 1 MMA
-// issuer, the other warps promotion + epilogue (warp w owns TMEM lanes
-// 32*(w%4)..+31 and all, or from 64 tokens up half, of the token columns).
+// Roles: warp 0 TMA producer, warp 1 MMA issuer, the other warps promotion +
+// epilogue (warp w owns TMEM lanes 32*(w%4)..+31 and all, or from 64 tokens up
+// half, of the token columns); up to 64 tokens two such groups take
+// alternate K blocks (320 / 576 threads), at 128 tokens one group (320).
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -66,15 +67,22 @@ struct Fp8Shape {
   static constexpr int A_BYTES = kTileM * kBK;  // 16 KB
   static constexpr int B_BYTES = NT * kBK;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NS = (196 * 1024) / STAGE;
   static constexpr int NBUF = 4;  // TMEM partial buffers: the MMAs run up to 3 K blocks ahead
-  static constexpr int CG = NT < 64 ? 1 : 2;        // token-column groups of the epilogue
-  static constexpr int EPI = 128 * CG;              // epilogue threads: 4 lane quarters x CG
+  static constexpr int CG = NT < 128 ? 1 : 2;       // token-column groups of the epilogue
+  static constexpr int KG = NT <= 64 ? 2 : 1;       // epilogue groups taking alternate K blocks
+  static_assert(CG == 1 || KG == 1, "column groups or K groups, not both");
+  static constexpr int GT = 128 * CG;               // threads of one K group: 4 lane quarters x CG
+  static constexpr int EPI = GT * KG;
   static constexpr int THREADS = 64 + EPI;
+  static constexpr int HC = NT / CG;                // token columns per epilogue thread
+  static constexpr int XCH = KG > 1 ? kTileM * NT * 4 : 0;    // odd group's sums for the even group
+  static constexpr int SX = (EPI / 32) * 4 * HC * 4;          // [warps][2 buffers][2 row parities][HC]
+  static constexpr int NS = (200 * 1024 - XCH - SX) / STAGE;  // ring depth
   static constexpr int OFF_BAR = NS * STAGE;
-  static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 2) * 8;
-  static constexpr int OFF_SX = OFF_MISC + 64;  // [epilogue warps][2 buffers][2 row parities][NT/CG] scales
-  static constexpr int SMEM = OFF_SX + (EPI / 32) * 4 * (NT / CG) * 4 + 1024;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 4) * 8;
+  static constexpr int OFF_XCH = OFF_MISC + 64;
+  static constexpr int OFF_SX = OFF_XCH + XCH;
+  static constexpr int SMEM = OFF_SX + SX + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
   static constexpr uint32_t TCOLS = NBUF * TC;       // <= 512
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -123,6 +131,9 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
   uint64_t* part_full = empty + S::NS;        // [NBUF] partial buffer written by one K block's MMAs
   uint64_t* part_empty = part_full + S::NBUF; // [NBUF] partial buffer promoted by the epilogue
   uint64_t* drain = part_empty + S::NBUF;
+  uint64_t* xch_full = drain + 1;   // the odd K group's sums are in xch
+  uint64_t* xch_empty = drain + 2;  // the even K group has read them
+  float* xch = reinterpret_cast<float*>(smem + S::OFF_XCH);  // [NT][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
   volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
@@ -139,9 +150,11 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     }
     for (int b = 0; b < S::NBUF; ++b) {
       mbar_init(&part_full[b], 1);
-      mbar_init(&part_empty[b], S::EPI);
+      mbar_init(&part_empty[b], S::GT);  // one K group reads each buffer
     }
     mbar_init(drain, 1);
+    mbar_init(xch_full, S::GT);
+    mbar_init(xch_empty, S::GT);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -238,21 +251,26 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------- promotion + epilogue
-    // 8 warps: warp w reads TMEM lanes 32*(w%4)..+31 (weight rows of the
-    // tile) and token columns [h*HC, (h+1)*HC), h = (w-2)/4.
-    constexpr int HC = NT / S::CG;         // token columns per thread (16, 32 or 64)
+    // Warp w reads TMEM lanes 32*(w%4)..+31 (weight rows of the tile) and
+    // token columns [cg*HC, (cg+1)*HC); with KG = 2 two groups of such warps
+    // take alternate K blocks (by the parity of the running partial index),
+    // each summing its own blocks, and the even group adds the odd group's
+    // sums (handed over in shared memory) before the epilogue.
+    constexpr int HC = S::HC;              // token columns per thread (16, 32 or 64)
     constexpr int LW = HC < 32 ? HC : 32;  // columns per tcgen05.ld
     constexpr int NL = HC / LW;            // loads per K block
     constexpr int PER = (HC + 31) / 32;    // token scales loaded per lane
     const uint32_t qtr = warp & 3;
-    const int c0 = (int)((warp - 2) >> 2) * HC;  // this thread's first token column
-    const int r = (int)(qtr * 32 + lane);        // weight row within the tile (parity = lane parity)
-    const int et = threadIdx.x - 64;             // 0..EPI-1
+    // with KG = 2, CG = 1: warps 2-5 are K group 0, warps 6-9 K group 1
+    const int kg = S::KG == 1 ? 0 : (int)((warp - 2) >> 2);
+    const int c0 = S::KG == 1 ? (int)((warp - 2) >> 2) * HC : 0;  // this thread's first token column
+    const int r = (int)(qtr * 32 + lane);         // weight row within the tile (parity = lane parity)
+    const int et = (int)threadIdx.x - 64 - kg * S::GT;  // index within the K group
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     // this warp's scale vectors: [2 buffers][row parity][HC], sw(row) * sx[t] of one K block
     float* sxw = sx_smem + (warp - 2) * 4 * HC;
     UnitIter it{&p, NT};
-    int pk = 0;
+    int pk = 0, own = 0, u = 0;  // running partial index, K blocks this group promoted (KG > 1), units
     bool ok = true;
     while (ok && it.next()) {
       const int tbase = it.tok0 + it.nt * NT;
@@ -288,13 +306,19 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           }
         }
       };
-      __syncwarp();
-      load_sx(kb0);
-      store_sx(pk & 1);
-      __syncwarp();
+      // this group's first K block of the unit
+      const int kbf = S::KG == 1 ? kb0 : kb0 + (int)((kg - pk % S::KG + S::KG) % S::KG);
+      if (S::KG == 1 || kbf < kb1) {
+        __syncwarp();
+        load_sx(kbf);
+        store_sx((S::KG == 1 ? pk : own) & 1);
+        __syncwarp();
+      }
       for (int kb = kb0; kb < kb1; ++kb, ++pk) {
-        const int b = pk % S::NBUF, sb = pk & 1;  // TMEM partial buffer, scale buffer
-        if (kb + 1 < kb1) load_sx(kb + 1);
+        if (S::KG > 1 && pk % S::KG != kg) continue;
+        const int b = pk % S::NBUF, sb = (S::KG == 1 ? pk : own) & 1;  // TMEM partial buffer, scale buffer
+        if constexpr (S::KG > 1) ++own;
+        if (kb + S::KG < kb1) load_sx(kb + S::KG);
         if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk / S::NBUF) & 1, abort))) {
           raise_abort(abort, status, kStatusTimeout);
           ok = false;
@@ -325,13 +349,35 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
             acc[ci + 3] = fmaf(__uint_as_float(raw[i + 3]), sv.w, acc[ci + 3]);
           }
         }
-        if (kb + 1 < kb1) {
+        if (kb + S::KG < kb1) {
           __syncwarp();  // every lane is done with the buffer written next
           store_sx(sb ^ 1);
           __syncwarp();
         }
       }
       if (!ok) break;
+      if constexpr (S::KG > 1) {
+        // hand the odd group's sums to the even group (bounded waits)
+        if (kg == 1) {
+          if (u > 0 && !__all_sync(0xffffffffu, mbar_wait(xch_empty, (u - 1) & 1, abort))) {
+            raise_abort(abort, status, kStatusTimeout);
+            break;
+          }
+#pragma unroll
+          for (int i = 0; i < HC; ++i) xch[(c0 + i) * kTileM + r] = acc[i];
+          mbar_arrive(xch_full);
+          ++u;
+          continue;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(xch_full, u & 1, abort))) {
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
+#pragma unroll
+        for (int i = 0; i < HC; ++i) acc[i] = __fadd_rn(acc[i], xch[(c0 + i) * kTileM + r]);
+        mbar_arrive(xch_empty);
+        ++u;
+      }
 
       auto apply = [&](float (&v)[HC]) {
         if (silu) {
@@ -379,12 +425,12 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
 #pragma unroll
       for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
       __threadfence();
-      named_bar_sync(1, S::EPI);
+      named_bar_sync(1, S::GT);  // the even K group only
       if (et == 0) {
         const int prev = atomicAdd(&p.counters[tile_id], 1);
         *last_flag = (prev == p.splits - 1) ? 1 : 0;
       }
-      named_bar_sync(1, S::EPI);
+      named_bar_sync(1, S::GT);
       if (*last_flag != 0) {
         __threadfence();
         const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
