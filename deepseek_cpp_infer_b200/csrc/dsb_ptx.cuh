@@ -182,8 +182,16 @@ __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_add
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+// A rendezvous of the threads counted by `bar` (an mbarrier initialised with
+// their number): arrive, then wait for the phase to complete.  Unlike a named
+// barrier it cannot hang when a participant has left after an abort: the wait
+// gives up when *abort is raised or the time limit passes.  Shared-memory
+// writes before the arrive are visible to every participant after the wait.
+__device__ __forceinline__ bool mbar_rendezvous(uint64_t* bar, int& phase, volatile int* abort) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, (uint32_t)phase & 1u, abort);
+  ++phase;
+  return ok;
 }
 
 __device__ __forceinline__ void cluster_sync() {

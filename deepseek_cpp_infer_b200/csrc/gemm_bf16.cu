@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + S::NS;   // [2] accumulator slot written by the MMAs
   uint64_t* acc_empty = acc_full + 2;   // [2] accumulator slot read by the epilogue
   uint64_t* drain = acc_full + 4;
+  uint64_t* epi_bar = drain + 1;        // rendezvous of the 128 epilogue threads (split-K ticket)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
   volatile int* no_abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(epi_bar, 128);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;  // 0..127
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     UnitIter it{&p, NT};
-    int u = 0;
+    int u = 0, epi_phase = 0;
     while (it.next()) {
       const int slot = u & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[slot], (u >> 1) & 1, abort))) {
@@ -266,15 +268,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (it.mt * kTileM + r < p.M) {
           const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
+          // The token weights (ROWSCALE) are all loaded before the first
+          // store (a load cannot be moved above a store that may alias it, so
+          // interleaving them serialises 32 memory round trips); the residual
+          // add is a reduction into y, which needs no load: each element of y
+          // receives exactly one add, so the result is y + x rounded once.
+          float pre[32];
+          if (p.epi == DSB_EPI_ROWSCALE) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int t = c * 32 + i;
+              pre[i] = t < tcount ? __ldg(p.row_scale + tbase + t) : 0.0f;
+            }
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int t = c * 32 + i;
             if (t < tcount) {
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
               float x = v[i];
-              if (p.epi == DSB_EPI_ROWSCALE) x *= p.row_scale[tbase + t];
+              if (p.epi == DSB_EPI_ROWSCALE) x *= pre[i];
               if (p.epi == DSB_EPI_ADD) {
-                static_cast<float*>(p.y)[o] += x;
+                atomicAdd(static_cast<float*>(p.y) + o, x);
               } else if (p.y_f32) {
                 static_cast<float*>(p.y)[o] = x;
               } else {
@@ -307,12 +322,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (part != nullptr) {
         // the last split to finish sums the partials in split order
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
         if (et == 0) {
           const int prev = atomicAdd(&p.counters[tile_id], 1);
           *last_flag = (prev == p.splits - 1) ? 1 : 0;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
         if (*last_flag != 0) {
           __threadfence();
           const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
@@ -322,22 +343,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.0f;
             // four splits' loads in flight at a time, summed in split order
-            int s2 = 0;
-            for (; s2 + 4 <= p.splits; s2 += 4) {
+            for (int s2 = 0; s2 < p.splits; s2 += 4) {
               float w4[4][CW];
 #pragma unroll
               for (int j = 0; j < 4; ++j)
 #pragma unroll
                 for (int i = 0; i < CW; ++i)
-                  w4[j][i] = __ldcg(pbase + (int64_t)(s2 + j) * NT * kTileM + (c * 32 + i) * kTileM);
+                  w4[j][i] = s2 + j < p.splits ? __ldcg(pbase + (int64_t)(s2 + j) * NT * kTileM + (c * 32 + i) * kTileM)
+                                               : 0.0f;
 #pragma unroll
               for (int j = 0; j < 4; ++j)
+                if (s2 + j < p.splits) {
 #pragma unroll
-                for (int i = 0; i < CW; ++i) v[i] += w4[j][i];
-            }
-            for (; s2 < p.splits; ++s2) {
-#pragma unroll
-              for (int i = 0; i < CW; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c * 32 + i) * kTileM);
+                  for (int i = 0; i < CW; ++i) v[i] += w4[j][i];
+                }
             }
             apply(c, v);
           }

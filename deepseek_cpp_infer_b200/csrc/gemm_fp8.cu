@@ -24,8 +24,8 @@
 //
 // Roles: warp 0 TMA producer, warp 1 MMA issuer, the other warps promotion +
 // epilogue (warp w owns TMEM lanes 32*(w%4)..+31 and all, or from 64 tokens up
-// half, of the token columns); up to 64 tokens two such groups take
-// alternate K blocks (320 / 576 threads), at 128 tokens one group (320).
+// half, of the token columns); up to 32 tokens two such groups take
+// alternate K blocks; 320 threads in every case.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -67,9 +67,11 @@ struct Fp8Shape {
   static constexpr int A_BYTES = kTileM * kBK;  // 16 KB
   static constexpr int B_BYTES = NT * kBK;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NBUF = 4;  // TMEM partial buffers: the MMAs run up to 3 K blocks ahead
-  static constexpr int CG = NT < 128 ? 1 : 2;       // token-column groups of the epilogue
-  static constexpr int KG = NT <= 64 ? 2 : 1;       // epilogue groups taking alternate K blocks
+  // TMEM partial buffers filling all 512 columns: the MMAs run up to NBUF-1
+  // K blocks ahead of the promotion (and through the epilogue of a unit)
+  static constexpr int NBUF = 512 / (NT < 32 ? 32 : NT);
+  static constexpr int CG = NT < 64 ? 1 : 2;        // token-column groups of the epilogue
+  static constexpr int KG = NT < 64 ? 2 : 1;        // epilogue groups taking alternate K blocks
   static_assert(CG == 1 || KG == 1, "column groups or K groups, not both");
   static constexpr int GT = 128 * CG;               // threads of one K group: 4 lane quarters x CG
   static constexpr int EPI = GT * KG;
@@ -77,12 +79,14 @@ struct Fp8Shape {
   static constexpr int HC = NT / CG;                // token columns per epilogue thread
   static constexpr int XCH = KG > 1 ? kTileM * NT * 4 : 0;    // odd group's sums for the even group
   static constexpr int SX = (EPI / 32) * 4 * HC * 4;          // [warps][2 buffers][2 row parities][HC]
-  static constexpr int NS = (200 * 1024 - XCH - SX) / STAGE;  // ring depth
+  static constexpr int RS = (EPI / 32) * NT * 4;              // [warps][NT] token weights (ROWSCALE)
+  static constexpr int NS = (200 * 1024 - XCH - SX - RS) / STAGE;  // ring depth
   static constexpr int OFF_BAR = NS * STAGE;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 4) * 8;
   static constexpr int OFF_XCH = OFF_MISC + 64;
   static constexpr int OFF_SX = OFF_XCH + XCH;
-  static constexpr int SMEM = OFF_SX + SX + 1024;
+  static constexpr int OFF_RS = OFF_SX + SX;
+  static constexpr int SMEM = OFF_RS + RS + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
   static constexpr uint32_t TCOLS = NBUF * TC;       // <= 512
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -133,6 +137,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
   uint64_t* drain = part_empty + S::NBUF;
   uint64_t* xch_full = drain + 1;   // the odd K group's sums are in xch
   uint64_t* xch_empty = drain + 2;  // the even K group has read them
+  uint64_t* epi_bar = drain + 3;    // rendezvous of the even K group (split-K ticket)
   float* xch = reinterpret_cast<float*>(smem + S::OFF_XCH);  // [NT][128]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
@@ -155,6 +160,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(xch_full, S::GT);
     mbar_init(xch_empty, S::GT);
+    mbar_init(epi_bar, S::GT);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -269,6 +275,9 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     // this warp's scale vectors: [2 buffers][row parity][HC], sw(row) * sx[t] of one K block
     float* sxw = sx_smem + (warp - 2) * 4 * HC;
+    // this warp's copy of the unit's token weights (ROWSCALE), read by the epilogue
+    float* rsw = reinterpret_cast<float*>(smem + S::OFF_RS) + (warp - 2) * NT;
+    int epi_phase = 0;
     UnitIter it{&p, NT};
     int pk = 0, own = 0, u = 0;  // running partial index, K blocks this group promoted (KG > 1), units
     bool ok = true;
@@ -280,6 +289,12 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
       const float* ws_even = p.w_scale + (int64_t)tile_id * p.scale_rows * KB;
       const float* ws_odd = ws_even + (int64_t)(p.scale_rows - 1) * KB;
       const float* sxrow = p.x_scale + it.g * (p.x_group_col / kBK);
+      if (p.epi == DSB_EPI_ROWSCALE && kg == 0) {
+        // fetched now, used after the K loop (no load waits in the epilogue)
+        __syncwarp();
+        for (int j = (int)lane; j < NT; j += 32) rsw[j] = j < tcount ? __ldg(p.row_scale + tbase + j) : 0.0f;
+        __syncwarp();
+      }
       float acc[HC];
 #pragma unroll
       for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
@@ -397,15 +412,21 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           }
         } else if (it.mt * kTileM + r < p.M) {
           const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
+          // The token weights (ROWSCALE) come from shared memory, staged at
+          // the start of the unit; the residual add is a reduction into y,
+          // which needs no load: each element of y receives exactly one add,
+          // so the result is y + x rounded once.  (A global load here could
+          // not be moved above the previous column's store, which may alias
+          // it: one memory round trip per column.)
 #pragma unroll
           for (int i = 0; i < HC; ++i) {
             const int t = c0 + i;
             if (t < tcount) {
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
               float x = v[i];
-              if (p.epi == DSB_EPI_ROWSCALE) x *= p.row_scale[tbase + t];
+              if (p.epi == DSB_EPI_ROWSCALE) x *= rsw[t];
               if (p.epi == DSB_EPI_ADD) {
-                static_cast<float*>(p.y)[o] += x;
+                atomicAdd(static_cast<float*>(p.y) + o, x);
               } else if (p.y_f32) {
                 static_cast<float*>(p.y)[o] = x;
               } else {
@@ -425,12 +446,18 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
 #pragma unroll
       for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
       __threadfence();
-      named_bar_sync(1, S::GT);  // the even K group only
+      if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {  // the even K group only
+        raise_abort(abort, status, kStatusTimeout);
+        break;
+      }
       if (et == 0) {
         const int prev = atomicAdd(&p.counters[tile_id], 1);
         *last_flag = (prev == p.splits - 1) ? 1 : 0;
       }
-      named_bar_sync(1, S::GT);
+      if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
+        raise_abort(abort, status, kStatusTimeout);
+        break;
+      }
       if (*last_flag != 0) {
         __threadfence();
         const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
