@@ -30,6 +30,7 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "epi.cuh"
 
 namespace dsb {
 namespace {
@@ -52,6 +53,7 @@ struct GemmParams {
   int n_tiles;        // G * m_tiles * splits
   float* ws;          // split partials
   int* counters;      // per-tile tickets (zeroed; reset by the last split)
+  int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
 };
 
 template <int NT>
@@ -59,8 +61,10 @@ struct GemmShape {
   static constexpr int A_BYTES = kTileM * kBK * 2;  // 16 KB
   static constexpr int B_BYTES = NT * kBK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NS = (196 * 1024) / STAGE;   // ring depth: ~196 KB of stages
-  static constexpr int OFF_BAR = NS * STAGE;
+  static constexpr int STG = 4 * 32 * 32 * 4;       // output staging: 32 x 32 fp32 per epilogue warp
+  static constexpr int NS = (212 * 1024 - STG) / STAGE;  // ring depth
+  static constexpr int OFF_STG = NS * STAGE;
+  static constexpr int OFF_BAR = OFF_STG + STG;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
   static constexpr int SMEM = OFF_MISC + 32 + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per accumulator
@@ -235,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = (int)(qtr * 32 + lane);  // weight row within the tile
     const int et = threadIdx.x - 64;  // 0..127
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
+    float* stg = reinterpret_cast<float*>(smem + S::OFF_STG) + (warp - 2) * 32 * 32;  // this warp's staging block
     UnitIter it{&p, NT};
     int u = 0, epi_phase = 0;
     while (it.next()) {
@@ -249,51 +254,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tcount = min(NT, it.tok1 - tbase);
       const int tile_id = it.g * p.m_tiles + it.mt;
       constexpr int NCH = NT < 32 ? 1 : NT / 32;
-      // output of one 32-token chunk of this thread's weight row
+      // output of one 32-token chunk of this thread's weight row (called by
+      // all lanes of the warp)
       auto apply = [&](int c, float (&v)[32]) {
         if (silu) {
           // rows 2j / 2j+1 of the tile are gate / up of output feature 64*mt + j
-          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
+          float hv[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            hv[i] = v[i] / (1.0f + __expf(-v[i])) * up;
+          }
+          if (p.vec_out) {
+            warp_store_block<32, true, 0>(stg, hv, lane, tcount - c * 32, 16, p.y, p.ldy,
+                                       (int64_t)it.g * p.y_group_col + it.mt * 64 + qtr * 16, tbase + c * 32,
+                                       p.y_f32, false);
+            return;
+          }
+          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
             const int t = c * 32 + i;
             if ((r & 1) == 0 && t < tcount) {
-              const float gt = v[i];
-              const float hval = gt / (1.0f + __expf(-gt)) * up;
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
-              if (p.y_f32) static_cast<float*>(p.y)[o] = hval;
-              else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(hval);
+              if (p.y_f32) static_cast<float*>(p.y)[o] = hv[i];
+              else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(hv[i]);
             }
           }
-        } else if (it.mt * kTileM + r < p.M) {
-          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
-          // The token weights (ROWSCALE) are all loaded before the first
-          // store (a load cannot be moved above a store that may alias it, so
-          // interleaving them serialises 32 memory round trips); the residual
-          // add is a reduction into y, which needs no load: each element of y
-          // receives exactly one add, so the result is y + x rounded once.
+          return;
+        }
+        // The token weights (ROWSCALE) are all loaded before the first store
+        // (a load cannot be moved above a store that may alias it, so
+        // interleaving them serialises 32 memory round trips); the residual
+        // add is a reduction into y, which needs no load: each element of y
+        // receives exactly one add, so the result is y + x rounded once.
+        if (p.epi == DSB_EPI_ROWSCALE) {
           float pre[32];
-          if (p.epi == DSB_EPI_ROWSCALE) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int t = c * 32 + i;
-              pre[i] = t < tcount ? __ldg(p.row_scale + tbase + t) : 0.0f;
-            }
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            pre[i] = t < tcount ? __ldg(p.row_scale + tbase + t) : 0.0f;
           }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= pre[i];
+        }
+        if (p.vec_out) {
+          const int ncols = max(0, min(32, p.M - it.mt * kTileM - (int)qtr * 32));
+          warp_store_block<32, false, 0>(stg, v, lane, tcount - c * 32, ncols, p.y, p.ldy,
+                                      (int64_t)it.g * p.y_group_col + it.mt * kTileM + qtr * 32, tbase + c * 32,
+                                      p.y_f32, p.epi == DSB_EPI_ADD);
+          return;
+        }
+        if (it.mt * kTileM + r < p.M) {
+          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int t = c * 32 + i;
             if (t < tcount) {
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
-              float x = v[i];
-              if (p.epi == DSB_EPI_ROWSCALE) x *= pre[i];
               if (p.epi == DSB_EPI_ADD) {
-                atomicAdd(static_cast<float*>(p.y) + o, x);
+                atomicAdd(static_cast<float*>(p.y) + o, v[i]);
               } else if (p.y_f32) {
-                static_cast<float*>(p.y)[o] = x;
+                static_cast<float*>(p.y)[o] = v[i];
               } else {
-                static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(x);
+                static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(v[i]);
               }
             }
           }
@@ -402,6 +426,8 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int splits, int m_tiles)
   p.n_tiles = a->G * m_tiles * splits;
   p.ws = nullptr;
   p.counters = nullptr;
+  p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
+                         a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
   if (splits > 1) {
     const size_t tiles = (size_t)m_tiles * a->G;
     rc = ensure_workspace(ctx, tiles * splits * NT * kTileM * sizeof(float));

@@ -35,6 +35,7 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "epi.cuh"
 
 namespace dsb {
 namespace {
@@ -60,6 +61,7 @@ struct Fp8Params {
   int n_tiles;        // G * m_tiles * splits
   float* ws;          // split partials
   int* counters;      // per-tile tickets (zeroed; reset by the last split)
+  int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
 };
 
 template <int NT>
@@ -80,13 +82,15 @@ struct Fp8Shape {
   static constexpr int XCH = KG > 1 ? kTileM * NT * 4 : 0;    // odd group's sums for the even group
   static constexpr int SX = (EPI / 32) * 4 * HC * 4;          // [warps][2 buffers][2 row parities][HC]
   static constexpr int RS = (EPI / 32) * NT * 4;              // [warps][NT] token weights (ROWSCALE)
-  static constexpr int NS = (200 * 1024 - XCH - SX - RS) / STAGE;  // ring depth
+  static constexpr int STG = (GT / 32) * 32 * 32 * 4;         // output staging of the writing warps
+  static constexpr int NS = (212 * 1024 - XCH - SX - RS - STG) / STAGE;  // ring depth
   static constexpr int OFF_BAR = NS * STAGE;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 4) * 8;
   static constexpr int OFF_XCH = OFF_MISC + 64;
   static constexpr int OFF_SX = OFF_XCH + XCH;
   static constexpr int OFF_RS = OFF_SX + SX;
-  static constexpr int SMEM = OFF_RS + RS + 1024;
+  static constexpr int OFF_STG = OFF_RS + RS;
+  static constexpr int SMEM = OFF_STG + STG + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
   static constexpr uint32_t TCOLS = NBUF * TC;       // <= 512
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -277,6 +281,8 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     float* sxw = sx_smem + (warp - 2) * 4 * HC;
     // this warp's copy of the unit's token weights (ROWSCALE), read by the epilogue
     float* rsw = reinterpret_cast<float*>(smem + S::OFF_RS) + (warp - 2) * NT;
+    // output staging block of the warps that write (the even K group's, or all)
+    float* stg = reinterpret_cast<float*>(smem + S::OFF_STG) + ((warp - 2) % (S::GT / 32)) * 32 * 32;
     int epi_phase = 0;
     UnitIter it{&p, NT};
     int pk = 0, own = 0, u = 0;  // running partial index, K blocks this group promoted (KG > 1), units
@@ -394,83 +400,106 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
         ++u;
       }
 
-      auto apply = [&](float (&v)[HC]) {
+      auto apply = [&](float (&v)[HC]) {  // called by all lanes of the warp
+        constexpr int BT = HC < 32 ? HC : 32;  // token rows per staged block
         if (silu) {
           // rows 2j / 2j+1 of the tile are gate / up of output feature 64*mt + j
-          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
+          // in place: the partner lane's v[i] is read before either lane rewrites it
 #pragma unroll
           for (int i = 0; i < HC; ++i) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            v[i] = v[i] / (1.0f + __expf(-v[i])) * up;
+          }
+          if (p.vec_out) {
+            const int64_t col0 = (int64_t)it.g * p.y_group_col + it.mt * 64 + qtr * 16;
+            warp_store_block<BT, true, 0>(stg, v, lane, tcount - c0, 16, p.y, p.ldy, col0, tbase + c0, p.y_f32, false);
+            if constexpr (HC > BT)
+              warp_store_block<BT, true, BT>(stg, v, lane, tcount - c0 - BT, 16, p.y, p.ldy, col0, tbase + c0 + BT,
+                                             p.y_f32, false);
+            return;
+          }
+          const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * 64 + (r >> 1);
+#pragma unroll
+          for (int i = 0; i < HC; ++i) {
             const int t = c0 + i;
             if ((r & 1) == 0 && t < tcount) {
-              const float gt = v[i];
-              const float hval = gt / (1.0f + __expf(-gt)) * up;
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
-              if (p.y_f32) static_cast<float*>(p.y)[o] = hval;
-              else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(hval);
+              if (p.y_f32) static_cast<float*>(p.y)[o] = v[i];
+              else static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(v[i]);
             }
           }
-        } else if (it.mt * kTileM + r < p.M) {
+          return;
+        }
+        // The token weights (ROWSCALE) come from shared memory, staged at the
+        // start of the unit (a global load here could not be moved above the
+        // previous column's store, which may alias it: one memory round trip
+        // per column); the residual add is a reduction into y, which needs no
+        // load: each element of y receives exactly one add, so the result is
+        // y + x rounded once.
+        if (p.epi == DSB_EPI_ROWSCALE) {
+#pragma unroll
+          for (int i = 0; i < HC; ++i) v[i] *= rsw[c0 + i];
+        }
+        if (p.vec_out) {
+          const int ncols = max(0, min(32, p.M - it.mt * kTileM - (int)qtr * 32));
+          const int64_t col0 = (int64_t)it.g * p.y_group_col + it.mt * kTileM + qtr * 32;
+          const bool add = p.epi == DSB_EPI_ADD;
+          warp_store_block<BT, false, 0>(stg, v, lane, tcount - c0, ncols, p.y, p.ldy, col0, tbase + c0, p.y_f32, add);
+          if constexpr (HC > BT)
+            warp_store_block<BT, false, BT>(stg, v, lane, tcount - c0 - BT, ncols, p.y, p.ldy, col0, tbase + c0 + BT,
+                                            p.y_f32, add);
+          return;
+        }
+        if (it.mt * kTileM + r < p.M) {
           const int64_t col = (int64_t)it.g * p.y_group_col + it.mt * kTileM + r;
-          // The token weights (ROWSCALE) come from shared memory, staged at
-          // the start of the unit; the residual add is a reduction into y,
-          // which needs no load: each element of y receives exactly one add,
-          // so the result is y + x rounded once.  (A global load here could
-          // not be moved above the previous column's store, which may alias
-          // it: one memory round trip per column.)
 #pragma unroll
           for (int i = 0; i < HC; ++i) {
             const int t = c0 + i;
             if (t < tcount) {
               const int64_t o = (int64_t)(tbase + t) * p.ldy + col;
-              float x = v[i];
-              if (p.epi == DSB_EPI_ROWSCALE) x *= rsw[t];
               if (p.epi == DSB_EPI_ADD) {
-                atomicAdd(static_cast<float*>(p.y) + o, x);
+                atomicAdd(static_cast<float*>(p.y) + o, v[i]);
               } else if (p.y_f32) {
-                static_cast<float*>(p.y)[o] = x;
+                static_cast<float*>(p.y)[o] = v[i];
               } else {
-                static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(x);
+                static_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(v[i]);
               }
             }
           }
         }
       };
 
-      if (p.splits == 1) {
-        apply(acc);
-        continue;
-      }
-      // split-K: publish this split's promoted sum; the last split reduces
-      float* part = p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM;
+      if (p.splits > 1) {
+        // split-K: publish this split's promoted sum; the last split reduces
+        // (into acc, in split order) and runs the epilogue
+        float* part = p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM;
 #pragma unroll
-      for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
-      __threadfence();
-      if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {  // the even K group only
-        raise_abort(abort, status, kStatusTimeout);
-        break;
-      }
-      if (et == 0) {
-        const int prev = atomicAdd(&p.counters[tile_id], 1);
-        *last_flag = (prev == p.splits - 1) ? 1 : 0;
-      }
-      if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
-        raise_abort(abort, status, kStatusTimeout);
-        break;
-      }
-      if (*last_flag != 0) {
+        for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
+        __threadfence();
+        if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {  // the even K group only
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
+        if (et == 0) {
+          const int prev = atomicAdd(&p.counters[tile_id], 1);
+          *last_flag = (prev == p.splits - 1) ? 1 : 0;
+        }
+        if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
+          raise_abort(abort, status, kStatusTimeout);
+          break;
+        }
+        if (*last_flag == 0) continue;
         __threadfence();
         const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
-        float v[HC];
 #pragma unroll
-        for (int i = 0; i < HC; ++i) v[i] = 0.0f;
+        for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
         for (int s2 = 0; s2 < p.splits; ++s2) {
 #pragma unroll
-          for (int i = 0; i < HC; ++i) v[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c0 + i) * kTileM);
+          for (int i = 0; i < HC; ++i) acc[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c0 + i) * kTileM);
         }
-        apply(v);
         if (et == 0) p.counters[tile_id] = 0;
       }
+      apply(acc);
     }
   }
   tc_fence_before();
@@ -514,6 +543,8 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_til
   p.n_tiles = a->G * m_tiles * splits;
   p.ws = nullptr;
   p.counters = nullptr;
+  p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
+                         a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
   if (splits > 1) {
     const size_t tiles = (size_t)m_tiles * a->G;
     rc = ensure_workspace(ctx, tiles * splits * NT * kTileM * sizeof(float));

@@ -157,6 +157,32 @@ def test_linear_fp8_plain(gpu_ctx, T, M, K):
     assert max_rel(yb, ref) <= TOL16
 
 
+@pytest.mark.parametrize("M", [200, 300])
+@pytest.mark.parametrize("T", [7, 33, 90])
+def test_linear_fp8_partial_tile_and_unaligned_output(gpu_ctx, T, M):
+    """M = 200 ends inside a 128-row tile on a 16-byte boundary (vector
+    output, clipped per warp); M = 300 leaves rows that are not a whole
+    vector (element-wise output).  Store to f32 / bf16 and residual add."""
+    import torch
+
+    lut = e4m3_lut()
+    K = 512
+    wq, ws = quant_w(gpu_ctx, normal(M, K, scale=0.05, seed=41))
+    xq, xs = quant_x(gpu_ctx, normal(T, K, seed=42, dtype=torch.bfloat16))
+    ref = deq_x(lut, xq, xs) @ deq_w(lut, wq, ws).T
+    y = torch.full((T, M), float("nan"), dtype=torch.float32, device="cuda")
+    gpu_ctx.linear_fp8(wq, ws, xq, xs, y, M=M, K=K)
+    yb = torch.full((T, M), float("nan"), dtype=torch.bfloat16, device="cuda")
+    gpu_ctx.linear_fp8(wq, ws, xq, xs, yb, M=M, K=K)
+    h = normal(T, M, seed=43)
+    h0 = h.clone()
+    gpu_ctx.linear_fp8(wq, ws, xq, xs, h, M=M, K=K, epilogue=dsb.EPI_ADD)
+    gpu_ctx.sync()
+    assert max_rel(y, ref) <= TOL32
+    assert max_rel(yb, ref) <= TOL16
+    assert max_rel(h, h0.double() + ref) <= TOL32
+
+
 def test_linear_fp8_residual_add_split_k(gpu_ctx):
     import torch
 

@@ -76,6 +76,31 @@ def test_linear_residual_add(gpu_ctx):
     assert max_rel(h, ref) <= 1e-4
 
 
+@pytest.mark.parametrize("M", [200, 300])
+@pytest.mark.parametrize("T", [7, 33])
+def test_linear_partial_tile_and_unaligned_output(gpu_ctx, T, M):
+    """M = 200 ends inside a 128-row tile on a 16-byte boundary (vector
+    output, clipped per warp); M = 300 leaves rows that are not a whole
+    vector (element-wise output).  Store to f32 / bf16 and residual add."""
+    import torch
+
+    K = 512
+    w = rand(M, K, scale=0.05, seed=31)
+    x = rand(T, K, seed=32)
+    ref = x.float() @ w.float().T
+    y = torch.full((T, M), float("nan"), dtype=torch.float32, device="cuda")
+    gpu_ctx.linear(w, x, y, M=M, K=K)
+    yb = torch.full((T, M), float("nan"), dtype=torch.bfloat16, device="cuda")
+    gpu_ctx.linear(w, x, yb, M=M, K=K)
+    h = torch.randn(T, M, device="cuda")
+    h0 = h.clone()
+    gpu_ctx.linear(w, x, h, M=M, K=K, epilogue=dsb.EPI_ADD)
+    gpu_ctx.sync()
+    assert max_rel(y, ref) <= 1e-4
+    assert max_rel(yb, ref) <= 1e-2
+    assert max_rel(h, h0 + ref) <= 1e-4
+
+
 @pytest.mark.parametrize("T", [1, 32, 200])
 def test_linear_silu_gate(gpu_ctx, T):
     import torch
