@@ -31,6 +31,7 @@
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
 #include "epi.cuh"
+#include "sched.cuh"
 
 namespace dsb {
 namespace {
@@ -48,11 +49,10 @@ struct GemmParams {
   int y_f32;
   int epi;
   const float* row_scale;
-  int splits;
+  int max_splits;     // parts of each unit of the partial last round (sched.cuh)
   int m_tiles;
-  int n_tiles;        // G * m_tiles * splits
-  float* ws;          // split partials
-  int* counters;      // per-tile tickets (zeroed; reset by the last split)
+  float* ws;          // split partials: [tail unit][split][NT][128]
+  int* counters;      // per-tail-unit tickets (zeroed; reset by the last split)
   int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
 };
 
@@ -64,43 +64,14 @@ struct GemmShape {
   static constexpr int STG = 4 * 32 * 32 * 4;       // output staging: 32 x 32 fp32 per epilogue warp
   static constexpr int NS = (212 * 1024 - STG) / STAGE;  // ring depth
   static constexpr int OFF_STG = NS * STAGE;
-  static constexpr int OFF_BAR = OFF_STG + STG;
+  static constexpr int OFF_SCHED = OFF_STG + STG;
+  static constexpr int OFF_BAR = OFF_SCHED + ((int)sizeof(SchedTable) + 15) / 16 * 16;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
   static constexpr int SMEM = OFF_MISC + 32 + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per accumulator
   static constexpr uint32_t TCOLS = 2 * TC;          // double-buffered
   static_assert(STAGE % 1024 == 0, "stage alignment");
   static_assert(SMEM <= 232448, "shared memory");
-};
-
-// The sequence of work units of this CTA: tiles blockIdx.x + i*gridDim.x, and
-// inside each tile its token tiles.  Every role walks the same sequence.
-struct UnitIter {
-  const GemmParams* p;
-  int NT;
-  int tile = -1, nt = 0, n_tt = 0;
-  int g = 0, mt = 0, split = 0, tok0 = 0, tok1 = 0;
-
-  __device__ bool next() {
-    if (tile >= 0 && ++nt < n_tt) return true;
-    for (tile = (tile < 0 ? (int)blockIdx.x : tile + (int)gridDim.x); tile < p->n_tiles; tile += gridDim.x) {
-      split = tile % p->splits;
-      const int gm = tile / p->splits;
-      mt = gm % p->m_tiles;
-      g = gm / p->m_tiles;
-      if (p->tok_offsets != nullptr) {
-        tok0 = p->tok_offsets[g];
-        tok1 = p->tok_offsets[g + 1];
-      } else {
-        tok0 = 0;
-        tok1 = p->T;
-      }
-      n_tt = (tok1 - tok0 + NT - 1) / NT;
-      nt = 0;
-      if (n_tt > 0) return true;  // groups without tokens are skipped
-    }
-    return false;
-  }
 };
 
 template <int NT>
@@ -147,26 +118,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&map_w);
     tma_prefetch_desc(&map_x);
   }
+  SchedTable* sched = reinterpret_cast<SchedTable*>(smem + S::OFF_SCHED);
+  const bool dense = p.tok_offsets == nullptr;
+  if (dense && warp == 2) sched_build(sched, nullptr, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous
   // kernel; its outputs (x, token offsets, y for ADD) are read only from here.
-  // A dense GEMM's first work units are known without them, so its producer
-  // also starts the weight half of the first ring stages before the wait.
+  // A dense GEMM's work items are known without them, so its producer also
+  // starts the weight half of the first ring stages before the wait.
   int npre = 0;
-  if (warp == 0 && lane == 0 && p.tok_offsets == nullptr) {
+  if (warp == 0 && lane == 0 && dense) {
     const uint64_t pol_w = l2_policy_evict_first();
-    UnitIter it{&p, NT};
+    SchedIter it{sched, p.m_tiles, NT, KB};
     while (npre < S::NS && it.next()) {
-      const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-      for (int kb = kb0; kb < kb1 && npre < S::NS; ++kb, ++npre) {
+      for (int kb = it.kb0; kb < it.kb1 && npre < S::NS; ++kb, ++npre) {
         mbar_arrive_expect_tx(&full[npre], S::STAGE);
         tma_load_2d(smem + npre * S::STAGE, &map_w, &full[npre], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
       }
     }
   }
   pdl_wait();
+  if (!dense) {  // the unit table of a grouped GEMM needs the token offsets
+    if (warp == 2) sched_build(sched, p.tok_offsets, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
+    __syncthreads();
+  }
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
@@ -174,12 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();  // weights stream once; activations stay in L2
-      UnitIter it{&p, NT};
+      SchedIter it{sched, p.m_tiles, NT, KB};
       int q = 0;  // global stage counter
       bool ok = true;
       while (ok && it.next()) {
-        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-        for (int kb = kb0; kb < kb1; ++kb, ++q) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb, ++q) {
           const int s = q % S::NS;
           if (q >= S::NS && !mbar_wait(&empty[s], ((q / S::NS) - 1) & 1, abort)) {
             raise_abort(abort, status, kStatusTimeout);
@@ -204,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_bf16_f32(kTileM, NT < 16 ? 16 : NT, 0, 0);
-      UnitIter it{&p, NT};
+      SchedIter it{sched, p.m_tiles, NT, KB};
       int q = 0, u = 0;
       bool ok = true;
       while (ok && it.next()) {
@@ -212,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (u >= 2 && !mbar_wait(&acc_empty[slot], ((u >> 1) - 1) & 1, abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + slot * S::TC;
-        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+        const int kb0 = it.kb0, kb1 = it.kb1;
         for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int s = q % S::NS;
           if (!mbar_wait(&full[s], (q / S::NS) & 1, abort)) { ok = false; break; }
@@ -240,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;  // 0..127
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     float* stg = reinterpret_cast<float*>(smem + S::OFF_STG) + (warp - 2) * 32 * 32;  // this warp's staging block
-    UnitIter it{&p, NT};
+    SchedIter it{sched, p.m_tiles, NT, KB};
     int u = 0, epi_phase = 0;
     while (it.next()) {
       const int slot = u & 1;
@@ -252,7 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem + ((qtr * 32) << 16) + slot * S::TC;
       const int tbase = it.tok0 + it.nt * NT;
       const int tcount = min(NT, it.tok1 - tbase);
-      const int tile_id = it.g * p.m_tiles + it.mt;
       constexpr int NCH = NT < 32 ? 1 : NT / 32;
       // output of one 32-token chunk of this thread's weight row (called by
       // all lanes of the warp)
@@ -323,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      float* part = p.splits > 1 ? p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM : nullptr;
+      const int nsplit = it.nsplit, tail_j = it.tail_j;
+      float* part = nsplit > 1 ? p.ws + ((int64_t)tail_j * nsplit + it.split) * (int64_t)NT * kTileM : nullptr;
       for (int c = 0; c < NCH; ++c) {
         uint32_t raw[32];
         tmem_ld32(taddr + c * 32, raw);
@@ -351,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         if (et == 0) {
-          const int prev = atomicAdd(&p.counters[tile_id], 1);
-          *last_flag = (prev == p.splits - 1) ? 1 : 0;
+          const int prev = atomicAdd(&p.counters[tail_j], 1);
+          *last_flag = (prev == nsplit - 1) ? 1 : 0;
         }
         if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
           raise_abort(abort, status, kStatusTimeout);
@@ -360,31 +336,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (*last_flag != 0) {
           __threadfence();
-          const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
+          const float* pbase = p.ws + (int64_t)tail_j * nsplit * (int64_t)NT * kTileM + r;
           constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
           for (int c = 0; c < NCH; ++c) {
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.0f;
             // four splits' loads in flight at a time, summed in split order
-            for (int s2 = 0; s2 < p.splits; s2 += 4) {
+            for (int s2 = 0; s2 < nsplit; s2 += 4) {
               float w4[4][CW];
 #pragma unroll
               for (int j = 0; j < 4; ++j)
 #pragma unroll
                 for (int i = 0; i < CW; ++i)
-                  w4[j][i] = s2 + j < p.splits ? __ldcg(pbase + (int64_t)(s2 + j) * NT * kTileM + (c * 32 + i) * kTileM)
+                  w4[j][i] = s2 + j < nsplit ? __ldcg(pbase + (int64_t)(s2 + j) * NT * kTileM + (c * 32 + i) * kTileM)
                                                : 0.0f;
 #pragma unroll
               for (int j = 0; j < 4; ++j)
-                if (s2 + j < p.splits) {
+                if (s2 + j < nsplit) {
 #pragma unroll
                   for (int i = 0; i < CW; ++i) v[i] += w4[j][i];
                 }
             }
             apply(c, v);
           }
-          if (et == 0) p.counters[tile_id] = 0;  // ready for the next call
+          if (et == 0) p.counters[tail_j] = 0;  // ready for the next call
         }
       }
     }
@@ -398,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int NT>
-int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int splits, int m_tiles) {
+int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int max_splits, int m_tiles) {
   using S = GemmShape<NT>;
   CUtensorMap map_w, map_x;
   const uint64_t w_rows = (uint64_t)a->G * a->M;
@@ -421,18 +397,23 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int splits, int m_tiles)
   p.y_f32 = a->y_f32;
   p.epi = a->epilogue;
   p.row_scale = a->row_scale;
-  p.splits = splits;
+  p.max_splits = max_splits;
   p.m_tiles = m_tiles;
-  p.n_tiles = a->G * m_tiles * splits;
   p.ws = nullptr;
   p.counters = nullptr;
   p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
                          a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
-  if (splits > 1) {
-    const size_t tiles = (size_t)m_tiles * a->G;
-    rc = ensure_workspace(ctx, tiles * splits * NT * kTileM * sizeof(float));
+  // A grouped launch's units are known only on the device (sched.cuh), so it
+  // takes every SM; a dense one launches no more CTAs than it has work items.
+  int grid = ctx->sm_count;
+  if (a->tok_offsets == nullptr)
+    grid = std::min(grid, sched_shape(a->G * m_tiles * ((a->T + NT - 1) / NT), grid, max_splits).items);
+  grid = std::max(grid, 1);
+  if (max_splits > 1) {
+    // split partials and tickets: at most one per CTA of the last round
+    rc = ensure_workspace(ctx, (size_t)grid * NT * kTileM * sizeof(float));
     if (rc != DSB_OK) return rc;
-    rc = ensure_counters(ctx, tiles);
+    rc = ensure_counters(ctx, grid);
     if (rc != DSB_OK) return rc;
     p.ws = static_cast<float*>(ctx->ws);
     p.counters = ctx->counters;
@@ -443,7 +424,6 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int splits, int m_tiles)
     DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
     attr_set = true;
   }
-  const int grid = std::min(p.n_tiles, ctx->sm_count);
   DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, kThreads, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
@@ -459,8 +439,9 @@ extern "C" int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* a) {
   if (ctx == nullptr) return DSB_EINVAL;
   if (a == nullptr || a->w == nullptr || a->x == nullptr || a->y == nullptr)
     return fail(ctx, DSB_EINVAL, "dsb_linear: null argument");
-  if (a->T <= 0 || a->M <= 0 || a->K <= 0 || a->G <= 0 || a->ldw < a->K || a->ldx <= 0)
-    return fail(ctx, DSB_EINVAL, "dsb_linear: bad sizes T=%d M=%d K=%d G=%d", a->T, a->M, a->K, a->G);
+  if (a->T <= 0 || a->M <= 0 || a->K <= 0 || a->G <= 0 || a->G > kSchedMaxGroups || a->ldw < a->K || a->ldx <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_linear: bad sizes T=%d M=%d K=%d G=%d (G <= %d)", a->T, a->M, a->K, a->G,
+                kSchedMaxGroups);
   if ((a->K % 64) || (a->ldw % 8) || (a->ldx % 8) || (a->x_group_col % 8))
     return fail(ctx, DSB_EINVAL, "dsb_linear: K must be a multiple of 64, row pitches and group column offsets multiples of 8");
   if (a->epilogue < DSB_EPI_STORE || a->epilogue > DSB_EPI_ROWSCALE)
@@ -476,16 +457,19 @@ extern "C" int dsb_linear(dsb_ctx* ctx, const dsb_linear_args* a) {
   const int KB = (a->K + kBK - 1) / kBK;
   int NT = 16;
   while (NT < bound && NT < 256) NT *= 2;
-  int splits = 1;
-  if (a->tok_offsets == nullptr && a->T <= 256) {
-    // small decode GEMMs: split K so the SMs share the weight stream
-    splits = pick_splits(m_tiles * a->G, KB, ctx->sm_count, 4, 128.0 * a->K * 2, NT);
+  // K splits of the units of the partial last round (sched.cuh): a small
+  // dense GEMM (fewer units than SMs) takes the cost model's choice, so the
+  // SMs share its weight stream; otherwise parts of at least 8 K blocks
+  int max_splits = std::max(1, std::min(8, KB / 8));
+  if (a->tok_offsets == nullptr) {
+    const int units = a->G * m_tiles * ((a->T + NT - 1) / NT);
+    if (units < ctx->sm_count) max_splits = pick_splits(units, KB, ctx->sm_count, 4, 128.0 * a->K * 2, NT);
   }
   switch (NT) {
-    case 16: return launch_gemm<16>(ctx, a, splits, m_tiles);
-    case 32: return launch_gemm<32>(ctx, a, splits, m_tiles);
-    case 64: return launch_gemm<64>(ctx, a, splits, m_tiles);
-    case 128: return launch_gemm<128>(ctx, a, splits, m_tiles);
-    default: return launch_gemm<256>(ctx, a, splits, m_tiles);
+    case 16: return launch_gemm<16>(ctx, a, max_splits, m_tiles);
+    case 32: return launch_gemm<32>(ctx, a, max_splits, m_tiles);
+    case 64: return launch_gemm<64>(ctx, a, max_splits, m_tiles);
+    case 128: return launch_gemm<128>(ctx, a, max_splits, m_tiles);
+    default: return launch_gemm<256>(ctx, a, max_splits, m_tiles);
   }
 }

@@ -36,6 +36,7 @@
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
 #include "epi.cuh"
+#include "sched.cuh"
 
 namespace dsb {
 namespace {
@@ -56,11 +57,10 @@ struct Fp8Params {
   int y_f32;
   int epi;
   const float* row_scale;
-  int splits;
+  int max_splits;     // parts of each unit of the partial last round (sched.cuh)
   int m_tiles;
-  int n_tiles;        // G * m_tiles * splits
-  float* ws;          // split partials
-  int* counters;      // per-tile tickets (zeroed; reset by the last split)
+  float* ws;          // split partials: [tail unit][split][NT][128]
+  int* counters;      // per-tail-unit tickets (zeroed; reset by the last split)
   int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
 };
 
@@ -83,48 +83,20 @@ struct Fp8Shape {
   static constexpr int SX = (EPI / 32) * 4 * HC * 4;          // [warps][2 buffers][2 row parities][HC]
   static constexpr int RS = (EPI / 32) * NT * 4;              // [warps][NT] token weights (ROWSCALE)
   static constexpr int STG = (GT / 32) * 32 * 32 * 4;         // output staging of the writing warps
-  static constexpr int NS = (212 * 1024 - XCH - SX - RS - STG) / STAGE;  // ring depth
+  static constexpr int SCH = ((int)sizeof(SchedTable) + 15) / 16 * 16;  // work schedule table
+  static constexpr int NS = (212 * 1024 - XCH - SX - RS - STG - SCH) / STAGE;  // ring depth
   static constexpr int OFF_BAR = NS * STAGE;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 2 * NBUF + 4) * 8;
   static constexpr int OFF_XCH = OFF_MISC + 64;
   static constexpr int OFF_SX = OFF_XCH + XCH;
   static constexpr int OFF_RS = OFF_SX + SX;
   static constexpr int OFF_STG = OFF_RS + RS;
-  static constexpr int SMEM = OFF_STG + STG + 1024;
+  static constexpr int OFF_SCHED = OFF_STG + STG;
+  static constexpr int SMEM = OFF_SCHED + SCH + 1024;
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per partial buffer
   static constexpr uint32_t TCOLS = NBUF * TC;       // <= 512
   static_assert(STAGE % 1024 == 0, "stage alignment");
   static_assert(SMEM <= 232448, "shared memory");
-};
-
-// Work units of this CTA: tiles blockIdx.x + i*gridDim.x, and inside each
-// tile its token tiles.  Every role walks the same sequence.
-struct UnitIter {
-  const Fp8Params* p;
-  int NT;
-  int tile = -1, nt = 0, n_tt = 0;
-  int g = 0, mt = 0, split = 0, tok0 = 0, tok1 = 0;
-
-  __device__ bool next() {
-    if (tile >= 0 && ++nt < n_tt) return true;
-    for (tile = (tile < 0 ? (int)blockIdx.x : tile + (int)gridDim.x); tile < p->n_tiles; tile += gridDim.x) {
-      split = tile % p->splits;
-      const int gm = tile / p->splits;
-      mt = gm % p->m_tiles;
-      g = gm / p->m_tiles;
-      if (p->tok_offsets != nullptr) {
-        tok0 = p->tok_offsets[g];
-        tok1 = p->tok_offsets[g + 1];
-      } else {
-        tok0 = 0;
-        tok1 = p->T;
-      }
-      n_tt = (tok1 - tok0 + NT - 1) / NT;
-      nt = 0;
-      if (n_tt > 0) return true;
-    }
-    return false;
-  }
 };
 
 template <int NT>
@@ -177,26 +149,32 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     tma_prefetch_desc(&map_w);
     tma_prefetch_desc(&map_x);
   }
+  SchedTable* sched = reinterpret_cast<SchedTable*>(smem + S::OFF_SCHED);
+  const bool dense = p.tok_offsets == nullptr;
+  if (dense && warp == 2) sched_build(sched, nullptr, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   // everything above (barriers, TMEM, descriptor prefetch) overlaps the previous
   // kernel; its outputs (x, token offsets, y for ADD) are read only from here.
-  // A dense GEMM's first work units are known without them, so its producer
-  // also starts the weight half of the first ring stages before the wait.
+  // A dense GEMM's work items are known without them, so its producer also
+  // starts the weight half of the first ring stages before the wait.
   int npre = 0;
-  if (warp == 0 && lane == 0 && p.tok_offsets == nullptr) {
+  if (warp == 0 && lane == 0 && dense) {
     const uint64_t pol_w = l2_policy_evict_first();
-    UnitIter it{&p, NT};
+    SchedIter it{sched, p.m_tiles, NT, KB};
     while (npre < S::NS && it.next()) {
-      const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-      for (int kb = kb0; kb < kb1 && npre < S::NS; ++kb, ++npre) {
+      for (int kb = it.kb0; kb < it.kb1 && npre < S::NS; ++kb, ++npre) {
         mbar_arrive_expect_tx(&full[npre], S::STAGE);
         tma_load_2d(smem + npre * S::STAGE, &map_w, &full[npre], kb * kBK, it.g * p.M + it.mt * kTileM, pol_w);
       }
     }
   }
   pdl_wait();
+  if (!dense) {  // the unit table of a grouped GEMM needs the token offsets
+    if (warp == 2) sched_build(sched, p.tok_offsets, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
+    __syncthreads();
+  }
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
@@ -204,12 +182,11 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
-      UnitIter it{&p, NT};
+      SchedIter it{sched, p.m_tiles, NT, KB};
       int q = 0;
       bool ok = true;
       while (ok && it.next()) {
-        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-        for (int kb = kb0; kb < kb1; ++kb, ++q) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb, ++q) {
           const int s = q % S::NS;
           if (q >= S::NS && !mbar_wait(&empty[s], ((q / S::NS) - 1) & 1, abort)) {
             raise_abort(abort, status, kStatusTimeout);
@@ -234,11 +211,11 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_e4m3_f32(kTileM, NT < 16 ? 16 : NT);
-      UnitIter it{&p, NT};
+      SchedIter it{sched, p.m_tiles, NT, KB};
       int q = 0, pk = 0;
       bool ok = true;
       while (ok && it.next()) {
-        const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
+        const int kb0 = it.kb0, kb1 = it.kb1;
         for (int kb = kb0; kb < kb1; ++kb, ++q, ++pk) {
           const int s = q % S::NS, b = pk % S::NBUF;
           if (pk >= S::NBUF && !mbar_wait(&part_empty[b], ((pk / S::NBUF) - 1) & 1, abort)) { ok = false; break; }
@@ -284,15 +261,15 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     // output staging block of the warps that write (the even K group's, or all)
     float* stg = reinterpret_cast<float*>(smem + S::OFF_STG) + ((warp - 2) % (S::GT / 32)) * 32 * 32;
     int epi_phase = 0;
-    UnitIter it{&p, NT};
+    SchedIter it{sched, p.m_tiles, NT, KB};
     int pk = 0, own = 0, u = 0;  // running partial index, K blocks this group promoted (KG > 1), units
     bool ok = true;
     while (ok && it.next()) {
       const int tbase = it.tok0 + it.nt * NT;
       const int tcount = min(NT, it.tok1 - tbase);
-      const int tile_id = it.g * p.m_tiles + it.mt;
-      const int kb0 = (int)((int64_t)it.split * KB / p.splits), kb1 = (int)((int64_t)(it.split + 1) * KB / p.splits);
-      const float* ws_even = p.w_scale + (int64_t)tile_id * p.scale_rows * KB;
+      const int wtile = it.g * p.m_tiles + it.mt;  // weight tile (its scale rows)
+      const int kb0 = it.kb0, kb1 = it.kb1;
+      const float* ws_even = p.w_scale + (int64_t)wtile * p.scale_rows * KB;
       const float* ws_odd = ws_even + (int64_t)(p.scale_rows - 1) * KB;
       const float* sxrow = p.x_scale + it.g * (p.x_group_col / kBK);
       if (p.epi == DSB_EPI_ROWSCALE && kg == 0) {
@@ -469,10 +446,11 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
         }
       };
 
-      if (p.splits > 1) {
+      const int nsplit = it.nsplit, tail_j = it.tail_j;
+      if (nsplit > 1) {
         // split-K: publish this split's promoted sum; the last split reduces
         // (into acc, in split order) and runs the epilogue
-        float* part = p.ws + ((int64_t)tile_id * p.splits + it.split) * (int64_t)NT * kTileM;
+        float* part = p.ws + ((int64_t)tail_j * nsplit + it.split) * (int64_t)NT * kTileM;
 #pragma unroll
         for (int i = 0; i < HC; ++i) part[(c0 + i) * kTileM + r] = acc[i];
         __threadfence();
@@ -481,8 +459,8 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           break;
         }
         if (et == 0) {
-          const int prev = atomicAdd(&p.counters[tile_id], 1);
-          *last_flag = (prev == p.splits - 1) ? 1 : 0;
+          const int prev = atomicAdd(&p.counters[tail_j], 1);
+          *last_flag = (prev == nsplit - 1) ? 1 : 0;
         }
         if (!__all_sync(0xffffffffu, mbar_rendezvous(epi_bar, epi_phase, abort))) {
           raise_abort(abort, status, kStatusTimeout);
@@ -490,14 +468,14 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
         }
         if (*last_flag == 0) continue;
         __threadfence();
-        const float* pbase = p.ws + (int64_t)tile_id * p.splits * (int64_t)NT * kTileM + r;
+        const float* pbase = p.ws + (int64_t)tail_j * nsplit * (int64_t)NT * kTileM + r;
 #pragma unroll
         for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
-        for (int s2 = 0; s2 < p.splits; ++s2) {
+        for (int s2 = 0; s2 < nsplit; ++s2) {
 #pragma unroll
           for (int i = 0; i < HC; ++i) acc[i] += __ldcg(pbase + (int64_t)s2 * NT * kTileM + (c0 + i) * kTileM);
         }
-        if (et == 0) p.counters[tile_id] = 0;
+        if (et == 0) p.counters[tail_j] = 0;
       }
       apply(acc);
     }
@@ -511,7 +489,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
 }
 
 template <int NT>
-int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_tiles) {
+int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int max_splits, int m_tiles) {
   using S = Fp8Shape<NT>;
   CUtensorMap map_w, map_x;
   const uint64_t w_rows = (uint64_t)a->G * a->M;
@@ -538,18 +516,23 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_til
   p.y_f32 = a->y_f32;
   p.epi = a->epilogue;
   p.row_scale = a->row_scale;
-  p.splits = splits;
+  p.max_splits = max_splits;
   p.m_tiles = m_tiles;
-  p.n_tiles = a->G * m_tiles * splits;
   p.ws = nullptr;
   p.counters = nullptr;
   p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
                          a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
-  if (splits > 1) {
-    const size_t tiles = (size_t)m_tiles * a->G;
-    rc = ensure_workspace(ctx, tiles * splits * NT * kTileM * sizeof(float));
+  // A grouped launch's units are known only on the device (sched.cuh), so it
+  // takes every SM; a dense one launches no more CTAs than it has work items.
+  int grid = ctx->sm_count;
+  if (a->tok_offsets == nullptr)
+    grid = std::min(grid, sched_shape(a->G * m_tiles * ((a->T + NT - 1) / NT), grid, max_splits).items);
+  grid = std::max(grid, 1);
+  if (max_splits > 1) {
+    // split partials and tickets: at most one per CTA of the last round
+    rc = ensure_workspace(ctx, (size_t)grid * NT * kTileM * sizeof(float));
     if (rc != DSB_OK) return rc;
-    rc = ensure_counters(ctx, tiles);
+    rc = ensure_counters(ctx, grid);
     if (rc != DSB_OK) return rc;
     p.ws = static_cast<float*>(ctx->ws);
     p.counters = ctx->counters;
@@ -560,7 +543,6 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int splits, int m_til
     DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
     attr_set = true;
   }
-  const int grid = std::min(p.n_tiles, ctx->sm_count);
   DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, S::THREADS, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
@@ -577,8 +559,10 @@ extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
   if (a == nullptr || a->w == nullptr || a->w_scale == nullptr || a->x == nullptr || a->x_scale == nullptr ||
       a->y == nullptr)
     return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: null argument");
-  if (a->T <= 0 || a->M <= 0 || a->K <= 0 || a->G <= 0 || a->ldw < a->K || a->ldx <= 0 || a->ld_xs <= 0)
-    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: bad sizes T=%d M=%d K=%d G=%d", a->T, a->M, a->K, a->G);
+  if (a->T <= 0 || a->M <= 0 || a->K <= 0 || a->G <= 0 || a->G > kSchedMaxGroups || a->ldw < a->K || a->ldx <= 0 ||
+      a->ld_xs <= 0)
+    return fail(ctx, DSB_EINVAL, "dsb_linear_fp8: bad sizes T=%d M=%d K=%d G=%d (G <= %d)", a->T, a->M, a->K, a->G,
+                kSchedMaxGroups);
   if ((a->K % kBK) || (a->ldw % 16) || (a->ldx % 16) || (a->x_group_col % kBK))
     return fail(ctx, DSB_EINVAL,
                 "dsb_linear_fp8: K and group column offsets must be multiples of 128, row pitches multiples of 16");
@@ -597,20 +581,21 @@ extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
   const int KB = a->K / kBK;
   int NT = 16;
   while (NT < bound && NT < 128) NT *= 2;
-  int splits = 1;
-  if (a->tok_offsets == nullptr && a->T <= 128) {
-    // small decode GEMMs (one token tile, so the split partials are per
-    // weight tile): split K so the SMs share the weight stream, in one wave
-    // of work units (the per-K-block promotion keeps this kernel's per-SM
-    // stream rate below the bf16 kernel's, so extra waves cost more than
-    // the idle SMs of a partial wave)
-    const int tiles = m_tiles * a->G;
-    splits = std::max(1, std::min({ctx->sm_count / std::max(1, tiles), KB / 2, 8}));
+  // K splits of the units of the partial last round (sched.cuh): a small
+  // dense GEMM (fewer units than SMs) splits K so the SMs share its weight
+  // stream, in one wave of work items (the per-K-block promotion keeps this
+  // kernel's per-SM stream rate below the bf16 kernel's, so extra waves cost
+  // more than the idle SMs of a partial wave); otherwise parts of at least
+  // 8 K blocks
+  int max_splits = std::max(1, std::min(8, KB / 8));
+  if (a->tok_offsets == nullptr) {
+    const int units = a->G * m_tiles * ((a->T + NT - 1) / NT);
+    if (units < ctx->sm_count) max_splits = std::max(1, std::min({ctx->sm_count / units, KB / 2, 8}));
   }
   switch (NT) {
-    case 16: return launch_fp8<16>(ctx, a, splits, m_tiles);
-    case 32: return launch_fp8<32>(ctx, a, splits, m_tiles);
-    case 64: return launch_fp8<64>(ctx, a, splits, m_tiles);
-    default: return launch_fp8<128>(ctx, a, splits, m_tiles);
+    case 16: return launch_fp8<16>(ctx, a, max_splits, m_tiles);
+    case 32: return launch_fp8<32>(ctx, a, max_splits, m_tiles);
+    case 64: return launch_fp8<64>(ctx, a, max_splits, m_tiles);
+    default: return launch_fp8<128>(ctx, a, max_splits, m_tiles);
   }
 }
