@@ -44,22 +44,26 @@ struct dsb_mla_plan {
 
 namespace dsb {
 
-// Split-K count for a dense decode GEMM: `tiles` 128-row weight tiles of
-// tile_bytes each, over `sm` SMs.  Each count s (1..8, every split at least
-// min_kb of the KB K blocks) costs the weight bytes plus, for s > 1, its fp32
-// partials (written and read back: tiles * s * 128 * NT * 8 bytes), divided
-// by the share of SM slots its waves of work units fill; the cheapest wins.
+// Split-K count for a small dense decode GEMM: `tiles` 128-row weight tiles
+// of tile_bytes each over `sm` SMs, every split at least min_kb of the KB K
+// blocks.  Time model per count s: the busiest CTA streams its waves of
+// tile_bytes / s at the per-SM rate (75 GB/s, or the HBM rate shared by the
+// busy SMs when that is lower), the fp32 partials (tiles * s * 128 * NT * 8
+// bytes written and read back) move at the HBM rate, and s > 1 adds the
+// split reduction's fixed latency (partial store, fence, ticket, two L2
+// round trips: about 4 us measured on B200).  The fastest count wins.
 inline int pick_splits(int tiles, int KB, int sm, int min_kb, double tile_bytes, int NT) {
+  constexpr double kSmRate = 75e9, kHbmRate = 6.5e12, kReduceLatency = 4e-6;
   int best = 1;
-  double best_cost = 0.0;
+  double best_t = 0.0;
   for (int s = 1; s <= 8; ++s) {
     if (s > 1 && KB / s < min_kb) break;
-    const int units = tiles * s, waves = (units + sm - 1) / sm;
-    const double fill = (double)units / ((double)waves * sm);
-    const double bytes = tiles * tile_bytes + (s > 1 ? (double)tiles * s * 128.0 * NT * 8.0 : 0.0);
-    const double cost = bytes / fill;
-    if (s == 1 || cost < best_cost) {
-      best_cost = cost;
+    const int units = tiles * s, waves = (units + sm - 1) / sm, active = units < sm ? units : sm;
+    const double rate = kSmRate < kHbmRate / active ? kSmRate : kHbmRate / active;
+    double t = waves * (tile_bytes / s) / rate;
+    if (s > 1) t += (double)tiles * s * 128.0 * NT * 8.0 / kHbmRate + kReduceLatency;
+    if (s == 1 || t < best_t) {
+      best_t = t;
       best = s;
     }
   }
@@ -103,8 +107,11 @@ int ensure_workspace(dsb_ctx* ctx, size_t bytes);
 int ensure_aux(dsb_ctx* ctx, size_t bytes);
 // Same for ctx->step (decode-step activations).
 int ensure_step(dsb_ctx* ctx, size_t bytes);
-// Ensure ctx->counters holds at least n zeroed ints.
+// Ensure ctx->counters holds at least n zeroed ints.  GEMM split tickets use
+// [0, kTicketFront) (at most one per CTA of a launch), the fused MoE front's
+// per-token tickets start at kTicketFront.
 int ensure_counters(dsb_ctx* ctx, size_t n);
+constexpr int kTicketFront = 1024;
 
 // 2D bf16/u8/f32 tiled tensor map over a row-major matrix [rows, cols] with
 // row pitch `pitch_bytes`; box = box_cols x box_rows; swizzle per CU enum.
@@ -142,10 +149,14 @@ int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pai
 // row's next RMSNorm (weights w_next) to xn_next as bf16.
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
                 float* h, const float* w_next = nullptr, float eps = 0.0f, void* xn_next = nullptr);
-// Post-attention RMSNorm + router logits + routing, one CTA per token.
+// Post-attention RMSNorm + router logits + routing (+ with `permute`, the
+// permutation of moe_permute over E + n_extra groups) in one launch, for
+// decode batches where moe_front_fits.  logits: [T, E] scratch.
+bool moe_front_fits(int T, int D, int E, int N);
 int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
               int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
-              float routed_scale, int n_extra, void* xn, int32_t* ids, float* weights);
+              float routed_scale, int n_extra, void* xn, float* logits, int32_t* ids, float* weights, int permute,
+              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm);
 // dsb_ep_combine with the next RMSNorm fused as in moe_combine.
 int ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
                int n_shared, float* h, const float* w_next, float eps, void* xn_next);

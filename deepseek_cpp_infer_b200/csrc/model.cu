@@ -1267,10 +1267,9 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     bf16* cache = kv->pool + (int64_t)li * layer_stride;
     // the RMSNorm after this layer's MoE block: the next layer's input norm, or the final norm
     const float* next_norm = li + 1 < c.num_hidden_layers ? m->layers[li + 1].in_norm : m->final_norm;
-    // post-attention norm, router and routing in one kernel (one CTA per token):
-    // it pulls the whole router matrix through one SM per token, slower than the
-    // three spread-out kernels at V2-Lite shape, so it is off
-    const bool fused_front = false;
+    // post-attention norm, router, routing (and the permutation) in one launch
+    // when the router is small enough to be read once per token from L2
+    const bool fused_front = L.moe && moe_front_fits(B, D, E, B * (k + L.n_shared));
     // attention block (model.cpp:126-138)
     if (!xn_ready) DSB_STEP(rmsnorm_rows(ctx, h, D, L.in_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
     xn_ready = false;
@@ -1326,7 +1325,8 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       // the shared experts run here on this rank's tokens
       if (fused_front) {
         DSB_STEP(moe_front(ctx, h, L.post_norm, B, D, c.rms_norm_eps, L.w_router, E, L.router_bias, k, c.scoring_func,
-                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, 0, xn, ids, wts));
+                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, 0, xn, lr, ids, wts, 0,
+                           nullptr, nullptr, nullptr, nullptr, nullptr));
       } else {
         DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
         DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
@@ -1371,15 +1371,15 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       const int kk = k + L.n_shared, G = E + L.n_shared;
       if (fused_front) {
         DSB_STEP(moe_front(ctx, h, L.post_norm, B, D, c.rms_norm_eps, L.w_router, E, L.router_bias, k, c.scoring_func,
-                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, L.n_shared, xn, ids,
-                           wts));
+                           c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, L.n_shared, xn, lr, ids,
+                           wts, 1, cnt, offs, dest, src, wperm));
       } else {
         DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
         DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
         DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
                            c.norm_topk_prob, c.routed_scaling_factor, ids, wts, L.n_shared));
+        DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
       }
-      DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
       const int eI = L.e_inter;
       if (L.e_gu8 != nullptr) {
         // gather + quantise the permuted rows in one pass, then the FP8 expert GEMMs

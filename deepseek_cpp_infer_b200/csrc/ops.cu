@@ -45,15 +45,12 @@ __device__ float block_sum(float v, float* red) {
 
 // y = x * (1 / sqrt(mean(x^2) + eps)) * w per row (src/ops/core/ops.cpp:17-23,
 // ds_rmsnorm_kernel elementwise_kernels.cu:13-28), written as bf16 and/or fp32.
-__global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int n,
-                                    float eps, __nv_bfloat16* __restrict__ yb, int64_t ldyb, float* __restrict__ yf,
-                                    int64_t ldyf) {
-  pdl_wait();
-  __shared__ float red[32];
-  const float* xr = x + blockIdx.x * ldx;
+// 1 / sqrt(mean(x^2) + eps) of one row, by the whole block; the summation
+// order depends only on blockDim.x, so every kernel that normalises a row
+// with the same block size gets the same bits.
+__device__ float row_inv_rms(const float* xr, int n, bool vec, float eps, float* red) {
   float ss = 0.0f;
-  const bool vec = (n % 4) == 0 && (ldx % 4) == 0;  // 16-byte rows
-  if (vec) {
+  if (vec) {  // 16-byte rows
     for (int i4 = threadIdx.x; i4 < n / 4; i4 += blockDim.x) {
       const float4 v = reinterpret_cast<const float4*>(xr)[i4];
       ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
@@ -65,7 +62,16 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, co
     for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
   }
   const float mean2 = __fdiv_rn(block_sum(ss, red), (float)n);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+}
+
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int n,
+                                    float eps, __nv_bfloat16* __restrict__ yb, int64_t ldyb, float* __restrict__ yf,
+                                    int64_t ldyf) {
+  pdl_wait();
+  __shared__ float red[32];
+  const float* xr = x + blockIdx.x * ldx;
+  const float inv = row_inv_rms(xr, n, (n % 4) == 0 && (ldx % 4) == 0, eps, red);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
     if (yb) yb[blockIdx.x * ldyb + i] = __float2bfloat16_rn(v);
@@ -150,21 +156,30 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
 
 // logits[t, e] = x[t] . W_gate[e] in fp32 (the reference's gate linear,
 // ops.cpp:115-117); one warp per (token, expert).
+// One warp's dot product of a normalised row with a router row (D a multiple
+// of 4): each lane takes every 32nd float4 in one explicit FMA chain, then
+// the warp sums the lanes, so the bits do not depend on where x lives.
+__device__ __forceinline__ float router_dot(const float* xr, const float* __restrict__ wr, int D, int lane) {
+  float acc = 0.0f;
+#pragma unroll 16  // loads in flight: one warp per expert leaves little else to hide their latency
+  for (int i = lane * 4; i < D; i += 128) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + i);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(wr + i));
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    acc = fmaf(a.w, b.w, acc);
+  }
+  return warp_sum(acc);
+}
+
 __global__ void router_logits_kernel(const float* __restrict__ x, const float* __restrict__ w, int T, int D, int E,
                                      float* __restrict__ logits) {
   pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= T * E) return;
   const int t = gw / E, e = gw % E;
-  const float* xr = x + (int64_t)t * D;
-  const float* wr = w + (int64_t)e * D;
-  float acc = 0.0f;
-  for (int i = lane * 4; i < D; i += 128) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + i);
-    const float4 b = *reinterpret_cast<const float4*>(wr + i);
-    acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
-  }
-  acc = warp_sum(acc);
+  const float acc = router_dot(x + (int64_t)t * D, w + (int64_t)e * D, D, lane);
   if (lane == 0) logits[(int64_t)t * E + e] = acc;
 }
 
@@ -320,10 +335,13 @@ __device__ __forceinline__ void route_token(const float* lg, const float* __rest
     }
   }
   // top-k by selection key, ties to the lower expert id
+  // k <= 8 picks, kept in registers (every index a compile-time constant)
   float wsel[8];
   int isel[8];
   float wsum = 0.0f;
-  for (int r = 0; r < k; ++r) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r >= k) break;
     float v = -INFINITY;
     int idx = 1 << 30;
 #pragma unroll
@@ -350,7 +368,9 @@ __device__ __forceinline__ void route_token(const float* lg, const float* __rest
   }
   if (lane == 0) {
     // the k routed picks, then n_extra always-on groups
-    for (int r = 0; r < k; ++r) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= k) break;
       float wv = wsel[r];
       if (norm_topk && wsum > 0.0f) wv = __fdiv_rn(wv, wsum);
       ids_row[r] = isel[r];
@@ -374,65 +394,16 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
               ids + (int64_t)t * kk, weights + (int64_t)t * kk, n_extra, lane);
 }
 
-// Post-attention RMSNorm, router logits and routing of one token per CTA (256
-// threads): the normalised row goes out as bf16 (the experts' input) and
-// stays in shared memory as fp32 for the E router dot products (one warp per
-// expert, the lane striding of router_logits_kernel), then warp 0 routes.
-// Replaces rmsnorm_rows + router_logits + route for decode batches.
-__global__ void __launch_bounds__(256) moe_front_kernel(const float* __restrict__ h, const float* __restrict__ w_norm,
-                                                        int D, float eps, const float* __restrict__ w_router, int E,
-                                                        const float* __restrict__ bias, int k, int scoring,
-                                                        int n_group, int topk_group, int norm_topk,
-                                                        float routed_scale, int n_extra,
-                                                        __nv_bfloat16* __restrict__ xn, int32_t* __restrict__ ids,
-                                                        float* __restrict__ weights) {
-  pdl_wait();
-  extern __shared__ float xs[];  // [D] normalised row, then [E] logits
-  __shared__ float red[32];
-  const int t = blockIdx.x;
-  const float* hr = h + (int64_t)t * D;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(hr[i], hr[i]));
-  const float mean2 = __fdiv_rn(block_sum(ss, red), (float)D);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    const float v = __fmul_rn(__fmul_rn(hr[i], inv), w_norm[i]);
-    xn[(int64_t)t * D + i] = __float2bfloat16_rn(v);
-    xs[i] = v;
-  }
-  __syncthreads();
-  float* lg = xs + D;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = warp; e < E; e += blockDim.x >> 5) {
-    const float* wr = w_router + (int64_t)e * D;
-    float acc = 0.0f;
-    for (int i = lane * 4; i < D; i += 128) {
-      const float4 a = *reinterpret_cast<const float4*>(xs + i);
-      const float4 b = *reinterpret_cast<const float4*>(wr + i);
-      acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) lg[e] = acc;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const int kk = k + n_extra;
-    route_token(lg, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids + (int64_t)t * kk,
-                weights + (int64_t)t * kk, n_extra, lane);
-  }
-}
-
 // Deterministic permutation of the N = T*k (token, slot) pairs by expert: the
 // pair with flat index i goes to dest[i] = offsets[e] + (number of earlier
 // pairs routed to e); src_pair is the inverse.  One warp walks the pairs in
 // order, 32 at a time, ranking equal experts with match.any.
-__global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ counts,
-                               int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
-                               int32_t* __restrict__ src_pair, const float* __restrict__ weights,
-                               float* __restrict__ w_perm, int* __restrict__ status) {
-  pdl_wait();
-  extern __shared__ int32_t cnt[];  // [E]
-  const int lane = threadIdx.x;
+// ids: the N expert ids, and weights (when w_perm is wanted) their routing
+// weights, both in shared memory; cnt is [E] ints of shared memory.
+__device__ void permute_warp(const int32_t* ids, int N, int E, int32_t* __restrict__ counts,
+                             int32_t* __restrict__ offsets, int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
+                             const float* weights, float* __restrict__ w_perm, int* __restrict__ status, int32_t* cnt,
+                             int lane) {
   for (int e = lane; e < E; e += 32) cnt[e] = 0;
   __syncwarp();
   for (int c = 0; c < N; c += 32) {
@@ -469,13 +440,120 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
   }
   if (lane == 0) offsets[E] = carry;
   __syncwarp();
+#pragma unroll 4
   for (int i = lane; i < N; i += 32) {
-    if ((unsigned)ids[i] >= (unsigned)E) continue;
-    const int d = offsets[ids[i]] + dest[i];
+    const int e = ids[i];
+    if ((unsigned)e >= (unsigned)E) continue;
+    const int d = offsets[e] + dest[i];
     dest[i] = d;
     src_pair[d] = i;
     if (w_perm != nullptr) w_perm[d] = weights[i];
   }
+}
+
+__global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ counts,
+                               int32_t* __restrict__ offsets, int32_t* __restrict__ dest,
+                               int32_t* __restrict__ src_pair, const float* __restrict__ weights,
+                               float* __restrict__ w_perm, int* __restrict__ status) {
+  pdl_wait();
+  extern __shared__ int32_t cnt[];  // [E] counts, then the N ids and their weights
+  int32_t* sids = cnt + E;
+  float* swts = reinterpret_cast<float*>(sids + N);
+#pragma unroll 8
+  for (int i = threadIdx.x; i < N; i += 32) {
+    sids[i] = ids[i];
+    if (w_perm != nullptr) swts[i] = weights[i];
+  }
+  __syncwarp();
+  permute_warp(sids, N, E, counts, offsets, dest, src_pair, swts, w_perm, status, cnt, threadIdx.x);
+}
+
+// The MoE front of a decode step in one launch: post-attention RMSNorm,
+// router logits, routing and (single GPU) the permutation by expert.  CTA
+// (b, t) normalises token t's row (the bf16 row for the experts is written by
+// b == 0) and computes the router logits of experts [16b, 16b+16), one warp
+// per expert.  The last of token t's CTAs to finish (a ticket) routes the
+// token; with the permutation, the last token to be routed permutes all
+// pairs.  Row norms, logits, routes and the permutation are bit-identical to
+// rmsnorm_rows + router_logits + route + permute (the same device functions,
+// the same block size).  tickets: T + 1 zeroed ints, re-zeroed here.
+constexpr int kFrontExperts = 16;
+
+__global__ void __launch_bounds__(256) moe_front_kernel(
+    const float* __restrict__ h, const float* __restrict__ w_norm, int D, float eps, const float* __restrict__ w_router,
+    int E, const float* __restrict__ bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
+    float routed_scale, int n_extra, __nv_bfloat16* __restrict__ xn, float* __restrict__ logits,
+    int32_t* __restrict__ ids, float* __restrict__ weights, int permute, int32_t* __restrict__ counts,
+    int32_t* __restrict__ offsets, int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
+    float* __restrict__ w_perm, int* __restrict__ tickets, int* __restrict__ status) {
+  pdl_wait();
+  extern __shared__ float xs[];  // [D] normalised row, [E] logits, [E + n_extra] permute counts
+  __shared__ float red[32];
+  __shared__ int last;
+  const int b = blockIdx.x, t = blockIdx.y, EB = gridDim.x, T = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* hr = h + (int64_t)t * D;
+  const float inv = row_inv_rms(hr, D, true, eps, red);
+  // (the element formula of rmsnorm_rows, four columns per thread and step)
+#pragma unroll 2
+  for (int i4 = threadIdx.x; i4 < D / 4; i4 += blockDim.x) {
+    const float4 hv = reinterpret_cast<const float4*>(hr)[i4];
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(w_norm) + i4);
+    float4 v;
+    v.x = __fmul_rn(__fmul_rn(hv.x, inv), wv.x);
+    v.y = __fmul_rn(__fmul_rn(hv.y, inv), wv.y);
+    v.z = __fmul_rn(__fmul_rn(hv.z, inv), wv.z);
+    v.w = __fmul_rn(__fmul_rn(hv.w, inv), wv.w);
+    reinterpret_cast<float4*>(xs)[i4] = v;
+    if (b == 0) {
+      __nv_bfloat162 p2[2] = {__floats2bfloat162_rn(v.x, v.y), __floats2bfloat162_rn(v.z, v.w)};
+      reinterpret_cast<uint2*>(xn + (int64_t)t * D)[i4] = *reinterpret_cast<const uint2*>(p2);
+    }
+  }
+  __syncthreads();
+  const int e1 = min(E, (b + 1) * kFrontExperts);
+  for (int e = b * kFrontExperts + warp; e < e1; e += blockDim.x >> 5) {
+    const float acc = router_dot(xs, w_router + (int64_t)e * D, D, lane);
+    if (lane == 0) logits[(int64_t)t * E + e] = acc;
+  }
+  // the last CTA of this token routes it
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(&tickets[t], 1) == EB - 1;
+    if (last) tickets[t] = 0;  // every CTA of the token has taken its ticket
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float* lg = xs + D;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) lg[e] = __ldcg(logits + (int64_t)t * E + e);
+  __syncthreads();
+  const int kk = k + n_extra;
+  if (warp == 0)
+    route_token(lg, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids + (int64_t)t * kk,
+                weights + (int64_t)t * kk, n_extra, lane);
+  if (!permute) return;
+  // the last token to be routed permutes every pair
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(&tickets[T], 1) == T - 1;
+    if (last) tickets[T] = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  int32_t* cnt = reinterpret_cast<int32_t*>(lg + E);  // [E + n_extra]
+  int32_t* sids = cnt + E + n_extra;                   // [T * kk] ids, then their weights
+  float* swts = reinterpret_cast<float*>(sids + T * kk);
+  for (int i = threadIdx.x; i < T * kk; i += blockDim.x) {
+    sids[i] = __ldcg(ids + i);
+    swts[i] = __ldcg(weights + i);
+  }
+  __syncthreads();
+  if (warp == 0)
+    permute_warp(sids, T * kk, E + n_extra, counts, offsets, dest, src_pair, swts, w_perm, status, cnt, lane);
 }
 
 // out[p] = x[src_pair[p] / k] (bf16 rows, 16-byte vectors).
@@ -679,10 +757,21 @@ int router_logits(dsb_ctx* ctx, const float* x, const float* w, int T, int D, in
   return launched(ctx);
 }
 
+bool moe_front_fits(int T, int D, int E, int N) {
+  // every CTA of a token re-reads nothing but its 16 router rows; the whole
+  // router matrix is read once per token from L2, so the fused front is for
+  // decode batches with a small router (the single-warp permutation bounds N)
+  return T >= 1 && (D % 4) == 0 && E <= 256 && N <= kPermSingleWarpMax &&
+         (double)T * E * D * 4.0 <= 32.0 * (1 << 20);
+}
+
 int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
               int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
-              float routed_scale, int n_extra, void* xn, int32_t* ids, float* weights) {
-  const size_t smem = (size_t)(D + E) * sizeof(float);
+              float routed_scale, int n_extra, void* xn, float* logits, int32_t* ids, float* weights, int permute,
+              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm) {
+  int rc = ensure_counters(ctx, kTicketFront + T + 1);
+  if (rc != DSB_OK) return rc;
+  const size_t smem = (size_t)(D + E + E + n_extra + 2 * T * (k + n_extra)) * sizeof(float);
   if (smem > 48 * 1024) {
     static bool attr_set = false;
     if (!attr_set) {
@@ -690,8 +779,10 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
       attr_set = true;
     }
   }
-  launch_pdl(moe_front_kernel, T, 256, smem, ctx->stream, h, w_norm, D, eps, w_router, E, bias, k, scoring, n_group,
-             topk_group, norm_topk, routed_scale, n_extra, static_cast<__nv_bfloat16*>(xn), ids, weights);
+  const dim3 grid((E + kFrontExperts - 1) / kFrontExperts, T);
+  launch_pdl(moe_front_kernel, grid, 256, smem, ctx->stream, h, w_norm, D, eps, w_router, E, bias, k, scoring, n_group,
+             topk_group, norm_topk, routed_scale, n_extra, static_cast<__nv_bfloat16*>(xn), logits, ids, weights,
+             permute, counts, offsets, dest, src_pair, w_perm, ctx->counters + kTicketFront, ctx->d_status);
   return launched(ctx);
 }
 
@@ -705,7 +796,7 @@ int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
                 int32_t* src_pair, const float* weights, float* w_perm) {
   if (N <= kPermSingleWarpMax) {
-    launch_pdl(permute_kernel, 1, 32, E * sizeof(int32_t), ctx->stream, ids, N, E, counts, offsets, dest, src_pair, weights,
+    launch_pdl(permute_kernel, 1, 32, (E + 2 * N) * sizeof(int32_t), ctx->stream, ids, N, E, counts, offsets, dest, src_pair, weights,
                                                                  w_perm, ctx->d_status);
     return launched(ctx);
   }
