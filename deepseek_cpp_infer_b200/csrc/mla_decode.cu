@@ -15,8 +15,10 @@
 //   MMA warp   : S = Q_r K_r^T (tcgen05, A = Q from TMEM, B = page from smem)
 //                then O_r += P V_r (A = P from TMEM, B = the same page, MN-major)
 //   4 softmax warps (thread i <-> head i <-> TMEM lane i):
-//                read S_r, exchange it with the peer CTA through distributed
-//                shared memory, S = S_0 + S_1 (bitwise equal in both CTAs),
+//                read S_r, exchange it with the peer CTA (each CTA writes
+//                its fp16 partial to a local send buffer, one thread ships
+//                the 16 KB tile with a single shared-to-shared bulk copy),
+//                S = S_0 + S_1 (bitwise equal in both CTAs),
 //                online softmax in the exp2 domain with a lazy running max,
 //                write P (bf16) to TMEM.
 // TMEM (512 columns): O [VD] | S [64] | P [32] | Q [(VD+PD)/2].
@@ -70,7 +72,9 @@ struct MlaShape {
   static constexpr int STAGE_BYTES = NCH * CH_BYTES + ROPE_BYTES;
   static constexpr int NSTAGE = (NCTA == 2) ? 4 : 8;
   static constexpr int XCH_BUF = kHeadsPad * kTok * 2;             // one tile of fp16 partial scores
-  static constexpr int XCH_BYTES = (NCTA == 2) ? 2 * XCH_BUF : 0;  // double-buffered
+  // send [2] then receive [2] buffers (double-buffered by page parity)
+  static constexpr int XCH_BYTES = (NCTA == 2) ? 4 * XCH_BUF : 0;
+  static constexpr int OFF_RECV_REL = 2 * XCH_BUF;
   // TMEM column map
   static constexpr uint32_t T_O = 0;
   static constexpr uint32_t T_S = VD;
@@ -86,11 +90,12 @@ struct MlaShape {
   static constexpr int OFF_XCH = NSTAGE * STAGE_BYTES;
   static constexpr int OFF_RED = OFF_XCH + XCH_BYTES;  // [3 slots][2 half][128]: row maxima (2 parities), final sums
   static constexpr int OFF_BAR = OFF_RED + 3 * 2 * kHeadsPad * 4;
-  static constexpr int NBAR = 2 * NSTAGE + 13;
+  static constexpr int NBAR = 2 * NSTAGE + 15;
   static constexpr int OFF_PAGES = OFF_BAR + NBAR * 8;
   static constexpr int OFF_MISC = OFF_PAGES + kMaxItemPages * 4;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static_assert(OFF_XCH % 128 == 0 && XCH_BUF % 16 == 0, "bulk copy alignment");
 };
 
 constexpr int kSoftmaxWarps = 8;    // two warps per TMEM lane quarter (column halves)
@@ -120,6 +125,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   uint64_t* peer_free = bars + 2 * S::NSTAGE + 8;  // [2] peer finished reading its XCH buffer
   uint64_t* red_bar = bars + 2 * S::NSTAGE + 10;   // [2] both column halves posted their row maxima
   uint64_t* fin_bar = bars + 2 * S::NSTAGE + 12;   // both halves posted their softmax sums
+  uint64_t* send_ready = bars + 2 * S::NSTAGE + 13;  // [2] every softmax thread wrote its send row
   int32_t* pages = reinterpret_cast<int32_t*>(smem + S::OFF_PAGES);
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
@@ -146,11 +152,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     mbar_init(q_ready, kSoftmaxThreads);
     mbar_init(drain, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&xch_full[b], 1);            // the local expect_tx arrival + 32 KB of st.async bytes
+      mbar_init(&xch_full[b], 1);            // the local expect_tx arrival + the peer's 16 KB bulk copy
       mbar_init(&peer_free[b], kSoftmaxWarps);  // one remote arrival per peer softmax warp
       mbar_init(&red_bar[b], kSoftmaxThreads);
     }
     mbar_init(fin_bar, kSoftmaxThreads);
+    for (int b = 0; b < 2; ++b) mbar_init(&send_ready[b], kSoftmaxThreads);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -263,31 +270,46 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     const int t = (int)(q * 32 + lane);  // head index == TMEM lane
     const uint32_t lane_off = (q * 32) << 16;
     const bool live = t < H;
-    // Q slice -> TMEM (K order: latent columns of this CTA, then its rope columns)
+    // Q slice -> TMEM (K order: latent columns of this CTA, then its rope
+    // columns): this thread's 16-column chunks c = hf, hf + 2, ..., every load
+    // issued before the first store
     {
-      uint32_t qv[16];
-      const uint32_t* ql = reinterpret_cast<const uint32_t*>(q_lat + ((int64_t)item.b * H + (live ? t : 0)) * R + rank * S::VD);
-      const uint32_t* qr = reinterpret_cast<const uint32_t*>(q_rope + ((int64_t)item.b * H + (live ? t : 0)) * P + rank * S::PD);
-      constexpr int NQC = S::QD / 32;  // 16-column chunks
-#pragma unroll 1
-      for (int c = (int)hf; c < NQC; c += 2) {
-        const uint32_t* src = (c < S::VD / 32) ? ql + c * 16 : qr + (c - S::VD / 32) * 16;
+      constexpr int NQC = S::QD / 32;        // 16-column chunks (32 bf16)
+      constexpr int NMY = (NQC + 1) / 2;     // chunks per thread (at most)
+      const uint4* ql = reinterpret_cast<const uint4*>(q_lat + ((int64_t)item.b * H + (live ? t : 0)) * R +
+                                                       rank * S::VD);
+      const uint4* qr = reinterpret_cast<const uint4*>(q_rope + ((int64_t)item.b * H + (live ? t : 0)) * P +
+                                                       rank * S::PD);
+      uint4 v[NMY][4];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          uint4 v = live ? *reinterpret_cast<const uint4*>(src + i) : make_uint4(0, 0, 0, 0);
-          qv[i] = v.x; qv[i + 1] = v.y; qv[i + 2] = v.z; qv[i + 3] = v.w;
+      for (int k = 0; k < NMY; ++k) {
+        const int c = 2 * k + (int)hf;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 x = make_uint4(0, 0, 0, 0);
+          if (live && c < NQC) x = (c < S::VD / 32) ? ql[c * 4 + i] : qr[(c - S::VD / 32) * 4 + i];
+          v[k][i] = x;
         }
-        tmem_st16(tmem + lane_off + S::T_Q + c * 16, qv);
+      }
+#pragma unroll
+      for (int k = 0; k < NMY; ++k) {
+        const int c = 2 * k + (int)hf;
+        if (c < NQC) {
+          const uint32_t w[16] = {v[k][0].x, v[k][0].y, v[k][0].z, v[k][0].w, v[k][1].x, v[k][1].y,
+                                  v[k][1].z, v[k][1].w, v[k][2].x, v[k][2].y, v[k][2].z, v[k][2].w,
+                                  v[k][3].x, v[k][3].y, v[k][3].z, v[k][3].w};
+          tmem_st16(tmem + lane_off + S::T_Q + c * 16, w);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(q_ready);
     }
 
-    uint32_t peer_xch = 0, peer_xch_full = 0, peer_peer_free = 0;
+    uint32_t peer_recv = 0, peer_xch_full = 0, peer_peer_free = 0;
     if (NCTA == 2) {
       const uint32_t peer = rank ^ 1u;
-      peer_xch = mapa_shared(smem_base + S::OFF_XCH + t * 128, peer);
+      peer_recv = mapa_shared(smem_base + S::OFF_XCH + S::OFF_RECV_REL, peer);
       peer_xch_full = mapa_shared(smem_u32(xch_full), peer);
       peer_peer_free = mapa_shared(smem_u32(peer_free), peer);
     }
@@ -314,8 +336,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       if (NCTA == 2) {
         // Scores are summed over the two CTAs' column slices.  Each partial is
         // scaled into the log2 domain and rounded to fp16 in both CTAs, so the
-        // pair computes bit-identical sums; my partial goes to the peer with
-        // st.async, completing on the peer's xch_full[buf].
+        // pair computes bit-identical sums.  My partial goes to my send
+        // buffer (row t = 128 bytes, 16-byte chunk c at c ^ (t & 7)); once all
+        // rows are written, thread 0 copies the tile to the peer's receive
+        // buffer in one bulk copy that completes on the peer's xch_full[buf].
+        // peer_free[buf] (the peer consumed page j-2) frees both my send
+        // buffer (that copy has landed) and the peer's receive buffer.
         uint32_t hv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -328,15 +354,21 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           ok = false;
           break;
         }
-        const uint32_t dst = peer_xch + buf * S::XCH_BUF;
-        const uint32_t rbar = peer_xch_full + buf * 8;
+        uint4* srow = reinterpret_cast<uint4*>(smem + S::OFF_XCH + buf * S::XCH_BUF + t * 128);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int pc = ((int)hf * 4 + c) ^ (t & 7);  // 16-byte chunk within the 128-byte row
-          st_async_v4_b32(dst + pc * 16, hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3], rbar);
+        for (int c = 0; c < 4; ++c)
+          srow[((int)hf * 4 + c) ^ (t & 7)] = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
+        fence_proxy_async_shared();  // read by the bulk copy
+        mbar_arrive(&send_ready[buf]);
+        if (threadIdx.x == 0) {
+          if (mbar_wait(&send_ready[buf], (j >> 1) & 1, abort)) {
+            bulk_copy_to_peer(peer_recv + buf * S::XCH_BUF, smem_base + S::OFF_XCH + buf * S::XCH_BUF, S::XCH_BUF,
+                              peer_xch_full + buf * 8);
+          }
         }
         if (!__all_sync(0xffffffffu, mbar_wait<true>(&xch_full[buf], (j >> 1) & 1, abort))) { ok = false; break; }
-        const uint4* row = reinterpret_cast<const uint4*>(smem + S::OFF_XCH + buf * S::XCH_BUF + t * 128);
+        const uint4* row =
+            reinterpret_cast<const uint4*>(smem + S::OFF_XCH + S::OFF_RECV_REL + buf * S::XCH_BUF + t * 128);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint4 v = row[((int)hf * 4 + c) ^ (t & 7)];
