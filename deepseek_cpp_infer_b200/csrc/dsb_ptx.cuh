@@ -182,13 +182,24 @@ __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_add
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-// A rendezvous of the threads counted by `bar` (an mbarrier initialised with
-// their number): arrive, then wait for the phase to complete.  Unlike a named
-// barrier it cannot hang when a participant has left after an abort: the wait
-// gives up when *abort is raised or the time limit passes.  Shared-memory
-// writes before the arrive are visible to every participant after the wait.
+// One arrival per warp on a barrier initialised with a warp count: lane 0
+// arrives after a __syncwarp, which orders the other lanes' earlier writes
+// (and, after their tcgen05 fences, their tensor-memory accesses) before the
+// arrival.  One arrival instead of 32 keeps the mbarrier traffic per event
+// at a warp count.  Every lane of the warp must call it.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+// A rendezvous of the warps counted by `bar` (an mbarrier initialised with
+// their number; every lane calls it): arrive once per warp, then wait for the
+// phase to complete.  Unlike a named barrier it cannot hang when a
+// participant has left after an abort: the wait gives up when *abort is
+// raised or the time limit passes.  Memory writes before the call are visible
+// to every participant after it.
 __device__ __forceinline__ bool mbar_rendezvous(uint64_t* bar, int& phase, volatile int* abort) {
-  mbar_arrive(bar);
+  warp_arrive(bar);
   const bool ok = mbar_wait(bar, (uint32_t)phase & 1u, abort);
   ++phase;
   return ok;

@@ -102,10 +102,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
-    mbar_init(epi_bar, 128);
+    mbar_init(epi_bar, 4);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // the accumulator slot is free once every chunk has been read
       tc_fence_before();
-      mbar_arrive(&acc_empty[slot]);
+      warp_arrive(&acc_empty[slot]);
       ++u;
       if (part != nullptr) {
         // the last split to finish sums the partials in split order

@@ -131,12 +131,12 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     }
     for (int b = 0; b < S::NBUF; ++b) {
       mbar_init(&part_full[b], 1);
-      mbar_init(&part_empty[b], S::GT);  // one K group reads each buffer
+      mbar_init(&part_empty[b], S::GT / 32);  // one arrival per warp of the K group reading the buffer
     }
     mbar_init(drain, 1);
-    mbar_init(xch_full, S::GT);
-    mbar_init(xch_empty, S::GT);
-    mbar_init(epi_bar, S::GT);
+    mbar_init(xch_full, S::GT / 32);  // (warp counts)
+    mbar_init(xch_empty, S::GT / 32);
+    mbar_init(epi_bar, S::GT / 32);
     *abort = 0;
     *no_abort = 0;
     fence_mbar_init();
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           if (l == NL - 1) {
             // the partial buffer is free once it has been read into registers
             tc_fence_before();
-            mbar_arrive(&part_empty[b]);
+            warp_arrive(&part_empty[b]);
           }
 #pragma unroll
           for (int i = 0; i < LW; i += 4) {
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           }
 #pragma unroll
           for (int i = 0; i < HC; ++i) xch[(c0 + i) * kTileM + r] = acc[i];
-          mbar_arrive(xch_full);
+          warp_arrive(xch_full);
           ++u;
           continue;
         }
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
         }
 #pragma unroll
         for (int i = 0; i < HC; ++i) acc[i] = __fadd_rn(acc[i], xch[(c0 + i) * kTileM + r]);
-        mbar_arrive(xch_empty);
+        warp_arrive(xch_empty);
         ++u;
       }
 

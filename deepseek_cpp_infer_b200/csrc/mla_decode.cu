@@ -146,20 +146,23 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, kSoftmaxThreads);
-    mbar_init(p_full, kSoftmaxThreads);
+    mbar_init(s_free, kSoftmaxWarps);
+    mbar_init(p_full, kSoftmaxWarps);
     mbar_init(pv_done, 1);
-    mbar_init(q_ready, kSoftmaxThreads);
+    mbar_init(q_ready, kSoftmaxWarps);
     mbar_init(drain, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&xch_full[b], 1);            // the local expect_tx arrival + the peer's 16 KB bulk copy
       mbar_init(&peer_free[b], kSoftmaxWarps);  // one remote arrival per peer softmax warp
-      mbar_init(&red_bar[b], kSoftmaxThreads);
+      mbar_init(&red_bar[b], kSoftmaxWarps);
     }
-    mbar_init(fin_bar, kSoftmaxThreads);
-    for (int b = 0; b < 2; ++b) mbar_init(&send_ready[b], kSoftmaxThreads);
+    mbar_init(fin_bar, kSoftmaxWarps);
+    for (int b = 0; b < 2; ++b) mbar_init(&send_ready[b], kSoftmaxWarps);
     *abort = 0;
     *no_abort = 0;
+    // the softmax warps' barriers count warps: each warp arrives once, from
+    // lane 0 after a __syncwarp that orders the other lanes' writes (shared
+    // memory, and TMEM with their tcgen05 fences) before the arrival
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(q_ready);
+      warp_arrive(q_ready);
     }
 
     uint32_t peer_recv = 0, peer_xch_full = 0, peer_peer_free = 0;
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(r0[i]);
       }
       tc_fence_before();
-      mbar_arrive(s_free);
+      warp_arrive(s_free);
 
       if (NCTA == 2) {
         // Scores are summed over the two CTAs' column slices.  Each partial is
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         for (int c = 0; c < 4; ++c)
           srow[((int)hf * 4 + c) ^ (t & 7)] = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
         fence_proxy_async_shared();  // read by the bulk copy
-        mbar_arrive(&send_ready[buf]);
+        warp_arrive(&send_ready[buf]);
         if (threadIdx.x == 0) {
           if (mbar_wait(&send_ready[buf], (j >> 1) & 1, abort)) {
             bulk_copy_to_peer(peer_recv + buf * S::XCH_BUF, smem_base + S::OFF_XCH + buf * S::XCH_BUF, S::XCH_BUF,
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
       float* red_j = red + (j & 1) * 2 * kHeadsPad;
       red_j[hf * kHeadsPad + t] = mx[0];
-      mbar_arrive(&red_bar[j & 1]);
+      warp_arrive(&red_bar[j & 1]);
       if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[j & 1], (j >> 1) & 1, abort))) { ok = false; break; }
       const float mt = fmaxf(mx[0], red_j[(hf ^ 1) * kHeadsPad + t]);
       // lazy rescale: keep the running max until a tile exceeds it by 2^8
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       tmem_st16(tmem + lane_off + S::T_P + hf * 16, pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      warp_arrive(p_full);
     }
     if (ok && n_tiles > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (n_tiles - 1) & 1, abort))) ok = false;
     if (!ok) {
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       // combine the two column halves of the softmax denominator
       float* red_l = red + 2 * 2 * kHeadsPad;  // slot 2
       red_l[hf * kHeadsPad + t] = l_half;
-      mbar_arrive(fin_bar);
+      warp_arrive(fin_bar);
       ok = __all_sync(0xffffffffu, mbar_wait(fin_bar, 0, abort));
     }
     if (!ok) {
