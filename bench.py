@@ -513,9 +513,12 @@ def run_model_ours(args):
     prefill_s = time.time() - t0
     nxt = greedy
 
+    # the logits come back into pinned host memory (the copy runs at PCIe rate)
+    logits_host = torch.empty((B, cfg["vocab_size"]), dtype=torch.float32, pin_memory=True).numpy()
+
     def step(want_logits=False):
         nonlocal nxt
-        nxt, lg = dsb.decode_step(ctx, model, kv, seqs, nxt, want_logits=want_logits)
+        nxt, lg = dsb.decode_step(ctx, model, kv, seqs, nxt, logits_out=logits_host if want_logits else None)
         return lg
 
     def timed(n, want_logits=False):
@@ -542,7 +545,7 @@ def run_model_ours(args):
     ms_max = max_over_ranks(ms)
     ctx_len = kv.seq_len(seqs[0])
     # end to end: the reference's ForwardOutput carries the logits, so e2e also
-    # copies every step's [B, vocab] fp32 logits back to the host
+    # copies every step's [B, vocab] fp32 logits back to (pinned) host memory
     barrier()
     ms_e2e = max_over_ranks(timed(args.steps, want_logits=True))
     # the dominant kernel alone, for the roofline line

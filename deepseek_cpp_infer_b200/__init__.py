@@ -595,17 +595,28 @@ class KVCache:
             pass
 
 
-def decode_step(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_logits=False):
-    """dsb_decode_step: one token per sequence; returns (greedy ids, logits or None)."""
+def decode_step(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_logits=False, logits_out=None):
+    """dsb_decode_step: one token per sequence; returns (greedy ids, logits or None).
+
+    logits_out: an optional C-contiguous float32 [B, vocab] host array that
+    receives the logits (e.g. a view of pinned memory, so the copy back runs
+    at full PCIe rate); otherwise a new array is allocated when want_logits.
+    """
     import numpy as np
 
     B = len(seq_ids)
     sids = (ctypes.c_int32 * B)(*[int(x) for x in seq_ids])
     toks = (ctypes.c_int32 * B)(*[int(x) for x in tokens])
     greedy = (ctypes.c_int32 * B)()
-    logits = np.empty((B, model.cfg.vocab_size), np.float32) if want_logits else None
+    logits = logits_out
+    if logits is not None:
+        if (logits.dtype != np.float32 or logits.shape != (B, model.cfg.vocab_size)
+                or not logits.flags["C_CONTIGUOUS"]):
+            raise ValueError("logits_out must be a C-contiguous float32 [B, vocab] array")
+    elif want_logits:
+        logits = np.empty((B, model.cfg.vocab_size), np.float32)
     ctx._check(ctx._l.dsb_decode_step(ctx.h, model.h, kv.h, sids, toks, B,
-                                      logits.ctypes.data if want_logits else None, greedy))
+                                      logits.ctypes.data if logits is not None else None, greedy))
     return np.array(greedy[:], np.int32), logits
 
 

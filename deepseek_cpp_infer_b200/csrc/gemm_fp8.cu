@@ -284,16 +284,21 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
       // The scales of the next K block are fetched (one value per lane) while
       // the current one is promoted, then stored premultiplied by the weight
       // scale of each row parity, so the promotion is one FMA per element.
+      // The loads run two of this group's K blocks ahead (registers nx/nwe/nwo
+      // hold the next block's scales, qx/qwe/qwo the one after), so an L2
+      // round trip has two promotion periods to land.
       float nx[PER], nwe = 0.0f, nwo = 0.0f;
-      auto load_sx = [&](int kb) {
+      float qx[PER], qwe = 0.0f, qwo = 0.0f;
+      auto fetch = [&](int kb, float (&x)[PER], float& we, float& wo) {
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
           const int i = (int)lane + 32 * j, t = c0 + i;
-          nx[j] = (i < HC && t < tcount) ? __ldg(sxrow + (int64_t)(tbase + t) * p.ld_xs + kb) : 0.0f;
+          x[j] = (i < HC && t < tcount) ? __ldg(sxrow + (int64_t)(tbase + t) * p.ld_xs + kb) : 0.0f;
         }
-        nwe = __ldg(ws_even + kb);
-        nwo = __ldg(ws_odd + kb);
+        we = __ldg(ws_even + kb);
+        wo = __ldg(ws_odd + kb);
       };
+      auto load_sx = [&](int kb) { fetch(kb, nx, nwe, nwo); };
       auto store_sx = [&](int buf) {
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
@@ -311,12 +316,13 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
         load_sx(kbf);
         store_sx((S::KG == 1 ? pk : own) & 1);
         __syncwarp();
+        if (kbf + S::KG < kb1) load_sx(kbf + S::KG);
       }
       for (int kb = kb0; kb < kb1; ++kb, ++pk) {
         if (S::KG > 1 && pk % S::KG != kg) continue;
         const int b = pk % S::NBUF, sb = (S::KG == 1 ? pk : own) & 1;  // TMEM partial buffer, scale buffer
         if constexpr (S::KG > 1) ++own;
-        if (kb + S::KG < kb1) load_sx(kb + S::KG);
+        if (kb + 2 * S::KG < kb1) fetch(kb + 2 * S::KG, qx, qwe, qwo);
         if (!__all_sync(0xffffffffu, mbar_wait(&part_full[b], (pk / S::NBUF) & 1, abort))) {
           raise_abort(abort, status, kStatusTimeout);
           ok = false;
@@ -351,6 +357,10 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
           __syncwarp();  // every lane is done with the buffer written next
           store_sx(sb ^ 1);
           __syncwarp();
+#pragma unroll
+          for (int j = 0; j < PER; ++j) nx[j] = qx[j];
+          nwe = qwe;
+          nwo = qwo;
         }
       }
       if (!ok) break;
