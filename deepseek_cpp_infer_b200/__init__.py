@@ -45,6 +45,7 @@ class Stats(ctypes.Structure):
         ("workspace_bytes", ctypes.c_uint64),
         ("gemm_calls", ctypes.c_uint64),
         ("decode_steps", ctypes.c_uint64),
+        ("prefill_tokens", ctypes.c_uint64),
     ]
 
 
@@ -164,6 +165,7 @@ _PROTOS = [
     ("dsb_kvcache_seq_len", ctypes.c_int, [_vp, _ci, ctypes.POINTER(ctypes.c_int)]),
     ("dsb_kvcache_free_blocks", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int64)]),
     ("dsb_decode_step", ctypes.c_int, [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, _vp, _c_i32p]),
+    ("dsb_prefill", ctypes.c_int, [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, _vp, _c_i32p, ctypes.POINTER(ctypes.c_int)]),
     ("dsb_mla_decode_noalloc", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _i64, _ci, _vp, _ci, _c_i32p, _ci, _ci, _ci, _ci, _cf, _vp]),
     (
@@ -618,6 +620,50 @@ def decode_step(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_l
     ctx._check(ctx._l.dsb_decode_step(ctx.h, model.h, kv.h, sids, toks, B,
                                       logits.ctypes.data if logits is not None else None, greedy))
     return np.array(greedy[:], np.int32), logits
+
+
+PREFILL_MAX_TOKENS = 4096
+
+
+def prefill(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, want_logits=False):
+    """dsb_prefill: token rows (seq_ids[i], tokens[i]) in one pass, a sequence's
+    tokens in order; returns (greedy ids, logits or None) for the last row of
+    each distinct sequence, in order of first appearance."""
+    import numpy as np
+
+    n = len(seq_ids)
+    if len(tokens) != n:
+        raise ValueError("seq_ids and tokens differ in length")
+    sids = (ctypes.c_int32 * n)(*[int(x) for x in seq_ids])
+    toks = (ctypes.c_int32 * n)(*[int(x) for x in tokens])
+    n_distinct = len(dict.fromkeys(int(x) for x in seq_ids))
+    greedy = (ctypes.c_int32 * max(1, n_distinct))()
+    logits = np.empty((n_distinct, model.cfg.vocab_size), np.float32) if want_logits else None
+    n_seq = ctypes.c_int(0)
+    ctx._check(ctx._l.dsb_prefill(ctx.h, model.h, kv.h, sids, toks, n,
+                                  logits.ctypes.data if want_logits else None, greedy, ctypes.byref(n_seq)))
+    return np.array(greedy[:n_seq.value], np.int32), logits
+
+
+def prefill_prompts(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, chunk: int = PREFILL_MAX_TOKENS):
+    """Prefill every sequence's prompt (lists of ids) through dsb_prefill in
+    chunks of at most `chunk` rows (the prompts interleaved position by
+    position); returns each sequence's greedy next id."""
+    import numpy as np
+
+    rows = []
+    longest = max(len(p) for p in prompts)
+    for i in range(longest):
+        for s, p in zip(seq_ids, prompts):
+            if i < len(p):
+                rows.append((int(s), int(p[i])))
+    nxt = {}
+    for c0 in range(0, len(rows), chunk):
+        part = rows[c0:c0 + chunk]
+        g, _ = prefill(ctx, model, kv, [r[0] for r in part], [r[1] for r in part])
+        for s, gid in zip(dict.fromkeys(r[0] for r in part), g):
+            nxt[s] = int(gid)
+    return np.array([nxt[int(s)] for s in seq_ids], np.int32)
 
 
 def generate(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, max_new_tokens: int, eos_id: int = -1):

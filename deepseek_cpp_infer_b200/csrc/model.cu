@@ -1120,33 +1120,51 @@ int lin8(dsb_ctx* ctx, const uint8_t* w, const float* ws, int scale_rows, const 
 
 }  // namespace
 
-extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
-                               const int32_t* tokens, int B, float* logits_host, int32_t* greedy_host) {
+namespace {
+
+constexpr int kPrefillMaxTokens = DSB_PREFILL_MAX_TOKENS;
+
+// One pass of B token rows through every layer.  Decode (prefill = false):
+// B distinct sequences, one token each; greedy ids (and logits) for every row.
+// Prefill: a sequence may appear several times (its tokens in order, appended
+// at consecutive positions; each attends to its cache up to its own
+// position), and the lm_head runs only on the last row of each distinct
+// sequence (in order of first appearance): *n_seq_out of them.
+int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, const int32_t* tokens,
+                   int B, bool prefill, float* logits_host, int32_t* greedy_host, int* n_seq_out) {
+  const char* fn = prefill ? "dsb_prefill" : "dsb_decode_step";
   if (ctx == nullptr || m == nullptr || kv == nullptr) return DSB_EINVAL;
-  if (!m->finalized) return fail(ctx, DSB_EINVAL, "dsb_decode_step: model not finalized");
-  if (seq_ids == nullptr || tokens == nullptr || greedy_host == nullptr || B <= 0 || B > kv->max_seqs)
-    return fail(ctx, DSB_EINVAL, "dsb_decode_step: bad arguments");
+  if (!m->finalized) return fail(ctx, DSB_EINVAL, "%s: model not finalized", fn);
+  if (seq_ids == nullptr || tokens == nullptr || greedy_host == nullptr || B <= 0 ||
+      B > (prefill ? kPrefillMaxTokens : kv->max_seqs))
+    return fail(ctx, DSB_EINVAL, "%s: bad arguments (B=%d)", fn, B);
+  if (prefill && m->ep != nullptr)
+    return fail(ctx, DSB_EUNSUPPORTED, "dsb_prefill: expert-parallel models decode token by token");
   const dsb_model_config& c = m->cfg;
   const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
   const int nope = c.qk_nope_head_dim, v = c.v_head_dim, V = c.vocab_size, E = c.n_routed_experts;
   const int k = c.num_experts_per_tok, QH = H * (nope + P), MB = kv->max_blocks_per_seq;
 
-  // ---- host: validate, append one position per sequence, build the step tables
+  // ---- host: validate, append one position per token, build the step tables
+  std::vector<int> seq_order;            // distinct sequences in order of first appearance
+  std::vector<int> added(kv->max_seqs, 0), last_row(kv->max_seqs, -1);
+  int need_pages = 0;
   for (int b = 0; b < B; ++b) {
     const int s = seq_ids[b];
     if (s < 0 || s >= kv->max_seqs || !kv->seq_live[s])
-      return fail(ctx, DSB_EINVAL, "dsb_decode_step: seq_ids[%d]=%d is not a live sequence", b, s);
-    if (tokens[b] < 0 || tokens[b] >= V)
-      return fail(ctx, DSB_EINVAL, "dsb_decode_step: token %d out of range", tokens[b]);
-    for (int b2 = 0; b2 < b; ++b2)
-      if (seq_ids[b2] == s) return fail(ctx, DSB_EINVAL, "dsb_decode_step: sequence %d appears twice", s);
-    if (kv->seq_len[s] >= MB * 64)
-      return fail(ctx, DSB_EINVAL, "dsb_decode_step: sequence %d is full (%d tokens)", s, kv->seq_len[s]);
+      return fail(ctx, DSB_EINVAL, "%s: seq_ids[%d]=%d is not a live sequence", fn, b, s);
+    if (tokens[b] < 0 || tokens[b] >= V) return fail(ctx, DSB_EINVAL, "%s: token %d out of range", fn, tokens[b]);
+    if (added[s] > 0 && !prefill) return fail(ctx, DSB_EINVAL, "dsb_decode_step: sequence %d appears twice", s);
+    const int pos = kv->seq_len[s] + added[s];
+    if (pos >= MB * 64) return fail(ctx, DSB_EINVAL, "%s: sequence %d is full (%d tokens)", fn, s, pos);
+    if (added[s] == 0) seq_order.push_back(s);
+    need_pages += (pos % 64 == 0) ? 1 : 0;
+    ++added[s];
+    last_row[s] = b;
   }
-  int need_pages = 0;
-  for (int b = 0; b < B; ++b) need_pages += (kv->seq_len[seq_ids[b]] % 64 == 0) ? 1 : 0;
-  if ((size_t)need_pages > kv->free_pages.size())
-    return fail(ctx, DSB_ENOMEM, "dsb_decode_step: out of cache pages");
+  if ((size_t)need_pages > kv->free_pages.size()) return fail(ctx, DSB_ENOMEM, "%s: out of cache pages", fn);
+  const int n_seq = (int)seq_order.size();
+  const int LM = prefill ? n_seq : B;  // rows through the lm_head
   int max_ns_host = 0;
   for (auto& L : m->layers) max_ns_host = std::max(max_ns_host, L.n_shared);
   const bool ep = m->ep != nullptr;
@@ -1157,9 +1175,12 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
     ep_cap = wd * ep_tmax * kg;
     if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "dsb_decode_step: B=%d above the expert group's max_tokens", B);
   }
-  // tokens | positions | block table | (expert parallel) shared-expert row sources and offsets
+  // tokens | positions | block table | (expert parallel) shared-expert row
+  // sources and offsets | (prefill) the lm_head rows
   const size_t n_shared_tab = ep ? (size_t)max_ns_host * B + max_ns_host + 1 : 0;
-  std::vector<int32_t> host_i((size_t)B * (2 + MB) + n_shared_tab, 0);
+  std::vector<int32_t> host_i((size_t)B * (2 + MB) + n_shared_tab + (prefill ? n_seq : 0), 0);
+  if (prefill)
+    for (int i = 0; i < n_seq; ++i) host_i[(size_t)B * (2 + MB) + n_shared_tab + i] = last_row[seq_order[i]];
   std::vector<int32_t> lens(B);
   for (int b = 0; b < B; ++b) {
     const int s = seq_ids[b];
@@ -1207,14 +1228,15 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   const size_t o_lr = take((size_t)B * std::max(E, 1) * 4), o_wts = take((size_t)BK * 4 + 4);
   const size_t o_wperm = take((size_t)BK * 4), o_yperm = take((size_t)RX * D * 4);
   const size_t o_ys = take(ep ? (size_t)max_ns * B * D * 4 : 4);
-  const size_t o_logits = take((size_t)B * V * 4), o_xn = take((size_t)B * D * 2), o_q = take((size_t)B * QH * 2);
+  const size_t o_logits = take((size_t)LM * V * 4), o_xn = take((size_t)B * D * 2), o_q = take((size_t)B * QH * 2);
+  const size_t o_xlm = take(prefill ? (size_t)n_seq * D * 2 : 4);  // (prefill) the lm_head rows of xn
   const size_t o_qrope = take((size_t)B * H * P * 2), o_qlat = take((size_t)B * H * R * 2);
   const size_t o_olat = take((size_t)B * H * R * 2), o_attn = take((size_t)B * H * v * 2);
   const size_t o_mid = take((size_t)B * std::max(max_I, 64) * 2);
   const size_t o_xperm = take((size_t)BK * D * 2), o_midp = take((size_t)RX * std::max(max_eI, 64) * 2);
   const size_t o_ids = take((size_t)BK * 4 + 4), o_cnt = take((size_t)(E + max_ns + 1) * 4);
   const size_t o_off = take((size_t)(E + max_ns + 2) * 4);
-  const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)B * 4);
+  const size_t o_dest = take((size_t)BK * 4), o_src = take((size_t)BK * 4), o_greedy = take((size_t)LM * 4);
   const size_t o_tab = take(host_i.size() * 4);
   // FP8 layers: activations quantised per token and 128 columns
   bool any_fp8 = false;
@@ -1246,6 +1268,7 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   const int32_t *d_tok = tab, *d_pos = tab + B, *d_bt = tab + 2 * B;
   const int32_t* d_srows = tab + (size_t)B * (2 + MB);           // shared-expert row sources (expert parallel)
   const int32_t* d_soff = d_srows + (size_t)max_ns_host * B;     // shared-expert row offsets
+  const int32_t* d_lmrows = tab + (size_t)B * (2 + MB) + n_shared_tab;  // (prefill) lm_head rows
   DSB_CUDA_TRY(ctx, cudaMemcpyAsync(tab, host_i.data(), host_i.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
 
   dsb_mla_plan plan;
@@ -1401,16 +1424,39 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
       xn_ready = true;
     }
   }
-  // final norm, lm_head, greedy (model.cpp:160-179)
+  // final norm, lm_head, greedy (model.cpp:160-179); a prefill keeps only each
+  // sequence's last row
   if (!xn_ready) DSB_STEP(rmsnorm_rows(ctx, h, D, m->final_norm, B, D, c.rms_norm_eps, xn, D, nullptr, 0));
-  DSB_STEP(linear(ctx, m->lm_head, D, xn, D, B, V, D, logits, V, 1, DSB_EPI_STORE));
-  DSB_STEP(argmax_rows(ctx, logits, V, B, V, greedy));
+  const bf16* xlm = xn;
+  if (prefill) {
+    DSB_STEP(gather_rows(ctx, xn, D, d_lmrows, n_seq, 1, D, Bf(o_xlm)));
+    xlm = Bf(o_xlm);
+  }
+  DSB_STEP(linear(ctx, m->lm_head, D, xlm, D, LM, V, D, logits, V, 1, DSB_EPI_STORE));
+  DSB_STEP(argmax_rows(ctx, logits, V, LM, V, greedy));
 #undef DSB_STEP
-  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(greedy_host, greedy, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  DSB_CUDA_TRY(ctx, cudaMemcpyAsync(greedy_host, greedy, (size_t)LM * 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (logits_host != nullptr)
-    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(logits_host, logits, (size_t)B * V * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  ctx->stats.decode_steps++;
+    DSB_CUDA_TRY(ctx, cudaMemcpyAsync(logits_host, logits, (size_t)LM * V * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (prefill) {
+    ctx->stats.prefill_tokens += (uint64_t)B;
+    if (n_seq_out != nullptr) *n_seq_out = n_seq;
+  } else {
+    ctx->stats.decode_steps++;
+  }
   return dsb_sync(ctx);
+}
+
+}  // namespace
+
+extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
+                               const int32_t* tokens, int B, float* logits_host, int32_t* greedy_host) {
+  return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, greedy_host, nullptr);
+}
+
+extern "C" int dsb_prefill(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
+                           const int32_t* tokens, int n_tok, float* logits_host, int32_t* greedy_host, int* n_seq) {
+  return forward_tokens(ctx, m, kv, seq_ids, tokens, n_tok, true, logits_host, greedy_host, n_seq);
 }
 
 // Batched greedy generation on the host over dsb_decode_step: ds::rt::generate

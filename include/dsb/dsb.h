@@ -60,6 +60,7 @@ typedef struct dsb_stats {
   uint64_t workspace_bytes;
   uint64_t gemm_calls;     /* dsb_linear launches */
   uint64_t decode_steps;   /* dsb_decode_step calls */
+  uint64_t prefill_tokens; /* token rows run by dsb_prefill */
 } dsb_stats;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -498,6 +499,27 @@ DSB_API int dsb_kvcache_fill_random(dsb_kvcache* kv, int seq_id, int n_tokens, u
  * after the step completed on the device. */
 DSB_API int dsb_decode_step(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
                             const int32_t* tokens, int B, float* logits, int32_t* greedy);
+
+/* Most token rows of one dsb_prefill call (longer prompts are fed in chunks). */
+#define DSB_PREFILL_MAX_TOKENS 4096
+
+/* Chunked prefill: n_tok token rows in one pass through every layer.  Row i
+ * is token tokens[i] of live sequence seq_ids[i] (HOST arrays); a sequence
+ * may appear several times, its tokens in prompt order, appended at
+ * consecutive positions after its current length.  Each row attends to its
+ * sequence's cache up to and including its own position, so the result is
+ * the same computation as feeding the rows one at a time through
+ * dsb_decode_step (the reference's token-by-token forward(),
+ * model.cpp:104-110), with every GEMM and the MoE batched over all rows.
+ * The lm_head runs only on the last row of each distinct sequence, in order
+ * of first appearance in seq_ids: *n_seq (HOST, may be NULL) of them; their
+ * greedy ids go to greedy (HOST int32 [n_seq]) and, when logits is not NULL,
+ * their logits to logits (HOST fp32 [n_seq, vocab]).  n_tok <=
+ * DSB_PREFILL_MAX_TOKENS.  Not for models bound to an expert-parallel group
+ * (DSB_EUNSUPPORTED).  No counterpart in the reference (it prefills token by
+ * token). */
+DSB_API int dsb_prefill(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
+                        const int32_t* tokens, int n_tok, float* logits, int32_t* greedy, int* n_seq);
 
 /* Batched greedy generation: ds::rt::generate (src/runtime/model.cpp:14-49)
  * for B sequences of the cache at once, on the host over dsb_decode_step.

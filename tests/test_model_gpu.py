@@ -189,3 +189,53 @@ def test_generate_matches_reference_and_ragged_batches(gpu_ctx, tiny):
     assert stop == together[1][: together[1].index(together[1][4]) + 1]
     kv.free_seq(sq)
     kv.close()
+
+
+def test_prefill_matches_reference_and_token_by_token(gpu_ctx, tiny, ref_margins):
+    """dsb_prefill (all prompt rows in one pass, or in chunks) against the
+    token-by-token path: the golden prompt prefilled at once gives the
+    reference's first generated token, and the cache it leaves decodes the
+    reference's continuation (32-token bar); the last prompt position's logits
+    meet the logits bar where the golden file has them; ragged prompts of
+    several sequences, prefilled together in chunks that cut across
+    sequences and cache pages, give each sequence the logits of decoding its
+    prompt alone, token by token (max-rel <= 2e-2: the GEMMs see other row
+    counts, so their fp32 summation order differs)."""
+    m, g = tiny
+    kv = dsb.KVCache(gpu_ctx, m, n_blocks=64, max_seqs=4, max_blocks_per_seq=8)
+    prompt, gen_ref = list(g["prompt"]), g["generated"]
+    s = kv.alloc_seq()
+    gid, lg = dsb.prefill(gpu_ctx, m, kv, [s] * len(prompt), prompt, want_logits=True)
+    assert kv.seq_len(s) == len(prompt)
+    assert int(gid[0]) == int(gen_ref[0])
+    last = len(prompt) - 1
+    if last in g["steps"].tolist():
+        seq = np.concatenate([g["prompt"], gen_ref])
+        check_logits(last, lg[0], g["logits"][g["steps"].tolist().index(last)], ref_margins, seq)
+    gen, nxt = [int(gid[0])], int(gid[0])
+    for _ in range(31):
+        gid, _ = dsb.decode_step(gpu_ctx, m, kv, [s], [nxt])
+        nxt = int(gid[0])
+        gen.append(nxt)
+    assert gen == gen_ref[:32].tolist()
+    kv.free_seq(s)
+
+    rng = np.random.default_rng(11)
+    prompts = [list(rng.integers(0, 4096, n)) for n in (5, 70, 33)]
+    alone = [run_sequence(gpu_ctx, m, kv, p, 1)[1][-1] for p in prompts]
+    seqs = [kv.alloc_seq() for _ in prompts]
+    rows = [(sq, p[i]) for i in range(70) for sq, p in zip(seqs, prompts) if i < len(p)]
+    last_lg = {}
+    for c0 in range(0, len(rows), 41):  # chunks that cut across sequences and pages
+        part = rows[c0:c0 + 41]
+        _, lgs = dsb.prefill(gpu_ctx, m, kv, [r[0] for r in part], [r[1] for r in part], want_logits=True)
+        for sq, row in zip(dict.fromkeys(r[0] for r in part), lgs):
+            last_lg[sq] = row
+    for sq, p, ref in zip(seqs, prompts, alone):
+        assert kv.seq_len(sq) == len(p)
+        err = max_rel(last_lg[sq], ref)
+        print(f"prefill vs token-by-token, prompt of {len(p)}: logits max-rel {err:.2e}")
+        assert err <= TOL
+    with pytest.raises(dsb.DsbError):  # more rows than one call takes
+        dsb.prefill(gpu_ctx, m, kv, [seqs[0]] * (dsb.PREFILL_MAX_TOKENS + 1), [0] * (dsb.PREFILL_MAX_TOKENS + 1))
+    kv.close()
