@@ -257,10 +257,13 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
   const float* inbox = reinterpret_cast<const float*>(win + L.off_inbox);
   const int t = blockIdx.x, k = L.k, D = L.D;
   __shared__ float red[32];
+  __shared__ float wsm[32];  // the token's routing weights (k <= 8), looked up once
+  if ((int)threadIdx.x < k) wsm[threadIdx.x] = weights[(size_t)t * k + threadIdx.x];
+  __syncthreads();
   // the weighted outputs w * out, the single-GPU combine's pre-weighted rows
   auto pick = [&](int j, int i4) {
     const float4 v = __ldcv(reinterpret_cast<const float4*>(inbox + ((size_t)t * k + j) * D) + i4);
-    const float wj = weights[(size_t)t * k + j];
+    const float wj = wsm[j];
     return make_float4(__fmul_rn(v.x, wj), __fmul_rn(v.y, wj), __fmul_rn(v.z, wj), __fmul_rn(v.w, wj));
   };
   combine_row(pick, k, D, n_shared > 0 ? shared + (size_t)t * D : nullptr, n_shared, (int64_t)T * D, h + (size_t)t * D,
@@ -304,9 +307,10 @@ extern "C" int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, i
   if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
   *out = nullptr;
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || n_experts <= 0 || n_experts % world ||
-      n_experts > 256 || hidden <= 0 || hidden % 8 || top_k <= 0 || max_tokens <= 0 ||
+      n_experts > 256 || hidden <= 0 || hidden % 8 || top_k <= 0 || top_k > 32 || max_tokens <= 0 ||
       (int64_t)world * max_tokens * top_k >= (1 << 24))
-    return fail(ctx, DSB_EINVAL, "dsb_ep_create: bad sizes (world <= 8, E <= 256 and divisible by world)");
+    return fail(ctx, DSB_EINVAL,
+                "dsb_ep_create: bad sizes (world <= 8, E <= 256 and divisible by world, top_k <= 32)");
   auto* ep = new dsb_ep();
   ep->ctx = ctx;
   ep->E = n_experts;

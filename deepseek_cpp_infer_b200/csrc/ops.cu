@@ -471,13 +471,13 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
 // The MoE front of a decode step in one launch: post-attention RMSNorm,
 // router logits, routing and (single GPU) the permutation by expert.  CTA
 // (b, t) normalises token t's row (the bf16 row for the experts is written by
-// b == 0) and computes the router logits of experts [16b, 16b+16), one warp
-// per expert.  The last of token t's CTAs to finish (a ticket) routes the
+// b == 0) and computes the router logits of experts [8b, 8b+8), one warp per
+// expert.  The last of token t's CTAs to finish (a ticket) routes the
 // token; with the permutation, the last token to be routed permutes all
 // pairs.  Row norms, logits, routes and the permutation are bit-identical to
 // rmsnorm_rows + router_logits + route + permute (the same device functions,
 // the same block size).  tickets: T + 1 zeroed ints, re-zeroed here.
-constexpr int kFrontExperts = 16;
+constexpr int kFrontExperts = 8;  // one expert per warp: more CTAs share the router matrix
 
 __global__ void __launch_bounds__(256) moe_front_kernel(
     const float* __restrict__ h, const float* __restrict__ w_norm, int D, float eps, const float* __restrict__ w_router,
@@ -663,14 +663,18 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, i
 // h[t] += (y[dest[t*k]] + ... + y[dest[t*k+k-1]]) + shared[t]: the order of
 // moe_step's accumulation (ops.cpp:133-145) followed by the residual add
 // (model.cpp:209).
+constexpr int kMaxCombinePicks = 32;  // k + shared groups per token
+
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ dest, int k, int D,
                                    const float* __restrict__ shared, float* __restrict__ h,
                                    const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next) {
   pdl_wait();
   __shared__ float red[32];
+  __shared__ const float4* rows[kMaxCombinePicks];  // the token's pick rows, looked up once
   const int t = blockIdx.x;
-  const int32_t* dt = dest + (int64_t)t * k;
-  auto pick = [&](int j, int i4) { return reinterpret_cast<const float4*>(y + (int64_t)dt[j] * D)[i4]; };
+  if ((int)threadIdx.x < k) rows[threadIdx.x] = reinterpret_cast<const float4*>(y + (int64_t)dest[(int64_t)t * k + threadIdx.x] * D);
+  __syncthreads();
+  auto pick = [&](int j, int i4) { return rows[j][i4]; };
   combine_row(pick, k, D, shared ? shared + (int64_t)t * D : nullptr, shared ? 1 : 0, 0, h + (int64_t)t * D, w_next,
               eps, xn_next ? xn_next + (int64_t)t * D : nullptr, red);
 }
@@ -826,6 +830,8 @@ int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pai
 
 int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k, int D, const float* shared,
                 float* h, const float* w_next, float eps, void* xn_next) {
+  if (k > kMaxCombinePicks || (D % 4) != 0)
+    return fail(ctx, DSB_EINVAL, "moe_combine: k=%d (at most %d) or D=%d (a multiple of 4)", k, kMaxCombinePicks, D);
   launch_pdl(moe_combine_kernel, T, 256, 0, ctx->stream, y, dest, k, D, shared, h, w_next, eps,
              static_cast<__nv_bfloat16*>(xn_next));
   return launched(ctx);

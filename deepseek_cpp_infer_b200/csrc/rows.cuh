@@ -43,11 +43,23 @@ __device__ __forceinline__ void combine_row(Pick pick, int k, int D, const float
                                             float eps, __nv_bfloat16* __restrict__ xn, float* red) {
   const int D4 = D / 4;
   float ss = 0.0f;
-  for (int i4 = threadIdx.x; i4 < D4; i4 += blockDim.x) {
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  // two columns (i4 and i4 + blockDim.x) per step keep twice the row loads
+  // in flight; every column's sum and the squares' order are unchanged
+  const int stride = (int)blockDim.x;
+  for (int i4 = threadIdx.x; i4 < D4; i4 += 2 * stride) {
+    const int i4b = i4 + stride;
+    const bool two = i4b < D4;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f), accb = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 4
-    for (int j = 0; j < k; ++j) add4(acc, pick(j, i4));
-    for (int s = 0; s < n_shared; ++s) add4(acc, reinterpret_cast<const float4*>(shared + s * shared_stride)[i4]);
+    for (int j = 0; j < k; ++j) {
+      add4(acc, pick(j, i4));
+      if (two) add4(accb, pick(j, i4b));
+    }
+    for (int s = 0; s < n_shared; ++s) {
+      const float4* sh = reinterpret_cast<const float4*>(shared + s * shared_stride);
+      add4(acc, sh[i4]);
+      if (two) add4(accb, sh[i4b]);
+    }
     float4 hv = reinterpret_cast<float4*>(h)[i4];
     add4(hv, acc);
     reinterpret_cast<float4*>(h)[i4] = hv;
@@ -55,6 +67,15 @@ __device__ __forceinline__ void combine_row(Pick pick, int k, int D, const float
     ss = __fadd_rn(ss, __fmul_rn(hv.y, hv.y));
     ss = __fadd_rn(ss, __fmul_rn(hv.z, hv.z));
     ss = __fadd_rn(ss, __fmul_rn(hv.w, hv.w));
+    if (two) {
+      float4 hb = reinterpret_cast<float4*>(h)[i4b];
+      add4(hb, accb);
+      reinterpret_cast<float4*>(h)[i4b] = hb;
+      ss = __fadd_rn(ss, __fmul_rn(hb.x, hb.x));
+      ss = __fadd_rn(ss, __fmul_rn(hb.y, hb.y));
+      ss = __fadd_rn(ss, __fmul_rn(hb.z, hb.z));
+      ss = __fadd_rn(ss, __fmul_rn(hb.w, hb.w));
+    }
   }
   if (w_next == nullptr) return;
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(rows_block_sum(ss, red), (float)D), eps)));
