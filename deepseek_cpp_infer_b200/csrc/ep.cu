@@ -422,7 +422,7 @@ int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float*
                                                            ep->d_ticket + 1, epoch);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   if (T > 0) {
-    launch_pdl(ep_combine_kernel, T, 256, 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, w_next,
+    launch_pdl(ep_combine_kernel, T, combine_threads(ep->L.D), 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, w_next,
                eps, static_cast<__nv_bfloat16*>(xn_next), epoch,
                                                   ctx->d_status);
     DSB_CUDA_TRY(ctx, cudaGetLastError());

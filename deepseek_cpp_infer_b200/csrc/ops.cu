@@ -832,7 +832,7 @@ int moe_combine(dsb_ctx* ctx, const float* y, const int32_t* dest, int T, int k,
                 float* h, const float* w_next, float eps, void* xn_next) {
   if (k > kMaxCombinePicks || (D % 4) != 0)
     return fail(ctx, DSB_EINVAL, "moe_combine: k=%d (at most %d) or D=%d (a multiple of 4)", k, kMaxCombinePicks, D);
-  launch_pdl(moe_combine_kernel, T, 256, 0, ctx->stream, y, dest, k, D, shared, h, w_next, eps,
+  launch_pdl(moe_combine_kernel, T, combine_threads(D), 0, ctx->stream, y, dest, k, D, shared, h, w_next, eps,
              static_cast<__nv_bfloat16*>(xn_next));
   return launched(ctx);
 }

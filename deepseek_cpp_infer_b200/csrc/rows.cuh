@@ -34,6 +34,16 @@ __device__ __forceinline__ void add4(float4& a, const float4 b) {
   a.w = __fadd_rn(a.w, b.w);
 }
 
+// Threads per token row for combine_row: enough that a row's float4 columns
+// go out in one step of two columns per thread (all of a row's loads in
+// flight together), at least 64 and at most 1024, a multiple of 32.  The
+// row's sum of squares is accumulated in this thread order, so every combine
+// of the same D (single GPU or expert parallel) must use the same count.
+__host__ __device__ inline int combine_threads(int D) {
+  int n = ((D / 4) / 2 + 31) / 32 * 32;
+  return n < 64 ? 64 : (n > 1024 ? 1024 : n);
+}
+
 // One token row of D (a multiple of 4), 16-byte vectors: acc = pick(0) + ...
 // + pick(k-1) + shared_0 + ... (fp32, in that order), h += acc; with w_next,
 // then xn = bf16(h * rsqrt(mean(h^2) + eps) * w_next).
