@@ -6,16 +6,17 @@
 //
 // The scales change every 128 columns of K, so the tensor cores cannot carry
 // one accumulator across K: each 128-deep K block is its own 4-instruction
-// kind::f8f6f4 MMA chain into one of two TMEM partial buffers, and the
-// epilogue warps promote it - acc += partial * sw * sx[t] in fp32 registers -
-// while the MMAs of the next block fill the other buffer.
+// kind::f8f6f4 MMA chain into one of the TMEM partial buffers (a ring that
+// fills all 512 columns), and the epilogue warps promote it - acc += partial *
+// sw * sx[t] in fp32 registers - while the MMAs of later blocks fill the
+// other buffers.
 //
 // Same tiling as the bf16 kernel: weights are the 128-row A operand ("swap
 // AB"), tokens the N side (16..128 columns), one persistent CTA per SM walks
-// the work tiles, the TMA ring streams across tile boundaries, and split-K
-// (dense groups with <= 128 tokens) writes fp32 partials reduced in split
-// order by the last split.  One stage (128 weight rows x 128 bytes) is exactly
-// one scale block and one 128-byte swizzle row.
+// the work units of a schedule built on the device (sched.cuh), the TMA ring
+// streams across unit boundaries, and split units write fp32 partials
+// reduced in split order by the last split.  One stage (128 weight rows x 128
+// bytes) is exactly one scale block and one 128-byte swizzle row.
 //
 // The reference has no FP8 path (its safetensors dtype parser stops at
 // F32/F16/BF16, src/hf/safetensors.cpp:12-20); this replaces the expert and
