@@ -102,8 +102,29 @@ class ModelConfig(ctypes.Structure):
          ("weights_fp8", ctypes.c_int)]
 
 
+DTYPE_OTHER = -1
+CKPT_MAX_DIMS = 8
+
+
+class TensorInfo(ctypes.Structure):
+    """dsb_tensor_info: one tensor of an opened checkpoint."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("dtype_name", ctypes.c_char_p), ("dtype", ctypes.c_int),
+                ("ndim", ctypes.c_int), ("shape", ctypes.c_int64 * CKPT_MAX_DIMS), ("data", ctypes.c_void_p),
+                ("nbytes", ctypes.c_uint64)]
+
+
 # (name, restype, argtypes) for every function of include/dsb/dsb.h
 _PROTOS = [
+    ("dsb_checkpoint_open", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_checkpoint_close", ctypes.c_int, [ctypes.c_void_p]),
+    ("dsb_checkpoint_error", ctypes.c_char_p, []),
+    ("dsb_checkpoint_config", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ModelConfig)]),
+    ("dsb_checkpoint_num_tensors", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    ("dsb_checkpoint_tensor", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(TensorInfo)]),
+    ("dsb_checkpoint_find", ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]),
+    ("dsb_model_upload_checkpoint", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     ("dsb_version", ctypes.c_int, []),
     ("dsb_ctx_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
     ("dsb_ctx_destroy", ctypes.c_int, [ctypes.c_void_p]),
@@ -133,9 +154,6 @@ _PROTOS = [
      [_vp, _vp, _i64, _ci, _vp, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
     ("dsb_ep_combine", ctypes.c_int, [_vp, _vp, _i64, _ci, _vp, _vp, _ci, _vp]),
     ("dsb_ep_destroy", ctypes.c_int, [_vp]),
-    ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
-    ("dsb_kvcache_fill_random", ctypes.c_int, [_vp, _ci, _ci, ctypes.c_uint64, ctypes.c_float]),
-    ("dsb_generate", ctypes.c_int, [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, _vp, _vp]),
     ("dsb_model_set_ep", ctypes.c_int, [_vp, _vp]),
     ("dsb_kvcache_fill_random", ctypes.c_int, [_vp, _ci, _ci, ctypes.c_uint64, ctypes.c_float]),
     ("dsb_generate", ctypes.c_int, [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, _vp, _vp]),
@@ -451,6 +469,13 @@ class Model:
         shape = (ctypes.c_int64 * a.ndim)(*a.shape)
         self.ctx._check(self.ctx._l.dsb_model_set_tensor(self.h, name.encode(), dt, shape, a.ndim, a.ctypes.data))
 
+    def upload_checkpoint(self, ck: "Checkpoint") -> tuple[int, int]:
+        """Upload every decode-path tensor of an opened checkpoint; returns
+        (tensors uploaded, tensors skipped)."""
+        up, skip = ctypes.c_int(), ctypes.c_int()
+        self.ctx._check(self.ctx._l.dsb_model_upload_checkpoint(self.h, ck.h, ctypes.byref(up), ctypes.byref(skip)))
+        return up.value, skip.value
+
     def set_ep(self, ep: "EP"):
         """Keep only the routed experts of `ep`'s rank; MoE layers exchange through the group."""
         self.ctx._check(self.ctx._l.dsb_model_set_ep(self.h, ep.h))
@@ -476,6 +501,88 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+class Checkpoint:
+    """A Hugging Face model directory opened on the host (dsb_checkpoint):
+    config.json plus safetensors shards, memory-mapped.  Needs no GPU."""
+
+    def __init__(self, path: str):
+        self._l = lib()
+        h = ctypes.c_void_p()
+        rc = self._l.dsb_checkpoint_open(os.fsencode(path), ctypes.byref(h))
+        if rc != DSB_OK:
+            raise DsbError(rc, self._l.dsb_checkpoint_error().decode())
+        self.h = h
+
+    def _check(self, rc: int):
+        if rc != DSB_OK:
+            raise DsbError(rc, self._l.dsb_checkpoint_error().decode())
+
+    def config(self) -> ModelConfig:
+        c = ModelConfig()
+        self._check(self._l.dsb_checkpoint_config(self.h, ctypes.byref(c)))
+        return c
+
+    def __len__(self) -> int:
+        n = ctypes.c_int()
+        self._check(self._l.dsb_checkpoint_num_tensors(self.h, ctypes.byref(n)))
+        return n.value
+
+    def info(self, i: int) -> dict:
+        t = TensorInfo()
+        self._check(self._l.dsb_checkpoint_tensor(self.h, i, ctypes.byref(t)))
+        return {"name": t.name.decode(), "dtype": t.dtype, "dtype_name": t.dtype_name.decode(),
+                "shape": tuple(t.shape[: t.ndim]), "nbytes": int(t.nbytes), "data": t.data}
+
+    def tensors(self) -> list[dict]:
+        return [self.info(i) for i in range(len(self))]
+
+    def find(self, name: str) -> int:
+        i = ctypes.c_int()
+        self._check(self._l.dsb_checkpoint_find(self.h, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def raw(self, name: str) -> bytes:
+        """A tensor's bytes, copied out of the mapped shard."""
+        i = self.find(name)
+        if i < 0:
+            raise KeyError(name)
+        t = self.info(i)
+        return ctypes.string_at(t["data"], t["nbytes"]) if t["nbytes"] else b""
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._l.dsb_checkpoint_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def load_model(ctx: "Context", path: str, ep: "EP | None" = None) -> "Model":
+    """Create a model from a checkpoint directory, bind it to `ep` (expert
+    parallel) when given, upload its decode-path tensors and finalize it."""
+    with Checkpoint(path) as ck:
+        m = Model(ctx, ck.config())
+        try:
+            if ep is not None:
+                m.set_ep(ep)
+            m.upload_checkpoint(ck)
+            m.finalize()
+        except Exception:
+            m.close()
+            raise
+    return m
 
 
 class EP:

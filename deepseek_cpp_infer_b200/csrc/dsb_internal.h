@@ -92,6 +92,11 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // Record an error message on the context and return `code`.
 int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 
+// The context and configuration a model was created with (for the host-side
+// checkpoint reader, which uploads through dsb_model_set_tensor).
+dsb_ctx* model_ctx(const dsb_model* m);
+const dsb_model_config* model_config(const dsb_model* m);
+
 // Check a CUDA runtime call; on failure record it and return DSB_ECUDA.
 #define DSB_CUDA_TRY(ctx, call)                                                                     \
   do {                                                                                              \

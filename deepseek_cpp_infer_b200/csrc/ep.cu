@@ -257,7 +257,7 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
   const float* inbox = reinterpret_cast<const float*>(win + L.off_inbox);
   const int t = blockIdx.x, k = L.k, D = L.D;
   __shared__ float red[32];
-  __shared__ float wsm[32];  // the token's routing weights (k <= 8), looked up once
+  __shared__ float wsm[32];  // the token's routing weights (k <= 32, checked at create), looked up once
   if ((int)threadIdx.x < k) wsm[threadIdx.x] = weights[(size_t)t * k + threadIdx.x];
   __syncthreads();
   // the weighted outputs w * out, the single-GPU combine's pre-weighted rows

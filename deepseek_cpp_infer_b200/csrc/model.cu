@@ -187,13 +187,23 @@ int upload_gate_up_half(dsb_model* m, bf16* dst, const std::vector<uint16_t>& sr
   return DSB_OK;
 }
 
+// Decimal digits [i, j) of s as an int; false past 9 digits (no exception
+// can leave the C ABI on a malformed name).
+bool parse_index(const std::string& s, size_t i, size_t j, int* out) {
+  if (j == i || j - i > 9) return false;
+  int v = 0;
+  for (size_t k = i; k < j; ++k) v = v * 10 + (s[k] - '0');
+  *out = v;
+  return true;
+}
+
 bool parse_layer(const std::string& name, int* layer, std::string* rest) {
   static const std::string pre = "model.layers.";
   if (name.compare(0, pre.size(), pre) != 0) return false;
   size_t i = pre.size(), j = i;
   while (j < name.size() && name[j] >= '0' && name[j] <= '9') ++j;
   if (j == i || j >= name.size() || name[j] != '.') return false;
-  *layer = std::stoi(name.substr(i, j - i));
+  if (!parse_index(name, i, j, layer)) return false;
   *rest = name.substr(j + 1);
   return true;
 }
@@ -204,7 +214,7 @@ bool parse_expert(const std::string& rest, int* e, std::string* proj) {
   size_t i = pre.size(), j = i;
   while (j < rest.size() && rest[j] >= '0' && rest[j] <= '9') ++j;
   if (j == i || j >= rest.size() || rest[j] != '.') return false;
-  *e = std::stoi(rest.substr(i, j - i));
+  if (!parse_index(rest, i, j, e)) return false;
   *proj = rest.substr(j + 1);
   return true;
 }
@@ -1515,3 +1525,6 @@ extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const i
   }
   return DSB_OK;
 }
+
+dsb_ctx* dsb::model_ctx(const dsb_model* m) { return m->ctx; }
+const dsb_model_config* dsb::model_config(const dsb_model* m) { return &m->cfg; }

@@ -534,6 +534,70 @@ DSB_API int dsb_generate(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const 
                          const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
                          int32_t eos_id, int32_t* out_ids, int32_t* out_counts);
 
+/* ------------------------------------------------------ checkpoint ingest */
+
+/* A Hugging Face model directory opened on the host: config.json plus either
+ * model.safetensors.index.json and the shards it names, or a single
+ * model.safetensors.  Shards are memory-mapped read-only; no tensor bytes are
+ * copied until dsb_model_upload_checkpoint.  Replaces the reference's loader
+ * chain: load_model_dir (src/hf/model_loader.cpp:17-94),
+ * load_safetensors_index (src/hf/weights_index.cpp:10-59),
+ * load_safetensors_header (src/hf/safetensors.cpp:42-95) and
+ * parse_deepseek_config (src/models/deepseek/config.cpp:9-52).  Beyond the
+ * reference: the F8_E4M3 dtype (its parse_dtype, safetensors.cpp:12-20, has
+ * none), the DeepSeek-V3 router fields of config.json, and checks that every
+ * tensor's byte range fits its shard and matches its dtype and shape, and
+ * that shard names stay inside the directory.  Host only: no GPU, no
+ * context. */
+typedef struct dsb_checkpoint dsb_checkpoint;
+
+#define DSB_DTYPE_OTHER (-1) /* a safetensors dtype the model does not take (I64, BOOL, F8_E5M2, ...) */
+#define DSB_CKPT_MAX_DIMS 8
+
+typedef struct dsb_tensor_info {
+  const char* name;       /* checkpoint name; valid until dsb_checkpoint_close */
+  const char* dtype_name; /* the safetensors dtype string ("BF16", "F8_E4M3", ...) */
+  int dtype;              /* DSB_DTYPE_* (F32, BF16, F16, F8E4M3) or DSB_DTYPE_OTHER */
+  int ndim;
+  int64_t shape[DSB_CKPT_MAX_DIMS];
+  const void* data; /* the tensor's bytes inside the mapped shard (host memory) */
+  uint64_t nbytes;
+} dsb_tensor_info;
+
+/* Open `dir`.  Fails with DSB_EINVAL (message from dsb_checkpoint_error) on a
+ * missing or malformed file, DSB_EUNSUPPORTED on a config this build does not
+ * run (a scoring_func other than softmax / sigmoid, FP8 blocks other than
+ * 128 x 128). */
+DSB_API int dsb_checkpoint_open(const char* dir, dsb_checkpoint** out);
+DSB_API int dsb_checkpoint_close(dsb_checkpoint* ck);
+/* The message of this thread's last failed dsb_checkpoint_* call. */
+DSB_API const char* dsb_checkpoint_error(void);
+/* config.json as a dsb_model_config, read the way parse_deepseek_config
+ * reads it (same keys, aliases and defaults), except:
+ *  - moe_intermediate_size is the key of that name; intermediate_size only
+ *    when it is absent (the reference lets intermediate_size override it,
+ *    config.cpp:35-36, and takes expert sizes from the weight shapes);
+ *  - scoring_func "sigmoid" with n_group / topk_group (DeepSeek-V3); softmax
+ *    routing is the plain top-k of the reference's moe_step (topk_method is
+ *    not read, as in the reference);
+ *  - weights_fp8 = 1 when quantization_config.quant_method is "fp8"
+ *    (informational: FP8 layers are chosen by each tensor's dtype). */
+DSB_API int dsb_checkpoint_config(const dsb_checkpoint* ck, dsb_model_config* out);
+DSB_API int dsb_checkpoint_num_tensors(const dsb_checkpoint* ck, int* n);
+/* Tensor i (0 <= i < n) in name order; dsb_checkpoint_find gives -1 in
+ * *index for a name the checkpoint lacks. */
+DSB_API int dsb_checkpoint_tensor(const dsb_checkpoint* ck, int i, dsb_tensor_info* out);
+DSB_API int dsb_checkpoint_find(const dsb_checkpoint* ck, const char* name, int* index);
+/* Upload every decode-path tensor of `ck` into `model` through
+ * dsb_model_set_tensor (create the model from dsb_checkpoint_config and bind
+ * it with dsb_model_set_ep first when expert-parallel; finalize afterwards).
+ * Skipped, and counted in *n_skipped: tensors of layers at or beyond the
+ * model's num_hidden_layers (DeepSeek-V3 ships its multi-token-prediction
+ * module as layer 61, which decoding does not run) and rotary_emb.inv_freq
+ * buffers.  Any other tensor the model does not know, or of a dtype it does
+ * not take, fails the call with the tensor's name. */
+DSB_API int dsb_model_upload_checkpoint(dsb_model* model, const dsb_checkpoint* ck, int* n_uploaded, int* n_skipped);
+
 #ifdef __cplusplus
 }
 #endif

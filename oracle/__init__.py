@@ -122,6 +122,7 @@ def ref() -> ctypes.CDLL:
         _proto(l, "ref_model_reset", None, [ctypes.c_void_p])
         _proto(l, "ref_model_step", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, f32p, i32p])
         _proto(l, "ref_model_generate", ctypes.c_int, [ctypes.c_void_p, i32p, ctypes.c_int, ctypes.c_int, i32p])
+        _proto(l, "ref_checkpoint_summary", ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int])
         _ref = l
     return _ref
 
@@ -160,3 +161,21 @@ def mla_decode_paged(q_lat, q_rope, cache, block_table, seq_lens, scale):
     assert rc == 0
     return out
 
+
+def ref_checkpoint_summary(path: str) -> tuple[dict, list[tuple]]:
+    """The reference's loader (parse_deepseek_config + load_model_dir) on a
+    model directory: (config fields, [(name, dtype enum, nbytes, shape)] in
+    name order).  Raises RuntimeError with the reference's message if it threw."""
+    buf = ctypes.create_string_buffer(1 << 22)
+    n = ref().ref_checkpoint_summary(os.fsencode(path), buf, len(buf))
+    text = buf.value.decode()
+    if n < 0:
+        raise RuntimeError(text)
+    cfg, tensors = {}, []
+    for line in text.splitlines():
+        f = line.split(" ")
+        if f[0] == "cfg":
+            cfg[f[1]] = f[2]
+        elif f[0] == "t":
+            tensors.append((f[1], int(f[2]), int(f[3]), tuple(int(x) for x in f[4:])))
+    return cfg, tensors

@@ -11,6 +11,7 @@
 #include "ds/core/math.h"
 #include "ds/core/ops.h"
 #include "ds/core/rope.h"
+#include "ds/hf/config.h"
 #include "ds/hf/model_loader.h"
 #include "ds/models/deepseek/config.h"
 #include "ds/models/deepseek/mla.h"
@@ -19,7 +20,9 @@
 #include "ds/models/deepseek/weights.h"
 #include "ds/runtime/model.h"
 
+#include <algorithm>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <exception>
 #include <memory>
@@ -277,6 +280,73 @@ __attribute__((visibility("default"))) int ref_model_generate(void* h, const std
   } catch (const std::exception&) {
     return -1;
   }
+}
+
+// The reference's loader on a model directory: parse_deepseek_config over
+// load_config_json(dir/config.json), and load_model_dir's tensor views, as
+// text ("cfg <field> <value>" lines, then "t <name> <dtype> <nbytes> <dims>"
+// per tensor in name order; dtype is the reference's DType enum value).
+// Returns the text length, or -1 with the exception message in buf.
+__attribute__((visibility("default"))) int ref_checkpoint_summary(const char* dir, char* buf, int len) {
+  std::string text;
+  int rc = 0;
+  try {
+    const std::string d(dir);
+    const auto cfg = ds::hf::parse_deepseek_config(ds::hf::load_config_json(d + "/config.json"));
+    // snprintf, not iostreams: this library is loaded into Python by ctypes
+    char line[512];
+    auto put_i = [&](const char* k, long long v) {
+      std::snprintf(line, sizeof line, "cfg %s %lld\n", k, v);
+      text += line;
+    };
+    auto put_f = [&](const char* k, double v) {
+      std::snprintf(line, sizeof line, "cfg %s %.9g\n", k, v);
+      text += line;
+    };
+    put_i("hidden_size", cfg.hidden_size);
+    put_i("intermediate_size", cfg.intermediate_size);
+    put_i("num_hidden_layers", cfg.num_hidden_layers);
+    put_i("num_attention_heads", cfg.num_attention_heads);
+    put_i("vocab_size", cfg.vocab_size);
+    put_i("max_position_embeddings", cfg.max_position_embeddings);
+    put_i("n_routed_experts", cfg.n_experts);
+    put_i("n_shared_experts", cfg.n_shared_experts);
+    put_i("num_experts_per_tok", cfg.moe_top_k);
+    put_i("moe_intermediate_size", cfg.moe_intermediate_size);
+    put_i("first_k_dense_replace", cfg.first_k_dense_replace);
+    put_i("norm_topk_prob", cfg.norm_topk_prob ? 1 : 0);
+    put_i("q_lora_rank", cfg.q_lora_rank);
+    put_i("kv_lora_rank", cfg.kv_lora_rank);
+    put_i("qk_nope_head_dim", cfg.qk_nope_head_dim);
+    put_i("qk_rope_head_dim", cfg.qk_rope_head_dim);
+    put_i("v_head_dim", cfg.v_head_dim);
+    text += "cfg scoring_func " + cfg.scoring_func + "\n";
+    put_f("rms_norm_eps", cfg.rms_norm_eps);
+    put_f("rope_theta", cfg.rope_theta);
+    put_f("routed_scaling_factor", cfg.routed_scaling_factor);
+    const auto m = ds::hf::load_model_dir(d);
+    std::vector<std::string> names;
+    for (const auto& kv : m.tensors) names.push_back(kv.first);
+    std::sort(names.begin(), names.end());
+    for (const auto& n : names) {
+      const auto& t = m.tensors.at(n);
+      std::snprintf(line, sizeof line, " %d %zu", static_cast<int>(t.dtype), t.nbytes);
+      text += "t " + n + line;
+      for (auto x : t.shape) {
+        std::snprintf(line, sizeof line, " %lld", static_cast<long long>(x));
+        text += line;
+      }
+      text += "\n";
+    }
+  } catch (const std::exception& e) {
+    text = e.what();
+    rc = -1;
+  }
+  if (len <= 0) return -1;
+  const int n = static_cast<int>(std::min<std::size_t>(text.size(), static_cast<std::size_t>(len - 1)));
+  std::memcpy(buf, text.data(), static_cast<std::size_t>(n));
+  buf[n] = 0;
+  return rc == 0 ? n : -1;
 }
 
 }  // extern "C"
