@@ -102,6 +102,13 @@ class ModelConfig(ctypes.Structure):
          ("weights_fp8", ctypes.c_int)]
 
 
+class Sampling(ctypes.Structure):
+    """dsb_sampling (ds::core::SamplerConfig)."""
+
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int), ("top_p", ctypes.c_float),
+                ("seed", ctypes.c_uint32)]
+
+
 DTYPE_OTHER = -1
 CKPT_MAX_DIMS = 8
 
@@ -116,6 +123,10 @@ class TensorInfo(ctypes.Structure):
 
 # (name, restype, argtypes) for every function of include/dsb/dsb.h
 _PROTOS = [
+    ("dsb_decode_step_sampled", ctypes.c_int,
+     [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, ctypes.POINTER(Sampling), ctypes.POINTER(ctypes.c_float), _vp, _c_i32p]),
+    ("dsb_generate_sampled", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, ctypes.POINTER(Sampling), _vp, _vp]),
     ("dsb_checkpoint_open", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     ("dsb_checkpoint_close", ctypes.c_int, [ctypes.c_void_p]),
     ("dsb_checkpoint_error", ctypes.c_char_p, []),
@@ -168,6 +179,7 @@ _PROTOS = [
     ("dsb_gather_rows", ctypes.c_int, [_vp, _vp, _i64, _vp, _ci, _ci, _ci, _vp]),
     ("dsb_moe_combine", ctypes.c_int, [_vp, _vp, _vp, _ci, _ci, _ci, _vp, _vp]),
     ("dsb_argmax", ctypes.c_int, [_vp, _vp, _i64, _ci, _ci, _vp]),
+    ("dsb_sample", ctypes.c_int, [_vp, _vp, _i64, _ci, _ci, _cf, _ci, _cf, _vp, _vp]),
     ("dsb_embed", ctypes.c_int, [_vp, _vp, _ci, _vp, _ci, _ci, _vp]),
     ("dsb_model_create", ctypes.c_int, [_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(ctypes.c_void_p)]),
     ("dsb_model_destroy", ctypes.c_int, [_vp]),
@@ -389,6 +401,12 @@ class Context:
     def argmax(self, logits, out):
         B, V = logits.shape
         self._check(self._l.dsb_argmax(self.h, _ptr(logits), logits.stride(0), B, V, _ptr(out)))
+
+    def sample(self, logits, uniforms, out, temperature=1.0, top_k=0, top_p=0.0):
+        """Sampled id per row of logits [B, V] (fp32) with one uniform draw per row."""
+        B, V = logits.shape
+        self._check(self._l.dsb_sample(self.h, _ptr(logits), logits.stride(0), B, V, temperature, top_k, top_p,
+                                       _ptr(uniforms), _ptr(out)))
 
     def embed(self, table, tokens, h):
         import torch
@@ -773,8 +791,10 @@ def prefill_prompts(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, c
     return np.array([nxt[int(s)] for s in seq_ids], np.int32)
 
 
-def generate(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, max_new_tokens: int, eos_id: int = -1):
-    """dsb_generate: greedy continuation of every prompt (lists of ids); returns one id list per sequence."""
+def generate(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, max_new_tokens: int, eos_id: int = -1,
+             sampling: "Sampling | None" = None):
+    """dsb_generate (greedy), or dsb_generate_sampled when `sampling` is given:
+    the continuation of every prompt (lists of ids); one id list per sequence."""
     import numpy as np
 
     B = len(prompts)
@@ -783,6 +803,28 @@ def generate(ctx: Context, model: Model, kv: KVCache, seq_ids, prompts, max_new_
     sid = np.ascontiguousarray(np.asarray(seq_ids, np.int32))
     out = np.zeros((B, max(1, max_new_tokens)), np.int32)
     cnt = np.zeros(B, np.int32)
-    ctx._check(ctx._l.dsb_generate(ctx.h, model.h, kv.h, sid.ctypes.data, B, toks.ctypes.data, offs.ctypes.data,
-                                   max_new_tokens, eos_id, out.ctypes.data, cnt.ctypes.data))
+    if sampling is None:
+        ctx._check(ctx._l.dsb_generate(ctx.h, model.h, kv.h, sid.ctypes.data, B, toks.ctypes.data,
+                                       offs.ctypes.data, max_new_tokens, eos_id, out.ctypes.data, cnt.ctypes.data))
+    else:
+        ctx._check(ctx._l.dsb_generate_sampled(ctx.h, model.h, kv.h, sid.ctypes.data, B, toks.ctypes.data,
+                                               offs.ctypes.data, max_new_tokens, eos_id, ctypes.byref(sampling),
+                                               out.ctypes.data, cnt.ctypes.data))
     return [out[b, :cnt[b]].tolist() for b in range(B)]
+
+
+def decode_step_sampled(ctx: Context, model: Model, kv: KVCache, seq_ids, tokens, sampling: "Sampling", uniforms,
+                        want_logits=False):
+    """dsb_decode_step_sampled: one token per sequence, next ids sampled with
+    one uniform draw per row; returns (ids, logits or None)."""
+    import numpy as np
+
+    B = len(seq_ids)
+    sids = (ctypes.c_int32 * B)(*[int(x) for x in seq_ids])
+    toks = (ctypes.c_int32 * B)(*[int(x) for x in tokens])
+    u = (ctypes.c_float * B)(*[float(x) for x in uniforms])
+    out = (ctypes.c_int32 * B)()
+    logits = np.empty((B, model.cfg.vocab_size), np.float32) if want_logits else None
+    ctx._check(ctx._l.dsb_decode_step_sampled(ctx.h, model.h, kv.h, sids, toks, B, ctypes.byref(sampling), u,
+                                              logits.ctypes.data if logits is not None else None, out))
+    return np.array(out[:], np.int32), logits

@@ -166,6 +166,9 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
 int ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
                int n_shared, float* h, const float* w_next, float eps, void* xn_next);
 int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
+// Sampled id per row (ds::core::Sampler::sample); uniforms[B] on the device.
+int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k, float top_p,
+                const float* uniforms, int32_t* out);
 int embed(dsb_ctx* ctx, const void* table, int bf16, const int32_t* tokens, int B, int D, float* h);
 
 }  // namespace dsb

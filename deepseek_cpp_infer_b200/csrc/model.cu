@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <cstring>
 #include <string>
+#include <random>
 #include <vector>
 
 #include "dsb_internal.h"
@@ -1140,14 +1141,24 @@ constexpr int kPrefillMaxTokens = DSB_PREFILL_MAX_TOKENS;
 // at consecutive positions; each attends to its cache up to its own
 // position), and the lm_head runs only on the last row of each distinct
 // sequence (in order of first appearance): *n_seq_out of them.
+// With `samp`, the id of each lm_head row is sampled (dsb_sample) with the
+// draw uniforms_host[row] instead of taken greedily.
 int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, const int32_t* tokens,
-                   int B, bool prefill, float* logits_host, int32_t* greedy_host, int* n_seq_out) {
-  const char* fn = prefill ? "dsb_prefill" : "dsb_decode_step";
+                   int B, bool prefill, float* logits_host, int32_t* greedy_host, int* n_seq_out,
+                   const dsb_sampling* samp = nullptr, const float* uniforms_host = nullptr) {
+  const char* fn = prefill ? "dsb_prefill" : (samp ? "dsb_decode_step_sampled" : "dsb_decode_step");
   if (ctx == nullptr || m == nullptr || kv == nullptr) return DSB_EINVAL;
   if (!m->finalized) return fail(ctx, DSB_EINVAL, "%s: model not finalized", fn);
   if (seq_ids == nullptr || tokens == nullptr || greedy_host == nullptr || B <= 0 ||
       B > (prefill ? kPrefillMaxTokens : kv->max_seqs))
     return fail(ctx, DSB_EINVAL, "%s: bad arguments (B=%d)", fn, B);
+  if (samp != nullptr) {
+    if (prefill || uniforms_host == nullptr || !std::isfinite(samp->temperature) || !std::isfinite(samp->top_p))
+      return fail(ctx, DSB_EINVAL, "%s: bad sampling arguments", fn);
+    for (int b = 0; b < B; ++b)
+      if (!(uniforms_host[b] >= 0.0f && uniforms_host[b] <= 1.0f))
+        return fail(ctx, DSB_EINVAL, "%s: uniforms[%d] is not in [0, 1]", fn, b);
+  }
   if (prefill && m->ep != nullptr)
     return fail(ctx, DSB_EUNSUPPORTED, "dsb_prefill: expert-parallel models decode token by token");
   const dsb_model_config& c = m->cfg;
@@ -1186,11 +1197,13 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "dsb_decode_step: B=%d above the expert group's max_tokens", B);
   }
   // tokens | positions | block table | (expert parallel) shared-expert row
-  // sources and offsets | (prefill) the lm_head rows
+  // sources and offsets | (prefill) the lm_head rows | (sampling) the draws
   const size_t n_shared_tab = ep ? (size_t)max_ns_host * B + max_ns_host + 1 : 0;
-  std::vector<int32_t> host_i((size_t)B * (2 + MB) + n_shared_tab + (prefill ? n_seq : 0), 0);
+  const size_t o_draws = (size_t)B * (2 + MB) + n_shared_tab + (prefill ? n_seq : 0);
+  std::vector<int32_t> host_i(o_draws + (samp ? (size_t)LM : 0), 0);
   if (prefill)
     for (int i = 0; i < n_seq; ++i) host_i[(size_t)B * (2 + MB) + n_shared_tab + i] = last_row[seq_order[i]];
+  if (samp) std::memcpy(host_i.data() + o_draws, uniforms_host, (size_t)LM * 4);
   std::vector<int32_t> lens(B);
   for (int b = 0; b < B; ++b) {
     const int s = seq_ids[b];
@@ -1443,7 +1456,11 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     xlm = Bf(o_xlm);
   }
   DSB_STEP(linear(ctx, m->lm_head, D, xlm, D, LM, V, D, logits, V, 1, DSB_EPI_STORE));
-  DSB_STEP(argmax_rows(ctx, logits, V, LM, V, greedy));
+  if (samp != nullptr)
+    DSB_STEP(sample_rows(ctx, logits, V, LM, V, samp->temperature, samp->top_k, samp->top_p,
+                         reinterpret_cast<const float*>(tab + o_draws), greedy));
+  else
+    DSB_STEP(argmax_rows(ctx, logits, V, LM, V, greedy));
 #undef DSB_STEP
   DSB_CUDA_TRY(ctx, cudaMemcpyAsync(greedy_host, greedy, (size_t)LM * 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (logits_host != nullptr)
@@ -1464,32 +1481,53 @@ extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, cons
   return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, greedy_host, nullptr);
 }
 
+extern "C" int dsb_decode_step_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
+                                       const int32_t* tokens, int B, const dsb_sampling* sampling,
+                                       const float* uniforms_host, float* logits_host, int32_t* ids_host) {
+  if (ctx != nullptr && sampling == nullptr) return fail(ctx, DSB_EINVAL, "dsb_decode_step_sampled: no sampling config");
+  return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, ids_host, nullptr, sampling, uniforms_host);
+}
+
 extern "C" int dsb_prefill(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
                            const int32_t* tokens, int n_tok, float* logits_host, int32_t* greedy_host, int* n_seq) {
   return forward_tokens(ctx, m, kv, seq_ids, tokens, n_tok, true, logits_host, greedy_host, n_seq);
 }
 
-// Batched greedy generation on the host over dsb_decode_step: ds::rt::generate
+namespace {
+
+// Batched generation on the host over the decode step: ds::rt::generate
 // (src/runtime/model.cpp:14-49) for B sequences at once.  Each sequence first
 // consumes its prompt token by token (DeepSeekModel::forward,
-// src/models/deepseek/model.cpp:104-110), then feeds back its greedy id; it
+// src/models/deepseek/model.cpp:104-110), then feeds back its next id; it
 // stops after max_new_tokens ids or at eos_id (>= 0; the eos id is kept, as
 // the reference does).  Sequences with different prompt lengths are stepped
 // together: each call decodes one token for every sequence still running.
-extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
-                            const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
-                            int32_t eos_id, int32_t* out_ids, int32_t* out_counts) {
+// The next id is greedy unless `samp` asks for sampling (temperature, top_k
+// or top_p above 0, model.cpp:32-34); then sequence b draws one uniform per
+// generated id from its own std::mt19937 seeded with seed + b (seed 0:
+// std::random_device), through a fresh std::uniform_real_distribution<float>,
+// as the reference's Sampler draws (src/core/sampler.cpp:21, 69-70).
+int generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+             const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens, int32_t eos_id,
+             const dsb_sampling* samp, int32_t* out_ids, int32_t* out_counts, const char* fn) {
   if (ctx == nullptr || m == nullptr || kv == nullptr) return DSB_EINVAL;
   if (seq_ids == nullptr || prompt_tokens == nullptr || prompt_offsets == nullptr || out_ids == nullptr ||
       out_counts == nullptr || B <= 0 || max_new_tokens < 0)
-    return fail(ctx, DSB_EINVAL, "dsb_generate: bad arguments");
+    return fail(ctx, DSB_EINVAL, "%s: bad arguments", fn);
   if (m->ep != nullptr)
-    return fail(ctx, DSB_EUNSUPPORTED, "dsb_generate: expert-parallel models step every rank together; drive "
-                                       "dsb_decode_step directly");
+    return fail(ctx, DSB_EUNSUPPORTED, "%s: expert-parallel models step every rank together; drive "
+                                       "dsb_decode_step directly", fn);
+  const bool sampling = samp != nullptr && (samp->temperature > 0.0f || samp->top_k > 0 || samp->top_p > 0.0f);
+  std::vector<std::mt19937> rng;
+  if (sampling) {
+    std::random_device rd;
+    for (int b = 0; b < B; ++b) rng.emplace_back(samp->seed != 0 ? samp->seed + (uint32_t)b : rd());
+  }
+  std::vector<float> draws;
   for (int b = 0; b < B; ++b) {
     out_counts[b] = 0;
     if (prompt_offsets[b + 1] - prompt_offsets[b] < 1)
-      return fail(ctx, DSB_EINVAL, "dsb_generate: sequence %d has an empty prompt", b);
+      return fail(ctx, DSB_EINVAL, "%s: sequence %d has an empty prompt", fn, b);
   }
   if (max_new_tokens == 0) return DSB_OK;
   std::vector<int> fed(B, 0);           // prompt tokens consumed
@@ -1510,7 +1548,22 @@ extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const i
     }
     if (rows.empty()) break;
     greedy.resize(rows.size());
-    const int rc = dsb_decode_step(ctx, m, kv, ids.data(), toks.data(), (int)rows.size(), nullptr, greedy.data());
+    int rc;
+    if (sampling) {
+      // one draw for each row whose step yields a generated id (prompt rows keep theirs)
+      draws.assign(rows.size(), 0.5f);
+      for (size_t r = 0; r < rows.size(); ++r) {
+        const int b = rows[r];
+        if (fed[b] + 1 >= prompt_offsets[b + 1] - prompt_offsets[b]) {
+          std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+          draws[r] = dist(rng[(size_t)b]);
+        }
+      }
+      rc = forward_tokens(ctx, m, kv, ids.data(), toks.data(), (int)rows.size(), false, nullptr, greedy.data(),
+                          nullptr, samp, draws.data());
+    } else {
+      rc = dsb_decode_step(ctx, m, kv, ids.data(), toks.data(), (int)rows.size(), nullptr, greedy.data());
+    }
     if (rc != DSB_OK) return rc;
     for (size_t r = 0; r < rows.size(); ++r) {
       const int b = rows[r];
@@ -1524,6 +1577,24 @@ extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const i
     }
   }
   return DSB_OK;
+}
+
+}  // namespace
+
+extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+                            const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
+                            int32_t eos_id, int32_t* out_ids, int32_t* out_counts) {
+  return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, nullptr, out_ids,
+                  out_counts, "dsb_generate");
+}
+
+extern "C" int dsb_generate_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+                                    const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
+                                    int32_t eos_id, const dsb_sampling* sampling, int32_t* out_ids,
+                                    int32_t* out_counts) {
+  if (ctx != nullptr && sampling == nullptr) return fail(ctx, DSB_EINVAL, "dsb_generate_sampled: no sampling config");
+  return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, sampling, out_ids,
+                  out_counts, "dsb_generate_sampled");
 }
 
 dsb_ctx* dsb::model_ctx(const dsb_model* m) { return m->ctx; }

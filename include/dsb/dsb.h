@@ -403,6 +403,22 @@ DSB_API int dsb_ep_destroy(dsb_ep* ep);
  * on the host, cuda_backend.cpp:746-757). */
 DSB_API int dsb_argmax(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
 
+/* Stochastic sampling: ds::core::Sampler::sample (src/core/sampler.cpp:23-77)
+ * for B rows of logits [B, V] (row pitch ld, fp32, device) at once.
+ * Temperature (<= 0 reads as 1), then a top-k cut (0 < top_k < V; ties at the
+ * boundary keep the lower ids), softmax over the kept items, a top-p nucleus
+ * cut (0 < top_p < 1: the shortest descending-probability prefix whose mass
+ * reaches top_p, renormalised), and the item at which the cumulative mass
+ * reaches uniforms[b] (device, one draw in [0, 1) per row, from the caller's
+ * generator, as the reference draws one per call).  The cumulative mass runs
+ * in id order when no cut is active (the reference's order) and in
+ * descending probability, ties to the lower id, when one is (the reference's
+ * order there is unspecified).  Deterministic for given inputs.  Rows
+ * holding NaN give an unspecified id in [0, V).  out_ids [B] int32 on the
+ * device. */
+DSB_API int dsb_sample(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k,
+                       float top_p, const float* uniforms, int32_t* out_ids);
+
 /* h[b] = fp32 embedding row tokens[b] of table [V, D] (bf16 when table_bf16,
  * else fp32); replaces embedding_to_slot (cuda_backend.cpp:716-732). */
 DSB_API int dsb_embed(dsb_ctx* ctx, const void* table, int table_bf16, const int32_t* tokens, int B, int D, float* h);
@@ -533,6 +549,35 @@ DSB_API int dsb_prefill(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const i
 DSB_API int dsb_generate(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids, int B,
                          const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
                          int32_t eos_id, int32_t* out_ids, int32_t* out_counts);
+
+/* Sampling settings: ds::core::SamplerConfig (include/ds/core/sampler.h:9-14)
+ * as ds::rt::GenerationConfig carries them. */
+typedef struct dsb_sampling {
+  float temperature; /* <= 0 reads as 1 */
+  int top_k;         /* 0 (or >= vocab) disables the top-k cut */
+  float top_p;       /* 0 (or >= 1) disables the top-p cut */
+  uint32_t seed;     /* dsb_generate_sampled: 0 = std::random_device, as the reference */
+} dsb_sampling;
+
+/* dsb_decode_step whose next id per row is sampled on the device (dsb_sample)
+ * instead of the greedy argmax: uniforms_host[B] holds one draw in [0, 1]
+ * per row (the caller's generator), ids_host[B] receives the sampled ids,
+ * logits_host as in dsb_decode_step.  No counterpart in the reference, whose
+ * sampler runs on the host over downloaded logits (sampler.cpp:23-77). */
+DSB_API int dsb_decode_step_sampled(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
+                                    const int32_t* tokens, int B, const dsb_sampling* sampling,
+                                    const float* uniforms_host, float* logits_host, int32_t* ids_host);
+
+/* dsb_generate with ds::rt::generate's sampling branch
+ * (src/runtime/model.cpp:21-34): when temperature, top_k or top_p is above
+ * 0 every generated id is sampled on the device, else greedy.  Sequence b
+ * draws one uniform per generated id from its own std::mt19937 seeded with
+ * seed + b through std::uniform_real_distribution<float>(0, 1), so for B = 1
+ * the draws are the reference Sampler's own (sampler.cpp:21, 69-70). */
+DSB_API int dsb_generate_sampled(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids, int B,
+                                 const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
+                                 int32_t eos_id, const dsb_sampling* sampling, int32_t* out_ids,
+                                 int32_t* out_counts);
 
 /* ------------------------------------------------------ checkpoint ingest */
 

@@ -51,6 +51,9 @@ def oracle() -> ctypes.CDLL:
         _proto(l, "orc_rope_inplace_f32", ctypes.c_int, [f32p, i64, i64, ctypes.c_float])
         _proto(l, "orc_softmax_f32", ctypes.c_int, [f32p, i64])
         _proto(l, "orc_argmax_f32", i64, [f32p, i64])
+        _proto(l, "orc_sample", ctypes.c_int32,
+               [f32p, i64, ctypes.c_float, ctypes.c_int32, ctypes.c_float, ctypes.c_float,
+                ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)])
         _proto(l, "orc_linear_f32", None, [f32p, f32p, i64, f32p, i64])
         _proto(l, "orc_bf16_to_f32_n", None, [u16p, i64, f32p])
         _proto(l, "orc_f32_to_bf16_n", None, [f32p, i64, u16p])
@@ -123,6 +126,9 @@ def ref() -> ctypes.CDLL:
         _proto(l, "ref_model_step", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, f32p, i32p])
         _proto(l, "ref_model_generate", ctypes.c_int, [ctypes.c_void_p, i32p, ctypes.c_int, ctypes.c_int, i32p])
         _proto(l, "ref_checkpoint_summary", ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int])
+        _proto(l, "ref_sampler_draws", ctypes.c_int,
+               [f32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float, ctypes.c_uint32, ctypes.c_int, i32p])
+        _proto(l, "ref_sampler_uniforms", ctypes.c_int, [ctypes.c_uint32, ctypes.c_int, f32p])
         _ref = l
     return _ref
 
@@ -179,3 +185,21 @@ def ref_checkpoint_summary(path: str) -> tuple[dict, list[tuple]]:
         elif f[0] == "t":
             tensors.append((f[1], int(f[2]), int(f[3]), tuple(int(x) for x in f[4:])))
     return cfg, tensors
+
+
+def sample(logits, temperature, top_k, top_p, r) -> tuple[int, float, float]:
+    """orc_sample on one fp32 row: (id, margin of r in the chosen interval, margin of the top-p cut)."""
+    x = np.ascontiguousarray(logits, np.float32)
+    m, c = ctypes.c_double(), ctypes.c_double()
+    i = oracle().orc_sample(p(x, f32p), x.size, temperature, top_k, top_p, r, ctypes.byref(m), ctypes.byref(c))
+    return int(i), m.value, c.value
+
+
+def ref_sampler(logits, temperature, top_k, top_p, seed, n) -> tuple[np.ndarray, np.ndarray]:
+    """The reference's Sampler with `seed`: (n sampled ids, the n uniform draws it made)."""
+    x = np.ascontiguousarray(logits, np.float32)
+    ids = np.zeros(n, np.int32)
+    u = np.zeros(n, np.float32)
+    assert ref().ref_sampler_draws(p(x, f32p), x.size, temperature, top_k, top_p, seed, n, p(ids, i32p)) == 0
+    ref().ref_sampler_uniforms(seed, n, p(u, f32p))
+    return ids, u

@@ -589,3 +589,106 @@ ORC_API void orc_fp8_linear(const uint8_t* w, const float* sw, const uint8_t* x,
     }
   }
 }
+
+/* ---------------------------------------------------------------- sampling */
+
+typedef struct {
+  int32_t id;
+  float x; /* logit / t */
+  float p;
+} orc_item;
+
+/* Descending x, ties to the lower id: the order the CUDA sampler scans a
+ * filtered row in, one of the orders std::nth_element / std::sort can leave
+ * (p is non-decreasing in x, so this is also a descending-p order). */
+static int orc_item_desc(const void* a, const void* b) {
+  const orc_item* u = (const orc_item*)a;
+  const orc_item* v = (const orc_item*)b;
+  if (u->x > v->x) return -1;
+  if (u->x < v->x) return 1;
+  return (u->id > v->id) - (u->id < v->id);
+}
+
+/* ds::core::Sampler::sample (src/core/sampler.cpp:23-77) for one row, with
+ * the uniform draw r in [0, 1) given instead of drawn.  Steps and float
+ * arithmetic as the reference: x = logit / t (t <= 0 reads as 1); top-k
+ * (0 < top_k < V) keeps the top_k largest x; softmax over the kept items in
+ * their current order (math.cpp:15-27); top-p (0 < top_p < 1) sorts by p,
+ * accumulates until cum >= top_p (that item kept, at least one) and divides
+ * by the kept sum; the draw returns the first item in order with r <= cum,
+ * else the last.  Orders the reference leaves unspecified (nth_element's
+ * arrangement, std::sort among equal p) are fixed to descending x with ties
+ * to the lower id; with no cut active the items stay in id order.
+ * margin: distance of r from the nearer end of the chosen item's cumulative
+ * interval; cut_margin: |cum - top_p| where the top-p cut stopped (1 when no
+ * top-p cut).  Either may be NULL.  Returns the id, or -1 when V <= 0 or the
+ * softmax sum is not positive (the reference throws). */
+ORC_API int32_t orc_sample(const float* logits, int64_t V, float temperature, int32_t top_k, float top_p, float r,
+                           double* margin, double* cut_margin) {
+  if (V <= 0) return -1;
+  orc_item* it = (orc_item*)malloc((size_t)V * sizeof *it);
+  if (it == NULL) return -1;
+  const float t = temperature <= 0.0f ? 1.0f : temperature;
+  for (int64_t i = 0; i < V; ++i) {
+    it[i].id = (int32_t)i;
+    it[i].x = logits[i] / t;
+    it[i].p = 0.0f;
+  }
+  int64_t n = V;
+  const int sorted = top_k > 0 && top_k < V;
+  if (sorted) {
+    qsort(it, (size_t)V, sizeof *it, orc_item_desc);
+    n = top_k;
+  }
+  float mx = it[0].x;
+  for (int64_t i = 1; i < n; ++i) mx = (mx < it[i].x) ? it[i].x : mx; /* std::max */
+  float sum = 0.0f;
+  for (int64_t i = 0; i < n; ++i) {
+    it[i].p = expf(it[i].x - mx);
+    sum += it[i].p;
+  }
+  if (!(sum > 0.0f)) {
+    free(it);
+    return -1;
+  }
+  const float inv = 1.0f / sum;
+  for (int64_t i = 0; i < n; ++i) it[i].p *= inv;
+  double cm = 1.0;
+  if (top_p > 0.0f && top_p < 1.0f) {
+    if (!sorted) qsort(it, (size_t)n, sizeof *it, orc_item_desc);
+    float cum = 0.0f;
+    int64_t keep = 0;
+    for (; keep < n; ++keep) {
+      cum += it[keep].p;
+      if (cum >= top_p) {
+        ++keep;
+        break;
+      }
+    }
+    cm = fabs((double)cum - (double)top_p);
+    if (keep < 1) keep = 1;
+    if (keep > n) keep = n;
+    n = keep;
+    float s = 0.0f;
+    for (int64_t i = 0; i < n; ++i) s += it[i].p;
+    for (int64_t i = 0; i < n; ++i) it[i].p /= s;
+  }
+  float cum = 0.0f;
+  int32_t id = it[n - 1].id;
+  double mg = -1.0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float prev = cum;
+    cum += it[i].p;
+    if (r <= cum) {
+      id = it[i].id;
+      const double a = (double)r - (double)prev, b = (double)cum - (double)r;
+      mg = a < b ? a : b;
+      break;
+    }
+  }
+  if (mg < 0.0) mg = (double)r - (double)cum;
+  if (margin) *margin = mg;
+  if (cut_margin) *cut_margin = cm;
+  free(it);
+  return id;
+}

@@ -11,6 +11,7 @@
 #include "ds/core/math.h"
 #include "ds/core/ops.h"
 #include "ds/core/rope.h"
+#include "ds/core/sampler.h"
 #include "ds/hf/config.h"
 #include "ds/hf/model_loader.h"
 #include "ds/models/deepseek/config.h"
@@ -26,6 +27,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -347,6 +349,32 @@ __attribute__((visibility("default"))) int ref_checkpoint_summary(const char* di
   std::memcpy(buf, text.data(), static_cast<std::size_t>(n));
   buf[n] = 0;
   return rc == 0 ? n : -1;
+}
+
+// ds::core::Sampler (src/core/sampler.cpp:23-77) with a fixed seed: n calls
+// of sample() on the same logits row.
+__attribute__((visibility("default"))) int ref_sampler_draws(const float* logits, int V, float temperature, int top_k,
+                                                             float top_p, std::uint32_t seed, int n, std::int32_t* out) {
+  try {
+    ds::core::Sampler sm(ds::core::SamplerConfig{temperature, top_k, top_p, seed});
+    const std::vector<float> row(logits, logits + V);
+    for (int i = 0; i < n; ++i) out[i] = sm.sample(row);
+    return 0;
+  } catch (const std::exception&) {
+    return -1;
+  }
+}
+
+// The uniform draws such a Sampler makes, one per sample() call: a
+// std::mt19937 seeded with `seed` through a fresh
+// std::uniform_real_distribution<float>(0, 1) each time (sampler.cpp:21, 69-70).
+__attribute__((visibility("default"))) int ref_sampler_uniforms(std::uint32_t seed, int n, float* out) {
+  std::mt19937 rng(seed);
+  for (int i = 0; i < n; ++i) {
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    out[i] = dist(rng);
+  }
+  return 0;
 }
 
 }  // extern "C"
