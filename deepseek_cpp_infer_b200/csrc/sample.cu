@@ -17,18 +17,22 @@
 // keep the lower ids.
 //
 // Nothing is sorted.  Each cut is a radix select over order-preserving 32-bit
-// keys of x (three passes of 11/11/10 bits, histograms in shared memory),
-// weighted by counts (the top-k cut) or by probability mass (the top-p cut
-// and the draw).  Masses are fixed point, q = round(p * 2^40) in uint64, so
-// the shared-memory atomic sums do not depend on the order the atomics land
-// in: a row's result is deterministic.  Rank among equal keys is kept in id
-// order by giving each warp a contiguous segment of the row that it walks in
-// 32-element steps (ballot + popc).  The row is re-read (from L2) on every
-// pass: at most 14 passes for the filtered case, 3 and a one-warp walk
-// unfiltered.
+// keys of x (four passes of 8 bits), weighted by counts (the top-k cut) or by
+// probability mass (the top-p cut and the draw).  Masses are fixed point,
+// q = round(p * 2^40) in uint64, so the shared-memory atomic sums do not
+// depend on the order the atomics land in: a row's result is deterministic.
+// The histogram has one column per lane (256 bins x 32 lanes, 64 KB), so
+// lanes of a warp never collide on an address even when their keys share a
+// bin.  Rank among equal keys is kept in id order by giving each warp a
+// contiguous segment of the row that it walks 32 items at a time (ballot +
+// popc), four loads ahead; ranks are only computed when a cut splits a run
+// of equal keys.  The row is re-read from L2 on every pass (at most 17 with
+// both cuts, 3 with none).  A top-k cut of at most 1024 items instead gathers
+// its survivors into shared memory and finishes there (6 passes).
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 
@@ -40,7 +44,9 @@ namespace {
 
 using u64 = unsigned long long;
 
-constexpr int kThreads = 1024, kWarps = kThreads / 32, kBins = 2048;
+constexpr int kMaxDevices = 64;
+constexpr int kThreads = 1024, kWarps = kThreads / 32, kBins = 256, kAhead = 4, kCompactMax = 1024;
+constexpr size_t kHistBytes = (size_t)kBins * 32 * sizeof(unsigned long long);  // dynamic shared memory
 constexpr double kFix = 1099511627776.0;  // 2^40: fixed-point unit of probability mass
 
 __device__ __forceinline__ uint32_t fkey(float x) {
@@ -53,14 +59,20 @@ __device__ __forceinline__ float key_to_float(uint32_t k) {
 }
 
 struct SampleSmem {
-  u64 hist[kBins];
+  u64 bins[kBins];     // a pass's histogram, lane columns summed
   u64 wval[kWarps];    // per-warp partial sums / counts
   u64 wbase[kWarps];   // their exclusive prefix
   float fred[kWarps];
-  u64 sel_excl, target;
+  u64 sel_excl, sel_h, target;
   int sel_bin, sel_warp;
   int out_id;
+  int ncomp;
 };
+
+__device__ __forceinline__ u64* hist_cols() {
+  extern __shared__ __align__(16) unsigned char dyn_smem[];
+  return reinterpret_cast<u64*>(dyn_smem);  // [kBins][32]
+}
 
 // The cuts of one row, as each warp sees its own segment.
 struct RowView {
@@ -80,27 +92,36 @@ template <class F>
 __device__ __forceinline__ void walk(const RowView& r, F f) {
   const uint32_t lane = threadIdx.x & 31, lt = (1u << lane) - 1u;
   int run_k = r.base_k, run_p = r.base_p;
-  for (int i0 = r.seg0; i0 < r.seg1; i0 += 32) {
-    const int i = i0 + (int)lane;
-    const bool in = i < r.seg1;
-    const float x = in ? __fdiv_rn(r.row[i], r.t) : -INFINITY;
-    const uint32_t key = fkey(x);
-    bool keep = in;
-    if (r.fk) {
-      const bool eq = in && key == r.Kk;
-      const uint32_t b = __ballot_sync(0xffffffffu, eq);
-      const int rank = run_k + __popc(b & lt);
-      run_k += __popc(b);
-      keep = in && (key > r.Kk || (eq && rank < r.need_k));
+  for (int i0 = r.seg0; i0 < r.seg1; i0 += 32 * kAhead) {
+    float v[kAhead];
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j) {
+      const int i = i0 + j * 32 + (int)lane;
+      v[j] = i < r.seg1 ? __ldg(r.row + i) : 0.0f;
     }
-    if (r.fp) {
-      const bool eq = keep && key == r.Kp;
-      const uint32_t b = __ballot_sync(0xffffffffu, eq);
-      const int rank = run_p + __popc(b & lt);
-      run_p += __popc(b);
-      keep = keep && (key > r.Kp || (eq && rank < r.need_p));
+#pragma unroll
+    for (int j = 0; j < kAhead; ++j) {
+      const int i = i0 + j * 32 + (int)lane;
+      const bool in = i < r.seg1;
+      const float x = in ? (r.t == 1.0f ? v[j] : __fdiv_rn(v[j], r.t)) : -INFINITY;
+      const uint32_t key = fkey(x);
+      bool keep = in;
+      if (r.fk) {
+        const bool eq = in && key == r.Kk;
+        const uint32_t b = __ballot_sync(0xffffffffu, eq);
+        const int rank = run_k + __popc(b & lt);
+        run_k += __popc(b);
+        keep = in && (key > r.Kk || (eq && rank < r.need_k));
+      }
+      if (r.fp) {
+        const bool eq = keep && key == r.Kp;
+        const uint32_t b = __ballot_sync(0xffffffffu, eq);
+        const int rank = run_p + __popc(b & lt);
+        run_p += __popc(b);
+        keep = keep && (key > r.Kp || (eq && rank < r.need_p));
+      }
+      f(i, x, key, in, keep);
     }
-    f(i, x, key, in, keep);
   }
 }
 
@@ -180,7 +201,7 @@ __device__ float block_sum(SampleSmem& s, float v) {
 struct Selected {
   uint32_t key;  // key of the item at which the cumulative weight reaches the target
   u64 rem;       // target minus the weight of the candidates with a larger key (>= 1)
-  u64 total;     // weight of all candidates
+  u64 eq;        // weight of the candidates with this key
 };
 
 // Among the candidates (keep == true), taken in descending key order, find
@@ -189,49 +210,55 @@ struct Selected {
 // the candidate's weight (1 for counts, its fixed-point mass otherwise).
 template <class Wt>
 __device__ Selected radix_select(SampleSmem& s, const RowView& r, Wt weight, u64 target, double frac) {
+  u64* H = hist_cols();
+  const uint32_t lane = threadIdx.x & 31;
   uint32_t prefix = 0;
-  int have = 0;
-  u64 rem = target, total = 0;
-  for (int pass = 0; pass < 3; ++pass) {
-    const int bits = pass < 2 ? 11 : 10, nb = 1 << bits, shift = 32 - have - bits;
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) s.hist[b] = 0;
+  u64 rem = target;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int c = threadIdx.x; c < kBins * 32; c += blockDim.x) H[c] = 0;
     __syncthreads();
     walk(r, [&](int, float x, uint32_t key, bool, bool keep) {
-      if (keep && (have == 0 || (key >> (32 - have)) == prefix))
-        atomicAdd(&s.hist[(key >> shift) & (uint32_t)(nb - 1)], weight(x, key));
+      if (keep && (pass == 0 || (key >> (shift + 8)) == prefix))
+        atomicAdd(&H[((key >> shift) & 255u) * 32 + lane], weight(x, key));
     });
     __syncthreads();
-    // descending bins: thread t holds bins nb-1-2t and nb-2-2t
-    const int j0 = 2 * (int)threadIdx.x, b0 = nb - 1 - j0, b1 = nb - 2 - j0;
-    const u64 h0 = b0 >= 0 ? s.hist[b0] : 0, h1 = b1 >= 0 ? s.hist[b1] : 0;
+    {  // bin totals: 4 threads per bin, 8 lane columns each
+      const int bin = threadIdx.x >> 2, q = threadIdx.x & 3;
+      u64 t = 0;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) t += H[bin * 32 + q * 8 + c];
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      if (q == 0) s.bins[bin] = t;
+    }
+    __syncthreads();
+    // descending bins: thread t < 256 holds bin 255 - t
+    const int b0 = kBins - 1 - (int)threadIdx.x;
+    const u64 h0 = b0 >= 0 ? s.bins[b0] : 0;
     u64 group = 0;
-    const u64 excl = block_excl_scan(s, h0 + h1, &group);
-    if (pass == 0) {
-      total = group;
-      if (frac >= 0.0) {
-        const double c = ceil(frac * (double)total);
-        rem = c < 1.0 ? 1ull : (c > (double)total ? total : (u64)c);
-      }
+    const u64 excl = block_excl_scan(s, h0, &group);
+    if (pass == 0 && frac >= 0.0) {
+      const double c = ceil(frac * (double)group);
+      rem = c < 1.0 ? 1ull : (c > (double)group ? group : (u64)c);
     }
     if (threadIdx.x == 0) {
       s.sel_bin = 0;
       s.sel_excl = 0;
+      s.sel_h = 0;
     }
     __syncthreads();
     if (b0 >= 0 && excl < rem && rem <= excl + h0) {
       s.sel_bin = b0;
       s.sel_excl = excl;
-    } else if (b1 >= 0 && excl + h0 < rem && rem <= excl + h0 + h1) {
-      s.sel_bin = b1;
-      s.sel_excl = excl + h0;
+      s.sel_h = h0;
     }
     __syncthreads();
-    prefix = (prefix << bits) | (uint32_t)s.sel_bin;
-    have += bits;
+    prefix = (prefix << 8) | (uint32_t)s.sel_bin;
     rem -= s.sel_excl;
     __syncthreads();
   }
-  return {prefix, rem, total};
+  return {prefix, rem, s.sel_h};
 }
 
 // Items of this warp's segment that are candidates with key == K, counted per
@@ -243,6 +270,85 @@ __device__ int eq_base(SampleSmem& s, const RowView& r, uint32_t K) {
   });
   warps_excl_scan(s, (u64)n);
   return (int)s.wbase[threadIdx.x >> 5];
+}
+
+// Small top-k (k <= kCompactMax): the k survivors are gathered into shared
+// memory, sorted (bitonic, descending x then ascending id), and the softmax,
+// top-p cut and draw run over that list in the reference's own float order
+// (sampler.cpp:42-76): sums left to right, p = e * (1 / sum), renormalised by
+// division.  Returns the id (valid in thread 0).
+__device__ int compact_and_draw(SampleSmem& s, const RowView& r, int k, bool fp, float top_p, float u) {
+  u64* A = hist_cols();                                  // [kCompactMax] (key << 32) | ~id, sorted ascending
+  float* e = reinterpret_cast<float*>(A + kCompactMax);  // [kCompactMax] exp(x - max) in descending order
+  int* idv = reinterpret_cast<int*>(e + kCompactMax);    // [kCompactMax] ids in descending order
+  int N = 2;
+  while (N < k) N <<= 1;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) A[j] = 0;  // pads sort first (smallest)
+  if (threadIdx.x == 0) s.ncomp = 0;
+  __syncthreads();
+  walk(r, [&](int i, float, uint32_t key, bool, bool keep) {
+    if (keep) {
+      const int slot = atomicAdd(&s.ncomp, 1);
+      if (slot < N) A[slot] = ((u64)key << 32) | (u64)(~(uint32_t)i);
+    }
+  });
+  __syncthreads();
+  for (int kk = 2; kk <= N; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const u64 a = A[i], b = A[ixj];
+          if (((i & kk) == 0) ? (a > b) : (a < b)) {
+            A[i] = b;
+            A[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const int n = min(s.ncomp, N);
+  const float mx = key_to_float((uint32_t)(A[N - 1] >> 32));
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const u64 c = A[N - 1 - j];
+    e[j] = expf(key_to_float((uint32_t)(c >> 32)) - mx);
+    idv[j] = (int)(~(uint32_t)c);
+  }
+  __syncthreads();
+  int id = 0;
+  if (threadIdx.x == 0 && n > 0) {
+    float sum = 0.0f;
+    for (int j = 0; j < n; ++j) sum += e[j];
+    const float inv = 1.0f / sum;
+    int keep = n;
+    float s2 = 1.0f;
+    if (fp) {
+      float cum = 0.0f;
+      keep = 0;
+      for (; keep < n; ++keep) {
+        cum += e[keep] * inv;
+        if (cum >= top_p) {
+          ++keep;
+          break;
+        }
+      }
+      keep = max(1, min(keep, n));
+      s2 = 0.0f;
+      for (int j = 0; j < keep; ++j) s2 += e[j] * inv;
+    }
+    id = idv[keep - 1];
+    float cum = 0.0f;
+    for (int j = 0; j < keep; ++j) {
+      const float pj = fp ? (e[j] * inv) / s2 : e[j] * inv;
+      cum += pj;
+      if (u <= cum) {
+        id = idv[j];
+        break;
+      }
+    }
+  }
+  return id;
 }
 
 __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __restrict__ logits, int64_t ld, int V,
@@ -272,9 +378,18 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
   if (fk) {
     const Selected c = radix_select(s, r, [](float, uint32_t) { return 1ull; }, (u64)top_k, -1.0);
     r.Kk = c.key;
-    r.need_k = (int)c.rem;
-    r.base_k = eq_base(s, r, c.key);  // r.fk is still off: counts every item with the key
+    if (c.rem < c.eq) {  // the cut splits a run of equal keys: rank them by id
+      r.need_k = (int)c.rem;
+      r.base_k = eq_base(s, r, c.key);  // r.fk is still off: counts every item with the key
+    } else {
+      r.need_k = 0x7fffffff;
+    }
     r.fk = true;
+    if (top_k <= kCompactMax) {
+      const int id = compact_and_draw(s, r, top_k, top_p > 0.0f && top_p < 1.0f, top_p, u);
+      if (threadIdx.x == 0) out[blockIdx.x] = id;
+      return;
+    }
   }
 
   // softmax over the survivors: p = exp(x - max) * (1 / sum)   (math.cpp:15-27)
@@ -321,14 +436,37 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
       const Selected c = radix_select(s, r, mass, 0, (double)top_p);
       const u64 q = mass(key_to_float(c.key), c.key);
       r.Kp = c.key;
-      r.need_p = q > 0 ? (int)((c.rem + q - 1) / q) : 0;
-      r.base_p = eq_base(s, r, c.key);  // r.fp still off: survivors of the top-k cut with the key
+      const u64 m = q > 0 ? (c.rem + q - 1) / q : 0;  // items with the key that the cut keeps
+      if (m * q < c.eq) {  // the cut splits a run of equal keys: rank them by id
+        r.need_p = (int)m;
+        r.base_p = eq_base(s, r, c.key);  // r.fp still off: survivors of the top-k cut with the key
+      } else {
+        r.need_p = 0x7fffffff;
+      }
       r.fp = true;
     }
     // the draw: the item at which the survivors' mass, in descending order, reaches u * total
     const Selected d = radix_select(s, r, mass, 0, (double)u);
     const u64 qd = mass(key_to_float(d.key), d.key);
     const int m = qd > 0 ? (int)((d.rem + qd - 1) / qd) : 1;  // the m-th survivor with this key, in id order
+    if (m == 1) {
+      // the first survivor with the key: each warp's first, then the lowest
+      int first = 0x7fffffff;
+      walk(r, [&](int i, float, uint32_t key, bool, bool keep) {
+        const uint32_t b = __ballot_sync(0xffffffffu, keep && key == d.key);
+        if (b != 0u && first == 0x7fffffff) first = __shfl_sync(0xffffffffu, i, __ffs(b) - 1);
+      });
+      if (lane == 0) s.wval[w] = (u64)(uint32_t)first;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int best = 0x7fffffff;
+        for (int j = 0; j < kWarps; ++j) best = min(best, (int)(uint32_t)s.wval[j]);
+        s.out_id = best == 0x7fffffff ? 0 : best;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) out[blockIdx.x] = s.out_id;
+      return;
+    }
     const int base = eq_base(s, r, d.key);
     const int n = (int)s.wval[w];  // this warp's count, left by eq_base
     if (threadIdx.x == 0) s.sel_warp = -1;
@@ -359,8 +497,15 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
 int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k, float top_p,
                 const float* uniforms, int32_t* out) {
   const float t = temperature <= 0.0f ? 1.0f : temperature;
-  DSB_CUDA_TRY(ctx, launch_pdl(sample_rows_kernel, B, kThreads, 0, ctx->stream, logits, ld, V, t, top_k, top_p,
-                               uniforms, out));
+  static std::atomic<bool> attr_set[kMaxDevices];
+  if (ctx->device < 0 || ctx->device >= kMaxDevices) return fail(ctx, DSB_EUNSUPPORTED, "dsb_sample: device index");
+  if (!attr_set[ctx->device].load()) {
+    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kHistBytes));
+    attr_set[ctx->device].store(true);
+  }
+  DSB_CUDA_TRY(ctx, launch_pdl(sample_rows_kernel, B, kThreads, kHistBytes, ctx->stream, logits, ld, V, t, top_k,
+                               top_p, uniforms, out));
   ctx->stats.kernel_launches++;
   return DSB_OK;
 }

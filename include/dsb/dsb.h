@@ -543,8 +543,8 @@ DSB_API int dsb_prefill(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const i
  * (at least one token), consumed token by token as the reference's forward()
  * does; then its greedy ids are fed back until max_new_tokens ids or eos_id
  * (>= 0, kept in the output; < 0 for none).  out_ids [B, max_new_tokens]
- * (host), out_counts [B] (host) the ids written per sequence.  Sampling
- * (temperature / top-k / top-p) is not covered: greedy only.  Not for models
+ * (host), out_counts [B] (host) the ids written per sequence.  Greedy; see
+ * dsb_generate_sampled for temperature / top-k / top-p.  Not for models
  * bound to an expert-parallel group (their ranks step together). */
 DSB_API int dsb_generate(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids, int B,
                          const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
