@@ -26,7 +26,7 @@
 // bin.  Rank among equal keys is kept in id order by giving each warp a
 // contiguous segment of the row that it walks 32 items at a time (ballot +
 // popc), four loads ahead; ranks are only computed when a cut splits a run
-// of equal keys.  The row is re-read from L2 on every pass (at most 17 with
+// of equal keys, and every other pass loads float4s in no particular order.  The row is re-read from L2 on every pass (at most 17 with
 // both cuts, 3 with none).  A top-k cut of at most 1024 items instead gathers
 // its survivors into shared memory and finishes there (6 passes).
 
@@ -45,7 +45,7 @@ namespace {
 using u64 = unsigned long long;
 
 constexpr int kMaxDevices = 64;
-constexpr int kThreads = 1024, kWarps = kThreads / 32, kBins = 256, kAhead = 4, kCompactMax = 1024;
+constexpr int kThreads = 1024, kWarps = kThreads / 32, kBins = 256, kAhead = 4, kAheadVec = 2, kCompactMax = 1024;
 constexpr size_t kHistBytes = (size_t)kBins * 32 * sizeof(unsigned long long);  // dynamic shared memory
 constexpr double kFix = 1099511627776.0;  // 2^40: fixed-point unit of probability mass
 
@@ -79,17 +79,19 @@ struct RowView {
   const float* row;
   int seg0, seg1;  // this warp's items [seg0, seg1)
   float t;
+  bool vec;        // row 16-byte aligned: unordered walks load float4
   bool fk, fp;     // top-k / top-p cut active
   uint32_t Kk, Kp;
   int need_k, need_p;  // how many items with the cut's key survive it (lowest ids first)
   int base_k, base_p;
 };
 
-// f(i, x, key, in, keep) for every lane of every 32-item step of this warp's
-// segment, in id order; keep = the item survives the active cuts.  All 32
-// lanes take part (ballots); lanes past the segment get in = keep = false.
+// Ordered walk: f(i, x, key, in, keep) for every lane of every 32-item step
+// of this warp's segment, in id order; keep = the item survives the active
+// cuts.  All 32 lanes take part (ballots); lanes past the segment get
+// in = keep = false.
 template <class F>
-__device__ __forceinline__ void walk(const RowView& r, F f) {
+__device__ __forceinline__ void walk_ordered(const RowView& r, F f) {
   const uint32_t lane = threadIdx.x & 31, lt = (1u << lane) - 1u;
   int run_k = r.base_k, run_p = r.base_p;
   for (int i0 = r.seg0; i0 < r.seg1; i0 += 32 * kAhead) {
@@ -121,6 +123,52 @@ __device__ __forceinline__ void walk(const RowView& r, F f) {
         keep = keep && (key > r.Kp || (eq && rank < r.need_p));
       }
       f(i, x, key, in, keep);
+    }
+  }
+}
+
+__device__ __forceinline__ bool ranked(const RowView& r) {
+  return (r.fk && r.need_k != 0x7fffffff) || (r.fp && r.need_p != 0x7fffffff);
+}
+
+// Unordered walk: f for every item of the segment, in no particular order
+// (each lane takes four consecutive items per 128-item step, loaded as one
+// float4, kAheadVec steps ahead).  Every lane makes the same number of calls, so
+// f may use warp votes, but not id order.  Falls back to the ordered walk
+// when a cut must rank equal keys or the row is not 16-byte aligned.
+template <class F>
+__device__ __forceinline__ void walk(const RowView& r, F f) {
+  if (!r.vec || ranked(r)) {
+    walk_ordered(r, f);
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  for (int i0 = r.seg0; i0 < r.seg1; i0 += 128 * kAheadVec) {
+    float4 v[kAheadVec];
+#pragma unroll
+    for (int j = 0; j < kAheadVec; ++j) {
+      const int i = i0 + j * 128 + 4 * lane;
+      if (i + 3 < r.seg1) {
+        v[j] = __ldg(reinterpret_cast<const float4*>(r.row + i));
+      } else {
+        v[j].x = i < r.seg1 ? __ldg(r.row + i) : 0.0f;
+        v[j].y = i + 1 < r.seg1 ? __ldg(r.row + i + 1) : 0.0f;
+        v[j].z = i + 2 < r.seg1 ? __ldg(r.row + i + 2) : 0.0f;
+        v[j].w = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kAheadVec; ++j) {
+      const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = i0 + j * 128 + 4 * lane + c;
+        const bool in = i < r.seg1;
+        const float x = in ? (r.t == 1.0f ? e[c] : __fdiv_rn(e[c], r.t)) : -INFINITY;
+        const uint32_t key = fkey(x);
+        const bool keep = in && (!r.fk || key >= r.Kk) && (!r.fp || key >= r.Kp);
+        f(i, x, key, in, keep);
+      }
     }
   }
 }
@@ -354,16 +402,17 @@ __device__ int compact_and_draw(SampleSmem& s, const RowView& r, int k, bool fp,
 __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                                float t, int top_k, float top_p,
                                                                const float* __restrict__ uniforms,
-                                                               int32_t* __restrict__ out) {
+                                                               int32_t* __restrict__ out, int vec) {
   pdl_wait();
   __shared__ SampleSmem s;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = ((V + kThreads - 1) / kThreads) * 32;  // warp segment, a multiple of 32
+  const int S = ((V + kWarps * 128 - 1) / (kWarps * 128)) * 128;  // warp segment, a multiple of 128
   RowView r{};
   r.row = logits + (int64_t)blockIdx.x * ld;
   r.seg0 = min(V, w * S);
   r.seg1 = min(V, r.seg0 + S);
   r.t = t;
+  r.vec = vec != 0;
   const float u = uniforms[blockIdx.x];
   if (threadIdx.x == 0) s.out_id = 0;
 
@@ -419,7 +468,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
     if (w == s.sel_warp) {
       u64 run = s.wbase[w];
       bool found = false;
-      walk(r, [&](int i, float x, uint32_t key, bool in, bool) {
+      walk_ordered(r, [&](int i, float x, uint32_t key, bool in, bool) {
         const u64 q = in ? mass(x, key) : 0ull;
         const u64 incl = run + warp_incl_scan(q);
         const uint32_t hit = __ballot_sync(0xffffffffu, in && !found && incl >= R);
@@ -453,9 +502,10 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
       // the first survivor with the key: each warp's first, then the lowest
       int first = 0x7fffffff;
       walk(r, [&](int i, float, uint32_t key, bool, bool keep) {
-        const uint32_t b = __ballot_sync(0xffffffffu, keep && key == d.key);
-        if (b != 0u && first == 0x7fffffff) first = __shfl_sync(0xffffffffu, i, __ffs(b) - 1);
+        if (keep && key == d.key) first = min(first, i);
       });
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
       if (lane == 0) s.wval[w] = (u64)(uint32_t)first;
       __syncthreads();
       if (threadIdx.x == 0) {
@@ -475,7 +525,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
     __syncthreads();
     if (w == s.sel_warp) {
       int run = base;
-      walk(r, [&](int i, float, uint32_t key, bool, bool keep) {
+      walk_ordered(r, [&](int i, float, uint32_t key, bool, bool keep) {
         const uint32_t b = __ballot_sync(0xffffffffu, keep && key == d.key);
         const int c = __popc(b);
         if (run < m && m <= run + c) {
@@ -504,8 +554,9 @@ int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, flo
                                            (int)kHistBytes));
     attr_set[ctx->device].store(true);
   }
+  const int vec = ((uintptr_t)logits % 16 == 0 && ld % 4 == 0) ? 1 : 0;
   DSB_CUDA_TRY(ctx, launch_pdl(sample_rows_kernel, B, kThreads, kHistBytes, ctx->stream, logits, ld, V, t, top_k,
-                               top_p, uniforms, out));
+                               top_p, uniforms, out, vec));
   ctx->stats.kernel_launches++;
   return DSB_OK;
 }

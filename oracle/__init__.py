@@ -67,6 +67,11 @@ def oracle() -> ctypes.CDLL:
             [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_float] + [f32p] * 6 + [ctypes.c_int, f32p],
         )
         _proto(
+            l, "orc_mla_layer_seq_fp8act_f32", ctypes.c_int,
+            [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_float] + [f32p] * 6 + [ctypes.c_int, f32p],
+        )
+        _proto(l, "orc_act_fp8_roundtrip", None, [f32p, i64, i64])
+        _proto(
             l, "orc_kv_norm_rope_append", ctypes.c_int,
             [f32p, f32p, f32p, i32p, i32p] + [ctypes.c_int] * 7 + [ctypes.c_float, ctypes.c_float, u16p, f32p],
         )

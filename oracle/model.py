@@ -20,6 +20,17 @@ its router broken the near-tie the other way.
 
 Covers the configurations with q_lora_rank 0 and softmax scoring (DeepSeek-V2
 style); dimensions come from the same config dict as workloads.TINY.
+
+forward_fp8 is the same forward for a block-scaled FP8 checkpoint (weights
+e4m3 + 128x128 scales, as DeepSeek-V3 ships them; the reference has no FP8
+path, so this is a restatement): every FP8 linear uses the dequantised
+weight (e4m3 * scale) and sees its input as the FP8 GEMM does, rounded to
+the bf16 activation and quantised per token and 128 columns
+(orc_act_fp8_roundtrip).  The quantisation points are the projections' input
+(the attention norm), o_proj's input, the dense FFN's input and its
+SiLU(gate) * up activation, and every routed and shared expert's input and
+activation; kv_b_proj is dequantised to bf16 once (absorbed attention keeps
+it in bf16), the router and lm_head stay unquantised.
 """
 
 from __future__ import annotations
@@ -169,3 +180,80 @@ def moe_fp8(x, ids, weights, gate_q, gate_s, up_q, up_s, down_q, down_s):
             acc = _f32(acc + np.float32(wt) * y)
         out[t] = acc
     return out
+
+
+def _act_fp8(x):
+    """orc_act_fp8_roundtrip on a copy of x (rows = tokens)."""
+    a = np.array(_f32(x), copy=True)
+    a2 = a.reshape(-1, a.shape[-1])
+    oracle().orc_act_fp8_roundtrip(p(a2, f32p), a2.shape[0], a2.shape[1])
+    return a
+
+
+def _silu_mul(g, u):
+    return _f32(g / (np.float32(1) + np.exp(-g)) * u)
+
+
+def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq):
+    """Logits [T, V] of `seq` for a block-scaled FP8 checkpoint: `tensors`
+    holds every tensor (fp32 values), `fp8` maps the FP8 weights' names to
+    their dequantised fp32 matrices (e4m3 * scale).  Softmax-greedy routing
+    as forward(); near-tie swaps are not modelled."""
+    if cfg.get("q_lora_rank", 0) or cfg.get("scoring_func", 0) != 0:
+        raise NotImplementedError("oracle.model covers q_lora_rank 0 with softmax scoring")
+    c = cfg
+    W = {n: _f32(a) for n, a in tensors.items()}
+    for n, a in fp8.items():
+        W[n] = _bf16_round(a) if n.endswith("kv_b_proj.weight") else _f32(a)
+    seq = np.asarray(seq, np.int64)
+    T = len(seq)
+    D, H, R = c["hidden_size"], c["num_attention_heads"], c["kv_lora_rank"]
+    nope, rope, v = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+    E, k = c["n_routed_experts"], c["num_experts_per_tok"]
+    eps = c["rms_norm_eps"]
+    orc = oracle()
+    h = _f32(W["model.embed_tokens.weight"][seq])
+    for li in range(c["num_hidden_layers"]):
+        pre = f"model.layers.{li}."
+        xn = _act_fp8(_rmsnorm_rows(h, W[pre + "input_layernorm.weight"], eps))
+        out = np.zeros((T, D), np.float32)
+        rc = orc.orc_mla_layer_seq_fp8act_f32(
+            D, H, nope, rope, v, R, eps, c["rope_theta"],
+            *(p(W[pre + "self_attn." + n + ".weight"], f32p)
+              for n in ("q_proj", "kv_a_proj_with_mqa", "kv_a_layernorm", "kv_b_proj", "o_proj")),
+            p(xn, f32p), T, p(out, f32p))
+        assert rc == 0
+        h = _f32(h + out)
+        xn = _rmsnorm_rows(h, W[pre + "post_attention_layernorm.weight"], eps)
+        xq = _act_fp8(xn)
+
+        def ffn(wg, wu, wd, x):
+            mid = _act_fp8(_silu_mul(x @ wg.T, x @ wu.T))
+            return _f32(mid @ wd.T)
+
+        if pre + "mlp.gate.weight" not in W:
+            out = ffn(*(W[pre + "mlp." + n + "_proj.weight"] for n in ("gate", "up", "down")), xq)
+        else:
+            wgate = W[pre + "mlp.gate.weight"]
+            shared = pre + "mlp.shared_experts.gate_proj.weight" in W
+            out = np.zeros((T, D), np.float32)
+            for t in range(T):
+                logits = np.zeros(E, np.float32)
+                orc.orc_linear_f32(p(wgate, f32p), p(_f32(xn[t]), f32p), D, p(logits, f32p), E)
+                ids = np.zeros(k, np.int32)
+                w = np.zeros(k, np.float32)
+                assert orc.orc_route_softmax_greedy(p(logits, f32p), 1, E, k, int(c["norm_topk_prob"]),
+                                                    float(c["routed_scaling_factor"]), p(ids, i32p),
+                                                    p(w, f32p)) == 0
+                acc = np.zeros(D, np.float32)
+                x = xq[t:t + 1]
+                for e, wt in zip(ids, w):
+                    y = ffn(*(W[pre + f"mlp.experts.{e}.{n}_proj.weight"] for n in ("gate", "up", "down")), x)
+                    acc = _f32(acc + np.float32(wt) * y[0])
+                if shared:
+                    y = ffn(*(W[pre + f"mlp.shared_experts.{n}_proj.weight"] for n in ("gate", "up", "down")), x)
+                    acc = _f32(acc + y[0])
+                out[t] = acc
+        h = _f32(h + out)
+    hn = _rmsnorm_rows(h, W["model.norm.weight"], eps)
+    return _f32(hn @ W["lm_head.weight"].T)

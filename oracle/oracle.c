@@ -221,9 +221,31 @@ ORC_API int orc_mla_decode_paged(const uint16_t* q_lat, const uint16_t* q_rope, 
  * The latent cache is kept in fp32 here; the test pins this restatement to
  * the reference's non-absorbed mla_decode_step.
  */
+ORC_API void orc_act_fp8_roundtrip(float* x, int64_t T, int64_t K);
+
+static int mla_layer_seq(int D, int H, int nope, int rope, int v, int R, float eps, float theta, const float* w_q,
+                         const float* w_kva, const float* w_kva_norm, const float* w_kvb, const float* w_o,
+                         const float* hidden, int T, float* out, int fp8_o);
+
 ORC_API int orc_mla_layer_seq_f32(int D, int H, int nope, int rope, int v, int R, float eps, float theta,
                                   const float* w_q, const float* w_kva, const float* w_kva_norm, const float* w_kvb,
                                   const float* w_o, const float* hidden, int T, float* out) {
+  return mla_layer_seq(D, H, nope, rope, v, R, eps, theta, w_q, w_kva, w_kva_norm, w_kvb, w_o, hidden, T, out, 0);
+}
+
+/* The same layer for a block-scaled FP8 checkpoint: the o_proj input (the
+ * heads' outputs) goes through orc_act_fp8_roundtrip first, as the FP8 GEMM
+ * quantises its activations; the weights are the dequantised ones. */
+ORC_API int orc_mla_layer_seq_fp8act_f32(int D, int H, int nope, int rope, int v, int R, float eps, float theta,
+                                         const float* w_q, const float* w_kva, const float* w_kva_norm,
+                                         const float* w_kvb, const float* w_o, const float* hidden, int T,
+                                         float* out) {
+  return mla_layer_seq(D, H, nope, rope, v, R, eps, theta, w_q, w_kva, w_kva_norm, w_kvb, w_o, hidden, T, out, 1);
+}
+
+static int mla_layer_seq(int D, int H, int nope, int rope, int v, int R, float eps, float theta, const float* w_q,
+                         const float* w_kva, const float* w_kva_norm, const float* w_kvb, const float* w_o,
+                         const float* hidden, int T, float* out, int fp8_o) {
   const int qh = nope + rope;
   const float scale = 1.0f / sqrtf((float)qh);
   float* q = (float*)calloc((size_t)H * qh, sizeof(float));
@@ -257,6 +279,7 @@ ORC_API int orc_mla_layer_seq_f32(int D, int H, int nope, int rope, int v, int R
       if (orc_attend_latent(qfull, lat, pos + 1, R + rope, R, scale, scores, olat) != 0) rc = -1;
       orc_linear_f32(wuv, olat, R, attn + (int64_t)h * v, v);
     }
+    if (fp8_o) orc_act_fp8_roundtrip(attn, 1, (int64_t)H * v);
     orc_linear_f32(w_o, attn, (int64_t)H * v, out + (int64_t)pos * D, D);
   }
   free(q);
@@ -549,6 +572,25 @@ ORC_API void orc_quant_act_1x128(const float* x, int64_t T, int64_t K, uint8_t* 
       for (int64_t c = c0; c < c1; ++c) q[t * K + c] = orc_f32_to_e4m3(x[t * K + c] / sc);
     }
   }
+}
+
+/* An activation as a block-scaled FP8 GEMM sees it: each value rounded to
+ * the bf16 activation buffer, quantised per token and 128 columns
+ * (orc_quant_act_1x128) and dequantised (e4m3 * scale), in place. */
+ORC_API void orc_act_fp8_roundtrip(float* x, int64_t T, int64_t K) {
+  const int64_t G = (K + 127) / 128;
+  uint8_t* q = (uint8_t*)malloc((size_t)(T * K));
+  float* sc = (float*)malloc(sizeof(float) * (size_t)(T * G));
+  uint16_t b;
+  for (int64_t i = 0; i < T * K; ++i) {
+    orc_f32_to_bf16_n(x + i, 1, &b);
+    orc_bf16_to_f32_n(&b, 1, x + i);
+  }
+  orc_quant_act_1x128(x, T, K, q, sc);
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t c = 0; c < K; ++c) x[t * K + c] = orc_e4m3_to_f32(q[t * K + c]) * sc[t * G + c / 128];
+  free(q);
+  free(sc);
 }
 
 /* Weight quantisation per 128x128 block: scale = amax / 448 over the block
