@@ -27,8 +27,10 @@
 // contiguous segment of the row that it walks 32 items at a time (ballot +
 // popc), four loads ahead; ranks are only computed when a cut splits a run
 // of equal keys, and every other pass loads float4s in no particular order.  The row is re-read from L2 on every pass (at most 17 with
-// both cuts, 3 with none).  A top-k cut of at most 1024 items instead gathers
-// its survivors into shared memory and finishes there (6 passes).
+// both cuts, 3 with none).  A top-k cut of at most 1024 items, or a top-p
+// nucleus of at most 1024, is instead gathered into shared memory, sorted,
+// and drawn from there in the reference's float order (5 passes for top-k,
+// 8 for top-p).
 
 #include <cuda_runtime.h>
 
@@ -320,27 +322,29 @@ __device__ int eq_base(SampleSmem& s, const RowView& r, uint32_t K) {
   return (int)s.wbase[threadIdx.x >> 5];
 }
 
-// Small top-k (k <= kCompactMax): the k survivors are gathered into shared
-// memory, sorted (bitonic, descending x then ascending id), and the softmax,
-// top-p cut and draw run over that list in the reference's own float order
-// (sampler.cpp:42-76): sums left to right, p = e * (1 / sum), renormalised by
-// division.  Returns the id (valid in thread 0).
-__device__ int compact_and_draw(SampleSmem& s, const RowView& r, int k, bool fp, float top_p, float u) {
-  u64* A = hist_cols();                                  // [kCompactMax] (key << 32) | ~id, sorted ascending
-  float* e = reinterpret_cast<float*>(A + kCompactMax);  // [kCompactMax] exp(x - max) in descending order
-  int* idv = reinterpret_cast<int*>(e + kCompactMax);    // [kCompactMax] ids in descending order
-  int N = 2;
-  while (N < k) N <<= 1;
-  for (int j = threadIdx.x; j < N; j += blockDim.x) A[j] = 0;  // pads sort first (smallest)
+// Gather the survivors of the active cuts (at most kCompactMax) into shared
+// memory, sorted by descending x, ties to the lower id: e[j] = exp(x_j - mx)
+// (mx = the first item's x when mx is NaN) and idv[j] for j < n.  Returns n,
+// or -1 (in every thread) when there are more survivors than kCompactMax.
+__device__ int gather_sorted(SampleSmem& s, const RowView& r, float mx, float*& e, int*& idv) {
+  u64* A = hist_cols();  // [kCompactMax] (key << 32) | ~id, sorted ascending
+  e = reinterpret_cast<float*>(A + kCompactMax);
+  idv = reinterpret_cast<int*>(e + kCompactMax);
+  for (int j = threadIdx.x; j < kCompactMax; j += blockDim.x) A[j] = 0;  // pads sort first (smallest)
   if (threadIdx.x == 0) s.ncomp = 0;
   __syncthreads();
   walk(r, [&](int i, float, uint32_t key, bool, bool keep) {
     if (keep) {
       const int slot = atomicAdd(&s.ncomp, 1);
-      if (slot < N) A[slot] = ((u64)key << 32) | (u64)(~(uint32_t)i);
+      if (slot < kCompactMax) A[slot] = ((u64)key << 32) | (u64)(~(uint32_t)i);
     }
   });
   __syncthreads();
+  const int total = s.ncomp;
+  if (total > kCompactMax) return -1;
+  int N = 2;
+  while (N < total) N <<= 1;
+  // the first N slots hold every survivor (the pads are zero)
   for (int kk = 2; kk <= N; kk <<= 1) {
     for (int j = kk >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < N; i += blockDim.x) {
@@ -356,44 +360,55 @@ __device__ int compact_and_draw(SampleSmem& s, const RowView& r, int k, bool fp,
       __syncthreads();
     }
   }
-  const int n = min(s.ncomp, N);
-  const float mx = key_to_float((uint32_t)(A[N - 1] >> 32));
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+  const float m0 = mx == mx ? mx : key_to_float((uint32_t)(A[N - 1] >> 32));
+  for (int j = threadIdx.x; j < total; j += blockDim.x) {
     const u64 c = A[N - 1 - j];
-    e[j] = expf(key_to_float((uint32_t)(c >> 32)) - mx);
+    e[j] = expf(key_to_float((uint32_t)(c >> 32)) - m0);
     idv[j] = (int)(~(uint32_t)c);
   }
   __syncthreads();
-  int id = 0;
-  if (threadIdx.x == 0 && n > 0) {
+  return total;
+}
+
+// The draw over a gathered list in the reference's float order
+// (sampler.cpp:42-76): the running sums left to right, p = e * inv.
+// top_k mode (inv < 0): the softmax over the list (inv = 1 / sum e), then the
+// top-p cut when fp, renormalised by division; nucleus mode (inv >= 0): the
+// list is the top-p nucleus of a softmax whose 1 / sum is inv, renormalised
+// by the list's sum.  Thread 0's result.
+__device__ int draw_sorted(const float* e, const int* idv, int n, float inv, bool fp, float top_p, float u) {
+  if (threadIdx.x != 0 || n <= 0) return 0;
+  const bool topk = inv < 0.0f;
+  if (topk) {
     float sum = 0.0f;
     for (int j = 0; j < n; ++j) sum += e[j];
-    const float inv = 1.0f / sum;
-    int keep = n;
-    float s2 = 1.0f;
-    if (fp) {
-      float cum = 0.0f;
-      keep = 0;
-      for (; keep < n; ++keep) {
-        cum += e[keep] * inv;
-        if (cum >= top_p) {
-          ++keep;
-          break;
-        }
-      }
-      keep = max(1, min(keep, n));
-      s2 = 0.0f;
-      for (int j = 0; j < keep; ++j) s2 += e[j] * inv;
-    }
-    id = idv[keep - 1];
+    inv = 1.0f / sum;
+  }
+  int keep = n;
+  if (topk && fp) {
     float cum = 0.0f;
-    for (int j = 0; j < keep; ++j) {
-      const float pj = fp ? (e[j] * inv) / s2 : e[j] * inv;
-      cum += pj;
-      if (u <= cum) {
-        id = idv[j];
+    keep = 0;
+    for (; keep < n; ++keep) {
+      cum += e[keep] * inv;
+      if (cum >= top_p) {
+        ++keep;
         break;
       }
+    }
+    keep = max(1, min(keep, n));
+  }
+  const bool renorm = fp;  // a top-p cut was taken: divide by the kept sum
+  float s2 = 0.0f;
+  if (renorm)
+    for (int j = 0; j < keep; ++j) s2 += e[j] * inv;
+  int id = idv[keep - 1];
+  float cum = 0.0f;
+  for (int j = 0; j < keep; ++j) {
+    const float pj = renorm ? (e[j] * inv) / s2 : e[j] * inv;
+    cum += pj;
+    if (u <= cum) {
+      id = idv[j];
+      break;
     }
   }
   return id;
@@ -416,14 +431,16 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
   const float u = uniforms[blockIdx.x];
   if (threadIdx.x == 0) s.out_id = 0;
 
+  const bool fk = top_k > 0 && top_k < V, fp = top_p > 0.0f && top_p < 1.0f;
+  const bool small_k = fk && top_k <= kCompactMax;  // finished on the gathered survivors
   // max of x: the top-k survivors always include it, so it is the softmax's max
   float mx = -INFINITY;
-  walk(r, [&](int, float x, uint32_t, bool in, bool) {
-    if (in) mx = fmaxf(mx, x);
-  });
-  mx = block_max(s, mx);
-
-  const bool fk = top_k > 0 && top_k < V, fp = top_p > 0.0f && top_p < 1.0f;
+  if (!small_k) {
+    walk(r, [&](int, float x, uint32_t, bool in, bool) {
+      if (in) mx = fmaxf(mx, x);
+    });
+    mx = block_max(s, mx);
+  }
   if (fk) {
     const Selected c = radix_select(s, r, [](float, uint32_t) { return 1ull; }, (u64)top_k, -1.0);
     r.Kk = c.key;
@@ -434,8 +451,11 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
       r.need_k = 0x7fffffff;
     }
     r.fk = true;
-    if (top_k <= kCompactMax) {
-      const int id = compact_and_draw(s, r, top_k, top_p > 0.0f && top_p < 1.0f, top_p, u);
+    if (small_k) {
+      float* e;
+      int* idv;
+      const int n = gather_sorted(s, r, NAN, e, idv);  // exactly top_k survivors
+      const int id = draw_sorted(e, idv, n, -1.0f, fp, top_p, u);
       if (threadIdx.x == 0) out[blockIdx.x] = id;
       return;
     }
@@ -493,6 +513,15 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
         r.need_p = 0x7fffffff;
       }
       r.fp = true;
+      // a nucleus of at most kCompactMax items is drawn from in shared memory
+      float* e;
+      int* idv;
+      const int n = gather_sorted(s, r, mx, e, idv);
+      if (n > 0) {
+        const int id = draw_sorted(e, idv, n, inv, true, top_p, u);
+        if (threadIdx.x == 0) out[blockIdx.x] = id;
+        return;
+      }
     }
     // the draw: the item at which the survivors' mass, in descending order, reaches u * total
     const Selected d = radix_select(s, r, mass, 0, (double)u);
