@@ -127,6 +127,16 @@ _PROTOS = [
      [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, ctypes.POINTER(Sampling), ctypes.POINTER(ctypes.c_float), _vp, _c_i32p]),
     ("dsb_generate_sampled", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _ci, _vp, _vp, _ci, ctypes.c_int32, ctypes.POINTER(Sampling), _vp, _vp]),
+    ("dsb_tokenizer_load", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_tokenizer_destroy", ctypes.c_int, [_vp]),
+    ("dsb_tokenizer_error", ctypes.c_char_p, []),
+    ("dsb_tokenizer_info", ctypes.c_int,
+     [_vp, ctypes.POINTER(_ci), ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32),
+      ctypes.POINTER(ctypes.c_int32)]),
+    ("dsb_tokenizer_encode", ctypes.c_int,
+     [_vp, ctypes.c_char_p, ctypes.c_size_t, _c_i32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    ("dsb_tokenizer_decode", ctypes.c_int,
+     [_vp, _c_i32p, ctypes.c_size_t, _ci, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     ("dsb_checkpoint_open", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     ("dsb_checkpoint_close", ctypes.c_int, [ctypes.c_void_p]),
     ("dsb_checkpoint_error", ctypes.c_char_p, []),
@@ -579,6 +589,58 @@ class Checkpoint:
 
     def __exit__(self, *exc):
         self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Tokenizer:
+    """dsb_tokenizer: the reference's greedy tokenizer over a tokenizer.json (host only)."""
+
+    def __init__(self, path: str):
+        self._l = lib()
+        h = ctypes.c_void_p()
+        rc = self._l.dsb_tokenizer_load(os.fsencode(path), ctypes.byref(h))
+        if rc != DSB_OK:
+            raise DsbError(rc, self._l.dsb_tokenizer_error().decode())
+        self.h = h
+
+    def _check(self, rc: int):
+        if rc != DSB_OK:
+            raise DsbError(rc, self._l.dsb_tokenizer_error().decode())
+
+    def info(self) -> dict:
+        n, b, e, u = ctypes.c_int(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        self._check(self._l.dsb_tokenizer_info(self.h, ctypes.byref(n), ctypes.byref(b), ctypes.byref(e),
+                                               ctypes.byref(u)))
+        return {"n_ids": n.value, "bos": b.value, "eos": e.value, "unk": u.value}
+
+    def encode(self, text: "str | bytes") -> list[int]:
+        data = text.encode() if isinstance(text, str) else bytes(text)
+        n = ctypes.c_size_t()
+        cap = len(data) + 1  # at most one id per byte
+        ids = (ctypes.c_int32 * cap)()
+        self._check(self._l.dsb_tokenizer_encode(self.h, data, len(data), ids, cap, ctypes.byref(n)))
+        return list(ids[: n.value])
+
+    def decode(self, ids, skip_special: bool = True) -> bytes:
+        arr = (ctypes.c_int32 * max(1, len(ids)))(*[int(i) for i in ids])
+        n = ctypes.c_size_t()
+        rc = self._l.dsb_tokenizer_decode(self.h, arr, len(ids), int(skip_special), None, 0, ctypes.byref(n))
+        if rc != DSB_OK and n.value == 0:
+            self._check(rc)
+        buf = ctypes.create_string_buffer(n.value + 1)
+        self._check(self._l.dsb_tokenizer_decode(self.h, arr, len(ids), int(skip_special), buf, n.value + 1,
+                                                 ctypes.byref(n)))
+        return buf.raw[: n.value]
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._l.dsb_tokenizer_destroy(self.h)
+            self.h = None
 
     def __del__(self):
         try:

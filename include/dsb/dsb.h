@@ -643,6 +643,38 @@ DSB_API int dsb_checkpoint_find(const dsb_checkpoint* ck, const char* name, int*
  * not take, fails the call with the tensor's name. */
 DSB_API int dsb_model_upload_checkpoint(dsb_model* model, const dsb_checkpoint* ck, int* n_uploaded, int* n_skipped);
 
+/* ---------------------------------------------------------------- tokenizer */
+
+/* ds::rt::Tokenizer (src/runtime/tokenizer.cpp:1-171) on the host: the
+ * reference's greedy longest-match encoder and trimming decoder over a
+ * Hugging Face tokenizer.json (model.vocab, model.unk_token_id,
+ * added_tokens, root bos/eos ids).  Same ids and text as the reference for
+ * the same file, except that an added token's "special": true counts as
+ * special (the reference reads JSON booleans as false) and ids must lie in
+ * [0, 2^24).  Host only: no GPU, no context; messages from
+ * dsb_tokenizer_error. */
+typedef struct dsb_tokenizer dsb_tokenizer;
+
+DSB_API int dsb_tokenizer_load(const char* path, dsb_tokenizer** out);
+DSB_API int dsb_tokenizer_destroy(dsb_tokenizer* tok);
+/* The message of this thread's last failed dsb_tokenizer_* call. */
+DSB_API const char* dsb_tokenizer_error(void);
+/* Number of ids (largest id + 1) and the bos / eos / unk ids (-1: none). */
+DSB_API int dsb_tokenizer_info(const dsb_tokenizer* tok, int* n_ids, int32_t* bos_id, int32_t* eos_id,
+                               int32_t* unk_id);
+/* Tokenizer::encode (tokenizer.cpp:116-155) of text[0, len): *n_ids receives
+ * the number of ids, written to ids[0, cap); a call with too small a buffer
+ * (cap = 0 to ask) fails with DSB_EINVAL after setting *n_ids.  Text the
+ * vocabulary cannot cover fails with DSB_EINVAL and the byte offset. */
+DSB_API int dsb_tokenizer_encode(const dsb_tokenizer* tok, const char* text, size_t len, int32_t* ids, size_t cap,
+                                 size_t* n_ids);
+/* Tokenizer::decode (tokenizer.cpp:157-171): the pieces of ids[0, n),
+ * trimmed, special ids left out when skip_special; *len receives the byte
+ * count, written to out[0, cap) (NUL-terminated when there is room); too
+ * small a buffer fails with DSB_EINVAL after setting *len. */
+DSB_API int dsb_tokenizer_decode(const dsb_tokenizer* tok, const int32_t* ids, size_t n, int skip_special, char* out,
+                                 size_t cap, size_t* len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -134,6 +134,10 @@ def ref() -> ctypes.CDLL:
         _proto(l, "ref_sampler_draws", ctypes.c_int,
                [f32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float, ctypes.c_uint32, ctypes.c_int, i32p])
         _proto(l, "ref_sampler_uniforms", ctypes.c_int, [ctypes.c_uint32, ctypes.c_int, f32p])
+        _proto(l, "ref_tokenizer_encode", ctypes.c_int,
+               [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, i32p, ctypes.c_int, ctypes.c_char_p, ctypes.c_int])
+        _proto(l, "ref_tokenizer_decode", ctypes.c_int,
+               [ctypes.c_char_p, i32p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int])
         _ref = l
     return _ref
 
@@ -208,3 +212,26 @@ def ref_sampler(logits, temperature, top_k, top_p, seed, n) -> tuple[np.ndarray,
     assert ref().ref_sampler_draws(p(x, f32p), x.size, temperature, top_k, top_p, seed, n, p(ids, i32p)) == 0
     ref().ref_sampler_uniforms(seed, n, p(u, f32p))
     return ids, u
+
+
+def ref_tokenize(path: str, data: bytes):
+    """The reference's Tokenizer::encode on `data`: the id list, or the error message (str)."""
+    cap = len(data) + 1
+    ids = np.zeros(cap, np.int32)
+    msg = ctypes.create_string_buffer(512)
+    n = ref().ref_tokenizer_encode(os.fsencode(path), data, len(data), p(ids, i32p), cap, msg, len(msg))
+    return msg.value.decode() if n < 0 else ids[:n].tolist()
+
+
+def ref_detokenize(path: str, ids, skip_special: bool = True):
+    """The reference's Tokenizer::decode: bytes, or None if it threw."""
+    a = np.ascontiguousarray(np.asarray(ids, np.int32).reshape(-1))
+    if a.size == 0:
+        a = np.zeros(1, np.int32)
+        n_ids = 0
+    else:
+        n_ids = a.size
+    cap = 1 << 20
+    out = ctypes.create_string_buffer(cap)
+    n = ref().ref_tokenizer_decode(os.fsencode(path), p(a, i32p), n_ids, int(skip_special), out, cap)
+    return None if n < 0 else out.raw[:n]

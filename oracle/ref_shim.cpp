@@ -20,6 +20,7 @@
 #include "ds/models/deepseek/ops.h"
 #include "ds/models/deepseek/weights.h"
 #include "ds/runtime/model.h"
+#include "ds/runtime/tokenizer.h"
 
 #include <algorithm>
 #include <cstdint>
@@ -375,6 +376,35 @@ __attribute__((visibility("default"))) int ref_sampler_uniforms(std::uint32_t se
     out[i] = dist(rng);
   }
   return 0;
+}
+
+// ds::rt::Tokenizer (src/runtime/tokenizer.cpp) loaded from `path`: encode
+// text[0, len) into ids[0, cap); returns the id count, or -1 with the
+// exception message in msg.
+__attribute__((visibility("default"))) int ref_tokenizer_encode(const char* path, const char* text, int len,
+                                                                std::int32_t* ids, int cap, char* msg, int msg_len) {
+  try {
+    const auto tok = ds::rt::Tokenizer::load_from_file(path);
+    const auto v = tok.encode(std::string(text, text + len));
+    for (std::size_t i = 0; i < v.size() && static_cast<int>(i) < cap; ++i) ids[i] = v[i];
+    return static_cast<int>(v.size());
+  } catch (const std::exception& e) {
+    std::snprintf(msg, static_cast<std::size_t>(msg_len), "%s", e.what());
+    return -1;
+  }
+}
+
+// Tokenizer::decode of ids[0, n) into out[0, cap); returns the byte count, or -1.
+__attribute__((visibility("default"))) int ref_tokenizer_decode(const char* path, const std::int32_t* ids, int n,
+                                                                int skip_special, char* out, int cap) {
+  try {
+    const auto tok = ds::rt::Tokenizer::load_from_file(path);
+    const auto s = tok.decode(std::vector<std::int32_t>(ids, ids + n), skip_special != 0);
+    std::memcpy(out, s.data(), std::min<std::size_t>(s.size(), static_cast<std::size_t>(cap)));
+    return static_cast<int>(s.size());
+  } catch (const std::exception&) {
+    return -1;
+  }
 }
 
 }  // extern "C"
