@@ -28,7 +28,7 @@ def model_dir(tmp_path_factory):
     d = str(tmp_path_factory.mktemp("tiny_cli"))
     tensors = list(tiny_tensors())
     write_model_dir(d, hf_config(TINY), tensors, n_shards=3)
-    make_tokenizer(os.path.join(d, "tokenizer.json"))
+    make_tokenizer(os.path.join(d, "tokenizer.json"), min_ids=TINY["vocab_size"])
     return d, len(tensors)
 
 

@@ -29,7 +29,7 @@ def cli(*args):
 def model_dir(tmp_path_factory):
     d = str(tmp_path_factory.mktemp("tiny_cli_gpu"))
     write_model_dir(d, hf_config(TINY), list(tiny_tensors()), n_shards=2)
-    make_tokenizer(os.path.join(d, "tokenizer.json"))
+    make_tokenizer(os.path.join(d, "tokenizer.json"), min_ids=TINY["vocab_size"])
     return d
 
 

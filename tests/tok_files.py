@@ -18,7 +18,9 @@ PUNCT = list(".,;:!?'\"-()[]")
 BOOL_SPECIAL = 9  # flagged "special": true
 
 
-def make_tokenizer(path, seed=0, root_ids=False):
+def make_tokenizer(path, seed=0, root_ids=False, min_ids=0):
+    """Write tokenizer.json; min_ids pads the vocabulary with filler pieces so
+    that every id a model of that vocabulary size emits decodes."""
     rng = np.random.default_rng(seed)
     pieces = set("abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789") | set(PUNCT)
     extra = ["".join(rng.choice(list("abcdefghijklmnopqrstuvwxyz"), size=int(rng.integers(2, 9)))) for _ in range(300)]
@@ -32,6 +34,7 @@ def make_tokenizer(path, seed=0, root_ids=False):
         pieces.add(SPM + u)
     pieces |= set(VARIANT_ONLY.values()) | {"##zebra", "##yak"}
     pieces = sorted(pieces)
+    pieces += [f"<filler_{i}>" for i in range(max(0, min_ids - len(pieces)))]
     ids = rng.permutation(len(pieces))
     vocab = {p: int(i) for p, i in zip(pieces, ids)}
     added = [
