@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -96,6 +97,23 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 // checkpoint reader, which uploads through dsb_model_set_tensor).
 dsb_ctx* model_ctx(const dsb_model* m);
 const dsb_model_config* model_config(const dsb_model* m);
+
+// Devices a process may drive; per-device one-time state is sized by it.
+constexpr int kMaxDevices = 64;
+
+// Raise `kernel`'s dynamic shared memory limit to `bytes` the first time it
+// runs on ctx's device (the attribute belongs to the kernel in each device's
+// context).  `done` is the caller's per-kernel flag array.
+template <class Kernel>
+int smem_attr_once(dsb_ctx* ctx, Kernel kernel, size_t bytes, std::atomic<bool> (&done)[kMaxDevices]) {
+  if (ctx->device < 0 || ctx->device >= kMaxDevices) return fail(ctx, DSB_EUNSUPPORTED, "device %d", ctx->device);
+  if (!done[ctx->device].load(std::memory_order_acquire)) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return fail(ctx, DSB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done[ctx->device].store(true, std::memory_order_release);
+  }
+  return DSB_OK;
+}
 
 // Check a CUDA runtime call; on failure record it and return DSB_ECUDA.
 #define DSB_CUDA_TRY(ctx, call)                                                                     \

@@ -419,11 +419,8 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int max_splits, int m_ti
     p.counters = ctx->counters;
   }
   auto kern = gemm_bf16_kernel<NT>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
-    attr_set = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  if (int rc = smem_attr_once(ctx, kern, S::SMEM, attr_set); rc != DSB_OK) return rc;
   DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, kThreads, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;

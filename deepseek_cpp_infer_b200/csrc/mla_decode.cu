@@ -633,11 +633,8 @@ int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const 
   if (rc != DSB_OK) return rc;
 
   auto kern = mla_decode_kernel<R, P, NCTA>;
-  static bool attr_set = false;  // per template instance
-  if (!attr_set) {
-    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];  // per template instance
+  if (int rc = smem_attr_once(ctx, kern, S::SMEM_BYTES, attr_set); rc != DSB_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(plan->n_items * NCTA));
   cfg.blockDim = dim3(kMlaThreads);

@@ -777,11 +777,8 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
   if (rc != DSB_OK) return rc;
   const size_t smem = (size_t)(D + E + E + n_extra + 2 * T * (k + n_extra)) * sizeof(float);
   if (smem > 48 * 1024) {
-    static bool attr_set = false;
-    if (!attr_set) {
-      DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(moe_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-      attr_set = true;
-    }
+    static std::atomic<bool> attr_set[kMaxDevices];
+    if (int rc2 = smem_attr_once(ctx, moe_front_kernel, 200 * 1024, attr_set); rc2 != DSB_OK) return rc2;
   }
   const dim3 grid((E + kFrontExperts - 1) / kFrontExperts, T);
   launch_pdl(moe_front_kernel, grid, 256, smem, ctx->stream, h, w_norm, D, eps, w_router, E, bias, k, scoring, n_group,

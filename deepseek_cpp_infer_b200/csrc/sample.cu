@@ -46,7 +46,6 @@ namespace {
 
 using u64 = unsigned long long;
 
-constexpr int kMaxDevices = 64;
 constexpr int kThreads = 1024, kWarps = kThreads / 32, kBins = 256, kAhead = 4, kAheadVec = 2, kCompactMax = 1024;
 constexpr size_t kHistBytes = (size_t)kBins * 32 * sizeof(unsigned long long);  // dynamic shared memory
 constexpr double kFix = 1099511627776.0;  // 2^40: fixed-point unit of probability mass
@@ -577,12 +576,7 @@ int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, flo
                 const float* uniforms, int32_t* out) {
   const float t = temperature <= 0.0f ? 1.0f : temperature;
   static std::atomic<bool> attr_set[kMaxDevices];
-  if (ctx->device < 0 || ctx->device >= kMaxDevices) return fail(ctx, DSB_EUNSUPPORTED, "dsb_sample: device index");
-  if (!attr_set[ctx->device].load()) {
-    DSB_CUDA_TRY(ctx, cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)kHistBytes));
-    attr_set[ctx->device].store(true);
-  }
+  if (int rc = smem_attr_once(ctx, sample_rows_kernel, kHistBytes, attr_set); rc != DSB_OK) return rc;
   const int vec = ((uintptr_t)logits % 16 == 0 && ld % 4 == 0) ? 1 : 0;
   DSB_CUDA_TRY(ctx, launch_pdl(sample_rows_kernel, B, kThreads, kHistBytes, ctx->stream, logits, ld, V, t, top_k,
                                top_p, uniforms, out, vec));
