@@ -33,15 +33,15 @@
 
 namespace dsb {
 namespace {
-thread_local std::string g_host_error;
+thread_local std::string g_host_error[2];
 }  // namespace
 
-int host_fail(int code, std::string msg) {
-  g_host_error = std::move(msg);
+int host_fail(int code, std::string msg, HostChannel channel) {
+  g_host_error[channel] = std::move(msg);
   return code;
 }
 
-const char* host_error() { return g_host_error.c_str(); }
+const char* host_error(HostChannel channel) { return g_host_error[channel].c_str(); }
 }  // namespace dsb
 
 namespace {

@@ -16,9 +16,12 @@
 
 namespace dsb {
 
-// Record `msg` as this thread's last host-side error and return `code`.
-int host_fail(int code, std::string msg);
-const char* host_error();
+// This thread's last error message of a host-only subsystem of the C ABI
+// (each has its own: dsb_checkpoint_error, dsb_tokenizer_error).
+enum HostChannel { kHostCheckpoint = 0, kHostTokenizer = 1 };
+// Record `msg` on `channel` and return `code`.
+int host_fail(int code, std::string msg, HostChannel channel = kHostCheckpoint);
+const char* host_error(HostChannel channel = kHostCheckpoint);
 
 struct Json {
   enum Kind { Null, Bool, Int, Num, Str, Arr, Obj } kind = Null;

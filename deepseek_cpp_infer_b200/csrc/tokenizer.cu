@@ -50,7 +50,7 @@ using dsb::Json;
 
 constexpr int64_t kMaxTokenId = (1 << 24) - 1;
 
-int tk_fail(int code, std::string msg) { return dsb::host_fail(code, std::move(msg)); }
+int tk_fail(int code, std::string msg) { return dsb::host_fail(code, std::move(msg), dsb::kHostTokenizer); }
 
 bool read_file(const std::string& path, std::string* out) {
   FILE* f = std::fopen(path.c_str(), "rb");
@@ -173,7 +173,7 @@ bool lookup(const dsb_tokenizer& tk, const char* p, size_t n, bool word_start, s
 
 }  // namespace
 
-extern "C" const char* dsb_tokenizer_error(void) { return dsb::host_error(); }
+extern "C" const char* dsb_tokenizer_error(void) { return dsb::host_error(dsb::kHostTokenizer); }
 
 extern "C" int dsb_tokenizer_load(const char* path, dsb_tokenizer** out) {
   if (path == nullptr || out == nullptr) return tk_fail(DSB_EINVAL, "dsb_tokenizer_load: bad arguments");
