@@ -17,8 +17,9 @@
 // keep the lower ids.
 //
 // Nothing is sorted.  Each cut is a radix select over order-preserving 32-bit
-// keys of x (four passes of 8 bits), weighted by counts (the top-k cut) or by
-// probability mass (the top-p cut and the draw).  Masses are fixed point,
+// keys of x (four passes of 8 bits), weighted by counts (the top-k cut, in
+// 32-bit counters) or by probability mass (the top-p cut and the draw).
+// Masses are fixed point,
 // q = round(p * 2^40) in uint64, so the shared-memory atomic sums do not
 // depend on the order the atomics land in: a row's result is deterministic.
 // The histogram has one column per lane (256 bins x 32 lanes, 64 KB), so
@@ -257,26 +258,34 @@ struct Selected {
 // the item at which the cumulative weight first reaches the target: `target`
 // itself, or with frac >= 0 max(1, ceil(frac * total)).  weight(x, key) is
 // the candidate's weight (1 for counts, its fixed-point mass otherwise).
-template <class Wt>
+// COUNT: every weight is 1 and the histogram uses 32-bit counters.
+template <bool COUNT, class Wt>
 __device__ Selected radix_select(SampleSmem& s, const RowView& r, Wt weight, u64 target, double frac) {
   u64* H = hist_cols();
+  unsigned* H32 = reinterpret_cast<unsigned*>(H);
   const uint32_t lane = threadIdx.x & 31;
   uint32_t prefix = 0;
   u64 rem = target;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int c = threadIdx.x; c < kBins * 32; c += blockDim.x) H[c] = 0;
+    for (int c = threadIdx.x; c < kBins * 32; c += blockDim.x) {
+      if (COUNT) H32[c] = 0u;
+      else H[c] = 0;
+    }
     __syncthreads();
     walk(r, [&](int, float x, uint32_t key, bool, bool keep) {
-      if (keep && (pass == 0 || (key >> (shift + 8)) == prefix))
-        atomicAdd(&H[((key >> shift) & 255u) * 32 + lane], weight(x, key));
+      if (keep && (pass == 0 || (key >> (shift + 8)) == prefix)) {
+        const uint32_t cell = ((key >> shift) & 255u) * 32 + lane;
+        if (COUNT) atomicAdd(&H32[cell], 1u);
+        else atomicAdd(&H[cell], weight(x, key));
+      }
     });
     __syncthreads();
     {  // bin totals: 4 threads per bin, 8 lane columns each
       const int bin = threadIdx.x >> 2, q = threadIdx.x & 3;
       u64 t = 0;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) t += H[bin * 32 + q * 8 + c];
+      for (int c = 0; c < 8; ++c) t += COUNT ? (u64)H32[bin * 32 + q * 8 + c] : H[bin * 32 + q * 8 + c];
       t += __shfl_xor_sync(0xffffffffu, t, 1);
       t += __shfl_xor_sync(0xffffffffu, t, 2);
       if (q == 0) s.bins[bin] = t;
@@ -441,7 +450,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
     mx = block_max(s, mx);
   }
   if (fk) {
-    const Selected c = radix_select(s, r, [](float, uint32_t) { return 1ull; }, (u64)top_k, -1.0);
+    const Selected c = radix_select<true>(s, r, [](float, uint32_t) { return 1ull; }, (u64)top_k, -1.0);
     r.Kk = c.key;
     if (c.rem < c.eq) {  // the cut splits a run of equal keys: rank them by id
       r.need_k = (int)c.rem;
@@ -501,7 +510,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
     __syncthreads();
   } else {
     if (fp) {
-      const Selected c = radix_select(s, r, mass, 0, (double)top_p);
+      const Selected c = radix_select<false>(s, r, mass, 0, (double)top_p);
       const u64 q = mass(key_to_float(c.key), c.key);
       r.Kp = c.key;
       const u64 m = q > 0 ? (c.rem + q - 1) / q : 0;  // items with the key that the cut keeps
@@ -523,7 +532,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
       }
     }
     // the draw: the item at which the survivors' mass, in descending order, reaches u * total
-    const Selected d = radix_select(s, r, mass, 0, (double)u);
+    const Selected d = radix_select<false>(s, r, mass, 0, (double)u);
     const u64 qd = mass(key_to_float(d.key), d.key);
     const int m = qd > 0 ? (int)((d.rem + qd - 1) / qd) : 1;  // the m-th survivor with this key, in id order
     if (m == 1) {
