@@ -17,12 +17,12 @@
 // keep the lower ids.
 //
 // Nothing is sorted.  Each cut is a radix select over order-preserving 32-bit
-// keys of x (four passes of 8 bits), weighted by counts (the top-k cut, in
-// 32-bit counters) or by probability mass (the top-p cut and the draw).
-// Masses are fixed point,
+// keys of x (four passes of 8 bits), weighted by counts (the top-k cut) or
+// by probability mass (the top-p cut and the draw), all in 32-bit shared
+// counters (a mass in two: its high and low 16 bits).  Masses are fixed point,
 // q = round(p * 2^40) in uint64, so the shared-memory atomic sums do not
 // depend on the order the atomics land in: a row's result is deterministic.
-// The histogram has one column per lane (256 bins x 32 lanes, 64 KB), so
+// The histogram has one column per lane (256 bins x 32 lanes x 2, 64 KB), so
 // lanes of a warp never collide on an address even when their keys share a
 // bin.  Rank among equal keys is kept in id order by giving each warp a
 // contiguous segment of the row that it walks 32 items at a time (ballot +
@@ -258,26 +258,31 @@ struct Selected {
 // the item at which the cumulative weight first reaches the target: `target`
 // itself, or with frac >= 0 max(1, ceil(frac * total)).  weight(x, key) is
 // the candidate's weight (1 for counts, its fixed-point mass otherwise).
-// COUNT: every weight is 1 and the histogram uses 32-bit counters.
+// COUNT: every weight is 1, one 32-bit counter per cell.  Otherwise a
+// weight q (< 2^41) goes into two 32-bit counters, q >> 16 and q & 0xffff:
+// the high parts of a cell sum to at most the row's mass / 2^16 (~2^24), the
+// low parts to at most V/32 items x 2^16, below 2^32 for V <= 2^21.
 template <bool COUNT, class Wt>
 __device__ Selected radix_select(SampleSmem& s, const RowView& r, Wt weight, u64 target, double frac) {
-  u64* H = hist_cols();
-  unsigned* H32 = reinterpret_cast<unsigned*>(H);
+  unsigned* Hh = reinterpret_cast<unsigned*>(hist_cols());  // [kBins][32] counts or high parts
+  unsigned* Hl = Hh + kBins * 32;                            // [kBins][32] low parts
   const uint32_t lane = threadIdx.x & 31;
   uint32_t prefix = 0;
   u64 rem = target;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int c = threadIdx.x; c < kBins * 32; c += blockDim.x) {
-      if (COUNT) H32[c] = 0u;
-      else H[c] = 0;
-    }
+    for (int c = threadIdx.x; c < kBins * 32 * (COUNT ? 1 : 2); c += blockDim.x) Hh[c] = 0u;
     __syncthreads();
     walk(r, [&](int, float x, uint32_t key, bool, bool keep) {
       if (keep && (pass == 0 || (key >> (shift + 8)) == prefix)) {
         const uint32_t cell = ((key >> shift) & 255u) * 32 + lane;
-        if (COUNT) atomicAdd(&H32[cell], 1u);
-        else atomicAdd(&H[cell], weight(x, key));
+        if (COUNT) {
+          atomicAdd(&Hh[cell], 1u);
+        } else {
+          const u64 w = weight(x, key);
+          atomicAdd(&Hh[cell], (unsigned)(w >> 16));
+          atomicAdd(&Hl[cell], (unsigned)(w & 0xffffu));
+        }
       }
     });
     __syncthreads();
@@ -285,7 +290,10 @@ __device__ Selected radix_select(SampleSmem& s, const RowView& r, Wt weight, u64
       const int bin = threadIdx.x >> 2, q = threadIdx.x & 3;
       u64 t = 0;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) t += COUNT ? (u64)H32[bin * 32 + q * 8 + c] : H[bin * 32 + q * 8 + c];
+      for (int c = 0; c < 8; ++c) {
+        const int cell = bin * 32 + q * 8 + c;
+        t += COUNT ? (u64)Hh[cell] : ((u64)Hh[cell] << 16) + (u64)Hl[cell];
+      }
       t += __shfl_xor_sync(0xffffffffu, t, 1);
       t += __shfl_xor_sync(0xffffffffu, t, 2);
       if (q == 0) s.bins[bin] = t;
@@ -598,7 +606,7 @@ int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, flo
 extern "C" int dsb_sample(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k,
                           float top_p, const float* uniforms, int32_t* out_ids) {
   if (ctx == nullptr) return DSB_EINVAL;
-  if (logits == nullptr || uniforms == nullptr || out_ids == nullptr || B <= 0 || V <= 0 || ld < V ||
+  if (logits == nullptr || uniforms == nullptr || out_ids == nullptr || B <= 0 || V <= 0 || V > (1 << 21) || ld < V ||
       !(temperature == temperature) || !(top_p == top_p))
     return dsb::fail(ctx, DSB_EINVAL, "dsb_sample: bad arguments");
   return dsb::sample_rows(ctx, logits, ld, B, V, temperature, top_k, top_p, uniforms, out_ids);

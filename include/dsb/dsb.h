@@ -414,8 +414,8 @@ DSB_API int dsb_argmax(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int
  * in id order when no cut is active (the reference's order) and in
  * descending probability, ties to the lower id, when one is (the reference's
  * order there is unspecified).  Deterministic for given inputs.  Rows
- * holding NaN give an unspecified id in [0, V).  out_ids [B] int32 on the
- * device. */
+ * holding NaN give an unspecified id in [0, V).  V <= 2^21.  out_ids [B]
+ * int32 on the device. */
 DSB_API int dsb_sample(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k,
                        float top_p, const float* uniforms, int32_t* out_ids);
 
