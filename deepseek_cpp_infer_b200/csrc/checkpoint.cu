@@ -453,7 +453,12 @@ extern "C" int dsb_model_upload_checkpoint(dsb_model* model, const dsb_checkpoin
                        t.name.c_str(), t.dtype_name.c_str());
     if (t.ndim < 1 || t.ndim > 2)
       return dsb::fail(ctx, DSB_EINVAL, "dsb_model_upload_checkpoint: %s has %d dimensions", t.name.c_str(), t.ndim);
-    const int rc = dsb_model_set_tensor(model, t.name.c_str(), t.dtype, t.shape, t.ndim, t.data);
+    int rc;
+    try {
+      rc = dsb_model_set_tensor(model, t.name.c_str(), t.dtype, t.shape, t.ndim, t.data);
+    } catch (const std::exception& e) {  // host-side conversion buffers
+      return dsb::fail(ctx, DSB_ENOMEM, "dsb_model_upload_checkpoint: %s: %s", t.name.c_str(), e.what());
+    }
     if (rc != DSB_OK) return rc;
     ++up;
   }

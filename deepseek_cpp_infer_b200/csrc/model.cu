@@ -1520,8 +1520,14 @@ int generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids
   const bool sampling = samp != nullptr && (samp->temperature > 0.0f || samp->top_k > 0 || samp->top_p > 0.0f);
   std::vector<std::mt19937> rng;
   if (sampling) {
-    std::random_device rd;
-    for (int b = 0; b < B; ++b) rng.emplace_back(samp->seed != 0 ? samp->seed + (uint32_t)b : rd());
+    for (int b = 0; b < B; ++b) {
+      if (samp->seed != 0) {
+        rng.emplace_back(samp->seed + (uint32_t)b);
+      } else {
+        std::random_device rd;  // only for seed 0, as the reference's Sampler does
+        rng.emplace_back(rd());
+      }
+    }
   }
   std::vector<float> draws;
   for (int b = 0; b < B; ++b) {
@@ -1593,8 +1599,12 @@ extern "C" int dsb_generate_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv,
                                     int32_t eos_id, const dsb_sampling* sampling, int32_t* out_ids,
                                     int32_t* out_counts) {
   if (ctx != nullptr && sampling == nullptr) return fail(ctx, DSB_EINVAL, "dsb_generate_sampled: no sampling config");
-  return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, sampling, out_ids,
-                  out_counts, "dsb_generate_sampled");
+  try {
+    return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, sampling, out_ids,
+                    out_counts, "dsb_generate_sampled");
+  } catch (const std::exception& e) {  // std::random_device or host allocation
+    return ctx ? fail(ctx, DSB_EINVAL, "dsb_generate_sampled: %s", e.what()) : DSB_EINVAL;
+  }
 }
 
 dsb_ctx* dsb::model_ctx(const dsb_model* m) { return m->ctx; }
