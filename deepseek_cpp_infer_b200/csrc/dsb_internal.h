@@ -7,6 +7,8 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <new>
+#include <stdexcept>
 #include <string>
 
 #include "dsb/dsb.h"
@@ -97,6 +99,22 @@ int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 // checkpoint reader, which uploads through dsb_model_set_tensor).
 dsb_ctx* model_ctx(const dsb_model* m);
 const dsb_model_config* model_config(const dsb_model* m);
+
+// Run an entry point's body so that no C++ exception crosses the C ABI: host
+// allocation failures become DSB_ENOMEM, anything else DSB_EINVAL, with the
+// message recorded on ctx (when there is one).
+template <class F>
+int guarded(dsb_ctx* ctx, const char* fn, F&& body) {
+  try {
+    return body();
+  } catch (const std::bad_alloc&) {
+    return ctx ? fail(ctx, DSB_ENOMEM, "%s: out of host memory", fn) : DSB_ENOMEM;
+  } catch (const std::exception& e) {
+    return ctx ? fail(ctx, DSB_EINVAL, "%s: %s", fn, e.what()) : DSB_EINVAL;
+  } catch (...) {
+    return ctx ? fail(ctx, DSB_EINVAL, "%s: unexpected error", fn) : DSB_EINVAL;
+  }
+}
 
 // Devices a process may drive; per-device one-time state is sized by it.
 constexpr int kMaxDevices = 64;

@@ -544,7 +544,7 @@ int set_fp8(dsb_model* m, dsb_model::Layer& L, const std::string& base, bool is_
 
 // ===================================================================== model
 
-extern "C" int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out) {
+static int model_create_impl(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out) {
   if (ctx == nullptr || cfg == nullptr || out == nullptr) return DSB_EINVAL;
   *out = nullptr;
   const dsb_model_config& c = *cfg;
@@ -592,7 +592,7 @@ extern "C" int dsb_model_destroy(dsb_model* m) {
   return DSB_OK;
 }
 
-extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, const int64_t* shape, int ndim,
+static int model_set_tensor_impl(dsb_model* m, const char* cname, int dtype, const int64_t* shape, int ndim,
                                     const void* data) {
   if (m == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = m->ctx;
@@ -938,7 +938,7 @@ extern "C" int dsb_model_weight_bytes(const dsb_model* m, uint64_t* bytes) {
 
 // ================================================================= KV cache
 
-extern "C" int dsb_kvcache_create(dsb_ctx* ctx, const dsb_model* m, int64_t n_blocks, int max_seqs,
+static int kvcache_create_impl(dsb_ctx* ctx, const dsb_model* m, int64_t n_blocks, int max_seqs,
                                   int max_blocks_per_seq, dsb_kvcache** out) {
   if (ctx == nullptr || m == nullptr || out == nullptr) return DSB_EINVAL;
   *out = nullptr;
@@ -984,7 +984,7 @@ extern "C" int dsb_kvcache_destroy(dsb_kvcache* kv) {
   return DSB_OK;
 }
 
-extern "C" int dsb_kvcache_alloc_seq(dsb_kvcache* kv, int* seq_id) {
+static int kvcache_alloc_seq_impl(dsb_kvcache* kv, int* seq_id) {
   if (kv == nullptr || seq_id == nullptr) return DSB_EINVAL;
   for (int s = 0; s < kv->max_seqs; ++s) {
     if (!kv->seq_live[s]) {
@@ -1055,7 +1055,7 @@ __global__ void kv_fill_kernel(bf16* __restrict__ pool, int64_t layer_stride, in
 
 // Append n_tokens synthetic positions to a sequence: pages as decode would
 // take them, every layer's rows filled with N(0, stddev) latents (seeded).
-extern "C" int dsb_kvcache_fill_random(dsb_kvcache* kv, int seq_id, int n_tokens, uint64_t seed, float stddev) {
+static int kvcache_fill_random_impl(dsb_kvcache* kv, int seq_id, int n_tokens, uint64_t seed, float stddev) {
   if (kv == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = kv->ctx;
   if (seq_id < 0 || seq_id >= kv->max_seqs || !kv->seq_live[seq_id] || n_tokens < 0)
@@ -1478,19 +1478,26 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
 
 extern "C" int dsb_decode_step(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
                                const int32_t* tokens, int B, float* logits_host, int32_t* greedy_host) {
-  return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, greedy_host, nullptr);
+  return guarded(ctx, "dsb_decode_step", [&] {
+    return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, greedy_host, nullptr);
+  });
 }
 
 extern "C" int dsb_decode_step_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
                                        const int32_t* tokens, int B, const dsb_sampling* sampling,
                                        const float* uniforms_host, float* logits_host, int32_t* ids_host) {
   if (ctx != nullptr && sampling == nullptr) return fail(ctx, DSB_EINVAL, "dsb_decode_step_sampled: no sampling config");
-  return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, ids_host, nullptr, sampling, uniforms_host);
+  return guarded(ctx, "dsb_decode_step_sampled", [&] {
+    return forward_tokens(ctx, m, kv, seq_ids, tokens, B, false, logits_host, ids_host, nullptr, sampling,
+                          uniforms_host);
+  });
 }
 
 extern "C" int dsb_prefill(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids,
                            const int32_t* tokens, int n_tok, float* logits_host, int32_t* greedy_host, int* n_seq) {
-  return forward_tokens(ctx, m, kv, seq_ids, tokens, n_tok, true, logits_host, greedy_host, n_seq);
+  return guarded(ctx, "dsb_prefill", [&] {
+    return forward_tokens(ctx, m, kv, seq_ids, tokens, n_tok, true, logits_host, greedy_host, n_seq);
+  });
 }
 
 namespace {
@@ -1590,8 +1597,10 @@ int generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids
 extern "C" int dsb_generate(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
                             const int32_t* prompt_tokens, const int32_t* prompt_offsets, int max_new_tokens,
                             int32_t eos_id, int32_t* out_ids, int32_t* out_counts) {
-  return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, nullptr, out_ids,
-                  out_counts, "dsb_generate");
+  return guarded(ctx, "dsb_generate", [&] {
+    return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, nullptr, out_ids,
+                    out_counts, "dsb_generate");
+  });
 }
 
 extern "C" int dsb_generate_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* seq_ids, int B,
@@ -1599,13 +1608,36 @@ extern "C" int dsb_generate_sampled(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv,
                                     int32_t eos_id, const dsb_sampling* sampling, int32_t* out_ids,
                                     int32_t* out_counts) {
   if (ctx != nullptr && sampling == nullptr) return fail(ctx, DSB_EINVAL, "dsb_generate_sampled: no sampling config");
-  try {
+  return guarded(ctx, "dsb_generate_sampled", [&] {  // std::random_device or host allocation may throw
     return generate(ctx, m, kv, seq_ids, B, prompt_tokens, prompt_offsets, max_new_tokens, eos_id, sampling, out_ids,
                     out_counts, "dsb_generate_sampled");
-  } catch (const std::exception& e) {  // std::random_device or host allocation
-    return ctx ? fail(ctx, DSB_EINVAL, "dsb_generate_sampled: %s", e.what()) : DSB_EINVAL;
-  }
+  });
 }
 
 dsb_ctx* dsb::model_ctx(const dsb_model* m) { return m->ctx; }
 const dsb_model_config* dsb::model_config(const dsb_model* m) { return &m->cfg; }
+
+extern "C" int dsb_model_create(dsb_ctx* ctx, const dsb_model_config* cfg, dsb_model** out) {
+  return guarded(ctx, "dsb_model_create", [&] { return model_create_impl(ctx, cfg, out); });
+}
+
+extern "C" int dsb_model_set_tensor(dsb_model* m, const char* cname, int dtype, const int64_t* shape, int ndim,
+                                    const void* data) {
+  return guarded(m ? m->ctx : nullptr, "dsb_model_set_tensor",
+                 [&] { return model_set_tensor_impl(m, cname, dtype, shape, ndim, data); });
+}
+
+extern "C" int dsb_kvcache_create(dsb_ctx* ctx, const dsb_model* m, int64_t n_blocks, int max_seqs,
+                                  int max_blocks_per_seq, dsb_kvcache** out) {
+  return guarded(ctx, "dsb_kvcache_create",
+                 [&] { return kvcache_create_impl(ctx, m, n_blocks, max_seqs, max_blocks_per_seq, out); });
+}
+
+extern "C" int dsb_kvcache_alloc_seq(dsb_kvcache* kv, int* seq_id) {
+  return guarded(kv ? kv->ctx : nullptr, "dsb_kvcache_alloc_seq", [&] { return kvcache_alloc_seq_impl(kv, seq_id); });
+}
+
+extern "C" int dsb_kvcache_fill_random(dsb_kvcache* kv, int seq_id, int n_tokens, uint64_t seed, float stddev) {
+  return guarded(kv ? kv->ctx : nullptr, "dsb_kvcache_fill_random",
+                 [&] { return kvcache_fill_random_impl(kv, seq_id, n_tokens, seed, stddev); });
+}
