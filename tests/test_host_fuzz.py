@@ -8,7 +8,6 @@ import json
 import os
 import struct
 
-import numpy as np
 from hypothesis import HealthCheck, given, settings
 from hypothesis import strategies as st
 
