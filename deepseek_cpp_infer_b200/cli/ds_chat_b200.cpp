@@ -3,8 +3,9 @@
 // over libdsb.so's C ABI, plus a decode-throughput `bench` subcommand.
 //
 //   info      config, tokenizer, index and shards of the model directory
-//   verify    open the checkpoint: index, every shard header, byte ranges
-//   strict    verify, then the dense / MoE layer map from the tensor names
+//   verify    open the checkpoint (index, every shard header, byte ranges)
+//             and check the tensors every layer needs
+//   strict    verify, then the dense / MoE layer map
 //   load      upload every decode tensor to the GPU and finalize the model
 //   run       prefill the prompt, print the next-token prediction
 //   generate  prefill, then decode up to --max-new-tokens ids (greedy, or
@@ -138,6 +139,47 @@ void print_config(const dsb_model_config& c) {
               c.weights_fp8 ? "block-scaled fp8" : "bf16/f32");
 }
 
+// inspect_index (src/models/deepseek/package.cpp:58-120): the tensors every
+// layer needs, "dense" / "MoE" per layer from the experts' presence.  Unlike
+// the reference, a q_lora layer (q_a_proj, q_a_layernorm, q_b_proj) stands in
+// for q_proj and shared experts are required only when the config has some.
+std::vector<std::string> layer_map(const dsb_checkpoint* ckpt, const dsb_model_config& c) {
+  auto has = [&](const std::string& name) {
+    int idx = -1;
+    ck(dsb_checkpoint_find(ckpt, name.c_str(), &idx), "find");
+    return idx >= 0;
+  };
+  auto require = [&](const std::string& name) {
+    if (!has(name)) throw std::runtime_error("missing tensor in index: " + name);
+  };
+  require("lm_head.weight");
+  require("model.embed_tokens.weight");
+  require("model.norm.weight");
+  std::vector<std::string> kinds;
+  for (int i = 0; i < c.num_hidden_layers; ++i) {
+    const std::string base = "model.layers." + std::to_string(i) + ".", attn = base + "self_attn.", mlp = base + "mlp.";
+    for (const char* n : {"input_layernorm.weight", "post_attention_layernorm.weight"}) require(base + n);
+    for (const char* n : {"o_proj.weight", "kv_a_layernorm.weight", "kv_a_proj_with_mqa.weight", "kv_b_proj.weight"})
+      require(attn + n);
+    if (!has(attn + "q_proj.weight"))
+      for (const char* n : {"q_a_proj.weight", "q_a_layernorm.weight", "q_b_proj.weight"}) require(attn + n);
+    const bool moe = has(mlp + "experts.0.gate_proj.weight");
+    kinds.push_back(moe ? "MoE" : "dense");
+    if (!moe) {
+      for (const char* n : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"}) require(mlp + n);
+      continue;
+    }
+    require(mlp + "gate.weight");
+    if (c.n_shared_experts > 0)
+      for (const char* n : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+        require(mlp + "shared_experts." + n);
+    for (int e : {0, c.n_routed_experts - 1})
+      for (const char* n : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+        require(mlp + "experts." + std::to_string(e) + "." + n);
+  }
+  return kinds;
+}
+
 std::vector<int32_t> parse_ids(const std::string& csv) {
   std::vector<int32_t> out;
   size_t i = 0;
@@ -211,6 +253,17 @@ int main_impl(int argc, char** argv) {
   if (cmd == "verify" || cmd == "strict") {
     print_config(cfg);
     if (!has_tok) std::printf("warn: tokenizer.json missing: %s\n", tok_path.c_str());
+    const std::vector<std::string> kinds = layer_map(s.ckpt, cfg);
+    std::printf("Index OK (required tensor keys present). keys=%d\n", n_tensors);
+    if (cmd == "strict") {
+      int moe = 0;
+      std::printf("Layer map (from index):\n");
+      for (size_t li = 0; li < kinds.size(); ++li) {
+        std::printf("  layer %zu: %s\n", li, kinds[li].c_str());
+        moe += kinds[li] == "MoE";
+      }
+      std::printf("MoE layers: %d/%d\n", moe, cfg.num_hidden_layers);
+    }
     uint64_t bytes = 0;
     for (int i = 0; i < n_tensors; ++i) {
       dsb_tensor_info t;
@@ -218,18 +271,6 @@ int main_impl(int argc, char** argv) {
       bytes += t.nbytes;
     }
     std::printf("OK (parsed headers). total_tensors=%d bytes=%llu\n", n_tensors, (unsigned long long)bytes);
-    if (cmd == "strict") {
-      int moe = 0;
-      std::printf("Layer map (from tensor names):\n");
-      for (int li = 0; li < cfg.num_hidden_layers; ++li) {
-        int idx = -1;
-        const std::string e0 = "model.layers." + std::to_string(li) + ".mlp.experts.0.gate_proj.weight";
-        ck(dsb_checkpoint_find(s.ckpt, e0.c_str(), &idx), "find");
-        std::printf("  layer %d: %s\n", li, idx >= 0 ? "MoE" : "dense");
-        moe += idx >= 0;
-      }
-      std::printf("MoE layers: %d/%d\n", moe, cfg.num_hidden_layers);
-    }
     return 0;
   }
 

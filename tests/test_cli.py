@@ -10,6 +10,7 @@ import subprocess
 import pytest
 
 import deepseek_cpp_infer_b200 as dsb
+import oracle as O
 from ckpt_files import hf_config, tiny_tensors, write_model_dir
 from deepseek_cpp_infer_b200.workloads import TINY
 from tok_files import make_tokenizer
@@ -39,9 +40,17 @@ def test_info_verify_strict(model_dir):
     assert "layers: 4" in r.stdout and "Tokenizer: OK" in r.stdout and f"Tensors: {n}" in r.stdout
     r = cli(d)  # verify is the default
     assert r.returncode == 0 and f"OK (parsed headers). total_tensors={n}" in r.stdout, r.stderr
+    assert "Index OK (required tensor keys present)" in r.stdout
     r = cli(d, "strict")
     assert r.returncode == 0, r.stderr
     assert "layer 0: dense" in r.stdout and "layer 3: MoE" in r.stdout and "MoE layers: 3/4" in r.stdout
+
+
+def test_verify_names_a_missing_tensor(tmp_path):
+    tensors = [t for t in tiny_tensors(extras=False) if t[0] != "model.layers.2.mlp.experts.15.down_proj.weight"]
+    write_model_dir(str(tmp_path), hf_config(TINY), tensors, n_shards=1)
+    r = cli(str(tmp_path), "verify")
+    assert r.returncode == 1 and "missing tensor in index: model.layers.2.mlp.experts.15.down_proj.weight" in r.stderr
 
 
 def test_failures_are_fatal_with_a_message(model_dir, tmp_path):
@@ -59,3 +68,32 @@ def test_failures_are_fatal_with_a_message(model_dir, tmp_path):
     for args, text in cases:
         r = cli(*args)
         assert r.returncode == 1 and "fatal: " in r.stderr and text in r.stderr, (args, r.stderr)
+
+
+REF_CLI = os.path.join(os.path.dirname(O.REF_SO), "ds_chat")
+
+
+@pytest.mark.skipif(not os.path.exists(REF_CLI), reason="reference command line (oracle/_ref/ds_chat) not built")
+def test_strict_matches_the_reference_command_line(model_dir, tmp_path):
+    """`strict` on the same checkpoint: the reference's ds_chat and this one
+    report the same key count, layer map and tensor total; a missing expert
+    tensor fails both with the same message."""
+    d, n = model_dir
+
+    def lines(out):
+        keep = ("Index OK", "  layer ", "MoE layers", "total_tensors")
+        return [ln.split(" bytes=")[0] for ln in out.splitlines() if ln.startswith(keep) or "total_tensors=" in ln]
+
+    ref = subprocess.run([REF_CLI, d, "strict"], capture_output=True, text=True, timeout=120)
+    ours = cli(d, "strict")
+    assert ref.returncode == 0 == ours.returncode, ref.stderr
+    ref_lines = [ln.split("OK (parsed headers). ")[-1] for ln in lines(ref.stdout)]
+    our_lines = [ln.split("OK (parsed headers). ")[-1] for ln in lines(ours.stdout)]
+    assert ref_lines == our_lines, (ref_lines, our_lines)
+    tensors = [t for t in tiny_tensors(extras=False) if t[0] != "model.layers.2.mlp.experts.15.down_proj.weight"]
+    write_model_dir(str(tmp_path), hf_config(TINY), tensors, n_shards=1)
+    ref = subprocess.run([REF_CLI, str(tmp_path), "verify"], capture_output=True, text=True, timeout=120)
+    ours = cli(str(tmp_path), "verify")
+    assert ref.returncode == 1 == ours.returncode
+    msg = "missing tensor in index: model.layers.2.mlp.experts.15.down_proj.weight"
+    assert msg in ref.stderr and msg in ours.stderr
