@@ -97,3 +97,20 @@ def test_strict_matches_the_reference_command_line(model_dir, tmp_path):
     assert ref.returncode == 1 == ours.returncode
     msg = "missing tensor in index: model.layers.2.mlp.experts.15.down_proj.weight"
     assert msg in ref.stderr and msg in ours.stderr
+
+
+@pytest.mark.skipif(not os.path.exists(REF_CLI), reason="reference command line (oracle/_ref/ds_chat) not built")
+def test_reference_command_line_reads_our_checkpoint_files(model_dir):
+    """The reference's own ds_chat, on the checkpoint directory written by
+    tests/ckpt_files.py, generates the golden continuation of the golden
+    prompt (its CPU backend): the files are what its loader expects."""
+    import numpy as np
+
+    d, _ = model_dir
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "tiny_model.npz"))
+    ids = ",".join(map(str, g["prompt"].tolist()))
+    r = subprocess.run([REF_CLI, d, "generate", "--prompt-ids", ids, "--max-new-tokens", "16", "--backend", "cpu"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    line = next(ln for ln in r.stdout.splitlines() if ln.startswith("Generated ids:"))
+    assert [int(x) for x in line.split(":")[1].split()] == g["generated"][:16].tolist()

@@ -66,3 +66,15 @@ def test_text_prompt_load_and_bench(gpu_ctx, model_dir):
     assert "OK" in cli(d, "load")
     out = cli(d, "bench", "--batch", 4, "--prompt-len", 64, "--steps", 4)
     assert re.search(r"Decode: 4 steps of 4 sequences .* tokens/s", out), out
+
+
+def test_generate_prints_the_reference_continuation(gpu_ctx, model_dir):
+    """The same command as the reference's ds_chat on the same checkpoint
+    directory: the golden prompt's first 16 generated ids, which the
+    reference's own CLI prints too (tests/test_cli.py)."""
+    import numpy as np
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "tiny_model.npz"))
+    out = cli(model_dir, "generate", "--prompt-ids", ",".join(map(str, g["prompt"].tolist())), "--max-new-tokens", 16)
+    got = [int(x) for x in re.search(r"Generated ids:([ 0-9]*)", out).group(1).split()]
+    assert got == g["generated"][:16].tolist(), got
