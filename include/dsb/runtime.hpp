@@ -10,6 +10,7 @@
 //   generate(model, session, prompt, GenerationConfig, tokenizer, pieces)
 //   ModelExecutor: prefill / decode_next / generate / reset / position
 //   Tokenizer::load_from_file / encode / decode / metadata
+// plus BatchSession, the batched session the reference does not have.
 // Differences: the backend is always the B200 path (RunConfig carries a CUDA
 // device instead of a BackendKind), and failures throw dsb::rt::Error (a
 // std::runtime_error carrying the DSB_E* code) where the reference throws
@@ -149,6 +150,7 @@ struct ModelState {
 
 class Model;
 class ModelSession;
+class BatchSession;
 inline std::vector<std::int32_t> generate(const Model& model, ModelSession& session,
                                           const std::vector<std::int32_t>& prompt_ids, const GenerationConfig& gen_cfg,
                                           const Tokenizer* tokenizer = nullptr,
@@ -249,6 +251,7 @@ class Model {
  private:
   friend std::vector<std::int32_t> generate(const Model&, ModelSession&, const std::vector<std::int32_t>&,
                                             const GenerationConfig&, const Tokenizer*, std::vector<std::string>*);
+  friend class BatchSession;
   Model() = default;
   std::shared_ptr<detail::ModelState> st_;
   ModelInfo info_;
@@ -306,6 +309,78 @@ inline std::vector<std::int32_t> generate(const Model& model, ModelSession& sess
   }
   return generated;
 }
+
+// The batched session the reference lacks: one paged cache shared by up to
+// max_seqs sequences, stepped together (dsb_decode_step / dsb_prefill /
+// dsb_generate).  Sequence ids come from add() and return through release().
+class BatchSession {
+ public:
+  BatchSession(std::shared_ptr<const Model> model, int max_seqs, std::size_t max_seq)
+      : model_(std::move(model)), st_(model_->st_) {
+    if (max_seqs <= 0 || max_seq == 0 || max_seq > (std::size_t)std::max(1, model_->info().max_position_embeddings))
+      throw Error(DSB_EINVAL, "BatchSession: bad sizes");
+    const int64_t pages = (int64_t)((max_seq + 63) / 64);
+    st_->check(dsb_kvcache_create(st_->ctx, st_->model, pages * max_seqs, max_seqs, (int)pages, &kv_),
+               "dsb_kvcache_create");
+  }
+  ~BatchSession() {
+    if (kv_) dsb_kvcache_destroy(kv_);
+  }
+  BatchSession(const BatchSession&) = delete;
+  BatchSession& operator=(const BatchSession&) = delete;
+
+  int add() {
+    int seq = -1;
+    st_->check(dsb_kvcache_alloc_seq(kv_, &seq), "dsb_kvcache_alloc_seq");
+    return seq;
+  }
+  void release(int seq) { st_->check(dsb_kvcache_free_seq(kv_, seq), "dsb_kvcache_free_seq"); }
+  std::size_t position(int seq) const {
+    int len = 0;
+    st_->check(dsb_kvcache_seq_len(kv_, seq, &len), "dsb_kvcache_seq_len");
+    return (std::size_t)len;
+  }
+
+  // One token for each of the given (distinct) sequences; their greedy ids.
+  std::vector<std::int32_t> step(const std::vector<int>& seqs, const std::vector<std::int32_t>& tokens) {
+    if (seqs.size() != tokens.size() || seqs.empty()) throw Error(DSB_EINVAL, "BatchSession::step: bad arguments");
+    std::vector<std::int32_t> next(seqs.size());
+    st_->check(dsb_decode_step(st_->ctx, st_->model, kv_, seqs.data(), tokens.data(), (int)seqs.size(), nullptr,
+                               next.data()),
+               "dsb_decode_step");
+    return next;
+  }
+
+  // ds::rt::generate for every sequence at once: prompts[i] continues
+  // sequence seqs[i]; the generated ids per sequence (stopping at eos_id
+  // when >= 0).
+  std::vector<std::vector<std::int32_t>> generate(const std::vector<int>& seqs,
+                                                  const std::vector<std::vector<std::int32_t>>& prompts,
+                                                  const GenerationConfig& gen_cfg, std::int32_t eos_id = -1) {
+    if (seqs.size() != prompts.size() || seqs.empty()) throw Error(DSB_EINVAL, "BatchSession::generate: bad arguments");
+    const int B = (int)seqs.size(), n = std::max(0, gen_cfg.max_new_tokens);
+    std::vector<std::int32_t> flat, offsets(1, 0);
+    for (const auto& p : prompts) {
+      flat.insert(flat.end(), p.begin(), p.end());
+      offsets.push_back((std::int32_t)flat.size());
+    }
+    std::vector<std::int32_t> out((std::size_t)B * (std::size_t)std::max(1, n)), counts((std::size_t)B);
+    const dsb_sampling smp{gen_cfg.temperature, gen_cfg.top_k, gen_cfg.top_p, gen_cfg.seed};
+    st_->check(dsb_generate_sampled(st_->ctx, st_->model, kv_, seqs.data(), B, flat.data(), offsets.data(), n, eos_id,
+                                    &smp, out.data(), counts.data()),
+               "dsb_generate_sampled");
+    std::vector<std::vector<std::int32_t>> res((std::size_t)B);
+    for (int b = 0; b < B; ++b)
+      res[(std::size_t)b].assign(out.begin() + (std::ptrdiff_t)b * std::max(1, n),
+                                 out.begin() + (std::ptrdiff_t)b * std::max(1, n) + counts[(std::size_t)b]);
+    return res;
+  }
+
+ private:
+  std::shared_ptr<const Model> model_;
+  std::shared_ptr<detail::ModelState> st_;
+  dsb_kvcache* kv_ = nullptr;
+};
 
 // ds::rt::ModelExecutor: one model and one session.
 class ModelExecutor {

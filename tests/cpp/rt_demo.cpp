@@ -2,6 +2,7 @@
 //   rt_demo tok <tokenizer.json> <text>          encode + decode, no GPU
 //   rt_demo load <model_dir>                     load_model (needs a GPU)
 //   rt_demo gen <model_dir> <ids,...> <n> [temperature top_k top_p seed]
+//   rt_demo batch <model_dir> <ids,...> <ids,...> <n>   two prompts together
 // Prints one line per result; exit status 1 with "error <code>: <what>".
 #include <cstdio>
 #include <cstdlib>
@@ -63,7 +64,22 @@ int main(int argc, char** argv) {
       std::printf("steps %d %d %zu\n", first.greedy_token_id, second.greedy_token_id, ex.position());
       return 0;
     }
-    std::fprintf(stderr, "usage: rt_demo tok|load|gen ...\n");
+    if (cmd == "batch" && argc == 6) {
+      // batch <model_dir> <ids,...> <ids,...> <n>: two prompts generated together, greedy
+      auto model = rt::load_model(argv[2]);
+      rt::BatchSession batch(model, 2, 256);
+      const std::vector<int> seqs = {batch.add(), batch.add()};
+      rt::GenerationConfig g;
+      g.max_new_tokens = std::atoi(argv[5]);
+      const auto out = batch.generate(seqs, {parse_ids(argv[3]), parse_ids(argv[4])}, g);
+      for (const auto& ids : out) {
+        std::printf("ids");
+        for (std::int32_t id : ids) std::printf(" %d", id);
+        std::printf("\n");
+      }
+      return 0;
+    }
+    std::fprintf(stderr, "usage: rt_demo tok|load|gen|batch ...\n");
     return 2;
   } catch (const rt::Error& e) {
     std::fprintf(stderr, "error %d: %s\n", e.code(), e.what());

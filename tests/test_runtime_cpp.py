@@ -1,11 +1,13 @@
 """dsb/runtime.hpp, the reference's ds::rt C++ API (load_model, Model,
-ModelSession, ModelExecutor, generate, Tokenizer) over the C ABI: a C++
+ModelSession, ModelExecutor, generate, Tokenizer, and BatchSession) over
+the C ABI: a C++
 program (tests/cpp/rt_demo.cpp) compiled against the header with warnings
 as errors.  On the CPU: the tokenizer gives the C ABI's ids and text, and
 load_model without a GPU throws dsb::rt::Error with its message.  On the GPU:
 ModelExecutor::generate on the golden prompt prints the reference's
-continuation, prefill / decode_next agree with it, and sampled generation
-prints the ids of dsb_generate_sampled for the same seed."""
+continuation, prefill / decode_next agree with it, sampled generation
+prints the ids of dsb_generate_sampled for the same seed, and a BatchSession
+generates two prompts together as the Python batched generate does."""
 
 import os
 import subprocess
@@ -82,3 +84,19 @@ def test_executor_generates_the_reference_continuation(gpu_ctx, demo, model_dir)
     kv.close()
     m.close()
     assert got == want
+
+
+@pytest.mark.gpu
+def test_batch_session_matches_the_python_batched_generate(gpu_ctx, demo, model_dir):
+    g = np.load(GOLD)
+    p0, p1 = g["prompt"].tolist(), [5, 99, 1024, 7, 3000]
+    r = run(demo, "batch", model_dir, ",".join(map(str, p0)), ",".join(map(str, p1)), 10)
+    assert r.returncode == 0, r.stderr
+    got = [[int(x) for x in ln.split()[1:]] for ln in r.stdout.splitlines()]
+    assert got[0] == g["generated"][:10].tolist()
+    m = dsb.load_model(gpu_ctx, model_dir)
+    kv = dsb.KVCache(gpu_ctx, m, n_blocks=8, max_seqs=2, max_blocks_per_seq=4)
+    seqs = [kv.alloc_seq(), kv.alloc_seq()]
+    assert got == dsb.generate(gpu_ctx, m, kv, seqs, [p0, p1], 10)
+    kv.close()
+    m.close()
