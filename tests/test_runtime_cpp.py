@@ -6,7 +6,8 @@ as errors.  On the CPU: the tokenizer gives the C ABI's ids and text, and
 load_model without a GPU throws dsb::rt::Error with its message.  On the GPU:
 ModelExecutor::generate on the golden prompt prints the reference's
 continuation, prefill / decode_next agree with it, sampled generation
-prints the ids of dsb_generate_sampled for the same seed, and a BatchSession
+prints the ids of the same calls replayed from Python with the reference
+Sampler's draws for the seed, and a BatchSession
 generates two prompts together as the Python batched generate does."""
 
 import os
@@ -73,14 +74,26 @@ def test_executor_generates_the_reference_continuation(gpu_ctx, demo, model_dir)
     assert int(lines["position"]) == len(prompt) + 15  # the last generated id is not fed back
     first, second, pos = (int(x) for x in lines["steps"].split())
     assert (first, second, pos) == (int(g["generated"][0]), int(g["generated"][1]), len(prompt) + 1)
-    # sampled: the ids of dsb_generate_sampled with the same seed (one sequence)
+    # sampled: the same calls replayed from Python (prefill of all but the last
+    # prompt token, then sampled steps) with the reference Sampler's own
+    # uniforms for seed 5 (std::mt19937(5)), as dsb::rt::generate draws them
     r = run(demo, "gen", model_dir, ",".join(map(str, prompt)), 12, 1.2, 40, 0.9, 5)
     assert r.returncode == 0, r.stderr
     got = [int(x) for x in r.stdout.splitlines()[0].split()[1:]]
+    import oracle as O
+
+    u = np.zeros(12, np.float32)
+    O.ref().ref_sampler_uniforms(5, 12, O.p(u, O.f32p))
+    cfg = dsb.Sampling(1.2, 40, 0.9, 5)
     m = dsb.load_model(gpu_ctx, model_dir)
     kv = dsb.KVCache(gpu_ctx, m, n_blocks=8, max_seqs=1, max_blocks_per_seq=4)
     s = kv.alloc_seq()
-    want = dsb.generate(gpu_ctx, m, kv, [s], [prompt], 12, sampling=dsb.Sampling(1.2, 40, 0.9, 5))[0]
+    dsb.prefill(gpu_ctx, m, kv, [s] * (len(prompt) - 1), prompt[:-1])
+    tok, want = prompt[-1], []
+    for j in range(12):
+        ids, _ = dsb.decode_step_sampled(gpu_ctx, m, kv, [s], [tok], cfg, [float(u[j])])
+        want.append(int(ids[0]))
+        tok = want[-1]
     kv.close()
     m.close()
     assert got == want
