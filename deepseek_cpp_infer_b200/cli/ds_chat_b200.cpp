@@ -370,6 +370,14 @@ int main_impl(int argc, char** argv) {
 }  // namespace
 
 int main(int argc, char** argv) {
+  if (argc == 2 && (std::string(argv[1]) == "-h" || std::string(argv[1]) == "--help")) {
+    try {
+      usage();
+    } catch (const std::exception& e) {
+      std::printf("%s\n", e.what());
+    }
+    return 0;
+  }
   try {
     return main_impl(argc, argv);
   } catch (const std::exception& e) {

@@ -53,6 +53,11 @@ def test_verify_names_a_missing_tensor(tmp_path):
     assert r.returncode == 1 and "missing tensor in index: model.layers.2.mlp.experts.15.down_proj.weight" in r.stderr
 
 
+def test_help():
+    r = cli("--help")
+    assert r.returncode == 0 and r.stdout.startswith("usage: ds_chat_b200") and "generate" in r.stdout
+
+
 def test_failures_are_fatal_with_a_message(model_dir, tmp_path):
     d, _ = model_dir
     cases = [
