@@ -10,6 +10,8 @@
 #include <cstring>
 #include <mutex>
 
+#include <new>
+
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
 
@@ -149,7 +151,8 @@ int dsb_ctx_create(int device, dsb_ctx** out) {
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
   if (major != 10 || minor != 0) return DSB_EUNSUPPORTED;  // kernels are built for sm_100a only
-  auto* ctx = new dsb_ctx();
+  auto* ctx = new (std::nothrow) dsb_ctx();
+  if (ctx == nullptr) return DSB_ENOMEM;
   ctx->device = device;
   cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {

@@ -302,7 +302,7 @@ int dsb::ep_params(const dsb_ep* ep, int* rank, int* world, int* n_experts, int*
   return DSB_OK;
 }
 
-extern "C" int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, int hidden, int top_k,
+static int ep_create_impl(dsb_ctx* ctx, int rank, int world, int n_experts, int hidden, int top_k,
                              int max_tokens, dsb_ep** out) {
   if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
   *out = nullptr;
@@ -433,4 +433,10 @@ int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float*
   }
   ctx->stats.kernel_launches += 2;
   return DSB_OK;
+}
+
+extern "C" int dsb_ep_create(dsb_ctx* ctx, int rank, int world, int n_experts, int hidden, int top_k,
+                             int max_tokens, dsb_ep** out) {
+  return dsb::guarded(ctx, "dsb_ep_create",
+                      [&] { return ep_create_impl(ctx, rank, world, n_experts, hidden, top_k, max_tokens, out); });
 }

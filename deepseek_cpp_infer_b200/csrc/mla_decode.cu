@@ -672,7 +672,7 @@ int launch_mla(dsb_ctx* ctx, const dsb_mla_plan* plan, const void* q_lat, const 
 }  // namespace
 }  // namespace dsb
 
-extern "C" int dsb_mla_plan_create(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P,
+static int mla_plan_create_impl(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P,
                                    int block_size, dsb_mla_plan** out) {
   using namespace dsb;
   if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
@@ -796,7 +796,7 @@ int mla_plan_into_aux(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R
 
 }  // namespace dsb
 
-extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
+static int mla_decode_impl(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
                               int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
                               const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
                               void* out_lat) {
@@ -930,7 +930,7 @@ int noalloc_launch(cudaStream_t stream, uint8_t* scratch, const std::vector<MlaI
 }  // namespace
 }  // namespace dsb
 
-extern "C" int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
+static int mla_decode_noalloc_impl(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
                                       int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
                                       const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
                                       void* out_lat) {
@@ -983,4 +983,32 @@ extern "C" int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const voi
                                       max_blocks, H, softmax_scale, out_lat);
   return noalloc_launch<128, 32, 1>(s, d->scratch, items, combines, q_lat, q_rope, kv_cache, n_blocks, block_table,
                                     max_blocks, H, softmax_scale, out_lat);
+}
+
+// The C entry points: no C++ exception (a host allocation of the work list)
+// crosses the ABI.
+extern "C" int dsb_mla_plan_create(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R, int P,
+                                   int block_size, dsb_mla_plan** out) {
+  return dsb::guarded(ctx, "dsb_mla_plan_create",
+                      [&] { return mla_plan_create_impl(ctx, seq_lens, B, H, R, P, block_size, out); });
+}
+
+extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, const void* kv_cache,
+                              int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                              const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                              void* out_lat) {
+  return dsb::guarded(ctx, "dsb_mla_decode", [&] {
+    return mla_decode_impl(ctx, q_lat, q_rope, kv_cache, n_blocks, block_size, block_table, max_blocks, seq_lens, B,
+                           H, R, P, softmax_scale, out_lat);
+  });
+}
+
+extern "C" int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
+                                      int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
+                                      const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
+                                      void* out_lat) {
+  return dsb::guarded(nullptr, "dsb_mla_decode_noalloc", [&] {
+    return mla_decode_noalloc_impl(stream, q_lat, q_rope, kv_cache, n_blocks, block_size, block_table, max_blocks,
+                                   seq_lens, B, H, R, P, softmax_scale, out_lat);
+  });
 }
