@@ -119,3 +119,21 @@ def test_reference_command_line_reads_our_checkpoint_files(model_dir):
     assert r.returncode == 0, r.stderr
     line = next(ln for ln in r.stdout.splitlines() if ln.startswith("Generated ids:"))
     assert [int(x) for x in line.split(":")[1].split()] == g["generated"][:16].tolist()
+
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+_words = st.sampled_from(["info", "verify", "strict", "run", "generate", "bench", "load", "--prompt", "--prompt-ids",
+                          "--max-new-tokens", "--top-k", "--top-p", "--temperature", "--seed", "--max-seq", "1",
+                          "-3", "x", "", "1,2,3", "0.5", "--device", "99"])
+
+
+@settings(max_examples=40, deadline=None, derandomize=True)
+@given(args=st.lists(_words, max_size=6))
+def test_random_arguments_never_crash(model_dir, args):
+    """Any argument list ends with status 0 or 1 (fatal message), never a signal."""
+    d, _ = model_dir
+    r = subprocess.run([CLI, d, *args], capture_output=True, text=True, timeout=120)
+    assert r.returncode in (0, 1), (args, r.returncode, r.stderr[-200:])
+    if r.returncode == 1:
+        assert r.stderr.startswith("fatal: ")

@@ -58,3 +58,31 @@ def test_unfiltered_top_k_one_and_tiny_top_p_are_greedy():
     for r in (0.0, 0.3, 0.999999):
         assert O.sample(x, 1.0, 1, 0.0, r)[0] == 17
         assert O.sample(x, 1.0, 0, 1e-6, r)[0] == 17
+
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=60, deadline=None, derandomize=True)
+@given(seed=st.integers(0, 10**6), V=st.integers(2, 300), k=st.integers(0, 320), top_p=st.floats(0.0, 1.0),
+       t=st.one_of(st.just(0.0), st.just(-1.0), st.floats(0.05, 3.0)), u1=st.floats(0.0, 0.999),
+       u2=st.floats(0.0, 0.999))
+def test_oracle_properties(seed, V, k, top_p, t, u1, u2):
+    """orc_sample: the pick lies in the top-k set; with u growing the pick
+    never moves earlier in the scan order (descending x, ties to the lower
+    id, when a cut is active; id order otherwise); top_k = 1 is the argmax."""
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(V) * 2).astype(np.float32)
+    if rng.random() < 0.3:
+        x = np.round(x).astype(np.float32)  # ties
+    lo, hi = sorted((u1, u2))
+    a, b = O.sample(x, t, k, top_p, lo)[0], O.sample(x, t, k, top_p, hi)[0]
+    p32 = np.float32(top_p)  # the arguments travel as float32
+    filt = (0 < k < V) or (0.0 < p32 < 1.0)
+    t32 = np.float32(t)
+    xs = x / (np.float32(1.0) if t32 <= 0 else t32)
+    order = list(np.lexsort((np.arange(V), -xs))) if filt else list(range(V))
+    assert order.index(a) <= order.index(b)
+    if 0 < k < V:
+        assert a in order[:k] and b in order[:k]
+    assert O.sample(x, t, 1, top_p, hi)[0] == int(np.argmax(xs))
