@@ -208,6 +208,10 @@ _PROTOS = [
     ("dsb_prefill", ctypes.c_int, [_vp, _vp, _vp, _c_i32p, _c_i32p, _ci, _vp, _c_i32p, ctypes.POINTER(ctypes.c_int)]),
     ("dsb_mla_decode_noalloc", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _i64, _ci, _vp, _ci, _c_i32p, _ci, _ci, _ci, _ci, _cf, _vp]),
+    ("dsb_mla_noalloc_status", ctypes.c_int, [_vp]),
+    ("dsb_ctx_set_wait_limit", ctypes.c_int, [_vp, ctypes.c_uint64]),
+    ("dsb_ep_window_ptr", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsb_ep_connect_local", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     (
         "dsb_mla_decode",
         ctypes.c_int,
@@ -291,6 +295,10 @@ class Context:
 
     def sync(self):
         self._check(self._l.dsb_sync(self.h))
+
+    def set_wait_limit(self, limit_ns: int):
+        """Bound of the expert-parallel flag waits launched from now on (dsb_ctx_set_wait_limit)."""
+        self._check(self._l.dsb_ctx_set_wait_limit(self.h, int(limit_ns)))
 
     def stats(self) -> dict:
         s = Stats()
@@ -449,6 +457,11 @@ def mla_decode_noalloc(stream_handle, q_lat, q_rope, kv_cache, block_table, seq_
     return lib().dsb_mla_decode_noalloc(
         stream_handle or None, _ptr(q_lat), _ptr(q_rope), _ptr(kv_cache), kv_cache.shape[0], block_size,
         _ptr(block_table), block_table.shape[1], lens, B, H, R, P, float(softmax_scale), _ptr(out))
+
+
+def mla_noalloc_status(stream_handle) -> int:
+    """dsb_mla_noalloc_status: waits for the stream, returns the last allocation-free call's status code."""
+    return lib().dsb_mla_noalloc_status(stream_handle or None)
 
 
 class MlaPlan:
@@ -692,6 +705,16 @@ class EP:
         blob = b"".join(handles)
         assert len(blob) == self.world * self.HANDLE_BYTES
         self.ctx._check(self._l.dsb_ep_connect(self.h, ctypes.create_string_buffer(blob, len(blob))))
+
+    def window_ptr(self) -> int:
+        p = ctypes.c_void_p()
+        self.ctx._check(self._l.dsb_ep_window_ptr(self.h, ctypes.byref(p)))
+        return p.value
+
+    def connect_local(self, windows):
+        """Connect with every rank's window device pointer (ranks driven from this process)."""
+        arr = (ctypes.c_void_p * self.world)(*[int(w) if w else None for w in windows])
+        self.ctx._check(self._l.dsb_ep_connect_local(self.h, arr))
 
     def dispatch(self, x, ids):
         """x bf16 [T, hidden], ids int32 [T, top_k] -> (recv_x, recv_offsets) torch views of the group's buffers."""

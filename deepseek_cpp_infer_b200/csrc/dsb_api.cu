@@ -225,6 +225,15 @@ int dsb_sync(dsb_ctx* ctx) {
   return DSB_OK;
 }
 
+int dsb_ctx_set_wait_limit(dsb_ctx* ctx, uint64_t limit_ns) {
+  if (ctx == nullptr) return DSB_EINVAL;
+  if (limit_ns < 1000000ull || limit_ns > 60000000000ull)
+    return dsb::fail(ctx, DSB_EINVAL, "dsb_ctx_set_wait_limit: %llu ns outside [1 ms, 60 s]",
+                     (unsigned long long)limit_ns);
+  ctx->wait_limit_ns = limit_ns;
+  return DSB_OK;
+}
+
 int dsb_get_stats(const dsb_ctx* ctx, dsb_stats* out) {
   if (ctx == nullptr || out == nullptr) return DSB_EINVAL;
   *out = ctx->stats;

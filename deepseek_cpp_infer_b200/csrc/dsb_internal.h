@@ -19,6 +19,7 @@ struct dsb_ctx {
   bool own_stream = false;
   int sm_count = 0;
   int* d_status = nullptr;  // device status word written by bounded waits
+  uint64_t wait_limit_ns = 2000000000ull;  // bound of the expert-parallel flag waits
   void* ws = nullptr;       // reusable device workspace
   size_t ws_bytes = 0;
   void* aux = nullptr;      // reusable device buffer for per-call plans

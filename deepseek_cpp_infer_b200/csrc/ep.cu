@@ -50,6 +50,7 @@ struct EpPeers {
 struct EpLayout {
   int world, rank, E_local, D, k, T_max, cap;
   size_t off_counts, off_flags, off_meta, off_recv, off_inbox, bytes;
+  uint64_t wait_ns;  // bound of every flag wait (the context's limit at launch)
 };
 
 EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) {
@@ -87,8 +88,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Bounded wait until flags[s] == epoch for every source s (one thread).
-__device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch) {
+// Bounded wait until flags[s] == epoch for every source s (one thread); gives
+// up after limit_ns of %globaltimer.
+__device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch, uint64_t limit_ns) {
   uint64_t t0 = 0;
   for (uint32_t it = 1;; ++it) {
     bool all = true;
@@ -97,7 +99,7 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch) {
     if ((it & 255u) == 0) {
       const uint64_t now = globaltimer_ns();
       if (t0 == 0) t0 = now;
-      else if (now - t0 > kWaitLimitNs) return false;
+      else if (now - t0 > limit_ns) return false;
     }
   }
 }
@@ -152,7 +154,9 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {
-    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 0 * L.world, L.world, epoch) ? 1 : 0;
+    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 0 * L.world, L.world, epoch, L.wait_ns)
+               ? 1
+               : 0;
     if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
   }
   __syncthreads();
@@ -208,15 +212,19 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
 __global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t epoch, int* status) {
   pdl_wait();
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.win[L.rank] + L.off_flags) + phase * L.world;
-  if (!wait_flags(flags, L.world, epoch)) atomicCAS(status, 0, kStatusTimeout);
+  if (!wait_flags(flags, L.world, epoch, L.wait_ns)) atomicCAS(status, 0, kStatusTimeout);
 }
 
 // 4. Expert outputs (fp32 [cap][D], rows in receive order) back to the home
-// ranks' inboxes; the last CTA raises the return flag in every window.
+// ranks' inboxes; the last CTA raises the return flag in every window.  After
+// an earlier wait of this exchange ran out (status set), the receive offsets
+// and meta may be stale: no row is stored, but the flag is still raised so
+// that the peers' waits end with the status they already report.
 __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const int32_t* __restrict__ recv_offsets,
-                                 EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
+                                 EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch,
+                                 const int* __restrict__ status) {
   pdl_wait();
-  const int n_recv = recv_offsets[L.E_local];
+  const int n_recv = *reinterpret_cast<const volatile int*>(status) != 0 ? 0 : recv_offsets[L.E_local];
   const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 4;  // 16-byte vectors of fp32
@@ -249,7 +257,9 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {
-    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 2 * L.world, L.world, epoch) ? 1 : 0;
+    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 2 * L.world, L.world, epoch, L.wait_ns)
+               ? 1
+               : 0;
     if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
   }
   __syncthreads();
@@ -358,6 +368,27 @@ extern "C" int dsb_ep_connect(dsb_ep* ep, const void* handles) {
   return DSB_OK;
 }
 
+extern "C" int dsb_ep_window_ptr(dsb_ep* ep, void** ptr) {
+  if (ep == nullptr || ptr == nullptr) return DSB_EINVAL;
+  *ptr = ep->win;
+  return DSB_OK;
+}
+
+extern "C" int dsb_ep_connect_local(dsb_ep* ep, void* const* windows) {
+  if (ep == nullptr) return DSB_EINVAL;
+  if (windows == nullptr) return fail(ep->ctx, DSB_EINVAL, "dsb_ep_connect_local: null window list");
+  if (ep->connected) return fail(ep->ctx, DSB_EINVAL, "dsb_ep_connect_local: already connected");
+  for (int p = 0; p < ep->L.world; ++p) {
+    if (p == ep->L.rank) continue;
+    if (windows[p] == nullptr || (reinterpret_cast<uintptr_t>(windows[p]) & 255u))
+      return fail(ep->ctx, DSB_EINVAL, "dsb_ep_connect_local: window %d null or not 256-byte aligned", p);
+  }
+  for (int p = 0; p < ep->L.world; ++p)
+    if (p != ep->L.rank) ep->peers.win[p] = static_cast<uint8_t*>(windows[p]);
+  ep->connected = true;
+  return DSB_OK;
+}
+
 extern "C" int dsb_ep_destroy(dsb_ep* ep) {
   if (ep == nullptr) return DSB_OK;
   cudaStreamSynchronize(ep->ctx->stream);
@@ -387,6 +418,7 @@ extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, co
   if (x == nullptr || ids == nullptr || T < 0 || T > ep->L.T_max || ldx < ep->L.D || (ldx % 8) ||
       (reinterpret_cast<uintptr_t>(x) & 15u))
     return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
+  ep->L.wait_ns = ctx->wait_limit_ns;
   const uint32_t epoch = ++ep->epoch * 2 - 1;  // odd: dispatch, even: the return of the same call
   const int n = T * ep->L.k;
   launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, n, ep->E, ep->L, ep->peers, ep->d_slot, epoch, ctx->d_status);
@@ -417,9 +449,10 @@ int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float*
       (ldy % 4) || (reinterpret_cast<uintptr_t>(y) & 15u) || n_shared < 0 || (n_shared > 0 && shared == nullptr))
     return fail(ctx, DSB_EINVAL, "dsb_ep_combine: bad arguments");
   if (ep->epoch == 0) return fail(ctx, DSB_EINVAL, "dsb_ep_combine: no dispatch to return");
+  ep->L.wait_ns = ctx->wait_limit_ns;
   const uint32_t epoch = ep->epoch * 2;
   launch_pdl(ep_return_kernel, ctx->sm_count, 256, 0, ctx->stream, y, ldy, ep->d_recv_off, ep->L, ep->peers,
-                                                           ep->d_ticket + 1, epoch);
+             ep->d_ticket + 1, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   if (T > 0) {
     launch_pdl(ep_combine_kernel, T, combine_threads(ep->L.D), 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, w_next,

@@ -754,6 +754,9 @@ extern "C" int dsb_mla_decode_planned(dsb_ctx* ctx, const dsb_mla_plan* plan, co
   if ((reinterpret_cast<uintptr_t>(q_lat) | reinterpret_cast<uintptr_t>(q_rope) |
        reinterpret_cast<uintptr_t>(out_lat) | reinterpret_cast<uintptr_t>(kv_cache)) & 15u)
     return fail(ctx, DSB_EINVAL, "dsb_mla_decode: pointers must be 16-byte aligned");
+  if (plan->device != ctx->device)
+    return fail(ctx, DSB_EINVAL, "dsb_mla_decode: plan made on device %d, context on device %d", plan->device,
+                ctx->device);
   if (plan->R == 512)
     return launch_mla<512, 64, 2>(ctx, plan, q_lat, q_rope, kv_cache, n_blocks, block_table, max_blocks,
                                   softmax_scale, out_lat);
@@ -821,14 +824,13 @@ static int mla_decode_impl(dsb_ctx* ctx, const void* q_lat, const void* q_rope, 
 // ===================================================== allocation-free variant
 //
 // dsb_mla_decode_noalloc serves callers that cannot allocate device memory on
-// the call path: code running while a CUDA graph is being captured (cudaMalloc
-// is not a capturable operation and invalidates the capture), allocators and
-// runtimes that own every byte of device memory themselves and forbid stray
-// cudaMalloc/cudaFree (a cudaFree also synchronises the whole device), and
-// plug-in hosts that hand this library only a stream and their own buffers.
-// Its scratch - the work list, the split-KV partials and the bounded-wait
-// status word - lives in the fixed array below, which every GPU that loads
-// the library holds until the process exits.
+// the call path: allocators and runtimes that own every byte of device memory
+// themselves and forbid stray cudaMalloc/cudaFree (a cudaFree also
+// synchronises the whole device), and plug-in hosts that hand this library
+// only a stream and their own buffers.  Its scratch - the work list, the
+// split-KV partials and the bounded-wait status word - lives in the fixed
+// array below, which every GPU that loads the library holds until the process
+// exits.  dsb_mla_noalloc_status reads the status word back.
 
 namespace dsb {
 namespace {
@@ -1001,6 +1003,29 @@ extern "C" int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rop
     return mla_decode_impl(ctx, q_lat, q_rope, kv_cache, n_blocks, block_size, block_table, max_blocks, seq_lens, B,
                            H, R, P, softmax_scale, out_lat);
   });
+}
+
+// Status of the last dsb_mla_decode_noalloc call enqueued on this device:
+// waits for `stream`, then reads the status word of the fixed scratch (a
+// device-to-host copy of one int into the caller's stack, no allocation).
+static int mla_noalloc_status_impl(void* stream) {
+  using namespace dsb;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DSB_ECUDA;
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_setup(dev, &d);
+  if (rc != DSB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = 0;
+  if (cudaMemcpyAsync(&st, d->scratch, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return DSB_ECUDA;
+  if (st == kStatusOk) return DSB_OK;
+  return st == kStatusBadInput ? DSB_EINVAL : DSB_ETIMEOUT;
+}
+
+extern "C" int dsb_mla_noalloc_status(void* stream) {
+  return dsb::guarded(nullptr, "dsb_mla_noalloc_status", [&] { return mla_noalloc_status_impl(stream); });
 }
 
 extern "C" int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,

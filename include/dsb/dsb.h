@@ -84,6 +84,12 @@ DSB_API const char* dsb_last_error(const dsb_ctx* ctx);
  * DSB_ETIMEOUT if a kernel's bounded wait ran out since the last dsb_sync. */
 DSB_API int dsb_sync(dsb_ctx* ctx);
 
+/* Time limit of the expert-parallel flag waits of kernels launched on this
+ * context from now on (default 2 s, accepted range 1 ms .. 60 s): a wait that
+ * runs out sets the status word (dsb_sync returns DSB_ETIMEOUT) and its kernel
+ * returns.  The reference has no bounded waits: no counterpart. */
+DSB_API int dsb_ctx_set_wait_limit(dsb_ctx* ctx, uint64_t limit_ns);
+
 /* Copy the context counters (replaces stats(), cuda_backend.h:52). */
 DSB_API int dsb_get_stats(const dsb_ctx* ctx, dsb_stats* out);
 DSB_API int dsb_reset_stats(dsb_ctx* ctx); /* replaces reset_stats(), cuda_backend.h:51 */
@@ -136,9 +142,9 @@ DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, 
 /*
  * Allocation-free MLA decode: the same computation as dsb_mla_decode, for
  * callers that cannot allocate device memory while they run this call - a
- * CUDA graph being captured (cudaMalloc cannot be captured and breaks the
- * capture), a host runtime that owns all device memory through its own
- * allocator, or a plug-in that only receives a stream and its buffers.  It
+ * host runtime that owns all device memory through its own allocator and
+ * forbids stray cudaMalloc/cudaFree (a cudaFree also synchronises the whole
+ * device), or a plug-in that only receives a stream and its buffers.  It
  * takes no dsb_ctx (creating one allocates) and calls no cudaMalloc/cudaFree:
  * its scratch (work list, split-KV partials, status word) is one fixed
  * device array of about 6.4 MB inside libdsb.so, held by every GPU that loads
@@ -147,20 +153,27 @@ DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, 
  *  stream  cudaStream_t to enqueue on (NULL = the legacy default stream);
  *          the current CUDA device must be the one that holds the buffers.
  *  other arguments as dsb_mla_decode.
- * Limits: at most 4096 work items and 24 split-KV partials per call (a call
- * that would need more, e.g. more than 24 sequences longer than 16384
- * tokens, returns DSB_ELIMIT and enqueues nothing).
+ * Limits: at most 4096 work items and 24 split-KV partials per call.  When
+ * the usual plan needs more than 24 partials, the call falls back to one
+ * work item per 16384 tokens of each sequence; only sequences longer than
+ * 16384 tokens then split, into ceil(len / 16384) partials each.  A call
+ * whose fallback still needs more than 24 partials (for example 13 sequences
+ * of 17000 tokens, 2 partials each) returns DSB_ELIMIT and enqueues nothing.
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) and sets kernel attributes; make that first call
- * before any stream capture.  Every call reuses the same array, so calls that
- * overlap on the GPU (different streams, or different host threads on one
- * device) race and must be serialised by the caller.  A bounded wait that
- * times out inside the kernel is not reported by this entry point.
+ * (cudaGetSymbolAddress) and sets kernel attributes.  Every call reuses the
+ * same array, so calls that overlap on the GPU (different streams, or
+ * different host threads on one device) race and must be serialised by the
+ * caller.  Each call clears the status word; dsb_mla_noalloc_status reads it.
  */
 DSB_API int dsb_mla_decode_noalloc(void* stream, const void* q_lat, const void* q_rope, const void* kv_cache,
                                    int64_t n_blocks, int block_size, const int32_t* block_table, int max_blocks,
                                    const int32_t* seq_lens, int B, int H, int R, int P, float softmax_scale,
                                    void* out_lat);
+/* Waits for `stream` and returns the status of the last dsb_mla_decode_noalloc
+ * call on the current device: DSB_OK, or DSB_ETIMEOUT when a bounded wait in
+ * its kernel ran out (its output is then not valid).  Allocates nothing.
+ * No counterpart in the reference. */
+DSB_API int dsb_mla_noalloc_status(void* stream);
 
 /*
  * Grouped bf16 linear layer (tcgen05, fp32 accumulation):
@@ -397,6 +410,13 @@ DSB_API int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, const
 DSB_API int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,
                            const float* shared, int n_shared, float* h);
 DSB_API int dsb_ep_destroy(dsb_ep* ep);
+/* Ranks driven from ONE process (one GPU each, peer access enabled by the
+ * caller): connect with the device pointers of every rank's window
+ * (dsb_ep_window_ptr; windows[rank] is ignored) instead of IPC handles.  The
+ * ranks' kernels wait on one another, so two ranks of a group must never be
+ * driven on the same GPU. */
+DSB_API int dsb_ep_window_ptr(dsb_ep* ep, void** ptr);
+DSB_API int dsb_ep_connect_local(dsb_ep* ep, void* const* windows);
 
 /* Greedy ids: first index of the row maximum of logits [B, ld] (argmax_f32,
  * src/core/math.cpp:29-40; the reference downloads the logits and does this

@@ -98,3 +98,51 @@ def test_ep_model_decode_matches_single_gpu(tmp_path, fp8):
     worst = [float(open(tmp_path / f"rank{r}").read()) for r in range(world)]
     print("EP vs single-GPU logits max-rel per rank:", worst)
     assert all(w == 0.0 for w in worst), worst
+
+
+def test_ep_wait_runs_out_and_context_survives(gpu_ctx):
+    """A bounded wait that runs out, on one GPU, with no fault.
+
+    Rank 0 of a 2-rank group is connected to a zeroed window that stands for
+    rank 1, and rank 1 is never driven, so no kernel ever raises its flags.
+    With a 10 ms limit the dispatch's count wait and the combine's return wait
+    give up: dsb_sync reports DSB_ETIMEOUT, the return kernel stores no row
+    (its exchange already failed), and the context keeps working.
+    """
+    import time
+
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+
+    E, D, k, T = 16, 256, 4, 8
+    ep = dsb.EP(gpu_ctx, 0, 2, E, D, k, max_tokens=T)
+    peer = torch.zeros(ep.window_bytes, dtype=torch.uint8, device="cuda")
+    try:
+        ep.connect_local([ep.window_ptr(), peer.data_ptr()])
+        gpu_ctx.set_wait_limit(10_000_000)  # 10 ms
+        g = torch.Generator().manual_seed(7)
+        x = torch.randn(T, D, generator=g).to(torch.bfloat16).cuda()
+        ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32).cuda()
+        w = torch.full((T, k), 0.25, device="cuda")
+        h = torch.zeros(T, D, device="cuda")
+        t0 = time.perf_counter()
+        ep.dispatch(x, ids)
+        y = torch.ones(ep.capacity, D, device="cuda")
+        ep.combine(y, w, h)
+        with pytest.raises(dsb.DsbError) as err:
+            gpu_ctx.sync()
+        elapsed = time.perf_counter() - t0
+        assert err.value.code == dsb.DSB_ETIMEOUT
+        assert elapsed < 1.5, elapsed  # the 10 ms limit ended the waits, not the default 2 s
+        # the combine gave up before adding anything to h
+        assert torch.count_nonzero(h).item() == 0
+        # the context still works: a plain kernel runs and syncs clean
+        logits = torch.randn(3, 1000, device="cuda")
+        out = torch.empty(3, dtype=torch.int32, device="cuda")
+        gpu_ctx.argmax(logits, out)
+        gpu_ctx.sync()
+        assert torch.equal(out.long().cpu(), logits.argmax(dim=1).cpu())
+    finally:
+        gpu_ctx.set_wait_limit(2_000_000_000)
+        ep.close()
