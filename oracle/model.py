@@ -31,6 +31,22 @@ the bf16 activation and quantised per token and 128 columns
 SiLU(gate) * up activation, and every routed and shared expert's input and
 activation; kv_b_proj is dequantised to bf16 once (absorbed attention keeps
 it in bf16), the router and lm_head stay unquantised.
+
+An e4m3 code is 6-12% wide, so a quantiser that sees an input one bf16 step
+away rounds it to another code, and such flips compound over the layers.
+forward_fp8 therefore also stores every activation at the precision a
+batched B200 decode stores it, so that both feed the same bytes to every
+quantiser: the latent cache rows [c | kr] in bf16, the query's nope part and
+rotated rope part in bf16, the absorbed query q_lat = W_UK^T q_nope in bf16,
+the attention probabilities in bf16 relative to a running maximum that is
+only raised when a 64-token tile exceeds it by 2^8 (log2 domain), the
+latent output and the per-head W_UV output in bf16, and the final norm in
+bf16 before the lm_head.  A sequence longer than a work item (runs of whole
+64-token pages planned from the lengths and the number of SMs, as
+_mla_items restates) is attended per item and the items' partial sums are
+merged by their maxima.  The arithmetic is the reference's absorbed MLA
+(mla.cpp:41-119 re-associated); only where values are rounded follows the
+batched kernels.
 """
 
 from __future__ import annotations
@@ -194,11 +210,166 @@ def _silu_mul(g, u):
     return _f32(g / (np.float32(1) + np.exp(-g)) * u)
 
 
-def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq):
+def _bf16(a):
+    """fp32 -> bf16 (round to nearest even) -> fp32, vectorised (finite inputs)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(np.shape(a))
+
+
+def _mla_items(seq_lens, slots):
+    """Work items of the split-KV MLA decode: runs of whole 64-token pages per
+    sequence, (b, first page, pages, end token, split).  A few candidate run
+    lengths are scored by a longest-first list schedule over `slots` (the
+    cost of an item is its pages + 2, + 2 more when its sequence is split);
+    the cheapest wins, at most 256 pages per item."""
+    import heapq
+
+    pages = [(int(L) + 63) // 64 for L in seq_lens]
+    total, maxp = sum(pages), max([1] + pages)
+    caps = {min(maxp, 256)}
+    for k in range(1, 9):
+        c = (total + k * slots - 1) // (k * slots)
+        caps.add(max(2, min(c, 256)))
+    caps = sorted(caps)
+    best_cap, best = caps[-1], 1e300
+    for cap in caps:
+        costs = []
+        for n_p in pages:
+            n = (n_p + cap - 1) // cap
+            for i in range(n):
+                costs.append((i + 1) * n_p // n - i * n_p // n + 2.0 + (2.0 if n > 1 else 0.0))
+        costs.sort(reverse=True)
+        heap = [0.0] * slots
+        span = 0.0
+        for c in costs:
+            t0 = heapq.heappop(heap)
+            heapq.heappush(heap, t0 + c)
+            span = max(span, t0 + c)
+        if span < best - 1e-9:
+            best, best_cap = span, cap
+    items = []
+    for b, n_p in enumerate(pages):
+        n = (n_p + best_cap - 1) // best_cap
+        for i in range(n):
+            p0, p1 = i * n_p // n, (i + 1) * n_p // n
+            items.append((b, p0, p1 - p0, min(int(seq_lens[b]), p1 * 64), n > 1))
+    return items
+
+
+def _attend_item(q_lat, q_rope, c, kr, tok0, tok_end, scale_log2):
+    """One work item of the latent attention for all heads: tokens [tok0,
+    tok_end) of the cache rows c [T, R], kr [T, P] (bf16 values); q_lat
+    [H, R], q_rope [H, P] (bf16 values).  Scores in the log2 domain, a
+    running maximum per head raised only when a 64-token tile exceeds it by
+    8, probabilities rounded to bf16 and summed as rounded.  Returns the
+    unnormalised output O [H, R] (fp32), the maximum m and the sum l [H]."""
+    H = q_lat.shape[0]
+    m = np.full(H, -np.inf, np.float32)
+    l = np.zeros(H, np.float64)
+    O = np.zeros((H, c.shape[1]), np.float64)
+    for t0 in range(tok0, tok_end, 64):
+        t1 = min(t0 + 64, tok_end)
+        s = q_lat.astype(np.float64) @ c[t0:t1].T.astype(np.float64) + \
+            q_rope.astype(np.float64) @ kr[t0:t1].T.astype(np.float64)
+        s = s.astype(np.float32) * np.float32(scale_log2)
+        mt = s.max(axis=1)
+        up = mt > m + np.float32(8.0)
+        factor = np.where(up, np.exp2((m - mt).astype(np.float64)).astype(np.float32), np.float32(1.0))
+        m = np.where(up, mt, m)
+        O *= factor[:, None].astype(np.float64)
+        l *= factor.astype(np.float64)
+        pr = _bf16(np.exp2((s - m[:, None]).astype(np.float64)).astype(np.float32))
+        l += pr.astype(np.float64).sum(axis=1)
+        O += pr.astype(np.float64) @ c[t0:t1].astype(np.float64)
+    return O.astype(np.float32), m, l.astype(np.float32)
+
+
+def _attend_sequence(q_lat, q_rope, c, kr, items, scale_log2):
+    """One sequence's latent attention output [H, R] (bf16 values) over its
+    work items (all items of `items` must belong to it): a whole-sequence item
+    normalises its own sum; split items are merged as
+    sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i."""
+    parts = [(_attend_item(q_lat, q_rope, c, kr, p0 * 64, end, scale_log2), split)
+             for (_, p0, n_p, end, split) in items]
+    if len(parts) == 1 and not parts[0][1]:
+        Ow, _, lw = parts[0][0]
+        return _bf16(Ow * (np.float32(1.0) / lw)[:, None])
+    M = np.max(np.stack([m for (_, m, _), _ in parts]), axis=0)
+    den = np.zeros(q_lat.shape[0], np.float32)
+    acc = np.zeros((q_lat.shape[0], c.shape[1]), np.float32)
+    for (Ow, m, lw), _ in parts:
+        w = np.exp2((m - M).astype(np.float64)).astype(np.float32)
+        den = _f32(den + w * lw)
+        acc = _f32(acc + w[:, None] * Ow)
+    return _bf16(acc * (np.float32(1.0) / den)[:, None])
+
+
+def mla_decode_storage_points(q_lat, q_rope, cache, block_table, seq_lens, scale, slots=148):
+    """Absorbed MLA decode over a paged latent cache (kv_lora_rank 128, one
+    CTA per work item) at the batched kernel's storage points: q_lat [B, H,
+    R], q_rope [B, H, P], cache [n_blocks, 64, R + P] as fp32 arrays of bf16
+    values; the batch is planned into work items as the kernel plans it
+    (_mla_items over `slots`); returns [B, H, R] bf16 values as fp32."""
+    B, H, R = q_lat.shape
+    scale_log2 = np.float32(np.float32(scale) * np.float32(1.4426950408889634))
+    items = _mla_items(seq_lens, slots)
+    out = np.zeros((B, H, R), np.float32)
+    for b in range(B):
+        L = int(seq_lens[b])
+        pages = block_table[b, : (L + 63) // 64]
+        rows = cache[pages].reshape(-1, cache.shape[2])
+        out[b] = _attend_sequence(_f32(q_lat[b]), _f32(q_rope[b]), rows[:, :R], rows[:, R:],
+                                  [it for it in items if it[0] == b], scale_log2)
+    return out
+
+
+def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots):
+    """The attention block of one layer for a teacher-forced sequence, at the
+    batched decode's storage points (see the module docstring).  xq [T, D]:
+    the layer input as the FP8 GEMM sees it; returns the o_proj output [T, D]."""
+    orc = oracle()
+    T = xq.shape[0]
+    H, R, nope, P, v = (c["num_attention_heads"], c["kv_lora_rank"], c["qk_nope_head_dim"], c["qk_rope_head_dim"],
+                        c["v_head_dim"])
+    eps, theta = c["rms_norm_eps"], c["rope_theta"]
+    q = _f32(xq.astype(np.float64) @ Wq.T.astype(np.float64)).reshape(T, H, nope + P)
+    kva = _f32(xq.astype(np.float64) @ Wkva.T.astype(np.float64))
+    cache = np.zeros((T, R), np.float32)
+    kr = np.zeros((T, P), np.float32)
+    q_rope = np.zeros((T, H, P), np.float32)
+    for t in range(T):
+        row = np.zeros(R, np.float32)
+        orc.orc_rmsnorm_f32(p(_f32(kva[t, :R]), f32p), p(w_norm, f32p), R, eps, p(row, f32p))
+        cache[t] = row
+        r = _f32(kva[t, R:]).copy()
+        orc.orc_rope_inplace_f32(p(r, f32p), P, t, theta)
+        kr[t] = r
+        for h in range(H):
+            r = _f32(q[t, h, nope:]).copy()
+            orc.orc_rope_inplace_f32(p(r, f32p), P, t, theta)
+            q_rope[t, h] = r
+    cache, kr, q_rope = _bf16(cache), _bf16(kr), _bf16(q_rope)
+    q_nope = _bf16(q[:, :, :nope])
+    wkvb = Wkvb.reshape(H, nope + v, R)
+    w_uk, w_uv = wkvb[:, :nope, :].astype(np.float64), wkvb[:, nope:, :].astype(np.float64)  # [H, nope, R], [H, v, R]
+    q_lat = _bf16(_f32(np.einsum("thn,hnr->thr", q_nope.astype(np.float64), w_uk)))
+    scale = np.float32(1.0) / np.sqrt(np.float32(nope + P), dtype=np.float32)
+    scale_log2 = np.float32(scale * np.float32(1.4426950408889634))
+    o_lat = np.zeros((T, H, R), np.float32)
+    for t in range(T):
+        # position t decodes with t + 1 cached tokens, planned as a batch of one sequence
+        o_lat[t] = _attend_sequence(q_lat[t], q_rope[t], cache, kr, _mla_items([t + 1], slots), scale_log2)
+    attn = _bf16(_f32(np.einsum("thr,hvr->thv", o_lat.astype(np.float64), w_uv))).reshape(T, H * v)
+    return _f32(_act_fp8(attn).astype(np.float64) @ Wo.T.astype(np.float64))
+
+
+def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148):
     """Logits [T, V] of `seq` for a block-scaled FP8 checkpoint: `tensors`
     holds every tensor (fp32 values), `fp8` maps the FP8 weights' names to
     their dequantised fp32 matrices (e4m3 * scale).  Softmax-greedy routing
-    as forward(); near-tie swaps are not modelled."""
+    as forward(); near-tie swaps are not modelled.  `slots`: the split-KV
+    planner's parallel work slots (the GPU's SM count for kv_lora_rank 128)."""
     if cfg.get("q_lora_rank", 0) or cfg.get("scoring_func", 0) != 0:
         raise NotImplementedError("oracle.model covers q_lora_rank 0 with softmax scoring")
     c = cfg
@@ -207,8 +378,7 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq):
         W[n] = _bf16_round(a) if n.endswith("kv_b_proj.weight") else _f32(a)
     seq = np.asarray(seq, np.int64)
     T = len(seq)
-    D, H, R = c["hidden_size"], c["num_attention_heads"], c["kv_lora_rank"]
-    nope, rope, v = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+    D = c["hidden_size"]
     E, k = c["n_routed_experts"], c["num_experts_per_tok"]
     eps = c["rms_norm_eps"]
     orc = oracle()
@@ -216,20 +386,19 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq):
     for li in range(c["num_hidden_layers"]):
         pre = f"model.layers.{li}."
         xn = _act_fp8(_rmsnorm_rows(h, W[pre + "input_layernorm.weight"], eps))
-        out = np.zeros((T, D), np.float32)
-        rc = orc.orc_mla_layer_seq_fp8act_f32(
-            D, H, nope, rope, v, R, eps, c["rope_theta"],
-            *(p(W[pre + "self_attn." + n + ".weight"], f32p)
-              for n in ("q_proj", "kv_a_proj_with_mqa", "kv_a_layernorm", "kv_b_proj", "o_proj")),
-            p(xn, f32p), T, p(out, f32p))
-        assert rc == 0
+        a = pre + "self_attn."
+        out = _mla_fp8_layer(c, W[a + "q_proj.weight"], W[a + "kv_a_proj_with_mqa.weight"],
+                             W[a + "kv_a_layernorm.weight"], W[a + "kv_b_proj.weight"], W[a + "o_proj.weight"], xn,
+                             slots)
         h = _f32(h + out)
         xn = _rmsnorm_rows(h, W[pre + "post_attention_layernorm.weight"], eps)
         xq = _act_fp8(xn)
 
         def ffn(wg, wu, wd, x):
-            mid = _act_fp8(_silu_mul(x @ wg.T, x @ wu.T))
-            return _f32(mid @ wd.T)
+            g = _f32(x.astype(np.float64) @ wg.T.astype(np.float64))
+            u = _f32(x.astype(np.float64) @ wu.T.astype(np.float64))
+            mid = _act_fp8(_silu_mul(g, u))
+            return _f32(mid.astype(np.float64) @ wd.T.astype(np.float64))
 
         if pre + "mlp.gate.weight" not in W:
             out = ffn(*(W[pre + "mlp." + n + "_proj.weight"] for n in ("gate", "up", "down")), xq)
@@ -255,5 +424,5 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq):
                     acc = _f32(acc + y[0])
                 out[t] = acc
         h = _f32(h + out)
-    hn = _rmsnorm_rows(h, W["model.norm.weight"], eps)
-    return _f32(hn @ W["lm_head.weight"].T)
+    hn = _bf16(_rmsnorm_rows(h, W["model.norm.weight"], eps))
+    return _f32(hn.astype(np.float64) @ W["lm_head.weight"].T.astype(np.float64))

@@ -121,3 +121,77 @@ def test_mla_rejects_unsupported(gpu_ctx):
         gpu_ctx.mla_decode(case.q_lat, case.q_rope, case.cache, case.block_table, [64], case.scale, out,
                            block_size=32)
     assert e.value.code == DSB_EUNSUPPORTED
+
+
+def _oracle_rows_worker(args):
+    """Oracle attention of a few sequences (their pages gathered into a compact cache)."""
+    import oracle as O
+
+    q_lat, q_rope, cache, bt, lens, scale = args
+    return O.mla_decode_paged(q_lat, q_rope, cache, bt, lens, scale)
+
+
+def test_mla_cfg2_all_rows_against_oracle(gpu_ctx):
+    """The benchmark configuration (B=64, H=128, R=512, P=64, ctx U[1024,
+    8192], seed 1) with every one of its 64 rows against
+    orc_mla_decode_paged, the sequences spread over a spawn pool of host
+    processes (each gets only its sequences' pages)."""
+    import multiprocessing as mp
+    import os
+
+    case = mla_case(seed=1)
+    o = run_gpu(gpu_ctx, case).float().cpu().numpy()
+    cache = to_u16(case.cache)
+    ql, qr = to_u16(case.q_lat), to_u16(case.q_rope)
+    workers = max(1, min(32, os.cpu_count() or 1))
+    groups = [list(range(case.B))[i::workers] for i in range(workers)]
+    jobs = []
+    for rows in groups:
+        if not rows:
+            continue
+        pages = [case.block_table_host[b, : (case.seq_lens[b] + 63) // 64] for b in rows]
+        bt = np.zeros((len(rows), max(len(p) for p in pages)), np.int32)
+        k = 0
+        for i, p in enumerate(pages):
+            bt[i, : len(p)] = np.arange(k, k + len(p))
+            k += len(p)
+        jobs.append((ql[rows], qr[rows], cache[np.concatenate(pages)], bt, case.seq_lens[rows], case.scale))
+    with mp.get_context("spawn").Pool(len(jobs)) as pool:
+        refs = pool.map(_oracle_rows_worker, jobs)
+    ref = np.zeros_like(o)
+    for rows, r in zip([g for g in groups if g], refs):
+        ref[rows] = r
+    errs = np.abs(o - ref).max(axis=(1, 2)) / np.abs(ref).max(axis=(1, 2))
+    print("cfg2 per-row max-rel: median %.2e worst %.2e" % (np.median(errs), errs.max()))
+    assert errs.max() <= TOL, errs
+
+
+def test_mla_small_rank_storage_points(gpu_ctx):
+    """kv_lora_rank 128 (one CTA per work item, fp32 scores): the kernel
+    against oracle.model.mla_decode_storage_points, which rounds where the
+    kernel stores (bf16 probabilities relative to the lazily raised running
+    maximum, bf16 output, split items merged by their maxima) and plans the
+    same work items.  Only fp32 summation order and the hardware exp2 differ,
+    so nearly every output value is the same bf16 number."""
+    import torch
+
+    import oracle.model as OM
+
+    slots = torch.cuda.get_device_properties(0).multi_processor_count
+    case = mla_case(H=8, R=128, P=32, lens=[1, 40, 64, 65, 500, 3000, 130, 9000], seed=19, nope=64)
+    plan = gpu_ctx.mla_plan(case.seq_lens, 8, 128, 32)
+    try:
+        info = plan.info()
+    finally:
+        plan.close()
+    items = OM._mla_items(case.seq_lens, slots)
+    assert info["n_items"] == len(items)
+    assert info["n_partial"] == sum(1 for it in items if it[4])
+    out = run_gpu(gpu_ctx, case).float().cpu().numpy()
+    ref = OM.mla_decode_storage_points(case.q_lat.float().cpu().numpy(), case.q_rope.float().cpu().numpy(),
+                                       case.cache.float().cpu().numpy(), case.block_table_host, case.seq_lens,
+                                       case.scale, slots)
+    same = float((out == ref).mean())
+    err = max_rel(out, ref)
+    print(f"storage-point oracle: {same * 100:.3f}% identical bf16 values, max-rel {err:.2e}")
+    assert same >= 0.995 and err <= 1e-2, (same, err)

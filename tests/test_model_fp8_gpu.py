@@ -67,42 +67,48 @@ def test_fp8_weight_without_scale_is_rejected(gpu_ctx):
 def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     """The FP8 checkpoint model against oracle.model.forward_fp8, the
     composed restatement with the same activation quantisation points (bf16
-    activation, e4m3 per token and 128 columns before every FP8 GEMM) and
-    the dequantised weights, over 16 teacher-forced steps.
+    activation, e4m3 per token and 128 columns before every FP8 GEMM), the
+    dequantised weights, and every activation stored where the batched
+    decode stores it (bf16 cache rows, queries, probabilities, latent and
+    per-head outputs; the split-KV plan of the decode), so that both feed
+    the same bytes to every e4m3 quantiser.
 
-    On this random tiny model the FP8 path is chaotic: a relative change of
-    2^-9 (bf16 resolution) in the input embeddings moves the oracle's own
-    logits by ~8% (median max-rel; the fp32 path moves 0.2%), because such a
-    change flips e4m3 roundings (one e4m3 step is 6-12%) and the flips
-    compound over the layers.  The GPU path differs from the oracle by bf16
-    roundings of that size, so the bar is that noise floor, measured here:
-    the GPU's median and worst max-rel against the oracle within 1.5x the
-    oracle's own under the 2^-9 perturbation, greedy ids equal at >= 12 of
-    16 steps (measured: 7.2e-2 / 9.0e-2 against 7.7e-2 / 1.2e-1, 14/16)."""
+    The GPU decodes a 16-token prompt and then generates 32 tokens greedily;
+    the oracle is teacher-forced on the same 48 tokens.  Bar (the stated
+    layer-output tolerance, on the logits): max-rel <= 2e-2 at every one of
+    the 48 positions, and at each of the 32 generation steps the oracle's
+    greedy id equals the token the GPU generated."""
+    import torch
+
     import oracle.model as OM
     from fp8_tiny import FP8_SUFFIXES
 
+    slots = torch.cuda.get_device_properties(0).multi_processor_count
     m8 = build(gpu_ctx, fp8=True)
     t = model_tensors(TINY, seed=0)
     fp8 = {n: quantise(a)[2] for n, a in t.items()
            if n.startswith("model.layers.") and n.endswith(FP8_SUFFIXES) and "mlp.gate." not in n}
-    seq = np.random.default_rng(7).integers(0, TINY["vocab_size"], 16)
+    prompt = [int(x) for x in np.random.default_rng(7).integers(0, TINY["vocab_size"], 16)]
     kv = dsb.KVCache(gpu_ctx, m8, n_blocks=16, max_seqs=1, max_blocks_per_seq=4)
     s = kv.alloc_seq()
-    got = np.stack([dsb.decode_step(gpu_ctx, m8, kv, [s], [int(x)], want_logits=True)[1][0] for x in seq])
+    seq, rows, gen = [], [], []
+    nxt = None
+    for i in range(16 + 32):
+        tok = prompt[i] if i < 16 else nxt
+        seq.append(tok)
+        g, lg = dsb.decode_step(gpu_ctx, m8, kv, [s], [tok], want_logits=True)
+        rows.append(lg[0])
+        nxt = int(g[0])
+        if i >= 15 and len(gen) < 32:
+            gen.append(nxt)
     kv.close()
     m8.close()
-    ref = OM.forward_fp8(TINY, t, fp8, seq)
-    emb = t["model.embed_tokens.weight"].astype(np.float32)
-    noise = np.random.default_rng(1).uniform(-2.0 ** -9, 2.0 ** -9, emb.shape).astype(np.float32)
-    ref_noisy = OM.forward_fp8(TINY, dict(t, **{"model.embed_tokens.weight": emb * (1 + noise)}), fp8, seq)
-
-    def max_rel(a):
-        return np.abs(a - ref).max(1) / np.abs(ref).max(1)
-
-    err, floor = max_rel(got), max_rel(ref_noisy)
-    same = int((got.argmax(1) == ref.argmax(1)).sum())
-    print(f"FP8 model vs FP8 oracle: max-rel median {np.median(err):.3e} worst {err.max():.3e}, greedy {same}/16; "
-          f"oracle under 2^-9 input noise: median {np.median(floor):.3e} worst {floor.max():.3e}")
-    assert np.median(err) <= 1.5 * np.median(floor) and err.max() <= 1.5 * floor.max(), (err, floor)
-    assert same >= 12
+    got = np.stack(rows)
+    ref = OM.forward_fp8(TINY, t, fp8, seq, slots=slots)
+    err = np.abs(got - ref).max(1) / np.abs(ref).max(1)
+    oracle_ids = ref.argmax(1)[15:47]
+    same = int((oracle_ids == np.array(gen[:32])).sum())
+    print(f"FP8 model vs FP8 oracle: logits max-rel median {np.median(err):.3e} worst {err.max():.3e}; "
+          f"greedy {same}/32")
+    assert err.max() <= 2e-2, err
+    assert same == 32, (oracle_ids, gen)

@@ -106,6 +106,73 @@ def test_moe_ffn_fp8_large_batch_rows_and_determinism(gpu_ctx):
     assert float((got - ref).abs().max() / ref.abs().max()) <= TOL
 
 
+def expected_from_device(layer, x, ids, wts, rows):
+    """expected() for a layer made without keep_separate: only the experts
+    the sampled rows pick are copied back, their gate and up codes taken out
+    of the interleaved [2I, D] matrix (row 2f gate f, 2f+1 up f) and their
+    scales out of the per-128-row-tile layout."""
+    E, ns = layer.E, layer.n_shared
+    ids_n, w_n = ids.cpu().numpy()[rows], wts.cpu().numpy()[rows]
+    ids_x = np.concatenate([ids_n, np.tile(E + np.arange(ns, dtype=np.int32), (len(rows), 1))], 1)
+    w_x = np.concatenate([w_n, np.ones((len(rows), ns), np.float32)], 1)
+    used = np.unique(ids_x)
+    remap = {int(e): i for i, e in enumerate(used)}
+    gu = layer.gate_up[used.tolist()].cpu().numpy()
+    gs = layer.gate_up_scale[used.tolist()].cpu().numpy()
+    gate_q, up_q = np.ascontiguousarray(gu[:, 0::2]), np.ascontiguousarray(gu[:, 1::2])
+    gate_s, up_s = np.ascontiguousarray(gs[:, 0::2, 0]), np.ascontiguousarray(gs[:, 0::2, 1])
+    down_q = np.ascontiguousarray(layer.down[used.tolist()].cpu().numpy())
+    down_s = np.ascontiguousarray(layer.down_scale[used.tolist()].cpu().numpy())
+    ids_l = np.vectorize(remap.get)(ids_x).astype(np.int32)
+    return OM.moe_fp8(x.float().cpu().numpy()[rows], ids_l, w_x, gate_q, gate_s, up_q, up_s, down_q, down_s)
+
+
+@pytest.mark.parametrize("T", [128, 4096])
+def test_moe_fp8_cfg3_full_shape(gpu_ctx, T):
+    """The isolated DeepSeek-V3 MoE layer of the benchmark at its own shape:
+    D=7168, 256 routed experts + 1 shared, I=2048, sigmoid + bias router
+    with 8 groups / top-4 groups / top-8, routed scale 2.5, T tokens N(0,1).
+    Router ids bit-exact against the oracle (except at fp32 near-ties of
+    expf, each checked to be one); the layer's expert output within 2e-2 of
+    oracle.model.moe_fp8 on a sample of rows."""
+    import torch
+
+    from test_ops_gpu import sigmoid_route_boundary_ulps
+
+    E, ns, D, I, k, G, TG = 256, 1, 7168, 2048, 8, 8, 4
+    layer = MoeFp8Weights(gpu_ctx, E, ns, D, I, seed=2)
+    x = torch.randn(T, D, generator=torch.Generator(device="cuda").manual_seed(52), device="cuda").to(torch.bfloat16)
+    gen = torch.Generator(device="cuda").manual_seed(53)
+    w_gate = torch.randn(E, D, generator=gen, device="cuda") * 0.02
+    bias = torch.randn(E, generator=gen, device="cuda") * 0.01
+    logits = torch.empty(T, E, device="cuda")
+    gpu_ctx.router_logits(x.float().contiguous(), w_gate, logits)
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.empty(T, k, device="cuda")
+    gpu_ctx.moe_route(logits, ids, wts, k, scoring=dsb.SCORE_SIGMOID, bias=bias, n_group=G, topk_group=TG,
+                      norm_topk=1, routed_scale=2.5)
+    gpu_ctx.sync()
+    lg = np.ascontiguousarray(logits.cpu().numpy())
+    b = np.ascontiguousarray(bias.cpu().numpy())
+    rid = np.zeros((T, k), np.int32)
+    rw = np.zeros((T, k), np.float32)
+    assert O.oracle().orc_route_sigmoid_grouped(O.p(lg, O.f32p), O.p(b, O.f32p), T, E, G, TG, k, 1, 2.5,
+                                                O.p(rid, O.i32p), O.p(rw, O.f32p)) == 0
+    got_ids = ids.cpu().numpy()
+    mism = np.nonzero(np.any(got_ids != rid, axis=1))[0]
+    for t in mism:
+        g_ulps, e_ulps = sigmoid_route_boundary_ulps(lg[t], b, G, TG, k)
+        assert e_ulps <= 4.0 or g_ulps <= 8.0, (t, g_ulps, e_ulps)
+    print(f"T={T}: router rows differing at near-ties: {len(mism)}")
+    out = run(gpu_ctx, layer, x, ids, wts, seed=54)
+    rows = np.array(sorted({0, 1, T // 2, T - 1}))
+    ref = torch.from_numpy(expected_from_device(layer, x, ids, wts, rows)).double().cuda()
+    got = out[torch.from_numpy(rows).cuda()]
+    err = float((got - ref).abs().max() / ref.abs().max())
+    print(f"T={T}: expert output max-rel {err:.3e} on rows {rows.tolist()}")
+    assert err <= TOL
+
+
 def test_moe_ffn_fp8_rejects_bad_sizes(gpu_ctx):
     import torch
 

@@ -134,12 +134,40 @@ def test_route_sigmoid_grouped_ids_bit_exact(gpu_ctx, T):
     O.oracle().orc_route_sigmoid_grouped(O.p(logits, O.f32p), O.p(bias, O.f32p), T, E, G, TG, k, 1, 2.5,
                                          O.p(rid, O.i32p), O.p(rw, O.f32p))
     got = ids.cpu().numpy()
-    # exact except where the fp32 sigmoid scores of CUDA's and the C library's
-    # expf differ in the last place and reorder an exact near-tie
-    mism = np.any(got != rid, axis=1)
-    assert mism.sum() <= max(1, T // 1000), np.nonzero(mism)
-    ok = ~mism
+    # Bit-exact except at exact fp32 ties: CUDA's expf and the C library's
+    # differ by up to 2 ulp, so a row may differ only where a selection
+    # boundary is within that error - the 4th/5th group scores (each a sum
+    # of two biased sigmoids) or the 8th/9th biased sigmoid of the kept groups
+    mism = np.nonzero(np.any(got != rid, axis=1))[0]
+    for t in mism:
+        g_ulps, e_ulps = sigmoid_route_boundary_ulps(logits[t], bias, G, TG, k)
+        print(f"row {t}: group boundary {g_ulps:.1f} ulp, expert boundary {e_ulps:.1f} ulp")
+        # a biased sigmoid carries up to ~4 ulp (expf 2, the add, the division,
+        # the bias), a group score the sum of two of them
+        assert e_ulps <= 4.0 or g_ulps <= 8.0, (t, g_ulps, e_ulps, got[t], rid[t])
+    ok = np.ones(T, bool)
+    ok[mism] = False
     assert np.abs(wts.cpu().numpy()[ok] - rw[ok]).max() <= 2e-6 * 2.5
+
+
+def sigmoid_route_boundary_ulps(x, bias, G, TG, k):
+    """Gaps, in fp32 ulps of the boundary value, at the two decisions of the
+    sigmoid + bias grouped router for one row: the TG-th vs (TG+1)-th group
+    score (sum of the group's two largest biased sigmoids) and the k-th vs
+    (k+1)-th biased sigmoid among the kept groups' experts.  Scores are
+    computed in float64 and rounded to fp32, as an exact sigmoid would give."""
+    s = (1.0 / (1.0 + np.exp(-x.astype(np.float64)))).astype(np.float32)
+    sb = (s + bias).astype(np.float32)
+    E = len(x)
+    grp = sb.reshape(G, E // G)
+    gs = np.sort(np.sort(grp, axis=1)[:, -2:].astype(np.float64).sum(axis=1).astype(np.float32))[::-1]
+    g_gap = float(gs[TG - 1]) - float(gs[TG]) if TG < G else np.inf
+    g_ulps = g_gap / float(np.spacing(np.float32(abs(gs[TG - 1]))))
+    kept = np.argsort(-np.sort(grp, axis=1)[:, -2:].astype(np.float64).sum(axis=1), kind="stable")[:TG]
+    cand = np.sort(np.concatenate([grp[g] for g in kept]))[::-1]
+    e_gap = float(cand[k - 1]) - float(cand[k])
+    e_ulps = e_gap / float(np.spacing(np.float32(abs(cand[k - 1]))))
+    return g_ulps, e_ulps
 
 
 @pytest.mark.parametrize("T,k,E", [(1, 8, 256), (37, 4, 16), (32, 6, 64), (4096, 8, 256)])
