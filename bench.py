@@ -625,6 +625,40 @@ def ep_tiny_parity(ctx, rank, world, steps=6):
         ep.close()
 
 
+def trace_steps(out_dir, rank, step, n, stream):
+    """Per-kernel device times of n decode steps from CUPTI activity records
+    (torch.profiler; unlike an ncu replay it does not serialise the launches,
+    so the expert-parallel kernels that wait on peer ranks run as they do
+    untraced).  Writes <out_dir>/kernels_rank<r>.md: per kernel name its
+    launches, total and mean device time and share of the summed time."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    os.makedirs(out_dir, exist_ok=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        e0.record(stream)
+        for _ in range(n):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    rows = []
+    for ev in prof.key_averages():
+        t = getattr(ev, "device_time_total", None)
+        if t is None:
+            t = getattr(ev, "cuda_time_total", 0.0)
+        if t and ev.count:
+            rows.append((ev.key, ev.count, float(t)))
+    total = sum(r[2] for r in rows) or 1.0
+    rows.sort(key=lambda r: -r[2])
+    with open(os.path.join(out_dir, f"kernels_rank{rank}.md"), "w") as f:
+        f.write(f"rank {rank}: {n} steps, {e0.elapsed_time(e1) / n * 1e3:.1f} us per step (CUDA events, traced)\n\n")
+        f.write("| kernel | launches/step | us/step | mean us | share |\n|---|---|---|---|---|\n")
+        for name, cnt, t in rows:
+            f.write(f"| {name[:90]} | {cnt / n:.1f} | {t / n:.1f} | {t / cnt:.2f} | {100 * t / total:.1f}% |\n")
+
+
 def measure_model(args, cfg, B, P, steps, env):
     """Build the random-init model (expert parallel over the world ranks when
     world > 1), fill every sequence's context, run warm-up steps, then time
@@ -712,6 +746,9 @@ def measure_model(args, cfg, B, P, steps, env):
         barrier()
         ms_e2e = max_over_ranks(timed(steps, want_logits=True))
         ctx.sync()
+        if args.trace:
+            barrier()
+            trace_steps(args.trace, rank, lambda: step(), 3, stream)
     finally:
         if kv is not None:
             kv.close()
@@ -1227,6 +1264,9 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
     ap.add_argument("--layers", type=int, default=0, help="model layers (0 = the configuration's 27)")
+    ap.add_argument("--trace", default="",
+                    help="model workload: also write per-kernel device times of 3 traced steps per rank "
+                         "(CUPTI via torch.profiler) into this directory")
     ap.add_argument("--no-fractions", action="store_true",
                     help="model workload: skip the isolated MLA (cfg2) and FP8 MoE layer (cfg3) fractions")
     ap.add_argument("--target", action="store_true",
