@@ -10,7 +10,7 @@ the host.  On one GPU the prompts go through chunked dsb_prefill (untimed).
 Under torchrun (N > 1) the routed experts are split over the ranks (expert
 parallel, dispatch / combine kernels writing into the peers' memory) and
 attention stays data parallel: every rank decodes its own B sequences
-(weak scaling), prefilling token by token; before that, the tiny model's
+(weak scaling), prefilling in chunks of 512 rows in step; before that, the tiny model's
 expert-parallel logits are checked against the unsplit model ("ep_parity").
 The line also carries the isolated MLA (cfg2) and FP8 MoE layer (cfg3)
 roofline fractions, and at 8 GPUs the DeepSeek-V3 target ("target").
@@ -39,6 +39,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s (box) at 1/2/4/8 B200; MLA/MoE HBM GB/s as % of peak"
 L2_BYTES = 126 * 1024 * 1024
+# rows per expert-parallel prefill pass (bounds the exchange windows: world x rows x k)
+EP_PREFILL_CHUNK = 512
 # ncu summary of the expert gate|up GEMM launch the default roofline line times
 EXPERT_GEMM_PROFILE = "profiles/gemm_bf16_expert_gateup_v2lite.md"
 
@@ -680,8 +682,9 @@ def measure_model(args, cfg, B, P, steps, env):
         if world > 1:
             # expert parallel: rank r owns routed experts [r*E/world, (r+1)*E/world); attention and
             # the shared experts stay data parallel (every rank decodes its own B sequences)
+            # windows sized for the prefill chunks (rows of every rank's chunk may meet at one expert)
             ep = dsb.EP(ctx, rank, world, cfg["n_routed_experts"], cfg["hidden_size"], cfg["num_experts_per_tok"],
-                        max_tokens=B)
+                        max_tokens=B if v3 else max(B, EP_PREFILL_CHUNK))
             handles = [None] * world
             dist.all_gather_object(handles, ep.window_handle())
             ep.connect(handles)
@@ -707,9 +710,10 @@ def measure_model(args, cfg, B, P, steps, env):
             greedy = dsb.prefill_prompts(ctx, model, kv, seqs, [list(p) for p in prompts])
             prefill = "chunked dsb_prefill (<= 4096 rows per pass)"
         else:
-            for i in range(P):  # token-serial prefill (expert-parallel ranks step together)
-                greedy, _ = dsb.decode_step(ctx, model, kv, seqs, prompts[:, i])
-            prefill = "token by token"
+            # expert parallel: every rank prefills its own prompts in chunks of the same row
+            # count, in step (each chunk's MoE layers exchange all its rows' picks)
+            greedy = dsb.prefill_prompts(ctx, model, kv, seqs, [list(p) for p in prompts], chunk=EP_PREFILL_CHUNK)
+            prefill = f"chunked dsb_prefill, expert parallel (<= {EP_PREFILL_CHUNK} rows per pass)"
         prefill_s = time.time() - t0
         nxt = greedy
         logits_host = torch.empty((B, cfg["vocab_size"]), dtype=torch.float32, pin_memory=True).numpy()

@@ -199,6 +199,12 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
               int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
               float routed_scale, int n_extra, void* xn, float* logits, int32_t* ids, float* weights, int permute,
               int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm);
+// dsb_ep_dispatch in two parts, so that local work can run between them:
+// ep_publish sends this rank's pick counts (and starts the call's epoch);
+// ep_send then copies the rows to their owners (after every rank's counts
+// arrived) and waits for the rows sent here.
+int ep_publish(dsb_ep* ep, int T, const int32_t* ids);
+int ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x, int32_t** recv_offsets);
 // dsb_ep_combine with the next RMSNorm fused as in moe_combine.
 int ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
                int n_shared, float* h, const float* w_next, float eps, void* xn_next);

@@ -293,6 +293,7 @@ struct dsb_ep {
   bool connected = false;
   bool opened[dsb::kMaxWorld] = {};
   uint32_t epoch = 0;
+  int published_T = -1;           // tokens of the dispatch whose counts went out last
   int32_t* d_slot = nullptr;      // [T_max * k]
   int32_t* d_recv_off = nullptr;  // [E_local + 1]
   int* d_ticket = nullptr;        // [2]: dispatch, return
@@ -410,30 +411,51 @@ extern "C" int dsb_ep_info(const dsb_ep* ep, int* E_local, int* recv_capacity, u
   return DSB_OK;
 }
 
-extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
-                               int32_t** recv_offsets) {
+int dsb::ep_publish(dsb_ep* ep, int T, const int32_t* ids) {
   if (ep == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = ep->ctx;
   if (!ep->connected && ep->L.world > 1) return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: dsb_ep_connect first");
-  if (x == nullptr || ids == nullptr || T < 0 || T > ep->L.T_max || ldx < ep->L.D || (ldx % 8) ||
-      (reinterpret_cast<uintptr_t>(x) & 15u))
-    return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
+  if (ids == nullptr || T < 0 || T > ep->L.T_max)
+    return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens)");
   ep->L.wait_ns = ctx->wait_limit_ns;
   const uint32_t epoch = ++ep->epoch * 2 - 1;  // odd: dispatch, even: the return of the same call
-  const int n = T * ep->L.k;
-  launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, n, ep->E, ep->L, ep->peers, ep->d_slot, epoch, ctx->d_status);
+  ep->published_T = T;
+  launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, T * ep->L.k, ep->E, ep->L, ep->peers, ep->d_slot, epoch,
+             ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
+  ctx->stats.kernel_launches += 1;
+  return DSB_OK;
+}
+
+int dsb::ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
+                 int32_t** recv_offsets) {
+  if (ep == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = ep->ctx;
+  if (x == nullptr || ids == nullptr || T != ep->published_T || ldx < ep->L.D || (ldx % 8) ||
+      (reinterpret_cast<uintptr_t>(x) & 15u))
+    return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (the published T, 16-byte aligned rows)");
+  const uint32_t epoch = ep->epoch * 2 - 1;
+  const int n = T * ep->L.k;
   const int blocks = std::max(1, std::min(ctx->sm_count, (n + 7) / 8));
-  launch_pdl(ep_dispatch_kernel, blocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, ids, ep->d_slot, n,
-                                                      ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch,
-                                                      ctx->d_status);
+  launch_pdl(ep_dispatch_kernel, blocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, ids,
+             ep->d_slot, n, ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   launch_pdl(ep_wait_kernel, 1, 1, 0, ctx->stream, ep->L, ep->peers, 1, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
-  ctx->stats.kernel_launches += 3;
+  ctx->stats.kernel_launches += 2;
   if (recv_x) *recv_x = ep->win + ep->L.off_recv;
   if (recv_offsets) *recv_offsets = ep->d_recv_off;
   return DSB_OK;
+}
+
+extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
+                               int32_t** recv_offsets) {
+  if (ep == nullptr) return DSB_EINVAL;
+  if (x == nullptr || ldx < ep->L.D || (ldx % 8) || (reinterpret_cast<uintptr_t>(x) & 15u))
+    return fail(ep->ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
+  int rc = dsb::ep_publish(ep, T, ids);
+  if (rc != DSB_OK) return rc;
+  return dsb::ep_send(ep, x, ldx, T, ids, recv_x, recv_offsets);
 }
 
 extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,

@@ -1159,8 +1159,6 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
       if (!(uniforms_host[b] >= 0.0f && uniforms_host[b] <= 1.0f))
         return fail(ctx, DSB_EINVAL, "%s: uniforms[%d] is not in [0, 1]", fn, b);
   }
-  if (prefill && m->ep != nullptr)
-    return fail(ctx, DSB_EUNSUPPORTED, "dsb_prefill: expert-parallel models decode token by token");
   const dsb_model_config& c = m->cfg;
   const int D = c.hidden_size, H = c.num_attention_heads, R = c.kv_lora_rank, P = c.qk_rope_head_dim;
   const int nope = c.qk_nope_head_dim, v = c.v_head_dim, V = c.vocab_size, E = c.n_routed_experts;
@@ -1194,7 +1192,7 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     int rk, wd, Eg, kg, Dg;
     ep_params(m->ep, &rk, &wd, &Eg, &kg, &Dg, &ep_tmax, nullptr);
     ep_cap = wd * ep_tmax * kg;
-    if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "dsb_decode_step: B=%d above the expert group's max_tokens", B);
+    if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "%s: %d rows above the expert group's max_tokens %d", fn, B, ep_tmax);
   }
   // tokens | positions | block table | (expert parallel) shared-expert row
   // sources and offsets | (prefill) the lm_head rows | (sampling) the draws
@@ -1379,29 +1377,20 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
         DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
                            c.norm_topk_prob, c.routed_scaling_factor, ids, wts, 0));
       }
-      void* rx = nullptr;
-      int32_t* roff = nullptr;
-      DSB_STEP(dsb_ep_dispatch(m->ep, xn, D, B, ids, &rx, &roff));
+      // this rank's pick counts go out first; the shared experts on this
+      // rank's tokens run while they travel, then the rows go to their owners
+      DSB_STEP(ep_publish(m->ep, B, ids));
       const int eI = L.e_inter, EL = m->E_own, ns = L.n_shared;
-      if (L.e_gu8 != nullptr) {
-        const int64_t gs = (2 * eI / 128) * 2 * (D / 128), ds = (D / 128) * (eI / 128);  // scales per group
-        DSB_STEP(q8(rx, D, ep_cap, D));
-        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, ep_cap, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL,
-                      roff, B));
-        DSB_STEP(q8(midp, eI, ep_cap, eI));
-        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, ep_cap, D, yperm, D, 1, DSB_EPI_STORE, EL, roff, B));
-        if (ns > 0) {
+      const int64_t gs = (2 * eI / 128) * 2 * (D / 128), ds = (D / 128) * (eI / 128);  // FP8 scales per group
+      if (ns > 0) {
+        if (L.e_gu8 != nullptr) {
           DSB_STEP(q8(xn, D, ns * B, D, d_srows, 1));
           DSB_STEP(lin8(ctx, L.e_gu8 + (size_t)EL * 2 * eI * D, L.e_gu8_s + EL * gs, 2, xq8, sx8, D, ns * B, 2 * eI,
                         midp, eI, 0, DSB_EPI_SILU_GATE, ns, d_soff, B));
           DSB_STEP(q8(midp, eI, ns * B, eI));
           DSB_STEP(lin8(ctx, L.e_down8 + (size_t)EL * D * eI, L.e_down8_s + EL * ds, 1, xq8, sx8, eI, ns * B, D, ys, D,
                         1, DSB_EPI_STORE, ns, d_soff, B));
-        }
-      } else {
-        DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
-        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
-        if (ns > 0) {
+        } else {
           const bf16* s_gu = L.e_gu + (size_t)EL * 2 * eI * D;
           const bf16* s_down = L.e_down + (size_t)EL * D * eI;
           DSB_STEP(gather_rows(ctx, xn, D, d_srows, ns * B, 1, D, xperm));
@@ -1409,6 +1398,19 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
                           B));
           DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
         }
+      }
+      void* rx = nullptr;
+      int32_t* roff = nullptr;
+      DSB_STEP(ep_send(m->ep, xn, D, B, ids, &rx, &roff));
+      if (L.e_gu8 != nullptr) {
+        DSB_STEP(q8(rx, D, ep_cap, D));
+        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, ep_cap, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL,
+                      roff, B));
+        DSB_STEP(q8(midp, eI, ep_cap, eI));
+        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, ep_cap, D, yperm, D, 1, DSB_EPI_STORE, EL, roff, B));
+      } else {
+        DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
+        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
       }
       DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, ys, ns, h, next_norm, c.rms_norm_eps, xn));
       xn_ready = true;

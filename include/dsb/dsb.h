@@ -551,8 +551,10 @@ DSB_API int dsb_decode_step(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, con
  * of first appearance in seq_ids: *n_seq (HOST, may be NULL) of them; their
  * greedy ids go to greedy (HOST int32 [n_seq]) and, when logits is not NULL,
  * their logits to logits (HOST fp32 [n_seq, vocab]).  n_tok <=
- * DSB_PREFILL_MAX_TOKENS.  Not for models bound to an expert-parallel group
- * (DSB_EUNSUPPORTED).  No counterpart in the reference (it prefills token by
+ * DSB_PREFILL_MAX_TOKENS.  A model bound to an expert-parallel group
+ * exchanges every MoE layer's picks of all n_tok rows: every rank calls
+ * dsb_prefill in step (at least one row each, at most the group's
+ * max_tokens).  No counterpart in the reference (it prefills token by
  * token). */
 DSB_API int dsb_prefill(dsb_ctx* ctx, dsb_model* model, dsb_kvcache* kv, const int32_t* seq_ids,
                         const int32_t* tokens, int n_tok, float* logits, int32_t* greedy, int* n_seq);

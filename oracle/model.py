@@ -364,11 +364,13 @@ def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots):
     return _f32(_act_fp8(attn).astype(np.float64) @ Wo.T.astype(np.float64))
 
 
-def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148):
+def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148, swaps=(), margins=None):
     """Logits [T, V] of `seq` for a block-scaled FP8 checkpoint: `tensors`
     holds every tensor (fp32 values), `fp8` maps the FP8 weights' names to
     their dequantised fp32 matrices (e4m3 * scale).  Softmax-greedy routing
-    as forward(); near-tie swaps are not modelled.  `slots`: the split-KV
+    as forward(), with the same router margins (into the dict `margins`,
+    {layer: [T]}, when given) and near-tie `swaps` ((layer, position) pairs
+    whose (k+1)-th expert takes the k-th slot).  `slots`: the split-KV
     planner's parallel work slots (the GPU's SM count for kv_lora_rank 128)."""
     if cfg.get("q_lora_rank", 0) or cfg.get("scoring_func", 0) != 0:
         raise NotImplementedError("oracle.model covers q_lora_rank 0 with softmax scoring")
@@ -381,6 +383,7 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148):
     D = c["hidden_size"]
     E, k = c["n_routed_experts"], c["num_experts_per_tok"]
     eps = c["rms_norm_eps"]
+    swaps = set(swaps)
     orc = oracle()
     h = _f32(W["model.embed_tokens.weight"][seq])
     for li in range(c["num_hidden_layers"]):
@@ -406,14 +409,28 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148):
             wgate = W[pre + "mlp.gate.weight"]
             shared = pre + "mlp.shared_experts.gate_proj.weight" in W
             out = np.zeros((T, D), np.float32)
+            margin = np.zeros(T)
             for t in range(T):
                 logits = np.zeros(E, np.float32)
                 orc.orc_linear_f32(p(wgate, f32p), p(_f32(xn[t]), f32p), D, p(logits, f32p), E)
-                ids = np.zeros(k, np.int32)
-                w = np.zeros(k, np.float32)
-                assert orc.orc_route_softmax_greedy(p(logits, f32p), 1, E, k, int(c["norm_topk_prob"]),
-                                                    float(c["routed_scaling_factor"]), p(ids, i32p),
+                srt = np.sort(logits.astype(np.float64))[::-1]
+                margin[t] = srt[k - 1] - srt[k] if k < E else np.inf
+                kx = k + 1 if k < E else k
+                ids = np.zeros(kx, np.int32)
+                w = np.zeros(kx, np.float32)
+                # top-(k+1) unnormalised, then the swap and the reference's renormalisation
+                assert orc.orc_route_softmax_greedy(p(logits, f32p), 1, E, kx, 0, 1.0, p(ids, i32p),
                                                     p(w, f32p)) == 0
+                if (li, t) in swaps:
+                    ids[k - 1], w[k - 1] = ids[k], w[k]
+                ids, w = np.ascontiguousarray(ids[:k]), _f32(w[:k])
+                if c["norm_topk_prob"]:
+                    s_ = np.float32(0)
+                    for j in range(k):
+                        s_ = np.float32(s_ + w[j])
+                    if s_ > 0:
+                        w = _f32(w / s_)
+                w = _f32(w * np.float32(c["routed_scaling_factor"]))
                 acc = np.zeros(D, np.float32)
                 x = xq[t:t + 1]
                 for e, wt in zip(ids, w):
@@ -423,6 +440,8 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148):
                     y = ffn(*(W[pre + f"mlp.shared_experts.{n}_proj.weight"] for n in ("gate", "up", "down")), x)
                     acc = _f32(acc + y[0])
                 out[t] = acc
+            if margins is not None:
+                margins[li] = margin
         h = _f32(h + out)
     hn = _bf16(_rmsnorm_rows(h, W["model.norm.weight"], eps))
     return _f32(hn.astype(np.float64) @ W["lm_head.weight"].T.astype(np.float64))

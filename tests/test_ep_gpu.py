@@ -29,6 +29,90 @@ def _port():
     return p
 
 
+def _prefill_worker(rank, world, port, out_dir):
+    """Expert-parallel dsb_prefill: each rank prefills its own ragged prompts
+    (a different total on every rank, the same number of chunks) on the EP
+    model and on the unsplit model, then decodes 4 steps on both."""
+    import torch
+    import torch.distributed as dist
+
+    import deepseek_cpp_infer_b200 as dsb
+    from deepseek_cpp_infer_b200.workloads import TINY, model_tensors
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(rank)
+    ctx = dsb.Context(rank)
+    chunk = 24
+    ep = dsb.EP(ctx, rank, world, TINY["n_routed_experts"], TINY["hidden_size"], TINY["num_experts_per_tok"],
+                max_tokens=chunk)
+    handles = [None] * world
+    dist.all_gather_object(handles, ep.window_handle())
+    ep.connect(handles)
+    tensors = model_tensors(TINY, seed=0)
+    models = []
+    for use_ep in (True, False):
+        m = dsb.Model(ctx, dsb.ModelConfig(**TINY))
+        if use_ep:
+            m.set_ep(ep)
+        for name, a in tensors.items():
+            m.set_tensor(name, a)
+        m.finalize()
+        models.append(m)
+    kvs = [dsb.KVCache(ctx, m, n_blocks=16, max_seqs=4, max_blocks_per_seq=2) for m in models]
+    rng = np.random.default_rng(70 + rank)
+    lens = [40 + 7 * rank, 13, 61 - rank]  # ragged, 3 chunks of <= 24 rows on every rank
+    prompts = [rng.integers(0, TINY["vocab_size"], n).tolist() for n in lens]
+    rows = [(s, p[i]) for i in range(max(lens)) for s, p in enumerate(prompts) if i < len(p)]
+    n_chunks = 6
+    per = (len(rows) + n_chunks - 1) // n_chunks
+    assert per <= chunk
+    seqs = [[kv.alloc_seq() for _ in prompts] for kv in kvs]
+    worst, same = 0.0, True
+    for c in range(n_chunks):
+        part = rows[c * per:(c + 1) * per]
+        outs = []
+        for mi in range(2):
+            g, lg = dsb.prefill(ctx, models[mi], kvs[mi], [seqs[mi][r[0]] for r in part], [r[1] for r in part],
+                                want_logits=True)
+            outs.append((g, lg))
+        same &= bool(np.array_equal(outs[0][0], outs[1][0]))
+        worst = max(worst, float(np.abs(outs[0][1] - outs[1][1]).max() / np.abs(outs[1][1]).max()))
+    nxt = [outs[0][0]] * 2
+    for _ in range(4):
+        res = [dsb.decode_step(ctx, models[mi], kvs[mi], seqs[mi], nxt[mi], want_logits=True) for mi in range(2)]
+        same &= bool(np.array_equal(res[0][0], res[1][0]))
+        worst = max(worst, float(np.abs(res[0][1] - res[1][1]).max() / np.abs(res[1][1]).max()))
+        nxt = [res[0][0], res[1][0]]
+    with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+        f.write(f"{worst} {int(same)}\n")
+    dist.barrier()
+    for kv in kvs:
+        kv.close()
+    for m in models:
+        m.close()
+    ep.close()
+    ctx.close()
+    dist.destroy_process_group()
+
+
+def test_ep_prefill_matches_single_gpu(tmp_path):
+    """Chunked prefill on an expert-parallel model against the unsplit model
+    (then 4 decode steps): greedy ids equal, logits within the 2e-2 bar."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("expert parallelism needs at least 2 GPUs")
+    mp.spawn(_prefill_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    res = [open(tmp_path / f"rank{r}").read().split() for r in range(world)]
+    print("EP prefill vs single-GPU prefill (max-rel, greedy equal) per rank:", res)
+    assert all(r[1] == "1" for r in res), res
+    assert all(float(r[0]) <= 2e-2 for r in res), res
+
+
 def _worker(rank, world, port, out_dir, fp8):
     import torch
     import torch.distributed as dist

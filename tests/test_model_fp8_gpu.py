@@ -64,6 +64,12 @@ def test_fp8_weight_without_scale_is_rejected(gpu_ctx):
     m.close()
 
 
+# gate-logit gap (logit units) below which the last routed expert may swap: one
+# activation moved across an e4m3 boundary (6-12% of one element of a K=512
+# GEMM input) moves this model's gate logits by ~1e-3; the bound is 5x that
+NEAR_TIE = 0.005
+
+
 def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     """The FP8 checkpoint model against oracle.model.forward_fp8, the
     composed restatement with the same activation quantisation points (bf16
@@ -77,7 +83,16 @@ def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     the oracle is teacher-forced on the same 48 tokens.  Bar (the stated
     layer-output tolerance, on the logits): max-rel <= 2e-2 at every one of
     the 48 positions, and at each of the 32 generation steps the oracle's
-    greedy id equals the token the GPU generated."""
+    greedy id equals the token the GPU generated.
+
+    Router near-ties, as in the bf16 whole-model test: fp32 summation order
+    can still move one activation across an e4m3 rounding boundary (a 6-12%
+    change of that element), which may swap the last routed expert where
+    the oracle's k-th and (k+1)-th gate logits are closer than NEAR_TIE.
+    Position by position, a position over the bar is checked against the
+    oracle with one more such swap forced (at that position or an earlier
+    one, whose cache rows it reads); every swap taken is printed, and each
+    must be a near-tie."""
     import torch
 
     import oracle.model as OM
@@ -104,11 +119,35 @@ def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     kv.close()
     m8.close()
     got = np.stack(rows)
-    ref = OM.forward_fp8(TINY, t, fp8, seq, slots=slots)
-    err = np.abs(got - ref).max(1) / np.abs(ref).max(1)
+
+    def max_rel(ref):
+        return np.abs(got - ref).max(1) / np.abs(ref).max(1)
+
+    swaps = []
+    margins = {}
+    ref = OM.forward_fp8(TINY, t, fp8, seq, slots=slots, margins=margins)
+    err = max_rel(ref)
+    print(f"FP8 model vs FP8 oracle: logits max-rel per position {np.array2string(err, precision=1)}")
+    for _ in range(6):
+        bad = np.nonzero(err > 2e-2)[0]
+        if len(bad) == 0:
+            break
+        p0 = int(bad[0])
+        cands = sorted((float(m[q]), li, q) for li, m in margins.items() for q in range(p0 + 1) if m[q] < NEAR_TIE)
+        assert cands, f"position {p0}: max-rel {err[p0]:.3e} with no router near-tie at or before it"
+        best = None
+        for gap, li, q in cands[:8]:
+            r2 = OM.forward_fp8(TINY, t, fp8, seq, slots=slots, swaps=swaps + [(li, q)])
+            e2 = max_rel(r2)
+            if best is None or e2[p0] < best[0][p0]:
+                best = (e2, r2, (li, q, gap))
+        err, ref = best[0], best[1]
+        swaps.append(best[2][:2])
+        print(f"near-tie swap at layer {best[2][0]}, position {best[2][1]} (gate gap {best[2][2]:.2e}): "
+              f"position {p0} max-rel {err[p0]:.3e}")
     oracle_ids = ref.argmax(1)[15:47]
     same = int((oracle_ids == np.array(gen[:32])).sum())
     print(f"FP8 model vs FP8 oracle: logits max-rel median {np.median(err):.3e} worst {err.max():.3e}; "
-          f"greedy {same}/32")
+          f"greedy {same}/32; near-tie swaps {swaps}")
     assert err.max() <= 2e-2, err
     assert same == 32, (oracle_ids, gen)
