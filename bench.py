@@ -645,20 +645,33 @@ def trace_steps(out_dir, rank, step, n, stream):
             step()
         e1.record(stream)
         e1.synchronize()
-    rows = []
-    for ev in prof.key_averages():
-        t = getattr(ev, "device_time_total", None)
-        if t is None:
-            t = getattr(ev, "cuda_time_total", 0.0)
-        if t and ev.count:
-            rows.append((ev.key, ev.count, float(t)))
-    total = sum(r[2] for r in rows) or 1.0
-    rows.sort(key=lambda r: -r[2])
+    # device activity records in start order; with one stream the kernels end in
+    # launch order, so end_k - end_(k-1) is how far kernel k moved the stream on
+    # (its own time, less what it overlapped with its predecessor through
+    # programmatic dependent launch); these advances sum to the traced time
+    evs = []
+    for ev in prof.events():
+        if str(getattr(ev, "device_type", "")).endswith("CUDA") and ev.time_range.end > ev.time_range.start:
+            evs.append((ev.time_range.start, ev.time_range.end, ev.name))
+    evs.sort()
+    stats = {}
+    prev_end = None
+    for t0, t1, name in evs:
+        adv = t1 - t0 if prev_end is None else max(0.0, t1 - max(prev_end, t0))
+        prev_end = t1 if prev_end is None else max(prev_end, t1)
+        cnt, dur, a = stats.get(name, (0, 0.0, 0.0))
+        stats[name] = (cnt + 1, dur + (t1 - t0), a + adv)
+    rows = sorted(stats.items(), key=lambda kv: -kv[1][2])
+    total = sum(v[2] for _, v in rows) or 1.0
     with open(os.path.join(out_dir, f"kernels_rank{rank}.md"), "w") as f:
-        f.write(f"rank {rank}: {n} steps, {e0.elapsed_time(e1) / n * 1e3:.1f} us per step (CUDA events, traced)\n\n")
-        f.write("| kernel | launches/step | us/step | mean us | share |\n|---|---|---|---|---|\n")
-        for name, cnt, t in rows:
-            f.write(f"| {name[:90]} | {cnt / n:.1f} | {t / n:.1f} | {t / cnt:.2f} | {100 * t / total:.1f}% |\n")
+        f.write(f"rank {rank}: {n} steps, {e0.elapsed_time(e1) / n * 1e3:.1f} us per step (CUDA events, traced); "
+                f"advance = end of the kernel minus end of the previous one (the stream's progress it accounts "
+                f"for), duration = its own start to end\n\n")
+        f.write("| kernel | launches/step | advance us/step | share | duration us/step | mean duration us |\n"
+                "|---|---|---|---|---|---|\n")
+        for name, (cnt, dur, adv) in rows:
+            f.write(f"| {name[:80]} | {cnt / n:.1f} | {adv / n:.1f} | {100 * adv / total:.1f}% | {dur / n:.1f} | "
+                    f"{dur / cnt:.2f} |\n")
 
 
 def measure_model(args, cfg, B, P, steps, env):
@@ -752,7 +765,10 @@ def measure_model(args, cfg, B, P, steps, env):
         ctx.sync()
         if args.trace:
             barrier()
-            trace_steps(args.trace, rank, lambda: step(), 3, stream)
+            try:
+                trace_steps(args.trace, rank, lambda: step(), 3, stream)
+            except Exception as e:  # noqa: BLE001  diagnostics only; the measured line stands
+                print(f"trace failed: {type(e).__name__}: {e}", file=sys.stderr)
     finally:
         if kv is not None:
             kv.close()

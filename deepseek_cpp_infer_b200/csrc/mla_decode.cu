@@ -543,11 +543,14 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaCombine* __re
 }
 
 // Split each sequence into page runs so that the clusters of one wave finish
-// together.  A handful of candidate run lengths (caps) are scored by a
-// longest-first list schedule over the available cluster slots with cost =
-// pages + a fixed per-item overhead (+ the partial write and merge of split
-// sequences); the cheapest cap wins.
-void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>* items,
+// together.  A handful of candidate run lengths (caps: the longest sequence
+// in 1..16 equal runs, and the even spread of all pages over 1..8 waves) are
+// scored by a longest-first list schedule over the available cluster slots
+// with cost = pages + a fixed per-item overhead (prologue, pipeline fill,
+// epilogue: 2 pages) + for an item of a split sequence the merge: its fp32
+// partial [H, R] written and read back, in pages of the same bytes, plus one
+// page for the merge launch; the cheapest cap wins.
+void plan_items(const int32_t* seq_lens, int B, int slots, int H, int R, int P, std::vector<MlaItem>* items,
                 std::vector<MlaCombine>* combines, int* n_partial) {
   std::vector<int> pages(B);
   int64_t total = 0;
@@ -558,9 +561,10 @@ void plan_items(const int32_t* seq_lens, int B, int slots, std::vector<MlaItem>*
     maxp = std::max(maxp, pages[b]);
   }
   const double overhead = 2.0;  // pages-equivalent cost of an item's setup
-  const double split_cost = 2.0;  // partial write + merge of a split sequence
+  const double split_cost = 1.0 + (double)H * R * 4 * 2 / ((double)kTok * (R + P) * 2);
   std::vector<int> caps;
   caps.push_back(std::min(maxp, kMaxItemPages));
+  for (int n = 2; n <= 16; ++n) caps.push_back(std::max(2, std::min((maxp + n - 1) / n, kMaxItemPages)));
   for (int k = 1; k <= 8; ++k) {
     const int64_t c = (total + (int64_t)k * slots - 1) / ((int64_t)k * slots);
     caps.push_back((int)std::max<int64_t>(2, std::min<int64_t>(c, kMaxItemPages)));
@@ -691,7 +695,7 @@ static int mla_plan_create_impl(dsb_ctx* ctx, const int32_t* seq_lens, int B, in
   std::vector<MlaItem> items;
   std::vector<MlaCombine> combines;
   int n_partial = 0;
-  plan_items(seq_lens, B, std::max(1, ctx->sm_count / nct), &items, &combines, &n_partial);
+  plan_items(seq_lens, B, std::max(1, ctx->sm_count / nct), H, R, P, &items, &combines, &n_partial);
   auto* plan = new dsb_mla_plan();
   plan->B = B;
   plan->H = H;
@@ -774,7 +778,7 @@ int mla_plan_into_aux(dsb_ctx* ctx, const int32_t* seq_lens, int B, int H, int R
   std::vector<MlaItem> items;
   std::vector<MlaCombine> combines;
   int n_partial = 0;
-  plan_items(seq_lens, B, std::max(1, ctx->sm_count / (R == 512 ? 2 : 1)), &items, &combines, &n_partial);
+  plan_items(seq_lens, B, std::max(1, ctx->sm_count / (R == 512 ? 2 : 1)), H, R, P, &items, &combines, &n_partial);
   const size_t off_comb = (items.size() * sizeof(MlaItem) + 255) & ~size_t(255);
   int rc = ensure_aux(ctx, off_comb + std::max<size_t>(1, combines.size()) * sizeof(MlaCombine));
   if (rc != DSB_OK) return rc;
@@ -955,7 +959,7 @@ static int mla_decode_noalloc_impl(void* stream, const void* q_lat, const void* 
   std::vector<MlaItem> items;
   std::vector<MlaCombine> combines;
   int n_partial = 0;
-  plan_items(seq_lens, B, slots, &items, &combines, &n_partial);
+  plan_items(seq_lens, B, slots, H, R, P, &items, &combines, &n_partial);
   if (n_partial > kNoAllocMaxPartials) {
     // too many splits for the fixed scratch: one item per sequence where the
     // 16384-token item limit allows
@@ -968,7 +972,7 @@ static int mla_decode_noalloc_impl(void* stream, const void* q_lat, const void* 
       std::vector<MlaCombine> cb;
       int np = 0;
       one[0] = seq_lens[b];
-      plan_items(one.data(), 1, 1, &it, &cb, &np);  // a single slot never splits below the item limit
+      plan_items(one.data(), 1, 1, H, R, P, &it, &cb, &np);  // a single slot never splits below the item limit
       for (auto& x : it) {
         x.b = b;
         if (x.partial >= 0) x.partial += n_partial;

@@ -206,6 +206,59 @@ def _act_fp8(x):
     return a
 
 
+class Fp8Quantiser:
+    """The e4m3 activation quantisation points of forward_fp8, with rounding
+    ambiguity made explicit.  An activation is rounded to bf16 and then
+    quantised per 128 columns; the GPU computes the fp32 value before the
+    bf16 rounding with another summation order, so where that value lies
+    within `eps` (relative) of a bf16 rounding midpoint the GPU may hold the
+    other bf16 neighbour, and where that neighbour quantises to another e4m3
+    code the difference reaches the next GEMM.  Such elements are recorded
+    in `fragile` as (tag, position, column, distance); `flips` holds
+    (tag, position, column) triples for which the other neighbour is used."""
+
+    def __init__(self, flips=(), eps=1e-5, record=True):
+        self.flips = set(flips)
+        self.eps = eps
+        self.record = record
+        self.fragile = []
+
+    def __call__(self, x, tag, positions):
+        a = _f32(x).reshape(-1, np.shape(x)[-1])
+        b = _bf16(a)
+        # the other bf16 neighbour (one bf16 step = 2^16 in the fp32 bit
+        # pattern), on the side of the fp32 value
+        u = b.view(np.uint32).astype(np.int64)
+        step = np.where((a > b) == (b >= 0), 1, -1) * 65536
+        other = (u + step).astype(np.uint32).view(np.float32).reshape(a.shape)
+        mid = (b.astype(np.float64) + other.astype(np.float64)) / 2
+        # distance to the midpoint relative to the value, or to a hundredth of
+        # its 128-column block's largest value where the value is smaller
+        # (a GEMM's fp32 error scales with its terms, not with a small sum)
+        nb = (a.shape[1] + 127) // 128
+        pad = np.zeros((a.shape[0], nb * 128))
+        pad[:, : a.shape[1]] = np.abs(a)
+        bmax = np.repeat(pad.reshape(a.shape[0], nb, 128).max(axis=2), 128, axis=1)[:, : a.shape[1]]
+        dist = np.abs(a.astype(np.float64) - mid) / np.maximum(np.abs(a.astype(np.float64)), 0.01 * bmax + 1e-30)
+        if self.flips:
+            row_of = {pos: r for r, pos in enumerate(positions)}
+            for (ftag, pos, c) in self.flips:
+                if ftag == tag and pos in row_of:
+                    b[row_of[pos], c] = other[row_of[pos], c]
+        out = b.copy()
+        oracle().orc_act_fp8_roundtrip(p(out, f32p), out.shape[0], out.shape[1])
+        if self.record:
+            for r, c in zip(*np.nonzero(dist <= self.eps)):
+                if (tag, positions[r], c) in self.flips:
+                    continue
+                row = b[r:r + 1].copy()
+                row[0, c] = other[r, c]
+                oracle().orc_act_fp8_roundtrip(p(row, f32p), 1, row.shape[1])
+                if not np.array_equal(row[0], out[r]):
+                    self.fragile.append((tag, positions[r], int(c), float(dist[r, c])))
+        return out.reshape(np.shape(x))
+
+
 def _silu_mul(g, u):
     return _f32(g / (np.float32(1) + np.exp(-g)) * u)
 
@@ -217,17 +270,22 @@ def _bf16(a):
     return u.astype(np.uint32).view(np.float32).reshape(np.shape(a))
 
 
-def _mla_items(seq_lens, slots):
+def _mla_items(seq_lens, slots, H, R, P):
     """Work items of the split-KV MLA decode: runs of whole 64-token pages per
-    sequence, (b, first page, pages, end token, split).  A few candidate run
-    lengths are scored by a longest-first list schedule over `slots` (the
-    cost of an item is its pages + 2, + 2 more when its sequence is split);
-    the cheapest wins, at most 256 pages per item."""
+    sequence, (b, first page, pages, end token, split).  Candidate run
+    lengths (the longest sequence in 1..16 equal runs, all pages spread over
+    1..8 waves) are scored by a longest-first list schedule over `slots`:
+    an item costs its pages + 2, and when its sequence is split, 1 + the
+    bytes of its fp32 partial [H, R] written and read back in pages
+    (64 x (R + P) bf16); the cheapest wins, at most 256 pages per item."""
     import heapq
 
     pages = [(int(L) + 63) // 64 for L in seq_lens]
     total, maxp = sum(pages), max([1] + pages)
+    split_cost = 1.0 + float(H) * R * 4 * 2 / (64.0 * (R + P) * 2)
     caps = {min(maxp, 256)}
+    for n in range(2, 17):
+        caps.add(max(2, min((maxp + n - 1) // n, 256)))
     for k in range(1, 9):
         c = (total + k * slots - 1) // (k * slots)
         caps.add(max(2, min(c, 256)))
@@ -238,7 +296,7 @@ def _mla_items(seq_lens, slots):
         for n_p in pages:
             n = (n_p + cap - 1) // cap
             for i in range(n):
-                costs.append((i + 1) * n_p // n - i * n_p // n + 2.0 + (2.0 if n > 1 else 0.0))
+                costs.append((i + 1) * n_p // n - i * n_p // n + 2.0 + (split_cost if n > 1 else 0.0))
         costs.sort(reverse=True)
         heap = [0.0] * slots
         span = 0.0
@@ -313,7 +371,7 @@ def mla_decode_storage_points(q_lat, q_rope, cache, block_table, seq_lens, scale
     (_mla_items over `slots`); returns [B, H, R] bf16 values as fp32."""
     B, H, R = q_lat.shape
     scale_log2 = np.float32(np.float32(scale) * np.float32(1.4426950408889634))
-    items = _mla_items(seq_lens, slots)
+    items = _mla_items(seq_lens, slots, H, R, q_rope.shape[2])
     out = np.zeros((B, H, R), np.float32)
     for b in range(B):
         L = int(seq_lens[b])
@@ -324,7 +382,7 @@ def mla_decode_storage_points(q_lat, q_rope, cache, block_table, seq_lens, scale
     return out
 
 
-def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots):
+def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots, quant=None, layer=0):
     """The attention block of one layer for a teacher-forced sequence, at the
     batched decode's storage points (see the module docstring).  xq [T, D]:
     the layer input as the FP8 GEMM sees it; returns the o_proj output [T, D]."""
@@ -359,22 +417,28 @@ def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots):
     o_lat = np.zeros((T, H, R), np.float32)
     for t in range(T):
         # position t decodes with t + 1 cached tokens, planned as a batch of one sequence
-        o_lat[t] = _attend_sequence(q_lat[t], q_rope[t], cache, kr, _mla_items([t + 1], slots), scale_log2)
-    attn = _bf16(_f32(np.einsum("thr,hvr->thv", o_lat.astype(np.float64), w_uv))).reshape(T, H * v)
-    return _f32(_act_fp8(attn).astype(np.float64) @ Wo.T.astype(np.float64))
+        o_lat[t] = _attend_sequence(q_lat[t], q_rope[t], cache, kr, _mla_items([t + 1], slots, H, R, P), scale_log2)
+    # the per-head W_UV output before its bf16 rounding (the quantiser rounds it)
+    attn = _f32(np.einsum("thr,hvr->thv", o_lat.astype(np.float64), w_uv)).reshape(T, H * v)
+    attn_q = _act_fp8(attn) if quant is None else quant(attn, ("o_proj", layer), list(range(T)))
+    return _f32(attn_q.astype(np.float64) @ Wo.T.astype(np.float64))
 
 
-def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148, swaps=(), margins=None):
+def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148, swaps=(), margins=None, quant=None):
     """Logits [T, V] of `seq` for a block-scaled FP8 checkpoint: `tensors`
     holds every tensor (fp32 values), `fp8` maps the FP8 weights' names to
     their dequantised fp32 matrices (e4m3 * scale).  Softmax-greedy routing
     as forward(), with the same router margins (into the dict `margins`,
     {layer: [T]}, when given) and near-tie `swaps` ((layer, position) pairs
     whose (k+1)-th expert takes the k-th slot).  `slots`: the split-KV
-    planner's parallel work slots (the GPU's SM count for kv_lora_rank 128)."""
+    planner's parallel work slots (the GPU's SM count for kv_lora_rank 128).
+    `quant`: an Fp8Quantiser (records the ambiguous roundings, applies
+    chosen flips); None quantises plainly."""
     if cfg.get("q_lora_rank", 0) or cfg.get("scoring_func", 0) != 0:
         raise NotImplementedError("oracle.model covers q_lora_rank 0 with softmax scoring")
     c = cfg
+    if quant is None:
+        quant = Fp8Quantiser(record=False)
     W = {n: _f32(a) for n, a in tensors.items()}
     for n, a in fp8.items():
         W[n] = _bf16_round(a) if n.endswith("kv_b_proj.weight") else _f32(a)
@@ -388,23 +452,25 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148, swap
     h = _f32(W["model.embed_tokens.weight"][seq])
     for li in range(c["num_hidden_layers"]):
         pre = f"model.layers.{li}."
-        xn = _act_fp8(_rmsnorm_rows(h, W[pre + "input_layernorm.weight"], eps))
+        allpos = list(range(T))
+        xn = quant(_rmsnorm_rows(h, W[pre + "input_layernorm.weight"], eps), ("attn_in", li), allpos)
         a = pre + "self_attn."
         out = _mla_fp8_layer(c, W[a + "q_proj.weight"], W[a + "kv_a_proj_with_mqa.weight"],
                              W[a + "kv_a_layernorm.weight"], W[a + "kv_b_proj.weight"], W[a + "o_proj.weight"], xn,
-                             slots)
+                             slots, quant, li)
         h = _f32(h + out)
         xn = _rmsnorm_rows(h, W[pre + "post_attention_layernorm.weight"], eps)
-        xq = _act_fp8(xn)
+        xq = quant(xn, ("ffn_in", li), allpos)
 
-        def ffn(wg, wu, wd, x):
+        def ffn(wg, wu, wd, x, tag, pos):
             g = _f32(x.astype(np.float64) @ wg.T.astype(np.float64))
             u = _f32(x.astype(np.float64) @ wu.T.astype(np.float64))
-            mid = _act_fp8(_silu_mul(g, u))
+            mid = quant(_silu_mul(g, u), tag, pos)
             return _f32(mid.astype(np.float64) @ wd.T.astype(np.float64))
 
         if pre + "mlp.gate.weight" not in W:
-            out = ffn(*(W[pre + "mlp." + n + "_proj.weight"] for n in ("gate", "up", "down")), xq)
+            out = ffn(*(W[pre + "mlp." + n + "_proj.weight"] for n in ("gate", "up", "down")), xq, ("mid", li, -1),
+                      allpos)
         else:
             wgate = W[pre + "mlp.gate.weight"]
             shared = pre + "mlp.shared_experts.gate_proj.weight" in W
@@ -434,10 +500,12 @@ def forward_fp8(cfg: dict, tensors: dict, fp8: dict, seq, slots: int = 148, swap
                 acc = np.zeros(D, np.float32)
                 x = xq[t:t + 1]
                 for e, wt in zip(ids, w):
-                    y = ffn(*(W[pre + f"mlp.experts.{e}.{n}_proj.weight"] for n in ("gate", "up", "down")), x)
+                    y = ffn(*(W[pre + f"mlp.experts.{e}.{n}_proj.weight"] for n in ("gate", "up", "down")), x,
+                            ("mid", li, int(e)), [t])
                     acc = _f32(acc + np.float32(wt) * y[0])
                 if shared:
-                    y = ffn(*(W[pre + f"mlp.shared_experts.{n}_proj.weight"] for n in ("gate", "up", "down")), x)
+                    y = ffn(*(W[pre + f"mlp.shared_experts.{n}_proj.weight"] for n in ("gate", "up", "down")), x,
+                            ("mid", li, E), [t])
                     acc = _f32(acc + y[0])
                 out[t] = acc
             if margins is not None:

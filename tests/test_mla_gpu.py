@@ -184,7 +184,7 @@ def test_mla_small_rank_storage_points(gpu_ctx):
         info = plan.info()
     finally:
         plan.close()
-    items = OM._mla_items(case.seq_lens, slots)
+    items = OM._mla_items(case.seq_lens, slots, 8, 128, 32)
     assert info["n_items"] == len(items)
     assert info["n_partial"] == sum(1 for it in items if it[4])
     out = run_gpu(gpu_ctx, case).float().cpu().numpy()

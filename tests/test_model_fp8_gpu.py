@@ -64,9 +64,12 @@ def test_fp8_weight_without_scale_is_rejected(gpu_ctx):
     m.close()
 
 
-# gate-logit gap (logit units) below which the last routed expert may swap: one
-# activation moved across an e4m3 boundary (6-12% of one element of a K=512
-# GEMM input) moves this model's gate logits by ~1e-3; the bound is 5x that
+# A position this far from the oracle (logits max-rel) holds a discrete
+# difference to explain; after explaining them every position must be within
+# FINAL of the oracle, ten times inside the stated 2e-2 bar.
+STRICT = 5e-4
+FINAL = 2e-3
+# gate-logit gap (logit units) below which the last routed expert may swap
 NEAR_TIE = 0.005
 
 
@@ -80,19 +83,22 @@ def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     the same bytes to every e4m3 quantiser.
 
     The GPU decodes a 16-token prompt and then generates 32 tokens greedily;
-    the oracle is teacher-forced on the same 48 tokens.  Bar (the stated
-    layer-output tolerance, on the logits): max-rel <= 2e-2 at every one of
-    the 48 positions, and at each of the 32 generation steps the oracle's
-    greedy id equals the token the GPU generated.
+    the oracle is teacher-forced on the same 48 tokens.
 
-    Router near-ties, as in the bf16 whole-model test: fp32 summation order
-    can still move one activation across an e4m3 rounding boundary (a 6-12%
-    change of that element), which may swap the last routed expert where
-    the oracle's k-th and (k+1)-th gate logits are closer than NEAR_TIE.
-    Position by position, a position over the bar is checked against the
-    oracle with one more such swap forced (at that position or an earlier
-    one, whose cache rows it reads); every swap taken is printed, and each
-    must be a near-tie."""
+    Rounding ambiguity.  The GPU sums its GEMMs in another order, so where an
+    activation's fp32 value lies within ~1e-5 of a bf16 rounding midpoint
+    the two sides may store the two bf16 neighbours, and where those
+    quantise to different e4m3 codes one element of the next GEMM's input
+    differs by 6-12%.  On this random tiny model one such element moves the
+    logits by up to 5% (so no implementation that sums differently can hold
+    the whole model to 2e-2 without accounting for it).  The oracle records
+    every such ambiguous element (oracle.model.Fp8Quantiser); position by
+    position, the first position more than STRICT away is explained by the
+    one ambiguous element of that position (or router near-tie, gap below
+    NEAR_TIE) whose other rounding brings it at least 4x closer, and the
+    oracle continues with that choice.  Bar: every choice taken is such an
+    ambiguity, and with them all 48 positions are within FINAL (2e-3) of the
+    oracle, whose greedy id equals each of the 32 generated tokens."""
     import torch
 
     import oracle.model as OM
@@ -123,31 +129,44 @@ def test_fp8_model_matches_fp8_oracle(gpu_ctx):
     def max_rel(ref):
         return np.abs(got - ref).max(1) / np.abs(ref).max(1)
 
-    swaps = []
-    margins = {}
-    ref = OM.forward_fp8(TINY, t, fp8, seq, slots=slots, margins=margins)
+    def run(flips, swaps, record=True):
+        q = OM.Fp8Quantiser(flips, record=record)
+        margins = {}
+        ref = OM.forward_fp8(TINY, t, fp8, seq, slots=slots, swaps=swaps, margins=margins, quant=q)
+        return ref, q.fragile, margins
+
+    flips, swaps = set(), []
+    ref, fragile, margins = run(flips, swaps)
     err = max_rel(ref)
-    print(f"FP8 model vs FP8 oracle: logits max-rel per position {np.array2string(err, precision=1)}")
-    for _ in range(6):
-        bad = np.nonzero(err > 2e-2)[0]
+    print(f"FP8 model vs FP8 oracle before explaining ambiguities: max-rel per position "
+          f"{np.array2string(err, precision=1)}")
+    for _ in range(24):
+        bad = np.nonzero(err > STRICT)[0]
         if len(bad) == 0:
             break
         p0 = int(bad[0])
-        cands = sorted((float(m[q]), li, q) for li, m in margins.items() for q in range(p0 + 1) if m[q] < NEAR_TIE)
-        assert cands, f"position {p0}: max-rel {err[p0]:.3e} with no router near-tie at or before it"
+        cands = [("flip", f[:3], f[3]) for f in sorted(fragile, key=lambda f: f[3]) if f[1] == p0][:12]
+        cands += [("swap", (li, p0), float(m[p0])) for li, m in margins.items() if m[p0] < NEAR_TIE]
+        assert cands, f"position {p0}: max-rel {err[p0]:.3e} with no ambiguous rounding or router near-tie"
         best = None
-        for gap, li, q in cands[:8]:
-            r2 = OM.forward_fp8(TINY, t, fp8, seq, slots=slots, swaps=swaps + [(li, q)])
-            e2 = max_rel(r2)
-            if best is None or e2[p0] < best[0][p0]:
-                best = (e2, r2, (li, q, gap))
-        err, ref = best[0], best[1]
-        swaps.append(best[2][:2])
-        print(f"near-tie swap at layer {best[2][0]}, position {best[2][1]} (gate gap {best[2][2]:.2e}): "
-              f"position {p0} max-rel {err[p0]:.3e}")
+        for kind, what, gap in cands:
+            r2, _, _ = run(flips | {what} if kind == "flip" else flips, swaps + [what] if kind == "swap" else swaps,
+                           record=False)
+            e2 = max_rel(r2)[p0]
+            if best is None or e2 < best[0]:
+                best = (e2, kind, what, gap)
+        assert best[0] <= err[p0] / 4, (p0, float(err[p0]), best)
+        if best[1] == "flip":
+            flips.add(best[2])
+        else:
+            swaps.append(best[2])
+        print(f"position {p0}: {best[1]} {best[2]} (distance {best[3]:.1e}) takes max-rel {err[p0]:.2e} "
+              f"-> {best[0]:.2e}")
+        ref, fragile, margins = run(flips, swaps)
+        err = max_rel(ref)
     oracle_ids = ref.argmax(1)[15:47]
     same = int((oracle_ids == np.array(gen[:32])).sum())
     print(f"FP8 model vs FP8 oracle: logits max-rel median {np.median(err):.3e} worst {err.max():.3e}; "
-          f"greedy {same}/32; near-tie swaps {swaps}")
-    assert err.max() <= 2e-2, err
+          f"greedy {same}/32; rounding choices taken {len(flips)}, router swaps {len(swaps)}")
+    assert err.max() <= FINAL, err
     assert same == 32, (oracle_ids, gen)
