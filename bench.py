@@ -628,11 +628,17 @@ def ep_tiny_parity(ctx, rank, world, steps=6):
 
 
 def trace_steps(out_dir, rank, step, n, stream):
-    """Per-kernel device times of n decode steps from CUPTI activity records
+    """Per-kernel device times of decode steps from CUPTI activity records
     (torch.profiler; unlike an ncu replay it does not serialise the launches,
     so the expert-parallel kernels that wait on peer ranks run as they do
-    untraced).  Writes <out_dir>/kernels_rank<r>.md: per kernel name its
-    launches, total and mean device time and share of the summed time."""
+    untraced).  Runs n + 2 steps and keeps the last n (the first ones absorb
+    the ranks' different profiler start-up).  Writes
+    <out_dir>/kernels_rank<r>.md: per kernel name its launches, "advance"
+    (end of the kernel minus end of the previous one: the stream's progress
+    it accounts for, less what it overlapped with its predecessor through
+    programmatic dependent launch; the advances sum to the traced time) and
+    duration; then the kernels of one layer in order (the layers cut at each
+    MLA launch), averaged over the layers of the same sequence."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
@@ -640,38 +646,52 @@ def trace_steps(out_dir, rank, step, n, stream):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(2):
+            step()
         e0.record(stream)
         for _ in range(n):
             step()
         e1.record(stream)
         e1.synchronize()
-    # device activity records in start order; with one stream the kernels end in
-    # launch order, so end_k - end_(k-1) is how far kernel k moved the stream on
-    # (its own time, less what it overlapped with its predecessor through
-    # programmatic dependent launch); these advances sum to the traced time
     evs = []
     for ev in prof.events():
         if str(getattr(ev, "device_type", "")).endswith("CUDA") and ev.time_range.end > ev.time_range.start:
             evs.append((ev.time_range.start, ev.time_range.end, ev.name))
     evs.sort()
-    stats = {}
-    prev_end = None
+    per_step = len(evs) // (n + 2)
+    prev_end = evs[2 * per_step - 1][1] if per_step else None
+    evs = evs[2 * per_step:]
+    stats, seq = {}, []
     for t0, t1, name in evs:
         adv = t1 - t0 if prev_end is None else max(0.0, t1 - max(prev_end, t0))
         prev_end = t1 if prev_end is None else max(prev_end, t1)
         cnt, dur, a = stats.get(name, (0, 0.0, 0.0))
         stats[name] = (cnt + 1, dur + (t1 - t0), a + adv)
+        seq.append((name, adv, t1 - t0))
     rows = sorted(stats.items(), key=lambda kv: -kv[1][2])
     total = sum(v[2] for _, v in rows) or 1.0
+    short = lambda nm: nm.replace("dsb::(anonymous namespace)::", "").split("(")[0][:60]  # noqa: E731
     with open(os.path.join(out_dir, f"kernels_rank{rank}.md"), "w") as f:
-        f.write(f"rank {rank}: {n} steps, {e0.elapsed_time(e1) / n * 1e3:.1f} us per step (CUDA events, traced); "
-                f"advance = end of the kernel minus end of the previous one (the stream's progress it accounts "
-                f"for), duration = its own start to end\n\n")
+        f.write(f"rank {rank}: {n} steps, {e0.elapsed_time(e1) / n * 1e3:.1f} us per step (CUDA events, traced)\n\n")
         f.write("| kernel | launches/step | advance us/step | share | duration us/step | mean duration us |\n"
                 "|---|---|---|---|---|---|\n")
         for name, (cnt, dur, adv) in rows:
-            f.write(f"| {name[:80]} | {cnt / n:.1f} | {adv / n:.1f} | {100 * adv / total:.1f}% | {dur / n:.1f} | "
+            f.write(f"| {short(name)} | {cnt / n:.1f} | {adv / n:.1f} | {100 * adv / total:.1f}% | {dur / n:.1f} | "
                     f"{dur / cnt:.2f} |\n")
+        # one layer in order: segments between MLA launches of the last step, grouped by kernel sequence
+        last = seq[-per_step:] if per_step else []
+        cuts = [i for i, (nm, _, _) in enumerate(last) if "mla_decode_kernel" in nm]
+        segs = [last[a:b] for a, b in zip(cuts, cuts[1:])]
+        groups = {}
+        for sg in segs:
+            groups.setdefault(tuple(short(nm) for nm, _, _ in sg), []).append(sg)
+        if groups:
+            key, members = max(groups.items(), key=lambda kv: len(kv[1]))
+            f.write(f"\nOne layer, MLA to MLA, mean over {len(members)} layers of the last step:\n\n"
+                    "| # | kernel | advance us | duration us |\n|---|---|---|---|\n")
+            for i, nm in enumerate(key):
+                f.write(f"| {i} | {nm} | {sum(m[i][1] for m in members) / len(members):.1f} | "
+                        f"{sum(m[i][2] for m in members) / len(members):.1f} |\n")
 
 
 def measure_model(args, cfg, B, P, steps, env):

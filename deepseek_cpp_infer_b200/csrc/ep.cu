@@ -151,6 +151,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    int* status) {
   pdl_wait();
   __shared__ int32_t my_off[256];  // [dst][el] (world * E_local = E <= 256): this rank's first row in dst's buffer
+  __shared__ int32_t cnt_s[kMaxWorld * 256];  // the count matrix [src][dst][el] (world * E <= 2048)
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {
@@ -161,22 +162,32 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
   __syncthreads();
   if (!ok_s) return;
+  // every source's counts in one parallel pass (the flags' acquire ordered
+  // them before this point), then the prefix sums from shared memory
   const int32_t* counts = reinterpret_cast<const int32_t*>(win + L.off_counts);  // [src][dst][el]
   const int W = L.world, EL = L.E_local;
+  __shared__ int32_t tot_s[256];  // [dst][el]: rows of local expert el that dst receives from all sources
+  for (int i = threadIdx.x; i < W * W * EL; i += blockDim.x) cnt_s[i] = __ldcv(counts + i);
+  __syncthreads();
   for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
     const int dst = idx / EL, el = idx % EL;
     int o = 0;
-    for (int e2 = 0; e2 < el; ++e2)
-      for (int s = 0; s < W; ++s) o += __ldcv(counts + ((size_t)s * W + dst) * EL + e2);
-    for (int s = 0; s < L.rank; ++s) o += __ldcv(counts + ((size_t)s * W + dst) * EL + el);
+    for (int s = 0; s < W; ++s) o += cnt_s[(s * W + dst) * EL + el];
+    tot_s[idx] = o;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
+    const int dst = idx / EL, el = idx % EL;
+    int o = 0;
+    for (int e2 = 0; e2 < el; ++e2) o += tot_s[dst * EL + e2];
+    for (int s = 0; s < L.rank; ++s) o += cnt_s[(s * W + dst) * EL + el];
     my_off[idx] = o;
   }
   if (blockIdx.x == 0) {
     // receive offsets of this rank's experts (all sources), the GEMM's groups
     for (int el = threadIdx.x; el <= EL; el += blockDim.x) {
       int o = 0;
-      for (int e2 = 0; e2 < el; ++e2)
-        for (int s = 0; s < W; ++s) o += __ldcv(counts + ((size_t)s * W + L.rank) * EL + e2);
+      for (int e2 = 0; e2 < el; ++e2) o += tot_s[L.rank * EL + e2];
       recv_offsets[el] = o;
     }
   }

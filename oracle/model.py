@@ -217,14 +217,28 @@ class Fp8Quantiser:
     in `fragile` as (tag, position, column, distance); `flips` holds
     (tag, position, column) triples for which the other neighbour is used."""
 
-    def __init__(self, flips=(), eps=1e-5, record=True):
+    def __init__(self, flips=(), eps=3e-5, eps_store=3e-6, record=True):
         self.flips = set(flips)
         self.eps = eps
+        self.eps_store = eps_store
         self.record = record
         self.fragile = []
 
-    def __call__(self, x, tag, positions):
+    def bf16(self, x, tag, positions):
+        """A bf16 storage point (rows = positions): the value rounded to bf16,
+        or to the other neighbour where flipped; every element within
+        eps_store of a rounding midpoint is recorded (any flip changes the
+        stored value)."""
         a = _f32(x).reshape(-1, np.shape(x)[-1])
+        b, other, dist = self._neighbours(a)
+        self._apply(b, other, tag, positions)
+        if self.record:
+            for r, c in zip(*np.nonzero(dist <= self.eps_store)):
+                if (tag, positions[r], c) not in self.flips:
+                    self.fragile.append((tag, positions[r], int(c), float(dist[r, c])))
+        return b.reshape(np.shape(x))
+
+    def _neighbours(self, a):
         b = _bf16(a)
         # the other bf16 neighbour (one bf16 step = 2^16 in the fp32 bit
         # pattern), on the side of the fp32 value
@@ -240,11 +254,19 @@ class Fp8Quantiser:
         pad[:, : a.shape[1]] = np.abs(a)
         bmax = np.repeat(pad.reshape(a.shape[0], nb, 128).max(axis=2), 128, axis=1)[:, : a.shape[1]]
         dist = np.abs(a.astype(np.float64) - mid) / np.maximum(np.abs(a.astype(np.float64)), 0.01 * bmax + 1e-30)
+        return b, other, dist
+
+    def _apply(self, b, other, tag, positions):
         if self.flips:
             row_of = {pos: r for r, pos in enumerate(positions)}
             for (ftag, pos, c) in self.flips:
                 if ftag == tag and pos in row_of:
                     b[row_of[pos], c] = other[row_of[pos], c]
+
+    def __call__(self, x, tag, positions):
+        a = _f32(x).reshape(-1, np.shape(x)[-1])
+        b, other, dist = self._neighbours(a)
+        self._apply(b, other, tag, positions)
         out = b.copy()
         oracle().orc_act_fp8_roundtrip(p(out, f32p), out.shape[0], out.shape[1])
         if self.record:
@@ -315,7 +337,7 @@ def _mla_items(seq_lens, slots, H, R, P):
     return items
 
 
-def _attend_item(q_lat, q_rope, c, kr, tok0, tok_end, scale_log2):
+def _attend_item(q_lat, q_rope, c, kr, tok0, tok_end, scale_log2, pstore=None):
     """One work item of the latent attention for all heads: tokens [tok0,
     tok_end) of the cache rows c [T, R], kr [T, P] (bf16 values); q_lat
     [H, R], q_rope [H, P] (bf16 values).  Scores in the log2 domain, a
@@ -337,22 +359,23 @@ def _attend_item(q_lat, q_rope, c, kr, tok0, tok_end, scale_log2):
         m = np.where(up, mt, m)
         O *= factor[:, None].astype(np.float64)
         l *= factor.astype(np.float64)
-        pr = _bf16(np.exp2((s - m[:, None]).astype(np.float64)).astype(np.float32))
+        pr = np.exp2((s - m[:, None]).astype(np.float64)).astype(np.float32)
+        pr = _bf16(pr) if pstore is None else pstore(pr, t0)
         l += pr.astype(np.float64).sum(axis=1)
         O += pr.astype(np.float64) @ c[t0:t1].astype(np.float64)
     return O.astype(np.float32), m, l.astype(np.float32)
 
 
-def _attend_sequence(q_lat, q_rope, c, kr, items, scale_log2):
-    """One sequence's latent attention output [H, R] (bf16 values) over its
-    work items (all items of `items` must belong to it): a whole-sequence item
-    normalises its own sum; split items are merged as
-    sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i."""
-    parts = [(_attend_item(q_lat, q_rope, c, kr, p0 * 64, end, scale_log2), split)
+def _attend_sequence(q_lat, q_rope, c, kr, items, scale_log2, pstore=None):
+    """One sequence's latent attention output [H, R] over its work items
+    (all items of `items` must belong to it), in fp32 before its bf16
+    rounding: a whole-sequence item normalises its own sum; split items are
+    merged as sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i."""
+    parts = [(_attend_item(q_lat, q_rope, c, kr, p0 * 64, end, scale_log2, pstore), split)
              for (_, p0, n_p, end, split) in items]
     if len(parts) == 1 and not parts[0][1]:
         Ow, _, lw = parts[0][0]
-        return _bf16(Ow * (np.float32(1.0) / lw)[:, None])
+        return _f32(Ow * (np.float32(1.0) / lw)[:, None])
     M = np.max(np.stack([m for (_, m, _), _ in parts]), axis=0)
     den = np.zeros(q_lat.shape[0], np.float32)
     acc = np.zeros((q_lat.shape[0], c.shape[1]), np.float32)
@@ -360,7 +383,7 @@ def _attend_sequence(q_lat, q_rope, c, kr, items, scale_log2):
         w = np.exp2((m - M).astype(np.float64)).astype(np.float32)
         den = _f32(den + w * lw)
         acc = _f32(acc + w[:, None] * Ow)
-    return _bf16(acc * (np.float32(1.0) / den)[:, None])
+    return _f32(acc * (np.float32(1.0) / den)[:, None])
 
 
 def mla_decode_storage_points(q_lat, q_rope, cache, block_table, seq_lens, scale, slots=148):
@@ -377,8 +400,8 @@ def mla_decode_storage_points(q_lat, q_rope, cache, block_table, seq_lens, scale
         L = int(seq_lens[b])
         pages = block_table[b, : (L + 63) // 64]
         rows = cache[pages].reshape(-1, cache.shape[2])
-        out[b] = _attend_sequence(_f32(q_lat[b]), _f32(q_rope[b]), rows[:, :R], rows[:, R:],
-                                  [it for it in items if it[0] == b], scale_log2)
+        out[b] = _bf16(_attend_sequence(_f32(q_lat[b]), _f32(q_rope[b]), rows[:, :R], rows[:, R:],
+                                        [it for it in items if it[0] == b], scale_log2))
     return out
 
 
@@ -407,17 +430,23 @@ def _mla_fp8_layer(c, Wq, Wkva, w_norm, Wkvb, Wo, xq, slots, quant=None, layer=0
             r = _f32(q[t, h, nope:]).copy()
             orc.orc_rope_inplace_f32(p(r, f32p), P, t, theta)
             q_rope[t, h] = r
-    cache, kr, q_rope = _bf16(cache), _bf16(kr), _bf16(q_rope)
-    q_nope = _bf16(q[:, :, :nope])
+    store = (lambda x, tag: _bf16(x)) if quant is None else \
+        (lambda x, tag: quant.bf16(x.reshape(T, -1), (tag, layer), list(range(T))).reshape(x.shape))
+    cache, kr, q_rope = store(cache, "c"), store(kr, "kr"), store(q_rope, "q_rope")
+    q_nope = store(_f32(q[:, :, :nope]), "q_nope")
     wkvb = Wkvb.reshape(H, nope + v, R)
     w_uk, w_uv = wkvb[:, :nope, :].astype(np.float64), wkvb[:, nope:, :].astype(np.float64)  # [H, nope, R], [H, v, R]
-    q_lat = _bf16(_f32(np.einsum("thn,hnr->thr", q_nope.astype(np.float64), w_uk)))
+    q_lat = store(_f32(np.einsum("thn,hnr->thr", q_nope.astype(np.float64), w_uk)), "q_lat")
     scale = np.float32(1.0) / np.sqrt(np.float32(nope + P), dtype=np.float32)
     scale_log2 = np.float32(scale * np.float32(1.4426950408889634))
     o_lat = np.zeros((T, H, R), np.float32)
     for t in range(T):
         # position t decodes with t + 1 cached tokens, planned as a batch of one sequence
-        o_lat[t] = _attend_sequence(q_lat[t], q_rope[t], cache, kr, _mla_items([t + 1], slots, H, R, P), scale_log2)
+        # the probabilities of a 64-token tile starting at token t0 as one stored row (head-major)
+        pstore = None if quant is None else (lambda x, t0, t=t: quant.bf16(x.reshape(1, -1), ("P", layer, t0),
+                                                                            [t]).reshape(x.shape))
+        o = _attend_sequence(q_lat[t], q_rope[t], cache, kr, _mla_items([t + 1], slots, H, R, P), scale_log2, pstore)
+        o_lat[t] = _bf16(o) if quant is None else quant.bf16(o.reshape(1, -1), ("o_lat", layer), [t]).reshape(H, R)
     # the per-head W_UV output before its bf16 rounding (the quantiser rounds it)
     attn = _f32(np.einsum("thr,hvr->thv", o_lat.astype(np.float64), w_uv)).reshape(T, H * v)
     attn_q = _act_fp8(attn) if quant is None else quant(attn, ("o_proj", layer), list(range(T)))
