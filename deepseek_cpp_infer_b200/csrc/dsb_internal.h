@@ -204,10 +204,15 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
 // ep_send then copies the rows to their owners (after every rank's counts
 // arrived) and waits for the rows sent here.
 int ep_publish(dsb_ep* ep, int T, const int32_t* ids);
-int ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x, int32_t** recv_offsets);
+// With n_shared > 0 the dispatch also copies this rank's T rows once per
+// shared expert after the rows it receives (recv_offsets[E_local + j + 1] ends
+// copy j), so one grouped GEMM over E_local + n_shared groups runs both.
+int ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x, int32_t** recv_offsets,
+            int n_shared);
 // dsb_ep_combine with the next RMSNorm fused as in moe_combine.
+// shared_row0 (device, may be NULL): the shared outputs start at that row of `shared`.
 int ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
-               int n_shared, float* h, const float* w_next, float eps, void* xn_next);
+               int n_shared, float* h, const float* w_next, float eps, void* xn_next, const int32_t* shared_row0);
 int argmax_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, int32_t* out);
 // Sampled id per row (ds::core::Sampler::sample); uniforms[B] on the device.
 int sample_rows(dsb_ctx* ctx, const float* logits, int64_t ld, int B, int V, float temperature, int top_k, float top_p,

@@ -23,7 +23,8 @@
 //   counts [world src][world dst][E_local] int32
 //   flags  [3 phases][world src] uint32 (counts, rows, return)
 //   meta   [cap] int32  (source rank << 24 | source pick index) per received row
-//   recv   [cap][D] bf16 received rows, cap = world * T_max * k
+//   recv   [cap + kMaxShared * T_max][D] bf16 received rows, cap = world * T_max * k,
+//          followed (when asked) by this rank's own rows once per shared expert
 //   inbox  [T_max * k][D] fp32 returned outputs of this rank's picks
 // Replaces nothing in the reference (single GPU, B = 1); the exchange model
 // is a host permutation: token -> rank = expert / (E / world).
@@ -42,6 +43,7 @@ namespace dsb {
 namespace {
 
 constexpr int kMaxWorld = 8;
+constexpr int kMaxShared = 4;  // shared-expert groups whose rows can follow the received ones
 
 struct EpPeers {
   uint8_t* win[kMaxWorld];  // every rank's window, mapped here (win[rank] = own)
@@ -71,7 +73,7 @@ EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) 
   L.off_meta = o;
   o += a((size_t)L.cap * 4);
   L.off_recv = o;
-  o += a((size_t)L.cap * D * 2);
+  o += a((size_t)(L.cap + kMaxShared * T_max) * D * 2);
   L.off_inbox = o;
   o += a((size_t)T_max * k * D * 4);
   L.bytes = o;
@@ -146,9 +148,9 @@ __global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, in
 // receive offsets for the expert GEMMs); warps copy one pick's row each.  The
 // last CTA to finish raises the rows flag in every window.
 __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ ids,
-                                   const int32_t* __restrict__ slot, int n_picks, EpLayout L, EpPeers peers,
-                                   int32_t* __restrict__ recv_offsets, int* __restrict__ ticket, uint32_t epoch,
-                                   int* status) {
+                                   const int32_t* __restrict__ slot, int n_picks, int n_shared, EpLayout L,
+                                   EpPeers peers, int32_t* __restrict__ recv_offsets, int* __restrict__ ticket,
+                                   uint32_t epoch, int* status) {
   pdl_wait();
   __shared__ int32_t my_off[256];  // [dst][el] (world * E_local = E <= 256): this rank's first row in dst's buffer
   __shared__ int32_t cnt_s[kMaxWorld * 256];  // the count matrix [src][dst][el] (world * E <= 2048)
@@ -183,15 +185,29 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
     for (int s = 0; s < L.rank; ++s) o += cnt_s[(s * W + dst) * EL + el];
     my_off[idx] = o;
   }
+  const int T = n_picks / L.k;
   if (blockIdx.x == 0) {
-    // receive offsets of this rank's experts (all sources), the GEMM's groups
-    for (int el = threadIdx.x; el <= EL; el += blockDim.x) {
+    // receive offsets of this rank's experts (all sources), the GEMM's groups;
+    // with shared experts, group EL + j is this rank's T rows copied after them
+    for (int el = threadIdx.x; el <= EL + n_shared; el += blockDim.x) {
       int o = 0;
-      for (int e2 = 0; e2 < el; ++e2) o += tot_s[L.rank * EL + e2];
-      recv_offsets[el] = o;
+      for (int e2 = 0; e2 < min(el, EL); ++e2) o += tot_s[L.rank * EL + e2];
+      recv_offsets[el] = o + (el > EL ? (el - EL) * T : 0);
     }
   }
   __syncthreads();
+  if (n_shared > 0) {
+    // this rank's own rows, once per shared group, after every row it receives
+    int n_recv = 0;
+    for (int e2 = 0; e2 < EL; ++e2) n_recv += tot_s[L.rank * EL + e2];
+    uint8_t* own = peers.win[L.rank] + L.off_recv;
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_shared * T; i += gridDim.x * warps) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i % T) * ldx);
+      uint4* out = reinterpret_cast<uint4*>(own + (size_t)(n_recv + i) * L.D * 2);
+      for (int v = lane; v < L.D / 8; v += 32) out[v] = src[v];
+    }
+  }
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 8;  // 16-byte vectors of bf16
   for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_picks; i += gridDim.x * warps) {
@@ -239,14 +255,18 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
   const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 4;  // 16-byte vectors of fp32
+  bool wrote = false;
   for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < n_recv; r += gridDim.x * warps) {
     const int m = __ldcv(meta + r);
     const int home = m >> 24, pick = m & 0xFFFFFF;
     const uint4* src = reinterpret_cast<const uint4*>(y + (int64_t)r * ldy);
     uint4* out = reinterpret_cast<uint4*>(peers.win[home] + L.off_inbox + (size_t)pick * L.D * 4);
     for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
+    wrote = true;
   }
-  __threadfence_system();
+  // only threads that stored rows order them (a system-scope fence waits for
+  // the thread's own stores to reach the peers)
+  if (wrote) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int prev = atomicAdd(ticket, 1);
@@ -261,7 +281,8 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
 
 // 5. h[t] += sum_j w[t,j] * inbox[t*k+j] (pick order) + sum_s shared[s*T + t].
 __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLayout L, EpPeers peers,
-                                  const float* __restrict__ shared, int n_shared, float* __restrict__ h,
+                                  const float* __restrict__ shared, const int32_t* __restrict__ shared_row0,
+                                  int n_shared, float* __restrict__ h,
                                   const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next,
                                   uint32_t epoch, int* status) {
   pdl_wait();
@@ -287,6 +308,8 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
     const float wj = wsm[j];
     return make_float4(__fmul_rn(v.x, wj), __fmul_rn(v.y, wj), __fmul_rn(v.z, wj), __fmul_rn(v.w, wj));
   };
+  // shared outputs: [n_shared][T][D], at row shared_row0[0] of `shared` when given
+  if (shared_row0 != nullptr) shared += (size_t)shared_row0[0] * D;
   combine_row(pick, k, D, n_shared > 0 ? shared + (size_t)t * D : nullptr, n_shared, (int64_t)T * D, h + (size_t)t * D,
               w_next, eps,
               xn_next ? xn_next + (size_t)t * D : nullptr, red);
@@ -340,9 +363,9 @@ static int ep_create_impl(dsb_ctx* ctx, int rank, int world, int n_experts, int 
   cudaError_t e = cudaMalloc(&ep->win, ep->L.bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->win, 0, ep->L.bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ep->d_slot, (size_t)max_tokens * top_k * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&ep->d_recv_off, (size_t)(ep->L.E_local + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->d_recv_off, (size_t)(ep->L.E_local + 1 + kMaxShared) * 4);
   // zero ranges until the first dispatch (a timed-out exchange leaves them as they were)
-  if (e == cudaSuccess) e = cudaMemset(ep->d_recv_off, 0, (size_t)(ep->L.E_local + 1) * 4);
+  if (e == cudaSuccess) e = cudaMemset(ep->d_recv_off, 0, (size_t)(ep->L.E_local + 1 + kMaxShared) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&ep->d_ticket, 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(ep->d_ticket, 0, 2 * sizeof(int));
   if (e != cudaSuccess) {
@@ -439,17 +462,17 @@ int dsb::ep_publish(dsb_ep* ep, int T, const int32_t* ids) {
 }
 
 int dsb::ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x,
-                 int32_t** recv_offsets) {
+                 int32_t** recv_offsets, int n_shared) {
   if (ep == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = ep->ctx;
   if (x == nullptr || ids == nullptr || T != ep->published_T || ldx < ep->L.D || (ldx % 8) ||
-      (reinterpret_cast<uintptr_t>(x) & 15u))
+      (reinterpret_cast<uintptr_t>(x) & 15u) || n_shared < 0 || n_shared > kMaxShared)
     return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (the published T, 16-byte aligned rows)");
   const uint32_t epoch = ep->epoch * 2 - 1;
   const int n = T * ep->L.k;
   const int blocks = std::max(1, std::min(ctx->sm_count, (n + 7) / 8));
   launch_pdl(ep_dispatch_kernel, blocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, ids,
-             ep->d_slot, n, ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch, ctx->d_status);
+             ep->d_slot, n, n_shared, ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   launch_pdl(ep_wait_kernel, 1, 1, 0, ctx->stream, ep->L, ep->peers, 1, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
@@ -466,16 +489,17 @@ extern "C" int dsb_ep_dispatch(dsb_ep* ep, const void* x, int64_t ldx, int T, co
     return fail(ep->ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens, 16-byte aligned rows)");
   int rc = dsb::ep_publish(ep, T, ids);
   if (rc != DSB_OK) return rc;
-  return dsb::ep_send(ep, x, ldx, T, ids, recv_x, recv_offsets);
+  return dsb::ep_send(ep, x, ldx, T, ids, recv_x, recv_offsets, 0);
 }
 
 extern "C" int dsb_ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights,
                               const float* shared, int n_shared, float* h) {
-  return dsb::ep_combine(ep, y, ldy, T, weights, shared, n_shared, h, nullptr, 0.0f, nullptr);
+  return dsb::ep_combine(ep, y, ldy, T, weights, shared, n_shared, h, nullptr, 0.0f, nullptr, nullptr);
 }
 
 int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float* weights, const float* shared,
-                    int n_shared, float* h, const float* w_next, float eps, void* xn_next) {
+                    int n_shared, float* h, const float* w_next, float eps, void* xn_next,
+                    const int32_t* shared_row0) {
   if (ep == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = ep->ctx;
   if (y == nullptr || weights == nullptr || h == nullptr || T < 0 || T > ep->L.T_max || ldy < ep->L.D ||
@@ -484,11 +508,14 @@ int dsb::ep_combine(dsb_ep* ep, const float* y, int64_t ldy, int T, const float*
   if (ep->epoch == 0) return fail(ctx, DSB_EINVAL, "dsb_ep_combine: no dispatch to return");
   ep->L.wait_ns = ctx->wait_limit_ns;
   const uint32_t epoch = ep->epoch * 2;
-  launch_pdl(ep_return_kernel, ctx->sm_count, 256, 0, ctx->stream, y, ldy, ep->d_recv_off, ep->L, ep->peers,
+  // at most cap rows come back, one per warp
+  const int ret_blocks = std::max(1, std::min(ctx->sm_count, (ep->L.cap + 7) / 8));
+  launch_pdl(ep_return_kernel, ret_blocks, 256, 0, ctx->stream, y, ldy, ep->d_recv_off, ep->L, ep->peers,
              ep->d_ticket + 1, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   if (T > 0) {
-    launch_pdl(ep_combine_kernel, T, combine_threads(ep->L.D), 0, ctx->stream, weights, T, ep->L, ep->peers, shared, n_shared, h, w_next,
+    launch_pdl(ep_combine_kernel, T, combine_threads(ep->L.D), 0, ctx->stream, weights, T, ep->L, ep->peers, shared,
+               shared_row0, n_shared, h, w_next,
                eps, static_cast<__nv_bfloat16*>(xn_next), epoch,
                                                   ctx->d_status);
     DSB_CUDA_TRY(ctx, cudaGetLastError());

@@ -1184,8 +1184,6 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
   if ((size_t)need_pages > kv->free_pages.size()) return fail(ctx, DSB_ENOMEM, "%s: out of cache pages", fn);
   const int n_seq = (int)seq_order.size();
   const int LM = prefill ? n_seq : B;  // rows through the lm_head
-  int max_ns_host = 0;
-  for (auto& L : m->layers) max_ns_host = std::max(max_ns_host, L.n_shared);
   const bool ep = m->ep != nullptr;
   int ep_cap = 0, ep_tmax = 0;
   if (ep) {
@@ -1194,13 +1192,11 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     ep_cap = wd * ep_tmax * kg;
     if (B > ep_tmax) return fail(ctx, DSB_EINVAL, "%s: %d rows above the expert group's max_tokens %d", fn, B, ep_tmax);
   }
-  // tokens | positions | block table | (expert parallel) shared-expert row
-  // sources and offsets | (prefill) the lm_head rows | (sampling) the draws
-  const size_t n_shared_tab = ep ? (size_t)max_ns_host * B + max_ns_host + 1 : 0;
-  const size_t o_draws = (size_t)B * (2 + MB) + n_shared_tab + (prefill ? n_seq : 0);
+  // tokens | positions | block table | (prefill) the lm_head rows | (sampling) the draws
+  const size_t o_draws = (size_t)B * (2 + MB) + (prefill ? n_seq : 0);
   std::vector<int32_t> host_i(o_draws + (samp ? (size_t)LM : 0), 0);
   if (prefill)
-    for (int i = 0; i < n_seq; ++i) host_i[(size_t)B * (2 + MB) + n_shared_tab + i] = last_row[seq_order[i]];
+    for (int i = 0; i < n_seq; ++i) host_i[(size_t)B * (2 + MB) + i] = last_row[seq_order[i]];
   if (samp) std::memcpy(host_i.data() + o_draws, uniforms_host, (size_t)LM * 4);
   std::vector<int32_t> lens(B);
   for (int b = 0; b < B; ++b) {
@@ -1217,12 +1213,6 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     const auto& pg = kv->seq_pages[s];
     std::memcpy(host_i.data() + 2 * B + (size_t)b * MB, pg.data(), pg.size() * 4);
   }
-  if (ep) {
-    int32_t* st = host_i.data() + (size_t)B * (2 + MB);
-    for (int j = 0; j < max_ns_host; ++j)
-      for (int b = 0; b < B; ++b) st[(size_t)j * B + b] = b;  // shared group j reads token b
-    for (int j = 0; j <= max_ns_host; ++j) st[(size_t)max_ns_host * B + j] = j * B;
-  }
 
   // ---- device buffers for this batch size (in the context workspace after the plan)
   int max_I = 0, max_eI = 0, max_ns = 0;
@@ -1235,7 +1225,9 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     any_qlora |= L.w_qa != nullptr;
   }
   const int BK = any_moe ? B * (k + max_ns) : 1;
-  const int RX = std::max(BK, ep_cap);  // expert rows: permuted picks, or the expert group's receive rows
+  // expert rows: permuted picks, or the expert group's receive rows followed by
+  // this rank's rows once per shared group
+  const int RX = std::max(BK, ep ? ep_cap + max_ns * B : 0);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1287,9 +1279,7 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
     return quant_act_1x128(ctx, x, DSB_DTYPE_BF16, ld, src, k, rows, K, xq8, K, sx8, K / 128);
   };
   const int32_t *d_tok = tab, *d_pos = tab + B, *d_bt = tab + 2 * B;
-  const int32_t* d_srows = tab + (size_t)B * (2 + MB);           // shared-expert row sources (expert parallel)
-  const int32_t* d_soff = d_srows + (size_t)max_ns_host * B;     // shared-expert row offsets
-  const int32_t* d_lmrows = tab + (size_t)B * (2 + MB) + n_shared_tab;  // (prefill) lm_head rows
+  const int32_t* d_lmrows = tab + (size_t)B * (2 + MB);  // (prefill) lm_head rows
   DSB_CUDA_TRY(ctx, cudaMemcpyAsync(tab, host_i.data(), host_i.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
 
   dsb_mla_plan plan;
@@ -1377,42 +1367,28 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
         DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
                            c.norm_topk_prob, c.routed_scaling_factor, ids, wts, 0));
       }
-      // this rank's pick counts go out first; the shared experts on this
-      // rank's tokens run while they travel, then the rows go to their owners
-      DSB_STEP(ep_publish(m->ep, B, ids));
+      // the routed and the shared experts in one grouped GEMM pair: the
+      // dispatch copies this rank's rows once per shared group after the rows
+      // it receives (groups E_own .. E_own + ns - 1, this rank's tokens)
       const int eI = L.e_inter, EL = m->E_own, ns = L.n_shared;
-      const int64_t gs = (2 * eI / 128) * 2 * (D / 128), ds = (D / 128) * (eI / 128);  // FP8 scales per group
-      if (ns > 0) {
-        if (L.e_gu8 != nullptr) {
-          DSB_STEP(q8(xn, D, ns * B, D, d_srows, 1));
-          DSB_STEP(lin8(ctx, L.e_gu8 + (size_t)EL * 2 * eI * D, L.e_gu8_s + EL * gs, 2, xq8, sx8, D, ns * B, 2 * eI,
-                        midp, eI, 0, DSB_EPI_SILU_GATE, ns, d_soff, B));
-          DSB_STEP(q8(midp, eI, ns * B, eI));
-          DSB_STEP(lin8(ctx, L.e_down8 + (size_t)EL * D * eI, L.e_down8_s + EL * ds, 1, xq8, sx8, eI, ns * B, D, ys, D,
-                        1, DSB_EPI_STORE, ns, d_soff, B));
-        } else {
-          const bf16* s_gu = L.e_gu + (size_t)EL * 2 * eI * D;
-          const bf16* s_down = L.e_down + (size_t)EL * D * eI;
-          DSB_STEP(gather_rows(ctx, xn, D, d_srows, ns * B, 1, D, xperm));
-          DSB_STEP(linear(ctx, s_gu, D, xperm, D, ns * B, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, ns, 0, 0, d_soff,
-                          B));
-          DSB_STEP(linear(ctx, s_down, eI, midp, eI, ns * B, D, eI, ys, D, 1, DSB_EPI_STORE, ns, 0, 0, d_soff, B));
-        }
-      }
       void* rx = nullptr;
       int32_t* roff = nullptr;
-      DSB_STEP(ep_send(m->ep, xn, D, B, ids, &rx, &roff));
+      DSB_STEP(ep_publish(m->ep, B, ids));
+      DSB_STEP(ep_send(m->ep, xn, D, B, ids, &rx, &roff, ns));
+      const int rows = ep_cap + ns * B;  // a bound: the groups' offsets hold the real rows
       if (L.e_gu8 != nullptr) {
-        DSB_STEP(q8(rx, D, ep_cap, D));
-        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, ep_cap, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL,
+        DSB_STEP(q8(rx, D, rows, D));
+        DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, rows, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL + ns,
                       roff, B));
-        DSB_STEP(q8(midp, eI, ep_cap, eI));
-        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, ep_cap, D, yperm, D, 1, DSB_EPI_STORE, EL, roff, B));
+        DSB_STEP(q8(midp, eI, rows, eI));
+        DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, rows, D, yperm, D, 1, DSB_EPI_STORE, EL + ns, roff,
+                      B));
       } else {
-        DSB_STEP(linear(ctx, L.e_gu, D, rx, D, ep_cap, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL, 0, 0, roff, B));
-        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, ep_cap, D, eI, yperm, D, 1, DSB_EPI_STORE, EL, 0, 0, roff, B));
+        DSB_STEP(linear(ctx, L.e_gu, D, rx, D, rows, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL + ns, 0, 0, roff,
+                        B));
+        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, rows, D, eI, yperm, D, 1, DSB_EPI_STORE, EL + ns, 0, 0, roff, B));
       }
-      DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, ys, ns, h, next_norm, c.rms_norm_eps, xn));
+      DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, yperm, ns, h, next_norm, c.rms_norm_eps, xn, roff + EL));
       xn_ready = true;
     } else {
       // each token routes to its top-k experts plus every shared group (weight 1)
