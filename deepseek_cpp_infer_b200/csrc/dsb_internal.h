@@ -154,6 +154,9 @@ int ensure_step(dsb_ctx* ctx, size_t bytes);
 // per-token tickets start at kTicketFront.
 int ensure_counters(dsb_ctx* ctx, size_t n);
 constexpr int kTicketFront = 1024;
+// the routing kernel's ticket (expert-parallel count publication), after the
+// fused front's per-token tickets (at most 4096 rows + 1)
+constexpr int kTicketRoute = kTicketFront + 4096 + 2;
 
 // 2D bf16/u8/f32 tiled tensor map over a row-major matrix [rows, cols] with
 // row pitch `pitch_bytes`; box = box_cols x box_rows; swizzle per CU enum.
@@ -181,8 +184,12 @@ int quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const
                     int K, void* q, int64_t ldq, float* scales, int64_t ld_scales);
 // n_extra > 0 appends groups E..E+n_extra-1 with weight 1 to every token's
 // picks (the shared experts); ids/weights rows then hold k + n_extra entries.
+// pub (expert parallel, may be NULL): the last CTA also publishes this rank's
+// pick counts (ep_publish_args), which replaces ep_publish's own launch.
+struct EpPublishArgs;
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
-              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra);
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra,
+              const EpPublishArgs* pub = nullptr);
 int moe_permute(dsb_ctx* ctx, const int32_t* ids, int N, int E, int32_t* counts, int32_t* offsets, int32_t* dest,
                 int32_t* src_pair, const float* weights, float* w_perm);
 int gather_rows(dsb_ctx* ctx, const void* x, int64_t ldx, const int32_t* src_pair, int n_pairs, int k, int D,
@@ -198,12 +205,17 @@ bool moe_front_fits(int T, int D, int E, int N);
 int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
               int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
               float routed_scale, int n_extra, void* xn, float* logits, int32_t* ids, float* weights, int permute,
-              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm);
+              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm,
+              const EpPublishArgs* pub = nullptr);
 // dsb_ep_dispatch in two parts, so that local work can run between them:
 // ep_publish sends this rank's pick counts (and starts the call's epoch);
 // ep_send then copies the rows to their owners (after every rank's counts
 // arrived) and waits for the rows sent here.
 int ep_publish(dsb_ep* ep, int T, const int32_t* ids);
+// ep_publish's bookkeeping without its launch: the arguments with which a
+// routing kernel (moe_front / moe_route) publishes the counts itself.
+struct EpPublishArgs;
+int ep_publish_args(dsb_ep* ep, int T, EpPublishArgs* out);
 // With n_shared > 0 the dispatch also copies this rank's T rows once per
 // shared expert after the rows it receives (recv_offsets[E_local + j + 1] ends
 // copy j), so one grouped GEMM over E_local + n_shared groups runs both.

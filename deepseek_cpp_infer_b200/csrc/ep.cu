@@ -37,23 +37,11 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "ep_common.cuh"
 #include "rows.cuh"
 
 namespace dsb {
 namespace {
-
-constexpr int kMaxWorld = 8;
-constexpr int kMaxShared = 4;  // shared-expert groups whose rows can follow the received ones
-
-struct EpPeers {
-  uint8_t* win[kMaxWorld];  // every rank's window, mapped here (win[rank] = own)
-};
-
-struct EpLayout {
-  int world, rank, E_local, D, k, T_max, cap;
-  size_t off_counts, off_flags, off_meta, off_recv, off_inbox, bytes;
-  uint64_t wait_ns;  // bound of every flag wait (the context's limit at launch)
-};
 
 EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) {
   EpLayout L{};
@@ -80,16 +68,6 @@ EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) 
   return L;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Bounded wait until flags[s] == epoch for every source s (one thread); gives
 // up after limit_ns of %globaltimer.
 __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch, uint64_t limit_ns) {
@@ -106,41 +84,13 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch, uin
   }
 }
 
-// 1. One warp: stable slot of every pick among this rank's picks of the same
-// expert, this rank's [world][E_local] counts written into every window, and
-// the counts flag raised there.
-__global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, int E, EpLayout L, EpPeers peers,
-                                int32_t* __restrict__ slot, uint32_t epoch, int* status) {
+// 1. One warp: the counts of this rank's picks to every rank (ep_count_warp).
+// The routing kernels do the same in their last CTA when given publish
+// arguments, so this launch is only for dsb_ep_dispatch called directly.
+__global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, EpPublishArgs pub, int* status) {
   pdl_wait();
   __shared__ int32_t cnt[256];
-  const int lane = threadIdx.x;
-  for (int e = lane; e < E; e += 32) cnt[e] = 0;
-  __syncwarp();
-  for (int c = 0; c < n_picks; c += 32) {
-    const int i = c + lane;
-    int e = i < n_picks ? ids[i] : -1 - lane;
-    if (i < n_picks && (unsigned)e >= (unsigned)E) {
-      atomicExch(status, kStatusBadInput);
-      e = -1 - lane;
-    }
-    const unsigned grp = __match_any_sync(0xffffffffu, e);
-    const int r = __popc(grp & ((1u << lane) - 1u));
-    const int base = e >= 0 ? cnt[e] : 0;
-    __syncwarp();
-    if (i < n_picks) slot[i] = e >= 0 ? base + r : -1;
-    if (e >= 0 && r == 0) cnt[e] = base + __popc(grp);
-    __syncwarp();
-  }
-  // this rank's row of the count matrix, into every window
-  const int row = L.world * L.E_local;
-  for (int p = 0; p < L.world; ++p) {
-    int32_t* dst = reinterpret_cast<int32_t*>(peers.win[p] + L.off_counts) + (size_t)L.rank * row;
-    for (int i = lane; i < row; i += 32) dst[i] = cnt[i];
-  }
-  __threadfence_system();
-  __syncwarp();
-  if (lane < L.world)
-    st_release_sys(reinterpret_cast<uint32_t*>(peers.win[lane] + L.off_flags) + 0 * L.world + L.rank, epoch);
+  ep_count_warp(ids, n_picks, pub, status, cnt, threadIdx.x);
 }
 
 // 2. Rows to their owners.  Every CTA waits for all counts, derives this
@@ -445,17 +395,31 @@ extern "C" int dsb_ep_info(const dsb_ep* ep, int* E_local, int* recv_capacity, u
   return DSB_OK;
 }
 
-int dsb::ep_publish(dsb_ep* ep, int T, const int32_t* ids) {
-  if (ep == nullptr) return DSB_EINVAL;
+int dsb::ep_publish_args(dsb_ep* ep, int T, EpPublishArgs* out) {
+  if (ep == nullptr || out == nullptr) return DSB_EINVAL;
   dsb_ctx* ctx = ep->ctx;
   if (!ep->connected && ep->L.world > 1) return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: dsb_ep_connect first");
-  if (ids == nullptr || T < 0 || T > ep->L.T_max)
-    return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens)");
+  if (T < 0 || T > ep->L.T_max) return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: bad arguments (T <= max_tokens)");
   ep->L.wait_ns = ctx->wait_limit_ns;
   const uint32_t epoch = ++ep->epoch * 2 - 1;  // odd: dispatch, even: the return of the same call
   ep->published_T = T;
-  launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, T * ep->L.k, ep->E, ep->L, ep->peers, ep->d_slot, epoch,
-             ctx->d_status);
+  out->L = ep->L;
+  out->peers = ep->peers;
+  out->slot = ep->d_slot;
+  out->epoch = epoch;
+  out->E = ep->E;
+  out->enabled = 1;
+  return DSB_OK;
+}
+
+int dsb::ep_publish(dsb_ep* ep, int T, const int32_t* ids) {
+  if (ep == nullptr) return DSB_EINVAL;
+  dsb_ctx* ctx = ep->ctx;
+  if (ids == nullptr) return fail(ctx, DSB_EINVAL, "dsb_ep_dispatch: null ids");
+  EpPublishArgs pub;
+  int rc = ep_publish_args(ep, T, &pub);
+  if (rc != DSB_OK) return rc;
+  launch_pdl(ep_count_kernel, 1, 32, 0, ctx->stream, ids, T * ep->L.k, pub, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches += 1;
   return DSB_OK;

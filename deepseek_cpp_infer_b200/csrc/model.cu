@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "dsb_internal.h"
+#include "ep_common.cuh"
 #include "dsb_ptx.cuh"
 
 struct dsb_model {
@@ -1356,16 +1357,19 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
       }
     } else if (ep) {
       // expert parallel: routed picks go to the experts' ranks and come back;
-      // the shared experts run here on this rank's tokens
+      // the shared experts run here on this rank's tokens.  The routing
+      // kernel's last CTA publishes this rank's pick counts to every rank.
+      EpPublishArgs pub;
+      DSB_STEP(ep_publish_args(m->ep, B, &pub));
       if (fused_front) {
         DSB_STEP(moe_front(ctx, h, L.post_norm, B, D, c.rms_norm_eps, L.w_router, E, L.router_bias, k, c.scoring_func,
                            c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor, 0, xn, lr, ids, wts, 0,
-                           nullptr, nullptr, nullptr, nullptr, nullptr));
+                           nullptr, nullptr, nullptr, nullptr, nullptr, &pub));
       } else {
         DSB_STEP(rmsnorm_rows(ctx, h, D, L.post_norm, B, D, c.rms_norm_eps, xn, D, xn32, D));
         DSB_STEP(router_logits(ctx, xn32, L.w_router, B, D, E, lr));
         DSB_STEP(moe_route(ctx, lr, L.router_bias, B, E, k, c.scoring_func, c.n_group, c.topk_group,
-                           c.norm_topk_prob, c.routed_scaling_factor, ids, wts, 0));
+                           c.norm_topk_prob, c.routed_scaling_factor, ids, wts, 0, &pub));
       }
       // the routed and the shared experts in one grouped GEMM pair: the
       // dispatch copies this rank's rows once per shared group after the rows
@@ -1373,7 +1377,6 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
       const int eI = L.e_inter, EL = m->E_own, ns = L.n_shared;
       void* rx = nullptr;
       int32_t* roff = nullptr;
-      DSB_STEP(ep_publish(m->ep, B, ids));
       DSB_STEP(ep_send(m->ep, xn, D, B, ids, &rx, &roff, ns));
       const int rows = ep_cap + ns * B;  // a bound: the groups' offsets hold the real rows
       if (L.e_gu8 != nullptr) {

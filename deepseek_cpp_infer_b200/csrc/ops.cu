@@ -12,6 +12,7 @@
 
 #include "dsb_internal.h"
 #include "dsb_ptx.cuh"
+#include "ep_common.cuh"
 #include "rows.cuh"
 
 namespace dsb {
@@ -383,15 +384,31 @@ __device__ __forceinline__ void route_token(const float* lg, const float* __rest
   }
 }
 
+// With pub.enabled (expert parallel, n_extra = 0), the last CTA to finish
+// publishes this rank's pick counts (ep_count_warp) once every token is routed.
 __global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                              int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
-                             int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra) {
+                             int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra, EpPublishArgs pub,
+                             int* __restrict__ ticket, int* __restrict__ status) {
   pdl_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (t >= T) return;
   const int kk = k + n_extra;
-  route_token(logits + (int64_t)t * E, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale,
-              ids + (int64_t)t * kk, weights + (int64_t)t * kk, n_extra, lane);
+  if (t < T)
+    route_token(logits + (int64_t)t * E, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale,
+                ids + (int64_t)t * kk, weights + (int64_t)t * kk, n_extra, lane);
+  if (!pub.enabled) return;
+  __shared__ int last;
+  __shared__ int32_t cnt[256];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(ticket, 1) == (int)gridDim.x - 1;
+    if (last) *ticket = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if ((threadIdx.x >> 5) == 0) ep_count_warp(ids, T * k, pub, status, cnt, lane);
 }
 
 // Deterministic permutation of the N = T*k (token, slot) pairs by expert: the
@@ -485,7 +502,7 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
     float routed_scale, int n_extra, __nv_bfloat16* __restrict__ xn, float* __restrict__ logits,
     int32_t* __restrict__ ids, float* __restrict__ weights, int permute, int32_t* __restrict__ counts,
     int32_t* __restrict__ offsets, int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
-    float* __restrict__ w_perm, int* __restrict__ tickets, int* __restrict__ status) {
+    float* __restrict__ w_perm, int* __restrict__ tickets, int* __restrict__ status, EpPublishArgs pub) {
   pdl_wait();
   extern __shared__ float xs[];  // [D] normalised row, [E] logits, [E + n_extra] permute counts
   __shared__ float red[32];
@@ -533,8 +550,9 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
   if (warp == 0)
     route_token(lg, bias, E, k, scoring, n_group, topk_group, norm_topk, routed_scale, ids + (int64_t)t * kk,
                 weights + (int64_t)t * kk, n_extra, lane);
-  if (!permute) return;
-  // the last token to be routed permutes every pair
+  if (!permute && !pub.enabled) return;
+  // the last token to be routed permutes every pair (or, expert parallel,
+  // publishes this rank's pick counts)
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -545,6 +563,10 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
   if (!last) return;
   __threadfence();
   int32_t* cnt = reinterpret_cast<int32_t*>(lg + E);  // [E + n_extra]
+  if (!permute) {
+    if (warp == 0) ep_count_warp(ids, T * k, pub, status, cnt, lane);
+    return;
+  }
   int32_t* sids = cnt + E + n_extra;                   // [T * kk] ids, then their weights
   float* swts = reinterpret_cast<float*>(sids + T * kk);
   for (int i = threadIdx.x; i < T * kk; i += blockDim.x) {
@@ -772,7 +794,11 @@ bool moe_front_fits(int T, int D, int E, int N) {
 int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, float eps, const float* w_router,
               int E, const float* bias, int k, int scoring, int n_group, int topk_group, int norm_topk,
               float routed_scale, int n_extra, void* xn, float* logits, int32_t* ids, float* weights, int permute,
-              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm) {
+              int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm,
+              const EpPublishArgs* pub) {
+  EpPublishArgs none{};
+  if (pub != nullptr && (permute || n_extra != 0))
+    return fail(ctx, DSB_EINVAL, "moe_front: publishing expert-parallel counts needs permute = 0 and no extra groups");
   int rc = ensure_counters(ctx, kTicketFront + T + 1);
   if (rc != DSB_OK) return rc;
   const size_t smem = (size_t)(D + E + E + n_extra + 2 * T * (k + n_extra)) * sizeof(float);
@@ -783,14 +809,22 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
   const dim3 grid((E + kFrontExperts - 1) / kFrontExperts, T);
   launch_pdl(moe_front_kernel, grid, 256, smem, ctx->stream, h, w_norm, D, eps, w_router, E, bias, k, scoring, n_group,
              topk_group, norm_topk, routed_scale, n_extra, static_cast<__nv_bfloat16*>(xn), logits, ids, weights,
-             permute, counts, offsets, dest, src_pair, w_perm, ctx->counters + kTicketFront, ctx->d_status);
+             permute, counts, offsets, dest, src_pair, w_perm, ctx->counters + kTicketFront, ctx->d_status,
+             pub != nullptr ? *pub : none);
   return launched(ctx);
 }
 
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
-              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra) {
-  launch_pdl(route_kernel, (T + 7) / 8, 256, 0, ctx->stream, logits, bias, T, E, k, scoring, n_group, topk_group, norm_topk,
-                                                     routed_scale, ids, weights, n_extra);
+              int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra,
+              const EpPublishArgs* pub) {
+  EpPublishArgs none{};
+  if (pub != nullptr && n_extra != 0)
+    return fail(ctx, DSB_EINVAL, "moe_route: publishing expert-parallel counts needs no extra groups");
+  int rc = ensure_counters(ctx, kTicketRoute + 1);
+  if (rc != DSB_OK) return rc;
+  launch_pdl(route_kernel, (T + 7) / 8, 256, 0, ctx->stream, logits, bias, T, E, k, scoring, n_group, topk_group,
+             norm_topk, routed_scale, ids, weights, n_extra, pub != nullptr ? *pub : none,
+             ctx->counters + kTicketRoute, ctx->d_status);
   return launched(ctx);
 }
 
