@@ -851,9 +851,10 @@ constexpr size_t kNoAllocScratchBytes =
 
 static __device__ __align__(256) uint8_t g_mla_noalloc_scratch[kNoAllocScratchBytes];
 
-// Per-device set-up, done by the first call on each device: the device address
-// of the scratch array (its name in host code is only a host-side stand-in),
-// the SM count for planning, and the kernels' shared-memory opt-in.
+// Per-device set-up, done by the first call on each device (which should come
+// before any stream capture on that device): the device address of the
+// scratch array (its name in host code is only a host-side stand-in), the SM
+// count for planning, and the kernels' shared-memory opt-in.
 struct NoAllocDevice {
   bool ready = false;
   uint8_t* scratch = nullptr;

@@ -160,7 +160,8 @@ DSB_API int dsb_mla_decode(dsb_ctx* ctx, const void* q_lat, const void* q_rope, 
  * whose fallback still needs more than 24 partials (for example 13 sequences
  * of 17000 tokens, 2 partials each) returns DSB_ELIMIT and enqueues nothing.
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) and sets kernel attributes.  Every call reuses the
+ * (cudaGetSymbolAddress) and sets kernel attributes; make that first call
+ * before any stream capture on the device.  Every call reuses the
  * same array, so calls that overlap on the GPU (different streams, or
  * different host threads on one device) race and must be serialised by the
  * caller.  Each call clears the status word; dsb_mla_noalloc_status reads it.
