@@ -160,6 +160,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 8;  // 16-byte vectors of bf16
+  bool wrote = false;
   for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_picks; i += gridDim.x * warps) {
     const int e = ids[i], s = slot[i];
     if (s < 0) continue;
@@ -170,8 +171,12 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
     uint4* out = reinterpret_cast<uint4*>(pw + L.off_recv + (size_t)row * L.D * 2);
     for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
     if (lane == 0) reinterpret_cast<int32_t*>(pw + L.off_meta)[row] = (L.rank << 24) | i;
+    wrote = true;
   }
-  __threadfence_system();
+  // only threads that stored rows order them (a system-scope fence waits for
+  // the thread's own stores to reach the peers); the shared rows above are
+  // local and read by the next kernels of this stream
+  if (wrote) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int prev = atomicAdd(ticket, 1);
