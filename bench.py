@@ -1163,6 +1163,61 @@ def run_expert_gemm(args):
     ctx.close()
 
 
+def run_attn_linears(args):
+    """The attention-side linears of one V2-Lite decode layer, each alone at
+    B tokens: fused q|kv_a (fp32 out), W_UK^T per head (16 groups), W_UV per
+    head (16 groups), o_proj (+ residual).  Each launch reads a different
+    copy of its weights (the copies together exceed L2 twice over), so every
+    launch streams its weights from HBM as in the step; CUDA events on the
+    context stream.  One JSON line."""
+    import torch
+
+    import deepseek_cpp_infer_b200 as dsb
+
+    torch.cuda.set_device(0)
+    ctx = dsb.Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    B, D, H, nope, P, R, v = args.batch, 2048, 16, 128, 64, 512, 128
+    QH = H * (nope + P)
+    shapes = [  # name, G, M, K, x [T, ldx], x_group_col, y [T, ldy] dtype, y_group_col, epilogue
+        ("q|kv_a", 1, QH + R + P, D, D, 0, QH + R + P, torch.float32, 0, dsb.EPI_STORE),
+        ("W_UK^T per head", H, R, nope, QH, nope + P, H * R, torch.bfloat16, R, dsb.EPI_STORE),
+        ("W_UV per head", H, v, R, H * R, R, H * v, torch.bfloat16, v, dsb.EPI_STORE),
+        ("o_proj (+ residual)", 1, D, H * v, H * v, 0, D, torch.float32, 0, dsb.EPI_ADD),
+    ]
+    peak, peak_kind = measured_peaks()
+    out = []
+    for name, G, M, K, ldx, xgc, ldy, ydt, ygc, epi in shapes:
+        wbytes = G * M * K * 2
+        copies = max(2, -(-2 * L2_BYTES // wbytes))
+        ws = [(torch.randn(G * M, K, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        x = torch.randn(B, ldx, device="cuda").to(torch.bfloat16)
+        y = torch.zeros(B, ldy, dtype=ydt, device="cuda")
+
+        def launch(i):
+            ctx.linear(ws[i % copies], x, y, M=M, K=K, G=G, x_group_col=xgc, y_group_col=ygc, epilogue=epi)
+
+        for i in range(5):
+            launch(i)
+        ctx.sync()
+        n = max(args.steps, 20)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            launch(i)
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / n * 1e3
+        nbytes = wbytes + B * G * K * 2 + B * G * M * (4 if ydt == torch.float32 else 2)
+        out.append({"linear": name, "G": G, "M": M, "K": K, "us_per_launch": us, "bytes": nbytes,
+                    "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / peak})
+        del ws
+    print(json.dumps({"workload": f"V2-Lite attention-side linears, B={B} tokens, weights from HBM (rotated copies)",
+                      "peak_gbs": peak, "peak_kind": peak_kind, "linears": out}), flush=True)
+    ctx.close()
+
+
 def fp8_peak_tflops():
     """Dense e4m3 GEMM throughput of this GPU (torch._scaled_mm, cuBLASLt,
     8192^3, 20 launches) as the tensor-roofline denominator for FP8 work."""
@@ -1308,7 +1363,8 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "v3", "mla", "expert-gemm", "moe-fp8"])
+    ap.add_argument("--workload", default="model",
+                    choices=["model", "v3", "mla", "expert-gemm", "moe-fp8", "attn-linears"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's configuration)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt tokens per sequence (model workload)")
@@ -1330,6 +1386,9 @@ def main():
     if args.workload == "expert-gemm":
         args.batch = args.batch or 32
         run_expert_gemm(args)
+    elif args.workload == "attn-linears":
+        args.batch = args.batch or 32
+        run_attn_linears(args)
     elif args.workload == "moe-fp8":
         args.batch = args.batch or 128
         run_moe_fp8(args)

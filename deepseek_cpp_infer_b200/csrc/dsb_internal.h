@@ -184,8 +184,9 @@ int quant_act_1x128(dsb_ctx* ctx, const void* x, int x_dtype, int64_t ldx, const
                     int K, void* q, int64_t ldq, float* scales, int64_t ld_scales);
 // n_extra > 0 appends groups E..E+n_extra-1 with weight 1 to every token's
 // picks (the shared experts); ids/weights rows then hold k + n_extra entries.
-// pub (expert parallel, may be NULL): the last CTA also publishes this rank's
-// pick counts (ep_publish_args), which replaces ep_publish's own launch.
+// pub (expert parallel, may be NULL): the last CTA also writes the picks'
+// slots and this rank's pick counts for the dispatch (ep_publish_args),
+// which replaces ep_publish's own launch.
 struct EpPublishArgs;
 int moe_route(dsb_ctx* ctx, const float* logits, const float* bias, int T, int E, int k, int scoring, int n_group,
               int topk_group, int norm_topk, float routed_scale, int32_t* ids, float* weights, int n_extra,
@@ -208,15 +209,16 @@ int moe_front(dsb_ctx* ctx, const float* h, const float* w_norm, int T, int D, f
               int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* src_pair, float* w_perm,
               const EpPublishArgs* pub = nullptr);
 // dsb_ep_dispatch in two parts, so that local work can run between them:
-// ep_publish sends this rank's pick counts (and starts the call's epoch);
-// ep_send then copies the rows to their owners (after every rank's counts
-// arrived) and waits for the rows sent here.
+// ep_publish computes every pick's slot and this rank's pick counts (and
+// starts the call's epoch); ep_send then copies the rows and the counts to
+// their owners and, once every source's rows have arrived here, lays out the
+// rows this rank received for the expert GEMMs.
 int ep_publish(dsb_ep* ep, int T, const int32_t* ids);
 // ep_publish's bookkeeping without its launch: the arguments with which a
-// routing kernel (moe_front / moe_route) publishes the counts itself.
+// routing kernel (moe_front / moe_route) computes the slots and counts itself.
 struct EpPublishArgs;
 int ep_publish_args(dsb_ep* ep, int T, EpPublishArgs* out);
-// With n_shared > 0 the dispatch also copies this rank's T rows once per
+// With n_shared > 0 the receive side also copies this rank's T rows once per
 // shared expert after the rows it receives (recv_offsets[E_local + j + 1] ends
 // copy j), so one grouped GEMM over E_local + n_shared groups runs both.
 int ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* ids, void** recv_x, int32_t** recv_offsets,

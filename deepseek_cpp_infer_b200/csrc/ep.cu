@@ -4,28 +4,34 @@
 // with no collective library on the data path.
 //
 // Expert e lives on rank e / E_local.  Every rank keeps its own tokens (data
-// parallel attention) and exchanges, per MoE layer:
-//   1. counts   each rank sends its [world][E_local] pick counts to every rank
-//   2. rows     each pick's bf16 token row goes to the owner's receive buffer,
-//               grouped by local expert, sources in rank order, picks of one
-//               source in pick order (so an expert sees the same row order as
-//               the single-GPU permutation restricted to it)
-//   3. return   each received row's expert output goes back into the home
+// parallel attention) and exchanges, per MoE layer, in two rendezvous:
+//   1. rows     each pick's bf16 token row goes, with no wait, to a staging
+//               slot of the owner's window fixed by (source rank, local
+//               expert, rank of the pick among the source's picks of that
+//               expert), and the source's [world][E_local] counts to every
+//               window; the owner waits for every source's rows flag and lays
+//               the rows out grouped by local expert, sources in rank order,
+//               picks of one source in pick order (so an expert sees the same
+//               row order as the single-GPU permutation restricted to it)
+//   2. return   each received row's expert output goes back into the home
 //               rank's inbox slot of that pick; the home rank sums
 //               w[t,j] * out[t,j] in pick order, then its shared experts
 //               (moe_step's order, src/models/deepseek/ops.cpp:133-145).
 // Every step publishes with a flag holding the call's epoch; a receiver waits
 // (bounded) until all sources show the epoch.  The windows are reused across
 // calls, which is safe because each rank's next dispatch needs every peer's
-// return of the previous call.
+// return of the previous call, and the owner reads its staging slots and
+// counts before it returns.
 //
 // Window layout (identical on every rank):
 //   counts [world src][world dst][E_local] int32
-//   flags  [3 phases][world src] uint32 (counts, rows, return)
+//   flags  [3][world src] uint32 (row 1: rows, row 2: return; row 0 unused)
 //   meta   [cap] int32  (source rank << 24 | source pick index) per received row
 //   recv   [cap + kMaxShared * T_max][D] bf16 received rows, cap = world * T_max * k,
 //          followed (when asked) by this rank's own rows once per shared expert
 //   inbox  [T_max * k][D] fp32 returned outputs of this rank's picks
+//   stage  [world src][E_local][T_max][D] bf16 rows as the sources sent them
+//   smeta  [world src][E_local][T_max] int32 their source pick indices
 // Replaces nothing in the reference (single GPU, B = 1); the exchange model
 // is a host permutation: token -> rank = expert / (E / world).
 
@@ -64,6 +70,10 @@ EpLayout make_layout(int world, int rank, int E_local, int D, int k, int T_max) 
   o += a((size_t)(L.cap + kMaxShared * T_max) * D * 2);
   L.off_inbox = o;
   o += a((size_t)T_max * k * D * 4);
+  L.off_stage = o;
+  o += a((size_t)world * E_local * T_max * D * 2);
+  L.off_smeta = o;
+  o += a((size_t)world * E_local * T_max * 4);
   L.bytes = o;
   return L;
 }
@@ -84,98 +94,51 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch, uin
   }
 }
 
-// 1. One warp: the counts of this rank's picks to every rank (ep_count_warp).
-// The routing kernels do the same in their last CTA when given publish
-// arguments, so this launch is only for dsb_ep_dispatch called directly.
+// 1. One warp: the slot of every pick and this rank's pick counts
+// (ep_count_warp).  The routing kernels do the same in their last CTA when
+// given publish arguments, so this launch is only for dsb_ep_dispatch called
+// directly.
 __global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, EpPublishArgs pub, int* status) {
   pdl_wait();
   __shared__ int32_t cnt[256];
   ep_count_warp(ids, n_picks, pub, status, cnt, threadIdx.x);
 }
 
-// 2. Rows to their owners.  Every CTA waits for all counts, derives this
-// rank's write offsets in each owner's buffer (and, CTA 0, this rank's own
-// receive offsets for the expert GEMMs); warps copy one pick's row each.  The
-// last CTA to finish raises the rows flag in every window.
+// 2. Rows to their owners, with no wait: pick i's row goes to the staging
+// slot [this rank][local expert][slot[i]] of the owner's window (a source's
+// picks of one expert are at most its T <= T_max tokens), its pick index to
+// the slot's meta; CTA 0 also writes this rank's counts into every window's
+// count matrix [src][dst][E_local].  The last CTA to finish raises the rows
+// flag in every window.
 __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ ids,
-                                   const int32_t* __restrict__ slot, int n_picks, int n_shared, EpLayout L,
-                                   EpPeers peers, int32_t* __restrict__ recv_offsets, int* __restrict__ ticket,
-                                   uint32_t epoch, int* status) {
+                                   const int32_t* __restrict__ slot, const int32_t* __restrict__ cnt, int n_picks,
+                                   EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
   pdl_wait();
-  __shared__ int32_t my_off[256];  // [dst][el] (world * E_local = E <= 256): this rank's first row in dst's buffer
-  __shared__ int32_t cnt_s[kMaxWorld * 256];  // the count matrix [src][dst][el] (world * E <= 2048)
-  __shared__ int ok_s;
-  const uint8_t* win = peers.win[L.rank];
-  if (threadIdx.x == 0) {
-    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 0 * L.world, L.world, epoch, L.wait_ns)
-               ? 1
-               : 0;
-    if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
-  }
-  __syncthreads();
-  if (!ok_s) return;
-  // every source's counts in one parallel pass (the flags' acquire ordered
-  // them before this point), then the prefix sums from shared memory
-  const int32_t* counts = reinterpret_cast<const int32_t*>(win + L.off_counts);  // [src][dst][el]
   const int W = L.world, EL = L.E_local;
-  __shared__ int32_t tot_s[256];  // [dst][el]: rows of local expert el that dst receives from all sources
-  for (int i = threadIdx.x; i < W * W * EL; i += blockDim.x) cnt_s[i] = __ldcv(counts + i);
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
-    const int dst = idx / EL, el = idx % EL;
-    int o = 0;
-    for (int s = 0; s < W; ++s) o += cnt_s[(s * W + dst) * EL + el];
-    tot_s[idx] = o;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
-    const int dst = idx / EL, el = idx % EL;
-    int o = 0;
-    for (int e2 = 0; e2 < el; ++e2) o += tot_s[dst * EL + e2];
-    for (int s = 0; s < L.rank; ++s) o += cnt_s[(s * W + dst) * EL + el];
-    my_off[idx] = o;
-  }
-  const int T = n_picks / L.k;
+  bool wrote = false;
   if (blockIdx.x == 0) {
-    // receive offsets of this rank's experts (all sources), the GEMM's groups;
-    // with shared experts, group EL + j is this rank's T rows copied after them
-    for (int el = threadIdx.x; el <= EL + n_shared; el += blockDim.x) {
-      int o = 0;
-      for (int e2 = 0; e2 < min(el, EL); ++e2) o += tot_s[L.rank * EL + e2];
-      recv_offsets[el] = o + (el > EL ? (el - EL) * T : 0);
-    }
-  }
-  __syncthreads();
-  if (n_shared > 0) {
-    // this rank's own rows, once per shared group, after every row it receives
-    int n_recv = 0;
-    for (int e2 = 0; e2 < EL; ++e2) n_recv += tot_s[L.rank * EL + e2];
-    uint8_t* own = peers.win[L.rank] + L.off_recv;
-    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-    for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_shared * T; i += gridDim.x * warps) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i % T) * ldx);
-      uint4* out = reinterpret_cast<uint4*>(own + (size_t)(n_recv + i) * L.D * 2);
-      for (int v = lane; v < L.D / 8; v += 32) out[v] = src[v];
+    for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
+      const int dst = idx / EL, el = idx % EL;
+      reinterpret_cast<int32_t*>(peers.win[dst] + L.off_counts)[(L.rank * W + dst) * EL + el] = cnt[idx];
+      wrote = true;
     }
   }
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 8;  // 16-byte vectors of bf16
-  bool wrote = false;
   for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_picks; i += gridDim.x * warps) {
     const int e = ids[i], s = slot[i];
-    if (s < 0) continue;
+    if (s < 0 || s >= L.T_max) continue;
     const int dst = e / EL, el = e % EL;
-    const int row = my_off[dst * EL + el] + s;
+    const size_t srow = ((size_t)L.rank * EL + el) * L.T_max + s;
     uint8_t* pw = peers.win[dst];
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i / L.k) * ldx);
-    uint4* out = reinterpret_cast<uint4*>(pw + L.off_recv + (size_t)row * L.D * 2);
+    uint4* out = reinterpret_cast<uint4*>(pw + L.off_stage + srow * L.D * 2);
     for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
-    if (lane == 0) reinterpret_cast<int32_t*>(pw + L.off_meta)[row] = (L.rank << 24) | i;
+    if (lane == 0) reinterpret_cast<int32_t*>(pw + L.off_smeta)[srow] = i;
     wrote = true;
   }
-  // only threads that stored rows order them (a system-scope fence waits for
-  // the thread's own stores to reach the peers); the shared rows above are
-  // local and read by the next kernels of this stream
+  // only threads that stored to a peer order their stores (a system-scope
+  // fence waits for the thread's own stores to reach the peers)
   if (wrote) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -186,6 +149,80 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
       for (int p = 0; p < W; ++p)
         st_release_sys(reinterpret_cast<uint32_t*>(peers.win[p] + L.off_flags) + 1 * W + L.rank, epoch);
     }
+  }
+}
+
+// 2'. The owner's side: wait (bounded) until every source has raised the rows
+// flag, then lay the staged rows out for the grouped expert GEMMs - local
+// experts in order, within one the sources in rank order, within a source
+// its picks in pick order (the single-GPU permutation restricted to this
+// rank) - with their (source << 24 | pick) meta for the return, the receive
+// offsets (CTA 0), and with shared experts this rank's own T rows once per
+// shared group after them (groups E_local .. E_local + n_shared - 1).
+// Counts are clamped to the staging capacity and the rows to the receive
+// capacity, so a corrupt count cannot move a copy out of its buffer.
+__global__ void ep_recv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int T, int n_shared, EpLayout L,
+                               EpPeers peers, int32_t* __restrict__ recv_offsets, uint32_t epoch, int* status) {
+  pdl_wait();
+  __shared__ int32_t base_s[257];  // [el][src] first receive row of each staged block, then n_recv
+  __shared__ int ok_s;
+  uint8_t* win = peers.win[L.rank];
+  const int W = L.world, EL = L.E_local, nb = W * EL;
+  if (threadIdx.x == 0) {
+    ok_s = wait_flags(reinterpret_cast<const uint32_t*>(win + L.off_flags) + 1 * W, W, epoch, L.wait_ns) ? 1 : 0;
+    if (!ok_s) atomicCAS(status, 0, kStatusTimeout);
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  // block b = el * W + s holds min(counts[s][rank][el], T_max) rows; one warp scans
+  const int32_t* counts = reinterpret_cast<const int32_t*>(win + L.off_counts);
+  if (threadIdx.x < 32) {
+    int run = 0;
+    for (int c = 0; c < nb; c += 32) {
+      const int b = c + (int)threadIdx.x;
+      int n = 0;
+      if (b < nb) n = min(max(__ldcv(counts + ((b % W) * W + L.rank) * EL + b / W), 0), L.T_max);
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((int)threadIdx.x >= o) incl += v;
+      }
+      if (b < nb) base_s[b] = min(run + incl - n, L.cap);
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (threadIdx.x == 0) base_s[nb] = min(run, L.cap);
+  }
+  __syncthreads();
+  const int n_recv = base_s[nb];
+  if (blockIdx.x == 0) {
+    for (int el = threadIdx.x; el <= EL + n_shared; el += blockDim.x)
+      recv_offsets[el] = el <= EL ? (el < EL ? base_s[el * W] : n_recv) : n_recv + (el - EL) * T;
+  }
+  uint8_t* recv = win + L.off_recv;
+  const int32_t* smeta = reinterpret_cast<const int32_t*>(win + L.off_smeta);
+  int32_t* meta = reinterpret_cast<int32_t*>(win + L.off_meta);
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int vec_per_row = L.D / 8;
+  for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < n_recv; r += gridDim.x * warps) {
+    // the block holding row r: the last b with base_s[b] <= r
+    int lo = 0, hi = nb - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (base_s[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int el = lo / W, s = lo % W, j = r - base_s[lo];
+    const size_t srow = ((size_t)s * EL + el) * L.T_max + j;
+    const uint4* src = reinterpret_cast<const uint4*>(win + L.off_stage + srow * L.D * 2);
+    uint4* out = reinterpret_cast<uint4*>(recv + (size_t)r * L.D * 2);
+    for (int v = lane; v < vec_per_row; v += 32) out[v] = __ldcv(src + v);
+    if (lane == 0) meta[r] = (s << 24) | __ldcv(smeta + srow);
+  }
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < n_shared * T; i += gridDim.x * warps) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(i % T) * ldx);
+    uint4* out = reinterpret_cast<uint4*>(recv + (size_t)(n_recv + i) * L.D * 2);
+    for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
   }
 }
 
@@ -284,6 +321,7 @@ struct dsb_ep {
   uint32_t epoch = 0;
   int published_T = -1;           // tokens of the dispatch whose counts went out last
   int32_t* d_slot = nullptr;      // [T_max * k]
+  int32_t* d_cnt = nullptr;       // [E] this rank's picks of each expert
   int32_t* d_recv_off = nullptr;  // [E_local + 1]
   int* d_ticket = nullptr;        // [2]: dispatch, return
 };
@@ -318,6 +356,7 @@ static int ep_create_impl(dsb_ctx* ctx, int rank, int world, int n_experts, int 
   cudaError_t e = cudaMalloc(&ep->win, ep->L.bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->win, 0, ep->L.bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ep->d_slot, (size_t)max_tokens * top_k * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->d_cnt, (size_t)n_experts * 4);
   if (e == cudaSuccess) e = cudaMalloc(&ep->d_recv_off, (size_t)(ep->L.E_local + 1 + kMaxShared) * 4);
   // zero ranges until the first dispatch (a timed-out exchange leaves them as they were)
   if (e == cudaSuccess) e = cudaMemset(ep->d_recv_off, 0, (size_t)(ep->L.E_local + 1 + kMaxShared) * 4);
@@ -326,6 +365,7 @@ static int ep_create_impl(dsb_ctx* ctx, int rank, int world, int n_experts, int 
   if (e != cudaSuccess) {
     cudaFree(ep->win);
     cudaFree(ep->d_slot);
+    cudaFree(ep->d_cnt);
     cudaFree(ep->d_recv_off);
     cudaFree(ep->d_ticket);
     delete ep;
@@ -386,6 +426,7 @@ extern "C" int dsb_ep_destroy(dsb_ep* ep) {
     if (ep->opened[p]) cudaIpcCloseMemHandle(ep->peers.win[p]);
   cudaFree(ep->win);
   cudaFree(ep->d_slot);
+  cudaFree(ep->d_cnt);
   cudaFree(ep->d_recv_off);
   cudaFree(ep->d_ticket);
   delete ep;
@@ -411,6 +452,7 @@ int dsb::ep_publish_args(dsb_ep* ep, int T, EpPublishArgs* out) {
   out->L = ep->L;
   out->peers = ep->peers;
   out->slot = ep->d_slot;
+  out->cnt = ep->d_cnt;
   out->epoch = epoch;
   out->E = ep->E;
   out->enabled = 1;
@@ -441,9 +483,12 @@ int dsb::ep_send(dsb_ep* ep, const void* x, int64_t ldx, int T, const int32_t* i
   const int n = T * ep->L.k;
   const int blocks = std::max(1, std::min(ctx->sm_count, (n + 7) / 8));
   launch_pdl(ep_dispatch_kernel, blocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, ids,
-             ep->d_slot, n, n_shared, ep->L, ep->peers, ep->d_recv_off, ep->d_ticket, epoch, ctx->d_status);
+             ep->d_slot, ep->d_cnt, n, ep->L, ep->peers, ep->d_ticket, epoch);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
-  launch_pdl(ep_wait_kernel, 1, 1, 0, ctx->stream, ep->L, ep->peers, 1, epoch, ctx->d_status);
+  // at most cap received rows plus the shared copies, one per warp
+  const int rblocks = std::max(1, std::min(ctx->sm_count, (ep->L.cap + n_shared * T + 7) / 8));
+  launch_pdl(ep_recv_kernel, rblocks, 256, 0, ctx->stream, static_cast<const __nv_bfloat16*>(x), ldx, T, n_shared,
+             ep->L, ep->peers, ep->d_recv_off, epoch, ctx->d_status);
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches += 2;
   if (recv_x) *recv_x = ep->win + ep->L.off_recv;

@@ -1,6 +1,6 @@
 // Expert-parallel pieces shared by the exchange kernels (ep.cu) and the
 // routing kernels (ops.cu): the window layout, the peers' window pointers,
-// and the publication of this rank's pick counts.
+// and the stable slot of every pick with this rank's pick counts.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -19,18 +19,19 @@ struct EpPeers {
 
 struct EpLayout {
   int world, rank, E_local, D, k, T_max, cap;
-  size_t off_counts, off_flags, off_meta, off_recv, off_inbox, bytes;
+  size_t off_counts, off_flags, off_meta, off_recv, off_inbox, off_stage, off_smeta, bytes;
   uint64_t wait_ns;  // bound of every flag wait (the context's limit at launch)
 };
 
-// What a kernel needs to publish this rank's pick counts for one exchange.
+// What a routing kernel needs to prepare this rank's side of one exchange.
 struct EpPublishArgs {
   EpLayout L;
   EpPeers peers;
   int32_t* slot;   // [T * k] out: rank of each pick among this rank's picks of its expert
+  int32_t* cnt;    // [E] out: this rank's picks of each expert
   uint32_t epoch;  // the exchange's epoch (odd)
   int E;           // experts over all ranks
-  int enabled;     // 0: nothing to publish
+  int enabled;     // 0: nothing to prepare
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -44,13 +45,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // One warp (lane = 0..31): the stable slot of every pick among this rank's
-// picks of the same expert, this rank's [world][E_local] counts written into
-// every rank's window, then the counts flag raised there.  ids: the n_picks
-// expert ids (global memory, complete when the warp starts); cnt: [E] ints of
-// shared memory.  An out-of-range id is flagged in *status and not counted.
+// picks of the same expert, and this rank's per-expert pick counts, both into
+// this rank's own memory (a.slot, a.cnt; the dispatch sends them).  ids: the
+// n_picks expert ids (global memory, complete when the warp starts); cnt:
+// [E] ints of shared memory.  An out-of-range id is flagged in *status and
+// not counted.
 __device__ __forceinline__ void ep_count_warp(const int32_t* ids, int n_picks, const EpPublishArgs& a, int* status,
                                               int32_t* cnt, int lane) {
-  const EpLayout& L = a.L;
   for (int e = lane; e < a.E; e += 32) cnt[e] = 0;
   __syncwarp();
   for (int c = 0; c < n_picks; c += 32) {
@@ -68,16 +69,7 @@ __device__ __forceinline__ void ep_count_warp(const int32_t* ids, int n_picks, c
     if (e >= 0 && r == 0) cnt[e] = base + __popc(grp);
     __syncwarp();
   }
-  // this rank's row of the count matrix, into every window
-  const int row = L.world * L.E_local;
-  for (int p = 0; p < L.world; ++p) {
-    int32_t* dst = reinterpret_cast<int32_t*>(a.peers.win[p] + L.off_counts) + (size_t)L.rank * row;
-    for (int i = lane; i < row; i += 32) dst[i] = cnt[i];
-  }
-  __threadfence_system();
-  __syncwarp();
-  if (lane < L.world)
-    st_release_sys(reinterpret_cast<uint32_t*>(a.peers.win[lane] + L.off_flags) + 0 * L.world + L.rank, a.epoch);
+  for (int e = lane; e < a.E; e += 32) a.cnt[e] = cnt[e];
 }
 
 }  // namespace dsb

@@ -385,7 +385,8 @@ __device__ __forceinline__ void route_token(const float* lg, const float* __rest
 }
 
 // With pub.enabled (expert parallel, n_extra = 0), the last CTA to finish
-// publishes this rank's pick counts (ep_count_warp) once every token is routed.
+// writes every pick's slot and this rank's pick counts for the dispatch
+// (ep_count_warp) once every token is routed.
 __global__ void route_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                              int scoring, int n_group, int topk_group, int norm_topk, float routed_scale,
                              int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra, EpPublishArgs pub,
@@ -552,7 +553,7 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
                 weights + (int64_t)t * kk, n_extra, lane);
   if (!permute && !pub.enabled) return;
   // the last token to be routed permutes every pair (or, expert parallel,
-  // publishes this rank's pick counts)
+  // writes the picks' slots and this rank's pick counts for the dispatch)
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {

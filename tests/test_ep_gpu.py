@@ -189,8 +189,8 @@ def test_ep_wait_runs_out_and_context_survives(gpu_ctx):
 
     Rank 0 of a 2-rank group is connected to a zeroed window that stands for
     rank 1, and rank 1 is never driven, so no kernel ever raises its flags.
-    With a 10 ms limit the dispatch's count wait and the combine's return wait
-    give up: dsb_sync reports DSB_ETIMEOUT, the return kernel stores no row
+    With a 10 ms limit the receive side's rows wait and the combine's return
+    wait give up: dsb_sync reports DSB_ETIMEOUT, the return kernel stores no row
     (its exchange already failed), and the context keeps working.
     """
     import time
