@@ -115,12 +115,10 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
   pdl_wait();
   const int W = L.world, EL = L.E_local;
-  bool wrote = false;
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
       const int dst = idx / EL, el = idx % EL;
       reinterpret_cast<int32_t*>(peers.win[dst] + L.off_counts)[(L.rank * W + dst) * EL + el] = cnt[idx];
-      wrote = true;
     }
   }
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -135,13 +133,13 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
     uint4* out = reinterpret_cast<uint4*>(pw + L.off_stage + srow * L.D * 2);
     for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
     if (lane == 0) reinterpret_cast<int32_t*>(pw + L.off_smeta)[srow] = i;
-    wrote = true;
   }
-  // only threads that stored to a peer order their stores (a system-scope
-  // fence waits for the thread's own stores to reach the peers)
-  if (wrote) __threadfence_system();
+  // the CTA's stores, ordered by the barrier, then one system-scope fence
+  // before its ticket (cumulative: it covers every store the barrier ordered
+  // before it, the pattern of a cooperative grid barrier)
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int prev = atomicAdd(ticket, 1);
     if (prev == (int)gridDim.x - 1) {
       *ticket = 0;
@@ -247,20 +245,17 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
   const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int vec_per_row = L.D / 4;  // 16-byte vectors of fp32
-  bool wrote = false;
   for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < n_recv; r += gridDim.x * warps) {
     const int m = __ldcv(meta + r);
     const int home = m >> 24, pick = m & 0xFFFFFF;
     const uint4* src = reinterpret_cast<const uint4*>(y + (int64_t)r * ldy);
     uint4* out = reinterpret_cast<uint4*>(peers.win[home] + L.off_inbox + (size_t)pick * L.D * 4);
     for (int v = lane; v < vec_per_row; v += 32) out[v] = src[v];
-    wrote = true;
   }
-  // only threads that stored rows order them (a system-scope fence waits for
-  // the thread's own stores to reach the peers)
-  if (wrote) __threadfence_system();
+  // as in the dispatch: the barrier, then one system-scope fence per CTA
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int prev = atomicAdd(ticket, 1);
     if (prev == (int)gridDim.x - 1) {
       *ticket = 0;
