@@ -141,6 +141,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return out;
 }
 
+// Generic address of the same shared-memory object in CTA `rank` of the
+// cluster (plain loads through it read that CTA's shared memory).
+template <class T>
+__device__ __forceinline__ const T* map_cluster_ptr(const T* p, uint32_t rank) {
+  uint64_t out;
+  asm("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
+  return reinterpret_cast<const T*>(out);
+}
+
+// 16-byte load from the shared memory of a CTA of the cluster (address from mapa).
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");

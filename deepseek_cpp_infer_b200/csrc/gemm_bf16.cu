@@ -20,7 +20,13 @@
 // epilogue (warp w reads TMEM lanes 32*(w%4)..+31 = weight rows of the tile).
 // Split-K (dense groups with <= 256 tokens only): every split writes an fp32
 // partial, the last split to finish (atomic ticket) sums the partials in split
-// order - deterministic - and runs the epilogue.
+// order - deterministic - and runs the epilogue.  A dense launch whose units
+// all fit one round runs the splits of a unit as one thread-block cluster
+// instead (plain store / add outputs): each CTA keeps its partial in its own
+// shared memory, and after a cluster barrier each sums its share of the
+// tile's 32-row x 8-token pieces from all the partials at once (distributed
+// shared memory, in split order: the same sums as the ticket path) and stores
+// them; no global round trip.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -54,6 +60,7 @@ struct GemmParams {
   float* ws;          // split partials: [tail unit][split][NT][128]
   int* counters;      // per-tail-unit tickets (zeroed; reset by the last split)
   int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
+  int csplit;         // > 1: the splits of a unit are one cluster of csplit CTAs (one unit each)
 };
 
 template <int NT>
@@ -68,6 +75,8 @@ struct GemmShape {
   static constexpr int OFF_BAR = OFF_SCHED + ((int)sizeof(SchedTable) + 15) / 16 * 16;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NS + 8) * 8;
   static constexpr int SMEM = OFF_MISC + 32 + 1024;
+  static constexpr int PART_LD = NT + 4;              // cluster split-K partial [128][NT + 4] fp32 in the ring
+  static_assert(kTileM * PART_LD * 4 <= NS * STAGE, "partial fits the ring");
   static constexpr uint32_t TC = NT < 32 ? 32 : NT;  // TMEM columns per accumulator
   static constexpr uint32_t TCOLS = 2 * TC;          // double-buffered
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -176,6 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = first; i < q; ++i) mbar_wait(&full[i % S::NS], (i / S::NS) & 1, no_abort);
       }
     }
+    if (p.csplit > 1) {  // the epilogue's two cluster barriers (every thread of the cluster passes both)
+      __syncwarp();
+      cluster_sync();
+      cluster_sync();
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -209,6 +223,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, no_abort);
     }
+    if (p.csplit > 1) {
+      __syncwarp();
+      cluster_sync();
+      cluster_sync();
+    }
   } else {
     // ------------------------------------------------------------- epilogue
     const uint32_t qtr = warp & 3;  // TMEM lane quarter of this warp
@@ -217,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool silu = p.epi == DSB_EPI_SILU_GATE;
     float* stg = reinterpret_cast<float*>(smem + S::OFF_STG) + (warp - 2) * 32 * 32;  // this warp's staging block
     SchedIter it{sched, p.m_tiles, NT, KB};
-    int u = 0, epi_phase = 0;
+    int u = 0, epi_phase = 0, csyncs = 0;
     while (it.next()) {
       const int slot = u & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[slot], (u >> 1) & 1, abort))) {
@@ -299,6 +318,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       const int nsplit = it.nsplit, tail_j = it.tail_j;
+      constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
+      if (p.csplit > 1) {
+        // cluster split-K: this CTA's only unit.  Its partial goes to its own
+        // shared memory (the ring, idle now: the unit's MMAs have completed),
+        // row r at part_s + r * PART_LD; after the cluster barrier, warp w of
+        // cluster CTA q sums the pieces (8 tokens, the 32 rows of warp w)
+        // numbered pc with pc % csplit == q over the CTAs in split order.
+        float* part_s = reinterpret_cast<float*>(smem) + r * S::PART_LD;
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(taddr + c * 32, raw);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < CW; i += 4)
+            *reinterpret_cast<float4*>(part_s + c * 32 + i) =
+                make_float4(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1]), __uint_as_float(raw[i + 2]),
+                            __uint_as_float(raw[i + 3]));
+        }
+        tc_fence_before();
+        warp_arrive(&acc_empty[slot]);
+        ++u;
+        cluster_sync();
+        ++csyncs;
+        if (!__any_sync(0xffffffffu, *abort != 0)) {
+          // pieces of 8 tokens x this warp's 32 rows; piece pc goes to cluster CTA pc % csplit
+          const uint32_t my = cluster_ctarank();
+          constexpr int HW = 8, NH = CW / HW;
+          const int ncols = max(0, min(32, p.M - it.mt * kTileM - (int)qtr * 32));
+          const int64_t col0 = (int64_t)it.g * p.y_group_col + it.mt * kTileM + qtr * 32;
+          for (int c = 0; c < NCH; ++c) {
+            for (int h = 0; h < NH; ++h) {
+              if (((c * NH + h) * 4 + (int)qtr) % p.csplit != (int)my) continue;  // warp-uniform
+              float4 w[8][HW / 4];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (j < p.csplit) {
+                  const float4* src =
+                      reinterpret_cast<const float4*>(map_cluster_ptr(part_s + c * 32 + h * HW, (uint32_t)j));
+#pragma unroll
+                  for (int i = 0; i < HW / 4; ++i) w[j][i] = src[i];
+                }
+              }
+              float v[HW];
+#pragma unroll
+              for (int i = 0; i < HW; ++i) v[i] = 0.0f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (j < p.csplit) {
+#pragma unroll
+                  for (int i = 0; i < HW / 4; ++i) {
+                    v[4 * i] += w[j][i].x;
+                    v[4 * i + 1] += w[j][i].y;
+                    v[4 * i + 2] += w[j][i].z;
+                    v[4 * i + 3] += w[j][i].w;
+                  }
+                }
+              }
+              warp_store_block<HW, false, 0>(stg, v, lane, tcount - c * 32 - h * HW, ncols, p.y, p.ldy, col0,
+                                             tbase + c * 32 + h * HW, p.y_f32, p.epi == DSB_EPI_ADD);
+            }
+          }
+        }
+        cluster_sync();  // no CTA leaves while a peer may still read its partial
+        ++csyncs;
+        continue;
+      }
       float* part = nsplit > 1 ? p.ws + ((int64_t)tail_j * nsplit + it.split) * (int64_t)NT * kTileM : nullptr;
       for (int c = 0; c < NCH; ++c) {
         uint32_t raw[32];
@@ -337,7 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*last_flag != 0) {
           __threadfence();
           const float* pbase = p.ws + (int64_t)tail_j * nsplit * (int64_t)NT * kTileM + r;
-          constexpr int CW = NT < 32 ? NT : 32;  // valid columns per chunk
           for (int c = 0; c < NCH; ++c) {
             float v[32];
 #pragma unroll
@@ -364,6 +448,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // an early exit (timed-out wait) still passes the cluster barriers
+    if (p.csplit > 1)
+      for (; csyncs < 2; ++csyncs) cluster_sync();
   }
   tc_fence_before();
   __syncthreads();
@@ -403,13 +490,55 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int max_splits, int m_ti
   p.counters = nullptr;
   p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
                          a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
+  p.csplit = 0;
+  auto kern = gemm_bf16_kernel<NT>;
+  static std::atomic<bool> attr_set[kMaxDevices];
+  if (int rc2 = smem_attr_once(ctx, kern, S::SMEM, attr_set); rc2 != DSB_OK) return rc2;
   // A grouped launch's units are known only on the device (sched.cuh), so it
   // takes every SM; a dense one launches no more CTAs than it has work items.
   int grid = ctx->sm_count;
-  if (a->tok_offsets == nullptr)
-    grid = std::min(grid, sched_shape(a->G * m_tiles * ((a->T + NT - 1) / NT), grid, max_splits).items);
+  if (a->tok_offsets == nullptr) {
+    const int units = a->G * m_tiles * ((a->T + NT - 1) / NT);
+    const SchedShape sh = sched_shape(units, grid, max_splits);
+    grid = std::min(grid, sh.items);
+    if (sh.full == 0 && sh.splits > 1 && p.vec_out &&
+        (a->epilogue == DSB_EPI_STORE || a->epilogue == DSB_EPI_ADD)) {
+      // one round of split units: the splits of a unit as one cluster, as
+      // many splits as lets every cluster be resident at once
+      static std::atomic<int> fit[kMaxDevices][9];
+      int cs = std::min(sh.splits, 8);
+      for (; cs > 1; --cs) {
+        std::atomic<int>& f = fit[ctx->device % kMaxDevices][cs];
+        int n = f.load();
+        if (n == 0) {
+          cudaLaunchConfig_t qc{};
+          qc.gridDim = dim3((unsigned)(units * cs));
+          qc.blockDim = dim3(kThreads);
+          qc.dynamicSmemBytes = S::SMEM;
+          cudaLaunchAttribute qa[1];
+          qa[0].id = cudaLaunchAttributeClusterDimension;
+          qa[0].val.clusterDim.x = (unsigned)cs;
+          qa[0].val.clusterDim.y = 1;
+          qa[0].val.clusterDim.z = 1;
+          qc.attrs = qa;
+          qc.numAttrs = 1;
+          if (cudaOccupancyMaxActiveClusters(&n, kern, &qc) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = -1;  // not available: the ticket reduction
+          }
+          f.store(n == 0 ? -1 : n);
+        }
+        if (n >= units) break;
+      }
+      if (cs > 1) {
+        p.csplit = cs;
+        max_splits = cs;
+        grid = units * cs;
+      }
+    }
+  }
   grid = std::max(grid, 1);
-  if (max_splits > 1) {
+  if (max_splits > 1 && p.csplit == 0) {
     // split partials and tickets: at most one per CTA of the last round
     rc = ensure_workspace(ctx, (size_t)grid * NT * kTileM * sizeof(float));
     if (rc != DSB_OK) return rc;
@@ -418,10 +547,26 @@ int launch_gemm(dsb_ctx* ctx, const dsb_linear_args* a, int max_splits, int m_ti
     p.ws = static_cast<float*>(ctx->ws);
     p.counters = ctx->counters;
   }
-  auto kern = gemm_bf16_kernel<NT>;
-  static std::atomic<bool> attr_set[kMaxDevices];
-  if (int rc = smem_attr_once(ctx, kern, S::SMEM, attr_set); rc != DSB_OK) return rc;
-  DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, kThreads, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
+  p.max_splits = max_splits;
+  if (p.csplit > 1) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = S::SMEM;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.csplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    DSB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, map_w, map_x, p, ctx->d_status));
+  } else {
+    DSB_CUDA_TRY(ctx, launch_pdl(kern, grid, kThreads, S::SMEM, ctx->stream, map_w, map_x, p, ctx->d_status));
+  }
   DSB_CUDA_TRY(ctx, cudaGetLastError());
   ctx->stats.kernel_launches++;
   ctx->stats.gemm_calls++;
