@@ -103,7 +103,9 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
   pdl_wait();
   __shared__ float red[32];
   __shared__ float cs[2][64];  // cos / sin of each rope pair at this token's position (P <= 128)
-  const int b = blockIdx.x;
+  // CTA (b, 0) appends the latent row; with gridDim.y > 1 the query's heads
+  // are split over CTAs (b, 1..), which run beside it
+  const int b = blockIdx.x, part = blockIdx.y, qparts = gridDim.y > 1 ? gridDim.y - 1 : 1;
   const int p = pos[b];
   const float* kv = kv_a + (int64_t)b * ld_kv;
   for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
@@ -113,28 +115,33 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
     cs[1][k] = sinf(ang);
   }
   __syncthreads();
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < R; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(kv[i], kv[i]));
-  const float mean2 = __fdiv_rn(block_sum(ss, red), (float)R);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
-  const int64_t page = block_table[(int64_t)b * max_blocks + p / 64];
-  __nv_bfloat16* row = cache + (page * 64 + p % 64) * (int64_t)(R + P);
-  for (int i = threadIdx.x; i < R; i += blockDim.x) row[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(kv[i], inv), w_norm[i]));
-  for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
-    float x0 = kv[R + 2 * k], x1 = kv[R + 2 * k + 1];
-    rotate_pair(x0, x1, cs[0][k], cs[1][k]);
-    row[R + 2 * k] = __float2bfloat16_rn(x0);
-    row[R + 2 * k + 1] = __float2bfloat16_rn(x1);
+  if (part == 0) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < R; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(kv[i], kv[i]));
+    const float mean2 = __fdiv_rn(block_sum(ss, red), (float)R);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean2, eps)));
+    const int64_t page = block_table[(int64_t)b * max_blocks + p / 64];
+    __nv_bfloat16* row = cache + (page * 64 + p % 64) * (int64_t)(R + P);
+    for (int i = threadIdx.x; i < R; i += blockDim.x) row[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(kv[i], inv), w_norm[i]));
+    for (int k = threadIdx.x; k < P / 2; k += blockDim.x) {
+      float x0 = kv[R + 2 * k], x1 = kv[R + 2 * k + 1];
+      rotate_pair(x0, x1, cs[0][k], cs[1][k]);
+      row[R + 2 * k] = __float2bfloat16_rn(x0);
+      row[R + 2 * k + 1] = __float2bfloat16_rn(x1);
+    }
   }
+  if (gridDim.y > 1 && part == 0) return;
+  const int qp = gridDim.y > 1 ? part - 1 : 0;
+  const int h0 = qp * H / qparts, h1 = (qp + 1) * H / qparts;  // this CTA's query heads
   const int qh = nope + P;
   if (qf != nullptr) {
     // fp32 query: its nope parts go out as the bf16 query of the absorb GEMM
-    for (int idx = threadIdx.x; idx < H * nope; idx += blockDim.x) {
+    for (int idx = h0 * nope + (int)threadIdx.x; idx < h1 * nope; idx += blockDim.x) {
       const int h = idx / nope, i = idx % nope;
       q_out[(int64_t)b * H * qh + (int64_t)h * qh + i] = __float2bfloat16_rn(qf[(int64_t)b * ld_qf + h * qh + i]);
     }
   }
-  for (int idx = threadIdx.x; idx < H * (P / 2); idx += blockDim.x) {
+  for (int idx = h0 * (P / 2) + (int)threadIdx.x; idx < h1 * (P / 2); idx += blockDim.x) {
     const int h = idx / (P / 2), k = idx % (P / 2);
     float x0, x1;
     if (qf != nullptr) {
@@ -766,7 +773,10 @@ int kv_norm_rope_append(dsb_ctx* ctx, const float* kv_a, int64_t ld_kv, const fl
                         const float* qf, int64_t ld_qf, void* q_out, const int32_t* pos, const int32_t* block_table,
                         int max_blocks, int B, int H, int nope, int R, int P, float eps, float theta, void* cache,
                         void* q_rope) {
-  launch_pdl(kv_norm_rope_append_kernel, B, 256, 0, ctx->stream, kv_a, ld_kv, w_norm,
+  // the latent row in CTA (b, 0), the query's heads over 1..8 more CTAs per token
+  const int qparts = std::min(8, std::max(1, H / 8));
+  launch_pdl(kv_norm_rope_append_kernel, dim3((unsigned)B, (unsigned)(1 + qparts)), 256, 0, ctx->stream, kv_a, ld_kv,
+             w_norm,
              static_cast<const __nv_bfloat16*>(q), qf, ld_qf, static_cast<__nv_bfloat16*>(q_out), pos, block_table,
              max_blocks, H, nope, R, P, eps, theta, static_cast<__nv_bfloat16*>(cache),
              static_cast<__nv_bfloat16*>(q_rope));
