@@ -93,6 +93,13 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// dsb_linear / dsb_linear_fp8; with offsets_ready (grouped launches whose
+// token offsets were written before the previous kernel of the stream began)
+// the unit table is built and the first weight stages are loaded before the
+// wait on the previous kernel, as for a dense launch.
+int linear_ex(dsb_ctx* ctx, const dsb_linear_args* a, bool offsets_ready);
+int linear_fp8_ex(dsb_ctx* ctx, const dsb_linear_fp8_args* a, bool offsets_ready);
+
 // Record an error message on the context and return `code`.
 int fail(dsb_ctx* ctx, int code, const char* fmt, ...);
 

@@ -63,6 +63,7 @@ struct Fp8Params {
   float* ws;          // split partials: [tail unit][split][NT][128]
   int* counters;      // per-tail-unit tickets (zeroed; reset by the last split)
   int vec_out;        // y meets the alignment of the vectorised output (epi.cuh)
+  int offsets_ready;  // grouped: the token offsets were complete before the previous kernel began
 };
 
 template <int NT>
@@ -152,7 +153,10 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
   }
   SchedTable* sched = reinterpret_cast<SchedTable*>(smem + S::OFF_SCHED);
   const bool dense = p.tok_offsets == nullptr;
-  if (dense && warp == 2) sched_build(sched, nullptr, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
+  // the unit table before the wait when nothing the previous kernel writes
+  // goes into it (dense, or offsets written earlier in the stream)
+  const bool early = dense || p.offsets_ready;
+  if (early && warp == 2) sched_build(sched, p.tok_offsets, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
   // A dense GEMM's work items are known without them, so its producer also
   // starts the weight half of the first ring stages before the wait.
   int npre = 0;
-  if (warp == 0 && lane == 0 && dense) {
+  if (warp == 0 && lane == 0 && early) {
     const uint64_t pol_w = l2_policy_evict_first();
     SchedIter it{sched, p.m_tiles, NT, KB};
     while (npre < S::NS && it.next()) {
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
     }
   }
   pdl_wait();
-  if (!dense) {  // the unit table of a grouped GEMM needs the token offsets
+  if (!early) {  // the unit table of a grouped GEMM needs the token offsets
     if (warp == 2) sched_build(sched, p.tok_offsets, p.G, p.T, NT, p.m_tiles, p.max_splits, lane);
     __syncthreads();
   }
@@ -500,7 +504,7 @@ __global__ void __launch_bounds__(Fp8Shape<NT>::THREADS, 1)
 }
 
 template <int NT>
-int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int max_splits, int m_tiles) {
+int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int max_splits, int m_tiles, bool offsets_ready) {
   using S = Fp8Shape<NT>;
   CUtensorMap map_w, map_x;
   const uint64_t w_rows = (uint64_t)a->G * a->M;
@@ -533,6 +537,7 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int max_splits, int m
   p.counters = nullptr;
   p.vec_out = vec_out_ok(a->y, a->y_f32, a->ldy, a->y_group_col,
                          a->epilogue == DSB_EPI_SILU_GATE ? a->M / 2 : a->M) ? 1 : 0;
+  p.offsets_ready = (offsets_ready && a->tok_offsets != nullptr) ? 1 : 0;
   // A grouped launch's units are known only on the device (sched.cuh), so it
   // takes every SM; a dense one launches no more CTAs than it has work items.
   int grid = ctx->sm_count;
@@ -561,7 +566,9 @@ int launch_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a, int max_splits, int m
 }  // namespace
 }  // namespace dsb
 
-extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
+extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) { return dsb::linear_fp8_ex(ctx, a, false); }
+
+int dsb::linear_fp8_ex(dsb_ctx* ctx, const dsb_linear_fp8_args* a, bool offsets_ready) {
   using namespace dsb;
   if (ctx == nullptr) return DSB_EINVAL;
   if (a == nullptr || a->w == nullptr || a->w_scale == nullptr || a->x == nullptr || a->x_scale == nullptr ||
@@ -601,9 +608,9 @@ extern "C" int dsb_linear_fp8(dsb_ctx* ctx, const dsb_linear_fp8_args* a) {
     if (units < ctx->sm_count) max_splits = std::max(1, std::min({ctx->sm_count / units, KB / 2, 8}));
   }
   switch (NT) {
-    case 16: return launch_fp8<16>(ctx, a, max_splits, m_tiles);
-    case 32: return launch_fp8<32>(ctx, a, max_splits, m_tiles);
-    case 64: return launch_fp8<64>(ctx, a, max_splits, m_tiles);
-    default: return launch_fp8<128>(ctx, a, max_splits, m_tiles);
+    case 16: return launch_fp8<16>(ctx, a, max_splits, m_tiles, offsets_ready);
+    case 32: return launch_fp8<32>(ctx, a, max_splits, m_tiles, offsets_ready);
+    case 64: return launch_fp8<64>(ctx, a, max_splits, m_tiles, offsets_ready);
+    default: return launch_fp8<128>(ctx, a, max_splits, m_tiles, offsets_ready);
   }
 }

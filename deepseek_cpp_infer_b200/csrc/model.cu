@@ -318,7 +318,8 @@ struct StepBuffers {
 
 int linear(dsb_ctx* ctx, const void* w, int64_t ldw, const void* x, int64_t ldx, int T, int M, int K, void* y,
            int64_t ldy, int y_f32, int epi, int G = 1, int64_t xgc = 0, int64_t ygc = 0,
-           const int32_t* tok_offsets = nullptr, int max_tok = 0, const float* row_scale = nullptr) {
+           const int32_t* tok_offsets = nullptr, int max_tok = 0, const float* row_scale = nullptr,
+           bool offsets_ready = false) {
   dsb_linear_args a{};
   a.w = w;
   a.ldw = ldw;
@@ -337,7 +338,7 @@ int linear(dsb_ctx* ctx, const void* w, int64_t ldw, const void* x, int64_t ldx,
   a.y_f32 = y_f32;
   a.epilogue = epi;
   a.row_scale = row_scale;
-  return dsb_linear(ctx, &a);
+  return linear_ex(ctx, &a, offsets_ready);
 }
 
 }  // namespace
@@ -1106,7 +1107,7 @@ namespace {
 // (xq, sx), then dsb_linear_fp8 (no group column offsets).
 int lin8(dsb_ctx* ctx, const uint8_t* w, const float* ws, int scale_rows, const uint8_t* xq, const float* sx, int K,
          int T, int M, void* y, int64_t ldy, int y_f32, int epi, int G = 1, const int32_t* offs = nullptr,
-         int max_tok = 0, const float* row_scale = nullptr) {
+         int max_tok = 0, const float* row_scale = nullptr, bool offsets_ready = false) {
   dsb_linear_fp8_args a{};
   a.w = w;
   a.ldw = K;
@@ -1127,7 +1128,7 @@ int lin8(dsb_ctx* ctx, const uint8_t* w, const float* ws, int scale_rows, const 
   a.y_f32 = y_f32;
   a.epilogue = epi;
   a.row_scale = row_scale;
-  return dsb_linear_fp8(ctx, &a);
+  return linear_fp8_ex(ctx, &a, offsets_ready);
 }
 
 }  // namespace
@@ -1379,17 +1380,20 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
       int32_t* roff = nullptr;
       DSB_STEP(ep_send(m->ep, xn, D, B, ids, &rx, &roff, ns));
       const int rows = ep_cap + ns * B;  // a bound: the groups' offsets hold the real rows
+      // the receive kernel writes the offsets right before the bf16 gate|up GEMM;
+      // every other expert GEMM here has a launch between (offsets_ready)
       if (L.e_gu8 != nullptr) {
         DSB_STEP(q8(rx, D, rows, D));
         DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, rows, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, EL + ns,
-                      roff, B));
+                      roff, B, nullptr, true));
         DSB_STEP(q8(midp, eI, rows, eI));
         DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, rows, D, yperm, D, 1, DSB_EPI_STORE, EL + ns, roff,
-                      B));
+                      B, nullptr, true));
       } else {
         DSB_STEP(linear(ctx, L.e_gu, D, rx, D, rows, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, EL + ns, 0, 0, roff,
                         B));
-        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, rows, D, eI, yperm, D, 1, DSB_EPI_STORE, EL + ns, 0, 0, roff, B));
+        DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, rows, D, eI, yperm, D, 1, DSB_EPI_STORE, EL + ns, 0, 0, roff, B,
+                        nullptr, true));
       }
       DSB_STEP(ep_combine(m->ep, yperm, D, B, wts, yperm, ns, h, next_norm, c.rms_norm_eps, xn, roff + EL));
       xn_ready = true;
@@ -1407,22 +1411,24 @@ int forward_tokens(dsb_ctx* ctx, dsb_model* m, dsb_kvcache* kv, const int32_t* s
                            c.norm_topk_prob, c.routed_scaling_factor, ids, wts, L.n_shared));
         DSB_STEP(moe_permute(ctx, ids, B * kk, G, cnt, offs, dest, src, wts, wperm));
       }
+      // (the expert GEMMs' offsets come from the routing kernel, two or more
+      // launches back: they may build their schedules before the wait)
       const int eI = L.e_inter;
       if (L.e_gu8 != nullptr) {
         // gather + quantise the permuted rows in one pass, then the FP8 expert GEMMs
         DSB_STEP(q8(xn, D, B * kk, D, src, kk));
         DSB_STEP(lin8(ctx, L.e_gu8, L.e_gu8_s, 2, xq8, sx8, D, B * kk, 2 * eI, midp, eI, 0, DSB_EPI_SILU_GATE, G, offs,
-                      B));
+                      B, nullptr, true));
         DSB_STEP(q8(midp, eI, B * kk, eI));
         DSB_STEP(lin8(ctx, L.e_down8, L.e_down8_s, 1, xq8, sx8, eI, B * kk, D, yperm, D, 1, DSB_EPI_ROWSCALE, G, offs,
-                      B, wperm));
+                      B, wperm, true));
       } else {
         DSB_STEP(gather_rows(ctx, xn, D, src, B * kk, kk, D, xperm));
         // every expert writes the same columns of its own (permuted) token rows
         DSB_STEP(linear(ctx, L.e_gu, D, xperm, D, B * kk, 2 * eI, D, midp, eI, 0, DSB_EPI_SILU_GATE, G, 0, 0, offs,
-                        B));
+                        B, nullptr, true));
         DSB_STEP(linear(ctx, L.e_down, eI, midp, eI, B * kk, D, eI, yperm, D, 1, DSB_EPI_ROWSCALE, G, 0, 0, offs, B,
-                        wperm));
+                        wperm, true));
       }
       DSB_STEP(moe_combine(ctx, yperm, dest, B, kk, D, nullptr, h, next_norm, c.rms_norm_eps, xn));
       xn_ready = true;
