@@ -100,6 +100,7 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t epoch, uin
 // directly.
 __global__ void ep_count_kernel(const int32_t* __restrict__ ids, int n_picks, EpPublishArgs pub, int* status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ int32_t cnt[256];
   ep_count_warp(ids, n_picks, pub, status, cnt, threadIdx.x);
 }
@@ -114,6 +115,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    const int32_t* __restrict__ slot, const int32_t* __restrict__ cnt, int n_picks,
                                    EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int W = L.world, EL = L.E_local;
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < W * EL; idx += blockDim.x) {
@@ -162,6 +164,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
 __global__ void ep_recv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int T, int n_shared, EpLayout L,
                                EpPeers peers, int32_t* __restrict__ recv_offsets, uint32_t epoch, int* status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ int32_t base_s[257];  // [el][src] first receive row of each staged block, then n_recv
   __shared__ int ok_s;
   uint8_t* win = peers.win[L.rank];
@@ -228,6 +231,7 @@ __global__ void ep_recv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
 // its rows have landed; phase 2, its returns have.
 __global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t epoch, int* status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.win[L.rank] + L.off_flags) + phase * L.world;
   if (!wait_flags(flags, L.world, epoch, L.wait_ns)) atomicCAS(status, 0, kStatusTimeout);
 }
@@ -241,6 +245,7 @@ __global__ void ep_return_kernel(const float* __restrict__ y, int64_t ldy, const
                                  EpLayout L, EpPeers peers, int* __restrict__ ticket, uint32_t epoch,
                                  const int* __restrict__ status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int n_recv = *reinterpret_cast<const volatile int*>(status) != 0 ? 0 : recv_offsets[L.E_local];
   const int32_t* meta = reinterpret_cast<const int32_t*>(peers.win[L.rank] + L.off_meta);
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -273,6 +278,7 @@ __global__ void ep_combine_kernel(const float* __restrict__ weights, int T, EpLa
                                   const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next,
                                   uint32_t epoch, int* status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ int ok_s;
   const uint8_t* win = peers.win[L.rank];
   if (threadIdx.x == 0) {

@@ -182,6 +182,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   tc_fence_after();
   if (NCTA == 2) cluster_sync();  // peer barriers initialised before any remote access
   pdl_wait();                     // the previous kernel's q / cache writes are visible from here
+  pdl_launch_dependents();        // the next kernel may begin its prologue; it still waits for this one
   const uint32_t tmem = *tmem_base_smem;
   const uint32_t smem_base = smem_u32(smem);
 
@@ -519,6 +520,7 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaCombine* __re
                                                           const float2* __restrict__ ws_ml,
                                                           __nv_bfloat16* __restrict__ out) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const MlaCombine cmb = list[blockIdx.x];
   const int h = blockIdx.y;
   float M = -INFINITY;

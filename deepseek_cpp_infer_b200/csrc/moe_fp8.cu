@@ -22,6 +22,7 @@ namespace {
 __global__ void append_shared_kernel(const int32_t* __restrict__ ids, const float* __restrict__ weights, int T, int k,
                                      int E, int ns, int32_t* __restrict__ ids_out, float* __restrict__ w_out) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const int kk = k + ns;

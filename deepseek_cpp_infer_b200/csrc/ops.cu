@@ -70,6 +70,7 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int64_t ldx, co
                                     float eps, __nv_bfloat16* __restrict__ yb, int64_t ldyb, float* __restrict__ yf,
                                     int64_t ldyf) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ float red[32];
   const float* xr = x + blockIdx.x * ldx;
   const float inv = row_inv_rms(xr, n, (n % 4) == 0 && (ldx % 4) == 0, eps, red);
@@ -91,8 +92,8 @@ __device__ __forceinline__ void rotate_pair(float& x0, float& x1, float c, float
   x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
-// One block per token b: c = rmsnorm(kv_a[b, :R]) * w and kr = rope(kv_a[b, R:])
-// go to the token's paged-cache row (mla.cpp:74-84); every head's rope query
+// Per token b: c = rmsnorm(kv_a[b, :R]) * w and kr = rope(kv_a[b, R:]) go to
+// the token's paged-cache row (mla.cpp:74-84), and every head's rope query
 // q[b, h, nope:] is rotated into q_rope[b, h] (mla.cpp:97).
 __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64_t ld_kv, const float* __restrict__ w_norm,
                                            const __nv_bfloat16* __restrict__ q, const float* __restrict__ qf,
@@ -101,6 +102,7 @@ __global__ void kv_norm_rope_append_kernel(const float* __restrict__ kv_a, int64
                                            int max_blocks, int H, int nope, int R, int P, float eps, float theta,
                                            __nv_bfloat16* __restrict__ cache, __nv_bfloat16* __restrict__ q_rope) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ float red[32];
   __shared__ float cs[2][64];  // cos / sin of each rope pair at this token's position (P <= 128)
   // CTA (b, 0) appends the latent row; with gridDim.y > 1 the query's heads
@@ -184,6 +186,7 @@ __device__ __forceinline__ float router_dot(const float* xr, const float* __rest
 __global__ void router_logits_kernel(const float* __restrict__ x, const float* __restrict__ w, int T, int D, int E,
                                      float* __restrict__ logits) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= T * E) return;
   const int t = gw / E, e = gw % E;
@@ -200,6 +203,7 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const float* _
                                                                    const float* __restrict__ w, int T, int D, int E,
                                                                    float* __restrict__ logits) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ float xs[kRtT][kRtD + 1];
   __shared__ float ws[kRtE][kRtD + 1];
   const int t0 = blockIdx.y * kRtT, e0 = blockIdx.x * kRtE;
@@ -399,6 +403,7 @@ __global__ void route_kernel(const float* __restrict__ logits, const float* __re
                              int32_t* __restrict__ ids, float* __restrict__ weights, int n_extra, EpPublishArgs pub,
                              int* __restrict__ ticket, int* __restrict__ status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int kk = k + n_extra;
   if (t < T)
@@ -481,6 +486,7 @@ __global__ void permute_kernel(const int32_t* __restrict__ ids, int N, int E, in
                                int32_t* __restrict__ src_pair, const float* __restrict__ weights,
                                float* __restrict__ w_perm, int* __restrict__ status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   extern __shared__ int32_t cnt[];  // [E] counts, then the N ids and their weights
   int32_t* sids = cnt + E;
   float* swts = reinterpret_cast<float*>(sids + N);
@@ -512,6 +518,7 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
     int32_t* __restrict__ offsets, int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
     float* __restrict__ w_perm, int* __restrict__ tickets, int* __restrict__ status, EpPublishArgs pub) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   extern __shared__ float xs[];  // [D] normalised row, [E] logits, [E + n_extra] permute counts
   __shared__ float red[32];
   __shared__ int last;
@@ -590,6 +597,7 @@ __global__ void __launch_bounds__(256) moe_front_kernel(
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src,
                                    int k, int D, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int p = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)(src[p] / k) * ldx);
   uint4* d = reinterpret_cast<uint4*>(out + (int64_t)p * D);
@@ -608,6 +616,7 @@ constexpr int kPermSingleWarpMax = 4096;
 __global__ void permute_count_kernel(const int32_t* __restrict__ ids, int N, int E, int32_t* __restrict__ hist,
                                      int* __restrict__ status) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   extern __shared__ int32_t h[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
@@ -624,6 +633,7 @@ __global__ void permute_count_kernel(const int32_t* __restrict__ ids, int N, int
 __global__ void permute_scan_kernel(int32_t* __restrict__ hist, int chunks, int E, int32_t* __restrict__ counts,
                                     int32_t* __restrict__ offsets) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   extern __shared__ int32_t tot[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int v = 0;
@@ -666,6 +676,7 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int N, i
                                        int32_t* __restrict__ dest, int32_t* __restrict__ src_pair,
                                        const float* __restrict__ weights, float* __restrict__ w_perm) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   extern __shared__ int32_t cur[];
   const int lane = threadIdx.x;
   for (int e = lane; e < E; e += 32) cur[e] = hist[(int64_t)blockIdx.x * E + e];
@@ -699,6 +710,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
                                    const float* __restrict__ shared, float* __restrict__ h,
                                    const float* __restrict__ w_next, float eps, __nv_bfloat16* __restrict__ xn_next) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ float red[32];
   __shared__ const float4* rows[kMaxCombinePicks];  // the token's pick rows, looked up once
   const int t = blockIdx.x;
@@ -712,6 +724,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
 // Greedy id per row: first index of the maximum (argmax_f32, math.cpp:29-40).
 __global__ void argmax_rows_kernel(const float* __restrict__ logits, int64_t ld, int V, int32_t* __restrict__ out) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ float sv[32];
   __shared__ int si[32];
   const float* row = logits + blockIdx.x * ld;
@@ -745,6 +758,7 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int64_t ld,
 __global__ void embed_kernel(const void* __restrict__ table, int bf16, const int32_t* __restrict__ tokens, int D,
                              float* __restrict__ h) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int b = blockIdx.x;
   const int64_t row = tokens[b];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {

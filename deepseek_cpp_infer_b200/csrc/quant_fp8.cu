@@ -37,6 +37,7 @@ __global__ void quant_act_kernel(const void* __restrict__ x, int64_t ldx, const 
                                  int k, int T, int G, uint8_t* __restrict__ q, int64_t ldq,
                                  float* __restrict__ scales, int64_t ld_scales) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= (int64_t)T * G) return;
@@ -70,6 +71,7 @@ template <bool kBf16>
 __global__ void quant_weight_kernel(const void* __restrict__ w, int64_t M, int64_t K, uint8_t* __restrict__ q,
                                     float* __restrict__ scales) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   const int64_t r0 = (int64_t)blockIdx.y * 128, c0 = (int64_t)blockIdx.x * 128;
   auto load = [&](int64_t r, int64_t c) -> float {
     if (kBf16) return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[r * K + c]);

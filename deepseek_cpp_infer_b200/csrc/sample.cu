@@ -435,6 +435,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(const float* __re
                                                                const float* __restrict__ uniforms,
                                                                int32_t* __restrict__ out, int vec) {
   pdl_wait();
+  pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
   __shared__ SampleSmem s;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = ((V + kWarps * 128 - 1) / (kWarps * 128)) * 128;  // warp segment, a multiple of 128
