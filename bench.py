@@ -17,10 +17,11 @@ roofline fractions, and at 8 GPUs the DeepSeek-V3 target ("target").
 
 Other workloads: "v3" (DeepSeek-V3 shape, FP8, 4096-token context), "mla"
 (isolated absorbed-MLA decode, B=64, 128 heads, context U[1024, 8192]),
-"expert-gemm" (the dominant kernel alone), "moe-fp8" (one V3 MoE layer).
+"expert-gemm" (the dominant kernel alone), "moe-fp8" (one V3 MoE layer),
+"attn-linears" (the four attention-side linears of a V2-Lite layer alone).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload model|v3|mla|expert-gemm|moe-fp8]
+                    [--workload model|v3|mla|expert-gemm|moe-fp8|attn-linears]
 """
 
 from __future__ import annotations
