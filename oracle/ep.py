@@ -65,3 +65,35 @@ def placements(ids: np.ndarray, cm: np.ndarray, rank: int, E: int):
     dst = flat // EL
     row = off[dst, flat % EL] + sl
     return dst, row
+
+
+def staged_layout(ids_per_rank, E: int, world: int, T_max: int):
+    """Owner-side layout of the exchange as the kernels run it in two steps:
+    every source s puts its pick of local expert el of owner d into the
+    staging slot [s][el][slot] of d (slot = the pick's rank among s's picks
+    of that expert, so slot < T <= T_max), with s's per-expert counts; the
+    owner then lays the staged rows out expert by expert, sources in rank
+    order, slots in order.  Returns, per owner, the (source, pick) of every
+    received row in row order and the owner's receive offsets [E_local + 1].
+    This must equal the direct placement (placements / recv_offsets)."""
+    EL = E // world
+    staged = [[[None] * T_max for _ in range(EL)] for _ in range(world * world)]  # [(s, d)][el][slot]
+    counts = np.zeros((world, world, EL), np.int64)
+    for s, ids in enumerate(ids_per_rank):
+        flat = np.asarray(ids).ravel()
+        sl = slots(ids) if flat.size else np.zeros(0, np.int64)
+        for i, e in enumerate(flat):
+            d, el = int(e) // EL, int(e) % EL
+            assert sl[i] < T_max
+            staged[s * world + d][el][sl[i]] = (s, i)
+            counts[s, d, el] += 1
+    out = []
+    for d in range(world):
+        rows = []
+        offs = [0]
+        for el in range(EL):
+            for s in range(world):
+                rows.extend(staged[s * world + d][el][: counts[s, d, el]])
+            offs.append(len(rows))
+        out.append((rows, np.asarray(offs, np.int64)))
+    return out

@@ -7,7 +7,10 @@ for bit (float64, linear experts), every expert sees its rows in the order of
 the single-GPU permutation (the oracle's orc_moe_permute over all ranks'
 picks in rank order), ranks with no tokens take part, and a rank that fails
 before the count exchange makes the others' exchange end with an error
-instead of hanging.
+instead of hanging.  The GPU kernels reach the same layout in two steps
+(fixed staging slots per source and local expert, then the owner's
+compaction); a host restatement of those steps is checked against the
+direct placement.
 """
 
 import datetime
@@ -151,3 +154,32 @@ def test_ep_exchange_fails_when_a_rank_dies(tmp_path):
         p.join(60)
     assert all(not p.is_alive() for p in ctx.processes)
     assert (tmp_path / "rank0_saw_error").exists()
+
+
+def test_staged_layout_equals_direct_placement():
+    """The two-step exchange (fixed staging slots per source and local expert,
+    then the owner's compaction) gives every owner the same rows in the same
+    order, and the same receive offsets, as placing each pick directly at
+    its final row from the full count matrix; ranks with no tokens included."""
+    import oracle.ep as OE
+
+    rng = np.random.default_rng(4)
+    for world, t_per_rank in [(2, [5, 0]), (4, [3, 7, 0, 1]), (8, [2] * 8), (2, [16, 16])]:
+        Ek = 8 * world
+        ids = [np.stack([rng.choice(Ek, K, replace=False) for _ in range(t)]) if t else np.zeros((0, K), np.int64)
+               for t in t_per_rank]
+        T_max = max(max(t_per_rank), 1)
+        cm = np.stack([OE.counts(i, Ek, world) if len(i) else np.zeros((world, Ek // world), np.int64) for i in ids])
+        staged = OE.staged_layout(ids, Ek, world, T_max)
+        for d in range(world):
+            direct = {}
+            for s in range(world):
+                if len(ids[s]) == 0:
+                    continue
+                dst, row = OE.placements(ids[s], cm, s, Ek)
+                for i in range(len(dst)):
+                    if dst[i] == d:
+                        direct[int(row[i])] = (s, i)
+            rows, offs = staged[d]
+            assert rows == [direct[r] for r in range(len(direct))]
+            assert np.array_equal(offs, OE.recv_offsets(cm, d))
