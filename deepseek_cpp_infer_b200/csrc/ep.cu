@@ -228,7 +228,9 @@ __global__ void ep_recv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
 }
 
 // 3. Wait until every source has raised `phase` here (one thread): phase 1,
-// its rows have landed; phase 2, its returns have.
+// its rows have landed; phase 2, its returns have.  Used for phase 2 by a
+// rank with no tokens, whose combine has nothing else to wait on (the rows
+// wait is the receive kernel's).
 __global__ void ep_wait_kernel(EpLayout L, EpPeers peers, int phase, uint32_t epoch, int* status) {
   pdl_wait();
   pdl_launch_dependents();  // the next kernel may begin its prologue; it still waits for this one
